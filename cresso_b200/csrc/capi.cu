@@ -1,0 +1,60 @@
+// Library info and the error plumbing of the C ABI.
+
+#include <cuda_runtime.h>
+#include <stdarg.h>
+#include <stdio.h>
+#include <string.h>
+
+#include "cresso_status.h"
+
+namespace cresso {
+
+static thread_local char g_last_error[1024] = {0};
+
+int set_error(int code, const char* fmt, ...) {
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(g_last_error, sizeof(g_last_error), fmt, ap);
+    va_end(ap);
+    return code;
+}
+
+int check_cuda(cudaError_t e, const char* what) {
+    if (e == cudaSuccess) return CRESSO_OK;
+    return set_error(CRESSO_ECUDA, "%s failed: %s (%s)", what, cudaGetErrorName(e), cudaGetErrorString(e));
+}
+
+int check_launch(const char* what) {
+    const cudaError_t e = cudaGetLastError();
+    if (e == cudaSuccess) return CRESSO_OK;
+    return set_error(CRESSO_ECUDA, "launch of %s failed: %s (%s)", what, cudaGetErrorName(e), cudaGetErrorString(e));
+}
+
+}  // namespace cresso
+
+extern "C" {
+
+const char* cresso_version(void) { return "cresso_b200 0.1.0 (CRESSO5 step, abi 1)"; }
+
+const char* cresso_arch(void) { return "sm_100a"; }
+
+int cresso_last_error(char* buf, size_t n) {
+    const size_t len = strlen(cresso::g_last_error);
+    if (buf != nullptr && n > 0) {
+        const size_t c = len < n - 1 ? len : n - 1;
+        memcpy(buf, cresso::g_last_error, c);
+        buf[c] = '\0';
+    }
+    return (int)len;
+}
+
+int cresso_abi_layout(int64_t* out, int n) {
+    if (out == nullptr || n < 4) return cresso::set_error(CRESSO_EINVAL, "abi_layout: need an array of >= 4");
+    out[0] = (int64_t)sizeof(cresso_hparams);
+    out[1] = (int64_t)sizeof(cresso_tensor_desc);
+    out[2] = CRESSO_MAX_NDIM;
+    out[3] = CRESSO_MAX_RANK;
+    return CRESSO_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,164 @@
+// Shared device / host helpers of the B200 CRESSO5 kernels.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <cmath>
+
+namespace cresso {
+
+constexpr int kThreads = 256;  // every kernel of the library runs 256-thread blocks
+constexpr int kWarps = kThreads / 32;
+constexpr int kMaxRank = 16;
+constexpr int kMaxTB = 8192;   // hash_tables * hash_bins held in shared memory
+constexpr int kMaxBins = 4096; // same bound as the reference CUDA hash path (cresso_v5.py:1002)
+
+// Salted three-round int64 coordinate hash, remainder taken Python-style.
+// Restates _hash_index_tensor (cresso_v5.py:495-516): torch int64 arithmetic
+// wraps modulo 2^64 (done here in uint64), `>>` is an arithmetic shift of the
+// signed value, and torch.remainder returns a value in [0, bins).
+__host__ __device__ __forceinline__ int64_t hash_bin(int64_t i, int64_t bins, int64_t salt) {
+    const uint64_t s = (uint64_t)(salt + 1);
+    uint64_t h = (uint64_t)i * (uint64_t)(1103515245ULL + 97ULL * s) + (12345ULL + 0x9E3779B1ULL * s);
+    int64_t v = (int64_t)h;
+    v ^= (v >> 16);
+    h = (uint64_t)v * (2246822519ULL + 1315423911ULL * s);
+    v = (int64_t)h;
+    v ^= (v >> 13);
+    h = (uint64_t)v * (3266489917ULL + 374761393ULL * s);
+    v = (int64_t)h;
+    v ^= (v >> 16);
+    if ((bins & (bins - 1)) == 0) return v & (bins - 1);
+    int64_t r = v % bins;
+    return r < 0 ? r + bins : r;
+}
+
+__host__ __device__ __forceinline__ int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
+
+__host__ __device__ __forceinline__ int pow2_ceil(int64_t v) {
+    int p = 1;
+    while (p < v && p < (1 << 30)) p <<= 1;
+    return p;
+}
+
+// Mode kinds of the carrier pack (cresso_v5.py:302-348): mode % 4 == 1 uses
+// per-axis products of cos and of sin; every other mode (and the zero mode,
+// whose tables are (1, 0)) is a complex exponential product.
+__host__ __device__ constexpr bool mode_is_product(int k) { return (k & 3) == 1; }
+
+// ---------------------------------------------------------------------------
+// Per-shape workspace layout (built by cresso_shape_workspace_init).
+//   rowtab : float [grows][RM][2]   (a1, a2) of mode k on global row i
+//   coltab : float [RM][2][gcols]   (b1, b2) of mode k on global column j
+//   stats  : double [RM][8]         mu_c, inv_c, mu_s, inv_s, mhat_c, mhat_s
+//   gram   : double [2RM][2RM]      mean(basis_p * basis_q), p = 2k (cos) / 2k+1 (sin)
+//   counts : float [T][B]           elements of the tensor in each hash bin
+//   tmp    : double                 table sums used while building stats / gram
+// For a 1-D tensor of n elements grows = 1 and gcols = n.
+// ---------------------------------------------------------------------------
+struct ShapeWsHeader {
+    int64_t magic, ndim, grows, gcols, rank, rm, bins, tables;
+    int64_t off_rowtab, off_coltab, off_stats, off_gram, off_counts, off_tmp, bytes, n;
+};
+constexpr int64_t kShapeWsMagic = 0x43524553534f3542LL;  // "CRESSO5B"
+
+__host__ __device__ inline int64_t align_up(int64_t v, int64_t a) { return (v + a - 1) / a * a; }
+
+__host__ inline ShapeWsHeader shape_ws_layout(int64_t ndim, int64_t grows, int64_t gcols, int64_t rank, int64_t rm,
+                                             int64_t bins, int64_t tables) {
+    ShapeWsHeader h{};
+    h.magic = kShapeWsMagic;
+    h.ndim = ndim;
+    h.grows = grows;
+    h.gcols = gcols;
+    h.rank = rank;
+    h.rm = rm;
+    h.bins = bins;
+    h.tables = tables;
+    h.n = grows * gcols;
+    int64_t off = align_up((int64_t)sizeof(ShapeWsHeader), 256);
+    h.off_rowtab = off;
+    off = align_up(off + grows * rm * 2 * 4, 256);
+    h.off_coltab = off;
+    off = align_up(off + rm * 2 * gcols * 4, 256);
+    h.off_stats = off;
+    off = align_up(off + rm * 8 * 8, 256);
+    h.off_gram = off;
+    off = align_up(off + (2 * rm) * (2 * rm) * 8, 256);
+    h.off_counts = off;
+    off = align_up(off + (bins > 0 ? bins * tables * 4 : 0), 256);
+    // set-up scratch: per-axis sums S1[p] and cross sums S2[p][q] of the tables
+    h.off_tmp = off;
+    off = align_up(off + 2 * ((2 * rm) * (2 * rm) + 2 * rm) * 8, 256);
+    h.bytes = off;
+    return h;
+}
+
+__host__ __device__ inline int rank_pad(int64_t rank) { return rank <= 4 ? 4 : (rank <= 8 ? 8 : 16); }
+
+// ---------------------------------------------------------------------------
+// Warp / block reductions (fixed order => run-to-run deterministic)
+// ---------------------------------------------------------------------------
+template <typename T>
+__device__ __forceinline__ T warp_sum(T v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+template <typename T>
+__device__ __forceinline__ T warp_max(T v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = max(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+// Sums N per-thread values across the block in a fixed order.  `red` is
+// shared scratch of N * kWarps doubles and `out` shared memory of N doubles,
+// readable by every thread on return; all threads must call.
+template <int N>
+__device__ __forceinline__ void block_sum_to(double (&v)[N], double* red, double* out) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+    for (int j = 0; j < N; ++j) {
+        double s = warp_sum(v[j]);
+        if (lane == 0) red[j * kWarps + warp] = s;
+    }
+    __syncthreads();
+    for (int j = threadIdx.x; j < N; j += blockDim.x) {
+        double s = 0.0;
+        for (int w = 0; w < kWarps; ++w) s += red[j * kWarps + w];
+        out[j] = s;
+    }
+    __syncthreads();
+}
+
+__device__ __forceinline__ double block_sum(double v, double* red) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    double s = warp_sum(v);
+    if (lane == 0) red[warp] = s;
+    __syncthreads();
+    double t = 0.0;
+    if (threadIdx.x == 0) {
+        for (int w = 0; w < kWarps; ++w) t += red[w];
+        red[kWarps] = t;
+    }
+    __syncthreads();
+    t = red[kWarps];
+    __syncthreads();
+    return t;
+}
+
+__device__ __forceinline__ float clampf(float v, float lo, float hi) { return fminf(fmaxf(v, lo), hi); }
+
+// EMA with a copy on the first step (reference _update_reservoir,
+// cresso_v5.py:900-905): old * decay + cur * (1 - decay).
+// decay is the Python float of the group; torch multiplies a float32 tensor
+// by (float)decay and adds with alpha (float)(1 - decay).
+__device__ __forceinline__ float reservoir(float old, float cur, double decay, int64_t step) {
+    if (step <= 1) return cur;
+    return old * (float)decay + cur * (float)(1.0 - decay);
+}
+
+}  // namespace cresso

@@ -1,0 +1,34 @@
+// Status / error plumbing of the C ABI: entry points return an int status and
+// leave a message in a thread-local buffer that cresso_last_error() copies out.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/cresso_b200.h"
+
+namespace cresso {
+
+int set_error(int code, const char* fmt, ...);
+int check_cuda(cudaError_t e, const char* what);
+// Status of the last kernel launch on this thread (cudaGetLastError).
+int check_launch(const char* what);
+
+}  // namespace cresso
+
+#define CRESSO_REQUIRE(cond, code, ...)                    \
+    do {                                                   \
+        if (!(cond)) return ::cresso::set_error((code), __VA_ARGS__); \
+    } while (0)
+
+#define CRESSO_CUDA(call)                                        \
+    do {                                                         \
+        int _st = ::cresso::check_cuda((call), #call);           \
+        if (_st != CRESSO_OK) return _st;                        \
+    } while (0)
+
+#define CRESSO_LAUNCHED(name)                                    \
+    do {                                                         \
+        int _st = ::cresso::check_launch(name);                  \
+        if (_st != CRESSO_OK) return _st;                        \
+    } while (0)

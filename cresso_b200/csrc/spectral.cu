@@ -1,0 +1,1195 @@
+// Fused CRESSO5 spectral-route step for a group of tensors.
+//
+// The reference step (cresso_v5.py:945-1353) is a chain of dense field ops
+// separated by global reductions.  Here it runs as five streaming passes over
+// each tensor, every pass a single grouped launch for all tensors:
+//
+//   P1  f = g (+wd p)                     -> sum f^2                    (force_rms)
+//   P2  rel, rel^p, log1p, axis density   -> hash bin sums, projection of log1p,
+//                                            row / column sums of the density
+//   P3  metric, instant and hash metrics  -> tangent t (stored), prediction error,
+//                                            projection of t, hash bin sums of the port
+//   P4  t, new prediction, echo, shapes   -> Gram of the drive components
+//   P5  t, drive                          -> p -= lr * gain * drive
+//
+// After each of P1..P4 a reduce kernel sums the per-block records of every
+// tensor in a fixed order into a float64 "reduction vector" (the only data a
+// row-sharded run all-reduces across GPUs), and a finalize kernel (one block
+// per tensor) updates the persistent rank / hash / scalar state and writes
+// the per-tensor constants the next pass needs.  No host synchronisation.
+
+#include <cuda_runtime.h>
+#include <math.h>
+#include <stdint.h>
+#include <string.h>
+
+#include <algorithm>
+#include <vector>
+
+#include "basis_dev.cuh"
+#include "cresso_common.cuh"
+#include "cresso_status.h"
+
+namespace cresso {
+
+constexpr int kNSRec = 36;  // float64 scalars per block record (>= 2 + 2 * kMaxRank, >= 29)
+constexpr int kGram = 29;   // 28 pair sums of (u, root, t, pred, nov, echo, hp) + sum rat^2
+
+enum : int32_t {
+    F_MAXIMIZE = 1,
+    F_WD = 2,
+    F_HARD = 4,
+    F_HASH = 8,
+    F_LOCAL = 16,
+    F_ECHO = 32,
+    F_INST2D = 64,
+    F_INST1D = 128,
+    F_IPOW1 = 256,  // instant_metric_power == 1 (density = rel)
+};
+
+struct TensorConsts {
+    float scale, inv_scale;
+    float m_al[kMaxRank], m_be[kMaxRank], m_K;     // metric field reconstruction (inv folded)
+    float p0_al[kMaxRank], p0_be[kMaxRank], p0_K;  // prediction from the old oscillators
+    float pr_al[kMaxRank], pr_be[kMaxRank], pr_K;  // prediction from the new oscillators
+    float ec_al[kMaxRank], ec_be[kMaxRank], ec_K;  // echo = reconstruction of proj(t)
+    float cb_al[kMaxRank], cb_be[kMaxRank], cb_K;  // c_pred * pred + c_echo * echo
+    float inst_k, inst_gm;
+    float S, sp, invD, clip, inv_clip, clip2;
+    float c_u, c_root, c_t, c_nov, c_hp, gain, neg_lr;
+    float pad[3];
+    double pv[2 * kMaxRank];  // old prediction coefficients on the normalised carriers
+};
+
+struct GroupHdr {
+    int64_t n_tensors, n_items, rm, bins, tables, tb, iters, idx_bytes;
+    int64_t grid[6];  // blocks of pass 1..5 (index 0 unused)
+    double hp[64];    // cresso_hparams
+};
+
+struct DevTensor {
+    int64_t rows, cols, row0, col0, gcols, N;
+    int64_t item_base, n_items, step, hidx_n;
+    int32_t ndim, R, TC, RPI, RB, n_ct, n_bands, flags;
+    int32_t cfirst[6], recbase[6], nrec[6], pad0;
+    float* param;
+    const float* grad;
+    float* tbuf;
+    const float* rowtab;
+    const float* coltab;
+    const ModeStats* stats;
+    const double* gram;
+    const float* counts;
+    const void* hidx;
+    float *omega, *q_cos, *q_sin, *p_cos, *p_sin, *m_cos, *m_sin, *mp_cos, *mp_sin, *ca_cos, *ca_sin, *conf;
+    float *h_energy, *h_impulse, *h_refractory, *force_rms, *drive_energy, *surprise, *action;
+    TensorConsts* cst;
+    float* htab;
+    float* rowf;
+    float* colf;
+    float* rowpart;
+    float* colpart;
+    double* red[5];  // slices of reduction vectors 1..4 (index 0 unused)
+};
+
+// hparams indices (field order of cresso_hparams)
+enum HP {
+    H_LR, H_WD, H_EP, H_DT, H_IF, H_CG, H_REST, H_CUBIC, H_MDT, H_MF, H_MC, H_LS, H_IC, H_IP, H_RCM, H_EM, H_TM,
+    H_HD, H_HID, H_HMC, H_HDM, H_DFM, H_RFM, H_RD, H_REFD, H_RG, H_CD, H_CONFG, H_SG, H_SD, H_PM, H_NM, H_WS, H_SB,
+    H_TGT, H_MING, H_MAXG, H_CLIP, H_SPIKE, H_EPS, H_MAX, H_RANK, H_MAXF, H_BINS, H_TABLES, H_HARDMIN, H_THINCUT,
+    H_COUNT
+};
+static_assert(sizeof(cresso_hparams) == H_COUNT * sizeof(double), "cresso_hparams field order");
+
+__device__ __forceinline__ int gram_idx(int a, int b) { return a * 7 - (a * (a - 1)) / 2 + (b - a); }
+
+__device__ __forceinline__ int find_tensor(const int64_t* __restrict__ item_base, int n, int64_t item) {
+    int lo = 0, hi = n - 1;
+    while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (item_base[mid] <= item) lo = mid; else hi = mid - 1;
+    }
+    return lo;
+}
+
+__device__ __forceinline__ int load_bin(const void* hidx, int idx_bytes, int64_t stride, int t, int64_t gflat) {
+    if (idx_bytes == 1) return __ldg(reinterpret_cast<const uint8_t*>(hidx) + t * stride + gflat);
+    return __ldg(reinterpret_cast<const uint16_t*>(hidx) + t * stride + gflat);
+}
+
+__device__ __forceinline__ float sgnf(float x) { return x > 0.f ? 1.f : (x < 0.f ? -1.f : 0.f); }
+
+// Per-element drive components shared by P4 and P5 (cresso_v5.py:1315-1326).
+struct DriveParts {
+    float u, root, nov;
+};
+__device__ __forceinline__ DriveParts drive_parts(float t, float pred, const TensorConsts& c, float eps) {
+    DriveParts d;
+    const float at = fabsf(t);
+    const float rat = t / (1.0f + at * c.inv_clip);
+    const float bnd = tanhf(t * c.inv_clip) * c.clip;
+    d.root = sgnf(t) * sqrtf(fminf(at, c.clip2) + eps);
+    d.u = (1.0f - c.sp) * rat + c.sp * bnd;
+    d.nov = tanhf((t - pred) * c.invD) * c.clip;
+    return d;
+}
+
+// ---------------------------------------------------------------------------
+// Pass kernel
+// ---------------------------------------------------------------------------
+template <int PASS>
+struct PassOcc { static constexpr int v = PASS == 1 ? 4 : 2; };
+
+template <int PASS, int RM>
+__global__ void __launch_bounds__(kThreads, (RM > 8 ? 1 : PassOcc<PASS>::v))
+spectral_pass_kernel(const GroupHdr* __restrict__ hdr, const DevTensor* __restrict__ dts,
+                     const int64_t* __restrict__ item_base, double* __restrict__ rec_scal,
+                     float* __restrict__ rec_bins) {
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int64_t n_items = hdr->n_items;
+    const int nt = (int)hdr->n_tensors;
+    const int TB = (int)hdr->tb, B = (int)hdr->bins, T = (int)hdr->tables;
+    const int ITERS = (int)hdr->iters;
+    const int idx_bytes = (int)hdr->idx_bytes;
+    const float eps = (float)hdr->hp[H_EPS];
+    const int64_t it0 = (int64_t)blockIdx.x * n_items / gridDim.x;
+    const int64_t it1 = ((int64_t)blockIdx.x + 1) * n_items / gridDim.x;
+
+    // shared memory carve-up
+    constexpr bool kBins = PASS == 2 || PASS == 3;
+    constexpr bool kTab = PASS >= 3;
+    const int ncopies = kBins ? max(1, min(kWarps, kMaxTB / max(TB, 1))) : 0;
+    double* s_red = reinterpret_cast<double*>(smem_raw);             // kNSRec * kWarps
+    double* s_tot = s_red + kNSRec * kWarps;                         // kNSRec
+    float* s_f = reinterpret_cast<float*>(s_tot + kNSRec);
+    float* s_bins = s_f;                                             // ncopies * TB
+    float* s_tab = s_bins + (kBins ? ncopies * TB : 0);              // TB
+    float* s_rowred = s_tab + (kTab ? TB : 0);                       // 8 * ITERS
+    float* s_colred = s_rowred + (PASS == 2 ? 8 * ITERS : 0);        // 256
+
+    int k = find_tensor(item_base, nt, it0);
+    int64_t it = it0;
+    while (it < it1) {
+        const DevTensor& D = dts[k];
+        const TensorConsts& C = *D.cst;
+        const int64_t seg_end = min(it1, D.item_base + D.n_items);
+        const int flags = D.flags;
+        const bool hash_on = (flags & F_HASH) != 0;
+        // ---- segment set-up
+        if constexpr (kBins) {
+            for (int b = tid; b < ncopies * TB; b += kThreads) s_bins[b] = 0.0f;
+        }
+        if constexpr (kTab) {
+            if (hash_on)
+                for (int b = tid; b < TB; b += kThreads) s_tab[b] = D.htab[b];
+        }
+        __syncthreads();
+        float* my_bins = s_bins + (kBins ? (warp % max(ncopies, 1)) * TB : 0);
+
+        // per-thread segment accumulators
+        double acc0 = 0.0, acc1 = 0.0;                 // P1: sum f^2 | P2: sum L, sum d | P3: sum e^2, sum t
+        double Cp[RM], Sp[RM];                         // projection contractions (P2, P3)
+        double G[kGram];                               // P4 Gram
+        if constexpr (PASS == 2 || PASS == 3) {
+#pragma unroll
+            for (int q = 0; q < RM; ++q) Cp[q] = Sp[q] = 0.0;
+        }
+        if constexpr (PASS == 4) {
+#pragma unroll
+            for (int q = 0; q < kGram; ++q) G[q] = 0.0;
+        }
+
+        const float sgn = (flags & F_MAXIMIZE) ? -1.0f : 1.0f;
+        const float wd = (float)hdr->hp[H_WD];
+        const float inv_scale = C.inv_scale, scale = C.scale;
+        const int TC = D.TC, RPI = D.RPI;
+        const int lc = tid & (TC - 1), rs = tid / TC;
+
+        for (; it < seg_end; ++it) {
+            const int64_t local = it - D.item_base;
+            const int ct = (int)(local / D.n_bands);
+            const int band = (int)(local % D.n_bands);
+            const int64_t col = (int64_t)ct * TC + lc;
+            const bool cvalid = col < D.cols;
+            const int64_t gc = D.col0 + (cvalid ? col : 0);
+            const int64_t rbase = (int64_t)band * D.RB;
+
+            // column-dependent factors
+            float b1[RM], b2[RM];
+            float U1[RM], V1[RM], U2[RM], V2[RM];
+            float colf = 1.0f;
+            if constexpr (PASS >= 3) {
+                load_col<RM>(D.coltab, D.gcols, gc, b1, b2);
+                if constexpr (PASS == 3) {
+                    make_uv<RM>(b1, b2, C.m_al, C.m_be, U1, V1);
+                    make_uv<RM>(b1, b2, C.p0_al, C.p0_be, U2, V2);
+                    if (flags & F_INST2D) colf = D.colf[cvalid ? col : 0];
+                } else if constexpr (PASS == 4) {
+                    make_uv<RM>(b1, b2, C.pr_al, C.pr_be, U1, V1);
+                    make_uv<RM>(b1, b2, C.ec_al, C.ec_be, U2, V2);
+                } else {
+                    make_uv<RM>(b1, b2, C.pr_al, C.pr_be, U1, V1);
+                    make_uv<RM>(b1, b2, C.cb_al, C.cb_be, U2, V2);
+                }
+            }
+            float z1[RM], z2[RM];
+            if constexpr (PASS == 2 || PASS == 3) {
+#pragma unroll
+                for (int q = 0; q < RM; ++q) z1[q] = z2[q] = 0.0f;
+            }
+            float g32[kGram];
+            if constexpr (PASS == 4) {
+#pragma unroll
+                for (int q = 0; q < kGram; ++q) g32[q] = 0.0f;
+            }
+            float s0 = 0.0f, s1 = 0.0f, colacc = 0.0f;
+
+            for (int m = 0; m < ITERS; ++m) {
+                const int64_t r = rbase + rs + (int64_t)RPI * m;
+                const bool valid = cvalid && r < D.rows;
+                const int64_t e = r * D.cols + col;              // local element
+                const int64_t gr = D.row0 + (r < D.rows ? r : 0);
+                const int64_t gflat = gr * D.gcols + gc;         // global flat index (hash)
+                float dval = 0.0f;
+                if (valid) {
+                    if constexpr (PASS == 1) {
+                        float f = sgn * __ldg(D.grad + e);
+                        if (flags & F_WD) f = f + wd * D.param[e];
+                        s0 = fmaf(f, f, s0);
+                    } else if constexpr (PASS == 2) {
+                        float f = sgn * __ldg(D.grad + e);
+                        if (flags & F_WD) f = f + wd * D.param[e];
+                        float a1[RM], a2[RM];
+                        load_row<RM>(D.rowtab, gr, a1, a2);
+                        const float rel = fminf(fabsf(f) * inv_scale + eps, 1.0e4f);
+                        const float ds = powf(rel, (float)hdr->hp[H_EP]);
+                        const float L = log1pf(ds);
+                        const float ip = fmaxf((float)hdr->hp[H_IP], 0.25f);
+                        dval = (flags & F_IPOW1) ? rel : fminf(powf(fmaxf(rel, eps), ip), 1.0e6f);
+                        s0 += L;
+                        s1 += dval;
+                        colacc += dval;
+#pragma unroll
+                        for (int q = 0; q < RM; ++q) {
+                            z1[q] = fmaf(L, a1[q], z1[q]);
+                            z2[q] = fmaf(L, a2[q], z2[q]);
+                        }
+                        if (hash_on) {
+                            for (int t = 0; t < T; ++t)
+                                atomicAdd(&my_bins[t * B + load_bin(D.hidx, idx_bytes, D.hidx_n, t, gflat)], ds);
+                        }
+                    } else if constexpr (PASS == 3) {
+                        float f = sgn * __ldg(D.grad + e);
+                        if (flags & F_WD) f = f + wd * D.param[e];
+                        float a1[RM], a2[RM];
+                        load_row<RM>(D.rowtab, gr, a1, a2);
+                        const float rel = fminf(fabsf(f) * inv_scale + eps, 1.0e4f);
+                        const float lm = clampf(recon_dot<RM>(C.m_K, a1, a2, U1, V1), -3.0f, 3.0f);
+                        const float metric = clampf(expf((float)hdr->hp[H_MC] * lm), 0.06f, 16.0f);
+                        float den = scale * metric;
+                        if (flags & F_LOCAL)
+                            den = den * clampf(1.0f + (float)hdr->hp[H_LS] * sqrtf(fminf(rel, 100.0f)), 1.0f, 8.0f);
+                        if (flags & F_INST2D) {
+                            den = den * clampf(D.rowf[r] * colf, 0.08f, 12.0f);
+                        } else if (flags & F_INST1D) {
+                            const float ip = fmaxf((float)hdr->hp[H_IP], 0.25f);
+                            const float dd = (flags & F_IPOW1) ? rel : fminf(powf(fmaxf(rel, eps), ip), 1.0e6f);
+                            den = den * clampf(expf(C.inst_k * logf(fmaxf(dd / C.inst_gm, eps))), 0.08f, 12.0f);
+                        }
+                        int bidx[8];
+                        if (hash_on) {
+                            float lsum = 0.0f;
+                            for (int t = 0; t < T; ++t) {
+                                bidx[t & 7] = load_bin(D.hidx, idx_bytes, D.hidx_n, t, gflat);
+                                lsum += s_tab[t * B + bidx[t & 7]];
+                            }
+                            den = den * clampf(expf(lsum / (float)T), 0.08f, 12.0f);
+                        }
+                        den = den + eps;
+                        const float t = clampf(__fdiv_rn(f, den), -1.0e4f, 1.0e4f);
+                        D.tbuf[e] = t;
+                        const float pred = recon_dot<RM>(C.p0_K, a1, a2, U2, V2);
+                        const float err = t - pred;
+                        s0 = fmaf(err, err, s0);
+                        s1 += t;
+#pragma unroll
+                        for (int q = 0; q < RM; ++q) {
+                            z1[q] = fmaf(t, a1[q], z1[q]);
+                            z2[q] = fmaf(t, a2[q], z2[q]);
+                        }
+                        if (hash_on) {
+                            const float port = err + (float)hdr->hp[H_TM] * t;
+                            for (int t2 = 0; t2 < T; ++t2) {
+                                const int bb = t2 < 8 ? bidx[t2] : load_bin(D.hidx, idx_bytes, D.hidx_n, t2, gflat);
+                                atomicAdd(&my_bins[t2 * B + bb], port);
+                            }
+                        }
+                    } else if constexpr (PASS == 4) {
+                        float a1[RM], a2[RM];
+                        load_row<RM>(D.rowtab, gr, a1, a2);
+                        const float t = D.tbuf[e];
+                        const float pred = recon_dot<RM>(C.pr_K, a1, a2, U1, V1);
+                        const float echo = (flags & F_ECHO) ? recon_dot<RM>(C.ec_K, a1, a2, U2, V2) : 0.0f;
+                        float hpv = 0.0f;
+                        if (hash_on) {
+                            for (int t2 = 0; t2 < T; ++t2)
+                                hpv += s_tab[t2 * B + load_bin(D.hidx, idx_bytes, D.hidx_n, t2, gflat)];
+                            hpv = hpv / (float)T;
+                        }
+                        const DriveParts dp = drive_parts(t, pred, C, eps);
+                        const float rat = t / (1.0f + fabsf(t) * C.inv_clip);
+                        const float v[7] = {dp.u, dp.root, t, pred, dp.nov, echo, hpv};
+#pragma unroll
+                        for (int a = 0; a < 7; ++a)
+#pragma unroll
+                            for (int b = a; b < 7; ++b) g32[gram_idx(a, b)] = fmaf(v[a], v[b], g32[gram_idx(a, b)]);
+                        g32[28] = fmaf(rat, rat, g32[28]);
+                    } else {  // PASS 5
+                        float a1[RM], a2[RM];
+                        load_row<RM>(D.rowtab, gr, a1, a2);
+                        const float t = D.tbuf[e];
+                        const float pred = recon_dot<RM>(C.pr_K, a1, a2, U1, V1);
+                        const float comb = recon_dot<RM>(C.cb_K, a1, a2, U2, V2);
+                        float hpv = 0.0f;
+                        if (hash_on) {
+                            for (int t2 = 0; t2 < T; ++t2)
+                                hpv += s_tab[t2 * B + load_bin(D.hidx, idx_bytes, D.hidx_n, t2, gflat)];
+                            hpv = hpv / (float)T;
+                        }
+                        const DriveParts dp = drive_parts(t, pred, C, eps);
+                        const float drive = C.c_u * dp.u + C.c_root * dp.root + C.c_t * t + comb + C.c_nov * dp.nov +
+                                            C.c_hp * hpv;
+                        const float p = D.param[e];
+                        D.param[e] = p + C.neg_lr * (drive * C.gain);
+                    }
+                }
+                if constexpr (PASS == 2) {
+                    // row sums of the axis density: reduce across the TC lanes of the row
+                    float rsum = dval;
+                    const int w = min(TC, 32);
+                    for (int o = w >> 1; o > 0; o >>= 1) rsum += __shfl_xor_sync(0xffffffffu, rsum, o);
+                    if (TC <= 32) {
+                        if (lc == 0 && r < D.rows) D.rowpart[(int64_t)ct * D.rows + r] = rsum;
+                    } else if (lane == 0) {
+                        const int nw = TC >> 5;
+                        s_rowred[(rs + RPI * m) * nw + ((tid & (TC - 1)) >> 5)] = rsum;
+                    }
+                }
+            }  // rows of the item
+
+            // ---- item epilogue
+            if constexpr (PASS == 1) {
+                acc0 += (double)s0;
+            } else if constexpr (PASS == 2 || PASS == 3) {
+                acc0 += (double)s0;
+                acc1 += (double)s1;
+                if (cvalid) {
+                    if constexpr (PASS == 2) load_col<RM>(D.coltab, D.gcols, gc, b1, b2);
+                    contract_col<RM>(b1, b2, z1, z2, Cp, Sp);
+                }
+            } else if constexpr (PASS == 4) {
+#pragma unroll
+                for (int q = 0; q < kGram; ++q) G[q] += (double)g32[q];
+            }
+            if constexpr (PASS == 2) {
+                if (TC > 32) {
+                    __syncthreads();
+                    const int nw = TC >> 5;
+                    for (int lr = tid; lr < D.RB; lr += kThreads) {
+                        float s = 0.0f;
+                        for (int w = 0; w < nw; ++w) s += s_rowred[lr * nw + w];
+                        if (rbase + lr < D.rows) D.rowpart[(int64_t)ct * D.rows + rbase + lr] = s;
+                    }
+                }
+                // column sums: combine the RPI threads that share a column
+                s_colred[tid] = colacc;
+                __syncthreads();
+                if (rs == 0 && cvalid) {
+                    float s = 0.0f;
+                    for (int q = 0; q < RPI; ++q) s += s_colred[q * TC + lc];
+                    D.colpart[(int64_t)band * D.cols + col] = s;
+                }
+                __syncthreads();
+            }
+        }  // items of the segment
+
+        // ---- segment flush: one record per (block, tensor)
+        if constexpr (PASS <= 4) {
+            const int rec = D.recbase[PASS] + ((int)blockIdx.x - D.cfirst[PASS]);
+            if constexpr (PASS == 1) {
+                double v[1] = {acc0};
+                block_sum_to<1>(v, s_red, s_tot);
+                if (tid == 0) rec_scal[(int64_t)rec * kNSRec] = s_tot[0];
+            } else if constexpr (PASS == 4) {
+                block_sum_to<kGram>(G, s_red, s_tot);
+                for (int j = tid; j < kGram; j += kThreads) rec_scal[(int64_t)rec * kNSRec + j] = s_tot[j];
+            } else {
+                double v[2 + 2 * RM];
+                v[0] = acc0;
+                v[1] = acc1;
+#pragma unroll
+                for (int q = 0; q < RM; ++q) {
+                    v[2 + q] = Cp[q];
+                    v[2 + RM + q] = Sp[q];
+                }
+                block_sum_to<2 + 2 * RM>(v, s_red, s_tot);
+                for (int j = tid; j < 2 + 2 * RM; j += kThreads) rec_scal[(int64_t)rec * kNSRec + j] = s_tot[j];
+                if (hash_on) {
+                    for (int b = tid; b < TB; b += kThreads) {
+                        float s = 0.0f;
+                        for (int c = 0; c < ncopies; ++c) s += s_bins[c * TB + b];
+                        rec_bins[(int64_t)rec * TB + b] = s;
+                    }
+                }
+            }
+        }
+        __syncthreads();
+        ++k;
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Reduce: fixed-order sums of block records into the reduction vectors
+// ---------------------------------------------------------------------------
+__host__ __device__ inline int64_t red_len(int pass, int64_t rm, int64_t tb, int64_t cols, int ndim) {
+    switch (pass) {
+        case 1: return 1;
+        case 2: return 2 + 2 * rm + tb + (ndim == 2 ? cols : 0);
+        case 3: return 2 + 2 * rm + tb;
+        default: return kGram;
+    }
+}
+
+__global__ void reduce_kernel(int pass, const GroupHdr* __restrict__ hdr, const DevTensor* __restrict__ dts,
+                              const double* __restrict__ rec_scal, const float* __restrict__ rec_bins) {
+    const DevTensor& D = dts[blockIdx.y];
+    const int64_t rm = hdr->rm, tb = hdr->tb;
+    const int64_t len = red_len(pass, rm, tb, D.cols, D.ndim);
+    const int64_t ns = pass == 1 ? 1 : (pass == 4 ? kGram : 2 + 2 * rm);
+    const int64_t o = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (o >= len) return;
+    const int r0 = D.recbase[pass], nr = D.nrec[pass];
+    double s = 0.0;
+    if (o < ns) {
+        for (int r = 0; r < nr; ++r) s += rec_scal[(int64_t)(r0 + r) * kNSRec + o];
+    } else if (o < ns + tb) {
+        if (D.flags & F_HASH)
+            for (int r = 0; r < nr; ++r) s += (double)rec_bins[(int64_t)(r0 + r) * tb + (o - ns)];
+    } else {
+        const int64_t c = o - ns - tb;
+        for (int b = 0; b < D.n_bands; ++b) s += (double)D.colpart[(int64_t)b * D.cols + c];
+    }
+    D.red[pass][o] = s;
+}
+
+// ---------------------------------------------------------------------------
+// Finalize kernels (one block per tensor)
+// ---------------------------------------------------------------------------
+
+// Folds (alpha, beta) on the normalised carriers into inv-scaled coefficients
+// and the constant term; threads k < RM, result K valid for all threads.
+template <int RM>
+__device__ void fold_recon(const ModeStats* stats, int R, double alpha, double beta, float* al, float* be, float* K,
+                           double* s_red) {
+    const int k = threadIdx.x;
+    double kpart = 0.0;
+    if (k < RM) {
+        double a = 0.0, b = 0.0;
+        if (k < R) {
+            a = alpha * stats[k].inv_c;
+            b = beta * stats[k].inv_s;
+            kpart = -(a * stats[k].mu_c + b * stats[k].mu_s);
+        }
+        al[k] = (float)a;
+        be[k] = (float)b;
+    }
+    const double tot = block_sum(kpart, s_red);
+    if (threadIdx.x == 0) *K = (float)tot;
+}
+
+__device__ __forceinline__ float sigmoidf_(float x) { return 1.0f / (1.0f + expf(-x)); }
+
+template <int RM>
+__global__ void finalize1_kernel(const GroupHdr* __restrict__ hdr, const DevTensor* __restrict__ dts) {
+    const DevTensor& D = dts[blockIdx.x];
+    if (threadIdx.x != 0) return;
+    const double* hp = hdr->hp;
+    const float eps = (float)hp[H_EPS];
+    const float frn = sqrtf((float)(D.red[1][0] / (double)D.N) + eps);
+    const float fr = reservoir(*D.force_rms, frn, hp[H_RD], D.step);
+    *D.force_rms = fr;
+    const float scale = fmaxf(fr, eps);
+    D.cst->scale = scale;
+    D.cst->inv_scale = 1.0f / scale;
+}
+
+template <int RM>
+__global__ void finalize2_kernel(const GroupHdr* __restrict__ hdr, const DevTensor* __restrict__ dts) {
+    __shared__ double s_red[kWarps + 1];
+    __shared__ float s_meanE[64];
+    const DevTensor& D = dts[blockIdx.x];
+    TensorConsts& C = *D.cst;
+    const double* hp = hdr->hp;
+    const float eps = (float)hp[H_EPS];
+    const int tid = threadIdx.x;
+    const int R = D.R, B = (int)hdr->bins, T = (int)hdr->tables, TB = (int)hdr->tb;
+    const double N = (double)D.N;
+    const double* red = D.red[2];
+    const double sumL = red[0], sumd = red[1];
+    const int64_t rm = hdr->rm;
+
+    // ---- hash metric (cresso_v5.py:1013-1056)
+    if (D.flags & F_HASH) {
+        const double* bins = red + 2 + 2 * rm;
+        for (int tb = tid; tb < TB; tb += kThreads) {
+            const float cell = (float)bins[tb] / fmaxf(D.counts[tb], 1.0f);
+            D.h_energy[tb] = reservoir(D.h_energy[tb], cell, hp[H_HD], D.step);
+        }
+        __syncthreads();
+        for (int t = 0; t < T; ++t) {
+            double s = 0.0;
+            for (int b = tid; b < B; b += kThreads) s += (double)D.h_energy[t * B + b];
+            s = block_sum(s, s_red);
+            if (tid == 0) s_meanE[t & 63] = (float)(s / (double)B);
+            __syncthreads();
+            const float meanE = fmaxf(s_meanE[t & 63], eps);
+            const float ex = (float)(hp[H_HMC] / fmax(0.25, hp[H_EP]));
+            for (int b = tid; b < B; b += kThreads) {
+                const float hm = fmaxf(D.h_energy[t * B + b] / meanE, eps);
+                const float v = clampf(powf(hm, ex), 0.08f, 12.0f);
+                D.htab[t * B + b] = logf(fmaxf(v, eps));
+            }
+            __syncthreads();
+        }
+    }
+
+    // ---- spectral metric oscillator (cresso_v5.py:1057-1088)
+    const double shrink = recon_shrink(R);
+    const float M = fmaxf((float)(sumL / N), eps);
+    double m_alpha = 0.0, m_beta = 0.0, p_alpha = 0.0, p_beta = 0.0;
+    if (tid < R) {
+        const int k = tid;
+        const ModeStats st = D.stats[k];
+        const float pc = (float)((st.inv_c * (red[2 + k] - st.mu_c * sumL) / N) / (double)M - st.mhat_c);
+        const float ps = (float)((st.inv_s * (red[2 + rm + k] - st.mu_s * sumL) / N) / (double)M - st.mhat_s);
+        const float mdt = (float)hp[H_MDT];
+        const float damp = (float)fmax(0.0, 1.0 - hp[H_MDT] * hp[H_MF]);
+        const float om = D.omega[k];
+        const float om2 = om * om;
+        float mp = D.mp_cos[k] * damp;
+        float mq = D.m_cos[k];
+        mp = mp + mdt * (pc - om2 * mq);
+        mq = clampf(mq + mdt * mp, -3.0f, 3.0f);
+        D.mp_cos[k] = mp;
+        D.m_cos[k] = mq;
+        float mps = D.mp_sin[k] * damp;
+        float mqs = D.m_sin[k];
+        mps = mps + mdt * (ps - om2 * mqs);
+        mqs = clampf(mqs + mdt * mps, -3.0f, 3.0f);
+        D.mp_sin[k] = mps;
+        D.m_sin[k] = mqs;
+        m_alpha = (double)mq * shrink;
+        m_beta = (double)mqs * shrink;
+        // prediction from the old oscillators (cresso_v5.py:1128-1129)
+        const float gate = sigmoidf_((float)hp[H_CONFG] * D.conf[k]);
+        p_alpha = (double)D.q_cos[k] * shrink * (double)gate;
+        p_beta = (double)D.q_sin[k] * shrink * (double)gate;
+    }
+    if (tid < 2 * kMaxRank) C.pv[tid] = 0.0;
+    __syncthreads();
+    if (tid < R) {
+        C.pv[2 * tid] = p_alpha;
+        C.pv[2 * tid + 1] = p_beta;
+    }
+    fold_recon<RM>(D.stats, R, m_alpha, m_beta, C.m_al, C.m_be, &C.m_K, s_red);
+    fold_recon<RM>(D.stats, R, p_alpha, p_beta, C.p0_al, C.p0_be, &C.p0_K, s_red);
+
+    // ---- instant axial metric factors (cresso_v5.py:243-262, 1102-1122)
+    const float pw = fmaxf((float)hp[H_IP], 0.25f);
+    const float gmc = fmaxf((float)(sumd / N), eps);
+    if (D.flags & F_INST2D) {
+        const float kk = (float)(hp[H_IC] / (2.0 * (double)pw));
+        const int64_t grows = D.ndim == 2 ? (D.N / D.gcols) : 1;
+        for (int64_t r = tid; r < D.rows; r += kThreads) {
+            double s = 0.0;
+            for (int c = 0; c < D.n_ct; ++c) s += (double)D.rowpart[(int64_t)c * D.rows + r];
+            const float rmean = (float)(s / (double)D.gcols);
+            D.rowf[r] = expf(kk * logf(fmaxf(rmean / gmc, eps)));
+        }
+        const double* cols = red + 2 + 2 * rm + TB;
+        for (int64_t c = tid; c < D.cols; c += kThreads) {
+            const float cmean = (float)(cols[c] / (double)grows);
+            D.colf[c] = expf(kk * logf(fmaxf(cmean / gmc, eps)));
+        }
+    }
+    if (tid == 0) {
+        C.inst_k = (float)(hp[H_IC] / (double)pw);
+        C.inst_gm = gmc;
+    }
+}
+
+template <int RM>
+__global__ void finalize3_kernel(const GroupHdr* __restrict__ hdr, const DevTensor* __restrict__ dts) {
+    __shared__ double s_red[kWarps + 1];
+    __shared__ float s_S;
+    __shared__ float s_pc[kMaxRank], s_ps[kMaxRank];
+    const DevTensor& D = dts[blockIdx.x];
+    TensorConsts& C = *D.cst;
+    const double* hp = hdr->hp;
+    const float eps = (float)hp[H_EPS];
+    const int tid = threadIdx.x, lane = tid & 31;
+    const int R = D.R, TB = (int)hdr->tb;
+    const int64_t rm = hdr->rm;
+    const double N = (double)D.N;
+    const double* red = D.red[3];
+
+    // surprise (cresso_v5.py:1131-1133)
+    if (tid == 0) {
+        const float sn = sqrtf((float)(red[0] / N) + eps);
+        const float S = reservoir(*D.surprise, sn, hp[H_SD], D.step);
+        *D.surprise = S;
+        s_S = S;
+    }
+    __syncthreads();
+    const float S = s_S;
+    const double sumt = red[1];
+
+    // projections of t and of the port  (cresso_v5.py:1135-1138; port = (1+tm) t - pred)
+    double Pc = 0.0, Ps = 0.0;
+    if (tid < R) {
+        const int k = tid;
+        const ModeStats st = D.stats[k];
+        Pc = st.inv_c * (red[2 + k] - st.mu_c * sumt) / N;
+        Ps = st.inv_s * (red[2 + rm + k] - st.mu_s * sumt) / N;
+        double gvc = 0.0, gvs = 0.0;
+        const int P = 2 * (int)rm;
+        for (int y = 0; y < 2 * R; ++y) {
+            gvc += D.gram[(2 * k) * P + y] * C.pv[y];
+            gvs += D.gram[(2 * k + 1) * P + y] * C.pv[y];
+        }
+        const double tm1 = 1.0 + hp[H_TM];
+        s_pc[k] = (float)(tm1 * Pc - gvc);
+        s_ps[k] = (float)(tm1 * Ps - gvs);
+    }
+
+    // hash impulse reservoirs (cresso_v5.py:1140-1184)
+    if (D.flags & F_HASH) {
+        const double* bins = red + 2 + 2 * rm;
+        const float hd = (float)hp[H_HD], hd1 = (float)(1.0 - hp[H_HD]);
+        const float hid = (float)hp[H_HID], hid1 = (float)(1.0 - hp[H_HID]);
+        const float rg = (float)hp[H_RG];
+        for (int tb = tid; tb < TB; tb += kThreads) {
+            const float cell = (float)bins[tb] / fmaxf(D.counts[tb], 1.0f);
+            const float ref = D.h_refractory[tb] * hd + fabsf(cell) * hd1;
+            const float gate = 1.0f / (1.0f + rg * ref);
+            const float imp = D.h_impulse[tb] * hid + (cell * gate) * hid1;
+            D.h_refractory[tb] = ref;
+            D.h_impulse[tb] = imp;
+            D.htab[tb] = imp;
+        }
+    }
+    __syncthreads();
+
+    // confidence and the two contact half-updates run in warp 0, lane = mode
+    if (tid < 32) {
+        const bool act = lane < R;
+        const int k = act ? lane : 0;
+        const float pc = act ? s_pc[k] : 0.0f, ps = act ? s_ps[k] : 0.0f;
+        float qc = act ? D.q_cos[k] : 0.0f, qs = act ? D.q_sin[k] : 0.0f;
+        // confidence (cresso_v5.py:1199-1202), with the old q
+        if (act) {
+            const float pe = sqrtf(pc * pc + ps * ps + eps);
+            const float sup = (pc * qc + ps * qs) / (pe * sqrtf(qc * qc + qs * qs + eps) + eps);
+            const float cd = (float)hp[H_CD];
+            float cf = D.conf[k] * cd + clampf(sup, -1.0f, 1.0f) * (float)(1.0 - hp[H_CD]);
+            D.conf[k] = clampf(cf, -4.0f, 4.0f);
+        }
+        // contact oscillators (cresso_v5.py:914-943, 1204-1250)
+        const float dt = (float)hp[H_DT];
+        const float rd = (float)hp[H_REFD], rd1 = (float)(1.0 - hp[H_REFD]);
+        const float plast = 1.0f + (float)hp[H_SG] * S / (1.0f + S);
+        const float brake = 1.0f / (1.0f + (float)hp[H_SB] * S);
+        const float om = act ? D.omega[k] : 0.0f;
+        float action = *D.action;
+        for (int half = 0; half < 2; ++half) {
+            float* qp = half == 0 ? D.q_cos : D.q_sin;
+            float* pp = half == 0 ? D.p_cos : D.p_sin;
+            float* cp = half == 0 ? D.ca_cos : D.ca_sin;
+            const float port = half == 0 ? pc : ps;
+            float q = act ? qp[k] : 0.0f, p = act ? pp[k] : 0.0f, ca = act ? cp[k] : 0.0f;
+            ca = ca * rd + fabsf(port) * rd1;
+            const float rgate = 1.0f / (1.0f + (float)hp[H_RG] * ca);
+            const float gp = port * rgate * plast * brake;
+            const float omq = om * q;
+            const float e2 = warp_sum(act ? p * p : 0.0f) / (float)R;
+            const float w2 = warp_sum(act ? omq * omq : 0.0f) / (float)R;
+            const float energy = 0.5f * (e2 + w2);
+            const float ppow = warp_sum(act ? gp * p : 0.0f) / (float)R;
+            action = action * 0.985f + (ppow - energy) * dt;
+            const float fr = (float)hp[H_IF] + (float)hp[H_CG] * tanhf(fabsf(action));
+            p = p * fmaxf(1.0f - dt * fr, 0.0f);
+            p = p + dt * (gp - (float)hp[H_REST] * (om * om) * q - (float)hp[H_CUBIC] * (q * q * q));
+            q = clampf(q + dt * p, -8.0f, 8.0f);
+            if (act) {
+                qp[k] = q;
+                pp[k] = p;
+                cp[k] = ca;
+            }
+        }
+        if (lane == 0) *D.action = action;
+    }
+    __syncthreads();
+
+    // new prediction and echo coefficients (cresso_v5.py:1252-1258)
+    const double shrink = recon_shrink(R);
+    double pa = 0.0, pb = 0.0, ea = 0.0, eb = 0.0;
+    if (tid < R) {
+        const float gate = sigmoidf_((float)hp[H_CONFG] * D.conf[tid]);
+        pa = (double)D.q_cos[tid] * shrink * (double)gate;
+        pb = (double)D.q_sin[tid] * shrink * (double)gate;
+        ea = (double)(float)Pc * shrink;
+        eb = (double)(float)Ps * shrink;
+    }
+    fold_recon<RM>(D.stats, R, pa, pb, C.pr_al, C.pr_be, &C.pr_K, s_red);
+    fold_recon<RM>(D.stats, R, ea, eb, C.ec_al, C.ec_be, &C.ec_K, s_red);
+    if (tid == 0) {
+        const float clip = (float)hp[H_CLIP];
+        C.S = S;
+        C.sp = (float)hp[H_SPIKE] / (1.0f + S);
+        C.invD = 1.0f / (clip * (1.0f + S));
+        C.clip = clip;
+        C.inv_clip = 1.0f / clip;
+        C.clip2 = (float)(hp[H_CLIP] * hp[H_CLIP]);
+    }
+}
+
+template <int RM>
+__global__ void finalize4_kernel(const GroupHdr* __restrict__ hdr, const DevTensor* __restrict__ dts) {
+    __shared__ float s_cp, s_ce;
+    const DevTensor& D = dts[blockIdx.x];
+    TensorConsts& C = *D.cst;
+    const double* hp = hdr->hp;
+    if (threadIdx.x == 0) {
+        const float eps = (float)hp[H_EPS];
+        const double N = (double)D.N;
+        const double* g = D.red[4];
+        auto Gm = [&](int a, int b) { return a <= b ? g[gram_idx(a, b)] : g[gram_idx(b, a)]; };
+        enum { U = 0, RT = 1, TT = 2, PR = 3, NV = 4, EC = 5, HP = 6 };
+        const bool hard = (D.flags & F_HARD) != 0;
+        const float S = C.S;
+        // cresso_v5.py:1303-1346
+        const float frms = sqrtf((float)(Gm(TT, TT) / N) + eps);
+        const float prms = sqrtf((float)(Gm(PR, PR) / N) + eps);
+        const float align = clampf((float)(Gm(TT, PR) / N) / (frms * prms + eps), -1.0f, 1.0f);
+        const float align_gate = prms > (float)sqrt(hp[H_EPS]) ? clampf((align + 1.0f) * 0.5f, 0.0f, 1.0f) : 0.0f;
+        const int ws = (int)hp[H_WS];
+        const double warm = ws == 0 ? 1.0 : (1.0 - exp(-(double)D.step / (double)(ws > 1 ? ws : 1)));
+        const float mix = (float)(hp[H_PM] * warm) * align_gate * (1.0f / (1.0f + S));
+        const float rat_rms = sqrtf((float)(g[28] / N) + eps);
+        const float root_rms = sqrtf((float)(Gm(RT, RT) / N) + eps);
+        const float k_root = rat_rms / fmaxf(root_rms, eps);
+        const float root_mix = (hard ? (float)hp[H_RCM] : 0.0f) / (1.0f + 0.5f * S);
+        const double a = 1.0 - (double)root_mix, b = (double)root_mix * (double)k_root;
+        const double sh2 = a * a * Gm(U, U) + 2.0 * a * b * Gm(U, RT) + b * b * Gm(RT, RT);
+        const float shaped_rms = sqrtf((float)(sh2 / N) + eps);
+        const bool echo_on = (D.flags & F_ECHO) != 0, hash_on = (D.flags & F_HASH) != 0;
+        const float k_e = echo_on ? shaped_rms / fmaxf(sqrtf((float)(Gm(EC, EC) / N) + eps), eps) : 0.0f;
+        const float k_h = hash_on ? shaped_rms / fmaxf(sqrtf((float)(Gm(HP, HP) / N) + eps), eps) : 0.0f;
+        const float dm = (float)hp[H_DFM] / (1.0f + 0.35f * S);
+        const float k_d = shaped_rms / fmaxf(frms, eps);
+        const double cu = (1.0 - dm) * a, cr = (1.0 - dm) * b, ctt = (double)dm * k_d;
+        const double core2 = cu * cu * Gm(U, U) + cr * cr * Gm(RT, RT) + ctt * ctt * Gm(TT, TT) +
+                             2.0 * (cu * cr * Gm(U, RT) + cu * ctt * Gm(U, TT) + cr * ctt * Gm(RT, TT));
+        const float core_rms = sqrtf((float)(core2 / N) + eps);
+        const float resm = (float)hp[H_RFM] / (1.0f + S);
+        const double err2 = Gm(TT, TT) - 2.0 * Gm(TT, PR) + Gm(PR, PR);
+        const float k_r = core_rms / fmaxf(sqrtf((float)(fmax(err2, 0.0) / N) + eps), eps);
+        double c[7];
+        c[U] = (1.0 - mix) * cu;
+        c[RT] = (1.0 - mix) * cr;
+        c[TT] = (1.0 - mix) * ctt + (double)resm * k_r;
+        c[PR] = (double)mix - (double)resm * k_r;
+        c[NV] = hp[H_NM];
+        c[EC] = (hard ? hp[H_EM] : 0.0) * (double)k_e;
+        c[HP] = (hard ? hp[H_HDM] : 0.0) * (double)k_h;
+        double d2 = 0.0;
+        for (int i = 0; i < 7; ++i)
+            for (int j = 0; j < 7; ++j) d2 += c[i] * c[j] * Gm(i, j);
+        const float den = (float)(fmax(d2, 0.0) / N);
+        const float DE = reservoir(*D.drive_energy, den, hp[H_RD], D.step);
+        *D.drive_energy = DE;
+        const float gain = clampf((float)hp[H_TGT] / sqrtf(DE + eps), (float)hp[H_MING], (float)hp[H_MAXG]);
+        C.c_u = (float)c[U];
+        C.c_root = (float)c[RT];
+        C.c_t = (float)c[TT];
+        C.c_nov = (float)c[NV];
+        C.c_hp = (float)c[HP];
+        C.gain = gain;
+        C.neg_lr = (float)(-hp[H_LR]);
+        s_cp = (float)c[PR];
+        s_ce = (float)c[EC];
+    }
+    __syncthreads();
+    if (threadIdx.x < RM) {
+        const int k = threadIdx.x;
+        C.cb_al[k] = s_cp * C.pr_al[k] + s_ce * C.ec_al[k];
+        C.cb_be[k] = s_cp * C.pr_be[k] + s_ce * C.ec_be[k];
+    }
+    if (threadIdx.x == 0) C.cb_K = s_cp * C.pr_K + s_ce * C.ec_K;
+}
+
+// ---------------------------------------------------------------------------
+// Host plan
+// ---------------------------------------------------------------------------
+struct Plan {
+    GroupHdr hdr;
+    std::vector<DevTensor> dts;
+    std::vector<int64_t> item_base;
+    int64_t off_hdr, off_dts, off_items, off_cst, off_htab, off_rowf, off_colf, off_rowpart, off_colpart;
+    int64_t off_recs, off_recb, off_red[5], len_red[5], off_tbuf, bytes;
+    int64_t n_rec_max;
+    int rm;
+};
+
+static int64_t take(int64_t& off, int64_t bytes) {
+    const int64_t o = off;
+    off = align_up(off + bytes, 256);
+    return o;
+}
+
+static int hp_flags_hard(const cresso_tensor_desc& d, const cresso_hparams& hp, int64_t N) {
+    const int64_t cutoff = (int64_t)hp.thin_matrix_hard_cutoff;
+    bool thin = false;
+    if (d.ndim == 2 && cutoff > 0) thin = std::min(d.shape[0], d.shape[1]) <= cutoff;
+    return N >= (int64_t)hp.hard_channel_min_size && !thin;
+}
+
+static int build_plan(const cresso_tensor_desc* descs, int64_t n, const cresso_hparams* hp, int64_t num_sms, Plan& P) {
+    CRESSO_REQUIRE(descs != nullptr && hp != nullptr, CRESSO_EINVAL, "spectral: NULL descriptors or hparams");
+    CRESSO_REQUIRE(n >= 1, CRESSO_EINVAL, "spectral: need at least one tensor");
+    CRESSO_REQUIRE(num_sms >= 1, CRESSO_EINVAL, "spectral: num_sms must be >= 1");
+    const int64_t rank = (int64_t)hp->rank, bins = (int64_t)hp->hash_bins, tables = (int64_t)hp->hash_tables;
+    CRESSO_REQUIRE(rank >= 1 && rank <= kMaxRank, CRESSO_EUNSUPPORTED,
+                   "rank must be in [1, %d] on the CUDA spectral path (got %lld)", kMaxRank, (long long)rank);
+    CRESSO_REQUIRE(tables >= 1 && bins >= 0, CRESSO_EINVAL, "hash_tables must be >= 1, hash_bins >= 0");
+    CRESSO_REQUIRE(bins <= kMaxBins && bins * tables <= kMaxTB, CRESSO_EUNSUPPORTED,
+                   "hash_bins <= %d and hash_bins * hash_tables <= %d on the CUDA path", kMaxBins, kMaxTB);
+    const int rm = rank_pad(rank);
+    P.rm = rm;
+    memset(&P.hdr, 0, sizeof(P.hdr));
+    GroupHdr& H = P.hdr;
+    H.n_tensors = n;
+    H.rm = rm;
+    H.bins = bins;
+    H.tables = tables;
+    H.tb = bins * tables;
+    H.idx_bytes = bins <= 256 ? 1 : 2;
+    memcpy(H.hp, hp, sizeof(cresso_hparams));
+    P.dts.assign(n, DevTensor{});
+    P.item_base.assign(n + 1, 0);
+
+    // geometry and item counts; ITERS chosen so that the busiest pass has >= ~8 items per block
+    int64_t total_rows_work = 0;
+    for (int64_t i = 0; i < n; ++i) {
+        const cresso_tensor_desc& d = descs[i];
+        CRESSO_REQUIRE(d.ndim == 1 || d.ndim == 2, CRESSO_EUNSUPPORTED,
+                       "tensor %lld: spectral route supports 1-D and 2-D tensors on the CUDA path (ndim=%lld)",
+                       (long long)i, (long long)d.ndim);
+        CRESSO_REQUIRE(d.param && d.grad && d.shape_ws, CRESSO_EINVAL, "tensor %lld: NULL param / grad / workspace",
+                       (long long)i);
+        CRESSO_REQUIRE(d.rows >= 1 && d.cols >= 1 && d.row0 >= 0 && d.col0 >= 0, CRESSO_EINVAL,
+                       "tensor %lld: bad local block", (long long)i);
+        const int64_t grows = d.ndim == 2 ? d.shape[0] : 1;
+        const int64_t gcols = d.ndim == 2 ? d.shape[1] : d.shape[0];
+        CRESSO_REQUIRE(d.row0 + d.rows <= grows && d.col0 + d.cols <= gcols, CRESSO_EINVAL,
+                       "tensor %lld: local block outside the global shape", (long long)i);
+        CRESSO_REQUIRE(d.ndim == 1 || (d.col0 == 0 && d.cols == gcols), CRESSO_EUNSUPPORTED,
+                       "tensor %lld: 2-D tensors are sharded by rows only", (long long)i);
+        CRESSO_REQUIRE(d.step >= 1, CRESSO_EINVAL, "tensor %lld: step must be >= 1", (long long)i);
+        total_rows_work += d.rows * ceil_div(d.cols, 256);
+    }
+    int iters = 32;
+    const int64_t target_blocks = num_sms * 2;
+    while (iters > 4 && total_rows_work / iters < target_blocks * 8) iters >>= 1;
+    H.iters = iters;
+
+    int64_t items = 0;
+    for (int64_t i = 0; i < n; ++i) {
+        const cresso_tensor_desc& d = descs[i];
+        DevTensor& D = P.dts[i];
+        D.ndim = (int32_t)d.ndim;
+        D.rows = d.rows;
+        D.cols = d.cols;
+        D.row0 = d.row0;
+        D.col0 = d.col0;
+        D.gcols = d.ndim == 2 ? d.shape[1] : d.shape[0];
+        D.N = d.ndim == 2 ? d.shape[0] * d.shape[1] : d.shape[0];
+        D.step = d.step;
+        D.R = (int32_t)rank;
+        D.TC = std::min(256, pow2_ceil(d.cols));
+        D.RPI = 256 / D.TC;
+        D.RB = D.RPI * iters;
+        D.n_ct = (int32_t)ceil_div(d.cols, D.TC);
+        D.n_bands = (int32_t)ceil_div(d.rows, D.RB);
+        D.n_items = (int64_t)D.n_ct * D.n_bands;
+        D.item_base = items;
+        P.item_base[i] = items;
+        items += D.n_items;
+        const bool hard = hp_flags_hard(d, *hp, D.N);
+        int fl = 0;
+        if (hp->maximize != 0.0) fl |= F_MAXIMIZE;
+        if (hp->weight_decay != 0.0) fl |= F_WD;
+        if (hard) fl |= F_HARD;
+        const bool hash_on = hard && bins > 0 && d.hash_energy && d.hash_impulse && d.hash_refractory;
+        if (hash_on) {
+            fl |= F_HASH;
+            CRESSO_REQUIRE(d.hash_cache != 0 && d.hash_cache_n >= D.N, CRESSO_EINVAL,
+                           "tensor %lld: hash cache missing or smaller than the tensor", (long long)i);
+        }
+        if (hp->local_sharpness != 0.0) fl |= F_LOCAL;
+        if (hard && hp->echo_mix != 0.0) fl |= F_ECHO;
+        const double ic = hard ? hp->instant_metric_coupling : 0.0;
+        if (ic != 0.0 && D.N > 1) fl |= (d.ndim == 2 ? F_INST2D : F_INST1D);
+        if (fmax(hp->instant_metric_power, 0.25) == 1.0) fl |= F_IPOW1;
+        D.flags = fl;
+        // pointers into the caller's objects
+        const char* ws = (const char*)d.shape_ws;
+        ShapeWsHeader wh = shape_ws_layout(d.ndim, d.ndim == 2 ? d.shape[0] : 1, D.gcols, rank, rm, bins,
+                                           hash_on || bins > 0 ? tables : 0);
+        if (bins == 0) wh = shape_ws_layout(d.ndim, d.ndim == 2 ? d.shape[0] : 1, D.gcols, rank, rm, 0, 0);
+        D.rowtab = (const float*)(ws + wh.off_rowtab);
+        D.coltab = (const float*)(ws + wh.off_coltab);
+        D.stats = (const ModeStats*)(ws + wh.off_stats);
+        D.gram = (const double*)(ws + wh.off_gram);
+        D.counts = (const float*)(ws + wh.off_counts);
+        D.hidx = (const void*)d.hash_cache;
+        D.hidx_n = d.hash_cache_n;
+        D.param = (float*)d.param;
+        D.grad = (const float*)d.grad;
+        D.omega = (float*)d.omega;
+        D.q_cos = (float*)d.q_cos;
+        D.q_sin = (float*)d.q_sin;
+        D.p_cos = (float*)d.p_cos;
+        D.p_sin = (float*)d.p_sin;
+        D.m_cos = (float*)d.metric_cos;
+        D.m_sin = (float*)d.metric_sin;
+        D.mp_cos = (float*)d.metric_p_cos;
+        D.mp_sin = (float*)d.metric_p_sin;
+        D.ca_cos = (float*)d.calcium_cos;
+        D.ca_sin = (float*)d.calcium_sin;
+        D.conf = (float*)d.mode_confidence;
+        D.h_energy = (float*)d.hash_energy;
+        D.h_impulse = (float*)d.hash_impulse;
+        D.h_refractory = (float*)d.hash_refractory;
+        D.force_rms = (float*)d.force_rms;
+        D.drive_energy = (float*)d.drive_energy;
+        D.surprise = (float*)d.surprise;
+        D.action = (float*)d.action;
+        CRESSO_REQUIRE(D.omega && D.q_cos && D.q_sin && D.p_cos && D.p_sin && D.m_cos && D.m_sin && D.mp_cos &&
+                           D.mp_sin && D.ca_cos && D.ca_sin && D.conf && D.force_rms && D.drive_energy &&
+                           D.surprise && D.action,
+                       CRESSO_EINVAL, "tensor %lld: NULL state pointer", (long long)i);
+    }
+    P.item_base[n] = items;
+    H.n_items = items;
+    // blocks per pass and record placement (a record per (block, tensor) pair)
+    const int occ[6] = {0, 4, 2, 2, 2, 2};
+    P.n_rec_max = 0;
+    for (int p = 1; p <= 5; ++p) {
+        const int64_t g = std::max<int64_t>(1, std::min<int64_t>(items, num_sms * (rm > 8 ? 1 : occ[p])));
+        H.grid[p] = g;
+        int64_t rb = 0;
+        int64_t c = 0;
+        for (int64_t i = 0; i < n; ++i) {
+            DevTensor& D = P.dts[i];
+            const int64_t first = D.item_base, last = D.item_base + D.n_items - 1;
+            // block c owns items [c*items/g, (c+1)*items/g)
+            while ((c + 1) * items / g <= first) ++c;
+            int64_t c_last = c;
+            while ((c_last + 1) * items / g <= last) ++c_last;
+            D.cfirst[p] = (int32_t)c;
+            D.recbase[p] = (int32_t)rb;
+            D.nrec[p] = (int32_t)(c_last - c + 1);
+            rb += D.nrec[p];
+        }
+        P.n_rec_max = std::max(P.n_rec_max, rb);
+    }
+
+    // scratch layout
+    int64_t off = 0;
+    P.off_hdr = take(off, sizeof(GroupHdr));
+    P.off_dts = take(off, sizeof(DevTensor) * n);
+    P.off_items = take(off, sizeof(int64_t) * (n + 1));
+    P.off_cst = take(off, sizeof(TensorConsts) * n);
+    int64_t rows_tot = 0, cols_tot = 0, rowpart_tot = 0, colpart_tot = 0, elems = 0;
+    for (auto& D : P.dts) {
+        rows_tot += D.rows;
+        cols_tot += D.cols;
+        rowpart_tot += (int64_t)D.n_ct * D.rows;
+        colpart_tot += (int64_t)D.n_bands * D.cols;
+        elems += D.rows * D.cols;
+    }
+    P.off_htab = take(off, 4 * std::max<int64_t>(H.tb, 1) * n);
+    P.off_rowf = take(off, 4 * rows_tot);
+    P.off_colf = take(off, 4 * cols_tot);
+    P.off_rowpart = take(off, 4 * rowpart_tot);
+    P.off_colpart = take(off, 4 * colpart_tot);
+    P.off_recs = take(off, 8 * kNSRec * P.n_rec_max);
+    P.off_recb = take(off, 4 * std::max<int64_t>(H.tb, 1) * P.n_rec_max);
+    for (int p = 1; p <= 4; ++p) {
+        int64_t len = 0;
+        for (auto& D : P.dts) len += red_len(p, rm, H.tb, D.cols, D.ndim);
+        P.len_red[p] = len;
+        P.off_red[p] = take(off, 8 * len);
+    }
+    P.off_tbuf = take(off, 4 * elems);
+    P.bytes = off;
+    return CRESSO_OK;
+}
+
+static void bind_scratch(Plan& P, char* base) {
+    int64_t rows_o = 0, cols_o = 0, rowpart_o = 0, colpart_o = 0, elem_o = 0, red_o[5] = {0, 0, 0, 0, 0};
+    const int64_t tbs = std::max<int64_t>(P.hdr.tb, 1);
+    for (size_t i = 0; i < P.dts.size(); ++i) {
+        DevTensor& D = P.dts[i];
+        D.cst = reinterpret_cast<TensorConsts*>(base + P.off_cst) + i;
+        D.htab = reinterpret_cast<float*>(base + P.off_htab) + i * tbs;
+        D.rowf = reinterpret_cast<float*>(base + P.off_rowf) + rows_o;
+        D.colf = reinterpret_cast<float*>(base + P.off_colf) + cols_o;
+        D.rowpart = reinterpret_cast<float*>(base + P.off_rowpart) + rowpart_o;
+        D.colpart = reinterpret_cast<float*>(base + P.off_colpart) + colpart_o;
+        D.tbuf = reinterpret_cast<float*>(base + P.off_tbuf) + elem_o;
+        for (int p = 1; p <= 4; ++p) {
+            D.red[p] = reinterpret_cast<double*>(base + P.off_red[p]) + red_o[p];
+            red_o[p] += red_len(p, P.rm, P.hdr.tb, D.cols, D.ndim);
+        }
+        D.red[0] = nullptr;
+        rows_o += D.rows;
+        cols_o += D.cols;
+        rowpart_o += (int64_t)D.n_ct * D.rows;
+        colpart_o += (int64_t)D.n_bands * D.cols;
+        elem_o += D.rows * D.cols;
+    }
+}
+
+static size_t pass_smem(int pass, const GroupHdr& H) {
+    const int tb = (int)H.tb;
+    size_t b = (size_t)(kNSRec * kWarps + kNSRec) * sizeof(double);
+    if (pass == 2 || pass == 3) {
+        const int ncopies = std::max(1, std::min(kWarps, kMaxTB / std::max(tb, 1)));
+        b += (size_t)ncopies * tb * 4;
+    }
+    if (pass >= 3) b += (size_t)tb * 4;
+    if (pass == 2) b += (size_t)(8 * H.iters + kThreads) * 4;
+    return b;
+}
+
+template <int RM>
+static int launch_stage(int stage, const Plan& P, char* base, cudaStream_t s) {
+    const GroupHdr* hdr = reinterpret_cast<const GroupHdr*>(base + P.off_hdr);
+    const DevTensor* dts = reinterpret_cast<const DevTensor*>(base + P.off_dts);
+    const int64_t* items = reinterpret_cast<const int64_t*>(base + P.off_items);
+    double* recs = reinterpret_cast<double*>(base + P.off_recs);
+    float* recb = reinterpret_cast<float*>(base + P.off_recb);
+    const int n = (int)P.hdr.n_tensors;
+    auto run_pass = [&](auto kern, int pass) -> int {
+        const size_t smem = pass_smem(pass, P.hdr);
+        if (smem > 48 * 1024) CRESSO_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+        kern<<<(unsigned)P.hdr.grid[pass], kThreads, smem, s>>>(hdr, dts, items, recs, recb);
+        CRESSO_LAUNCHED("spectral_pass_kernel");
+        return CRESSO_OK;
+    };
+    auto run_reduce = [&](int pass) -> int {
+        int64_t maxlen = 0;
+        for (auto& D : P.dts) maxlen = std::max(maxlen, red_len(pass, P.rm, P.hdr.tb, D.cols, D.ndim));
+        dim3 grid((unsigned)ceil_div(maxlen, kThreads), (unsigned)n);
+        reduce_kernel<<<grid, kThreads, 0, s>>>(pass, hdr, dts, recs, recb);
+        CRESSO_LAUNCHED("reduce_kernel");
+        return CRESSO_OK;
+    };
+    int st = CRESSO_OK;
+    switch (stage) {
+        case 1:
+            if ((st = run_pass(spectral_pass_kernel<1, RM>, 1))) return st;
+            return run_reduce(1);
+        case 2:
+            finalize1_kernel<RM><<<n, kThreads, 0, s>>>(hdr, dts);
+            CRESSO_LAUNCHED("finalize1_kernel");
+            if ((st = run_pass(spectral_pass_kernel<2, RM>, 2))) return st;
+            return run_reduce(2);
+        case 3:
+            finalize2_kernel<RM><<<n, kThreads, 0, s>>>(hdr, dts);
+            CRESSO_LAUNCHED("finalize2_kernel");
+            if ((st = run_pass(spectral_pass_kernel<3, RM>, 3))) return st;
+            return run_reduce(3);
+        case 4:
+            finalize3_kernel<RM><<<n, kThreads, 0, s>>>(hdr, dts);
+            CRESSO_LAUNCHED("finalize3_kernel");
+            if ((st = run_pass(spectral_pass_kernel<4, RM>, 4))) return st;
+            return run_reduce(4);
+        case 5:
+            finalize4_kernel<RM><<<n, kThreads, 0, s>>>(hdr, dts);
+            CRESSO_LAUNCHED("finalize4_kernel");
+            return run_pass(spectral_pass_kernel<5, RM>, 5);
+        default:
+            return CRESSO_OK;
+    }
+}
+
+}  // namespace cresso
+
+using namespace cresso;
+
+extern "C" {
+
+int cresso_spectral_layout(const cresso_tensor_desc* descs, int64_t n, const cresso_hparams* hp, int64_t num_sms,
+                           int64_t* layout, int64_t layout_len) {
+    CRESSO_REQUIRE(layout != nullptr && layout_len >= 9, CRESSO_EINVAL, "spectral_layout: need a layout array of >= 9");
+    Plan P;
+    int st = build_plan(descs, n, hp, num_sms, P);
+    if (st) return st;
+    layout[0] = P.bytes;
+    for (int p = 1; p <= 4; ++p) {
+        layout[2 * p - 1] = P.off_red[p];
+        layout[2 * p] = P.len_red[p];
+    }
+    return CRESSO_OK;
+}
+
+int cresso_spectral_run(const cresso_tensor_desc* descs, int64_t n, const cresso_hparams* hp, void* scratch,
+                        int64_t scratch_bytes, int64_t stage_begin, int64_t stage_end, int64_t num_sms,
+                        cresso_stream_t stream) {
+    Plan P;
+    int st = build_plan(descs, n, hp, num_sms, P);
+    if (st) return st;
+    CRESSO_REQUIRE(scratch != nullptr, CRESSO_EINVAL, "spectral_run: NULL scratch");
+    CRESSO_REQUIRE(scratch_bytes >= P.bytes, CRESSO_ESCRATCH, "spectral_run: scratch of %lld bytes, need %lld",
+                   (long long)scratch_bytes, (long long)P.bytes);
+    CRESSO_REQUIRE(stage_begin >= 0 && stage_end <= 6 && stage_begin <= stage_end, CRESSO_EINVAL,
+                   "spectral_run: stages must satisfy 0 <= begin <= end <= 6");
+    char* base = (char*)scratch;
+    cudaStream_t s = (cudaStream_t)stream;
+    bind_scratch(P, base);
+    if (stage_begin == 0) {
+        CRESSO_CUDA(cudaMemcpyAsync(base + P.off_hdr, &P.hdr, sizeof(GroupHdr), cudaMemcpyHostToDevice, s));
+        CRESSO_CUDA(cudaMemcpyAsync(base + P.off_dts, P.dts.data(), sizeof(DevTensor) * n, cudaMemcpyHostToDevice, s));
+        CRESSO_CUDA(cudaMemcpyAsync(base + P.off_items, P.item_base.data(), sizeof(int64_t) * (n + 1),
+                                    cudaMemcpyHostToDevice, s));
+    }
+    for (int64_t stage = std::max<int64_t>(stage_begin, 1); stage < stage_end; ++stage) {
+        switch (P.rm) {
+            case 4: st = launch_stage<4>((int)stage, P, base, s); break;
+            case 8: st = launch_stage<8>((int)stage, P, base, s); break;
+            default: st = launch_stage<16>((int)stage, P, base, s); break;
+        }
+        if (st) return st;
+    }
+    if (stage_begin == 0) {
+        // the plan's host vectors are released on return: wait for their upload
+        CRESSO_CUDA(cudaStreamSynchronize(s));
+    }
+    return CRESSO_OK;
+}
+
+}  // extern "C"

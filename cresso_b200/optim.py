@@ -1,0 +1,415 @@
+"""CRESSO5 on B200: the drop-in optimizer class.
+
+``CRESSO5`` keeps the reference API of ``cresso_v5.CRESSO5``
+(cresso_v5.py:612-1585): the same constructor keywords, validation and
+``param_groups`` keys, ``step(closure=None)``, the persistent state layout
+(keys, shapes, dtypes; cresso_v5.py:857-891) and therefore
+``state_dict()`` / ``load_state_dict()`` compatibility in both directions.
+
+The step itself runs as fused sm_100a CUDA kernels through the C ABI of
+``libcresso_b200.so``: per parameter group and device, all spectral-route
+tensors go through one grouped five-pass step and all scalar-route tensors
+through one grouped launch.  There is no PyTorch fallback: ``cuda_ops`` accepts
+``"auto"`` / ``"required"`` / ``True`` and always means required; ``"off"`` /
+``False`` raise ``ValueError`` (the reference PyTorch path lives in the
+reference package).
+"""
+
+from __future__ import annotations
+
+from typing import Callable, Dict, Iterable, List, Optional, Tuple
+
+import numpy as np
+import torch
+from torch import Tensor
+from torch.optim import Optimizer
+
+from . import _lib
+from ._host import (
+    count_optimizer_state_elements,
+    frequencies_tensor,
+    hard_enabled,
+    multiscale_frequencies,
+    normalize_thin_matrix_route,
+    omega_from_freqs,
+    theoretical_state_elements,
+    uses_spectral_route,
+    validate_scalar,
+)
+
+__all__ = ["CRESSO5", "CRESSO", "count_optimizer_state_elements", "theoretical_state_elements"]
+
+_SPECTRAL_RANK_STATE = ("q_cos", "q_sin", "p_cos", "p_sin", "metric_cos", "metric_sin", "metric_p_cos",
+                        "metric_p_sin", "calcium_cos", "calcium_sin", "mode_confidence")
+
+
+class CRESSO5(Optimizer):
+    """Contact-Refractory Axial-Spectral Optimizer (B200-native step).
+
+    Large tensors evolve a compact contact-dissipative multiwave state
+    (rank-R spectral oscillators, T x B hash-cell reservoirs, four scalars);
+    LoRA-thin and small tensors use the scalar contact route.
+    """
+
+    def __init__(
+        self,
+        params: Iterable[Tensor],
+        lr: float = 2.0e-3,
+        rank: int = 8,
+        max_frequency: int = 5,
+        weight_decay: float = 0.0,
+        energy_power: float = 1.20,
+        dt: float = 0.15,
+        impulse_friction: float = 0.18,
+        contact_gain: float = 0.16,
+        restoring: float = 0.62,
+        cubic: float = 0.006,
+        metric_dt: float = 0.09,
+        metric_friction: float = 0.22,
+        metric_coupling: float = 0.36,
+        local_sharpness: float = 0.0,
+        instant_metric_coupling: float = 0.55,
+        instant_metric_power: float = 1.0,
+        root_channel_mix: float = 0.16,
+        echo_mix: float = 0.06,
+        transport_mix: float = 0.18,
+        hash_bins: int = 128,
+        hash_tables: int = 2,
+        hash_decay: float = 0.92,
+        hash_impulse_decay: float = 0.78,
+        hash_metric_coupling: float = 0.42,
+        hash_drive_mix: float = 0.22,
+        direct_force_mix: float = 0.18,
+        residual_feedback_mix: float = 0.06,
+        micro_field_max_size: int = 0,
+        micro_decay: float = 0.94,
+        micro_impulse_decay: float = 0.82,
+        micro_drive_mix: float = 0.35,
+        reservoir_decay: float = 0.95,
+        refractory_decay: float = 0.90,
+        refractory_gain: float = 0.55,
+        confidence_decay: float = 0.92,
+        confidence_gain: float = 0.50,
+        surprise_gain: float = 0.18,
+        surprise_decay: float = 0.95,
+        prediction_mix: float = 0.16,
+        novelty_mix: float = 0.04,
+        warmup_steps: int = 10,
+        surprise_brake: float = 0.18,
+        target_update_rms: float = 1.0,
+        min_gain: float = 0.04,
+        max_gain: float = 6.0,
+        drive_clip: float = 4.0,
+        spike_mix: float = 0.25,
+        min_spectral_size: int = 1024,
+        basis_cache_limit_elements: int = 2_000_000,
+        cuda_ops: str | bool = "auto",
+        hard_channel_min_size: int = 16,
+        thin_matrix_hard_cutoff: int = 8,
+        thin_matrix_max_width: int = 64,
+        thin_matrix_min_aspect: float = 4.0,
+        thin_matrix_route: str = "scalar",
+        maximize: bool = False,
+        eps: float = 1e-8,
+    ) -> None:
+        # Validation of cresso_v5.py:682-758.
+        for name, value, lower, upper in [
+            ("lr", lr, 0.0, None), ("weight_decay", weight_decay, 0.0, None),
+            ("energy_power", energy_power, 0.25, None), ("dt", dt, 0.0, 1.0),
+            ("impulse_friction", impulse_friction, 0.0, None), ("contact_gain", contact_gain, 0.0, None),
+            ("restoring", restoring, 0.0, None), ("cubic", cubic, 0.0, None), ("metric_dt", metric_dt, 0.0, 1.0),
+            ("metric_friction", metric_friction, 0.0, None), ("metric_coupling", metric_coupling, 0.0, None),
+            ("local_sharpness", local_sharpness, 0.0, None),
+            ("instant_metric_coupling", instant_metric_coupling, 0.0, None),
+            ("instant_metric_power", instant_metric_power, 0.25, None),
+            ("root_channel_mix", root_channel_mix, 0.0, 1.0), ("echo_mix", echo_mix, 0.0, 1.0),
+            ("transport_mix", transport_mix, 0.0, 1.0), ("hash_decay", hash_decay, 0.0, 1.0),
+            ("hash_impulse_decay", hash_impulse_decay, 0.0, 1.0),
+            ("hash_metric_coupling", hash_metric_coupling, 0.0, None), ("hash_drive_mix", hash_drive_mix, 0.0, 1.0),
+            ("direct_force_mix", direct_force_mix, 0.0, 1.0),
+            ("residual_feedback_mix", residual_feedback_mix, 0.0, 1.0), ("micro_decay", micro_decay, 0.0, 1.0),
+            ("micro_impulse_decay", micro_impulse_decay, 0.0, 1.0), ("micro_drive_mix", micro_drive_mix, 0.0, 1.0),
+            ("reservoir_decay", reservoir_decay, 0.0, 1.0), ("refractory_decay", refractory_decay, 0.0, 1.0),
+            ("refractory_gain", refractory_gain, 0.0, None), ("confidence_decay", confidence_decay, 0.0, 1.0),
+            ("confidence_gain", confidence_gain, 0.0, None), ("surprise_gain", surprise_gain, 0.0, None),
+            ("surprise_decay", surprise_decay, 0.0, 1.0), ("prediction_mix", prediction_mix, 0.0, 1.0),
+            ("novelty_mix", novelty_mix, 0.0, 1.0), ("surprise_brake", surprise_brake, 0.0, None),
+            ("target_update_rms", target_update_rms, 0.0, None), ("min_gain", min_gain, 0.0, None),
+            ("max_gain", max_gain, 0.0, None), ("drive_clip", drive_clip, 0.1, None),
+            ("spike_mix", spike_mix, 0.0, 1.0), ("eps", eps, 0.0, None),
+        ]:
+            validate_scalar(name, value, lower, upper)
+        if int(rank) < 0:
+            raise ValueError("rank must be non-negative")
+        if int(max_frequency) < 0:
+            raise ValueError("max_frequency must be non-negative")
+        if int(hash_bins) < 0:
+            raise ValueError("hash_bins must be non-negative")
+        if int(hash_tables) < 1:
+            raise ValueError("hash_tables must be >= 1")
+        if int(min_spectral_size) < 1:
+            raise ValueError("min_spectral_size must be >= 1")
+        if int(micro_field_max_size) < 0:
+            raise ValueError("micro_field_max_size must be >= 0")
+        if int(basis_cache_limit_elements) < 0:
+            raise ValueError("basis_cache_limit_elements must be >= 0")
+        if int(hard_channel_min_size) < 0:
+            raise ValueError("hard_channel_min_size must be >= 0")
+        if int(thin_matrix_hard_cutoff) < 0:
+            raise ValueError("thin_matrix_hard_cutoff must be >= 0")
+        if int(thin_matrix_max_width) < 0:
+            raise ValueError("thin_matrix_max_width must be >= 0")
+        validate_scalar("thin_matrix_min_aspect", thin_matrix_min_aspect, 1.0, None)
+        if int(warmup_steps) < 0:
+            raise ValueError("warmup_steps must be non-negative")
+        if min_gain > max_gain:
+            raise ValueError("min_gain must be <= max_gain")
+        route = normalize_thin_matrix_route(thin_matrix_route)
+        mode = ("auto" if cuda_ops else "off") if isinstance(cuda_ops, bool) else str(cuda_ops).lower()
+        if mode not in {"auto", "required", "off"}:
+            raise ValueError("cuda_ops must be one of 'auto', 'required', or 'off'")
+        if mode == "off":
+            raise ValueError(
+                "cresso_b200.CRESSO5 runs only the fused CUDA path; cuda_ops='off' selects the reference "
+                "PyTorch implementation (cresso_v5.CRESSO5), which this package does not contain")
+        defaults = dict(
+            lr=float(lr), rank=int(rank), max_frequency=int(max_frequency), weight_decay=float(weight_decay),
+            energy_power=float(energy_power), dt=float(dt), impulse_friction=float(impulse_friction),
+            contact_gain=float(contact_gain), restoring=float(restoring), cubic=float(cubic),
+            metric_dt=float(metric_dt), metric_friction=float(metric_friction),
+            metric_coupling=float(metric_coupling), local_sharpness=float(local_sharpness),
+            instant_metric_coupling=float(instant_metric_coupling),
+            instant_metric_power=float(instant_metric_power), root_channel_mix=float(root_channel_mix),
+            echo_mix=float(echo_mix), transport_mix=float(transport_mix), hash_bins=int(hash_bins),
+            hash_tables=int(hash_tables), hash_decay=float(hash_decay),
+            hash_impulse_decay=float(hash_impulse_decay), hash_metric_coupling=float(hash_metric_coupling),
+            hash_drive_mix=float(hash_drive_mix), direct_force_mix=float(direct_force_mix),
+            residual_feedback_mix=float(residual_feedback_mix), micro_field_max_size=int(micro_field_max_size),
+            micro_decay=float(micro_decay), micro_impulse_decay=float(micro_impulse_decay),
+            micro_drive_mix=float(micro_drive_mix), reservoir_decay=float(reservoir_decay),
+            refractory_decay=float(refractory_decay), refractory_gain=float(refractory_gain),
+            confidence_decay=float(confidence_decay), confidence_gain=float(confidence_gain),
+            surprise_gain=float(surprise_gain), surprise_decay=float(surprise_decay),
+            prediction_mix=float(prediction_mix), novelty_mix=float(novelty_mix), warmup_steps=int(warmup_steps),
+            surprise_brake=float(surprise_brake), target_update_rms=float(target_update_rms),
+            min_gain=float(min_gain), max_gain=float(max_gain), drive_clip=float(drive_clip),
+            spike_mix=float(spike_mix), min_spectral_size=int(min_spectral_size),
+            basis_cache_limit_elements=int(basis_cache_limit_elements), cuda_ops=mode,
+            hard_channel_min_size=int(hard_channel_min_size), thin_matrix_hard_cutoff=int(thin_matrix_hard_cutoff),
+            thin_matrix_max_width=int(thin_matrix_max_width), thin_matrix_min_aspect=float(thin_matrix_min_aspect),
+            thin_matrix_route=route, maximize=bool(maximize), eps=float(eps),
+        )
+        super().__init__(params, defaults)
+        self._shape_ws: Dict[tuple, Tensor] = {}
+        self._hash_cache: Dict[tuple, Tuple[Tensor, int]] = {}
+        self._scratch: Dict[tuple, Tensor] = {}
+
+    # ------------------------------------------------------------------ state
+    def _init_common(self, state: dict, device, dtype) -> None:
+        """cresso_v5.py:857-862."""
+        state["step"] = 0
+        state["force_rms"] = torch.zeros((), device=device, dtype=dtype)
+        state["drive_energy"] = torch.ones((), device=device, dtype=dtype)
+        state["surprise"] = torch.zeros((), device=device, dtype=dtype)
+        state["action"] = torch.zeros((), device=device, dtype=dtype)
+
+    def _init_spectral(self, param: Tensor, group: dict, dtype) -> None:
+        """cresso_v5.py:864-883 (same keys, shapes and dtypes)."""
+        state = self.state[param]
+        self._init_common(state, param.device, dtype)
+        rank = int(group["rank"])
+        freqs = frequencies_tensor(rank, param.ndim, int(group["max_frequency"]), param.device)
+        state["freqs"] = freqs
+        state["omega"] = omega_from_freqs(freqs).to(device=param.device, dtype=dtype)
+        for name in _SPECTRAL_RANK_STATE:
+            state[name] = torch.zeros(rank, device=param.device, dtype=dtype)
+        bins = int(group.get("hash_bins", 0))
+        tables = int(group.get("hash_tables", 1))
+        cutoff = int(group.get("thin_matrix_hard_cutoff", 0))
+        thin = param.ndim == 2 and cutoff > 0 and min(param.shape) <= cutoff
+        if bins > 0 and param.numel() >= int(group.get("hard_channel_min_size", 0)) and not thin:
+            state["hash_energy"] = torch.ones(tables, bins, device=param.device, dtype=dtype)
+            state["hash_impulse"] = torch.zeros(tables, bins, device=param.device, dtype=dtype)
+            state["hash_refractory"] = torch.zeros(tables, bins, device=param.device, dtype=dtype)
+
+    def _init_scalar(self, param: Tensor, dtype) -> None:
+        """cresso_v5.py:885-891."""
+        state = self.state[param]
+        self._init_common(state, param.device, dtype)
+        for name in ("q", "impulse", "metric_q", "metric_impulse"):
+            state[name] = torch.zeros((), device=param.device, dtype=dtype)
+
+    def _use_spectral_route(self, param: Tensor, group: dict) -> bool:
+        return uses_spectral_route(tuple(param.shape), group)
+
+    # ------------------------------------------------------------- caches
+    def _workspace(self, device, shape: tuple, group: dict, freqs: Tensor) -> Tensor:
+        """Per-shape carrier tables / stats / Gram / hash counts, kept across steps
+        (a transient cache, never part of the state; cresso_v5.py:380-415)."""
+        rank, maxf = int(group["rank"]), int(group["max_frequency"])
+        bins, tables = int(group["hash_bins"]), int(group["hash_tables"])
+        if bins <= 0:
+            bins, tables = 0, 0
+        key = (device, shape, rank, maxf, bins, tables)
+        ws = self._shape_ws.get(key)
+        if ws is not None:
+            return ws
+        L = _lib.lib()
+        dims = _lib.i64_array(shape)
+        nbytes = np.zeros(1, dtype=np.int64)
+        _lib.check(L.cresso_shape_workspace_bytes(len(shape), dims, rank, bins, tables,
+                                                  nbytes.ctypes.data_as(_lib._pi64)), "shape_workspace_bytes")
+        ws = torch.empty(int(nbytes[0]), dtype=torch.uint8, device=device)
+        fr = np.ascontiguousarray(np.asarray(multiscale_frequencies(rank, len(shape), maxf), dtype=np.int64))
+        stored = freqs.detach().to("cpu", torch.int64).numpy()
+        if stored.shape != fr.shape or not np.array_equal(stored, fr):
+            raise RuntimeError("state['freqs'] differs from the deterministic CRESSO5 frequency pack")
+        stream = torch.cuda.current_stream(device).cuda_stream
+        _lib.check(L.cresso_shape_workspace_init(len(shape), dims, rank, fr.ctypes.data_as(_lib._pi64), bins, tables,
+                                                 _lib.ptr(ws), stream), "shape_workspace_init")
+        self._shape_ws[key] = ws
+        return ws
+
+    def _hash_index_cache(self, device, bins: int, tables: int, n: int) -> Tuple[Tensor, int]:
+        key = (device, bins, tables)
+        cur = self._hash_cache.get(key)
+        if cur is not None and cur[1] >= n:
+            return cur
+        L = _lib.lib()
+        cap = max(n, cur[1] * 2 if cur is not None else 0)
+        nbytes = np.zeros(1, dtype=np.int64)
+        _lib.check(L.cresso_hash_cache_bytes(cap, bins, tables, nbytes.ctypes.data_as(_lib._pi64)), "hash_cache_bytes")
+        buf = torch.empty(int(nbytes[0]), dtype=torch.uint8, device=device)
+        stream = torch.cuda.current_stream(device).cuda_stream
+        _lib.check(L.cresso_hash_cache_init(cap, bins, tables, _lib.ptr(buf), stream), "hash_cache_init")
+        self._hash_cache[key] = (buf, cap)
+        return self._hash_cache[key]
+
+    def _scratch_buffer(self, device, kind: str, nbytes: int) -> Tensor:
+        key = (device, kind)
+        buf = self._scratch.get(key)
+        if buf is None or buf.numel() < nbytes:
+            buf = torch.empty(max(int(nbytes), 256), dtype=torch.uint8, device=device)
+            self._scratch[key] = buf
+        return buf
+
+    # --------------------------------------------------------------- step
+    @torch.no_grad()
+    def step(self, closure: Optional[Callable] = None):  # type: ignore[override]
+        loss = None
+        if closure is not None:
+            with torch.enable_grad():
+                loss = closure()
+        for group in self.param_groups:
+            spectral: Dict[torch.device, list] = {}
+            scalar: Dict[torch.device, list] = {}
+            for param in group["params"]:
+                if param.grad is None or not torch.is_floating_point(param):
+                    continue
+                grad = param.grad.detach()
+                if grad.is_sparse:
+                    raise RuntimeError("CRESSO5 does not support sparse gradients")
+                if not param.is_cuda:
+                    raise RuntimeError(
+                        "CRESSO5 cuda_ops='required' requires every optimized parameter to be a CUDA parameter")
+                micro = int(group.get("micro_field_max_size", 0))
+                if micro > 0 and param.ndim > 0 and param.numel() <= micro:
+                    raise RuntimeError("CRESSO5 micro-field route (micro_field_max_size > 0) is not available on "
+                                       "the B200 CUDA path")
+                if param.dtype != torch.float32:
+                    raise RuntimeError(f"CRESSO5 B200 path supports float32 parameters (got {param.dtype})")
+                if not param.is_contiguous():
+                    raise RuntimeError("CRESSO5 B200 path updates parameters in place and needs them contiguous")
+                if grad.dtype != param.dtype or grad.device != param.device:
+                    raise RuntimeError("CRESSO5: grad must match its parameter's dtype and device")
+                if not grad.is_contiguous():
+                    grad = grad.contiguous()
+                state = self.state[param]
+                if self._use_spectral_route(param, group):
+                    if len(state) == 0:
+                        self._init_spectral(param, group, torch.float32)
+                    state["step"] += 1
+                    spectral.setdefault(param.device, []).append((param, grad, state))
+                else:
+                    if len(state) == 0:
+                        self._init_scalar(param, torch.float32)
+                    state["step"] += 1
+                    scalar.setdefault(param.device, []).append((param, grad, state))
+            hp = None
+            for device, items in spectral.items():
+                hp = _lib.pack_hparams(group) if hp is None else hp
+                self._run_spectral(group, hp, device, items)
+            for device, items in scalar.items():
+                hp = _lib.pack_hparams(group) if hp is None else hp
+                self._run_scalar(hp, device, items)
+        return loss
+
+    def _spectral_descs(self, group: dict, device, items: list) -> np.ndarray:
+        F = _lib.DESC_INDEX
+        descs = _lib.new_descs(len(items))
+        bins, tables = int(group["hash_bins"]), int(group["hash_tables"])
+        for i, (p, g, st) in enumerate(items):
+            shape = tuple(int(d) for d in p.shape)
+            d = descs[i]
+            d[F["ndim"]] = len(shape)
+            for a, s in enumerate(shape):
+                d[F["shape0"] + a] = s
+            d[F["row0"]] = 0
+            d[F["col0"]] = 0
+            d[F["rows"]] = shape[0] if len(shape) == 2 else 1
+            d[F["cols"]] = shape[-1]
+            d[F["step"]] = int(st["step"])
+            d[F["param"]] = p.data_ptr()
+            d[F["grad"]] = g.data_ptr()
+            d[F["shape_ws"]] = self._workspace(device, shape, group, st["freqs"]).data_ptr()
+            if "hash_energy" in st and bins > 0 and hard_enabled(shape, group):
+                buf, cap = self._hash_index_cache(device, bins, tables, p.numel())
+                d[F["hash_cache"]] = buf.data_ptr()
+                d[F["hash_cache_n"]] = cap
+                for name in ("hash_energy", "hash_impulse", "hash_refractory"):
+                    d[F[name]] = st[name].data_ptr()
+            for name in ("omega",) + _SPECTRAL_RANK_STATE + ("force_rms", "drive_energy", "surprise", "action"):
+                d[F[name]] = st[name].data_ptr()
+        return descs
+
+    def _run_spectral(self, group: dict, hp: np.ndarray, device, items: list) -> None:
+        if int(group["rank"]) > _lib.MAX_RANK:
+            raise RuntimeError(f"CRESSO5 B200 path supports rank <= {_lib.MAX_RANK} (got {group['rank']})")
+        L = _lib.lib()
+        descs = self._spectral_descs(group, device, items)
+        n = len(items)
+        num_sms = torch.cuda.get_device_properties(device).multi_processor_count
+        layout = np.zeros(9, dtype=np.int64)
+        _lib.check(L.cresso_spectral_layout(_lib.ptr(descs), n, _lib.ptr(hp), num_sms,
+                                            layout.ctypes.data_as(_lib._pi64), 9), "spectral_layout")
+        scratch = self._scratch_buffer(device, "spectral", int(layout[0]))
+        stream = torch.cuda.current_stream(device).cuda_stream
+        _lib.check(L.cresso_spectral_run(_lib.ptr(descs), n, _lib.ptr(hp), _lib.ptr(scratch), scratch.numel(), 0, 6,
+                                         num_sms, stream), "spectral_run")
+
+    def _run_scalar(self, hp: np.ndarray, device, items: list) -> None:
+        L = _lib.lib()
+        F = _lib.DESC_INDEX
+        descs = _lib.new_descs(len(items))
+        for i, (p, g, st) in enumerate(items):
+            d = descs[i]
+            d[F["ndim"]] = p.ndim
+            for a, s in enumerate(p.shape):
+                d[F["shape0"] + a] = int(s)
+            d[F["step"]] = int(st["step"])
+            d[F["param"]] = p.data_ptr()
+            d[F["grad"]] = g.data_ptr()
+            for name in ("force_rms", "drive_energy", "surprise", "action", "q", "impulse", "metric_q",
+                         "metric_impulse"):
+                d[F[name]] = st[name].data_ptr()
+        n = len(items)
+        nbytes = np.zeros(1, dtype=np.int64)
+        _lib.check(L.cresso_scalar_scratch_bytes(_lib.ptr(descs), n, nbytes.ctypes.data_as(_lib._pi64)),
+                   "scalar_scratch_bytes")
+        scratch = self._scratch_buffer(device, "scalar", int(nbytes[0]))
+        stream = torch.cuda.current_stream(device).cuda_stream
+        _lib.check(L.cresso_scalar_run(_lib.ptr(descs), n, _lib.ptr(hp), _lib.ptr(scratch), scratch.numel(), stream),
+                   "scalar_run")
+
+
+CRESSO = CRESSO5

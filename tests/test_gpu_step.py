@@ -1,0 +1,216 @@
+"""Full-step parity of the CUDA path (reference test_cresso_v5_cuda_ops.py:64-211
+widened): every golden case of tests/golden (outputs of the reference itself),
+multi-step runs at the benchmark shapes against the oracle, determinism and
+state_dict round trips.
+
+Tolerances (stated per check):
+* parameters: relative RMS of (p_cuda - p_ref) over RMS(p_ref) <= 1e-5, and of
+  the accumulated update (p - p0) <= 2e-4 of its own RMS;
+* every state tensor: relative RMS <= 2x the float32 reference's own distance
+  to a float64 run of the same reference arithmetic, plus 1e-5 (the reference
+  is float32; some states, e.g. metric_cos, sit on cancelling projections and
+  carry ~1e-4 float32 noise);
+* hash bins are integer work and bit-exact (tested in test_gpu_ops.py).
+"""
+
+import numpy as np
+import pytest
+import torch
+
+import cresso_b200
+from oracle import cresso5_oracle as O
+from tests._cases import case_inputs, golden_cases, rel_rms
+
+pytestmark = pytest.mark.gpu
+
+CASES = golden_cases()
+
+
+def run_cuda(shape, kw, init, grads):
+    p = torch.nn.Parameter(init.clone().cuda())
+    opt = cresso_b200.CRESSO5([p], cuda_ops="required", **kw)
+    for g in grads:
+        p.grad = g.clone().cuda()
+        opt.step()
+    torch.cuda.synchronize()
+    return p.detach().cpu(), {k: (v.detach().cpu() if torch.is_tensor(v) else v) for k, v in opt.state[p].items()}, opt
+
+
+def run_oracle(kw, init, grads, dtype=torch.float32, device="cpu"):
+    p = torch.nn.Parameter(init.clone().to(device=device, dtype=dtype))
+    opt = O.OracleCRESSO5([p], **kw)
+    for g in grads:
+        p.grad = g.clone().to(device=device, dtype=dtype)
+        opt.step()
+    return p.detach().cpu(), {k: (v.detach().cpu() if torch.is_tensor(v) else v) for k, v in opt.state[p].items()}
+
+
+def check_against(name, init, p, st, p_ref, st_ref, p64, st64, upd_tol=2e-4):
+    errs = {}
+    errs["param"] = rel_rms(p, p_ref)
+    errs["update"] = rel_rms(p - init, p_ref - init)
+    assert errs["param"] <= 1e-5, (name, errs)
+    assert errs["update"] <= upd_tol, (name, errs)
+    for k, v in st_ref.items():
+        if not torch.is_tensor(v):
+            assert st[k] == v, (name, k)
+            continue
+        if v.dtype == torch.int64:
+            assert torch.equal(st[k], v), (name, k)
+            continue
+        noise = rel_rms(st_ref[k].double(), st64[k].double())
+        e = rel_rms(st[k].double(), v.double())
+        errs[k] = (e, noise)
+        assert e <= 2.0 * noise + 1e-5, (name, k, e, noise)
+    return errs
+
+
+@pytest.mark.parametrize("name", list(CASES.keys()))
+def test_golden_case_parity(golden, name):
+    shape, kw, steps, seed, istd, gstd = CASES[name]
+    init, grads = case_inputs(golden, name, shape, steps, seed, istd, gstd)
+    p, st, opt = run_cuda(shape, kw, init, grads)
+    p_ref = torch.from_numpy(golden[f"step_{name}_final"])
+    st_ref = {k[len(f"step_{name}_state_"):]: golden[k] for k in golden if k.startswith(f"step_{name}_state_")
+              and k != f"step_{name}_state_elements"}
+    st_ref = {k: (torch.from_numpy(v) if v.ndim > 0 or v.dtype.kind == "f" else int(v)) for k, v in st_ref.items()}
+    p64, st64 = run_oracle(kw, init, grads, torch.float64)
+    check_against(name, init, p, st, p_ref, st_ref, p64, st64)
+    assert set(st.keys()) == set(st_ref.keys())
+    assert cresso_b200.count_optimizer_state_elements(opt) == int(golden[f"step_{name}_state_elements"])
+
+
+def _bench_inputs(cfg, steps):
+    g = torch.Generator().manual_seed(0)
+    if cfg == "c1":
+        shapes = [(2048, 2048)]
+        kw = dict(lr=2e-3, rank=8, max_frequency=5, hash_bins=64, hash_tables=2)
+        istd = 0.02
+    elif cfg == "c2":
+        shapes = [(4096, 4096)]
+        kw = dict(lr=2e-3, rank=8, max_frequency=5, hash_bins=64, hash_tables=2)
+        istd = 0.02
+    else:  # c3: 64 LoRA-like thin params
+        shapes = [(4096, 16) if i % 2 == 0 else (16, 4096) for i in range(64)]
+        kw = dict(lr=2e-3, rank=4, hash_bins=64, hash_tables=2)
+        istd = 0.01
+    inits = [torch.randn(s, generator=g) * istd for s in shapes]
+    row_scale = None
+    if cfg == "c2":
+        row_scale = torch.exp(0.5 * torch.randn((4096, 1), generator=torch.Generator().manual_seed(7)))
+    grads = []
+    for step in range(steps):
+        gg = torch.Generator().manual_seed(1000 + step)
+        gs = []
+        for s in shapes:
+            x = torch.randn(s, generator=gg) * 1e-3
+            if row_scale is not None:
+                x = x * row_scale
+            gs.append(x)
+        grads.append(gs)
+    return shapes, kw, inits, grads
+
+
+@pytest.mark.parametrize("cfg", ["c1", "c2", "c3"])
+def test_benchmark_config_ten_steps(cfg):
+    steps = 10
+    shapes, kw, inits, grads = _bench_inputs(cfg, steps)
+    dev = torch.device("cuda")
+    ps = [torch.nn.Parameter(x.clone().to(dev)) for x in inits]
+    opt = cresso_b200.CRESSO5(ps, cuda_ops="required", **kw)
+    refs32 = [torch.nn.Parameter(x.clone().to(dev)) for x in inits]
+    ref32 = O.OracleCRESSO5(refs32, **kw)
+    refs64 = [torch.nn.Parameter(x.clone().to(dev, torch.float64)) for x in inits]
+    ref64 = O.OracleCRESSO5(refs64, **kw)
+    for gs in grads:
+        for p, r, r64, g in zip(ps, refs32, refs64, gs):
+            g = g.to(dev)
+            p.grad = g.clone()
+            r.grad = g.clone()
+            r64.grad = g.double()
+        opt.step()
+        ref32.step()
+        ref64.step()
+    torch.cuda.synchronize()
+    for i, (p, r, r64, x0) in enumerate(zip(ps, refs32, refs64, inits)):
+        st = {k: (v.cpu() if torch.is_tensor(v) else v) for k, v in opt.state[p].items()}
+        st32 = {k: (v.cpu() if torch.is_tensor(v) else v) for k, v in ref32.state[r].items()}
+        st64 = {k: (v.cpu() if torch.is_tensor(v) else v) for k, v in ref64.state[r64].items()}
+        check_against(f"{cfg}[{i}]", x0, p.detach().cpu(), st, r.detach().cpu(), st32, r64.detach().cpu(), st64,
+                      upd_tol=5e-4)
+        if i >= 3:
+            break
+
+
+def test_run_to_run_deterministic():
+    shapes, kw, inits, grads = _bench_inputs("c1", 3)
+    outs = []
+    for _ in range(2):
+        p = torch.nn.Parameter(inits[0].clone().cuda())
+        opt = cresso_b200.CRESSO5([p], **kw)
+        for gs in grads:
+            p.grad = gs[0].cuda()
+            opt.step()
+        outs.append((p.detach().cpu(), {k: v.cpu() for k, v in opt.state[p].items() if torch.is_tensor(v)}))
+    assert torch.equal(outs[0][0], outs[1][0])
+    for k in outs[0][1]:
+        assert torch.equal(outs[0][1][k], outs[1][1][k]), k
+
+
+def test_state_dict_round_trip_with_oracle_layout():
+    """A CUDA state_dict loads into the oracle (reference layout) and the two
+    continue in step; and back."""
+    shapes, kw, inits, grads = _bench_inputs("c1", 4)
+    x0 = inits[0][:256, :256].contiguous()
+    gs = [g[0][:256, :256].contiguous() for g in grads]
+    p = torch.nn.Parameter(x0.clone().cuda())
+    opt = cresso_b200.CRESSO5([p], **kw)
+    for g in gs[:2]:
+        p.grad = g.cuda()
+        opt.step()
+    sd = opt.state_dict()
+    assert set(sd["state"][0].keys()) >= {"step", "freqs", "omega", "q_cos", "hash_energy", "force_rms"}
+    # a fresh CUDA optimizer continues identically after load_state_dict
+    p2 = torch.nn.Parameter(p.detach().clone())
+    opt2 = cresso_b200.CRESSO5([p2], **kw)
+    opt2.load_state_dict(sd)
+    for g in gs[2:]:
+        p.grad = g.cuda()
+        p2.grad = g.cuda()
+        opt.step()
+        opt2.step()
+    assert torch.equal(p.detach(), p2.detach())
+    # the oracle accepts the same state (reference keys / shapes / dtypes) and continues close by
+    pr = torch.nn.Parameter(p.detach().clone().cpu())
+    ref = O.OracleCRESSO5([pr], **kw)
+    ref.state[pr] = {k: (v.detach().cpu().clone() if torch.is_tensor(v) else v) for k, v in opt.state[p].items()}
+    g = torch.randn((256, 256), generator=torch.Generator().manual_seed(5)) * 1e-3
+    p.grad = g.cuda()
+    pr.grad = g.clone()
+    opt.step()
+    ref.step()
+    assert rel_rms(p.detach().cpu(), pr.detach()) <= 1e-5
+
+
+def test_mixed_routes_in_one_group():
+    """Spectral 2-D, spectral 1-D, LoRA-thin and small tensors in one param group."""
+    g = torch.Generator().manual_seed(1)
+    shapes = [(300, 200), (4096,), (512, 16), (16, 512), (7, 9), (100,), (), (3, 4, 5)]
+    inits = [torch.randn(s, generator=g) * 0.02 for s in shapes]
+    grads = [[torch.randn(s, generator=g) * 1e-3 for s in shapes] for _ in range(3)]
+    kw = dict(rank=8, hash_bins=64, hash_tables=2)
+    ps = [torch.nn.Parameter(x.clone().cuda()) for x in inits]
+    rs = [torch.nn.Parameter(x.clone()) for x in inits]
+    opt = cresso_b200.CRESSO5(ps, **kw)
+    ref = O.OracleCRESSO5(rs, **kw)
+    for gs in grads:
+        for p, r, gg in zip(ps, rs, gs):
+            p.grad = gg.cuda()
+            r.grad = gg.clone()
+        opt.step()
+        ref.step()
+    for p, r, s in zip(ps, rs, shapes):
+        assert rel_rms(p.detach().cpu(), r.detach()) <= 1e-5, s
+        for k, v in ref.state[r].items():
+            if torch.is_tensor(v) and v.dtype.is_floating_point:
+                assert rel_rms(opt.state[p][k].cpu(), v) <= 5e-3, (s, k)
