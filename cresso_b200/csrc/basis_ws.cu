@@ -186,19 +186,32 @@ struct Term {
     int p, q;
 };
 
-// Separable terms of raw basis function X = 2k + comp (comp 0 cos, 1 sin).
+// Separable terms of raw basis function X = 2k + comp (comp 0 cos, 1 sin):
+// raw_X(i, j) = sum_t c_t * rowtab_{p_t}(i) * coltab_{q_t}(j).
 __device__ int basis_terms(int X, Term* t) {
-    const int k = X >> 1, comp = X & 1;
+    const int k = X >> 1;
+    const int c0 = 2 * k, s0 = 2 * k + 1;
     if (mode_is_product(k)) {
-        t[0] = comp == 0 ? Term{1.0, 2 * k, 2 * k} : Term{1.0, 2 * k + 1, 2 * k + 1};
+        const int p = (X & 1) ? s0 : c0;
+        t[0].c = 1.0;
+        t[0].p = p;
+        t[0].q = p;
         return 1;
     }
-    if (comp == 0) {
-        t[0] = Term{1.0, 2 * k, 2 * k};
-        t[1] = Term{-1.0, 2 * k + 1, 2 * k + 1};
-    } else {
-        t[0] = Term{1.0, 2 * k, 2 * k + 1};
-        t[1] = Term{1.0, 2 * k + 1, 2 * k};
+    if ((X & 1) == 0) {  // a1 b1 - a2 b2
+        t[0].c = 1.0;
+        t[0].p = c0;
+        t[0].q = c0;
+        t[1].c = -1.0;
+        t[1].p = s0;
+        t[1].q = s0;
+    } else {  // a1 b2 + a2 b1
+        t[0].c = 1.0;
+        t[0].p = c0;
+        t[0].q = s0;
+        t[1].c = 1.0;
+        t[1].p = s0;
+        t[1].q = c0;
     }
     return 2;
 }

@@ -6,12 +6,15 @@ state_dict round trips.
 Tolerances (stated per check):
 * parameters: relative RMS of (p_cuda - p_ref) over RMS(p_ref) <= 1e-5, and of
   the accumulated update (p - p0) <= 2e-4 of its own RMS;
-* every state tensor: relative RMS <= 2x the float32 reference's own distance
-  to a float64 run of the same reference arithmetic, plus 1e-5 (the reference
-  is float32; some states, e.g. metric_cos, sit on cancelling projections and
-  carry ~1e-4 float32 noise);
+* every state tensor: relative RMS distance to a float64 run of the reference
+  arithmetic <= 2x the float32 reference's own distance to it, plus 1e-5, and
+  distance to the float32 reference <= 3x that plus 1e-5 (the reference is
+  float32; some states, e.g. metric_cos, sit on cancelling projections and
+  carry ~1e-5..1e-4 float32 noise);
 * hash bins are integer work and bit-exact (tested in test_gpu_ops.py).
 """
+
+import copy
 
 import numpy as np
 import pytest
@@ -59,9 +62,14 @@ def check_against(name, init, p, st, p_ref, st_ref, p64, st64, upd_tol=2e-4):
             assert torch.equal(st[k], v), (name, k)
             continue
         noise = rel_rms(st_ref[k].double(), st64[k].double())
-        e = rel_rms(st[k].double(), v.double())
-        errs[k] = (e, noise)
-        assert e <= 2.0 * noise + 1e-5, (name, k, e, noise)
+        e32 = rel_rms(st[k].double(), v.double())
+        e64 = rel_rms(st[k].double(), st64[k].double())
+        errs[k] = (e32, e64, noise)
+        # at least as close to the float64 truth as twice the float32 reference's own error,
+        # and therefore within 3x that error of the float32 reference
+        assert e64 <= 2.0 * noise + 1e-5, (name, k, e64, noise)
+        assert e32 <= 3.0 * noise + 1e-5, (name, k, e32, noise)
+    print(name, {k: (tuple(round(x, 9) for x in v) if isinstance(v, tuple) else round(v, 9)) for k, v in errs.items()})
     return errs
 
 
@@ -173,7 +181,7 @@ def test_state_dict_round_trip_with_oracle_layout():
     # a fresh CUDA optimizer continues identically after load_state_dict
     p2 = torch.nn.Parameter(p.detach().clone())
     opt2 = cresso_b200.CRESSO5([p2], **kw)
-    opt2.load_state_dict(sd)
+    opt2.load_state_dict(copy.deepcopy(sd))  # torch's load_state_dict keeps the tensors it is given
     for g in gs[2:]:
         p.grad = g.cuda()
         p2.grad = g.cuda()
