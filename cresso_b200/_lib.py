@@ -31,6 +31,9 @@ HPARAM_FIELDS = (
 
 MAX_NDIM = 8
 MAX_RANK = 16
+SPECTRAL_STAGES = 14
+# stage boundaries after which reduction vector k (1..4) is complete
+REDUCTION_BOUNDARIES = (3, 6, 9, 12)
 
 # Field order of cresso_tensor_desc; every field is 8 bytes.
 DESC_FIELDS = (
@@ -46,7 +49,7 @@ DESC_WORDS = len(DESC_FIELDS)
 STATUS = {0: "ok", 1: "invalid argument", 2: "unsupported on the CUDA path", 3: "CUDA error", 4: "scratch too small"}
 
 EXPORTS = (
-    "cresso_version", "cresso_arch", "cresso_last_error", "cresso_abi_layout",
+    "cresso_version", "cresso_arch", "cresso_last_error", "cresso_abi_layout", "cresso_launch_count",
     "cresso_hash_index", "cresso_hash_reduce_mean", "cresso_hash_gather", "cresso_hash_cache_bytes",
     "cresso_hash_cache_init", "cresso_shape_workspace_bytes", "cresso_shape_workspace_init",
     "cresso_basis_project", "cresso_basis_reconstruct", "cresso_instant_axis_metric",
@@ -69,6 +72,7 @@ def _declare(lib) -> None:
         "cresso_arch": (ctypes.c_char_p, []),
         "cresso_last_error": (ctypes.c_int, [ctypes.c_char_p, ctypes.c_size_t]),
         "cresso_abi_layout": (ctypes.c_int, [_pi64, ctypes.c_int]),
+        "cresso_launch_count": (ctypes.c_int64, []),
         "cresso_hash_index": (ctypes.c_int, [_i64, _i64, _i64, _i64, _p, _p]),
         "cresso_hash_reduce_mean": (ctypes.c_int, [_p, _i64, _i64, _i64, _p, _p]),
         "cresso_hash_gather": (ctypes.c_int, [_p, _i64, _i64, _i64, _p, _p]),
@@ -115,6 +119,11 @@ def lib():
             raise RuntimeError(f"cresso_b200 CUDA library failed to load: {exc}") from exc
         _lib = handle
         return _lib
+
+
+def launch_count() -> int:
+    """Kernels launched by the library in this process so far."""
+    return int(lib().cresso_launch_count())
 
 
 def last_error() -> str:

@@ -5,11 +5,14 @@
 #include <stdio.h>
 #include <string.h>
 
+#include <atomic>
+
 #include "cresso_status.h"
 
 namespace cresso {
 
 static thread_local char g_last_error[1024] = {0};
+static std::atomic<int64_t> g_launches{0};
 
 int set_error(int code, const char* fmt, ...) {
     va_list ap;
@@ -26,7 +29,10 @@ int check_cuda(cudaError_t e, const char* what) {
 
 int check_launch(const char* what) {
     const cudaError_t e = cudaGetLastError();
-    if (e == cudaSuccess) return CRESSO_OK;
+    if (e == cudaSuccess) {
+        g_launches.fetch_add(1, std::memory_order_relaxed);
+        return CRESSO_OK;
+    }
     return set_error(CRESSO_ECUDA, "launch of %s failed: %s (%s)", what, cudaGetErrorName(e), cudaGetErrorString(e));
 }
 
@@ -47,6 +53,8 @@ int cresso_last_error(char* buf, size_t n) {
     }
     return (int)len;
 }
+
+int64_t cresso_launch_count(void) { return cresso::g_launches.load(std::memory_order_relaxed); }
 
 int cresso_abi_layout(int64_t* out, int n) {
     if (out == nullptr || n < 4) return cresso::set_error(CRESSO_EINVAL, "abi_layout: need an array of >= 4");

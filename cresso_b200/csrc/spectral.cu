@@ -32,6 +32,7 @@
 
 namespace cresso {
 
+constexpr int kStages = 14;  // see launch_stage
 constexpr int kNSRec = 36;  // float64 scalars per block record (>= 2 + 2 * kMaxRank, >= 29)
 constexpr int kGram = 29;   // 28 pair sums of (u, root, t, pred, nov, echo, hp) + sum rat^2
 
@@ -1085,6 +1086,9 @@ static size_t pass_smem(int pass, const GroupHdr& H) {
     return b;
 }
 
+// Kernel-granularity stages of a spectral group step:
+//   0 upload | 1 P1  2 R1 | 3 F1  4 P2  5 R2 | 6 F2  7 P3  8 R3 | 9 F3  10 P4  11 R4 | 12 F4  13 P5
+// Reduction vector k (1..4) is complete after stage 3k - 1.
 template <int RM>
 static int launch_stage(int stage, const Plan& P, char* base, cudaStream_t s) {
     const GroupHdr* hdr = reinterpret_cast<const GroupHdr*>(base + P.off_hdr);
@@ -1108,32 +1112,33 @@ static int launch_stage(int stage, const Plan& P, char* base, cudaStream_t s) {
         CRESSO_LAUNCHED("reduce_kernel");
         return CRESSO_OK;
     };
-    int st = CRESSO_OK;
     switch (stage) {
-        case 1:
-            if ((st = run_pass(spectral_pass_kernel<1, RM>, 1))) return st;
-            return run_reduce(1);
-        case 2:
+        case 1: return run_pass(spectral_pass_kernel<1, RM>, 1);
+        case 2: return run_reduce(1);
+        case 3:
             finalize1_kernel<RM><<<n, kThreads, 0, s>>>(hdr, dts);
             CRESSO_LAUNCHED("finalize1_kernel");
-            if ((st = run_pass(spectral_pass_kernel<2, RM>, 2))) return st;
-            return run_reduce(2);
-        case 3:
+            return CRESSO_OK;
+        case 4: return run_pass(spectral_pass_kernel<2, RM>, 2);
+        case 5: return run_reduce(2);
+        case 6:
             finalize2_kernel<RM><<<n, kThreads, 0, s>>>(hdr, dts);
             CRESSO_LAUNCHED("finalize2_kernel");
-            if ((st = run_pass(spectral_pass_kernel<3, RM>, 3))) return st;
-            return run_reduce(3);
-        case 4:
+            return CRESSO_OK;
+        case 7: return run_pass(spectral_pass_kernel<3, RM>, 3);
+        case 8: return run_reduce(3);
+        case 9:
             finalize3_kernel<RM><<<n, kThreads, 0, s>>>(hdr, dts);
             CRESSO_LAUNCHED("finalize3_kernel");
-            if ((st = run_pass(spectral_pass_kernel<4, RM>, 4))) return st;
-            return run_reduce(4);
-        case 5:
+            return CRESSO_OK;
+        case 10: return run_pass(spectral_pass_kernel<4, RM>, 4);
+        case 11: return run_reduce(4);
+        case 12:
             finalize4_kernel<RM><<<n, kThreads, 0, s>>>(hdr, dts);
             CRESSO_LAUNCHED("finalize4_kernel");
-            return run_pass(spectral_pass_kernel<5, RM>, 5);
-        default:
             return CRESSO_OK;
+        case 13: return run_pass(spectral_pass_kernel<5, RM>, 5);
+        default: return CRESSO_OK;
     }
 }
 
@@ -1166,8 +1171,8 @@ int cresso_spectral_run(const cresso_tensor_desc* descs, int64_t n, const cresso
     CRESSO_REQUIRE(scratch != nullptr, CRESSO_EINVAL, "spectral_run: NULL scratch");
     CRESSO_REQUIRE(scratch_bytes >= P.bytes, CRESSO_ESCRATCH, "spectral_run: scratch of %lld bytes, need %lld",
                    (long long)scratch_bytes, (long long)P.bytes);
-    CRESSO_REQUIRE(stage_begin >= 0 && stage_end <= 6 && stage_begin <= stage_end, CRESSO_EINVAL,
-                   "spectral_run: stages must satisfy 0 <= begin <= end <= 6");
+    CRESSO_REQUIRE(stage_begin >= 0 && stage_end <= kStages && stage_begin <= stage_end, CRESSO_EINVAL,
+                   "spectral_run: stages must satisfy 0 <= begin <= end <= %d", kStages);
     char* base = (char*)scratch;
     cudaStream_t s = (cudaStream_t)stream;
     bind_scratch(P, base);
@@ -1185,10 +1190,8 @@ int cresso_spectral_run(const cresso_tensor_desc* descs, int64_t n, const cresso
         }
         if (st) return st;
     }
-    if (stage_begin == 0) {
-        // the plan's host vectors are released on return: wait for their upload
-        CRESSO_CUDA(cudaStreamSynchronize(s));
-    }
+    // The upload reads pageable host memory, which cudaMemcpyAsync stages
+    // before returning, so the plan's host vectors may be released here.
     return CRESSO_OK;
 }
 

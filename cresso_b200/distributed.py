@@ -1,0 +1,155 @@
+"""Multi-GPU CRESSO5: one process per GPU, ``torch.distributed`` over NCCL.
+
+The reference is single-GPU (it has no collective anywhere).  Two ways of
+spreading one optimizer step over the GPUs of a box are provided:
+
+``RowShardedCRESSO5`` (row sharding)
+    Every rank holds a contiguous row block of each large 2-D tensor and a
+    contiguous element range of each large 1-D tensor (mark the local blocks
+    with ``mark_row_shard`` / ``shard_rows``), i.e. the FSDP layout.  The fused
+    step runs locally; between its passes the per-tensor partial sums (force
+    energy; density / hash-bin / projection / column sums; error, projection
+    and port-bin sums; the drive Gram) are SUM-all-reduced as one float64
+    vector per pass, four small all-reduces per step for all tensors together.
+    Every rank then holds identical rank / hash / scalar state, and updates its
+    own rows.  Hash indices and carrier coordinates use global indices, so the
+    result equals the single-GPU step up to the float64 summation order.
+    Small and LoRA-thin (scalar-route) tensors are passed whole and stepped
+    redundantly on every rank.
+
+``ZeroCRESSO5`` (ZeRO-1 partition)
+    Whole tensors are assigned to ranks by a longest-processing-time greedy
+    partition on element counts.  A rank steps only the tensors it owns (no
+    collective during the step) and the updated tensors are then
+    all-gathered, so every rank ends with the full updated parameters.
+"""
+
+from __future__ import annotations
+
+from typing import Dict, Iterable, List, Optional, Sequence, Tuple
+
+import torch
+import torch.distributed as dist
+from torch import Tensor
+
+from . import _lib
+from .optim import CRESSO5
+
+
+def mark_row_shard(param: Tensor, global_shape: Sequence[int], offset: int) -> Tensor:
+    """Declares `param` to be the block of a larger tensor of `global_shape`
+    that starts at global row `offset` (2-D) or element `offset` (1-D)."""
+    param._cresso_shard = (tuple(int(d) for d in global_shape), int(offset))
+    return param
+
+
+def row_block(length: int, rank: int, world: int) -> Tuple[int, int]:
+    """[start, stop) of rank's contiguous block of `length` rows, sizes differing by at most one."""
+    base, extra = divmod(int(length), int(world))
+    start = rank * base + min(rank, extra)
+    return start, start + base + (1 if rank < extra else 0)
+
+
+def shard_rows(full: Tensor, rank: int, world: int) -> Tuple[Tensor, int]:
+    """This rank's block of `full` (rows of a 2-D, elements of a 1-D tensor) and its offset."""
+    start, stop = row_block(full.shape[0], rank, world)
+    return full[start:stop].contiguous(), start
+
+
+def lpt_partition(sizes: Sequence[int], world: int) -> List[int]:
+    """Owner rank of each item: largest first onto the least-loaded rank
+    (ties to the lowest rank), a deterministic greedy LPT schedule."""
+    order = sorted(range(len(sizes)), key=lambda i: (-int(sizes[i]), i))
+    load = [0] * int(world)
+    owner = [0] * len(sizes)
+    for i in order:
+        r = min(range(int(world)), key=lambda j: (load[j], j))
+        owner[i] = r
+        load[r] += int(sizes[i])
+    return owner
+
+
+class RowShardedCRESSO5(CRESSO5):
+    """CRESSO5 over row-sharded tensors with one float64 all-reduce per pass."""
+
+    def __init__(self, params: Iterable[Tensor], process_group=None, **kwargs):
+        super().__init__(params, **kwargs)
+        self.process_group = process_group
+
+    def _world(self) -> int:
+        if not dist.is_available() or not dist.is_initialized():
+            return 1
+        return dist.get_world_size(self.process_group)
+
+    def _spectral_stages(self, run, scratch: Tensor, layout) -> None:
+        if self._world() == 1:
+            run(0, _lib.SPECTRAL_STAGES)
+            return
+        begin = 0
+        for k, end in enumerate(_lib.REDUCTION_BOUNDARIES, start=1):
+            run(begin, end)
+            dist.all_reduce(self._reduction_view(scratch, layout, k), op=dist.ReduceOp.SUM, group=self.process_group)
+            begin = end
+        run(begin, _lib.SPECTRAL_STAGES)
+
+
+class ZeroCRESSO5(CRESSO5):
+    """ZeRO-1 style CRESSO5: each rank steps the whole tensors it owns, then
+    the updated parameters are all-gathered."""
+
+    def __init__(self, params: Iterable[Tensor], process_group=None, **kwargs):
+        super().__init__(params, **kwargs)
+        self.process_group = process_group
+        world = dist.get_world_size(process_group) if dist.is_initialized() else 1
+        self.rank = dist.get_rank(process_group) if dist.is_initialized() else 0
+        self.world = world
+        all_params = [p for g in self.param_groups for p in g["params"]]
+        self.owner: Dict[Tensor, int] = {}
+        for p, r in zip(all_params, lpt_partition([p.numel() for p in all_params], world)):
+            self.owner[p] = r
+
+    @torch.no_grad()
+    def step(self, closure=None):  # type: ignore[override]
+        hidden = []
+        for g in self.param_groups:
+            for p in g["params"]:
+                if self.owner[p] != self.rank and p.grad is not None:
+                    hidden.append((p, p.grad))
+                    p.grad = None
+        try:
+            loss = super().step(closure)
+        finally:
+            for p, gr in hidden:
+                p.grad = gr
+        if self.world > 1:
+            self.gather_params()
+        return loss
+
+    @torch.no_grad()
+    def gather_params(self) -> None:
+        """All-gathers every rank's owned parameters into all ranks."""
+        groups: Dict[torch.dtype, List[Tensor]] = {}
+        for g in self.param_groups:
+            for p in g["params"]:
+                groups.setdefault(p.dtype, []).append(p)
+        for dtype, params in groups.items():
+            per_rank = [[p for p in params if self.owner[p] == r] for r in range(self.world)]
+            sizes = [sum(p.numel() for p in ps) for ps in per_rank]
+            width = max(max(sizes), 1)
+            dev = params[0].device
+            local = torch.zeros(width, dtype=dtype, device=dev)
+            if per_rank[self.rank]:
+                flat = torch.cat([p.reshape(-1) for p in per_rank[self.rank]])
+                local[: flat.numel()].copy_(flat)
+            out = torch.empty(width * self.world, dtype=dtype, device=dev)
+            if dist.get_backend(self.process_group) == "nccl":
+                dist.all_gather_into_tensor(out, local, group=self.process_group)
+            else:
+                dist.all_gather(list(out.chunk(self.world)), local, group=self.process_group)
+            for r, ps in enumerate(per_rank):
+                if r == self.rank:
+                    continue
+                off = r * width
+                for p in ps:
+                    p.copy_(out[off:off + p.numel()].view_as(p))
+                    off += p.numel()

@@ -213,12 +213,38 @@ class CRESSO5(Optimizer):
         state["surprise"] = torch.zeros((), device=device, dtype=dtype)
         state["action"] = torch.zeros((), device=device, dtype=dtype)
 
-    def _init_spectral(self, param: Tensor, group: dict, dtype) -> None:
-        """cresso_v5.py:864-883 (same keys, shapes and dtypes)."""
+    def _geometry(self, param: Tensor):
+        """(global shape, row0, rows, col0, cols) of the block of the tensor this
+        rank holds.  An unsharded tensor is its own global tensor; a row-sharded
+        one (see cresso_b200.distributed) carries its global shape and offset."""
+        spec = getattr(param, "_cresso_shard", None)
+        if spec is None:
+            shape = tuple(int(d) for d in param.shape)
+            if len(shape) == 2:
+                return shape, 0, shape[0], 0, shape[1]
+            n = shape[-1] if shape else 1
+            return shape, 0, 1, 0, n
+        gshape, offset = spec
+        gshape = tuple(int(d) for d in gshape)
+        if len(gshape) == 2:
+            if tuple(param.shape) != (param.shape[0], gshape[1]) or param.ndim != 2:
+                raise RuntimeError("a row shard of a 2-D tensor must keep the full row width")
+            return gshape, int(offset), int(param.shape[0]), 0, gshape[1]
+        if len(gshape) == 1 and param.ndim == 1:
+            return gshape, 0, 1, int(offset), int(param.shape[0])
+        raise RuntimeError("only 1-D and 2-D tensors can be sharded")
+
+    def _init_spectral(self, param: Tensor, group: dict, dtype, shape: Optional[tuple] = None) -> None:
+        """cresso_v5.py:864-883 (same keys, shapes and dtypes).  `shape` is the
+        global shape of a sharded tensor (defaults to the parameter's)."""
+        shape = tuple(param.shape) if shape is None else tuple(shape)
+        numel = 1
+        for d in shape:
+            numel *= int(d)
         state = self.state[param]
         self._init_common(state, param.device, dtype)
         rank = int(group["rank"])
-        freqs = frequencies_tensor(rank, param.ndim, int(group["max_frequency"]), param.device)
+        freqs = frequencies_tensor(rank, len(shape), int(group["max_frequency"]), param.device)
         state["freqs"] = freqs
         state["omega"] = omega_from_freqs(freqs).to(device=param.device, dtype=dtype)
         for name in _SPECTRAL_RANK_STATE:
@@ -226,8 +252,8 @@ class CRESSO5(Optimizer):
         bins = int(group.get("hash_bins", 0))
         tables = int(group.get("hash_tables", 1))
         cutoff = int(group.get("thin_matrix_hard_cutoff", 0))
-        thin = param.ndim == 2 and cutoff > 0 and min(param.shape) <= cutoff
-        if bins > 0 and param.numel() >= int(group.get("hard_channel_min_size", 0)) and not thin:
+        thin = len(shape) == 2 and cutoff > 0 and min(shape) <= cutoff
+        if bins > 0 and numel >= int(group.get("hard_channel_min_size", 0)) and not thin:
             state["hash_energy"] = torch.ones(tables, bins, device=param.device, dtype=dtype)
             state["hash_impulse"] = torch.zeros(tables, bins, device=param.device, dtype=dtype)
             state["hash_refractory"] = torch.zeros(tables, bins, device=param.device, dtype=dtype)
@@ -240,7 +266,7 @@ class CRESSO5(Optimizer):
             state[name] = torch.zeros((), device=param.device, dtype=dtype)
 
     def _use_spectral_route(self, param: Tensor, group: dict) -> bool:
-        return uses_spectral_route(tuple(param.shape), group)
+        return uses_spectral_route(self._geometry(param)[0], group)
 
     # ------------------------------------------------------------- caches
     def _workspace(self, device, shape: tuple, group: dict, freqs: Tensor) -> Tensor:
@@ -327,10 +353,12 @@ class CRESSO5(Optimizer):
                 state = self.state[param]
                 if self._use_spectral_route(param, group):
                     if len(state) == 0:
-                        self._init_spectral(param, group, torch.float32)
+                        self._init_spectral(param, group, torch.float32, self._geometry(param)[0])
                     state["step"] += 1
                     spectral.setdefault(param.device, []).append((param, grad, state))
                 else:
+                    if getattr(param, "_cresso_shard", None) is not None:
+                        raise RuntimeError("scalar-route (small / LoRA-thin) tensors are not sharded: pass them whole")
                     if len(state) == 0:
                         self._init_scalar(param, torch.float32)
                     state["step"] += 1
@@ -349,21 +377,24 @@ class CRESSO5(Optimizer):
         descs = _lib.new_descs(len(items))
         bins, tables = int(group["hash_bins"]), int(group["hash_tables"])
         for i, (p, g, st) in enumerate(items):
-            shape = tuple(int(d) for d in p.shape)
+            shape, row0, rows, col0, cols = self._geometry(p)
+            numel = 1
+            for dd in shape:
+                numel *= dd
             d = descs[i]
             d[F["ndim"]] = len(shape)
-            for a, s in enumerate(shape):
-                d[F["shape0"] + a] = s
-            d[F["row0"]] = 0
-            d[F["col0"]] = 0
-            d[F["rows"]] = shape[0] if len(shape) == 2 else 1
-            d[F["cols"]] = shape[-1]
+            for a, sz in enumerate(shape):
+                d[F["shape0"] + a] = sz
+            d[F["row0"]] = row0
+            d[F["rows"]] = rows
+            d[F["col0"]] = col0
+            d[F["cols"]] = cols
             d[F["step"]] = int(st["step"])
             d[F["param"]] = p.data_ptr()
             d[F["grad"]] = g.data_ptr()
             d[F["shape_ws"]] = self._workspace(device, shape, group, st["freqs"]).data_ptr()
             if "hash_energy" in st and bins > 0 and hard_enabled(shape, group):
-                buf, cap = self._hash_index_cache(device, bins, tables, p.numel())
+                buf, cap = self._hash_index_cache(device, bins, tables, numel)
                 d[F["hash_cache"]] = buf.data_ptr()
                 d[F["hash_cache_n"]] = cap
                 for name in ("hash_energy", "hash_impulse", "hash_refractory"):
@@ -384,8 +415,22 @@ class CRESSO5(Optimizer):
                                             layout.ctypes.data_as(_lib._pi64), 9), "spectral_layout")
         scratch = self._scratch_buffer(device, "spectral", int(layout[0]))
         stream = torch.cuda.current_stream(device).cuda_stream
-        _lib.check(L.cresso_spectral_run(_lib.ptr(descs), n, _lib.ptr(hp), _lib.ptr(scratch), scratch.numel(), 0, 6,
-                                         num_sms, stream), "spectral_run")
+
+        def run(begin: int, end: int) -> None:
+            _lib.check(L.cresso_spectral_run(_lib.ptr(descs), n, _lib.ptr(hp), _lib.ptr(scratch), scratch.numel(),
+                                             begin, end, num_sms, stream), "spectral_run")
+
+        self._spectral_stages(run, scratch, layout)
+
+    def _spectral_stages(self, run: Callable[[int, int], None], scratch: Tensor, layout: np.ndarray) -> None:
+        """Runs the kernel stages of a group step; one GPU needs no exchange."""
+        run(0, _lib.SPECTRAL_STAGES)
+
+    @staticmethod
+    def _reduction_view(scratch: Tensor, layout: np.ndarray, k: int) -> Tensor:
+        """Float64 view of reduction vector k (1..4) inside the scratch."""
+        off, length = int(layout[2 * k - 1]), int(layout[2 * k])
+        return scratch[off:off + 8 * length].view(torch.float64)
 
     def _run_scalar(self, hp: np.ndarray, device, items: list) -> None:
         L = _lib.lib()

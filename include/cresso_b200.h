@@ -96,6 +96,9 @@ CRESSO_API int cresso_last_error(char* buf, size_t n);
 /* out[0] = sizeof(cresso_hparams), out[1] = sizeof(cresso_tensor_desc),
  * out[2] = CRESSO_MAX_NDIM, out[3] = CRESSO_MAX_RANK. */
 CRESSO_API int cresso_abi_layout(int64_t* out, int n);
+/* Number of kernels this library has launched in the process so far (all
+ * devices and threads); lets a caller count the GPU launches of a region. */
+CRESSO_API int64_t cresso_launch_count(void);
 
 /* ------------------------------------------------------------ hash ops --- */
 
@@ -160,21 +163,21 @@ CRESSO_API int cresso_instant_axis_metric(const float* rel, int64_t ndim, const 
  * _spectral_step (metric/confidence/contact/drive updates, hash metric and
  * impulse, projections and reconstructions; cresso_cuda.cpp:171-194).
  *
- * The step runs as stages; a stage ends where every tensor needs a global
- * reduction of the previous pass:
- *   stage 0  upload the group plan into the scratch
- *   stage 1  pass P1 (force energy)                  -> reduction vector 1
- *   stage 2  finalize 1, pass P2 (density, hash, axes) -> reduction vector 2
- *   stage 3  finalize 2, pass P3 (tangent, port)     -> reduction vector 3
- *   stage 4  finalize 3, pass P4 (drive statistics)  -> reduction vector 4
- *   stage 5  finalize 4, pass P5 (parameter update)
- * A single GPU runs stages [0, 6) in one call.  A row-sharded run calls one
- * stage at a time and SUM-all-reduces reduction vector k (float64, located
- * with cresso_spectral_layout) across ranks between stage k and k+1.
+ * The step is a sequence of CRESSO_SPECTRAL_STAGES kernel stages:
+ *    0 upload plan | 1 pass P1  2 reduce 1 | 3 finalize 1  4 pass P2  5 reduce 2 |
+ *    6 finalize 2  7 pass P3  8 reduce 3 | 9 finalize 3  10 pass P4  11 reduce 4 |
+ *   12 finalize 4  13 pass P5
+ * P1 force energy; P2 density, hash bins, projection, axis sums; P3 tangent,
+ * prediction error, port; P4 drive statistics; P5 parameter update.
+ * Reduction vector k (k = 1..4, float64) is complete after stage 3k-1.  A
+ * single GPU runs stages [0, 14) in one call.  A row-sharded run calls
+ * [0,3) [3,6) [6,9) [9,12) [12,14) and SUM-all-reduces reduction vector k
+ * across ranks between the k-th and (k+1)-th call.
  *
  * layout[0]  = scratch bytes needed
- * layout[1+2k], layout[2+2k] (k = 0..3) = byte offset in the scratch and
- *              length in doubles of reduction vector k+1. */
+ * layout[1+2(k-1)], layout[2+2(k-1)] (k = 1..4) = byte offset in the scratch
+ *              and length in doubles of reduction vector k. */
+enum { CRESSO_SPECTRAL_STAGES = 14 };
 CRESSO_API int cresso_spectral_layout(const cresso_tensor_desc* descs, int64_t n, const cresso_hparams* hp,
                            int64_t num_sms, int64_t* layout, int64_t layout_len);
 CRESSO_API int cresso_spectral_run(const cresso_tensor_desc* descs, int64_t n, const cresso_hparams* hp, void* scratch,

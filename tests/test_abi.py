@@ -15,13 +15,13 @@ HEADER = Path(__file__).resolve().parents[1] / "include" / "cresso_b200.h"
 
 
 def declared_symbols():
-    return sorted(set(re.findall(r"CRESSO_API\s+(?:const\s+char\s*\*|int)\s+(cresso_\w+)\s*\(", HEADER.read_text())))
+    return sorted(set(re.findall(r"CRESSO_API\s+(?:const\s+char\s*\*|int64_t|int)\s+(cresso_\w+)\s*\(", HEADER.read_text())))
 
 
 def test_library_exports_every_declared_symbol():
     lib = _lib.lib()
     names = declared_symbols()
-    assert len(names) == 18
+    assert len(names) == 19
     for name in names:
         assert hasattr(lib, name), name
     assert sorted(_lib.EXPORTS) == names
