@@ -46,7 +46,7 @@ if str(ROOT) not in sys.path:
 METRIC = "CRESSO5 ms/step and achieved HBM GB/s at 1/2/4/8 B200; vs host-CPU reference"
 BYTES_PER_ELEM = 12  # grad read + param read + param write, fp32
 # compulsory bytes per element of each pass kernel (the fp32 streams it must touch)
-PASS_BYTES = {"P1": 4, "P2": 4, "P3": 8, "P4": 4, "P5": 12}
+PASS_BYTES = {"P1": 4, "P2": 4, "P3": 8, "P4": 4, "P5": 12, "SCALAR": 12}
 PASS_STAGE = {"P1": 1, "P2": 4, "P3": 7, "P4": 10, "P5": 13}
 
 
@@ -360,8 +360,17 @@ def time_passes(opt, args, world, device, stream):
     import torch.distributed as dist
 
     acc = {k: 0.0 for k in PASS_STAGE}
+    acc["SCALAR"] = 0.0
     reps = max(1, min(args.steps, 3))
     orig = opt._spectral_stages
+    orig_scalar = opt._run_scalar
+
+    def scalar_timed(*a, **k):
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        ev0.record(stream)
+        orig_scalar(*a, **k)
+        ev1.record(stream)
+        events.append(("SCALAR", ev0, ev1))
 
     def instrumented(run, scratch, layout):
         bounds = set(_lib.REDUCTION_BOUNDARIES)
@@ -381,6 +390,7 @@ def time_passes(opt, args, world, device, stream):
                 dist.all_reduce(opt._reduction_view(scratch, layout, k))
 
     opt._spectral_stages = instrumented
+    opt._run_scalar = scalar_timed
     try:
         for _ in range(reps):
             events = []
@@ -390,7 +400,8 @@ def time_passes(opt, args, world, device, stream):
                 acc[name] += a.elapsed_time(b)
     finally:
         opt._spectral_stages = orig
-    return {k: v / reps for k, v in acc.items()}
+        opt._run_scalar = orig_scalar
+    return {k: v / reps for k, v in acc.items() if v > 0.0}
 
 
 def time_e2e(opt, params, grads_dev, args, world, device, stream, n_total):

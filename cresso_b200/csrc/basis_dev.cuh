@@ -21,13 +21,14 @@
 
 namespace cresso {
 
-// Loads (a1_k, a2_k) of global row `gr` for modes 0..RM-1.
+// Loads (a1_k, a2_k) of row `gr` of a row table for modes 0..RM-1.  The
+// table may sit in global or (staged) shared memory: plain generic loads.
 template <int RM>
 __device__ __forceinline__ void load_row(const float* __restrict__ rowtab, int64_t gr, float (&a1)[RM], float (&a2)[RM]) {
     const float4* p = reinterpret_cast<const float4*>(rowtab + gr * (2 * RM));
 #pragma unroll
     for (int q = 0; q < RM / 2; ++q) {
-        float4 v = __ldg(p + q);
+        float4 v = p[q];
         a1[2 * q] = v.x;
         a2[2 * q] = v.y;
         a1[2 * q + 1] = v.z;
@@ -72,6 +73,19 @@ __device__ __forceinline__ float recon_dot(float K, const float (&a1)[RM], const
     return s;
 }
 
+// Mode 0 of every CRESSO5 carrier pack is the zero-frequency mode, whose
+// tables are a = (1, 0), b = (1, 0): its reconstruction term is the constant
+// alpha'_0 (folded into K by the finalize kernels) and its projection is the
+// plain sum.  The streaming passes therefore loop over modes 1..RM-1 only.
+template <int RM>
+__device__ __forceinline__ float recon_dot_nz(float K, const float (&a1)[RM], const float (&a2)[RM],
+                                              const float (&U)[RM], const float (&V)[RM]) {
+    float s = K;
+#pragma unroll
+    for (int k = 1; k < RM; ++k) s = fmaf(a1[k], U[k], fmaf(a2[k], V[k], s));
+    return s;
+}
+
 // Adds the column contraction of (z1, z2) into (C, S): C_k += sum x raw_cos_k, S_k += sum x raw_sin_k.
 template <int RM>
 __device__ __forceinline__ void contract_col(const float (&b1)[RM], const float (&b2)[RM], const float (&z1)[RM],
@@ -95,9 +109,11 @@ __host__ __device__ inline double recon_shrink(int rank) {
     return 1.0 / sqrt(v > 1.0 ? v : 1.0);
 }
 
-// Per-mode normalisation record in the shape workspace.
+// Per-mode normalisation record in the shape workspace: carrier = (raw - mu) * inv
+// (mu = 0, inv = 1 for the unnormalised zero mode); mhat = mean of the carrier;
+// rawmean = mean of the raw separable product.
 struct ModeStats {
-    double mu_c, inv_c, mu_s, inv_s, mhat_c, mhat_s, pad0, pad1;
+    double mu_c, inv_c, mu_s, inv_s, mhat_c, mhat_s, rawmean_c, rawmean_s;
 };
 
 }  // namespace cresso

@@ -264,13 +264,13 @@ __global__ void stats_gram_kernel(ModePack modes, int rank, int rm, double n, co
             stats[k].mu_c = mu_x;
             stats[k].inv_c = inv_x;
             stats[k].mhat_c = mhat;
+            stats[k].rawmean_c = k < rank ? m : 0.0;
         } else {
             stats[k].mu_s = mu_x;
             stats[k].inv_s = inv_x;
             stats[k].mhat_s = mhat;
+            stats[k].rawmean_s = k < rank ? m : 0.0;
         }
-        stats[k].pad0 = 0.0;
-        stats[k].pad1 = 0.0;
     }
     __syncthreads();
     for (int w = threadIdx.x; w < P * P; w += blockDim.x) {

@@ -46,6 +46,7 @@ enum : int32_t {
     F_INST2D = 64,
     F_INST1D = 128,
     F_IPOW1 = 256,  // instant_metric_power == 1 (density = rel)
+    F_VEC = 512,    // rows 16-byte aligned: streaming tiles are staged with cp.async
 };
 
 struct TensorConsts {
@@ -63,7 +64,7 @@ struct TensorConsts {
 };
 
 struct GroupHdr {
-    int64_t n_tensors, n_items, rm, bins, tables, tb, iters, idx_bytes;
+    int64_t n_tensors, n_items, rm, bins, tables, tb, iters, idx_bytes, rb_max;
     int64_t grid[6];  // blocks of pass 1..5 (index 0 unused)
     double hp[64];    // cresso_hparams
 };
@@ -121,39 +122,115 @@ __device__ __forceinline__ int load_bin(const void* hidx, int idx_bytes, int64_t
 __device__ __forceinline__ float sgnf(float x) { return x > 0.f ? 1.f : (x < 0.f ? -1.f : 0.f); }
 
 // Per-element drive components shared by P4 and P5 (cresso_v5.py:1315-1326).
-struct DriveParts {
-    float u, root, nov;
+struct DriveK {
+    float clip, inv_clip, clip2, sp, invD, eps;
 };
-__device__ __forceinline__ DriveParts drive_parts(float t, float pred, const TensorConsts& c, float eps) {
+struct DriveParts {
+    float u, root, nov, rat;
+};
+__device__ __forceinline__ DriveParts drive_parts(float t, float pred, const DriveK& c) {
     DriveParts d;
     const float at = fabsf(t);
-    const float rat = t / (1.0f + at * c.inv_clip);
+    d.rat = __fdividef(t, 1.0f + at * c.inv_clip);  // denominator in [1, 1 + 1e4 / clip]
     const float bnd = tanhf(t * c.inv_clip) * c.clip;
-    d.root = sgnf(t) * sqrtf(fminf(at, c.clip2) + eps);
-    d.u = (1.0f - c.sp) * rat + c.sp * bnd;
+    d.root = sgnf(t) * sqrtf(fminf(at, c.clip2) + c.eps);
+    d.u = (1.0f - c.sp) * d.rat + c.sp * bnd;
     d.nov = tanhf((t - pred) * c.invD) * c.clip;
     return d;
 }
 
+// Sum of each of v[0..3] over aligned groups of `w` lanes (w a power of two,
+// 4 <= w <= 32) in 1.5 shuffles per value: after the call, lane l of a group
+// holds the sum of v[2 * ((l & (w/2)) != 0) + ((l & (w/4)) != 0)].
+__device__ __forceinline__ float group_sum4(const float (&v)[4], int w) {
+    const int lane = threadIdx.x & 31;
+    const int o1 = w >> 1, o2 = w >> 2;
+    const bool hi1 = (lane & o1) != 0;
+    const float s0 = hi1 ? v[0] : v[2], s1 = hi1 ? v[1] : v[3];
+    const float k0 = hi1 ? v[2] : v[0], k1 = hi1 ? v[3] : v[1];
+    const float w0 = k0 + __shfl_xor_sync(0xffffffffu, s0, o1);
+    const float w1 = k1 + __shfl_xor_sync(0xffffffffu, s1, o1);
+    const bool hi2 = (lane & o2) != 0;
+    float x = (hi2 ? w1 : w0) + __shfl_xor_sync(0xffffffffu, hi2 ? w0 : w1, o2);
+    for (int o = w >> 3; o > 0; o >>= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
+    return x;
+}
+
 // ---------------------------------------------------------------------------
 // Pass kernel
+//
+// Thread mapping: a block processes "items" of one tensor: TC columns x RB
+// rows (TC = min(256, next_pow2(cols)), RB = RPI * ITERS, RPI = 256 / TC).
+// Thread (lc, rs) owns column ct * TC + lc and rows rs, rs + RPI, ... of the
+// item, so per-column carrier factors stay in registers and per-row factors
+// are warp-uniform.  Blocks walk a contiguous range of the group's item list
+// (a static persistent schedule) and emit one record of partial sums per
+// tensor they touch.
+//
+// Staging: for tensors whose rows are 16-byte aligned (cols, col0 and the
+// global row length multiples of 16) the streaming tiles of an item -- the
+// gradient or tangent, the parameter when needed, the hash-bin bytes of the
+// first two tables and the item's rows of the carrier row table -- are copied
+// into shared memory with cp.async 16-byte copies, double buffered: the copies
+// of item i+1 are in flight while item i computes out of shared memory.  Other
+// tensors read the same tiles straight from global memory.
 // ---------------------------------------------------------------------------
-template <int PASS>
-struct PassOcc { static constexpr int v = PASS == 1 ? 4 : 2; };
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem, int src_bytes) {
+    const unsigned s = (unsigned)__cvta_generic_to_shared(smem);
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(s), "l"(gmem), "r"(src_bytes) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+    asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory");
+}
 
 template <int PASS, int RM>
-__global__ void __launch_bounds__(kThreads, (RM > 8 ? 1 : PassOcc<PASS>::v))
+struct PassCfg {
+    static constexpr int kAcc = PASS == 4 ? kGram : (PASS == 2 || PASS == 3 ? 2 * RM : 0);  // fp64 per-thread sums
+    static constexpr int kMinBlocks = RM > 8 ? 1 : 2;
+    static constexpr int kUnroll = PASS == 3 ? 2 : 4;  // rows computed together
+    static constexpr bool kP = PASS == 5;              // parameter tile always staged
+};
+
+// Shared-memory bytes of one staging buffer of an item.
+__host__ __device__ inline int stage_bytes(int iters, int rm, int tables2, int idx_bytes, bool with_p, int rb_max) {
+    const int tile = 256 * iters;
+    int b = tile * 4;  // gradient or tangent
+    if (with_p) b += tile * 4;
+    b += tables2 * tile * idx_bytes;
+    b += rb_max * 2 * rm * 4;  // the item's rows of the row table
+    return (int)align_up(b, 16);
+}
+
+template <int PASS, int RM, int NT>
+__global__ void __launch_bounds__(kThreads, PassCfg<PASS, RM>::kMinBlocks)
 spectral_pass_kernel(const GroupHdr* __restrict__ hdr, const DevTensor* __restrict__ dts,
                      const int64_t* __restrict__ item_base, double* __restrict__ rec_scal,
                      float* __restrict__ rec_bins) {
+    constexpr int NACC = PassCfg<PASS, RM>::kAcc;
+    constexpr int UNR = PassCfg<PASS, RM>::kUnroll;
     extern __shared__ __align__(16) unsigned char smem_raw[];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+
+    // group constants, once per block
     const int64_t n_items = hdr->n_items;
     const int nt = (int)hdr->n_tensors;
-    const int TB = (int)hdr->tb, B = (int)hdr->bins, T = (int)hdr->tables;
+    const int TB = (int)hdr->tb, B = (int)hdr->bins;
+    const int T = NT > 0 ? NT : (int)hdr->tables;  // hash tables (compile-time 1 or 2 on the fast path)
+    const int T2 = T < 2 ? T : 2;                    // tables whose bin bytes are staged
     const int ITERS = (int)hdr->iters;
-    const int idx_bytes = (int)hdr->idx_bytes;
+    const bool idx8 = hdr->idx_bytes == 1;
+    const int ib = idx8 ? 1 : 2;
+    const bool stage_p_any = PassCfg<PASS, RM>::kP || (PASS <= 3 && hdr->hp[H_WD] != 0.0);
     const float eps = (float)hdr->hp[H_EPS];
+    const float wd = (float)hdr->hp[H_WD];
+    const float ep = (float)hdr->hp[H_EP];
+    const float ipw = fmaxf((float)hdr->hp[H_IP], 0.25f);
+    const float mcpl = (float)hdr->hp[H_MC];
+    const float lsh = (float)hdr->hp[H_LS];
+    const float tmix = (float)hdr->hp[H_TM];
+    const float invT = 1.0f / (float)T;
     const int64_t it0 = (int64_t)blockIdx.x * n_items / gridDim.x;
     const int64_t it1 = ((int64_t)blockIdx.x + 1) * n_items / gridDim.x;
 
@@ -161,246 +238,396 @@ spectral_pass_kernel(const GroupHdr* __restrict__ hdr, const DevTensor* __restri
     constexpr bool kBins = PASS == 2 || PASS == 3;
     constexpr bool kTab = PASS >= 3;
     const int ncopies = kBins ? max(1, min(kWarps, kMaxTB / max(TB, 1))) : 0;
-    double* s_red = reinterpret_cast<double*>(smem_raw);             // kNSRec * kWarps
-    double* s_tot = s_red + kNSRec * kWarps;                         // kNSRec
-    float* s_f = reinterpret_cast<float*>(s_tot + kNSRec);
-    float* s_bins = s_f;                                             // ncopies * TB
-    float* s_tab = s_bins + (kBins ? ncopies * TB : 0);              // TB
-    float* s_rowred = s_tab + (kTab ? TB : 0);                       // 8 * ITERS
-    float* s_colred = s_rowred + (PASS == 2 ? 8 * ITERS : 0);        // 256
+    const int tile = 256 * ITERS;
+    const int sbytes = stage_bytes(ITERS, RM, PASS >= 2 ? T2 : 0, ib, stage_p_any, (int)hdr->rb_max);
+    unsigned char* s_stage = smem_raw;                                        // 2 * sbytes
+    double* s_red = reinterpret_cast<double*>(smem_raw + 2 * sbytes);         // kNSRec * kWarps
+    double* s_tot = s_red + kNSRec * kWarps;                                  // kNSRec
+    double* s_acc = s_tot + kNSRec;                                           // NACC * kThreads
+    float* s_coef = reinterpret_cast<float*>(s_acc + NACC * kThreads);       // 4 * RM + 4
+    float* s_bins = s_coef + 4 * RM + 4;                                      // ncopies * TB
+    float* s_tab = s_bins + (kBins ? ncopies * TB : 0);                       // TB
+    float* s_rowred = s_tab + (kTab ? TB : 0);                                // 8 * ITERS
+    float* s_colred = s_rowred + (PASS == 2 ? 8 * ITERS : 0);                 // kThreads
 
     int k = find_tensor(item_base, nt, it0);
     int64_t it = it0;
     while (it < it1) {
-        const DevTensor& D = dts[k];
-        const TensorConsts& C = *D.cst;
-        const int64_t seg_end = min(it1, D.item_base + D.n_items);
-        const int flags = D.flags;
+        // ---- tensor descriptor and constants into registers
+        const DevTensor* __restrict__ Dp = dts + k;
+        const int64_t rows = Dp->rows, cols = Dp->cols, row0 = Dp->row0, col0 = Dp->col0, gcols = Dp->gcols;
+        const int64_t ibase = Dp->item_base, hidx_n = Dp->hidx_n;
+        const int64_t seg_end = min(it1, ibase + Dp->n_items);
+        const int flags = Dp->flags;
+        const int TC = Dp->TC, RPI = Dp->RPI, RB = Dp->RB, n_bands = Dp->n_bands;
+        const int rows32 = (int)rows, cols32 = (int)cols, row032 = (int)row0, gcols32 = (int)gcols;
         const bool hash_on = (flags & F_HASH) != 0;
-        // ---- segment set-up
+        const bool vec = (flags & F_VEC) != 0;
+        const bool wd_on = (flags & F_WD) != 0;
+        const bool stage_p = PassCfg<PASS, RM>::kP || (PASS <= 3 && wd_on);
+        const float* __restrict__ grad = Dp->grad;
+        float* __restrict__ param = Dp->param;
+        float* __restrict__ tbuf = Dp->tbuf;
+        const float* __restrict__ rowtab = Dp->rowtab;
+        const float* __restrict__ coltab = Dp->coltab;
+        const unsigned char* __restrict__ hidx = reinterpret_cast<const unsigned char*>(Dp->hidx);
+        const float* __restrict__ rowf = Dp->rowf;
+        const float* __restrict__ xsrc = PASS <= 3 ? grad : tbuf;
+        const TensorConsts* __restrict__ Cp = Dp->cst;
+        const float sgn = (flags & F_MAXIMIZE) ? -1.0f : 1.0f;
+        float scale = 0.f, inv_scale = 0.f, inst_k = 0.f, inst_gm = 1.f;
+        DriveK dk{};
+        float c_u = 0.f, c_root = 0.f, c_t = 0.f, c_nov = 0.f, c_hp = 0.f, gain = 0.f, neg_lr = 0.f;
+        if constexpr (PASS >= 2 && PASS <= 3) {
+            scale = Cp->scale;
+            inv_scale = Cp->inv_scale;
+            inst_k = Cp->inst_k;
+            inst_gm = Cp->inst_gm;
+        }
+        if constexpr (PASS >= 4) {
+            dk = DriveK{Cp->clip, Cp->inv_clip, Cp->clip2, Cp->sp, Cp->invD, eps};
+        }
+        if constexpr (PASS == 5) {
+            c_u = Cp->c_u;
+            c_root = Cp->c_root;
+            c_t = Cp->c_t;
+            c_nov = Cp->c_nov;
+            c_hp = Cp->c_hp;
+            gain = Cp->gain;
+            neg_lr = Cp->neg_lr;
+        }
+        // reconstruction coefficients of this pass into shared memory
+        if constexpr (PASS >= 3) {
+            const float* al1 = PASS == 3 ? Cp->m_al : Cp->pr_al;
+            const float* be1 = PASS == 3 ? Cp->m_be : Cp->pr_be;
+            const float* al2 = PASS == 3 ? Cp->p0_al : (PASS == 4 ? Cp->ec_al : Cp->cb_al);
+            const float* be2 = PASS == 3 ? Cp->p0_be : (PASS == 4 ? Cp->ec_be : Cp->cb_be);
+            if (tid < RM) {
+                s_coef[tid] = al1[tid];
+                s_coef[RM + tid] = be1[tid];
+                s_coef[2 * RM + tid] = al2[tid];
+                s_coef[3 * RM + tid] = be2[tid];
+            }
+            if (tid == 0) {
+                s_coef[4 * RM] = PASS == 3 ? Cp->m_K : Cp->pr_K;
+                s_coef[4 * RM + 1] = PASS == 3 ? Cp->p0_K : (PASS == 4 ? Cp->ec_K : Cp->cb_K);
+            }
+        }
         if constexpr (kBins) {
             for (int b = tid; b < ncopies * TB; b += kThreads) s_bins[b] = 0.0f;
         }
         if constexpr (kTab) {
-            if (hash_on)
-                for (int b = tid; b < TB; b += kThreads) s_tab[b] = D.htab[b];
+            if (hash_on) {
+                const float* src = Dp->htab;
+                for (int b = tid; b < TB; b += kThreads) s_tab[b] = src[b];
+            }
+        }
+        if constexpr (NACC > 0) {
+            for (int j = 0; j < NACC; ++j) s_acc[j * kThreads + tid] = 0.0;
         }
         __syncthreads();
         float* my_bins = s_bins + (kBins ? (warp % max(ncopies, 1)) * TB : 0);
-
-        // per-thread segment accumulators
-        double acc0 = 0.0, acc1 = 0.0;                 // P1: sum f^2 | P2: sum L, sum d | P3: sum e^2, sum t
-        double Cp[RM], Sp[RM];                         // projection contractions (P2, P3)
-        double G[kGram];                               // P4 Gram
-        if constexpr (PASS == 2 || PASS == 3) {
-#pragma unroll
-            for (int q = 0; q < RM; ++q) Cp[q] = Sp[q] = 0.0;
-        }
-        if constexpr (PASS == 4) {
-#pragma unroll
-            for (int q = 0; q < kGram; ++q) G[q] = 0.0;
-        }
-
-        const float sgn = (flags & F_MAXIMIZE) ? -1.0f : 1.0f;
-        const float wd = (float)hdr->hp[H_WD];
-        const float inv_scale = C.inv_scale, scale = C.scale;
-        const int TC = D.TC, RPI = D.RPI;
+        const float K1 = kTab ? s_coef[4 * RM] : 0.f, K2 = kTab ? s_coef[4 * RM + 1] : 0.f;
+        double acc0 = 0.0, acc1 = 0.0;
         const int lc = tid & (TC - 1), rs = tid / TC;
+        const int wseg = min(TC, 32);
 
+        // stage layout inside one buffer
+        const int off_p = tile * 4;
+        const int off_b = off_p + (stage_p_any ? tile * 4 : 0);
+        const int off_r = off_b + (PASS >= 2 ? T2 * tile * ib : 0);
+        auto stage_item = [&](int64_t item, int buf) {
+            unsigned char* sb = s_stage + buf * sbytes;
+            const int64_t loc = item - ibase;
+            const int ct = (int)(loc / n_bands);
+            const int rb = (int)(loc - (int64_t)ct * n_bands) * RB;
+            const int cb = ct * TC;
+            const int cpr = TC >> 2;  // 16-byte chunks per tile row of floats
+            for (int c = tid; c < RB * cpr; c += kThreads) {
+                const int lr = c / cpr, cc = c - lr * cpr;
+                const int r = rb + lr, col = cb + 4 * cc;
+                const bool ok = r < rows32 && col < cols32;
+                const int64_t e = ok ? (int64_t)r * cols32 + col : 0;
+                cp_async16(sb + (lr * TC + 4 * cc) * 4, xsrc + e, ok ? 16 : 0);
+                if (stage_p) cp_async16(sb + off_p + (lr * TC + 4 * cc) * 4, param + e, ok ? 16 : 0);
+            }
+            if (PASS >= 2 && hash_on) {
+                const int cprb = (TC * ib) >> 4;  // 16-byte chunks per tile row of bin indices
+                for (int c = tid; c < T2 * RB * cprb; c += kThreads) {
+                    const int t = c / (RB * cprb);
+                    const int c2 = c - t * RB * cprb;
+                    const int lr = c2 / cprb, cc = c2 - lr * cprb;
+                    const int r = rb + lr;
+                    const bool ok = r < rows32 && cb + (16 / ib) * cc < cols32;
+                    const int64_t g = ok ? ((int64_t)(row032 + r) * gcols32 + col0 + cb) * ib + 16 * cc : 0;
+                    cp_async16(sb + off_b + (t * tile + lr * TC) * ib + 16 * cc, hidx + t * hidx_n * ib + g,
+                               ok ? 16 : 0);
+                }
+            }
+            if (PASS >= 2) {
+                const int n16 = RB * 2 * RM / 4;  // 16-byte chunks of the item's row-table rows
+                for (int c = tid; c < n16; c += kThreads) {
+                    const int lr = (4 * c) / (2 * RM);
+                    const bool ok = rb + lr < rows32;
+                    const int64_t g = ok ? (int64_t)(row032 + rb) * 2 * RM + 4 * c : 0;
+                    cp_async16(sb + off_r + 16 * c, rowtab + g, ok ? 16 : 0);
+                }
+            }
+            cp_async_commit();
+        };
+
+        int buf = 0;
+        if (vec && it < seg_end) stage_item(it, 0);
         for (; it < seg_end; ++it) {
-            const int64_t local = it - D.item_base;
-            const int ct = (int)(local / D.n_bands);
-            const int band = (int)(local % D.n_bands);
-            const int64_t col = (int64_t)ct * TC + lc;
-            const bool cvalid = col < D.cols;
-            const int64_t gc = D.col0 + (cvalid ? col : 0);
-            const int64_t rbase = (int64_t)band * D.RB;
+            const int64_t local = it - ibase;
+            const int ct = (int)(local / n_bands);
+            const int band = (int)(local - (int64_t)ct * n_bands);
+            const int col = ct * TC + lc;
+            const bool cvalid = col < cols32;
+            const int gc = (int)col0 + (cvalid ? col : 0);
+            const int rbase = band * RB;
+            if (vec) {
+                if (it + 1 < seg_end) {
+                    stage_item(it + 1, buf ^ 1);
+                    cp_async_wait<1>();
+                } else {
+                    cp_async_wait<0>();
+                }
+                __syncthreads();
+            }
+            // tile bases: shared memory (staged) or global (direct)
+            const unsigned char* sb = s_stage + buf * sbytes;
+            const float* xb = vec ? reinterpret_cast<const float*>(sb) : xsrc + (int64_t)rbase * cols32 + ct * TC;
+            const float* pb = vec ? reinterpret_cast<const float*>(sb + off_p) : param + (int64_t)rbase * cols32 + ct * TC;
+            const int xs = vec ? TC : cols32;
+            const unsigned char* bb = vec ? sb + off_b
+                                          : hidx + ((int64_t)(row032 + rbase) * gcols32 + col0 + ct * TC) * ib;
+            const int64_t bts = vec ? (int64_t)tile * ib : hidx_n * ib;  // bytes between tables
+            const int bs = vec ? TC : gcols32;                            // row stride in indices
+            const float* rtb = vec ? reinterpret_cast<const float*>(sb + off_r) : rowtab + (int64_t)(row032 + rbase) * 2 * RM;
 
-            // column-dependent factors
-            float b1[RM], b2[RM];
             float U1[RM], V1[RM], U2[RM], V2[RM];
             float colf = 1.0f;
             if constexpr (PASS >= 3) {
-                load_col<RM>(D.coltab, D.gcols, gc, b1, b2);
+                float b1[RM], b2[RM];
+                load_col<RM>(coltab, gcols, gc, b1, b2);
+                make_uv<RM>(b1, b2, s_coef, s_coef + RM, U1, V1);
+                make_uv<RM>(b1, b2, s_coef + 2 * RM, s_coef + 3 * RM, U2, V2);
                 if constexpr (PASS == 3) {
-                    make_uv<RM>(b1, b2, C.m_al, C.m_be, U1, V1);
-                    make_uv<RM>(b1, b2, C.p0_al, C.p0_be, U2, V2);
-                    if (flags & F_INST2D) colf = D.colf[cvalid ? col : 0];
-                } else if constexpr (PASS == 4) {
-                    make_uv<RM>(b1, b2, C.pr_al, C.pr_be, U1, V1);
-                    make_uv<RM>(b1, b2, C.ec_al, C.ec_be, U2, V2);
-                } else {
-                    make_uv<RM>(b1, b2, C.pr_al, C.pr_be, U1, V1);
-                    make_uv<RM>(b1, b2, C.cb_al, C.cb_be, U2, V2);
+                    if (flags & F_INST2D) colf = Dp->colf[cvalid ? col : 0];
                 }
             }
             float z1[RM], z2[RM];
+            float g32[PASS == 4 ? kGram : 1];
             if constexpr (PASS == 2 || PASS == 3) {
 #pragma unroll
                 for (int q = 0; q < RM; ++q) z1[q] = z2[q] = 0.0f;
             }
-            float g32[kGram];
             if constexpr (PASS == 4) {
 #pragma unroll
                 for (int q = 0; q < kGram; ++q) g32[q] = 0.0f;
             }
-            float s0 = 0.0f, s1 = 0.0f, colacc = 0.0f;
+            float s0 = 0.0f, s1 = 0.0f, colacc = 0.0f, zc = 0.0f;
 
-            for (int m = 0; m < ITERS; ++m) {
-                const int64_t r = rbase + rs + (int64_t)RPI * m;
-                const bool valid = cvalid && r < D.rows;
-                const int64_t e = r * D.cols + col;              // local element
-                const int64_t gr = D.row0 + (r < D.rows ? r : 0);
-                const int64_t gflat = gr * D.gcols + gc;         // global flat index (hash)
-                float dval = 0.0f;
-                if (valid) {
+            for (int m0 = 0; m0 < ITERS; m0 += UNR) {
+                float dv[UNR];
+#pragma unroll
+                for (int u = 0; u < UNR; ++u) {
+                    dv[u] = 0.0f;
+                    const int lr = rs + RPI * (m0 + u);
+                    const int r = rbase + lr;
+                    if (!(cvalid && r < rows32)) continue;
+                    const float xval = xb[lr * xs + lc];
+                    auto bin_of = [&](int t) -> int {
+                        if (NT > 0 || t < 2) {
+                            const unsigned char* q = bb + t * bts + (int64_t)(lr * bs + lc) * ib;
+                            return idx8 ? (int)*q : (int)*reinterpret_cast<const uint16_t*>(q);
+                        }
+                        const int64_t g = ((int64_t)(row032 + r) * gcols32 + gc) * ib + t * hidx_n * ib;
+                        return idx8 ? (int)__ldg(hidx + g) : (int)__ldg(reinterpret_cast<const uint16_t*>(hidx + g));
+                    };
                     if constexpr (PASS == 1) {
-                        float f = sgn * __ldg(D.grad + e);
-                        if (flags & F_WD) f = f + wd * D.param[e];
+                        float f = sgn * xval;
+                        if (wd_on) f = f + wd * pb[lr * xs + lc];
                         s0 = fmaf(f, f, s0);
                     } else if constexpr (PASS == 2) {
-                        float f = sgn * __ldg(D.grad + e);
-                        if (flags & F_WD) f = f + wd * D.param[e];
+                        float f = sgn * xval;
+                        if (wd_on) f = f + wd * pb[lr * xs + lc];
                         float a1[RM], a2[RM];
-                        load_row<RM>(D.rowtab, gr, a1, a2);
+                        load_row<RM>(rtb, lr, a1, a2);
                         const float rel = fminf(fabsf(f) * inv_scale + eps, 1.0e4f);
-                        const float ds = powf(rel, (float)hdr->hp[H_EP]);
+                        const float ds = exp2f(ep * log2f(rel));  // rel >= eps > 0
+                        // log1p(ds) - 1/2: the density is centred before the float32 partial sums
+                        // (the constant is added back exactly in the finalize)
                         const float L = log1pf(ds);
-                        const float ip = fmaxf((float)hdr->hp[H_IP], 0.25f);
-                        dval = (flags & F_IPOW1) ? rel : fminf(powf(fmaxf(rel, eps), ip), 1.0e6f);
+                        const float Lc = L - 0.5f;
+                        const float d = (flags & F_IPOW1) ? rel : fminf(powf(fmaxf(rel, eps), ipw), 1.0e6f);
+                        dv[u] = d;
                         s0 += L;
-                        s1 += dval;
-                        colacc += dval;
+                        s1 += d;
+                        colacc += d;
 #pragma unroll
-                        for (int q = 0; q < RM; ++q) {
-                            z1[q] = fmaf(L, a1[q], z1[q]);
-                            z2[q] = fmaf(L, a2[q], z2[q]);
+                        for (int q = 1; q < RM; ++q) {
+                            z1[q] = fmaf(Lc, a1[q], z1[q]);
+                            z2[q] = fmaf(Lc, a2[q], z2[q]);
                         }
+                        zc += Lc;
                         if (hash_on) {
-                            for (int t = 0; t < T; ++t)
-                                atomicAdd(&my_bins[t * B + load_bin(D.hidx, idx_bytes, D.hidx_n, t, gflat)], ds);
+#pragma unroll
+                            for (int t = 0; t < (NT > 0 ? NT : T); ++t) atomicAdd(&my_bins[t * B + bin_of(t)], ds);
                         }
                     } else if constexpr (PASS == 3) {
-                        float f = sgn * __ldg(D.grad + e);
-                        if (flags & F_WD) f = f + wd * D.param[e];
+                        float f = sgn * xval;
+                        if (wd_on) f = f + wd * pb[lr * xs + lc];
                         float a1[RM], a2[RM];
-                        load_row<RM>(D.rowtab, gr, a1, a2);
+                        load_row<RM>(rtb, lr, a1, a2);
                         const float rel = fminf(fabsf(f) * inv_scale + eps, 1.0e4f);
-                        const float lm = clampf(recon_dot<RM>(C.m_K, a1, a2, U1, V1), -3.0f, 3.0f);
-                        const float metric = clampf(expf((float)hdr->hp[H_MC] * lm), 0.06f, 16.0f);
+                        const float lm = clampf(recon_dot_nz<RM>(K1, a1, a2, U1, V1), -3.0f, 3.0f);
+                        const float metric = clampf(expf(mcpl * lm), 0.06f, 16.0f);
                         float den = scale * metric;
-                        if (flags & F_LOCAL)
-                            den = den * clampf(1.0f + (float)hdr->hp[H_LS] * sqrtf(fminf(rel, 100.0f)), 1.0f, 8.0f);
+                        if (flags & F_LOCAL) den = den * clampf(1.0f + lsh * sqrtf(fminf(rel, 100.0f)), 1.0f, 8.0f);
                         if (flags & F_INST2D) {
-                            den = den * clampf(D.rowf[r] * colf, 0.08f, 12.0f);
+                            den = den * clampf(rowf[r] * colf, 0.08f, 12.0f);
                         } else if (flags & F_INST1D) {
-                            const float ip = fmaxf((float)hdr->hp[H_IP], 0.25f);
-                            const float dd = (flags & F_IPOW1) ? rel : fminf(powf(fmaxf(rel, eps), ip), 1.0e6f);
-                            den = den * clampf(expf(C.inst_k * logf(fmaxf(dd / C.inst_gm, eps))), 0.08f, 12.0f);
+                            const float dd = (flags & F_IPOW1) ? rel : fminf(powf(fmaxf(rel, eps), ipw), 1.0e6f);
+                            den = den * clampf(expf(inst_k * logf(fmaxf(dd / inst_gm, eps))), 0.08f, 12.0f);
                         }
-                        int bidx[8];
+                        int bi[NT > 0 ? NT : 2];
                         if (hash_on) {
                             float lsum = 0.0f;
-                            for (int t = 0; t < T; ++t) {
-                                bidx[t & 7] = load_bin(D.hidx, idx_bytes, D.hidx_n, t, gflat);
-                                lsum += s_tab[t * B + bidx[t & 7]];
+#pragma unroll
+                            for (int t = 0; t < (NT > 0 ? NT : T); ++t) {
+                                const int bt = bin_of(t);
+                                if (NT > 0 || t < 2) bi[NT > 0 ? t : (t & 1)] = bt;
+                                lsum += s_tab[t * B + bt];
                             }
-                            den = den * clampf(expf(lsum / (float)T), 0.08f, 12.0f);
+                            den = den * clampf(expf(lsum * invT), 0.08f, 12.0f);
                         }
-                        den = den + eps;
-                        const float t = clampf(__fdiv_rn(f, den), -1.0e4f, 1.0e4f);
-                        D.tbuf[e] = t;
-                        const float pred = recon_dot<RM>(C.p0_K, a1, a2, U2, V2);
+                        const float t = clampf(__fdiv_rn(f, den + eps), -1.0e4f, 1.0e4f);
+                        tbuf[(int64_t)r * cols32 + col] = t;
+                        const float pred = recon_dot_nz<RM>(K2, a1, a2, U2, V2);
                         const float err = t - pred;
                         s0 = fmaf(err, err, s0);
                         s1 += t;
 #pragma unroll
-                        for (int q = 0; q < RM; ++q) {
+                        for (int q = 1; q < RM; ++q) {
                             z1[q] = fmaf(t, a1[q], z1[q]);
                             z2[q] = fmaf(t, a2[q], z2[q]);
                         }
+                        zc += t;
                         if (hash_on) {
-                            const float port = err + (float)hdr->hp[H_TM] * t;
-                            for (int t2 = 0; t2 < T; ++t2) {
-                                const int bb = t2 < 8 ? bidx[t2] : load_bin(D.hidx, idx_bytes, D.hidx_n, t2, gflat);
-                                atomicAdd(&my_bins[t2 * B + bb], port);
+                            const float port = err + tmix * t;
+#pragma unroll
+                            for (int t2 = 0; t2 < (NT > 0 ? NT : T); ++t2) {
+                                const int bt = (NT > 0 || t2 < 2) ? bi[NT > 0 ? t2 : (t2 & 1)] : bin_of(t2);
+                                atomicAdd(&my_bins[t2 * B + bt], port);
                             }
                         }
                     } else if constexpr (PASS == 4) {
                         float a1[RM], a2[RM];
-                        load_row<RM>(D.rowtab, gr, a1, a2);
-                        const float t = D.tbuf[e];
-                        const float pred = recon_dot<RM>(C.pr_K, a1, a2, U1, V1);
-                        const float echo = (flags & F_ECHO) ? recon_dot<RM>(C.ec_K, a1, a2, U2, V2) : 0.0f;
+                        load_row<RM>(rtb, lr, a1, a2);
+                        const float t = xval;
+                        const float pred = recon_dot_nz<RM>(K1, a1, a2, U1, V1);
+                        const float echo = (flags & F_ECHO) ? recon_dot_nz<RM>(K2, a1, a2, U2, V2) : 0.0f;
                         float hpv = 0.0f;
                         if (hash_on) {
-                            for (int t2 = 0; t2 < T; ++t2)
-                                hpv += s_tab[t2 * B + load_bin(D.hidx, idx_bytes, D.hidx_n, t2, gflat)];
-                            hpv = hpv / (float)T;
+#pragma unroll
+                            for (int t2 = 0; t2 < (NT > 0 ? NT : T); ++t2) hpv += s_tab[t2 * B + bin_of(t2)];
+                            hpv = hpv * invT;
                         }
-                        const DriveParts dp = drive_parts(t, pred, C, eps);
-                        const float rat = t / (1.0f + fabsf(t) * C.inv_clip);
+                        const DriveParts dp = drive_parts(t, pred, dk);
                         const float v[7] = {dp.u, dp.root, t, pred, dp.nov, echo, hpv};
 #pragma unroll
                         for (int a = 0; a < 7; ++a)
 #pragma unroll
                             for (int b = a; b < 7; ++b) g32[gram_idx(a, b)] = fmaf(v[a], v[b], g32[gram_idx(a, b)]);
-                        g32[28] = fmaf(rat, rat, g32[28]);
+                        g32[28] = fmaf(dp.rat, dp.rat, g32[28]);
                     } else {  // PASS 5
                         float a1[RM], a2[RM];
-                        load_row<RM>(D.rowtab, gr, a1, a2);
-                        const float t = D.tbuf[e];
-                        const float pred = recon_dot<RM>(C.pr_K, a1, a2, U1, V1);
-                        const float comb = recon_dot<RM>(C.cb_K, a1, a2, U2, V2);
+                        load_row<RM>(rtb, lr, a1, a2);
+                        const float t = xval;
+                        const float pred = recon_dot_nz<RM>(K1, a1, a2, U1, V1);
+                        const float comb = recon_dot_nz<RM>(K2, a1, a2, U2, V2);
                         float hpv = 0.0f;
                         if (hash_on) {
-                            for (int t2 = 0; t2 < T; ++t2)
-                                hpv += s_tab[t2 * B + load_bin(D.hidx, idx_bytes, D.hidx_n, t2, gflat)];
-                            hpv = hpv / (float)T;
+#pragma unroll
+                            for (int t2 = 0; t2 < (NT > 0 ? NT : T); ++t2) hpv += s_tab[t2 * B + bin_of(t2)];
+                            hpv = hpv * invT;
                         }
-                        const DriveParts dp = drive_parts(t, pred, C, eps);
-                        const float drive = C.c_u * dp.u + C.c_root * dp.root + C.c_t * t + comb + C.c_nov * dp.nov +
-                                            C.c_hp * hpv;
-                        const float p = D.param[e];
-                        D.param[e] = p + C.neg_lr * (drive * C.gain);
+                        const DriveParts dp = drive_parts(t, pred, dk);
+                        const float drive = c_u * dp.u + c_root * dp.root + c_t * t + comb + c_nov * dp.nov + c_hp * hpv;
+                        param[(int64_t)r * cols32 + col] = pb[lr * xs + lc] + neg_lr * (drive * gain);
                     }
                 }
                 if constexpr (PASS == 2) {
-                    // row sums of the axis density: reduce across the TC lanes of the row
-                    float rsum = dval;
-                    const int w = min(TC, 32);
-                    for (int o = w >> 1; o > 0; o >>= 1) rsum += __shfl_xor_sync(0xffffffffu, rsum, o);
-                    if (TC <= 32) {
-                        if (lc == 0 && r < D.rows) D.rowpart[(int64_t)ct * D.rows + r] = rsum;
-                    } else if (lane == 0) {
-                        const int nw = TC >> 5;
-                        s_rowred[(rs + RPI * m) * nw + ((tid & (TC - 1)) >> 5)] = rsum;
+                    // row sums of the axis density over the TC lanes of each row
+                    if (UNR == 4 && wseg >= 4) {
+                        float dv4[4] = {dv[0], dv[UNR > 1 ? 1 : 0], dv[UNR > 2 ? 2 : 0], dv[UNR > 3 ? 3 : 0]};
+                        const float x = group_sum4(dv4, wseg);
+                        const int sl = lane & (wseg - 1);
+                        const int o1 = wseg >> 1, o2 = wseg >> 2;
+                        const int ur = 2 * ((sl & o1) != 0) + ((sl & o2) != 0);
+                        if ((sl & (o2 - 1)) == 0) {  // lowest lane of its class writes row ur
+                            const int r = rbase + rs + RPI * (m0 + ur);
+                            if (TC <= 32) {
+                                if (r < rows32) Dp->rowpart[(int64_t)ct * rows + r] = x;
+                            } else {
+                                s_rowred[(rs + RPI * (m0 + ur)) * (TC >> 5) + (lc >> 5)] = x;
+                            }
+                        }
+                    } else {
+#pragma unroll
+                        for (int u = 0; u < UNR; ++u) {
+                            float x = dv[u];
+                            for (int o = wseg >> 1; o > 0; o >>= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
+                            const int r = rbase + rs + RPI * (m0 + u);
+                            if (TC <= 32) {
+                                if (lc == 0 && r < rows32) Dp->rowpart[(int64_t)ct * rows + r] = x;
+                            } else if (lane == 0) {
+                                s_rowred[(rs + RPI * (m0 + u)) * (TC >> 5) + (lc >> 5)] = x;
+                            }
+                        }
                     }
                 }
             }  // rows of the item
 
-            // ---- item epilogue
+            // ---- item epilogue: float32 item partials into float64 block state
             if constexpr (PASS == 1) {
                 acc0 += (double)s0;
             } else if constexpr (PASS == 2 || PASS == 3) {
                 acc0 += (double)s0;
                 acc1 += (double)s1;
                 if (cvalid) {
-                    if constexpr (PASS == 2) load_col<RM>(D.coltab, D.gcols, gc, b1, b2);
-                    contract_col<RM>(b1, b2, z1, z2, Cp, Sp);
+                    float b1[RM], b2[RM];
+                    load_col<RM>(coltab, gcols, gc, b1, b2);
+                    s_acc[tid] += (double)zc;  // zero mode: sum of the projected field
+#pragma unroll
+                    for (int q = 1; q < RM; ++q) {
+                        const double B1 = b1[q], B2 = b2[q], Z1 = z1[q], Z2 = z2[q];
+                        double c, s;
+                        if (mode_is_product(q)) {
+                            c = B1 * Z1;
+                            s = B2 * Z2;
+                        } else {
+                            c = B1 * Z1 - B2 * Z2;
+                            s = B2 * Z1 + B1 * Z2;
+                        }
+                        s_acc[q * kThreads + tid] += c;
+                        s_acc[(RM + q) * kThreads + tid] += s;
+                    }
                 }
             } else if constexpr (PASS == 4) {
 #pragma unroll
-                for (int q = 0; q < kGram; ++q) G[q] += (double)g32[q];
+                for (int q = 0; q < kGram; ++q) s_acc[q * kThreads + tid] += (double)g32[q];
             }
             if constexpr (PASS == 2) {
                 if (TC > 32) {
                     __syncthreads();
                     const int nw = TC >> 5;
-                    for (int lr = tid; lr < D.RB; lr += kThreads) {
+                    for (int lr = tid; lr < RB; lr += kThreads) {
                         float s = 0.0f;
                         for (int w = 0; w < nw; ++w) s += s_rowred[lr * nw + w];
-                        if (rbase + lr < D.rows) D.rowpart[(int64_t)ct * D.rows + rbase + lr] = s;
+                        if (rbase + lr < rows32) Dp->rowpart[(int64_t)ct * rows + rbase + lr] = s;
                     }
                 }
                 // column sums: combine the RPI threads that share a column
@@ -409,38 +636,42 @@ spectral_pass_kernel(const GroupHdr* __restrict__ hdr, const DevTensor* __restri
                 if (rs == 0 && cvalid) {
                     float s = 0.0f;
                     for (int q = 0; q < RPI; ++q) s += s_colred[q * TC + lc];
-                    D.colpart[(int64_t)band * D.cols + col] = s;
+                    Dp->colpart[(int64_t)band * cols + col] = s;
                 }
-                __syncthreads();
             }
+            __syncthreads();  // this buffer (and the reduction scratch) is free again
+            buf ^= 1;
         }  // items of the segment
 
         // ---- segment flush: one record per (block, tensor)
         if constexpr (PASS <= 4) {
-            const int rec = D.recbase[PASS] + ((int)blockIdx.x - D.cfirst[PASS]);
+            const int rec = Dp->recbase[PASS] + ((int)blockIdx.x - Dp->cfirst[PASS]);
+            double* out = rec_scal + (int64_t)rec * kNSRec;
             if constexpr (PASS == 1) {
                 double v[1] = {acc0};
                 block_sum_to<1>(v, s_red, s_tot);
-                if (tid == 0) rec_scal[(int64_t)rec * kNSRec] = s_tot[0];
-            } else if constexpr (PASS == 4) {
-                block_sum_to<kGram>(G, s_red, s_tot);
-                for (int j = tid; j < kGram; j += kThreads) rec_scal[(int64_t)rec * kNSRec + j] = s_tot[j];
+                if (tid == 0) out[0] = s_tot[0];
             } else {
-                double v[2 + 2 * RM];
-                v[0] = acc0;
-                v[1] = acc1;
+                constexpr int NS = PASS == 4 ? kGram : 2 + 2 * RM;
+                double v[NS];
+                if constexpr (PASS == 4) {
 #pragma unroll
-                for (int q = 0; q < RM; ++q) {
-                    v[2 + q] = Cp[q];
-                    v[2 + RM + q] = Sp[q];
+                    for (int q = 0; q < kGram; ++q) v[q] = s_acc[q * kThreads + tid];
+                } else {
+                    v[0] = acc0;
+                    v[1] = acc1;
+#pragma unroll
+                    for (int q = 0; q < 2 * RM; ++q) v[2 + q] = s_acc[q * kThreads + tid];
                 }
-                block_sum_to<2 + 2 * RM>(v, s_red, s_tot);
-                for (int j = tid; j < 2 + 2 * RM; j += kThreads) rec_scal[(int64_t)rec * kNSRec + j] = s_tot[j];
-                if (hash_on) {
-                    for (int b = tid; b < TB; b += kThreads) {
-                        float s = 0.0f;
-                        for (int c = 0; c < ncopies; ++c) s += s_bins[c * TB + b];
-                        rec_bins[(int64_t)rec * TB + b] = s;
+                block_sum_to<NS>(v, s_red, s_tot);
+                for (int j = tid; j < NS; j += kThreads) out[j] = s_tot[j];
+                if constexpr (kBins) {
+                    if (hash_on) {
+                        for (int b = tid; b < TB; b += kThreads) {
+                            float s = 0.0f;
+                            for (int c = 0; c < ncopies; ++c) s += s_bins[c * TB + b];
+                            rec_bins[(int64_t)rec * TB + b] = s;
+                        }
                     }
                 }
             }
@@ -505,6 +736,8 @@ __device__ void fold_recon(const ModeStats* stats, int R, double alpha, double b
         al[k] = (float)a;
         be[k] = (float)b;
     }
+    // mode 0 is the zero-frequency carrier (1, 0): fold its constant term into K
+    if (k == 0) kpart += alpha * stats[0].inv_c;
     const double tot = block_sum(kpart, s_red);
     if (threadIdx.x == 0) *K = (float)tot;
 }
@@ -572,8 +805,11 @@ __global__ void finalize2_kernel(const GroupHdr* __restrict__ hdr, const DevTens
     if (tid < R) {
         const int k = tid;
         const ModeStats st = D.stats[k];
-        const float pc = (float)((st.inv_c * (red[2 + k] - st.mu_c * sumL) / N) / (double)M - st.mhat_c);
-        const float ps = (float)((st.inv_s * (red[2 + rm + k] - st.mu_s * sumL) / N) / (double)M - st.mhat_s);
+        // P2 accumulated sum (log1p(ds) - 1/2) * raw; restore sum log1p(ds) * raw exactly
+        const double Cc = red[2 + k] + 0.5 * N * st.rawmean_c;
+        const double Cs = red[2 + rm + k] + 0.5 * N * st.rawmean_s;
+        const float pc = (float)((st.inv_c * (Cc - st.mu_c * sumL) / N) / (double)M - st.mhat_c);
+        const float ps = (float)((st.inv_s * (Cs - st.mu_s * sumL) / N) / (double)M - st.mhat_s);
         const float mdt = (float)hp[H_MDT];
         const float damp = (float)fmax(0.0, 1.0 - hp[H_MDT] * hp[H_MF]);
         const float om = D.omega[k];
@@ -853,6 +1089,8 @@ struct Plan {
     int rm;
 };
 
+static size_t pass_smem(int pass, const GroupHdr& H, int64_t iters);
+
 static int64_t take(int64_t& off, int64_t bytes) {
     const int64_t o = off;
     off = align_up(off + bytes, 256);
@@ -908,11 +1146,36 @@ static int build_plan(const cresso_tensor_desc* descs, int64_t n, const cresso_h
         CRESSO_REQUIRE(d.ndim == 1 || (d.col0 == 0 && d.cols == gcols), CRESSO_EUNSUPPORTED,
                        "tensor %lld: 2-D tensors are sharded by rows only", (long long)i);
         CRESSO_REQUIRE(d.step >= 1, CRESSO_EINVAL, "tensor %lld: step must be >= 1", (long long)i);
+        CRESSO_REQUIRE(grows * gcols < (1LL << 31), CRESSO_EUNSUPPORTED,
+                       "tensor %lld: more than 2^31 - 1 elements per tensor", (long long)i);
         total_rows_work += d.rows * ceil_div(d.cols, 256);
+    }
+    // Rows per thread and item: large enough to amortise the per-item set-up,
+    // small enough for >= ~8 items per block and for the staging buffers of
+    // every pass to leave room for two blocks per SM.
+    std::vector<char> vec(n, 0);
+    for (int64_t i = 0; i < n; ++i) {
+        const cresso_tensor_desc& d = descs[i];
+        const int64_t gcols = d.ndim == 2 ? d.shape[1] : d.shape[0];
+        const int64_t ib = bins <= 256 ? 1 : 2;
+        bool ok = d.cols >= 16 && d.cols % 16 == 0 && d.col0 % 16 == 0 && (d.ndim == 1 || gcols % 16 == 0);
+        ok = ok && d.param % 16 == 0 && d.grad % 16 == 0;
+        if (d.hash_cache) ok = ok && d.hash_cache % 16 == 0 && (d.hash_cache_n * ib) % 16 == 0;
+        vec[i] = ok;
     }
     int iters = 32;
     const int64_t target_blocks = num_sms * 2;
     while (iters > 4 && total_rows_work / iters < target_blocks * 8) iters >>= 1;
+    const size_t budget = rm > 8 ? 200 * 1024 : 110 * 1024;
+    for (;; iters >>= 1) {
+        int64_t rb_max = 0;
+        for (int64_t i = 0; i < n; ++i)
+            if (vec[i]) rb_max = std::max<int64_t>(rb_max, (int64_t)(256 / std::min(256, pow2_ceil(descs[i].cols))) * iters);
+        H.rb_max = rb_max;
+        size_t need = 0;
+        for (int p = 1; p <= 5; ++p) need = std::max(need, pass_smem(p, H, iters));
+        if (need <= budget || iters <= 4) break;
+    }
     H.iters = iters;
 
     int64_t items = 0;
@@ -953,6 +1216,7 @@ static int build_plan(const cresso_tensor_desc* descs, int64_t n, const cresso_h
         const double ic = hard ? hp->instant_metric_coupling : 0.0;
         if (ic != 0.0 && D.N > 1) fl |= (d.ndim == 2 ? F_INST2D : F_INST1D);
         if (fmax(hp->instant_metric_power, 0.25) == 1.0) fl |= F_IPOW1;
+        if (vec[i]) fl |= F_VEC;
         D.flags = fl;
         // pointers into the caller's objects
         const char* ws = (const char*)d.shape_ws;
@@ -1029,7 +1293,7 @@ static int build_plan(const cresso_tensor_desc* descs, int64_t n, const cresso_h
         cols_tot += D.cols;
         rowpart_tot += (int64_t)D.n_ct * D.rows;
         colpart_tot += (int64_t)D.n_bands * D.cols;
-        elems += D.rows * D.cols;
+        elems += align_up(D.rows * D.cols, 64);
     }
     P.off_htab = take(off, 4 * std::max<int64_t>(H.tb, 1) * n);
     P.off_rowf = take(off, 4 * rows_tot);
@@ -1070,26 +1334,29 @@ static void bind_scratch(Plan& P, char* base) {
         cols_o += D.cols;
         rowpart_o += (int64_t)D.n_ct * D.rows;
         colpart_o += (int64_t)D.n_bands * D.cols;
-        elem_o += D.rows * D.cols;
+        elem_o += align_up(D.rows * D.cols, 64);
     }
 }
 
-static size_t pass_smem(int pass, const GroupHdr& H) {
+static size_t pass_smem(int pass, const GroupHdr& H, int64_t iters) {
     const int tb = (int)H.tb;
-    size_t b = (size_t)(kNSRec * kWarps + kNSRec) * sizeof(double);
+    const int rm = (int)H.rm;
+    const int nacc = pass == 4 ? kGram : (pass == 2 || pass == 3 ? 2 * rm : 0);
+    const int T2 = H.tables < 2 ? (int)H.tables : 2;
+    const bool with_p = pass == 5 || (pass <= 3 && H.hp[H_WD] != 0.0);
+    size_t b = 2 * (size_t)stage_bytes((int)iters, rm, pass >= 2 ? T2 : 0, (int)H.idx_bytes, with_p, (int)H.rb_max);
+    b += (size_t)(kNSRec * kWarps + kNSRec + nacc * kThreads) * sizeof(double);
+    b += (size_t)(4 * rm + 4) * 4;
     if (pass == 2 || pass == 3) {
         const int ncopies = std::max(1, std::min(kWarps, kMaxTB / std::max(tb, 1)));
         b += (size_t)ncopies * tb * 4;
     }
     if (pass >= 3) b += (size_t)tb * 4;
-    if (pass == 2) b += (size_t)(8 * H.iters + kThreads) * 4;
+    if (pass == 2) b += (size_t)(8 * iters + kThreads) * 4;
     return b;
 }
 
-// Kernel-granularity stages of a spectral group step:
-//   0 upload | 1 P1  2 R1 | 3 F1  4 P2  5 R2 | 6 F2  7 P3  8 R3 | 9 F3  10 P4  11 R4 | 12 F4  13 P5
-// Reduction vector k (1..4) is complete after stage 3k - 1.
-template <int RM>
+template <int RM, int NT>
 static int launch_stage(int stage, const Plan& P, char* base, cudaStream_t s) {
     const GroupHdr* hdr = reinterpret_cast<const GroupHdr*>(base + P.off_hdr);
     const DevTensor* dts = reinterpret_cast<const DevTensor*>(base + P.off_dts);
@@ -1098,7 +1365,7 @@ static int launch_stage(int stage, const Plan& P, char* base, cudaStream_t s) {
     float* recb = reinterpret_cast<float*>(base + P.off_recb);
     const int n = (int)P.hdr.n_tensors;
     auto run_pass = [&](auto kern, int pass) -> int {
-        const size_t smem = pass_smem(pass, P.hdr);
+        const size_t smem = pass_smem(pass, P.hdr, P.hdr.iters);
         if (smem > 48 * 1024) CRESSO_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
         kern<<<(unsigned)P.hdr.grid[pass], kThreads, smem, s>>>(hdr, dts, items, recs, recb);
         CRESSO_LAUNCHED("spectral_pass_kernel");
@@ -1113,31 +1380,31 @@ static int launch_stage(int stage, const Plan& P, char* base, cudaStream_t s) {
         return CRESSO_OK;
     };
     switch (stage) {
-        case 1: return run_pass(spectral_pass_kernel<1, RM>, 1);
+        case 1: return run_pass(spectral_pass_kernel<1, RM, NT>, 1);
         case 2: return run_reduce(1);
         case 3:
             finalize1_kernel<RM><<<n, kThreads, 0, s>>>(hdr, dts);
             CRESSO_LAUNCHED("finalize1_kernel");
             return CRESSO_OK;
-        case 4: return run_pass(spectral_pass_kernel<2, RM>, 2);
+        case 4: return run_pass(spectral_pass_kernel<2, RM, NT>, 2);
         case 5: return run_reduce(2);
         case 6:
             finalize2_kernel<RM><<<n, kThreads, 0, s>>>(hdr, dts);
             CRESSO_LAUNCHED("finalize2_kernel");
             return CRESSO_OK;
-        case 7: return run_pass(spectral_pass_kernel<3, RM>, 3);
+        case 7: return run_pass(spectral_pass_kernel<3, RM, NT>, 3);
         case 8: return run_reduce(3);
         case 9:
             finalize3_kernel<RM><<<n, kThreads, 0, s>>>(hdr, dts);
             CRESSO_LAUNCHED("finalize3_kernel");
             return CRESSO_OK;
-        case 10: return run_pass(spectral_pass_kernel<4, RM>, 4);
+        case 10: return run_pass(spectral_pass_kernel<4, RM, NT>, 4);
         case 11: return run_reduce(4);
         case 12:
             finalize4_kernel<RM><<<n, kThreads, 0, s>>>(hdr, dts);
             CRESSO_LAUNCHED("finalize4_kernel");
             return CRESSO_OK;
-        case 13: return run_pass(spectral_pass_kernel<5, RM>, 5);
+        case 13: return run_pass(spectral_pass_kernel<5, RM, NT>, 5);
         default: return CRESSO_OK;
     }
 }
@@ -1183,10 +1450,17 @@ int cresso_spectral_run(const cresso_tensor_desc* descs, int64_t n, const cresso
                                     cudaMemcpyHostToDevice, s));
     }
     for (int64_t stage = std::max<int64_t>(stage_begin, 1); stage < stage_end; ++stage) {
-        switch (P.rm) {
-            case 4: st = launch_stage<4>((int)stage, P, base, s); break;
-            case 8: st = launch_stage<8>((int)stage, P, base, s); break;
-            default: st = launch_stage<16>((int)stage, P, base, s); break;
+        const int nt = P.hdr.tables == 1 ? 1 : (P.hdr.tables == 2 ? 2 : 0);
+        switch (P.rm * 4 + nt) {
+            case 16: st = launch_stage<4, 0>((int)stage, P, base, s); break;
+            case 17: st = launch_stage<4, 1>((int)stage, P, base, s); break;
+            case 18: st = launch_stage<4, 2>((int)stage, P, base, s); break;
+            case 32: st = launch_stage<8, 0>((int)stage, P, base, s); break;
+            case 33: st = launch_stage<8, 1>((int)stage, P, base, s); break;
+            case 34: st = launch_stage<8, 2>((int)stage, P, base, s); break;
+            case 64: st = launch_stage<16, 0>((int)stage, P, base, s); break;
+            case 65: st = launch_stage<16, 1>((int)stage, P, base, s); break;
+            default: st = launch_stage<16, 2>((int)stage, P, base, s); break;
         }
         if (st) return st;
     }

@@ -303,6 +303,7 @@ class CRESSO5(Optimizer):
             return cur
         L = _lib.lib()
         cap = max(n, cur[1] * 2 if cur is not None else 0)
+        cap = (cap + 255) // 256 * 256  # table rows stay 16-byte aligned for the staged copies
         nbytes = np.zeros(1, dtype=np.int64)
         _lib.check(L.cresso_hash_cache_bytes(cap, bins, tables, nbytes.ctypes.data_as(_lib._pi64)), "hash_cache_bytes")
         buf = torch.empty(int(nbytes[0]), dtype=torch.uint8, device=device)
