@@ -332,79 +332,106 @@ spectral_pass_kernel(const GroupHdr* __restrict__ hdr, const DevTensor* __restri
         const int lc = tid & (TC - 1), rs = tid / TC;
         const int wseg = min(TC, 32);
 
-        // stage layout inside one buffer
+        // stage layout inside one buffer: x tile, p tile, bin tiles, row-table rows
         const int off_p = tile * 4;
         const int off_b = off_p + (stage_p_any ? tile * 4 : 0);
         const int off_r = off_b + (PASS >= 2 ? T2 * tile * ib : 0);
-        auto stage_item = [&](int64_t item, int buf) {
+        const int lg_tc = 31 - __clz(TC);
+        const int lg_cpr = lg_tc - 2;                  // log2 of 16-byte chunks per tile row (floats)
+        const int lg_cprb = lg_tc + (ib == 2) - 4;     // same for the bin bytes
+        const int lg_rbcprb = 31 - __clz(RB) + lg_cprb;
+        const int lg_rm2 = 31 - __clz(RM) - 1;         // 16-byte chunks per row-table row = RM / 2
+        // Copies the tiles of item (ct, band) into buffer `buf`: cp.async 16-byte
+        // copies for aligned tensors, per-element loads for the others.
+        auto stage_item = [&](int ct, int band, int buf) {
             unsigned char* sb = s_stage + buf * sbytes;
-            const int64_t loc = item - ibase;
-            const int ct = (int)(loc / n_bands);
-            const int rb = (int)(loc - (int64_t)ct * n_bands) * RB;
+            const int rb = band * RB;
             const int cb = ct * TC;
-            const int cpr = TC >> 2;  // 16-byte chunks per tile row of floats
-            for (int c = tid; c < RB * cpr; c += kThreads) {
-                const int lr = c / cpr, cc = c - lr * cpr;
-                const int r = rb + lr, col = cb + 4 * cc;
-                const bool ok = r < rows32 && col < cols32;
-                const int64_t e = ok ? (int64_t)r * cols32 + col : 0;
-                cp_async16(sb + (lr * TC + 4 * cc) * 4, xsrc + e, ok ? 16 : 0);
-                if (stage_p) cp_async16(sb + off_p + (lr * TC + 4 * cc) * 4, param + e, ok ? 16 : 0);
-            }
-            if (PASS >= 2 && hash_on) {
-                const int cprb = (TC * ib) >> 4;  // 16-byte chunks per tile row of bin indices
-                for (int c = tid; c < T2 * RB * cprb; c += kThreads) {
-                    const int t = c / (RB * cprb);
-                    const int c2 = c - t * RB * cprb;
-                    const int lr = c2 / cprb, cc = c2 - lr * cprb;
-                    const int r = rb + lr;
-                    const bool ok = r < rows32 && cb + (16 / ib) * cc < cols32;
-                    const int64_t g = ok ? ((int64_t)(row032 + r) * gcols32 + col0 + cb) * ib + 16 * cc : 0;
-                    cp_async16(sb + off_b + (t * tile + lr * TC) * ib + 16 * cc, hidx + t * hidx_n * ib + g,
-                               ok ? 16 : 0);
+            if (vec) {
+                for (int c = tid; c < (RB << lg_cpr); c += kThreads) {
+                    const int lr = c >> lg_cpr, cc = c & ((1 << lg_cpr) - 1);
+                    const int r = rb + lr, col = cb + 4 * cc;
+                    const bool ok = r < rows32 && col < cols32;
+                    const int64_t e = ok ? (int64_t)r * cols32 + col : 0;
+                    cp_async16(sb + (lr * TC + 4 * cc) * 4, xsrc + e, ok ? 16 : 0);
+                    if (stage_p) cp_async16(sb + off_p + (lr * TC + 4 * cc) * 4, param + e, ok ? 16 : 0);
+                }
+                if (PASS >= 2 && hash_on) {
+                    for (int c = tid; c < (T2 << lg_rbcprb); c += kThreads) {
+                        const int t = c >> lg_rbcprb;
+                        const int c2 = c & ((1 << lg_rbcprb) - 1);
+                        const int lr = c2 >> lg_cprb, cc = c2 & ((1 << lg_cprb) - 1);
+                        const int r = rb + lr;
+                        const bool ok = r < rows32 && cb + (cc << (4 - (ib == 2))) < cols32;
+                        const int64_t g = ok ? ((int64_t)(row032 + r) * gcols32 + col0 + cb) * ib + 16 * cc : 0;
+                        cp_async16(sb + off_b + (t * tile + lr * TC) * ib + 16 * cc, hidx + t * hidx_n * ib + g,
+                                   ok ? 16 : 0);
+                    }
+                }
+                if (PASS >= 2) {
+                    for (int c = tid; c < (RB << lg_rm2); c += kThreads) {
+                        const bool ok = rb + (c >> lg_rm2) < rows32;
+                        const int64_t g = ok ? (int64_t)(row032 + rb) * 2 * RM + 4 * c : 0;
+                        cp_async16(sb + off_r + 16 * c, rowtab + g, ok ? 16 : 0);
+                    }
+                }
+                cp_async_commit();
+            } else {
+                const int col = cb + lc;
+                for (int m = 0; m < ITERS; ++m) {
+                    const int lr = rs + RPI * m, r = rb + lr;
+                    const bool ok = r < rows32 && col < cols32;
+                    const int64_t e = (int64_t)r * cols32 + col;
+                    const int o = lr * TC + lc;
+                    reinterpret_cast<float*>(sb)[o] = ok ? xsrc[e] : 0.0f;
+                    if (stage_p) reinterpret_cast<float*>(sb + off_p)[o] = ok ? param[e] : 0.0f;
+                    if (PASS >= 2 && hash_on) {
+                        const int64_t g = ((int64_t)(row032 + r) * gcols32 + col0 + col);
+                        for (int t = 0; t < T2; ++t) {
+                            if (idx8)
+                                sb[off_b + t * tile + o] = ok ? hidx[t * hidx_n + g] : 0;
+                            else
+                                reinterpret_cast<uint16_t*>(sb + off_b)[t * tile + o] =
+                                    ok ? reinterpret_cast<const uint16_t*>(hidx)[t * hidx_n + g] : 0;
+                        }
+                    }
                 }
             }
-            if (PASS >= 2) {
-                const int n16 = RB * 2 * RM / 4;  // 16-byte chunks of the item's row-table rows
-                for (int c = tid; c < n16; c += kThreads) {
-                    const int lr = (4 * c) / (2 * RM);
-                    const bool ok = rb + lr < rows32;
-                    const int64_t g = ok ? (int64_t)(row032 + rb) * 2 * RM + 4 * c : 0;
-                    cp_async16(sb + off_r + 16 * c, rowtab + g, ok ? 16 : 0);
-                }
-            }
-            cp_async_commit();
         };
 
+        float g32[PASS == 4 ? kGram : 1];
+#pragma unroll
+        for (int q = 0; q < (PASS == 4 ? kGram : 1); ++q) g32[q] = 0.0f;
         int buf = 0;
-        if (vec && it < seg_end) stage_item(it, 0);
+        int ct = (int)((it - ibase) / n_bands);
+        int band = (int)((it - ibase) - (int64_t)ct * n_bands);
+        if (vec && it < seg_end) stage_item(ct, band, 0);
+        int items_since_flush = 0;
         for (; it < seg_end; ++it) {
-            const int64_t local = it - ibase;
-            const int ct = (int)(local / n_bands);
-            const int band = (int)(local - (int64_t)ct * n_bands);
             const int col = ct * TC + lc;
             const bool cvalid = col < cols32;
             const int gc = (int)col0 + (cvalid ? col : 0);
             const int rbase = band * RB;
+            const int nband = band + 1 == n_bands ? 0 : band + 1;
+            const int nct = band + 1 == n_bands ? ct + 1 : ct;
             if (vec) {
                 if (it + 1 < seg_end) {
-                    stage_item(it + 1, buf ^ 1);
+                    stage_item(nct, nband, buf ^ 1);
                     cp_async_wait<1>();
                 } else {
                     cp_async_wait<0>();
                 }
-                __syncthreads();
+            } else {
+                stage_item(ct, band, buf);
             }
-            // tile bases: shared memory (staged) or global (direct)
+            __syncthreads();
+            // tiles of this item in shared memory (row table: staged, or global for unaligned tensors)
             const unsigned char* sb = s_stage + buf * sbytes;
-            const float* xb = vec ? reinterpret_cast<const float*>(sb) : xsrc + (int64_t)rbase * cols32 + ct * TC;
-            const float* pb = vec ? reinterpret_cast<const float*>(sb + off_p) : param + (int64_t)rbase * cols32 + ct * TC;
-            const int xs = vec ? TC : cols32;
-            const unsigned char* bb = vec ? sb + off_b
-                                          : hidx + ((int64_t)(row032 + rbase) * gcols32 + col0 + ct * TC) * ib;
-            const int64_t bts = vec ? (int64_t)tile * ib : hidx_n * ib;  // bytes between tables
-            const int bs = vec ? TC : gcols32;                            // row stride in indices
-            const float* rtb = vec ? reinterpret_cast<const float*>(sb + off_r) : rowtab + (int64_t)(row032 + rbase) * 2 * RM;
+            const float* xb = reinterpret_cast<const float*>(sb);
+            const float* pb = reinterpret_cast<const float*>(sb + off_p);
+            const unsigned char* bb = sb + off_b;
+            const float* rtb = vec ? reinterpret_cast<const float*>(sb + off_r)
+                                   : rowtab + (int64_t)(row032 + rbase) * 2 * RM;
 
             float U1[RM], V1[RM], U2[RM], V2[RM];
             float colf = 1.0f;
@@ -418,14 +445,9 @@ spectral_pass_kernel(const GroupHdr* __restrict__ hdr, const DevTensor* __restri
                 }
             }
             float z1[RM], z2[RM];
-            float g32[PASS == 4 ? kGram : 1];
             if constexpr (PASS == 2 || PASS == 3) {
 #pragma unroll
                 for (int q = 0; q < RM; ++q) z1[q] = z2[q] = 0.0f;
-            }
-            if constexpr (PASS == 4) {
-#pragma unroll
-                for (int q = 0; q < kGram; ++q) g32[q] = 0.0f;
             }
             float s0 = 0.0f, s1 = 0.0f, colacc = 0.0f, zc = 0.0f;
 
@@ -437,22 +459,22 @@ spectral_pass_kernel(const GroupHdr* __restrict__ hdr, const DevTensor* __restri
                     const int lr = rs + RPI * (m0 + u);
                     const int r = rbase + lr;
                     if (!(cvalid && r < rows32)) continue;
-                    const float xval = xb[lr * xs + lc];
+                    const int o = lr * TC + lc;  // offset inside the item tiles
+                    const float xval = xb[o];
                     auto bin_of = [&](int t) -> int {
                         if (NT > 0 || t < 2) {
-                            const unsigned char* q = bb + t * bts + (int64_t)(lr * bs + lc) * ib;
-                            return idx8 ? (int)*q : (int)*reinterpret_cast<const uint16_t*>(q);
+                            return idx8 ? (int)bb[t * tile + o] : (int)reinterpret_cast<const uint16_t*>(bb)[t * tile + o];
                         }
                         const int64_t g = ((int64_t)(row032 + r) * gcols32 + gc) * ib + t * hidx_n * ib;
                         return idx8 ? (int)__ldg(hidx + g) : (int)__ldg(reinterpret_cast<const uint16_t*>(hidx + g));
                     };
                     if constexpr (PASS == 1) {
                         float f = sgn * xval;
-                        if (wd_on) f = f + wd * pb[lr * xs + lc];
+                        if (wd_on) f = f + wd * pb[o];
                         s0 = fmaf(f, f, s0);
                     } else if constexpr (PASS == 2) {
                         float f = sgn * xval;
-                        if (wd_on) f = f + wd * pb[lr * xs + lc];
+                        if (wd_on) f = f + wd * pb[o];
                         float a1[RM], a2[RM];
                         load_row<RM>(rtb, lr, a1, a2);
                         const float rel = fminf(fabsf(f) * inv_scale + eps, 1.0e4f);
@@ -478,7 +500,7 @@ spectral_pass_kernel(const GroupHdr* __restrict__ hdr, const DevTensor* __restri
                         }
                     } else if constexpr (PASS == 3) {
                         float f = sgn * xval;
-                        if (wd_on) f = f + wd * pb[lr * xs + lc];
+                        if (wd_on) f = f + wd * pb[o];
                         float a1[RM], a2[RM];
                         load_row<RM>(rtb, lr, a1, a2);
                         const float rel = fminf(fabsf(f) * inv_scale + eps, 1.0e4f);
@@ -556,7 +578,7 @@ spectral_pass_kernel(const GroupHdr* __restrict__ hdr, const DevTensor* __restri
                         }
                         const DriveParts dp = drive_parts(t, pred, dk);
                         const float drive = c_u * dp.u + c_root * dp.root + c_t * t + comb + c_nov * dp.nov + c_hp * hpv;
-                        param[(int64_t)r * cols32 + col] = pb[lr * xs + lc] + neg_lr * (drive * gain);
+                        param[(int64_t)r * cols32 + col] = pb[o] + neg_lr * (drive * gain);
                     }
                 }
                 if constexpr (PASS == 2) {
@@ -617,8 +639,15 @@ spectral_pass_kernel(const GroupHdr* __restrict__ hdr, const DevTensor* __restri
                     }
                 }
             } else if constexpr (PASS == 4) {
+                // float32 Gram partials over up to 4 items, then into the float64 block state
+                if (++items_since_flush == 4 || it + 1 == seg_end) {
 #pragma unroll
-                for (int q = 0; q < kGram; ++q) s_acc[q * kThreads + tid] += (double)g32[q];
+                    for (int q = 0; q < kGram; ++q) {
+                        s_acc[q * kThreads + tid] += (double)g32[q];
+                        g32[q] = 0.0f;
+                    }
+                    items_since_flush = 0;
+                }
             }
             if constexpr (PASS == 2) {
                 if (TC > 32) {
@@ -640,7 +669,9 @@ spectral_pass_kernel(const GroupHdr* __restrict__ hdr, const DevTensor* __restri
                 }
             }
             __syncthreads();  // this buffer (and the reduction scratch) is free again
-            buf ^= 1;
+            if (vec) buf ^= 1;
+            ct = nct;
+            band = nband;
         }  // items of the segment
 
         // ---- segment flush: one record per (block, tensor)
