@@ -144,11 +144,6 @@ __global__ void __launch_bounds__(kThreads) scalar_route_kernel(const ScalHdr* _
         float* rowpart = D.work;  // [n_ct * nw][rows]
         const int nw = D.nw;
         float* colsum = D.work + (int64_t)D.n_ct * nw * D.rows + D.rows;  // [cols]
-        if (inst_mode == 3) {
-            int64_t tot = 0;
-            for (int64_t a = 0; a < D.ndim; ++a) tot += D.dims[a];
-            for (int64_t a = tid; a < tot; a += kThreads) D.work[a] = 0.0f;
-        }
         __syncthreads();
         double sL = 0.0, sd = 0.0;
         float colacc = 0.0f;
@@ -180,15 +175,6 @@ __global__ void __launch_bounds__(kThreads) scalar_route_kernel(const ScalHdr* _
                 d = dens(rel);
                 sd += (double)d;
                 colacc += d;
-                if (inst_mode == 3) {
-                    int64_t rem = e, base = 0;
-                    for (int64_t a = 0; a < D.ndim; ++a) base += D.dims[a];
-                    for (int64_t a = D.ndim - 1; a >= 0; --a) {
-                        base -= D.dims[a];
-                        atomicAdd(&D.work[base + rem % D.dims[a]], d);
-                        rem /= D.dims[a];
-                    }
-                }
             }
             if (inst_mode == 2) {
                 float v = d;
@@ -240,12 +226,28 @@ __global__ void __launch_bounds__(kThreads) scalar_route_kernel(const ScalHdr* _
             for (int64_t c = tid; c < D.cols; c += kThreads)
                 colsum[c] = expf(kk * logf(fmaxf((float)((double)colsum[c] / (double)D.rows) / gm, eps)));
         } else if (inst_mode == 3) {
-            int64_t base = 0;
-            for (int64_t a = 0; a < D.ndim; ++a) {
+            // N-d marginals: one thread per (axis, coordinate) sums its slab in a fixed
+            // order (deterministic), then turns the mean into the axis factor.
+            int64_t tot = 0;
+            for (int64_t a = 0; a < D.ndim; ++a) tot += D.dims[a];
+            for (int64_t j = tid; j < tot; j += kThreads) {
+                int64_t a = 0, c = j;
+                while (c >= D.dims[a]) {
+                    c -= D.dims[a];
+                    ++a;
+                }
+                int64_t inner = 1;
+                for (int64_t b = a + 1; b < D.ndim; ++b) inner *= D.dims[b];
+                const int64_t outer = D.N / (D.dims[a] * inner);
+                double m = 0.0;
+                for (int64_t o = 0; o < outer; ++o)
+                    for (int64_t i = 0; i < inner; ++i) {
+                        const int64_t e = (o * D.dims[a] + c) * inner + i;
+                        const float f = force(e);
+                        m += (double)dens(fminf(fabsf(f) * inv_scale + eps, 1.0e4f));
+                    }
                 const double per = N / (double)D.dims[a];
-                for (int64_t c = tid; c < D.dims[a]; c += kThreads)
-                    D.work[base + c] = expf(kk * logf(fmaxf((float)((double)D.work[base + c] / per) / gm, eps)));
-                base += D.dims[a];
+                D.work[j] = expf(kk * logf(fmaxf((float)(m / per) / gm, eps)));
             }
         }
         __syncthreads();

@@ -193,6 +193,14 @@ struct PassCfg {
     static constexpr bool kP = PASS == 5;              // parameter tile always staged
 };
 
+// Copies of the hash-bin accumulators in shared memory: up to four per warp
+// (selected by lane & 3, which cuts same-address conflicts of the atomics)
+// within a 32 KB budget.
+__host__ __device__ inline int bin_copies(int tb) {
+    const int c = 8192 / (tb + 1);
+    return c < 1 ? 1 : (c > 4 * kWarps ? 4 * kWarps : c);
+}
+
 // Shared-memory bytes of one staging buffer of an item.
 __host__ __device__ inline int stage_bytes(int iters, int rm, int tables2, int idx_bytes, bool with_p, int rb_max) {
     const int tile = 256 * iters;
@@ -237,7 +245,9 @@ spectral_pass_kernel(const GroupHdr* __restrict__ hdr, const DevTensor* __restri
     // shared memory carve-up
     constexpr bool kBins = PASS == 2 || PASS == 3;
     constexpr bool kTab = PASS >= 3;
-    const int ncopies = kBins ? max(1, min(kWarps, kMaxTB / max(TB, 1))) : 0;
+    // bin copies: four per warp (lane & 3) when they fit, padded so copies sit in different banks
+    const int ncopies = kBins ? bin_copies(TB) : 0;
+    const int cstride = TB + 1;
     const int tile = 256 * ITERS;
     const int sbytes = stage_bytes(ITERS, RM, PASS >= 2 ? T2 : 0, ib, stage_p_any, (int)hdr->rb_max);
     unsigned char* s_stage = smem_raw;                                        // 2 * sbytes
@@ -245,8 +255,8 @@ spectral_pass_kernel(const GroupHdr* __restrict__ hdr, const DevTensor* __restri
     double* s_tot = s_red + kNSRec * kWarps;                                  // kNSRec
     double* s_acc = s_tot + kNSRec;                                           // NACC * kThreads
     float* s_coef = reinterpret_cast<float*>(s_acc + NACC * kThreads);       // 4 * RM + 4
-    float* s_bins = s_coef + 4 * RM + 4;                                      // ncopies * TB
-    float* s_tab = s_bins + (kBins ? ncopies * TB : 0);                       // TB
+    float* s_bins = s_coef + 4 * RM + 4;                                      // ncopies * (TB + 1)
+    float* s_tab = s_bins + (kBins ? ncopies * cstride : 0);                  // TB
     float* s_rowred = s_tab + (kTab ? TB : 0);                                // 8 * ITERS
     float* s_colred = s_rowred + (PASS == 2 ? 8 * ITERS : 0);                 // kThreads
 
@@ -314,7 +324,7 @@ spectral_pass_kernel(const GroupHdr* __restrict__ hdr, const DevTensor* __restri
             }
         }
         if constexpr (kBins) {
-            for (int b = tid; b < ncopies * TB; b += kThreads) s_bins[b] = 0.0f;
+            for (int b = tid; b < ncopies * cstride; b += kThreads) s_bins[b] = 0.0f;
         }
         if constexpr (kTab) {
             if (hash_on) {
@@ -326,7 +336,7 @@ spectral_pass_kernel(const GroupHdr* __restrict__ hdr, const DevTensor* __restri
             for (int j = 0; j < NACC; ++j) s_acc[j * kThreads + tid] = 0.0;
         }
         __syncthreads();
-        float* my_bins = s_bins + (kBins ? (warp % max(ncopies, 1)) * TB : 0);
+        float* my_bins = s_bins + (kBins ? ((warp * 4 + (lane & 3)) % max(ncopies, 1)) * cstride : 0);
         const float K1 = kTab ? s_coef[4 * RM] : 0.f, K2 = kTab ? s_coef[4 * RM + 1] : 0.f;
         double acc0 = 0.0, acc1 = 0.0;
         const int lc = tid & (TC - 1), rs = tid / TC;
@@ -478,7 +488,7 @@ spectral_pass_kernel(const GroupHdr* __restrict__ hdr, const DevTensor* __restri
                         float a1[RM], a2[RM];
                         load_row<RM>(rtb, lr, a1, a2);
                         const float rel = fminf(fabsf(f) * inv_scale + eps, 1.0e4f);
-                        const float ds = exp2f(ep * log2f(rel));  // rel >= eps > 0
+                        const float ds = exp2f(ep * __log2f(rel));  // rel >= eps > 0 (normal)
                         // log1p(ds) - 1/2: the density is centred before the float32 partial sums
                         // (the constant is added back exactly in the finalize)
                         const float L = log1pf(ds);
@@ -516,16 +526,17 @@ spectral_pass_kernel(const GroupHdr* __restrict__ hdr, const DevTensor* __restri
                         }
                         int bi[NT > 0 ? NT : 2];
                         if (hash_on) {
-                            float lsum = 0.0f;
+                            // hash metric exp(mean_t log m_t) = prod_t m_t^(1/T), roots tabulated per bin
+                            float hm = 1.0f;
 #pragma unroll
                             for (int t = 0; t < (NT > 0 ? NT : T); ++t) {
                                 const int bt = bin_of(t);
                                 if (NT > 0 || t < 2) bi[NT > 0 ? t : (t & 1)] = bt;
-                                lsum += s_tab[t * B + bt];
+                                hm *= s_tab[t * B + bt];
                             }
-                            den = den * clampf(expf(lsum * invT), 0.08f, 12.0f);
+                            den = den * clampf(hm, 0.08f, 12.0f);
                         }
-                        const float t = clampf(__fdiv_rn(f, den + eps), -1.0e4f, 1.0e4f);
+                        const float t = clampf(__fdividef(f, den + eps), -1.0e4f, 1.0e4f);
                         tbuf[(int64_t)r * cols32 + col] = t;
                         const float pred = recon_dot_nz<RM>(K2, a1, a2, U2, V2);
                         const float err = t - pred;
@@ -700,7 +711,7 @@ spectral_pass_kernel(const GroupHdr* __restrict__ hdr, const DevTensor* __restri
                     if (hash_on) {
                         for (int b = tid; b < TB; b += kThreads) {
                             float s = 0.0f;
-                            for (int c = 0; c < ncopies; ++c) s += s_bins[c * TB + b];
+                            for (int c = 0; c < ncopies; ++c) s += s_bins[c * cstride + b];
                             rec_bins[(int64_t)rec * TB + b] = s;
                         }
                     }
@@ -823,7 +834,8 @@ __global__ void finalize2_kernel(const GroupHdr* __restrict__ hdr, const DevTens
             for (int b = tid; b < B; b += kThreads) {
                 const float hm = fmaxf(D.h_energy[t * B + b] / meanE, eps);
                 const float v = clampf(powf(hm, ex), 0.08f, 12.0f);
-                D.htab[t * B + b] = logf(fmaxf(v, eps));
+                // per-bin root m^(1/T); the per-element metric is the product over tables
+                D.htab[t * B + b] = (float)exp(log((double)fmaxf(v, eps)) / (double)T);
             }
             __syncthreads();
         }
@@ -1379,8 +1391,7 @@ static size_t pass_smem(int pass, const GroupHdr& H, int64_t iters) {
     b += (size_t)(kNSRec * kWarps + kNSRec + nacc * kThreads) * sizeof(double);
     b += (size_t)(4 * rm + 4) * 4;
     if (pass == 2 || pass == 3) {
-        const int ncopies = std::max(1, std::min(kWarps, kMaxTB / std::max(tb, 1)));
-        b += (size_t)ncopies * tb * 4;
+        b += (size_t)bin_copies(tb) * (tb + 1) * 4;
     }
     if (pass >= 3) b += (size_t)tb * 4;
     if (pass == 2) b += (size_t)(8 * iters + kThreads) * 4;

@@ -1,0 +1,142 @@
+"""Process entry points for the multi-process tests (importable by spawn)."""
+
+from __future__ import annotations
+
+import datetime
+import os
+import sys
+import time
+from pathlib import Path
+
+import numpy as np
+import torch
+import torch.distributed as dist
+
+ROOT = Path(__file__).resolve().parents[1]
+if str(ROOT) not in sys.path:
+    sys.path.insert(0, str(ROOT))
+
+
+def _init(rank, world, port, backend, timeout_s=60):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group(backend, rank=rank, world_size=world, timeout=datetime.timedelta(seconds=timeout_s))
+
+
+def stages_worker(rank, world, port, outdir):
+    """RowShardedCRESSO5 stage orchestration with a fake kernel runner (gloo)."""
+    from cresso_b200 import _lib
+    from cresso_b200.distributed import RowShardedCRESSO5
+
+    _init(rank, world, port, "gloo")
+    opt = RowShardedCRESSO5([torch.nn.Parameter(torch.zeros(4))], process_group=None)
+    layout = np.zeros(9, dtype=np.int64)
+    # four reduction vectors at 256-byte offsets with lengths 1, 5, 3, 29
+    lens = [1, 5, 3, 29]
+    off = 0
+    for k, n in enumerate(lens, start=1):
+        layout[2 * k - 1] = off
+        layout[2 * k] = n
+        off += (8 * n + 255) // 256 * 256
+    scratch = torch.zeros(off, dtype=torch.uint8)
+    calls = []
+
+    def run(b, e):
+        calls.append((b, e))
+        # the stage that completes vector k writes rank+1 into it
+        for k, bound in enumerate(_lib.REDUCTION_BOUNDARIES, start=1):
+            if e == bound:
+                opt._reduction_view(scratch, layout, k).fill_(float(rank + 1) * k)
+
+    opt._spectral_stages(run, scratch, layout)
+    out = [opt._reduction_view(scratch, layout, k).clone() for k in range(1, 5)]
+    torch.save({"calls": calls, "out": out}, os.path.join(outdir, f"stages_{rank}.pt"))
+    dist.destroy_process_group()
+
+
+def zero_gather_worker(rank, world, port, outdir):
+    from cresso_b200.distributed import ZeroCRESSO5
+
+    _init(rank, world, port, "gloo")
+    shapes = [(7, 5), (13,), (4, 4), (30,), (2, 3)]
+    ps = [torch.nn.Parameter(torch.full(s, -1.0)) for s in shapes]
+    opt = ZeroCRESSO5(ps)
+    for i, p in enumerate(ps):
+        if opt.owner[p] == rank:
+            p.data.fill_(float(100 * i + 7))
+    opt.gather_params()
+    torch.save({"vals": [p.detach().clone() for p in ps], "owner": [opt.owner[p] for p in ps]},
+               os.path.join(outdir, f"zero_{rank}.pt"))
+    dist.destroy_process_group()
+
+
+def failing_rank_worker(rank, world, port, outdir):
+    """Rank 1 fails before the first exchange; rank 0 must see an error, not hang."""
+    from cresso_b200.distributed import RowShardedCRESSO5
+
+    _init(rank, world, port, "gloo", timeout_s=5)
+    opt = RowShardedCRESSO5([torch.nn.Parameter(torch.zeros(4))])
+    layout = np.zeros(9, dtype=np.int64)
+    for k in range(1, 5):
+        layout[2 * k - 1] = 256 * (k - 1)
+        layout[2 * k] = 4
+    scratch = torch.zeros(1024, dtype=torch.uint8)
+
+    def run(b, e):
+        if rank == 1:
+            raise RuntimeError("injected failure on rank 1")
+
+    t0 = time.time()
+    status = "ok"
+    try:
+        opt._spectral_stages(run, scratch, layout)
+    except Exception as exc:  # the survivor's collective ends with an error
+        status = type(exc).__name__ + ": " + str(exc)[:200]
+    with open(os.path.join(outdir, f"fail_{rank}.txt"), "w") as f:
+        f.write(f"{status}\n{time.time() - t0:.2f}\n")
+    # no destroy_process_group: the peer is gone
+
+
+def gpu_row_shard_worker(rank, world, port, outdir):
+    """Row-sharded CUDA step on `world` GPUs against the single-GPU step."""
+    import cresso_b200
+    from cresso_b200.distributed import RowShardedCRESSO5, mark_row_shard, row_block
+
+    torch.cuda.set_device(rank)
+    _init(rank, world, port, "nccl", timeout_s=120)
+    dev = torch.device("cuda", rank)
+    g = torch.Generator().manual_seed(3)
+    shapes = [(256, 192), (1536,), (96, 64)]
+    inits = [torch.randn(s, generator=g) * 0.02 for s in shapes]
+    grads = [[torch.randn(s, generator=g) * 1e-3 for s in shapes] for _ in range(3)]
+    kw = dict(rank=8, hash_bins=64, hash_tables=2, min_spectral_size=1024)
+    ps = []
+    for s, x in zip(shapes, inits):
+        a, b = row_block(s[0], rank, world)
+        p = torch.nn.Parameter(x[a:b].clone().to(dev))
+        mark_row_shard(p, s, a)
+        ps.append(p)
+    opt = RowShardedCRESSO5(ps, **kw)
+    for gs in grads:
+        for p, s, gg in zip(ps, shapes, gs):
+            a, b = row_block(s[0], rank, world)
+            p.grad = gg[a:b].clone().to(dev)
+        opt.step()
+    torch.cuda.synchronize()
+    shard = [p.detach().cpu() for p in ps]
+    states = [{k: (v.detach().cpu() if torch.is_tensor(v) else v) for k, v in opt.state[p].items()} for p in ps]
+    if rank == 0:
+        full = [torch.nn.Parameter(x.clone().to(dev)) for x in inits]
+        ref = cresso_b200.CRESSO5(full, **kw)
+        for gs in grads:
+            for p, gg in zip(full, gs):
+                p.grad = gg.to(dev)
+            ref.step()
+        torch.cuda.synchronize()
+        ref_out = ([p.detach().cpu() for p in full],
+                   [{k: (v.detach().cpu() if torch.is_tensor(v) else v) for k, v in ref.state[p].items()} for p in full])
+    else:
+        ref_out = None
+    torch.save({"shard": shard, "states": states, "ref": ref_out}, os.path.join(outdir, f"gpu_rs_{rank}.pt"))
+    dist.barrier()
+    dist.destroy_process_group()

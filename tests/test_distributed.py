@@ -1,0 +1,103 @@
+"""Multi-process host logic of the distributed optimizers on CPU ranks (gloo),
+and the row-sharded CUDA step on 2 GPUs (NCCL) when the box has them."""
+
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+from cresso_b200 import _lib
+from cresso_b200.distributed import lpt_partition, row_block
+from tests import _dist_workers as W
+
+
+def free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def spawn(fn, world, tmp_path):
+    mp.spawn(fn, args=(world, free_port(), str(tmp_path)), nprocs=world, join=True)
+
+
+@pytest.mark.parametrize("length,world", [(4096, 8), (11008, 8), (7, 3), (32000, 6), (1, 2)])
+def test_row_blocks_tile_the_rows(length, world):
+    blocks = [row_block(length, r, world) for r in range(world)]
+    assert blocks[0][0] == 0 and blocks[-1][1] == length
+    for (a, b), (c, d) in zip(blocks, blocks[1:]):
+        assert b == c
+    sizes = [b - a for a, b in blocks]
+    assert max(sizes) - min(sizes) <= 1
+
+
+def test_lpt_partition_is_balanced_and_deterministic():
+    sizes = [32000 * 4096] * 2 + [4096 * 4096] * 128 + [11008 * 4096] * 96 + [4096] * 64
+    owner = lpt_partition(sizes, 8)
+    assert owner == lpt_partition(sizes, 8)
+    load = np.zeros(8)
+    for s, o in zip(sizes, owner):
+        load[o] += s
+    assert load.max() / load.mean() < 1.02
+
+
+def test_row_sharded_stage_orchestration_gloo(tmp_path):
+    spawn(W.stages_worker, 2, tmp_path)
+    r0 = torch.load(tmp_path / "stages_0.pt")
+    r1 = torch.load(tmp_path / "stages_1.pt")
+    assert r0["calls"] == [(0, 3), (3, 6), (6, 9), (9, 12), (12, _lib.SPECTRAL_STAGES)]
+    for k, (a, b) in enumerate(zip(r0["out"], r1["out"]), start=1):
+        # each rank wrote (rank + 1) * k; the exchange sums them
+        assert torch.equal(a, b)
+        assert torch.all(a == 3.0 * k)
+
+
+def test_zero_partition_gathers_owned_params_gloo(tmp_path):
+    spawn(W.zero_gather_worker, 2, tmp_path)
+    r0 = torch.load(tmp_path / "zero_0.pt")
+    r1 = torch.load(tmp_path / "zero_1.pt")
+    assert set(r0["owner"]) == {0, 1}
+    for i, (a, b) in enumerate(zip(r0["vals"], r1["vals"])):
+        assert torch.all(a == 100 * i + 7) and torch.equal(a, b)
+
+
+def test_failed_rank_surfaces_as_an_error_not_a_hang_gloo(tmp_path):
+    ctx = mp.get_context("spawn")
+    port = free_port()
+    procs = [ctx.Process(target=W.failing_rank_worker, args=(r, 2, port, str(tmp_path))) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=60)
+    for p in procs:
+        if p.is_alive():
+            p.kill()
+            pytest.fail("a rank hung instead of failing")
+    s0 = (tmp_path / "fail_0.txt").read_text().splitlines()
+    s1 = (tmp_path / "fail_1.txt").read_text().splitlines()
+    assert "injected failure" in s1[0]
+    assert s0[0] != "ok" and float(s0[1]) < 30.0
+
+
+@pytest.mark.gpu
+def test_row_sharded_step_matches_single_gpu(tmp_path):
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    spawn(W.gpu_row_shard_worker, 2, tmp_path)
+    r = [torch.load(tmp_path / f"gpu_rs_{k}.pt") for k in range(2)]
+    ref_params, ref_states = r[0]["ref"]
+    for i, full in enumerate(ref_params):
+        got = torch.cat([r[0]["shard"][i], r[1]["shard"][i]])
+        rel = float((got.double() - full.double()).pow(2).mean().sqrt() / full.double().pow(2).mean().sqrt())
+        assert rel <= 1e-6, (i, rel)
+        for k, v in ref_states[i].items():
+            a, b = r[0]["states"][i][k], r[1]["states"][i][k]
+            if torch.is_tensor(v):
+                assert torch.equal(a, b), (i, k)  # every rank holds the same rank / hash state
+                if v.dtype.is_floating_point:
+                    d = float((a.double() - v.double()).abs().max())
+                    assert d <= 1e-4 * max(float(v.double().abs().max()), 1e-6), (i, k, d)
+            else:
+                assert a == v == b
