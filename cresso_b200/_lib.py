@@ -34,6 +34,7 @@ MAX_RANK = 16
 SPECTRAL_STAGES = 14
 # stage boundaries after which reduction vector k (1..4) is complete
 REDUCTION_BOUNDARIES = (3, 6, 9, 12)
+NOALLOC_SCRATCH_BYTES = 8 << 20  # CRESSO_NOALLOC_SCRATCH_BYTES
 
 # Field order of cresso_tensor_desc; every field is 8 bytes.
 DESC_FIELDS = (
@@ -54,6 +55,7 @@ EXPORTS = (
     "cresso_hash_cache_init", "cresso_shape_workspace_bytes", "cresso_shape_workspace_init",
     "cresso_basis_project", "cresso_basis_reconstruct", "cresso_instant_axis_metric",
     "cresso_spectral_layout", "cresso_spectral_run", "cresso_scalar_scratch_bytes", "cresso_scalar_run",
+    "cresso_scalar_run_noalloc",
 )
 
 _lock = threading.Lock()
@@ -87,6 +89,7 @@ def _declare(lib) -> None:
         "cresso_spectral_run": (ctypes.c_int, [_p, _i64, _p, _p, _i64, _i64, _i64, _i64, _p]),
         "cresso_scalar_scratch_bytes": (ctypes.c_int, [_p, _i64, _pi64]),
         "cresso_scalar_run": (ctypes.c_int, [_p, _i64, _p, _p, _i64, _p]),
+        "cresso_scalar_run_noalloc": (ctypes.c_int, [_p, _i64, _p, _p]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)

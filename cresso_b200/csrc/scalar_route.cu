@@ -11,6 +11,7 @@
 #include <stdint.h>
 
 #include <algorithm>
+#include <mutex>
 #include <vector>
 
 #include "cresso_common.cuh"
@@ -528,4 +529,66 @@ int cresso_scalar_run(const cresso_tensor_desc* descs, int64_t n, const cresso_h
     return CRESSO_OK;
 }
 
+// ---------------------------------------------------------------------------
+// Allocation-free variant of the scalar-route step.
+//
+// Its scratch (the launch header, the tensor descriptors and the per-tensor
+// work floats) lives in this file-scope device array instead of caller memory.
+// Every GPU that loads the library keeps the array until the process exits.
+// ---------------------------------------------------------------------------
+static __device__ __align__(256) unsigned char g_noalloc_scratch[CRESSO_NOALLOC_SCRATCH_BYTES];
+
+static std::mutex g_noalloc_mutex;
+static void* g_noalloc_addr[256] = {nullptr};  // device address of the array, per device ordinal
+
+// Device address of g_noalloc_scratch on the current device.  In host code the
+// array's name is only a host-side stand-in, so the address is looked up once
+// per device with cudaGetSymbolAddress (with that device current) and cached.
+static int noalloc_scratch_address(void** out) {
+    int dev = -1;
+    CRESSO_CUDA(cudaGetDevice(&dev));
+    CRESSO_REQUIRE(dev >= 0 && dev < 256, CRESSO_EUNSUPPORTED, "scalar_run_noalloc: device ordinal %d out of range", dev);
+    std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+    if (g_noalloc_addr[dev] == nullptr) {
+        void* ptr = nullptr;
+        CRESSO_CUDA(cudaGetSymbolAddress(&ptr, g_noalloc_scratch));
+        CRESSO_REQUIRE(ptr != nullptr, CRESSO_ECUDA, "scalar_run_noalloc: cudaGetSymbolAddress returned NULL");
+        g_noalloc_addr[dev] = ptr;
+    }
+    *out = g_noalloc_addr[dev];
+    return CRESSO_OK;
+}
+
 }  // extern "C"
+
+extern "C" int cresso_scalar_run_noalloc(const cresso_tensor_desc* descs, int64_t n, const cresso_hparams* hp,
+                                         cresso_stream_t stream) {
+    CRESSO_REQUIRE(hp != nullptr, CRESSO_EINVAL, "scalar_run_noalloc: NULL hparams");
+    std::vector<ScalTensor> dts;
+    int64_t bytes = 0;
+    int st = scal_layout(descs, n, &dts, &bytes);
+    if (st) return st;
+    CRESSO_REQUIRE(bytes <= (int64_t)CRESSO_NOALLOC_SCRATCH_BYTES, CRESSO_ESCRATCH,
+                   "scalar_run_noalloc: these %lld tensors need %lld bytes of scratch, more than the %lld-byte "
+                   "built-in array; split them over several calls or use cresso_scalar_run",
+                   (long long)n, (long long)bytes, (long long)CRESSO_NOALLOC_SCRATCH_BYTES);
+    void* scratch = nullptr;
+    st = noalloc_scratch_address(&scratch);
+    if (st) return st;
+    // Same launch as cresso_scalar_run, on the built-in array.  Nothing in the
+    // array has to start at zero: the header and descriptors are uploaded here
+    // and the kernel writes every work float before reading it.
+    char* base = (char*)scratch;
+    for (auto& S : dts) S.work = (float*)(base + (intptr_t)S.work);
+    ScalHdr h{};
+    h.n = n;
+    memcpy(h.hp, hp, sizeof(cresso_hparams));
+    cudaStream_t s = (cudaStream_t)stream;
+    const int64_t off_dts = align_up((int64_t)sizeof(ScalHdr), 256);
+    CRESSO_CUDA(cudaMemcpyAsync(base, &h, sizeof(h), cudaMemcpyHostToDevice, s));
+    CRESSO_CUDA(cudaMemcpyAsync(base + off_dts, dts.data(), sizeof(ScalTensor) * n, cudaMemcpyHostToDevice, s));
+    scalar_route_kernel<<<(unsigned)n, kThreads, 0, s>>>(reinterpret_cast<const ScalHdr*>(base),
+                                                         reinterpret_cast<const ScalTensor*>(base + off_dts));
+    CRESSO_LAUNCHED("scalar_route_kernel");
+    return CRESSO_OK;
+}

@@ -195,6 +195,29 @@ CRESSO_API int cresso_scalar_scratch_bytes(const cresso_tensor_desc* descs, int6
 CRESSO_API int cresso_scalar_run(const cresso_tensor_desc* descs, int64_t n, const cresso_hparams* hp, void* scratch,
                       int64_t scratch_bytes, cresso_stream_t stream);
 
+/* ---------------------------------------------- allocation-free entry ---- */
+
+/* Size of the library's built-in device scratch array (8 MiB). */
+#define CRESSO_NOALLOC_SCRATCH_BYTES (8u << 20)
+
+/* cresso_scalar_run without caller scratch.  This entry point has no
+ * counterpart in the reference.  It is for callers that cannot allocate
+ * device memory themselves: hosts whose device memory is owned by another
+ * allocator (a framework's caching allocator or a pool reserved at start-up
+ * that forbids raw cudaMalloc later) and thin FFI hosts that have no device
+ * allocator of their own.  It calls no cudaMalloc / cudaFree or any
+ * allocating routine; its scratch is a file-scope device array of
+ * CRESSO_NOALLOC_SCRATCH_BYTES that every GPU loading the library holds until
+ * the process exits.  Tensor lists whose scratch (cresso_scalar_scratch_bytes)
+ * exceeds that size are rejected with CRESSO_ESCRATCH: split them over several
+ * calls.  The first call on a device looks up the array's device address
+ * (with that device current) and caches it; make that first call before any
+ * stream capture.  All calls share the one array, so calls that may overlap
+ * on the GPU (other streams, other host threads, same device) race: order
+ * them on one stream or serialise them. */
+CRESSO_API int cresso_scalar_run_noalloc(const cresso_tensor_desc* descs, int64_t n, const cresso_hparams* hp,
+                                         cresso_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -1,0 +1,94 @@
+"""The allocation-free scalar-route entry point (cresso_scalar_run_noalloc).
+
+Some callers cannot allocate device memory themselves: their device memory is
+owned by another allocator (a framework's caching allocator, or a pool
+reserved at start-up that forbids raw cudaMalloc later), or they are thin FFI
+hosts with no device allocator of their own.  For them the library offers one
+entry point whose scratch is a built-in device array instead of caller memory.
+This test drives it through the C ABI and checks it against the regular entry
+point (cresso_scalar_run with caller scratch) on two consecutive steps, with
+the parameter tolerance the other parity tests use (relative RMS <= 1e-6 here;
+both calls run the same kernel, so the results agree bit for bit in practice).
+The file is named so that pytest collects it last.
+"""
+
+import numpy as np
+import pytest
+import torch
+
+from cresso_b200 import _lib
+from oracle.cresso5_oracle import hparams
+
+pytestmark = pytest.mark.gpu
+
+SHAPES = [(512, 16), (16, 300), (7, 9), (100,), (3, 4, 5)]
+
+
+def _state(shape, dev):
+    z = lambda: torch.zeros((), device=dev)  # noqa: E731
+    return dict(force_rms=z(), drive_energy=torch.ones((), device=dev), surprise=z(), action=z(),
+                q=z(), impulse=z(), metric_q=z(), metric_impulse=z())
+
+
+def _descs(params, grads, states, step):
+    F = _lib.DESC_INDEX
+    d = _lib.new_descs(len(params))
+    for i, (p, g, st) in enumerate(zip(params, grads, states)):
+        d[i, F["ndim"]] = p.ndim
+        for a, s in enumerate(p.shape):
+            d[i, F["shape0"] + a] = s
+        d[i, F["step"]] = step
+        d[i, F["param"]] = p.data_ptr()
+        d[i, F["grad"]] = g.data_ptr()
+        for k, v in st.items():
+            d[i, F[k]] = v.data_ptr()
+    return d
+
+
+def test_noalloc_entry_matches_regular_entry_on_two_steps():
+    L = _lib.lib()
+    dev = torch.device("cuda")
+    gen = torch.Generator().manual_seed(11)
+    inits = [torch.randn(s, generator=gen) * 0.02 for s in SHAPES]
+    grads = [[(torch.randn(s, generator=gen) * 1e-3).to(dev) for s in SHAPES] for _ in range(2)]
+    hp = _lib.pack_hparams(hparams(rank=4, weight_decay=0.01))
+    stream = torch.cuda.current_stream(dev).cuda_stream
+
+    p_reg = [x.clone().to(dev) for x in inits]
+    p_na = [x.clone().to(dev) for x in inits]
+    s_reg = [_state(s, dev) for s in SHAPES]
+    s_na = [_state(s, dev) for s in SHAPES]
+    for step, gs in enumerate(grads, start=1):
+        d_reg = _descs(p_reg, gs, s_reg, step)
+        nbytes = np.zeros(1, dtype=np.int64)
+        _lib.check(L.cresso_scalar_scratch_bytes(_lib.ptr(d_reg), len(SHAPES), nbytes.ctypes.data_as(_lib._pi64)),
+                   "scalar_scratch_bytes")
+        assert 0 < int(nbytes[0]) <= _lib.NOALLOC_SCRATCH_BYTES
+        scratch = torch.empty(int(nbytes[0]), dtype=torch.uint8, device=dev)
+        _lib.check(L.cresso_scalar_run(_lib.ptr(d_reg), len(SHAPES), _lib.ptr(hp), _lib.ptr(scratch),
+                                       scratch.numel(), stream), "scalar_run")
+        d_na = _descs(p_na, gs, s_na, step)
+        _lib.check(L.cresso_scalar_run_noalloc(_lib.ptr(d_na), len(SHAPES), _lib.ptr(hp), stream),
+                   "scalar_run_noalloc")
+        torch.cuda.synchronize()
+        for a, b in zip(p_na, p_reg):
+            rel = float((a.double() - b.double()).pow(2).mean().sqrt() / b.double().pow(2).mean().sqrt())
+            assert rel <= 1e-6, (step, rel)
+        for sa, sb in zip(s_na, s_reg):
+            for k in sa:
+                assert abs(float(sa[k]) - float(sb[k])) <= 1e-6 * max(abs(float(sb[k])), 1e-6), (step, k)
+
+
+def test_noalloc_entry_rejects_lists_beyond_its_array():
+    L = _lib.lib()
+    dev = torch.device("cuda")
+    # 300 tensors of (4096, 16) need ~9.8 MB of scratch, beyond the 8 MiB array
+    shape = (4096, 16)
+    p = torch.zeros(shape, device=dev)
+    g = torch.zeros(shape, device=dev)
+    st = _state(shape, dev)
+    d = np.repeat(_descs([p], [g], [st], 1), 300, axis=0)
+    hp = _lib.pack_hparams(hparams(rank=4))
+    rc = L.cresso_scalar_run_noalloc(_lib.ptr(d), 300, _lib.ptr(hp), torch.cuda.current_stream(dev).cuda_stream)
+    assert rc == 4  # CRESSO_ESCRATCH, before any launch
+    assert "built-in array" in _lib.last_error()
