@@ -121,6 +121,33 @@ __device__ __forceinline__ int load_bin(const void* hidx, int idx_bytes, int64_t
 
 __device__ __forceinline__ float sgnf(float x) { return x > 0.f ? 1.f : (x < 0.f ? -1.f : 0.f); }
 
+// Per-element transcendentals of the streaming passes.
+//
+// log(1 + x) for x >= 0.  For x <= 1: log(1 + x) = 2 atanh(z) with
+// z = x / (x + 2) in [0, 1/3], summed as its Taylor series
+// 2 z (1 + z^2/3 + z^4/5 + ... + z^12/13), truncation below 2e-8 relative and
+// no cancellation near x = 0.  For x > 1: ln 2 * log2(1 + x) on the
+// special-function unit, within 2 ulp for arguments above 2.
+__device__ __forceinline__ float log1p_pos(float x) {
+    const float z = __fdividef(x, x + 2.0f);  // divisor in [2, 3] on the branch that uses it
+    const float w = z * z;
+    float p = 1.0f / 13.0f;
+    p = fmaf(p, w, 1.0f / 11.0f);
+    p = fmaf(p, w, 1.0f / 9.0f);
+    p = fmaf(p, w, 1.0f / 7.0f);
+    p = fmaf(p, w, 1.0f / 5.0f);
+    p = fmaf(p, w, 1.0f / 3.0f);
+    const float series = 2.0f * fmaf(z * w, p, z);
+    const float lg = 0.693147180559945309f * __log2f(1.0f + x);
+    return x <= 1.0f ? series : lg;
+}
+// Square root of a positive normal number, approximate (relative error ~2^-22).
+__device__ __forceinline__ float sqrt_sfu(float x) {
+    float r;
+    asm("sqrt.approx.f32 %0, %1;" : "=f"(r) : "f"(x));
+    return r;
+}
+
 // Per-element drive components shared by P4 and P5 (cresso_v5.py:1315-1326).
 struct DriveK {
     float clip, inv_clip, clip2, sp, invD, eps;
@@ -133,7 +160,7 @@ __device__ __forceinline__ DriveParts drive_parts(float t, float pred, const Dri
     const float at = fabsf(t);
     d.rat = __fdividef(t, 1.0f + at * c.inv_clip);  // denominator in [1, 1 + 1e4 / clip]
     const float bnd = tanhf(t * c.inv_clip) * c.clip;
-    d.root = sgnf(t) * sqrtf(fminf(at, c.clip2) + c.eps);
+    d.root = sgnf(t) * sqrt_sfu(fminf(at, c.clip2) + c.eps);
     d.u = (1.0f - c.sp) * d.rat + c.sp * bnd;
     d.nov = tanhf((t - pred) * c.invD) * c.clip;
     return d;
@@ -417,6 +444,18 @@ spectral_pass_kernel(const GroupHdr* __restrict__ hdr, const DevTensor* __restri
         int band = (int)((it - ibase) - (int64_t)ct * n_bands);
         if (vec && it < seg_end) stage_item(ct, band, 0);
         int items_since_flush = 0;
+        // Per-column state carried across the items of one column tile (items are
+        // column-tile major, so a block walks down the bands of a tile): the
+        // reconstruction factors of the column, and the float32 projection
+        // partials, contracted into the float64 block state every 4 items and
+        // whenever the tile changes.
+        float U1[RM], V1[RM], U2[RM], V2[RM];
+        float colf = 1.0f;
+        int uv_ct = -1;
+        float z1[RM], z2[RM];
+        float zc = 0.0f;
+#pragma unroll
+        for (int q = 0; q < RM; ++q) z1[q] = z2[q] = 0.0f;
         for (; it < seg_end; ++it) {
             const int col = ct * TC + lc;
             const bool cvalid = col < cols32;
@@ -443,23 +482,19 @@ spectral_pass_kernel(const GroupHdr* __restrict__ hdr, const DevTensor* __restri
             const float* rtb = vec ? reinterpret_cast<const float*>(sb + off_r)
                                    : rowtab + (int64_t)(row032 + rbase) * 2 * RM;
 
-            float U1[RM], V1[RM], U2[RM], V2[RM];
-            float colf = 1.0f;
             if constexpr (PASS >= 3) {
-                float b1[RM], b2[RM];
-                load_col<RM>(coltab, gcols, gc, b1, b2);
-                make_uv<RM>(b1, b2, s_coef, s_coef + RM, U1, V1);
-                make_uv<RM>(b1, b2, s_coef + 2 * RM, s_coef + 3 * RM, U2, V2);
-                if constexpr (PASS == 3) {
-                    if (flags & F_INST2D) colf = Dp->colf[cvalid ? col : 0];
+                if (ct != uv_ct) {
+                    uv_ct = ct;
+                    float b1[RM], b2[RM];
+                    load_col<RM>(coltab, gcols, gc, b1, b2);
+                    make_uv<RM>(b1, b2, s_coef, s_coef + RM, U1, V1);
+                    make_uv<RM>(b1, b2, s_coef + 2 * RM, s_coef + 3 * RM, U2, V2);
+                    if constexpr (PASS == 3) {
+                        if (flags & F_INST2D) colf = Dp->colf[cvalid ? col : 0];
+                    }
                 }
             }
-            float z1[RM], z2[RM];
-            if constexpr (PASS == 2 || PASS == 3) {
-#pragma unroll
-                for (int q = 0; q < RM; ++q) z1[q] = z2[q] = 0.0f;
-            }
-            float s0 = 0.0f, s1 = 0.0f, colacc = 0.0f, zc = 0.0f;
+            float s0 = 0.0f, s1 = 0.0f, colacc = 0.0f;
 
             for (int m0 = 0; m0 < ITERS; m0 += UNR) {
                 float dv[UNR];
@@ -491,7 +526,7 @@ spectral_pass_kernel(const GroupHdr* __restrict__ hdr, const DevTensor* __restri
                         const float ds = exp2f(ep * __log2f(rel));  // rel >= eps > 0 (normal)
                         // log1p(ds) - 1/2: the density is centred before the float32 partial sums
                         // (the constant is added back exactly in the finalize)
-                        const float L = log1pf(ds);
+                        const float L = log1p_pos(ds);
                         const float Lc = L - 0.5f;
                         const float d = (flags & F_IPOW1) ? rel : fminf(powf(fmaxf(rel, eps), ipw), 1.0e6f);
                         dv[u] = d;
@@ -515,9 +550,9 @@ spectral_pass_kernel(const GroupHdr* __restrict__ hdr, const DevTensor* __restri
                         load_row<RM>(rtb, lr, a1, a2);
                         const float rel = fminf(fabsf(f) * inv_scale + eps, 1.0e4f);
                         const float lm = clampf(recon_dot_nz<RM>(K1, a1, a2, U1, V1), -3.0f, 3.0f);
-                        const float metric = clampf(expf(mcpl * lm), 0.06f, 16.0f);
+                        const float metric = clampf(__expf(mcpl * lm), 0.06f, 16.0f);  // |mcpl * lm| <= 3 mcpl
                         float den = scale * metric;
-                        if (flags & F_LOCAL) den = den * clampf(1.0f + lsh * sqrtf(fminf(rel, 100.0f)), 1.0f, 8.0f);
+                        if (flags & F_LOCAL) den = den * clampf(1.0f + lsh * sqrt_sfu(fminf(rel, 100.0f)), 1.0f, 8.0f);
                         if (flags & F_INST2D) {
                             den = den * clampf(rowf[r] * colf, 0.08f, 12.0f);
                         } else if (flags & F_INST1D) {
@@ -630,24 +665,30 @@ spectral_pass_kernel(const GroupHdr* __restrict__ hdr, const DevTensor* __restri
             } else if constexpr (PASS == 2 || PASS == 3) {
                 acc0 += (double)s0;
                 acc1 += (double)s1;
-                if (cvalid) {
-                    float b1[RM], b2[RM];
-                    load_col<RM>(coltab, gcols, gc, b1, b2);
-                    s_acc[tid] += (double)zc;  // zero mode: sum of the projected field
+                if (nct != ct || it + 1 == seg_end || ++items_since_flush == 4) {
+                    if (cvalid) {
+                        float b1[RM], b2[RM];
+                        load_col<RM>(coltab, gcols, gc, b1, b2);
+                        s_acc[tid] += (double)zc;  // zero mode: sum of the projected field
 #pragma unroll
-                    for (int q = 1; q < RM; ++q) {
-                        const double B1 = b1[q], B2 = b2[q], Z1 = z1[q], Z2 = z2[q];
-                        double c, s;
-                        if (mode_is_product(q)) {
-                            c = B1 * Z1;
-                            s = B2 * Z2;
-                        } else {
-                            c = B1 * Z1 - B2 * Z2;
-                            s = B2 * Z1 + B1 * Z2;
+                        for (int q = 1; q < RM; ++q) {
+                            const double B1 = b1[q], B2 = b2[q], Z1 = z1[q], Z2 = z2[q];
+                            double c, s;
+                            if (mode_is_product(q)) {
+                                c = B1 * Z1;
+                                s = B2 * Z2;
+                            } else {
+                                c = B1 * Z1 - B2 * Z2;
+                                s = B2 * Z1 + B1 * Z2;
+                            }
+                            s_acc[q * kThreads + tid] += c;
+                            s_acc[(RM + q) * kThreads + tid] += s;
                         }
-                        s_acc[q * kThreads + tid] += c;
-                        s_acc[(RM + q) * kThreads + tid] += s;
                     }
+#pragma unroll
+                    for (int q = 0; q < RM; ++q) z1[q] = z2[q] = 0.0f;
+                    zc = 0.0f;
+                    items_since_flush = 0;
                 }
             } else if constexpr (PASS == 4) {
                 // float32 Gram partials over up to 4 items, then into the float64 block state
