@@ -220,12 +220,39 @@ struct PassCfg {
     static constexpr bool kP = PASS == 5;              // parameter tile always staged
 };
 
-// Copies of the hash-bin accumulators in shared memory: up to four per warp
-// (selected by lane & 3, which cuts same-address conflicts of the atomics)
-// within a 32 KB budget.
+// Hash-bin sums of P2 (density) and P3 (port) in shared memory.
+//
+// Values are added as int32 fixed point (value * 2^S, rounded to nearest) with
+// native shared-memory integer atomics, into `bin_copies` copies of the bins
+// (thread tid adds into copy tid % copies; copies padded by one word so that
+// they sit in different banks).  After every item the copies are emptied into
+// an exact int64 per-bin block sum, so the count of values one copy's bin can
+// take between flushes is at most (threads / copies) * ITERS = 2^lg_cnt.  The
+// scale S = max(16, 26 - lg_cnt) and the bound |value| < V = 2^(30 - lg_cnt - S)
+// keep every copy below 2^30 + 2^lg_cnt < 2^31; values at or above V (and
+// non-finite ones) go to a float32 per-bin sum with float atomics instead.
+// The fixed-point part is exact and order independent; its rounding error is
+// at most 2^-(S+1) per value.
 __host__ __device__ inline int bin_copies(int tb) {
-    const int c = 8192 / (tb + 1);
-    return c < 1 ? 1 : (c > 4 * kWarps ? 4 * kWarps : c);
+    int c = 4096 / (tb + 1);  // 16 KB of int32 copies
+    c = c < 1 ? 1 : (c > 16 ? 16 : c);
+    while (c & (c - 1)) c &= c - 1;  // power of two
+    return c;
+}
+struct BinFix {
+    int s;        // scale exponent S
+    float scale;  // 2^S
+    float vmax;   // values with |v| < vmax take the fixed-point path
+};
+__host__ __device__ inline BinFix bin_fix(int copies, int iters) {
+    int lg = 0;
+    while ((1 << lg) < (kThreads / copies) * iters) ++lg;
+    const int S = 26 - lg > 16 ? 26 - lg : 16;
+    BinFix f;
+    f.s = S;
+    f.scale = (float)(1 << (S - 16)) * 65536.0f;
+    f.vmax = (float)(1 << (30 - lg - S));
+    return f;
 }
 
 // Shared-memory bytes of one staging buffer of an item.
@@ -272,9 +299,10 @@ spectral_pass_kernel(const GroupHdr* __restrict__ hdr, const DevTensor* __restri
     // shared memory carve-up
     constexpr bool kBins = PASS == 2 || PASS == 3;
     constexpr bool kTab = PASS >= 3;
-    // bin copies: four per warp (lane & 3) when they fit, padded so copies sit in different banks
-    const int ncopies = kBins ? bin_copies(TB) : 0;
+    // hash-bin sums: int32 fixed-point copies, int64 block sums, float32 sums of the large values
+    const int ncopies = kBins ? bin_copies(TB) : 1;
     const int cstride = TB + 1;
+    const BinFix fix = bin_fix(ncopies, ITERS);
     const int tile = 256 * ITERS;
     const int sbytes = stage_bytes(ITERS, RM, PASS >= 2 ? T2 : 0, ib, stage_p_any, (int)hdr->rb_max);
     unsigned char* s_stage = smem_raw;                                        // 2 * sbytes
@@ -282,8 +310,10 @@ spectral_pass_kernel(const GroupHdr* __restrict__ hdr, const DevTensor* __restri
     double* s_tot = s_red + kNSRec * kWarps;                                  // kNSRec
     double* s_acc = s_tot + kNSRec;                                           // NACC * kThreads
     float* s_coef = reinterpret_cast<float*>(s_acc + NACC * kThreads);       // 4 * RM + 4
-    float* s_bins = s_coef + 4 * RM + 4;                                      // ncopies * (TB + 1)
-    float* s_tab = s_bins + (kBins ? ncopies * cstride : 0);                  // TB
+    long long* s_lbin = reinterpret_cast<long long*>(s_coef + 4 * RM + 4);   // TB (kBins)
+    float* s_fbin = reinterpret_cast<float*>(s_lbin + (kBins ? TB : 0));      // TB (kBins)
+    int* s_ibin = reinterpret_cast<int*>(s_fbin + (kBins ? TB : 0));          // ncopies * (TB + 1) (kBins)
+    float* s_tab = reinterpret_cast<float*>(s_ibin + (kBins ? ncopies * cstride : 0));  // TB
     float* s_rowred = s_tab + (kTab ? TB : 0);                                // 8 * ITERS
     float* s_colred = s_rowred + (PASS == 2 ? 8 * ITERS : 0);                 // kThreads
 
@@ -351,7 +381,11 @@ spectral_pass_kernel(const GroupHdr* __restrict__ hdr, const DevTensor* __restri
             }
         }
         if constexpr (kBins) {
-            for (int b = tid; b < ncopies * cstride; b += kThreads) s_bins[b] = 0.0f;
+            for (int b = tid; b < ncopies * cstride; b += kThreads) s_ibin[b] = 0;
+            for (int b = tid; b < TB; b += kThreads) {
+                s_lbin[b] = 0;
+                s_fbin[b] = 0.0f;
+            }
         }
         if constexpr (kTab) {
             if (hash_on) {
@@ -363,7 +397,7 @@ spectral_pass_kernel(const GroupHdr* __restrict__ hdr, const DevTensor* __restri
             for (int j = 0; j < NACC; ++j) s_acc[j * kThreads + tid] = 0.0;
         }
         __syncthreads();
-        float* my_bins = s_bins + (kBins ? ((warp * 4 + (lane & 3)) % max(ncopies, 1)) * cstride : 0);
+        int* my_bins = s_ibin + (tid & (ncopies - 1)) * cstride;
         const float K1 = kTab ? s_coef[4 * RM] : 0.f, K2 = kTab ? s_coef[4 * RM + 1] : 0.f;
         double acc0 = 0.0, acc1 = 0.0;
         const int lc = tid & (TC - 1), rs = tid / TC;
@@ -540,8 +574,16 @@ spectral_pass_kernel(const GroupHdr* __restrict__ hdr, const DevTensor* __restri
                         }
                         zc += Lc;
                         if (hash_on) {
+                            const bool fx = ds < fix.vmax;
+                            const int qv = __float2int_rn(ds * fix.scale);
 #pragma unroll
-                            for (int t = 0; t < (NT > 0 ? NT : T); ++t) atomicAdd(&my_bins[t * B + bin_of(t)], ds);
+                            for (int t = 0; t < (NT > 0 ? NT : T); ++t) {
+                                const int bt = bin_of(t);
+                                if (fx)
+                                    atomicAdd(&my_bins[t * B + bt], qv);
+                                else
+                                    atomicAdd(&s_fbin[t * B + bt], ds);
+                            }
                         }
                     } else if constexpr (PASS == 3) {
                         float f = sgn * xval;
@@ -585,10 +627,15 @@ spectral_pass_kernel(const GroupHdr* __restrict__ hdr, const DevTensor* __restri
                         zc += t;
                         if (hash_on) {
                             const float port = err + tmix * t;
+                            const bool fx = fabsf(port) < fix.vmax;
+                            const int qv = __float2int_rn(port * fix.scale);
 #pragma unroll
                             for (int t2 = 0; t2 < (NT > 0 ? NT : T); ++t2) {
                                 const int bt = (NT > 0 || t2 < 2) ? bi[NT > 0 ? t2 : (t2 & 1)] : bin_of(t2);
-                                atomicAdd(&my_bins[t2 * B + bt], port);
+                                if (fx)
+                                    atomicAdd(&my_bins[t2 * B + bt], qv);
+                                else
+                                    atomicAdd(&s_fbin[t2 * B + bt], port);
                             }
                         }
                     } else if constexpr (PASS == 4) {
@@ -721,6 +768,20 @@ spectral_pass_kernel(const GroupHdr* __restrict__ hdr, const DevTensor* __restri
                 }
             }
             __syncthreads();  // this buffer (and the reduction scratch) is free again
+            if constexpr (kBins) {
+                // empty the fixed-point copies into the exact block sums (ordered before the
+                // next item's atomics by the barrier that precedes its compute)
+                if (hash_on) {
+                    for (int b = tid; b < TB; b += kThreads) {
+                        long long s = 0;
+                        for (int c = 0; c < ncopies; ++c) {
+                            s += s_ibin[c * cstride + b];
+                            s_ibin[c * cstride + b] = 0;
+                        }
+                        s_lbin[b] += s;
+                    }
+                }
+            }
             if (vec) buf ^= 1;
             ct = nct;
             band = nband;
@@ -750,11 +811,9 @@ spectral_pass_kernel(const GroupHdr* __restrict__ hdr, const DevTensor* __restri
                 for (int j = tid; j < NS; j += kThreads) out[j] = s_tot[j];
                 if constexpr (kBins) {
                     if (hash_on) {
-                        for (int b = tid; b < TB; b += kThreads) {
-                            float s = 0.0f;
-                            for (int c = 0; c < ncopies; ++c) s += s_bins[c * cstride + b];
-                            rec_bins[(int64_t)rec * TB + b] = s;
-                        }
+                        const double inv_scale = ldexp(1.0, -fix.s);
+                        for (int b = tid; b < TB; b += kThreads)
+                            rec_bins[(int64_t)rec * TB + b] = (float)((double)s_lbin[b] * inv_scale + (double)s_fbin[b]);
                     }
                 }
             }
@@ -1432,7 +1491,7 @@ static size_t pass_smem(int pass, const GroupHdr& H, int64_t iters) {
     b += (size_t)(kNSRec * kWarps + kNSRec + nacc * kThreads) * sizeof(double);
     b += (size_t)(4 * rm + 4) * 4;
     if (pass == 2 || pass == 3) {
-        b += (size_t)bin_copies(tb) * (tb + 1) * 4;
+        b += (size_t)tb * (8 + 4) + (size_t)bin_copies(tb) * (tb + 1) * 4;
     }
     if (pass >= 3) b += (size_t)tb * 4;
     if (pass == 2) b += (size_t)(8 * iters + kThreads) * 4;
