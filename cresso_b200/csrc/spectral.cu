@@ -63,15 +63,20 @@ struct TensorConsts {
     double pv[2 * kMaxRank];  // old prediction coefficients on the normalised carriers
 };
 
+// The tensors of a group fall in two launch classes: class 0 ("full") holds
+// the tensors whose every item is a full, 16-byte aligned 256-column tile
+// with 8-bit bin indices; class 1 holds the rest.  Each pass runs one launch
+// per non-empty class over that class's item list.
 struct GroupHdr {
     int64_t n_tensors, n_items, rm, bins, tables, tb, iters, idx_bytes, rb_max;
-    int64_t grid[6];  // blocks of pass 1..5 (index 0 unused)
-    double hp[64];    // cresso_hparams
+    int64_t cls_items[2], cls_nt[2];  // items and tensors of each class
+    int64_t grid[2][6];               // blocks of pass 1..5 per class (index 0 unused)
+    double hp[64];                    // cresso_hparams
 };
 
 struct DevTensor {
     int64_t rows, cols, row0, col0, gcols, N;
-    int64_t item_base, n_items, step, hidx_n;
+    int64_t item_base, n_items, step, hidx_n;  // item_base: first item in the class's item list
     int32_t ndim, R, TC, RPI, RB, n_ct, n_bands, flags;
     int32_t cfirst[6], recbase[6], nrec[6], pad0;
     float* param;
@@ -265,24 +270,28 @@ __host__ __device__ inline int stage_bytes(int iters, int rm, int tables2, int i
     return (int)align_up(b, 16);
 }
 
-template <int PASS, int RM, int NT>
+template <int PASS, int RM, int NT, bool FULL>
 __global__ void __launch_bounds__(kThreads, PassCfg<PASS, RM>::kMinBlocks)
 spectral_pass_kernel(const GroupHdr* __restrict__ hdr, const DevTensor* __restrict__ dts,
-                     const int64_t* __restrict__ item_base, double* __restrict__ rec_scal,
-                     float* __restrict__ rec_bins) {
+                     const int64_t* __restrict__ item_lists, const int32_t* __restrict__ tensor_lists,
+                     double* __restrict__ rec_scal, float* __restrict__ rec_bins) {
     constexpr int NACC = PassCfg<PASS, RM>::kAcc;
     constexpr int UNR = PassCfg<PASS, RM>::kUnroll;
     extern __shared__ __align__(16) unsigned char smem_raw[];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
 
     // group constants, once per block
-    const int64_t n_items = hdr->n_items;
-    const int nt = (int)hdr->n_tensors;
+    // this launch's class: its item list (prefix sums over its tensors) and tensor indices
+    const int cls = FULL ? 0 : 1;
+    const int64_t n_items = hdr->cls_items[cls];
+    const int nt = (int)hdr->cls_nt[cls];
+    const int64_t* __restrict__ item_base = item_lists + (FULL ? 0 : hdr->cls_nt[0] + 1);
+    const int32_t* __restrict__ tmap = tensor_lists + (FULL ? 0 : hdr->cls_nt[0]);
     const int TB = (int)hdr->tb, B = (int)hdr->bins;
     const int T = NT > 0 ? NT : (int)hdr->tables;  // hash tables (compile-time 1 or 2 on the fast path)
     const int T2 = T < 2 ? T : 2;                    // tables whose bin bytes are staged
     const int ITERS = (int)hdr->iters;
-    const bool idx8 = hdr->idx_bytes == 1;
+    const bool idx8 = FULL || hdr->idx_bytes == 1;
     const int ib = idx8 ? 1 : 2;
     const bool stage_p_any = PassCfg<PASS, RM>::kP || (PASS <= 3 && hdr->hp[H_WD] != 0.0);
     const float eps = (float)hdr->hp[H_EPS];
@@ -321,15 +330,17 @@ spectral_pass_kernel(const GroupHdr* __restrict__ hdr, const DevTensor* __restri
     int64_t it = it0;
     while (it < it1) {
         // ---- tensor descriptor and constants into registers
-        const DevTensor* __restrict__ Dp = dts + k;
+        const DevTensor* __restrict__ Dp = dts + tmap[k];
         const int64_t rows = Dp->rows, cols = Dp->cols, row0 = Dp->row0, col0 = Dp->col0, gcols = Dp->gcols;
-        const int64_t ibase = Dp->item_base, hidx_n = Dp->hidx_n;
-        const int64_t seg_end = min(it1, ibase + Dp->n_items);
+        const int64_t ibase = item_base[k], hidx_n = Dp->hidx_n;
+        const int64_t seg_end = min(it1, item_base[k + 1]);
         const int flags = Dp->flags;
-        const int TC = Dp->TC, RPI = Dp->RPI, RB = Dp->RB, n_bands = Dp->n_bands;
+        // class 0: 256-column tiles (one thread per column, RPI = 1), no partial tiles
+        const int TC = FULL ? 256 : Dp->TC, RPI = FULL ? 1 : Dp->RPI, RB = FULL ? ITERS : Dp->RB;
+        const int n_bands = Dp->n_bands;
         const int rows32 = (int)rows, cols32 = (int)cols, row032 = (int)row0, gcols32 = (int)gcols;
         const bool hash_on = (flags & F_HASH) != 0;
-        const bool vec = (flags & F_VEC) != 0;
+        const bool vec = FULL || (flags & F_VEC) != 0;
         const bool wd_on = (flags & F_WD) != 0;
         const bool stage_p = PassCfg<PASS, RM>::kP || (PASS <= 3 && wd_on);
         const float* __restrict__ grad = Dp->grad;
@@ -422,7 +433,7 @@ spectral_pass_kernel(const GroupHdr* __restrict__ hdr, const DevTensor* __restri
                 for (int c = tid; c < (RB << lg_cpr); c += kThreads) {
                     const int lr = c >> lg_cpr, cc = c & ((1 << lg_cpr) - 1);
                     const int r = rb + lr, col = cb + 4 * cc;
-                    const bool ok = r < rows32 && col < cols32;
+                    const bool ok = FULL || (r < rows32 && col < cols32);
                     const int64_t e = ok ? (int64_t)r * cols32 + col : 0;
                     cp_async16(sb + (lr * TC + 4 * cc) * 4, xsrc + e, ok ? 16 : 0);
                     if (stage_p) cp_async16(sb + off_p + (lr * TC + 4 * cc) * 4, param + e, ok ? 16 : 0);
@@ -433,7 +444,7 @@ spectral_pass_kernel(const GroupHdr* __restrict__ hdr, const DevTensor* __restri
                         const int c2 = c & ((1 << lg_rbcprb) - 1);
                         const int lr = c2 >> lg_cprb, cc = c2 & ((1 << lg_cprb) - 1);
                         const int r = rb + lr;
-                        const bool ok = r < rows32 && cb + (cc << (4 - (ib == 2))) < cols32;
+                        const bool ok = FULL || (r < rows32 && cb + (cc << (4 - (ib == 2))) < cols32);
                         const int64_t g = ok ? ((int64_t)(row032 + r) * gcols32 + col0 + cb) * ib + 16 * cc : 0;
                         cp_async16(sb + off_b + (t * tile + lr * TC) * ib + 16 * cc, hidx + t * hidx_n * ib + g,
                                    ok ? 16 : 0);
@@ -441,7 +452,7 @@ spectral_pass_kernel(const GroupHdr* __restrict__ hdr, const DevTensor* __restri
                 }
                 if (PASS >= 2) {
                     for (int c = tid; c < (RB << lg_rm2); c += kThreads) {
-                        const bool ok = rb + (c >> lg_rm2) < rows32;
+                        const bool ok = FULL || rb + (c >> lg_rm2) < rows32;
                         const int64_t g = ok ? (int64_t)(row032 + rb) * 2 * RM + 4 * c : 0;
                         cp_async16(sb + off_r + 16 * c, rowtab + g, ok ? 16 : 0);
                     }
@@ -492,7 +503,7 @@ spectral_pass_kernel(const GroupHdr* __restrict__ hdr, const DevTensor* __restri
         for (int q = 0; q < RM; ++q) z1[q] = z2[q] = 0.0f;
         for (; it < seg_end; ++it) {
             const int col = ct * TC + lc;
-            const bool cvalid = col < cols32;
+            const bool cvalid = FULL || col < cols32;
             const int gc = (int)col0 + (cvalid ? col : 0);
             const int rbase = band * RB;
             const int nband = band + 1 == n_bands ? 0 : band + 1;
@@ -537,7 +548,7 @@ spectral_pass_kernel(const GroupHdr* __restrict__ hdr, const DevTensor* __restri
                     dv[u] = 0.0f;
                     const int lr = rs + RPI * (m0 + u);
                     const int r = rbase + lr;
-                    if (!(cvalid && r < rows32)) continue;
+                    if (!FULL && !(cvalid && r < rows32)) continue;
                     const int o = lr * TC + lc;  // offset inside the item tiles
                     const float xval = xb[o];
                     auto bin_of = [&](int t) -> int {
@@ -1225,8 +1236,9 @@ __global__ void finalize4_kernel(const GroupHdr* __restrict__ hdr, const DevTens
 struct Plan {
     GroupHdr hdr;
     std::vector<DevTensor> dts;
-    std::vector<int64_t> item_base;
-    int64_t off_hdr, off_dts, off_items, off_cst, off_htab, off_rowf, off_colf, off_rowpart, off_colpart;
+    std::vector<int64_t> item_lists;   // class 0 item prefix sums (n0 + 1), then class 1 (n1 + 1)
+    std::vector<int32_t> tensor_lists; // class 0 tensor indices, then class 1
+    int64_t off_hdr, off_dts, off_items, off_tmap, off_cst, off_htab, off_rowf, off_colf, off_rowpart, off_colpart;
     int64_t off_recs, off_recb, off_red[5], len_red[5], off_tbuf, bytes;
     int64_t n_rec_max;
     int rm;
@@ -1269,7 +1281,7 @@ static int build_plan(const cresso_tensor_desc* descs, int64_t n, const cresso_h
     H.idx_bytes = bins <= 256 ? 1 : 2;
     memcpy(H.hp, hp, sizeof(cresso_hparams));
     P.dts.assign(n, DevTensor{});
-    P.item_base.assign(n + 1, 0);
+    std::vector<char> full(n, 0);
 
     // geometry and item counts; ITERS chosen so that the busiest pass has >= ~8 items per block
     int64_t total_rows_work = 0;
@@ -1340,8 +1352,6 @@ static int build_plan(const cresso_tensor_desc* descs, int64_t n, const cresso_h
         D.n_ct = (int32_t)ceil_div(d.cols, D.TC);
         D.n_bands = (int32_t)ceil_div(d.rows, D.RB);
         D.n_items = (int64_t)D.n_ct * D.n_bands;
-        D.item_base = items;
-        P.item_base[i] = items;
         items += D.n_items;
         const bool hard = hp_flags_hard(d, *hp, D.N);
         int fl = 0;
@@ -1360,6 +1370,7 @@ static int build_plan(const cresso_tensor_desc* descs, int64_t n, const cresso_h
         if (ic != 0.0 && D.N > 1) fl |= (d.ndim == 2 ? F_INST2D : F_INST1D);
         if (fmax(hp->instant_metric_power, 0.25) == 1.0) fl |= F_IPOW1;
         if (vec[i]) fl |= F_VEC;
+        full[i] = vec[i] && D.TC == 256 && d.cols % 256 == 0 && d.rows % D.RB == 0 && bins <= 256;
         D.flags = fl;
         // pointers into the caller's objects
         const char* ws = (const char*)d.shape_ws;
@@ -1399,27 +1410,47 @@ static int build_plan(const cresso_tensor_desc* descs, int64_t n, const cresso_h
                            D.surprise && D.action,
                        CRESSO_EINVAL, "tensor %lld: NULL state pointer", (long long)i);
     }
-    P.item_base[n] = items;
     H.n_items = items;
-    // blocks per pass and record placement (a record per (block, tensor) pair)
+    // the two launch classes: item lists in tensor order within each class
+    P.item_lists.clear();
+    P.tensor_lists.clear();
+    for (int c = 0; c < 2; ++c) {
+        int64_t ci = 0, cn = 0;
+        for (int64_t i = 0; i < n; ++i) {
+            if ((full[i] ? 0 : 1) != c) continue;
+            P.item_lists.push_back(ci);
+            P.tensor_lists.push_back((int32_t)i);
+            P.dts[i].item_base = ci;
+            ci += P.dts[i].n_items;
+            ++cn;
+        }
+        P.item_lists.push_back(ci);
+        H.cls_items[c] = ci;
+        H.cls_nt[c] = cn;
+    }
+    // blocks per pass and class, and record placement (a record per (block, tensor) pair)
     const int occ[6] = {0, 4, 2, 2, 2, 2};
     P.n_rec_max = 0;
     for (int p = 1; p <= 5; ++p) {
-        const int64_t g = std::max<int64_t>(1, std::min<int64_t>(items, num_sms * (rm > 8 ? 1 : occ[p])));
-        H.grid[p] = g;
         int64_t rb = 0;
-        int64_t c = 0;
-        for (int64_t i = 0; i < n; ++i) {
-            DevTensor& D = P.dts[i];
-            const int64_t first = D.item_base, last = D.item_base + D.n_items - 1;
-            // block c owns items [c*items/g, (c+1)*items/g)
-            while ((c + 1) * items / g <= first) ++c;
-            int64_t c_last = c;
-            while ((c_last + 1) * items / g <= last) ++c_last;
-            D.cfirst[p] = (int32_t)c;
-            D.recbase[p] = (int32_t)rb;
-            D.nrec[p] = (int32_t)(c_last - c + 1);
-            rb += D.nrec[p];
+        for (int c = 0; c < 2; ++c) {
+            const int64_t ci = H.cls_items[c];
+            const int64_t g = ci == 0 ? 0 : std::max<int64_t>(1, std::min<int64_t>(ci, num_sms * (rm > 8 ? 1 : occ[p])));
+            H.grid[c][p] = g;
+            int64_t b = 0;
+            const int32_t* tl = P.tensor_lists.data() + (c == 0 ? 0 : H.cls_nt[0]);
+            for (int64_t j = 0; j < H.cls_nt[c]; ++j) {
+                DevTensor& D = P.dts[tl[j]];
+                const int64_t first = D.item_base, last = D.item_base + D.n_items - 1;
+                // block b of the class's launch owns items [b*ci/g, (b+1)*ci/g)
+                while ((b + 1) * ci / g <= first) ++b;
+                int64_t b_last = b;
+                while ((b_last + 1) * ci / g <= last) ++b_last;
+                D.cfirst[p] = (int32_t)b;
+                D.recbase[p] = (int32_t)rb;
+                D.nrec[p] = (int32_t)(b_last - b + 1);
+                rb += D.nrec[p];
+            }
         }
         P.n_rec_max = std::max(P.n_rec_max, rb);
     }
@@ -1428,7 +1459,8 @@ static int build_plan(const cresso_tensor_desc* descs, int64_t n, const cresso_h
     int64_t off = 0;
     P.off_hdr = take(off, sizeof(GroupHdr));
     P.off_dts = take(off, sizeof(DevTensor) * n);
-    P.off_items = take(off, sizeof(int64_t) * (n + 1));
+    P.off_items = take(off, sizeof(int64_t) * (n + 2));
+    P.off_tmap = take(off, sizeof(int32_t) * n);
     P.off_cst = take(off, sizeof(TensorConsts) * n);
     int64_t rows_tot = 0, cols_tot = 0, rowpart_tot = 0, colpart_tot = 0, elems = 0;
     for (auto& D : P.dts) {
@@ -1503,14 +1535,20 @@ static int launch_stage(int stage, const Plan& P, char* base, cudaStream_t s) {
     const GroupHdr* hdr = reinterpret_cast<const GroupHdr*>(base + P.off_hdr);
     const DevTensor* dts = reinterpret_cast<const DevTensor*>(base + P.off_dts);
     const int64_t* items = reinterpret_cast<const int64_t*>(base + P.off_items);
+    const int32_t* tmap = reinterpret_cast<const int32_t*>(base + P.off_tmap);
     double* recs = reinterpret_cast<double*>(base + P.off_recs);
     float* recb = reinterpret_cast<float*>(base + P.off_recb);
     const int n = (int)P.hdr.n_tensors;
-    auto run_pass = [&](auto kern, int pass) -> int {
+    auto run_pass = [&](auto kern_full, auto kern_gen, int pass) -> int {
         const size_t smem = pass_smem(pass, P.hdr, P.hdr.iters);
-        if (smem > 48 * 1024) CRESSO_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-        kern<<<(unsigned)P.hdr.grid[pass], kThreads, smem, s>>>(hdr, dts, items, recs, recb);
-        CRESSO_LAUNCHED("spectral_pass_kernel");
+        for (int c = 0; c < 2; ++c) {
+            if (P.hdr.grid[c][pass] == 0) continue;
+            auto kern = c == 0 ? kern_full : kern_gen;
+            if (smem > 48 * 1024)
+                CRESSO_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+            kern<<<(unsigned)P.hdr.grid[c][pass], kThreads, smem, s>>>(hdr, dts, items, tmap, recs, recb);
+            CRESSO_LAUNCHED("spectral_pass_kernel");
+        }
         return CRESSO_OK;
     };
     auto run_reduce = [&](int pass) -> int {
@@ -1522,31 +1560,31 @@ static int launch_stage(int stage, const Plan& P, char* base, cudaStream_t s) {
         return CRESSO_OK;
     };
     switch (stage) {
-        case 1: return run_pass(spectral_pass_kernel<1, RM, NT>, 1);
+        case 1: return run_pass(spectral_pass_kernel<1, RM, NT, true>, spectral_pass_kernel<1, RM, NT, false>, 1);
         case 2: return run_reduce(1);
         case 3:
             finalize1_kernel<RM><<<n, kThreads, 0, s>>>(hdr, dts);
             CRESSO_LAUNCHED("finalize1_kernel");
             return CRESSO_OK;
-        case 4: return run_pass(spectral_pass_kernel<2, RM, NT>, 2);
+        case 4: return run_pass(spectral_pass_kernel<2, RM, NT, true>, spectral_pass_kernel<2, RM, NT, false>, 2);
         case 5: return run_reduce(2);
         case 6:
             finalize2_kernel<RM><<<n, kThreads, 0, s>>>(hdr, dts);
             CRESSO_LAUNCHED("finalize2_kernel");
             return CRESSO_OK;
-        case 7: return run_pass(spectral_pass_kernel<3, RM, NT>, 3);
+        case 7: return run_pass(spectral_pass_kernel<3, RM, NT, true>, spectral_pass_kernel<3, RM, NT, false>, 3);
         case 8: return run_reduce(3);
         case 9:
             finalize3_kernel<RM><<<n, kThreads, 0, s>>>(hdr, dts);
             CRESSO_LAUNCHED("finalize3_kernel");
             return CRESSO_OK;
-        case 10: return run_pass(spectral_pass_kernel<4, RM, NT>, 4);
+        case 10: return run_pass(spectral_pass_kernel<4, RM, NT, true>, spectral_pass_kernel<4, RM, NT, false>, 4);
         case 11: return run_reduce(4);
         case 12:
             finalize4_kernel<RM><<<n, kThreads, 0, s>>>(hdr, dts);
             CRESSO_LAUNCHED("finalize4_kernel");
             return CRESSO_OK;
-        case 13: return run_pass(spectral_pass_kernel<5, RM, NT>, 5);
+        case 13: return run_pass(spectral_pass_kernel<5, RM, NT, true>, spectral_pass_kernel<5, RM, NT, false>, 5);
         default: return CRESSO_OK;
     }
 }
@@ -1588,7 +1626,9 @@ int cresso_spectral_run(const cresso_tensor_desc* descs, int64_t n, const cresso
     if (stage_begin == 0) {
         CRESSO_CUDA(cudaMemcpyAsync(base + P.off_hdr, &P.hdr, sizeof(GroupHdr), cudaMemcpyHostToDevice, s));
         CRESSO_CUDA(cudaMemcpyAsync(base + P.off_dts, P.dts.data(), sizeof(DevTensor) * n, cudaMemcpyHostToDevice, s));
-        CRESSO_CUDA(cudaMemcpyAsync(base + P.off_items, P.item_base.data(), sizeof(int64_t) * (n + 1),
+        CRESSO_CUDA(cudaMemcpyAsync(base + P.off_items, P.item_lists.data(), sizeof(int64_t) * (n + 2),
+                                    cudaMemcpyHostToDevice, s));
+        CRESSO_CUDA(cudaMemcpyAsync(base + P.off_tmap, P.tensor_lists.data(), sizeof(int32_t) * n,
                                     cudaMemcpyHostToDevice, s));
     }
     for (int64_t stage = std::max<int64_t>(stage_begin, 1); stage < stage_end; ++stage) {
