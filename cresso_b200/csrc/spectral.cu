@@ -217,9 +217,29 @@ __device__ __forceinline__ void cp_async_wait() {
     asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory");
 }
 
+// Sum over the 32 lanes of a warp of each of v[0..31], by a transposing
+// butterfly (31 shuffles in all): on return lane l holds the sum of v[l].
+// v is used as scratch.
+__device__ __forceinline__ float warp_transpose_sum32(float (&v)[32]) {
+    const int lane = threadIdx.x & 31;
+#pragma unroll
+    for (int s = 16; s >= 1; s >>= 1) {
+        const bool hi = (lane & s) != 0;
+#pragma unroll
+        for (int i = 0; i < s; ++i) {
+            const float send = hi ? v[i] : v[i + s];
+            const float keep = hi ? v[i + s] : v[i];
+            v[i] = keep + __shfl_xor_sync(0xffffffffu, send, s);
+        }
+    }
+    return v[0];
+}
+
 template <int PASS, int RM>
 struct PassCfg {
-    static constexpr int kAcc = PASS == 4 ? kGram : (PASS == 2 || PASS == 3 ? 2 * RM : 0);  // fp64 per-thread sums
+    // float64 block-state sums in shared memory: the projection contractions of
+    // P2 / P3 per thread, the drive Gram of P4 per warp (one entry per lane)
+    static constexpr int kAccDoubles = PASS == 4 ? kWarps * 32 : (PASS == 2 || PASS == 3 ? 2 * RM * kThreads : 0);
     static constexpr int kMinBlocks = RM > 8 ? 1 : 2;
     static constexpr int kUnroll = PASS == 3 ? 2 : 4;  // rows computed together
     static constexpr bool kP = PASS == 5;              // parameter tile always staged
@@ -275,7 +295,7 @@ __global__ void __launch_bounds__(kThreads, PassCfg<PASS, RM>::kMinBlocks)
 spectral_pass_kernel(const GroupHdr* __restrict__ hdr, const DevTensor* __restrict__ dts,
                      const int64_t* __restrict__ item_lists, const int32_t* __restrict__ tensor_lists,
                      double* __restrict__ rec_scal, float* __restrict__ rec_bins) {
-    constexpr int NACC = PassCfg<PASS, RM>::kAcc;
+    constexpr int NACC = PassCfg<PASS, RM>::kAccDoubles;
     constexpr int UNR = PassCfg<PASS, RM>::kUnroll;
     extern __shared__ __align__(16) unsigned char smem_raw[];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -317,8 +337,8 @@ spectral_pass_kernel(const GroupHdr* __restrict__ hdr, const DevTensor* __restri
     unsigned char* s_stage = smem_raw;                                        // 2 * sbytes
     double* s_red = reinterpret_cast<double*>(smem_raw + 2 * sbytes);         // kNSRec * kWarps
     double* s_tot = s_red + kNSRec * kWarps;                                  // kNSRec
-    double* s_acc = s_tot + kNSRec;                                           // NACC * kThreads
-    float* s_coef = reinterpret_cast<float*>(s_acc + NACC * kThreads);       // 4 * RM + 4
+    double* s_acc = s_tot + kNSRec;                                           // NACC
+    float* s_coef = reinterpret_cast<float*>(s_acc + NACC);                   // 4 * RM + 4
     long long* s_lbin = reinterpret_cast<long long*>(s_coef + 4 * RM + 4);   // TB (kBins)
     float* s_fbin = reinterpret_cast<float*>(s_lbin + (kBins ? TB : 0));      // TB (kBins)
     int* s_ibin = reinterpret_cast<int*>(s_fbin + (kBins ? TB : 0));          // ncopies * (TB + 1) (kBins)
@@ -405,7 +425,7 @@ spectral_pass_kernel(const GroupHdr* __restrict__ hdr, const DevTensor* __restri
             }
         }
         if constexpr (NACC > 0) {
-            for (int j = 0; j < NACC; ++j) s_acc[j * kThreads + tid] = 0.0;
+            for (int j = tid; j < NACC; j += kThreads) s_acc[j] = 0.0;
         }
         __syncthreads();
         int* my_bins = s_ibin + (tid & (ncopies - 1)) * cstride;
@@ -585,15 +605,14 @@ spectral_pass_kernel(const GroupHdr* __restrict__ hdr, const DevTensor* __restri
                         }
                         zc += Lc;
                         if (hash_on) {
+                            // fixed-point path for every value (zero for the large ones), one
+                            // rarely taken branch for the float path of the large values
                             const bool fx = ds < fix.vmax;
-                            const int qv = __float2int_rn(ds * fix.scale);
+                            const int qv = fx ? __float2int_rn(ds * fix.scale) : 0;
 #pragma unroll
-                            for (int t = 0; t < (NT > 0 ? NT : T); ++t) {
-                                const int bt = bin_of(t);
-                                if (fx)
-                                    atomicAdd(&my_bins[t * B + bt], qv);
-                                else
-                                    atomicAdd(&s_fbin[t * B + bt], ds);
+                            for (int t = 0; t < (NT > 0 ? NT : T); ++t) atomicAdd(&my_bins[t * B + bin_of(t)], qv);
+                            if (!fx) {
+                                for (int t = 0; t < (NT > 0 ? NT : T); ++t) atomicAdd(&s_fbin[t * B + bin_of(t)], ds);
                             }
                         }
                     } else if constexpr (PASS == 3) {
@@ -608,7 +627,7 @@ spectral_pass_kernel(const GroupHdr* __restrict__ hdr, const DevTensor* __restri
                         if (flags & F_LOCAL) den = den * clampf(1.0f + lsh * sqrt_sfu(fminf(rel, 100.0f)), 1.0f, 8.0f);
                         if (flags & F_INST2D) {
                             den = den * clampf(rowf[r] * colf, 0.08f, 12.0f);
-                        } else if (flags & F_INST1D) {
+                        } else if (!FULL && (flags & F_INST1D)) {  // 1-D tensors are never in class 0
                             const float dd = (flags & F_IPOW1) ? rel : fminf(powf(fmaxf(rel, eps), ipw), 1.0e6f);
                             den = den * clampf(expf(inst_k * logf(fmaxf(dd / inst_gm, eps))), 0.08f, 12.0f);
                         }
@@ -638,15 +657,18 @@ spectral_pass_kernel(const GroupHdr* __restrict__ hdr, const DevTensor* __restri
                         zc += t;
                         if (hash_on) {
                             const float port = err + tmix * t;
-                            const bool fx = fabsf(port) < fix.vmax;
-                            const int qv = __float2int_rn(port * fix.scale);
+                            const bool fx = fabsf(port) < fix.vmax;  // false for non-finite values
+                            const int qv = fx ? __float2int_rn(port * fix.scale) : 0;
 #pragma unroll
                             for (int t2 = 0; t2 < (NT > 0 ? NT : T); ++t2) {
                                 const int bt = (NT > 0 || t2 < 2) ? bi[NT > 0 ? t2 : (t2 & 1)] : bin_of(t2);
-                                if (fx)
-                                    atomicAdd(&my_bins[t2 * B + bt], qv);
-                                else
+                                atomicAdd(&my_bins[t2 * B + bt], qv);
+                            }
+                            if (!fx) {
+                                for (int t2 = 0; t2 < (NT > 0 ? NT : T); ++t2) {
+                                    const int bt = (NT > 0 || t2 < 2) ? bi[NT > 0 ? t2 : (t2 & 1)] : bin_of(t2);
                                     atomicAdd(&s_fbin[t2 * B + bt], port);
+                                }
                             }
                         }
                     } else if constexpr (PASS == 4) {
@@ -749,13 +771,16 @@ spectral_pass_kernel(const GroupHdr* __restrict__ hdr, const DevTensor* __restri
                     items_since_flush = 0;
                 }
             } else if constexpr (PASS == 4) {
-                // float32 Gram partials over up to 4 items, then into the float64 block state
-                if (++items_since_flush == 4 || it + 1 == seg_end) {
+                // float32 Gram partials over up to 2 items, summed across the warp (lane q
+                // ends with entry q) into the warp's float64 sums
+                if (++items_since_flush == 2 || it + 1 == seg_end) {
+                    float v[32];
 #pragma unroll
-                    for (int q = 0; q < kGram; ++q) {
-                        s_acc[q * kThreads + tid] += (double)g32[q];
-                        g32[q] = 0.0f;
-                    }
+                    for (int q = 0; q < 32; ++q) v[q] = q < kGram ? g32[q < kGram ? q : 0] : 0.0f;
+                    const float x = warp_transpose_sum32(v);
+                    if (lane < kGram) s_acc[warp * 32 + lane] += (double)x;
+#pragma unroll
+                    for (int q = 0; q < kGram; ++q) g32[q] = 0.0f;
                     items_since_flush = 0;
                 }
             }
@@ -806,18 +831,20 @@ spectral_pass_kernel(const GroupHdr* __restrict__ hdr, const DevTensor* __restri
                 double v[1] = {acc0};
                 block_sum_to<1>(v, s_red, s_tot);
                 if (tid == 0) out[0] = s_tot[0];
-            } else {
-                constexpr int NS = PASS == 4 ? kGram : 2 + 2 * RM;
-                double v[NS];
-                if constexpr (PASS == 4) {
-#pragma unroll
-                    for (int q = 0; q < kGram; ++q) v[q] = s_acc[q * kThreads + tid];
-                } else {
-                    v[0] = acc0;
-                    v[1] = acc1;
-#pragma unroll
-                    for (int q = 0; q < 2 * RM; ++q) v[2 + q] = s_acc[q * kThreads + tid];
+            } else if constexpr (PASS == 4) {
+                // the warps' sums in a fixed order (the item loop ended with a barrier)
+                if (tid < kGram) {
+                    double v = 0.0;
+                    for (int w = 0; w < kWarps; ++w) v += s_acc[w * 32 + tid];
+                    out[tid] = v;
                 }
+            } else {
+                constexpr int NS = 2 + 2 * RM;
+                double v[NS];
+                v[0] = acc0;
+                v[1] = acc1;
+#pragma unroll
+                for (int q = 0; q < 2 * RM; ++q) v[2 + q] = s_acc[q * kThreads + tid];
                 block_sum_to<NS>(v, s_red, s_tot);
                 for (int j = tid; j < NS; j += kThreads) out[j] = s_tot[j];
                 if constexpr (kBins) {
@@ -1516,11 +1543,11 @@ static void bind_scratch(Plan& P, char* base) {
 static size_t pass_smem(int pass, const GroupHdr& H, int64_t iters) {
     const int tb = (int)H.tb;
     const int rm = (int)H.rm;
-    const int nacc = pass == 4 ? kGram : (pass == 2 || pass == 3 ? 2 * rm : 0);
+    const int nacc = pass == 4 ? kWarps * 32 : (pass == 2 || pass == 3 ? 2 * rm * kThreads : 0);
     const int T2 = H.tables < 2 ? (int)H.tables : 2;
     const bool with_p = pass == 5 || (pass <= 3 && H.hp[H_WD] != 0.0);
     size_t b = 2 * (size_t)stage_bytes((int)iters, rm, pass >= 2 ? T2 : 0, (int)H.idx_bytes, with_p, (int)H.rb_max);
-    b += (size_t)(kNSRec * kWarps + kNSRec + nacc * kThreads) * sizeof(double);
+    b += (size_t)(kNSRec * kWarps + kNSRec + nacc) * sizeof(double);
     b += (size_t)(4 * rm + 4) * 4;
     if (pass == 2 || pass == 3) {
         b += (size_t)tb * (8 + 4) + (size_t)bin_copies(tb) * (tb + 1) * 4;
