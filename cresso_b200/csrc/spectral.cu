@@ -29,6 +29,7 @@
 #include "basis_dev.cuh"
 #include "cresso_common.cuh"
 #include "cresso_status.h"
+#include "tcgen05.cuh"
 
 namespace cresso {
 
@@ -69,6 +70,7 @@ struct TensorConsts {
 // per non-empty class over that class's item list.
 struct GroupHdr {
     int64_t n_tensors, n_items, rm, bins, tables, tb, iters, idx_bytes, rb_max;
+    int32_t* status;                  // device word: nonzero when a bounded wait gave up
     int64_t cls_items[2], cls_nt[2];  // items and tensors of each class
     int64_t grid[2][6];               // blocks of pass 1..5 per class (index 0 unused)
     double hp[64];                    // cresso_hparams
@@ -290,11 +292,60 @@ __host__ __device__ inline int stage_bytes(int iters, int rm, int tables2, int i
     return (int)align_up(b, 16);
 }
 
-template <int PASS, int RM, int NT, bool FULL>
+// Column factors of both reconstructions for global column gc, as tf32 hi / lo
+// splits into TMEM: reconstruction j at columns taddr + 64 j (hi) and + 16 (lo),
+// slots (K_j, 0, U_1, V_1, ..., U_7, V_7) (mode 0 is the carrier (1, 0), so its
+// slot pair carries the constant term).  Not inlined: it runs once per column
+// tile, and keeping it out of the item loop keeps that loop free of spills.
+template <int RM>
+__device__ __noinline__ void tc_column_factors(const float* __restrict__ coltab, int64_t gcols, int64_t gc,
+                                               const float* __restrict__ s_coef, uint32_t taddr) {
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+        float b1[RM], b2[RM];
+        load_col<RM>(coltab, gcols, gc, b1, b2);
+        float U[RM], V[RM];
+        make_uv<RM>(b1, b2, s_coef + 2 * j * RM, s_coef + (2 * j + 1) * RM, U, V);
+        U[0] = s_coef[4 * RM + j];
+        V[0] = 0.0f;
+        float w[2 * RM];
+#pragma unroll
+        for (int q = 0; q < RM; ++q) {
+            w[2 * q] = tf32_rna(U[q]);
+            w[2 * q + 1] = tf32_rna(V[q]);
+        }
+        tc_st16(taddr + 64 * j, w);
+#pragma unroll
+        for (int q = 0; q < RM; ++q) {
+            w[2 * q] = tf32_rna(U[q] - tf32_rna(U[q]));
+            w[2 * q + 1] = tf32_rna(V[q] - tf32_rna(V[q]));
+        }
+        tc_st16(taddr + 64 * j + 16, w);
+        tc_wait_st();
+    }
+}
+
+// TMEM columns of a block of the tensor-core kernels (two blocks per SM at most):
+// A operands [0, 128), two D buffers [128, 256).
+constexpr uint32_t kTcCols = 256;
+constexpr uint64_t kTcWaitNs = 1000000000ull;  // bound of one MMA wait (1 s)
+
+// TCR ("tensor-core reconstruction"): the two per-element reconstructions of P4
+// (prediction, echo) and P5 (prediction, drive combination) -- and, in a form
+// the host does not launch, P3 (metric, prediction) -- of a class-0 item (256
+// columns x 16 rows, rank pad 8) are one 3xTF32 tcgen05 product each,
+// D[col][row] = sum_k A[col][k] B[row][k] with A the column factors
+// (K, 0, U_1, V_1, ..., U_7, V_7) in TMEM and B the 16 carrier rows
+// (a1_k, a2_k) in shared memory; hi / lo tf32 splits of both operands give
+// A_hi B_hi + A_hi B_lo + A_lo B_hi, float32-level accuracy.  The products of
+// item i+1 are issued at the start of item i into the other D buffer, so the
+// tensor core runs under the CUDA-core work of the item.
+template <int PASS, int RM, int NT, bool FULL, bool TCR>
 __global__ void __launch_bounds__(kThreads, PassCfg<PASS, RM>::kMinBlocks)
 spectral_pass_kernel(const GroupHdr* __restrict__ hdr, const DevTensor* __restrict__ dts,
                      const int64_t* __restrict__ item_lists, const int32_t* __restrict__ tensor_lists,
                      double* __restrict__ rec_scal, float* __restrict__ rec_bins) {
+    static_assert(!TCR || (FULL && RM == 8 && PASS >= 3), "tensor-core reconstruction: class 0, rank pad 8, P3-P5");
     constexpr int NACC = PassCfg<PASS, RM>::kAccDoubles;
     constexpr int UNR = PassCfg<PASS, RM>::kUnroll;
     extern __shared__ __align__(16) unsigned char smem_raw[];
@@ -310,7 +361,7 @@ spectral_pass_kernel(const GroupHdr* __restrict__ hdr, const DevTensor* __restri
     const int TB = (int)hdr->tb, B = (int)hdr->bins;
     const int T = NT > 0 ? NT : (int)hdr->tables;  // hash tables (compile-time 1 or 2 on the fast path)
     const int T2 = T < 2 ? T : 2;                    // tables whose bin bytes are staged
-    const int ITERS = (int)hdr->iters;
+    const int ITERS = TCR ? 16 : (int)hdr->iters;  // the host launches TCR kernels only when iters == 16
     const bool idx8 = FULL || hdr->idx_bytes == 1;
     const int ib = idx8 ? 1 : 2;
     const bool stage_p_any = PassCfg<PASS, RM>::kP || (PASS <= 3 && hdr->hp[H_WD] != 0.0);
@@ -345,6 +396,27 @@ spectral_pass_kernel(const GroupHdr* __restrict__ hdr, const DevTensor* __restri
     float* s_tab = reinterpret_cast<float*>(s_ibin + (kBins ? ncopies * cstride : 0));  // TB
     float* s_rowred = s_tab + (kTab ? TB : 0);                                // 8 * ITERS
     float* s_colred = s_rowred + (PASS == 2 ? 8 * ITERS : 0);                 // kThreads
+    // TCR: B tiles [buffer][hi, lo] (128-byte aligned), the MMA mbarrier, TMEM base, wait flag
+    unsigned char* s_tcb = nullptr;
+    uint64_t* s_tcbar = nullptr;
+    uint32_t* s_tcslot = nullptr;
+    int* s_tcflag = nullptr;
+    uint32_t tc_base = 0, tc_parity = 0;
+    bool tc_abort = false;
+    if constexpr (TCR) {
+        const uint32_t raw = smem_u32(smem_raw);
+        const uint32_t end = smem_u32(s_colred + (PASS == 2 ? kThreads : 0));
+        s_tcb = smem_raw + (((end + 127u) & ~127u) - raw);
+        s_tcbar = reinterpret_cast<uint64_t*>(s_tcb + 4 * kTcTileBytes);
+        s_tcslot = reinterpret_cast<uint32_t*>(s_tcbar + 1);
+        s_tcflag = reinterpret_cast<int*>(s_tcslot + 1);
+        if (warp == 0) tc_alloc(s_tcslot, kTcCols);
+        if (tid == 0) mbar_init(s_tcbar, 1);
+        tc_fence_before();
+        __syncthreads();
+        tc_fence_after();
+        tc_base = *s_tcslot;
+    }
 
     int k = find_tensor(item_base, nt, it0);
     int64_t it = it0;
@@ -517,6 +589,67 @@ spectral_pass_kernel(const GroupHdr* __restrict__ hdr, const DevTensor* __restri
         float U1[RM], V1[RM], U2[RM], V2[RM];
         float colf = 1.0f;
         int uv_ct = -1;
+        int tcb = 0;    // TCR: D and B buffer of the current item
+        int a_ct = -1;  // TCR: column tile whose factors are in TMEM
+        const int tc_h = tid >> 7;                               // TCR: column half = M tile
+        const uint32_t tc_lane = (uint32_t)(tid & 96) << 16;     // TCR: this warp's TMEM lane quarter
+        // TCR helpers: the column factors of tile c into TMEM (A, both reconstructions, hi
+        // and lo); the 16 carrier rows of band bnd into B buffer bb; the products of one
+        // item into D buffer bb (one thread) and their commit to the mbarrier.
+        auto tc_build_a = [&](int c) {
+            if constexpr (TCR) tc_column_factors<RM>(coltab, gcols, col0 + (int64_t)c * 256 + lc, s_coef, tc_base + tc_lane + 32 * tc_h);
+        };
+        // this thread's value of the carrier rows of band bnd (row tid / 16, slot tid % 16)
+        auto tc_load_b = [&](int bnd) -> float {
+            if constexpr (TCR) return __ldg(rowtab + ((int64_t)row032 + bnd * 16 + (tid >> 4)) * 16 + (tid & 15));
+            return 0.0f;
+        };
+        auto tc_store_b = [&](float v, int bb) {
+            if constexpr (TCR) {
+                const float hi = tf32_rna(v);
+                unsigned char* tb = s_tcb + bb * 2 * kTcTileBytes;
+                const int o = tc_kmajor_off(tid >> 4, tid & 15);
+                *reinterpret_cast<float*>(tb + o) = hi;
+                *reinterpret_cast<float*>(tb + kTcTileBytes + o) = tf32_rna(v - hi);
+            }
+        };
+        auto tc_issue = [&](int bb) {
+            if constexpr (TCR) {
+                tc_fence_after();
+                const uint32_t bhi = smem_u32(s_tcb + bb * 2 * kTcTileBytes), blo = bhi + kTcTileBytes;
+                constexpr uint32_t idesc = tc_idesc_tf32(128, 16);
+#pragma unroll
+                for (int j = 0; j < 2; ++j) {
+#pragma unroll
+                    for (int hh = 0; hh < 2; ++hh) {
+                        const uint32_t d = tc_base + 128 + 64 * bb + 32 * j + 16 * hh;
+                        const uint32_t ahi = tc_base + 16 * (4 * j + 2 * hh), alo = ahi + 16;
+#pragma unroll
+                        for (int ks = 0; ks < 2; ++ks) {
+                            const uint32_t bo = 2 * kTcLBO * ks;
+                            tc_mma_tf32_ts(d, ahi + 8 * ks, tc_smem_desc(bhi + bo), idesc, ks > 0);
+                            tc_mma_tf32_ts(d, ahi + 8 * ks, tc_smem_desc(blo + bo), idesc, 1);
+                            tc_mma_tf32_ts(d, alo + 8 * ks, tc_smem_desc(bhi + bo), idesc, 1);
+                        }
+                    }
+                }
+                tc_commit(smem_u32(s_tcbar));
+            }
+        };
+        // TCR pipeline: the products of item i + 1 are issued at the start of item i and run
+        // under its CUDA-core work; the carrier rows of item i + 2 are fetched into a register
+        // at the start of item i and stored as B operand at its end.
+        float tc_bnext = 0.0f;
+        if constexpr (TCR) {  // segment prologue: B of the first two items, the first item's products
+            tc_build_a(ct);
+            a_ct = ct;
+            tc_store_b(tc_load_b(band), 0);
+            if (it + 1 < seg_end) tc_store_b(tc_load_b(band + 1 == n_bands ? 0 : band + 1), 1);
+            tc_fence_smem();
+            tc_fence_before();
+            __syncthreads();
+            if (tid == 0) tc_issue(0);
+        }
         float z1[RM], z2[RM];
         float zc = 0.0f;
 #pragma unroll
@@ -538,6 +671,11 @@ spectral_pass_kernel(const GroupHdr* __restrict__ hdr, const DevTensor* __restri
             } else {
                 stage_item(ct, band, buf);
             }
+            if constexpr (TCR) {
+                // this item's products were issued one item earlier (or in the segment prologue)
+                if (tid == 0) *s_tcflag = mbar_wait_bounded(smem_u32(s_tcbar), tc_parity, kTcWaitNs) ? 0 : 1;
+                tc_parity ^= 1;
+            }
             __syncthreads();
             // tiles of this item in shared memory (row table: staged, or global for unaligned tensors)
             const unsigned char* sb = s_stage + buf * sbytes;
@@ -550,19 +688,48 @@ spectral_pass_kernel(const GroupHdr* __restrict__ hdr, const DevTensor* __restri
             if constexpr (PASS >= 3) {
                 if (ct != uv_ct) {
                     uv_ct = ct;
-                    float b1[RM], b2[RM];
-                    load_col<RM>(coltab, gcols, gc, b1, b2);
-                    make_uv<RM>(b1, b2, s_coef, s_coef + RM, U1, V1);
-                    make_uv<RM>(b1, b2, s_coef + 2 * RM, s_coef + 3 * RM, U2, V2);
+                    if constexpr (!TCR) {
+                        float b1[RM], b2[RM];
+                        load_col<RM>(coltab, gcols, gc, b1, b2);
+                        make_uv<RM>(b1, b2, s_coef, s_coef + RM, U1, V1);
+                        make_uv<RM>(b1, b2, s_coef + 2 * RM, s_coef + 3 * RM, U2, V2);
+                    }
                     if constexpr (PASS == 3) {
                         if (flags & F_INST2D) colf = Dp->colf[cvalid ? col : 0];
                     }
                 }
             }
+            // TCR: this item's two reconstructions are in D buffer tcb (read per row group below)
+            if constexpr (TCR) {
+                if (*s_tcflag) {  // a product never completed: stop this block (uniform after the barrier)
+                    if (tid == 0) atomicExch(hdr->status, 1);
+                    tc_abort = true;
+                    break;
+                }
+                tc_fence_after();
+                if (it + 1 < seg_end) {
+                    if (nct != a_ct) {  // the next item starts a new column tile (block-uniform)
+                        tc_build_a(nct);
+                        a_ct = nct;
+                        tc_fence_before();
+                        __syncthreads();
+                    }
+                    if (tid == 0) tc_issue(tcb ^ 1);
+                }
+                if (it + 2 < seg_end) tc_bnext = tc_load_b(nband + 1 == n_bands ? 0 : nband + 1);
+            }
             float s0 = 0.0f, s1 = 0.0f, colacc = 0.0f;
 
             for (int m0 = 0; m0 < ITERS; m0 += UNR) {
                 float dv[UNR];
+                // TCR: rows m0 .. m0 + UNR - 1 of both reconstructions for this thread's column
+                float R1[TCR ? UNR : 1], R2[TCR ? UNR : 1];
+                if constexpr (TCR) {
+                    const uint32_t ta = tc_base + tc_lane + 128 + 64 * tcb + 16 * tc_h + m0;
+                    tc_ld<UNR>(ta, R1);
+                    tc_ld<UNR>(ta + 32, R2);
+                    tc_wait_ld();
+                }
 #pragma unroll
                 for (int u = 0; u < UNR; ++u) {
                     dv[u] = 0.0f;
@@ -621,7 +788,9 @@ spectral_pass_kernel(const GroupHdr* __restrict__ hdr, const DevTensor* __restri
                         float a1[RM], a2[RM];
                         load_row<RM>(rtb, lr, a1, a2);
                         const float rel = fminf(fabsf(f) * inv_scale + eps, 1.0e4f);
-                        const float lm = clampf(recon_dot_nz<RM>(K1, a1, a2, U1, V1), -3.0f, 3.0f);
+                        float lm_raw;
+                        if constexpr (TCR) lm_raw = R1[u]; else lm_raw = recon_dot_nz<RM>(K1, a1, a2, U1, V1);
+                        const float lm = clampf(lm_raw, -3.0f, 3.0f);
                         const float metric = clampf(__expf(mcpl * lm), 0.06f, 16.0f);  // |mcpl * lm| <= 3 mcpl
                         float den = scale * metric;
                         if (flags & F_LOCAL) den = den * clampf(1.0f + lsh * sqrt_sfu(fminf(rel, 100.0f)), 1.0f, 8.0f);
@@ -645,7 +814,8 @@ spectral_pass_kernel(const GroupHdr* __restrict__ hdr, const DevTensor* __restri
                         }
                         const float t = clampf(__fdividef(f, den + eps), -1.0e4f, 1.0e4f);
                         tbuf[(int64_t)r * cols32 + col] = t;
-                        const float pred = recon_dot_nz<RM>(K2, a1, a2, U2, V2);
+                        float pred;
+                        if constexpr (TCR) pred = R2[u]; else pred = recon_dot_nz<RM>(K2, a1, a2, U2, V2);
                         const float err = t - pred;
                         s0 = fmaf(err, err, s0);
                         s1 += t;
@@ -672,11 +842,17 @@ spectral_pass_kernel(const GroupHdr* __restrict__ hdr, const DevTensor* __restri
                             }
                         }
                     } else if constexpr (PASS == 4) {
-                        float a1[RM], a2[RM];
-                        load_row<RM>(rtb, lr, a1, a2);
+                        float pred, echo;
+                        if constexpr (TCR) {
+                            pred = R1[u];
+                            echo = (flags & F_ECHO) ? R2[u] : 0.0f;
+                        } else {
+                            float a1[RM], a2[RM];
+                            load_row<RM>(rtb, lr, a1, a2);
+                            pred = recon_dot_nz<RM>(K1, a1, a2, U1, V1);
+                            echo = (flags & F_ECHO) ? recon_dot_nz<RM>(K2, a1, a2, U2, V2) : 0.0f;
+                        }
                         const float t = xval;
-                        const float pred = recon_dot_nz<RM>(K1, a1, a2, U1, V1);
-                        const float echo = (flags & F_ECHO) ? recon_dot_nz<RM>(K2, a1, a2, U2, V2) : 0.0f;
                         float hpv = 0.0f;
                         if (hash_on) {
 #pragma unroll
@@ -691,11 +867,17 @@ spectral_pass_kernel(const GroupHdr* __restrict__ hdr, const DevTensor* __restri
                             for (int b = a; b < 7; ++b) g32[gram_idx(a, b)] = fmaf(v[a], v[b], g32[gram_idx(a, b)]);
                         g32[28] = fmaf(dp.rat, dp.rat, g32[28]);
                     } else {  // PASS 5
-                        float a1[RM], a2[RM];
-                        load_row<RM>(rtb, lr, a1, a2);
+                        float pred, comb;
+                        if constexpr (TCR) {
+                            pred = R1[u];
+                            comb = R2[u];
+                        } else {
+                            float a1[RM], a2[RM];
+                            load_row<RM>(rtb, lr, a1, a2);
+                            pred = recon_dot_nz<RM>(K1, a1, a2, U1, V1);
+                            comb = recon_dot_nz<RM>(K2, a1, a2, U2, V2);
+                        }
                         const float t = xval;
-                        const float pred = recon_dot_nz<RM>(K1, a1, a2, U1, V1);
-                        const float comb = recon_dot_nz<RM>(K2, a1, a2, U2, V2);
                         float hpv = 0.0f;
                         if (hash_on) {
 #pragma unroll
@@ -803,7 +985,15 @@ spectral_pass_kernel(const GroupHdr* __restrict__ hdr, const DevTensor* __restri
                     Dp->colpart[(int64_t)band * cols + col] = s;
                 }
             }
+            if constexpr (TCR) {  // item i + 2's carrier rows into this item's B buffer (its products are done)
+                if (it + 2 < seg_end) {
+                    tc_store_b(tc_bnext, tcb);
+                    tc_fence_smem();
+                }
+                tc_fence_before();
+            }
             __syncthreads();  // this buffer (and the reduction scratch) is free again
+            if constexpr (TCR) tcb ^= 1;
             if constexpr (kBins) {
                 // empty the fixed-point copies into the exact block sums (ordered before the
                 // next item's atomics by the barrier that precedes its compute)
@@ -858,6 +1048,17 @@ spectral_pass_kernel(const GroupHdr* __restrict__ hdr, const DevTensor* __restri
         }
         __syncthreads();
         ++k;
+        if (tc_abort) break;
+    }
+    if constexpr (TCR) {
+        cp_async_wait<0>();
+        if (tc_abort && tid == 0) mbar_wait_bounded(smem_u32(s_tcbar), tc_parity ^ 1, kTcWaitNs);
+        tc_fence_before();
+        __syncthreads();
+        if (warp == 0) {
+            tc_fence_after();
+            tc_dealloc(tc_base, kTcCols);
+        }
     }
 }
 
@@ -1265,13 +1466,14 @@ struct Plan {
     std::vector<DevTensor> dts;
     std::vector<int64_t> item_lists;   // class 0 item prefix sums (n0 + 1), then class 1 (n1 + 1)
     std::vector<int32_t> tensor_lists; // class 0 tensor indices, then class 1
+    int64_t off_status;
     int64_t off_hdr, off_dts, off_items, off_tmap, off_cst, off_htab, off_rowf, off_colf, off_rowpart, off_colpart;
     int64_t off_recs, off_recb, off_red[5], len_red[5], off_tbuf, bytes;
     int64_t n_rec_max;
     int rm;
 };
 
-static size_t pass_smem(int pass, const GroupHdr& H, int64_t iters);
+static size_t pass_smem(int pass, const GroupHdr& H, int64_t iters, bool tc = false);
 
 static int64_t take(int64_t& off, int64_t bytes) {
     const int64_t o = off;
@@ -1355,7 +1557,7 @@ static int build_plan(const cresso_tensor_desc* descs, int64_t n, const cresso_h
             if (vec[i]) rb_max = std::max<int64_t>(rb_max, (int64_t)(256 / std::min(256, pow2_ceil(descs[i].cols))) * iters);
         H.rb_max = rb_max;
         size_t need = 0;
-        for (int p = 1; p <= 5; ++p) need = std::max(need, pass_smem(p, H, iters));
+        for (int p = 1; p <= 5; ++p) need = std::max(need, pass_smem(p, H, iters, p >= 4 && rm == 8 && iters == 16));
         if (need <= budget || iters <= 4) break;
     }
     H.iters = iters;
@@ -1488,6 +1690,7 @@ static int build_plan(const cresso_tensor_desc* descs, int64_t n, const cresso_h
     P.off_dts = take(off, sizeof(DevTensor) * n);
     P.off_items = take(off, sizeof(int64_t) * (n + 2));
     P.off_tmap = take(off, sizeof(int32_t) * n);
+    P.off_status = take(off, sizeof(int32_t));
     P.off_cst = take(off, sizeof(TensorConsts) * n);
     int64_t rows_tot = 0, cols_tot = 0, rowpart_tot = 0, colpart_tot = 0, elems = 0;
     for (auto& D : P.dts) {
@@ -1540,7 +1743,7 @@ static void bind_scratch(Plan& P, char* base) {
     }
 }
 
-static size_t pass_smem(int pass, const GroupHdr& H, int64_t iters) {
+static size_t pass_smem(int pass, const GroupHdr& H, int64_t iters, bool tc) {
     const int tb = (int)H.tb;
     const int rm = (int)H.rm;
     const int nacc = pass == 4 ? kWarps * 32 : (pass == 2 || pass == 3 ? 2 * rm * kThreads : 0);
@@ -1554,6 +1757,12 @@ static size_t pass_smem(int pass, const GroupHdr& H, int64_t iters) {
     }
     if (pass >= 3) b += (size_t)tb * 4;
     if (pass == 2) b += (size_t)(8 * iters + kThreads) * 4;
+    if (tc) {
+        // B tiles (128-byte aligned), mbarrier, TMEM slot, wait flag; and at least 78 KB so
+        // that at most two blocks (2 x 256 TMEM columns) share an SM
+        b += 128 + 4 * kTcTileBytes + 16;
+        b = std::max<size_t>(b, 78 * 1024);
+    }
     return b;
 }
 
@@ -1566,11 +1775,16 @@ static int launch_stage(int stage, const Plan& P, char* base, cudaStream_t s) {
     double* recs = reinterpret_cast<double*>(base + P.off_recs);
     float* recb = reinterpret_cast<float*>(base + P.off_recb);
     const int n = (int)P.hdr.n_tensors;
-    auto run_pass = [&](auto kern_full, auto kern_gen, int pass) -> int {
-        const size_t smem = pass_smem(pass, P.hdr, P.hdr.iters);
+    // class 0 of P4 / P5 at rank pad 8 with 16-row items: the tensor-core kernels.  (The
+    // P3 form exists and passes the parity tests, but measured slower than the CUDA-core
+    // form: P3 still needs the row factors for its projection, and its tangent depends on
+    // the first reconstruction.)
+    auto run_pass = [&](auto kern_tc, auto kern_full, auto kern_gen, int pass) -> int {
         for (int c = 0; c < 2; ++c) {
             if (P.hdr.grid[c][pass] == 0) continue;
-            auto kern = c == 0 ? kern_full : kern_gen;
+            const bool tc = c == 0 && pass >= 4 && RM == 8 && P.hdr.iters == 16;
+            const size_t smem = pass_smem(pass, P.hdr, P.hdr.iters, tc);
+            auto kern = c == 0 ? (tc ? kern_tc : kern_full) : kern_gen;
             if (smem > 48 * 1024)
                 CRESSO_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
             kern<<<(unsigned)P.hdr.grid[c][pass], kThreads, smem, s>>>(hdr, dts, items, tmap, recs, recb);
@@ -1587,31 +1801,36 @@ static int launch_stage(int stage, const Plan& P, char* base, cudaStream_t s) {
         return CRESSO_OK;
     };
     switch (stage) {
-        case 1: return run_pass(spectral_pass_kernel<1, RM, NT, true>, spectral_pass_kernel<1, RM, NT, false>, 1);
+        case 1: return run_pass(spectral_pass_kernel<1, RM, NT, true, false>, spectral_pass_kernel<1, RM, NT, true, false>,
+                            spectral_pass_kernel<1, RM, NT, false, false>, 1);
         case 2: return run_reduce(1);
         case 3:
             finalize1_kernel<RM><<<n, kThreads, 0, s>>>(hdr, dts);
             CRESSO_LAUNCHED("finalize1_kernel");
             return CRESSO_OK;
-        case 4: return run_pass(spectral_pass_kernel<2, RM, NT, true>, spectral_pass_kernel<2, RM, NT, false>, 2);
+        case 4: return run_pass(spectral_pass_kernel<2, RM, NT, true, false>, spectral_pass_kernel<2, RM, NT, true, false>,
+                            spectral_pass_kernel<2, RM, NT, false, false>, 2);
         case 5: return run_reduce(2);
         case 6:
             finalize2_kernel<RM><<<n, kThreads, 0, s>>>(hdr, dts);
             CRESSO_LAUNCHED("finalize2_kernel");
             return CRESSO_OK;
-        case 7: return run_pass(spectral_pass_kernel<3, RM, NT, true>, spectral_pass_kernel<3, RM, NT, false>, 3);
+        case 7: return run_pass(spectral_pass_kernel<3, RM, NT, true, false>, spectral_pass_kernel<3, RM, NT, true, false>,
+                            spectral_pass_kernel<3, RM, NT, false, false>, 3);
         case 8: return run_reduce(3);
         case 9:
             finalize3_kernel<RM><<<n, kThreads, 0, s>>>(hdr, dts);
             CRESSO_LAUNCHED("finalize3_kernel");
             return CRESSO_OK;
-        case 10: return run_pass(spectral_pass_kernel<4, RM, NT, true>, spectral_pass_kernel<4, RM, NT, false>, 4);
+        case 10: return run_pass(spectral_pass_kernel<4, RM, NT, true, RM == 8>, spectral_pass_kernel<4, RM, NT, true, false>,
+                            spectral_pass_kernel<4, RM, NT, false, false>, 4);
         case 11: return run_reduce(4);
         case 12:
             finalize4_kernel<RM><<<n, kThreads, 0, s>>>(hdr, dts);
             CRESSO_LAUNCHED("finalize4_kernel");
             return CRESSO_OK;
-        case 13: return run_pass(spectral_pass_kernel<5, RM, NT, true>, spectral_pass_kernel<5, RM, NT, false>, 5);
+        case 13: return run_pass(spectral_pass_kernel<5, RM, NT, true, RM == 8>, spectral_pass_kernel<5, RM, NT, true, false>,
+                            spectral_pass_kernel<5, RM, NT, false, false>, 5);
         default: return CRESSO_OK;
     }
 }
@@ -1633,6 +1852,7 @@ int cresso_spectral_layout(const cresso_tensor_desc* descs, int64_t n, const cre
         layout[2 * p - 1] = P.off_red[p];
         layout[2 * p] = P.len_red[p];
     }
+    if (layout_len >= 10) layout[9] = P.off_status;
     return CRESSO_OK;
 }
 
@@ -1650,7 +1870,9 @@ int cresso_spectral_run(const cresso_tensor_desc* descs, int64_t n, const cresso
     char* base = (char*)scratch;
     cudaStream_t s = (cudaStream_t)stream;
     bind_scratch(P, base);
+    P.hdr.status = reinterpret_cast<int32_t*>(base + P.off_status);
     if (stage_begin == 0) {
+        CRESSO_CUDA(cudaMemsetAsync(base + P.off_status, 0, sizeof(int32_t), s));
         CRESSO_CUDA(cudaMemcpyAsync(base + P.off_hdr, &P.hdr, sizeof(GroupHdr), cudaMemcpyHostToDevice, s));
         CRESSO_CUDA(cudaMemcpyAsync(base + P.off_dts, P.dts.data(), sizeof(DevTensor) * n, cudaMemcpyHostToDevice, s));
         CRESSO_CUDA(cudaMemcpyAsync(base + P.off_items, P.item_lists.data(), sizeof(int64_t) * (n + 2),

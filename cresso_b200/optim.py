@@ -203,6 +203,7 @@ class CRESSO5(Optimizer):
         self._shape_ws: Dict[tuple, Tensor] = {}
         self._hash_cache: Dict[tuple, Tuple[Tensor, int]] = {}
         self._scratch: Dict[tuple, Tensor] = {}
+        self._status_words: Dict[object, Tensor] = {}
 
     # ------------------------------------------------------------------ state
     def _init_common(self, state: dict, device, dtype) -> None:
@@ -411,10 +412,11 @@ class CRESSO5(Optimizer):
         descs = self._spectral_descs(group, device, items)
         n = len(items)
         num_sms = torch.cuda.get_device_properties(device).multi_processor_count
-        layout = np.zeros(9, dtype=np.int64)
+        layout = np.zeros(10, dtype=np.int64)
         _lib.check(L.cresso_spectral_layout(_lib.ptr(descs), n, _lib.ptr(hp), num_sms,
-                                            layout.ctypes.data_as(_lib._pi64), 9), "spectral_layout")
+                                            layout.ctypes.data_as(_lib._pi64), 10), "spectral_layout")
         scratch = self._scratch_buffer(device, "spectral", int(layout[0]))
+        self._status_words[device] = scratch[int(layout[9]):int(layout[9]) + 4].view(torch.int32)
         stream = torch.cuda.current_stream(device).cuda_stream
 
         def run(begin: int, end: int) -> None:
@@ -422,6 +424,11 @@ class CRESSO5(Optimizer):
                                              begin, end, num_sms, stream), "spectral_run")
 
         self._spectral_stages(run, scratch, layout)
+
+    def _device_status(self) -> int:
+        """Status word of the last spectral step on each device (synchronises):
+        nonzero when a bounded wait inside a kernel gave up."""
+        return max((int(w.item()) for w in self._status_words.values()), default=0)
 
     def _spectral_stages(self, run: Callable[[int, int], None], scratch: Tensor, layout: np.ndarray) -> None:
         """Runs the kernel stages of a group step; one GPU needs no exchange."""

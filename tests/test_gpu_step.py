@@ -140,6 +140,7 @@ def test_benchmark_config_ten_steps(cfg):
         ref32.step()
         ref64.step()
     torch.cuda.synchronize()
+    assert opt._device_status() == 0  # no bounded in-kernel wait gave up
     for i, (p, r, r64, x0) in enumerate(zip(ps, refs32, refs64, inits)):
         st = {k: (v.cpu() if torch.is_tensor(v) else v) for k, v in opt.state[p].items()}
         st32 = {k: (v.cpu() if torch.is_tensor(v) else v) for k, v in ref32.state[r].items()}
