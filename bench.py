@@ -265,6 +265,9 @@ def b200_arm(args, world, rank, local):
             mark_row_shard(p, s, start)
         g = torch.empty(local_shape, device=device)
         g.normal_(0.0, 1e-3, generator=gen)
+        if args.workload == "c2":  # BASELINE c2: per-row log-normal(0, 0.5) gradient scale
+            row_scale = torch.empty((local_shape[0], 1), device=device).normal_(0.0, 1.0, generator=gen)
+            g.mul_(torch.exp(0.5 * row_scale))
         p.grad = g
         params.append(p)
         grads_dev.append(g)
