@@ -411,7 +411,7 @@ spectral_pass_kernel(const GroupHdr* __restrict__ hdr, const DevTensor* __restri
         s_tcslot = reinterpret_cast<uint32_t*>(s_tcbar + 1);
         s_tcflag = reinterpret_cast<int*>(s_tcslot + 1);
         if (warp == 0) tc_alloc(s_tcslot, kTcCols);
-        if (tid == 0) mbar_init(s_tcbar, 1);
+        if (tid == 0) mbar_init(s_tcbar, 4);  // one arrival per issuing thread
         tc_fence_before();
         __syncthreads();
         tc_fence_after();
@@ -613,25 +613,22 @@ spectral_pass_kernel(const GroupHdr* __restrict__ hdr, const DevTensor* __restri
                 *reinterpret_cast<float*>(tb + kTcTileBytes + o) = tf32_rna(v - hi);
             }
         };
+        // issued by the four threads tid % 64 == 0 (warps 0, 2, 4, 6), one reconstruction j and
+        // one column half each, so no single warp carries all 24 products of an item
         auto tc_issue = [&](int bb) {
             if constexpr (TCR) {
                 tc_fence_after();
+                const int j = (tid >> 6) & 1, hh = tid >> 7;
                 const uint32_t bhi = smem_u32(s_tcb + bb * 2 * kTcTileBytes), blo = bhi + kTcTileBytes;
                 constexpr uint32_t idesc = tc_idesc_tf32(128, 16);
+                const uint32_t d = tc_base + 128 + 64 * bb + 32 * j + 16 * hh;
+                const uint32_t ahi = tc_base + 16 * (4 * j + 2 * hh), alo = ahi + 16;
 #pragma unroll
-                for (int j = 0; j < 2; ++j) {
-#pragma unroll
-                    for (int hh = 0; hh < 2; ++hh) {
-                        const uint32_t d = tc_base + 128 + 64 * bb + 32 * j + 16 * hh;
-                        const uint32_t ahi = tc_base + 16 * (4 * j + 2 * hh), alo = ahi + 16;
-#pragma unroll
-                        for (int ks = 0; ks < 2; ++ks) {
-                            const uint32_t bo = 2 * kTcLBO * ks;
-                            tc_mma_tf32_ts(d, ahi + 8 * ks, tc_smem_desc(bhi + bo), idesc, ks > 0);
-                            tc_mma_tf32_ts(d, ahi + 8 * ks, tc_smem_desc(blo + bo), idesc, 1);
-                            tc_mma_tf32_ts(d, alo + 8 * ks, tc_smem_desc(bhi + bo), idesc, 1);
-                        }
-                    }
+                for (int ks = 0; ks < 2; ++ks) {
+                    const uint32_t bo = 2 * kTcLBO * ks;
+                    tc_mma_tf32_ts(d, ahi + 8 * ks, tc_smem_desc(bhi + bo), idesc, ks > 0);
+                    tc_mma_tf32_ts(d, ahi + 8 * ks, tc_smem_desc(blo + bo), idesc, 1);
+                    tc_mma_tf32_ts(d, alo + 8 * ks, tc_smem_desc(bhi + bo), idesc, 1);
                 }
                 tc_commit(smem_u32(s_tcbar));
             }
@@ -648,7 +645,7 @@ spectral_pass_kernel(const GroupHdr* __restrict__ hdr, const DevTensor* __restri
             tc_fence_smem();
             tc_fence_before();
             __syncthreads();
-            if (tid == 0) tc_issue(0);
+            if ((tid & 63) == 0) tc_issue(0);
         }
         float z1[RM], z2[RM];
         float zc = 0.0f;
@@ -714,7 +711,7 @@ spectral_pass_kernel(const GroupHdr* __restrict__ hdr, const DevTensor* __restri
                         tc_fence_before();
                         __syncthreads();
                     }
-                    if (tid == 0) tc_issue(tcb ^ 1);
+                    if ((tid & 63) == 0) tc_issue(tcb ^ 1);
                 }
                 if (it + 2 < seg_end) tc_bnext = tc_load_b(nband + 1 == n_bands ? 0 : nband + 1);
             }
