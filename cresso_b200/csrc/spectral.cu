@@ -330,10 +330,10 @@ __device__ __noinline__ void tc_column_factors(const float* __restrict__ coltab,
 constexpr uint32_t kTcCols = 256;
 constexpr uint64_t kTcWaitNs = 1000000000ull;  // bound of one MMA wait (1 s)
 
-// TCR ("tensor-core reconstruction"): the two per-element reconstructions of P4
-// (prediction, echo) and P5 (prediction, drive combination) -- and, in a form
-// the host does not launch, P3 (metric, prediction) -- of a class-0 item (256
-// columns x 16 rows, rank pad 8) are one 3xTF32 tcgen05 product each,
+// TCR ("tensor-core reconstruction"): the two per-element reconstructions of P3
+// (metric, prediction), P4 (prediction, echo) and P5 (prediction, drive
+// combination) of a class-0 item (256 columns x 16 rows, rank pad 8) are one
+// 3xTF32 tcgen05 product each,
 // D[col][row] = sum_k A[col][k] B[row][k] with A the column factors
 // (K, 0, U_1, V_1, ..., U_7, V_7) in TMEM and B the 16 carrier rows
 // (a1_k, a2_k) in shared memory; hi / lo tf32 splits of both operands give
@@ -347,7 +347,8 @@ spectral_pass_kernel(const GroupHdr* __restrict__ hdr, const DevTensor* __restri
                      double* __restrict__ rec_scal, float* __restrict__ rec_bins) {
     static_assert(!TCR || (FULL && RM == 8 && PASS >= 3), "tensor-core reconstruction: class 0, rank pad 8, P3-P5");
     constexpr int NACC = PassCfg<PASS, RM>::kAccDoubles;
-    constexpr int UNR = PassCfg<PASS, RM>::kUnroll;
+    // rows computed together; P3 keeps two on the CUDA-core form (register budget)
+    constexpr int UNR = (TCR && PASS == 3) ? 4 : PassCfg<PASS, RM>::kUnroll;
     extern __shared__ __align__(16) unsigned char smem_raw[];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
 
@@ -1554,7 +1555,7 @@ static int build_plan(const cresso_tensor_desc* descs, int64_t n, const cresso_h
             if (vec[i]) rb_max = std::max<int64_t>(rb_max, (int64_t)(256 / std::min(256, pow2_ceil(descs[i].cols))) * iters);
         H.rb_max = rb_max;
         size_t need = 0;
-        for (int p = 1; p <= 5; ++p) need = std::max(need, pass_smem(p, H, iters, p >= 4 && rm == 8 && iters == 16));
+        for (int p = 1; p <= 5; ++p) need = std::max(need, pass_smem(p, H, iters, p >= 3 && rm == 8 && iters == 16));
         if (need <= budget || iters <= 4) break;
     }
     H.iters = iters;
@@ -1772,14 +1773,11 @@ static int launch_stage(int stage, const Plan& P, char* base, cudaStream_t s) {
     double* recs = reinterpret_cast<double*>(base + P.off_recs);
     float* recb = reinterpret_cast<float*>(base + P.off_recb);
     const int n = (int)P.hdr.n_tensors;
-    // class 0 of P4 / P5 at rank pad 8 with 16-row items: the tensor-core kernels.  (The
-    // P3 form exists and passes the parity tests, but measured slower than the CUDA-core
-    // form: P3 still needs the row factors for its projection, and its tangent depends on
-    // the first reconstruction.)
+    // class 0 of P3-P5 at rank pad 8 with 16-row items: the tensor-core kernels
     auto run_pass = [&](auto kern_tc, auto kern_full, auto kern_gen, int pass) -> int {
         for (int c = 0; c < 2; ++c) {
             if (P.hdr.grid[c][pass] == 0) continue;
-            const bool tc = c == 0 && pass >= 4 && RM == 8 && P.hdr.iters == 16;
+            const bool tc = c == 0 && pass >= 3 && RM == 8 && P.hdr.iters == 16;
             const size_t smem = pass_smem(pass, P.hdr, P.hdr.iters, tc);
             auto kern = c == 0 ? (tc ? kern_tc : kern_full) : kern_gen;
             if (smem > 48 * 1024)
@@ -1812,7 +1810,7 @@ static int launch_stage(int stage, const Plan& P, char* base, cudaStream_t s) {
             finalize2_kernel<RM><<<n, kThreads, 0, s>>>(hdr, dts);
             CRESSO_LAUNCHED("finalize2_kernel");
             return CRESSO_OK;
-        case 7: return run_pass(spectral_pass_kernel<3, RM, NT, true, false>, spectral_pass_kernel<3, RM, NT, true, false>,
+        case 7: return run_pass(spectral_pass_kernel<3, RM, NT, true, RM == 8>, spectral_pass_kernel<3, RM, NT, true, false>,
                             spectral_pass_kernel<3, RM, NT, false, false>, 3);
         case 8: return run_reduce(3);
         case 9:
