@@ -1848,6 +1848,10 @@ int cresso_spectral_layout(const cresso_tensor_desc* descs, int64_t n, const cre
         layout[2 * p] = P.len_red[p];
     }
     if (layout_len >= 10) layout[9] = P.off_status;
+    if (layout_len >= 12) {
+        layout[10] = P.hdr.iters;
+        layout[11] = (P.hdr.cls_items[0] > 0 && P.rm == 8 && P.hdr.iters == 16) ? ((1 << 3) | (1 << 4) | (1 << 5)) : 0;
+    }
     return CRESSO_OK;
 }
 

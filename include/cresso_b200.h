@@ -176,7 +176,14 @@ CRESSO_API int cresso_instant_axis_metric(const float* rel, int64_t ndim, const 
  *
  * layout[0]  = scratch bytes needed
  * layout[1+2(k-1)], layout[2+2(k-1)] (k = 1..4) = byte offset in the scratch
- *              and length in doubles of reduction vector k. */
+ *              and length in doubles of reduction vector k.
+ * Written only when layout_len is large enough (no counterpart in the reference):
+ * layout[9]  = byte offset of an int32 status word in the scratch, zeroed by
+ *              stage 0 and set nonzero by a kernel whose bounded wait for its
+ *              tensor-core products gave up (the step's results are then invalid);
+ * layout[10] = rows per item of the 256-column tiles;
+ * layout[11] = bit p set when pass Pp of the full-tile tensors runs on the
+ *              tcgen05 tensor cores (p = 3, 4, 5). */
 enum { CRESSO_SPECTRAL_STAGES = 14 };
 CRESSO_API int cresso_spectral_layout(const cresso_tensor_desc* descs, int64_t n, const cresso_hparams* hp,
                            int64_t num_sms, int64_t* layout, int64_t layout_len);

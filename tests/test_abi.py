@@ -93,6 +93,31 @@ def test_spectral_layout_is_host_logic():
     assert lib.cresso_spectral_layout(_lib.ptr(d), 1, _lib.ptr(hp17), 148, lay.ctypes.data_as(_lib._pi64), 9) == 2
 
 
+def test_tensor_core_pass_selection():
+    """The planner's choice of the tcgen05 form (layout[10], layout[11]): large
+    full-tile tensors at rank pad 8 run P3-P5 on the tensor cores; small
+    workloads (fewer rows per item), other rank pads and unaligned shapes do not."""
+    from oracle.cresso5_oracle import hparams
+    lib = _lib.lib()
+
+    def plan(shape, **kw):
+        hp = _lib.pack_hparams(hparams(**{**dict(rank=8, hash_bins=64, hash_tables=2), **kw}))
+        lay = np.zeros(12, dtype=np.int64)
+        d = _fake_desc(shape)
+        assert lib.cresso_spectral_layout(_lib.ptr(d), 1, _lib.ptr(hp), 148, lay.ctypes.data_as(_lib._pi64), 12) == 0
+        return int(lay[10]), int(lay[11]), int(lay[9])
+
+    tc_bits = (1 << 3) | (1 << 4) | (1 << 5)
+    rows, bits, status_off = plan((8192, 2048))
+    assert (rows, bits) == (16, tc_bits) and status_off > 0
+    assert plan((4096, 4096))[:2] == (16, tc_bits)
+    assert plan((4096, 4096), rank=5)[:2] == (16, tc_bits)     # rank 5 pads to 8
+    assert plan((4096, 4096), rank=4)[1] == 0                  # rank pad 4: CUDA-core form
+    assert plan((4096, 4096), rank=12)[1] == 0                 # rank pad 16: CUDA-core form
+    assert plan((2048, 2048))[0] < 16 and plan((2048, 2048))[1] == 0  # small: shorter items
+    assert plan((4096, 4100))[1] == 0                          # ragged columns: general class only
+
+
 def test_scalar_scratch_is_host_logic():
     lib = _lib.lib()
     n = np.zeros(1, dtype=np.int64)

@@ -151,6 +151,49 @@ def test_benchmark_config_ten_steps(cfg):
             break
 
 
+# Hyper-parameter variants on a shape that takes the tensor-core (tcgen05) form
+# of P3-P5: 2-D, full 256-column tiles, 16-row items (the planner picks them for
+# >= ~38k row-tiles of work), rank padded to 8, <= 256 bins.
+TCR_VARIANTS = {
+    "wd_maximize": dict(weight_decay=0.01, maximize=True),
+    "no_echo_no_hash": dict(echo_mix=0.0, hash_bins=0),
+    "local_ipow_ep": dict(local_sharpness=0.5, instant_metric_power=0.7, energy_power=1.5),
+    "rank5_bins256": dict(rank=5, hash_bins=256, hash_tables=1),
+}
+
+
+@pytest.mark.parametrize("variant", list(TCR_VARIANTS.keys()))
+def test_tensor_core_path_variants(variant):
+    steps = 3
+    shape = (8192, 2048)
+    kw = dict(lr=2e-3, rank=8, max_frequency=5, hash_bins=64, hash_tables=2)
+    kw.update(TCR_VARIANTS[variant])
+    g = torch.Generator().manual_seed(11)
+    init = torch.randn(shape, generator=g) * 0.02
+    grads = [torch.randn(shape, generator=g) * 1e-3 for _ in range(steps)]
+    dev = torch.device("cuda")
+    p = torch.nn.Parameter(init.clone().to(dev))
+    opt = cresso_b200.CRESSO5([p], cuda_ops="required", **kw)
+    r32 = torch.nn.Parameter(init.clone().to(dev))
+    ref32 = O.OracleCRESSO5([r32], **kw)
+    r64 = torch.nn.Parameter(init.clone().to(dev, torch.float64))
+    ref64 = O.OracleCRESSO5([r64], **kw)
+    for gr in grads:
+        p.grad = gr.to(dev)
+        r32.grad = gr.to(dev)
+        r64.grad = gr.to(dev, torch.float64)
+        opt.step()
+        ref32.step()
+        ref64.step()
+    torch.cuda.synchronize()
+    assert opt._device_status() == 0
+    st = {k: (v.cpu() if torch.is_tensor(v) else v) for k, v in opt.state[p].items()}
+    st32 = {k: (v.cpu() if torch.is_tensor(v) else v) for k, v in ref32.state[r32].items()}
+    st64 = {k: (v.cpu() if torch.is_tensor(v) else v) for k, v in ref64.state[r64].items()}
+    check_against(f"tcr[{variant}]", init, p.detach().cpu(), st, r32.detach().cpu(), st32, r64.detach().cpu(), st64,
+                  upd_tol=5e-4)
+
+
 def test_run_to_run_deterministic():
     shapes, kw, inits, grads = _bench_inputs("c1", 3)
     outs = []
