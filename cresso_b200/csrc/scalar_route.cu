@@ -10,6 +10,8 @@
 #include <math.h>
 #include <stdint.h>
 
+#include <cooperative_groups.h>
+
 #include <algorithm>
 #include <mutex>
 #include <vector>
@@ -27,6 +29,10 @@ struct ScalTensor {
     const float* grad;
     float *q, *impulse, *metric_q, *metric_impulse, *force_rms, *drive_energy, *surprise, *action;
     float* work;  // per-tensor float scratch (row partials, row / column factors, N-d marginals)
+    // cluster form: slices are row ranges (split_rows) or column ranges of `chunk` rows /
+    // columns; ctc / crpi are the thread mapping of one slice
+    int64_t chunk;
+    int32_t split_rows, ctc, crpi, pad1;
 };
 
 struct ScalHdr {
@@ -415,6 +421,371 @@ __global__ void __launch_bounds__(kThreads) scalar_route_kernel(const ScalHdr* _
     }
 }
 
+// ---------------------------------------------------------------------------
+// Cluster form of the scalar route (tensors of rank <= 2 that fit).
+//
+// A cluster of CS CTAs steps one tensor.  The tensor is cut along its longer
+// axis into CS slices; CTA k keeps the force field of slice k in shared memory
+// for the whole step, so the gradient is read from HBM once and the parameter
+// once (plus once more when weight decay is on) and written once.  The five
+// stages are those of scalar_route_kernel; each global sum is a block sum in
+// every CTA, published in that CTA's shared memory, and added up over the
+// cluster's CTAs in rank order through distributed shared memory, so every
+// CTA obtains the same totals and runs the same scalar arithmetic.  The axis
+// sums of the instant metric are complete inside a CTA along the split axis;
+// the other axis's partial sums are added up over the cluster the same way.
+// CTA 0 alone writes the scalar state, and every CTA reads the old state
+// before the first cluster barrier.
+// ---------------------------------------------------------------------------
+namespace cg = cooperative_groups;
+
+constexpr int kClMax = 8;         // CTAs per cluster (portable maximum)
+constexpr int kClSlice = 16384;   // slice elements held in shared memory (with the row pad)
+constexpr int kClShort = 1024;    // longest unsplit axis
+constexpr int kClLocal = 4096;    // longest slice along the split axis
+
+struct ClShared {
+    double red[16 * kWarps];
+    double tot[16];
+    double slot1[1], slot2[2], slot3[2], slot4[16];  // this CTA's block totals, read by the cluster
+    double all[16];                                  // cluster totals
+    float scale, inv_scale, metric, gm, inst_k, q_new, S, sp, invD;
+    float c_u, c_root, c_t, c_pred, c_nov, gain;
+};
+
+// Sums the K block totals of every CTA of the cluster in rank order into sh.all.
+template <int K>
+__device__ __forceinline__ void cluster_sum(cg::cluster_group& cl, double (&v)[K], double* slot, ClShared& sh) {
+    block_sum_to<K>(v, sh.red, sh.tot);
+    if (threadIdx.x < K) slot[threadIdx.x] = sh.tot[threadIdx.x];
+    cl.sync();
+    if (threadIdx.x < K) {
+        double s = 0.0;
+        for (unsigned r = 0; r < cl.num_blocks(); ++r) s += cl.map_shared_rank(slot, r)[threadIdx.x];
+        sh.all[threadIdx.x] = s;
+    }
+    __syncthreads();
+}
+
+__global__ void __launch_bounds__(kThreads, 4) scalar_cluster_kernel(const ScalHdr* __restrict__ hdr,
+                                                                   const ScalTensor* __restrict__ dts,
+                                                                   int slice_cap, int loc_cap, int short_cap) {
+    cg::cluster_group cl = cg::this_cluster();
+    const int rank = (int)cl.block_rank(), cs = (int)cl.num_blocks();
+    const ScalTensor& D = dts[blockIdx.x / cs];
+    extern __shared__ __align__(16) float smf[];
+    float* F = smf;                       // slice: force, then tangent   [slice_cap]
+    float* loc_sum = F + slice_cap;       // split-axis sums, then factors [loc_cap]
+    float* sh_part = loc_sum + loc_cap;   // this CTA's partial sums of the other axis [short_cap]
+    float* sh_fac = sh_part + short_cap;  // the other axis's factors [short_cap]
+    __shared__ ClShared sh;
+    const double* hp = hdr->hp;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const float eps = (float)hp[S_EPS];
+    const float sgn = hp[S_MAX] != 0.0 ? -1.0f : 1.0f;
+    const float wd = (float)hp[S_WD];
+    const bool wd_on = hp[S_WD] != 0.0;
+    const double N = (double)D.N;
+    const int64_t cols = D.cols;
+    const float* __restrict__ grad = D.grad;
+    float* __restrict__ param = D.param;
+
+    // slice geometry
+    const bool sr = D.split_rows != 0;
+    const int64_t long_len = sr ? D.rows : D.cols;
+    const int64_t lo = (int64_t)rank * D.chunk;
+    const int64_t nloc = lo < long_len ? min(D.chunk, long_len - lo) : 0;
+    const int64_t lrows = sr ? nloc : D.rows, lcols = sr ? D.cols : nloc;
+    const int64_t r_off = sr ? lo : 0, c_off = sr ? 0 : lo;
+    const int64_t ld = (lcols & 1) ? lcols : lcols + 1;  // odd row pitch: conflict-free column sweeps
+    const int TC = D.ctc, RPI = D.crpi;
+    const int lc = tid & (TC - 1), rs = tid / TC;
+    auto for_slice = [&](auto fn) {  // fn(i, j, shared index, global index); no barriers inside
+        for (int64_t j0 = 0; j0 < lcols; j0 += TC) {
+            const int64_t j = j0 + lc;
+            if (j < lcols) {
+                int64_t i = rs;
+                for (; i + 3 * RPI < lrows; i += 4 * RPI) {
+                    fn(i, j, i * ld + j, (i + r_off) * cols + j + c_off);
+                    fn(i + RPI, j, (i + RPI) * ld + j, (i + RPI + r_off) * cols + j + c_off);
+                    fn(i + 2 * RPI, j, (i + 2 * RPI) * ld + j, (i + 2 * RPI + r_off) * cols + j + c_off);
+                    fn(i + 3 * RPI, j, (i + 3 * RPI) * ld + j, (i + 3 * RPI + r_off) * cols + j + c_off);
+                }
+                for (; i < lrows; i += RPI) fn(i, j, i * ld + j, (i + r_off) * cols + j + c_off);
+            }
+        }
+    };
+
+    // the old scalar state, read before any CTA of the cluster writes it
+    float st_fr = 0.f, st_mq = 0.f, st_mp = 0.f, st_q = 0.f, st_S = 0.f, st_imp = 0.f, st_act = 0.f, st_de = 0.f;
+    if (tid == 0) {
+        st_fr = *D.force_rms;
+        st_mq = *D.metric_q;
+        st_mp = *D.metric_impulse;
+        st_q = *D.q;
+        st_S = *D.surprise;
+        st_imp = *D.impulse;
+        st_act = *D.action;
+        st_de = *D.drive_energy;
+    }
+    const bool writer = rank == 0 && tid == 0;
+
+    // ---- stage 1: force field into shared memory, force energy -> force_rms, scale
+    {
+        // float partials over this thread's elements (at most kClSlice / kThreads), float64 above
+        float a0 = 0.0f;
+        for_slice([&](int64_t, int64_t, int64_t q, int64_t e) {
+            float f = sgn * __ldg(grad + e);
+            if (wd_on) f = f + wd * param[e];
+            F[q] = f;
+            a0 = fmaf(f, f, a0);
+        });
+        double v[1] = {(double)a0};
+        cluster_sum<1>(cl, v, sh.slot1, sh);
+        if (tid == 0) {
+            const float frn = sqrtf((float)(sh.all[0] / N) + eps);
+            const float fr = reservoir(st_fr, frn, hp[S_RD], D.step);
+            if (writer) *D.force_rms = fr;
+            sh.scale = fmaxf(fr, eps);
+            sh.inv_scale = 1.0f / sh.scale;
+        }
+        __syncthreads();
+    }
+    const float scale = sh.scale, inv_scale = sh.inv_scale;
+    const float ep = (float)hp[S_EP];
+    const float pw = fmaxf((float)hp[S_IP], 0.25f);
+    const bool ipow1 = pw == 1.0f;
+    const float ic = (float)hp[S_IC];
+    int inst_mode = 0;
+    if (ic != 0.0f && D.ndim > 0 && D.N > 1) inst_mode = D.ndim == 1 ? 1 : 2;
+    auto dens = [&](float rel) { return ipow1 ? rel : fminf(powf(fmaxf(rel, eps), pw), 1.0e6f); };
+    auto dens_of = [&](float f) { return dens(fminf(fabsf(f) * inv_scale + eps, 1.0e4f)); };
+
+    // ---- stage 2: density metric and the instant-metric axis sums
+    {
+        float a0 = 0.0f, a1 = 0.0f;
+        for_slice([&](int64_t, int64_t, int64_t q, int64_t) {
+            const float rel0 = fabsf(F[q]) * inv_scale + eps;  // >= eps > 0 (normal)
+            a0 += log1p_pos(exp2f(ep * __log2f(rel0)));
+            a1 += dens(fminf(rel0, 1.0e4f));
+        });
+        double v[2] = {(double)a0, (double)a1};
+        if (inst_mode == 2) {
+            // split-axis sums (complete here) and this CTA's part of the other axis's sums:
+            // one warp per line, lanes along it, float partials added in a fixed order
+            const int64_t n_loc = sr ? lrows : lcols, n_sh = sr ? lcols : lrows;
+            for (int64_t a = warp; a < n_loc + n_sh; a += kWarps) {
+                const bool is_loc = a < n_loc;
+                const int64_t idx = is_loc ? a : a - n_loc;
+                const bool is_row = is_loc == sr;  // a row of the slice
+                const int64_t len = is_row ? lcols : lrows;
+                float s = 0.0f;
+                for (int64_t b = lane; b < len; b += 32) s += dens_of(F[is_row ? idx * ld + b : b * ld + idx]);
+                for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+                if (lane == 0) (is_loc ? loc_sum : sh_part)[idx] = s;
+            }
+        }
+        cluster_sum<2>(cl, v, sh.slot2, sh);  // its cluster barrier also publishes sh_part
+        if (tid == 0) {
+            // metric oscillator on the scalar density  (cresso_v5.py:1510-1519)
+            const float density = (float)(sh.all[0] / N);
+            const float port = density - tanhf(st_mq);
+            const float mdt = (float)hp[S_MDT];
+            float mp = st_mp * (float)fmax(0.0, 1.0 - hp[S_MDT] * hp[S_MF]);
+            mp = mp + mdt * (port - st_mq);
+            const float mq = clampf(st_mq + mdt * mp, -3.0f, 3.0f);
+            if (writer) {
+                *D.metric_impulse = mp;
+                *D.metric_q = mq;
+            }
+            sh.metric = clampf(expf((float)hp[S_MC] * mq), 0.06f, 16.0f);
+            sh.gm = fmaxf((float)(sh.all[1] / N), eps);
+            sh.inst_k = ic / ((float)(D.ndim > 1 ? D.ndim : 1) * pw);
+        }
+        __syncthreads();
+        if (inst_mode == 2) {
+            // per-axis factors exp(k * log(max(mean / gmean, eps)))  (cresso_v5.py:243-262)
+            const float gm = sh.gm, kk = sh.inst_k;
+            const int64_t n_loc = sr ? lrows : lcols, n_sh = sr ? lcols : lrows;
+            const double len_loc = (double)(sr ? D.cols : D.rows), len_sh = (double)(sr ? D.rows : D.cols);
+            for (int64_t a = tid; a < n_loc; a += kThreads)
+                loc_sum[a] = expf(kk * logf(fmaxf((float)((double)loc_sum[a] / len_loc) / gm, eps)));
+            for (int64_t a = tid; a < n_sh; a += kThreads) {
+                double t = 0.0;
+                for (int r = 0; r < cs; ++r) t += (double)cl.map_shared_rank(sh_part, r)[a];
+                sh_fac[a] = expf(kk * logf(fmaxf((float)(t / len_sh) / gm, eps)));
+            }
+            __syncthreads();
+        }
+    }
+
+    const float metric = sh.metric, gm = sh.gm, kk = sh.inst_k;
+    const float ls = (float)hp[S_LS];
+    const bool local_on = hp[S_LS] != 0.0;
+    const float* rowf = sr ? loc_sum : sh_fac;  // indexed by local row
+    const float* colf = sr ? sh_fac : loc_sum;  // indexed by local column
+    auto tangent = [&](float f, int64_t i, int64_t j) {
+        const float rel = fminf(fabsf(f) * inv_scale + eps, 1.0e4f);
+        float den = scale * metric;
+        if (local_on) den = den * clampf(1.0f + ls * sqrt_sfu(fminf(rel, 100.0f)), 1.0f, 8.0f);
+        if (inst_mode == 1) {
+            den = den * clampf(expf(kk * logf(fmaxf(dens(rel) / gm, eps))), 0.08f, 12.0f);
+        } else if (inst_mode == 2) {
+            den = den * clampf(rowf[i] * colf[j], 0.08f, 12.0f);
+        }
+        return clampf(__fdividef(f, den + eps), -1.0e4f, 1.0e4f);
+    };
+
+    // ---- stage 3: tangent (kept in place of the force), prediction error, surprise, contact
+    {
+        const float q0 = st_q;
+        float q0b;
+        if (tid == 0) sh.q_new = q0;  // broadcast of the old q (only thread 0 read it)
+        __syncthreads();
+        q0b = sh.q_new;
+        float a0 = 0.0f, a1 = 0.0f;
+        for_slice([&](int64_t i, int64_t j, int64_t q, int64_t) {
+            const float t = tangent(F[q], i, j);
+            F[q] = t;
+            const float err = t - q0b;
+            a0 += err;
+            a1 = fmaf(err, err, a1);
+        });
+        double v[2] = {(double)a0, (double)a1};
+        cluster_sum<2>(cl, v, sh.slot3, sh);
+        if (tid == 0) {
+            const float sn = sqrtf((float)(sh.all[1] / N) + eps);
+            const float S = reservoir(st_S, sn, hp[S_SD], D.step);
+            const float port = (float)(sh.all[0] / N);
+            const float dt = (float)hp[S_DT];
+            const float plast = 1.0f + (float)hp[S_SG] * S / (1.0f + S);
+            const float brake = 1.0f / (1.0f + (float)hp[S_SB] * S);
+            float imp = st_imp, q = q0, action = st_act;
+            const float energy = 0.5f * (imp * imp + q * q);
+            action = action * 0.985f + (port * imp - energy) * dt;
+            const float fr = (float)hp[S_IF] + (float)hp[S_CG] * tanhf(fabsf(action));
+            imp = imp * fmaxf(1.0f - dt * fr, 0.0f);
+            imp = imp + dt * (plast * brake * port - (float)hp[S_REST] * q - (float)hp[S_CUBIC] * (q * q * q));
+            q = clampf(q + dt * imp, -8.0f, 8.0f);
+            if (writer) {
+                *D.surprise = S;
+                *D.impulse = imp;
+                *D.action = action;
+                *D.q = q;
+            }
+            sh.q_new = q;
+            sh.S = S;
+            sh.sp = (float)hp[S_SPIKE] / (1.0f + S);
+            sh.invD = 1.0f / ((float)hp[S_CLIP] * (1.0f + S));
+        }
+        __syncthreads();
+    }
+
+    const float qn = sh.q_new, S = sh.S, sp = sh.sp, invD = sh.invD;
+    const float clip = (float)hp[S_CLIP], inv_clip = 1.0f / clip, clip2 = (float)(hp[S_CLIP] * hp[S_CLIP]);
+    struct Parts {
+        float u, root, t, nov, rat;
+    };
+    auto parts = [&](float t) {
+        Parts P;
+        P.t = t;
+        const float at = fabsf(t);
+        P.rat = __fdividef(t, 1.0f + at * inv_clip);  // denominator in [1, 1 + 1e4 / clip]
+        const float bnd = tanhf(t * inv_clip) * clip;
+        P.root = sgnf_s(t) * sqrt_sfu(fminf(at, clip2) + eps);
+        P.u = (1.0f - sp) * P.rat + sp * bnd;
+        P.nov = tanhf((t - qn) * invD) * clip;
+        return P;
+    };
+
+    // ---- stage 4: drive statistics as a Gram of (u, root, t, pred, nov)
+    {
+        float g32[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) g32[j] = 0.0f;
+        for_slice([&](int64_t, int64_t, int64_t q, int64_t) {
+            const Parts P = parts(F[q]);
+            const float v[5] = {P.u, P.root, P.t, qn, P.nov};
+            int j = 0;
+#pragma unroll
+            for (int a = 0; a < 5; ++a)
+#pragma unroll
+                for (int b = a; b < 5; ++b, ++j) g32[j] = fmaf(v[a], v[b], g32[j]);
+            g32[15] = fmaf(P.rat, P.rat, g32[15]);
+        });
+        double g[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) g[j] = (double)g32[j];
+        cluster_sum<16>(cl, g, sh.slot4, sh);
+        if (tid == 0) {
+            const double* G = sh.all;
+            auto Gm = [&](int a, int b) {
+                if (a > b) {
+                    const int t = a;
+                    a = b;
+                    b = t;
+                }
+                return G[a * 5 - (a * (a - 1)) / 2 + (b - a)];
+            };
+            enum { U = 0, RT = 1, TT = 2, PR = 3, NV = 4 };
+            const float frms = sqrtf((float)(Gm(TT, TT) / N) + eps);
+            const float prms = sqrtf((float)(Gm(PR, PR) / N) + eps);
+            const float align = clampf((float)(Gm(TT, PR) / N) / (frms * prms + eps), -1.0f, 1.0f);
+            const float align_gate = prms > (float)sqrt(hp[S_EPS]) ? clampf((align + 1.0f) * 0.5f, 0.0f, 1.0f) : 0.0f;
+            const int ws = (int)hp[S_WS];
+            const double warm = ws == 0 ? 1.0 : (1.0 - exp(-(double)D.step / (double)(ws > 1 ? ws : 1)));
+            const float mix = (float)(hp[S_PM] * warm) * align_gate / (1.0f + S);
+            const float rat_rms = sqrtf((float)(G[15] / N) + eps);
+            const float root_rms = sqrtf((float)(Gm(RT, RT) / N) + eps);
+            const float k_root = rat_rms / fmaxf(root_rms, eps);
+            const float root_mix = (float)hp[S_RCM] / (1.0f + 0.5f * S);
+            const double a = 1.0 - (double)root_mix, b = (double)root_mix * (double)k_root;
+            const double sh2 = a * a * Gm(U, U) + 2.0 * a * b * Gm(U, RT) + b * b * Gm(RT, RT);
+            const float shaped_rms = sqrtf((float)(sh2 / N) + eps);
+            const float dm = (float)hp[S_DFM] / (1.0f + 0.35f * S);
+            const float k_d = shaped_rms / fmaxf(frms, eps);
+            const double cu = (1.0 - dm) * a, cr = (1.0 - dm) * b, ctt = (double)dm * k_d;
+            const double core2 = cu * cu * Gm(U, U) + cr * cr * Gm(RT, RT) + ctt * ctt * Gm(TT, TT) +
+                                 2.0 * (cu * cr * Gm(U, RT) + cu * ctt * Gm(U, TT) + cr * ctt * Gm(RT, TT));
+            const float core_rms = sqrtf((float)(core2 / N) + eps);
+            const float resm = (float)hp[S_RFM] / (1.0f + S);
+            const double err2 = Gm(TT, TT) - 2.0 * Gm(TT, PR) + Gm(PR, PR);
+            const float k_r = core_rms / fmaxf(sqrtf((float)(fmax(err2, 0.0) / N) + eps), eps);
+            double c[5];
+            c[U] = (1.0 - mix) * cu;
+            c[RT] = (1.0 - mix) * cr;
+            c[TT] = (1.0 - mix) * ctt + (double)resm * k_r;
+            c[PR] = (double)mix - (double)resm * k_r;
+            c[NV] = hp[S_NM];
+            double d2 = 0.0;
+            for (int i = 0; i < 5; ++i)
+                for (int j = 0; j < 5; ++j) d2 += c[i] * c[j] * Gm(i, j);
+            const float den = (float)(fmax(d2, 0.0) / N);
+            const float DE = reservoir(st_de, den, hp[S_RD], D.step);
+            if (writer) *D.drive_energy = DE;
+            sh.gain = clampf((float)hp[S_TGT] / sqrtf(DE + eps), (float)hp[S_MING], (float)hp[S_MAXG]);
+            sh.c_u = (float)c[U];
+            sh.c_root = (float)c[RT];
+            sh.c_t = (float)c[TT];
+            sh.c_pred = (float)c[PR];
+            sh.c_nov = (float)c[NV];
+        }
+        // no CTA leaves (or reuses) shared memory another CTA may still read
+        cl.sync();
+    }
+
+    // ---- stage 5: parameter update
+    {
+        const float cu = sh.c_u, cr = sh.c_root, ctt = sh.c_t, cp = sh.c_pred, cn = sh.c_nov, gain = sh.gain;
+        const float neg_lr = (float)(-hp[S_LR]);
+        for_slice([&](int64_t, int64_t, int64_t q, int64_t e) {
+            const Parts P = parts(F[q]);
+            const float drive = cu * P.u + cr * P.root + ctt * P.t + cp * qn + cn * P.nov;
+            param[e] = param[e] + neg_lr * (drive * gain);
+        });
+    }
+}
+
 static int64_t scal_work_floats(const cresso_tensor_desc& d, int* TC, int* RPI, int* n_ct, int* nw, int64_t* rows,
                                 int64_t* cols) {
     int64_t N = 1;
@@ -493,6 +864,102 @@ static int scal_layout(const cresso_tensor_desc* descs, int64_t n, std::vector<S
     return CRESSO_OK;
 }
 
+
+// Slice geometry of a tensor of rank <= 2 cut into cs slices along its longer
+// axis; false when a slice does not fit the cluster form's shared memory.
+struct ClGeom {
+    bool sr;
+    int64_t chunk, lrows, lcols, ld, shortlen;
+};
+static bool cl_geometry(const ScalTensor& S, int cs, ClGeom* g) {
+    if (S.ndim > 2) return false;
+    g->sr = S.ndim == 2 && S.rows >= S.cols;
+    const int64_t longlen = g->sr ? S.rows : S.cols;
+    g->shortlen = g->sr ? S.cols : S.rows;
+    g->chunk = ceil_div(longlen, cs);
+    g->lrows = g->sr ? g->chunk : S.rows;
+    g->lcols = g->sr ? S.cols : g->chunk;
+    g->ld = (g->lcols & 1) ? g->lcols : g->lcols + 1;
+    return g->lrows * g->ld <= kClSlice && g->shortlen <= kClShort && g->chunk <= kClLocal;
+}
+
+// Uploads the header and descriptors into the scratch at `base` and launches
+// the group: the tensors that fit go to the cluster form (listed first), the
+// rest to scalar_route_kernel.
+static int scal_launch(std::vector<ScalTensor>& dts, const cresso_hparams* hp, char* base, cudaStream_t s) {
+    const int64_t n = (int64_t)dts.size();
+    int dev = 0, sms = 148;
+    CRESSO_CUDA(cudaGetDevice(&dev));
+    CRESSO_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+    // smallest cluster size that holds every tensor that fits at all, then more CTAs per
+    // tensor while the grid is below two CTAs per SM
+    std::vector<char> fits(n, 0);
+    int cs = 1;
+    int64_t n_cl = 0;
+    for (int64_t i = 0; i < n; ++i) {
+        ClGeom g;
+        for (int c = 1; c <= kClMax; c *= 2)
+            if (cl_geometry(dts[i], c, &g)) {
+                fits[i] = 1;
+                cs = std::max(cs, c);
+                ++n_cl;
+                break;
+            }
+    }
+    while (cs < kClMax && n_cl * cs < 2 * (int64_t)sms) cs *= 2;
+    std::vector<ScalTensor> ord;
+    ord.reserve(n);
+    int64_t slice_cap = 1, loc_cap = 1, short_cap = 1;
+    for (int64_t i = 0; i < n; ++i) {
+        if (!fits[i]) continue;
+        ScalTensor S = dts[i];
+        ClGeom g;
+        cl_geometry(S, cs, &g);
+        S.chunk = g.chunk;
+        S.split_rows = g.sr ? 1 : 0;
+        S.ctc = std::min(256, pow2_ceil(std::max<int64_t>(g.lcols, 1)));
+        S.crpi = 256 / S.ctc;
+        slice_cap = std::max(slice_cap, g.lrows * g.ld);
+        loc_cap = std::max(loc_cap, g.chunk);
+        short_cap = std::max(short_cap, g.shortlen);
+        ord.push_back(S);
+    }
+    for (int64_t i = 0; i < n; ++i)
+        if (!fits[i]) ord.push_back(dts[i]);
+    ScalHdr h{};
+    h.n = n;
+    memcpy(h.hp, hp, sizeof(cresso_hparams));
+    const int64_t off_dts = align_up((int64_t)sizeof(ScalHdr), 256);
+    CRESSO_CUDA(cudaMemcpyAsync(base, &h, sizeof(h), cudaMemcpyHostToDevice, s));
+    CRESSO_CUDA(cudaMemcpyAsync(base + off_dts, ord.data(), sizeof(ScalTensor) * n, cudaMemcpyHostToDevice, s));
+    const ScalHdr* dh = reinterpret_cast<const ScalHdr*>(base);
+    const ScalTensor* dd = reinterpret_cast<const ScalTensor*>(base + off_dts);
+    if (n_cl > 0) {
+        const size_t smem = 4 * (size_t)(slice_cap + loc_cap + 2 * short_cap);
+        if (smem > 48 * 1024)
+            CRESSO_CUDA(cudaFuncSetAttribute(scalar_cluster_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3((unsigned)(n_cl * cs));
+        cfg.blockDim = dim3(kThreads);
+        cfg.dynamicSmemBytes = smem;
+        cfg.stream = s;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = (unsigned)cs;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        CRESSO_CUDA(cudaLaunchKernelEx(&cfg, scalar_cluster_kernel, dh, dd, (int)slice_cap, (int)loc_cap, (int)short_cap));
+        CRESSO_LAUNCHED("scalar_cluster_kernel");
+    }
+    if (n_cl < n) {
+        scalar_route_kernel<<<(unsigned)(n - n_cl), kThreads, 0, s>>>(dh, dd + n_cl);
+        CRESSO_LAUNCHED("scalar_route_kernel");
+    }
+    return CRESSO_OK;
+}
+
 }  // namespace cresso
 
 using namespace cresso;
@@ -516,17 +983,7 @@ int cresso_scalar_run(const cresso_tensor_desc* descs, int64_t n, const cresso_h
                    (long long)scratch_bytes, (long long)bytes);
     char* base = (char*)scratch;
     for (auto& S : dts) S.work = (float*)(base + (intptr_t)S.work);
-    ScalHdr h{};
-    h.n = n;
-    memcpy(h.hp, hp, sizeof(cresso_hparams));
-    cudaStream_t s = (cudaStream_t)stream;
-    const int64_t off_dts = align_up((int64_t)sizeof(ScalHdr), 256);
-    CRESSO_CUDA(cudaMemcpyAsync(base, &h, sizeof(h), cudaMemcpyHostToDevice, s));
-    CRESSO_CUDA(cudaMemcpyAsync(base + off_dts, dts.data(), sizeof(ScalTensor) * n, cudaMemcpyHostToDevice, s));
-    scalar_route_kernel<<<(unsigned)n, kThreads, 0, s>>>(reinterpret_cast<const ScalHdr*>(base),
-                                                         reinterpret_cast<const ScalTensor*>(base + off_dts));
-    CRESSO_LAUNCHED("scalar_route_kernel");
-    return CRESSO_OK;
+    return scal_launch(dts, hp, base, (cudaStream_t)stream);
 }
 
 // ---------------------------------------------------------------------------
@@ -580,15 +1037,5 @@ extern "C" int cresso_scalar_run_noalloc(const cresso_tensor_desc* descs, int64_
     // and the kernel writes every work float before reading it.
     char* base = (char*)scratch;
     for (auto& S : dts) S.work = (float*)(base + (intptr_t)S.work);
-    ScalHdr h{};
-    h.n = n;
-    memcpy(h.hp, hp, sizeof(cresso_hparams));
-    cudaStream_t s = (cudaStream_t)stream;
-    const int64_t off_dts = align_up((int64_t)sizeof(ScalHdr), 256);
-    CRESSO_CUDA(cudaMemcpyAsync(base, &h, sizeof(h), cudaMemcpyHostToDevice, s));
-    CRESSO_CUDA(cudaMemcpyAsync(base + off_dts, dts.data(), sizeof(ScalTensor) * n, cudaMemcpyHostToDevice, s));
-    scalar_route_kernel<<<(unsigned)n, kThreads, 0, s>>>(reinterpret_cast<const ScalHdr*>(base),
-                                                         reinterpret_cast<const ScalTensor*>(base + off_dts));
-    CRESSO_LAUNCHED("scalar_route_kernel");
-    return CRESSO_OK;
+    return scal_launch(dts, hp, base, (cudaStream_t)stream);
 }

@@ -128,33 +128,6 @@ __device__ __forceinline__ int load_bin(const void* hidx, int idx_bytes, int64_t
 
 __device__ __forceinline__ float sgnf(float x) { return x > 0.f ? 1.f : (x < 0.f ? -1.f : 0.f); }
 
-// Per-element transcendentals of the streaming passes.
-//
-// log(1 + x) for x >= 0.  For x <= 1: log(1 + x) = 2 atanh(z) with
-// z = x / (x + 2) in [0, 1/3], summed as its Taylor series
-// 2 z (1 + z^2/3 + z^4/5 + ... + z^12/13), truncation below 2e-8 relative and
-// no cancellation near x = 0.  For x > 1: ln 2 * log2(1 + x) on the
-// special-function unit, within 2 ulp for arguments above 2.
-__device__ __forceinline__ float log1p_pos(float x) {
-    const float z = __fdividef(x, x + 2.0f);  // divisor in [2, 3] on the branch that uses it
-    const float w = z * z;
-    float p = 1.0f / 13.0f;
-    p = fmaf(p, w, 1.0f / 11.0f);
-    p = fmaf(p, w, 1.0f / 9.0f);
-    p = fmaf(p, w, 1.0f / 7.0f);
-    p = fmaf(p, w, 1.0f / 5.0f);
-    p = fmaf(p, w, 1.0f / 3.0f);
-    const float series = 2.0f * fmaf(z * w, p, z);
-    const float lg = 0.693147180559945309f * __log2f(1.0f + x);
-    return x <= 1.0f ? series : lg;
-}
-// Square root of a positive normal number, approximate (relative error ~2^-22).
-__device__ __forceinline__ float sqrt_sfu(float x) {
-    float r;
-    asm("sqrt.approx.f32 %0, %1;" : "=f"(r) : "f"(x));
-    return r;
-}
-
 // Per-element drive components shared by P4 and P5 (cresso_v5.py:1315-1326).
 struct DriveK {
     float clip, inv_clip, clip2, sp, invD, eps;
