@@ -1,11 +1,14 @@
 // Scalar-route CRESSO5 step (cresso_v5.py:1434-1582): LoRA-thin matrices and
-// tensors below min_spectral_size.  One 256-thread block runs the whole step
-// of one tensor, re-reading the gradient between its five stages (the
-// tensors are small, so the re-reads hit L2); all tensors of a group go in
-// one launch.  The reference needs 13 launches + 2 memsets per tensor
-// (scalar_update_2d_cuda, cresso_cuda_kernel.cu:3225-3605) and covers only
-// 2-D tensors; this kernel covers 0-d to 8-d.
-
+// tensors below min_spectral_size.  All tensors of a group go in one launch
+// per form (the reference needs 13 launches + 2 memsets per tensor,
+// scalar_update_2d_cuda, cresso_cuda_kernel.cu:3225-3605, and covers only 2-D
+// tensors; this file covers 0-d to 8-d):
+//  * scalar_cluster_kernel (tensors of rank <= 2 whose slices fit): a
+//    thread-block cluster per tensor keeps the tensor in shared memory across
+//    the five stages and sums over the cluster through distributed shared
+//    memory;
+//  * scalar_route_kernel (the rest, e.g. N-d tensors): one 256-thread block
+//    per tensor, re-reading the gradient between the stages.
 #include <cuda_runtime.h>
 #include <math.h>
 #include <stdint.h>

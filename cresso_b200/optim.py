@@ -204,6 +204,11 @@ class CRESSO5(Optimizer):
         self._hash_cache: Dict[tuple, Tuple[Tensor, int]] = {}
         self._scratch: Dict[tuple, Tensor] = {}
         self._status_words: Dict[object, Tensor] = {}
+        # host-side caches for groups of many small tensors (LoRA adapters): the route of
+        # each (shape, shard, routing settings), and per device the scalar-route descriptor
+        # table of the last step with the identities it was built from
+        self._route_cache: Dict[tuple, bool] = {}
+        self._scalar_descs: Dict[object, tuple] = {}
 
     # ------------------------------------------------------------------ state
     def _init_common(self, state: dict, device, dtype) -> None:
@@ -331,29 +336,36 @@ class CRESSO5(Optimizer):
         for group in self.param_groups:
             spectral: Dict[torch.device, list] = {}
             scalar: Dict[torch.device, list] = {}
+            route_sig = (group["min_spectral_size"], group["rank"], group.get("thin_matrix_route", "scalar"),
+                         group.get("thin_matrix_max_width", 64), group.get("thin_matrix_min_aspect", 4.0))
+            micro = int(group.get("micro_field_max_size", 0))
+            f32 = torch.float32
             for param in group["params"]:
-                if param.grad is None or not torch.is_floating_point(param):
+                grad = param.grad  # step() runs under no_grad: no detach needed
+                if grad is None or not torch.is_floating_point(param):
                     continue
-                grad = param.grad.detach()
                 if grad.is_sparse:
                     raise RuntimeError("CRESSO5 does not support sparse gradients")
                 if not param.is_cuda:
                     raise RuntimeError(
                         "CRESSO5 cuda_ops='required' requires every optimized parameter to be a CUDA parameter")
-                micro = int(group.get("micro_field_max_size", 0))
                 if micro > 0 and param.ndim > 0 and param.numel() <= micro:
                     raise RuntimeError("CRESSO5 micro-field route (micro_field_max_size > 0) is not available on "
                                        "the B200 CUDA path")
-                if param.dtype != torch.float32:
+                if param.dtype is not f32:
                     raise RuntimeError(f"CRESSO5 B200 path supports float32 parameters (got {param.dtype})")
                 if not param.is_contiguous():
                     raise RuntimeError("CRESSO5 B200 path updates parameters in place and needs them contiguous")
-                if grad.dtype != param.dtype or grad.device != param.device:
+                if grad.dtype is not f32 or grad.device != param.device:
                     raise RuntimeError("CRESSO5: grad must match its parameter's dtype and device")
                 if not grad.is_contiguous():
                     grad = grad.contiguous()
                 state = self.state[param]
-                if self._use_spectral_route(param, group):
+                rkey = (param.shape, getattr(param, "_cresso_shard", None), route_sig)
+                spectral_route = self._route_cache.get(rkey)
+                if spectral_route is None:
+                    spectral_route = self._route_cache[rkey] = self._use_spectral_route(param, group)
+                if spectral_route:
                     if len(state) == 0:
                         self._init_spectral(param, group, torch.float32, self._geometry(param)[0])
                     state["step"] += 1
@@ -443,23 +455,35 @@ class CRESSO5(Optimizer):
     def _run_scalar(self, hp: np.ndarray, device, items: list) -> None:
         L = _lib.lib()
         F = _lib.DESC_INDEX
-        descs = _lib.new_descs(len(items))
-        for i, (p, g, st) in enumerate(items):
-            d = descs[i]
-            d[F["ndim"]] = p.ndim
-            for a, s in enumerate(p.shape):
-                d[F["shape0"] + a] = int(s)
-            d[F["step"]] = int(st["step"])
-            d[F["param"]] = p.data_ptr()
-            d[F["grad"]] = g.data_ptr()
-            for name in ("force_rms", "drive_energy", "surprise", "action", "q", "impulse", "metric_q",
-                         "metric_impulse"):
-                d[F[name]] = st[name].data_ptr()
         n = len(items)
-        nbytes = np.zeros(1, dtype=np.int64)
-        _lib.check(L.cresso_scalar_scratch_bytes(_lib.ptr(descs), n, nbytes.ctypes.data_as(_lib._pi64)),
-                   "scalar_scratch_bytes")
-        scratch = self._scratch_buffer(device, "scalar", int(nbytes[0]))
+        # the descriptor table depends on the parameters, their storage and their state
+        # tensors; reuse it while those stay the same and refresh the gradient pointers and
+        # step counters, which change from step to step
+        ident = tuple((id(p), p.data_ptr(), p.shape, id(st)) for p, g, st in items)
+        cached = self._scalar_descs.get(device)
+        if cached is not None and cached[0] == ident:
+            descs, nbytes = cached[1], cached[2]
+        else:
+            descs = _lib.new_descs(n)
+            for i, (p, g, st) in enumerate(items):
+                d = descs[i]
+                d[F["ndim"]] = p.ndim
+                for a, s in enumerate(p.shape):
+                    d[F["shape0"] + a] = int(s)
+                d[F["param"]] = p.data_ptr()
+                for name in ("force_rms", "drive_energy", "surprise", "action", "q", "impulse", "metric_q",
+                             "metric_impulse"):
+                    d[F[name]] = st[name].data_ptr()
+            descs[:, F["grad"]] = [g.data_ptr() for _, g, _ in items]
+            descs[:, F["step"]] = [int(st["step"]) for _, _, st in items]
+            nb = np.zeros(1, dtype=np.int64)
+            _lib.check(L.cresso_scalar_scratch_bytes(_lib.ptr(descs), n, nb.ctypes.data_as(_lib._pi64)),
+                       "scalar_scratch_bytes")
+            nbytes = int(nb[0])
+            self._scalar_descs[device] = (ident, descs, nbytes)
+        descs[:, F["grad"]] = [g.data_ptr() for _, g, _ in items]
+        descs[:, F["step"]] = [st["step"] for _, _, st in items]
+        scratch = self._scratch_buffer(device, "scalar", nbytes)
         stream = torch.cuda.current_stream(device).cuda_stream
         _lib.check(L.cresso_scalar_run(_lib.ptr(descs), n, _lib.ptr(hp), _lib.ptr(scratch), scratch.numel(), stream),
                    "scalar_run")
