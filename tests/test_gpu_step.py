@@ -194,6 +194,50 @@ def test_tensor_core_path_variants(variant):
                   upd_tol=5e-4)
 
 
+SCALAR_VARIANTS = {
+    "defaults": dict(),
+    "wd_maximize_local": dict(weight_decay=0.01, maximize=True, local_sharpness=0.5),
+    "power_no_instant": dict(instant_metric_power=0.7, energy_power=1.5, instant_metric_coupling=0.0),
+}
+
+
+@pytest.mark.parametrize("variant", list(SCALAR_VARIANTS.keys()))
+def test_scalar_route_cluster_shapes(variant):
+    """Scalar-route group mixing the cluster form (ragged row slices, an odd-width
+    wide tensor, 1-D, 0-d) with tensors it does not hold (a thin tensor too long
+    for one cluster, a 3-D tensor), which take the one-block-per-tensor kernel."""
+    steps = 3
+    shapes = [(4099, 16), (16, 4097), (32000, 16), (300,), (), (4, 5, 6), (24, 40)]
+    kw = dict(lr=2e-3, rank=4, hash_bins=64, hash_tables=2)
+    kw.update(SCALAR_VARIANTS[variant])
+    g = torch.Generator().manual_seed(21)
+    inits = [torch.randn(s, generator=g) * 0.01 for s in shapes]
+    grads = [[torch.randn(s, generator=g) * 1e-3 for s in shapes] for _ in range(steps)]
+    dev = torch.device("cuda")
+    ps = [torch.nn.Parameter(x.clone().to(dev)) for x in inits]
+    opt = cresso_b200.CRESSO5(ps, cuda_ops="required", **kw)
+    r32 = [torch.nn.Parameter(x.clone()) for x in inits]
+    ref32 = O.OracleCRESSO5(r32, **kw)
+    r64 = [torch.nn.Parameter(x.clone().double()) for x in inits]
+    ref64 = O.OracleCRESSO5(r64, **kw)
+    for gs in grads:
+        for p, a, b, gr in zip(ps, r32, r64, gs):
+            p.grad = gr.to(dev)
+            a.grad = gr.clone()
+            b.grad = gr.double()
+        opt.step()
+        ref32.step()
+        ref64.step()
+    torch.cuda.synchronize()
+    for i, (p, a, b, x0) in enumerate(zip(ps, r32, r64, inits)):
+        assert "q" in opt.state[p] and "freqs" not in opt.state[p]  # scalar route
+        st = {k: (v.cpu() if torch.is_tensor(v) else v) for k, v in opt.state[p].items()}
+        st32 = {k: (v if torch.is_tensor(v) else v) for k, v in ref32.state[a].items()}
+        st64 = {k: (v if torch.is_tensor(v) else v) for k, v in ref64.state[b].items()}
+        check_against(f"scalar[{variant}][{shapes[i]}]", x0, p.detach().cpu(), st, a.detach(), st32, b.detach(), st64,
+                      upd_tol=5e-4)
+
+
 def test_run_to_run_deterministic():
     shapes, kw, inits, grads = _bench_inputs("c1", 3)
     outs = []
