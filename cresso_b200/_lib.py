@@ -42,8 +42,9 @@ DESC_FIELDS = (
     + ["row0", "rows", "col0", "cols", "step", "param", "grad", "shape_ws", "hash_cache", "hash_cache_n",
        "omega", "q_cos", "q_sin", "p_cos", "p_sin", "metric_cos", "metric_sin", "metric_p_cos", "metric_p_sin",
        "calcium_cos", "calcium_sin", "mode_confidence", "hash_energy", "hash_impulse", "hash_refractory",
-       "force_rms", "drive_energy", "surprise", "action", "q", "impulse", "metric_q", "metric_impulse"]
+       "force_rms", "drive_energy", "surprise", "action", "q", "impulse", "metric_q", "metric_impulse", "dtype"]
 )
+DTYPE_CODES = {"float32": 0, "float16": 1, "bfloat16": 2}
 DESC_INDEX = {name: i for i, name in enumerate(DESC_FIELDS)}
 DESC_WORDS = len(DESC_FIELDS)
 

@@ -9,6 +9,8 @@
 //    memory;
 //  * scalar_route_kernel (the rest, e.g. N-d tensors): one 256-thread block
 //    per tensor, re-reading the gradient between the stages.
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <math.h>
 #include <stdint.h>
@@ -28,15 +30,49 @@ struct ScalTensor {
     int64_t ndim, N, rows, cols, step;
     int64_t dims[CRESSO_MAX_NDIM];
     int32_t TC, RPI, n_ct, nw;
-    float* param;
-    const float* grad;
+    float* param;       // element type `dtype` (CRESSO_DTYPE_*)
+    const float* grad;  // element type `dtype`
     float *q, *impulse, *metric_q, *metric_impulse, *force_rms, *drive_energy, *surprise, *action;
     float* work;  // per-tensor float scratch (row partials, row / column factors, N-d marginals)
     // cluster form: slices are row ranges (split_rows) or column ranges of `chunk` rows /
     // columns; ctc / crpi are the thread mapping of one slice
     int64_t chunk;
-    int32_t split_rows, ctc, crpi, pad1;
+    int32_t split_rows, ctc, crpi, dtype;
 };
+
+// Element e of a parameter / gradient of type dt (float32 work, cresso_v5.py:119-124).
+// -lr rounded (once, from double) to the parameter type dt; float32: -lr.
+__device__ __forceinline__ float neg_lr_in(double lr, int dt) {
+    if (dt == CRESSO_DTYPE_F16) return __half2float(__double2half(-lr));
+    if (dt == CRESSO_DTYPE_BF16) return __bfloat162float(__double2bfloat16(-lr));
+    return (float)(-lr);
+}
+
+__device__ __forceinline__ float load_elem(const void* p, int64_t e, int dt) {
+    if (dt == CRESSO_DTYPE_F16) return __half2float(reinterpret_cast<const __half*>(p)[e]);
+    if (dt == CRESSO_DTYPE_BF16) return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p)[e]);
+    return __ldg(reinterpret_cast<const float*>(p) + e);
+}
+// param.add_(update.to(param.dtype), alpha=-lr)  (cresso_v5.py:1582).  float32:
+// p + (-lr) u.  16-bit: round(p + round(-lr) round(u)), every rounding to the
+// parameter's type, as PyTorch's vectorised CPU kernel computes it (alpha
+// converted to the tensor's type, the sum formed in float32); neg_lr16 is
+// -lr rounded to that type.
+__device__ __forceinline__ void apply_update(void* p, int64_t e, int dt, float neg_lr, float neg_lr16,
+                                             float update) {
+    if (dt == CRESSO_DTYPE_F16) {
+        __half* h = reinterpret_cast<__half*>(p);
+        const float u = __half2float(__float2half_rn(update));
+        h[e] = __float2half_rn(__half2float(h[e]) + neg_lr16 * u);
+    } else if (dt == CRESSO_DTYPE_BF16) {
+        __nv_bfloat16* h = reinterpret_cast<__nv_bfloat16*>(p);
+        const float u = __bfloat162float(__float2bfloat16_rn(update));
+        h[e] = __float2bfloat16_rn(__bfloat162float(h[e]) + neg_lr16 * u);
+    } else {
+        float* f = reinterpret_cast<float*>(p);
+        f[e] = f[e] + neg_lr * update;
+    }
+}
 
 struct ScalHdr {
     int64_t n;
@@ -115,8 +151,8 @@ __global__ void __launch_bounds__(kThreads) scalar_route_kernel(const ScalHdr* _
     const bool wd_on = hp[S_WD] != 0.0;
     const double N = (double)D.N;
     auto force = [&](int64_t e) {
-        float f = sgn * __ldg(D.grad + e);
-        if (wd_on) f = f + wd * D.param[e];
+        float f = sgn * load_elem(D.grad, e, D.dtype);
+        if (wd_on) f = f + wd * load_elem(D.param, e, D.dtype);
         return f;
     };
 
@@ -414,11 +450,12 @@ __global__ void __launch_bounds__(kThreads) scalar_route_kernel(const ScalHdr* _
     {
         const float cu = sh.c_u, cr = sh.c_root, ctt = sh.c_t, cp = sh.c_pred, cn = sh.c_nov, gain = sh.gain;
         const float neg_lr = (float)(-hp[S_LR]);
+        const float neg_lr16 = neg_lr_in(hp[S_LR], D.dtype);
         walk_elems(D, [&](int64_t e, int64_t r, int64_t c, int, bool valid) {
             if (valid) {
                 const Parts P = parts(e, r, c);
                 const float drive = cu * P.u + cr * P.root + ctt * P.t + cp * qn + cn * P.nov;
-                D.param[e] = D.param[e] + neg_lr * (drive * gain);
+                apply_update(D.param, e, D.dtype, neg_lr, neg_lr16, drive * gain);
             }
         });
     }
@@ -492,6 +529,7 @@ __global__ void __launch_bounds__(kThreads, 4) scalar_cluster_kernel(const ScalH
     const int64_t cols = D.cols;
     const float* __restrict__ grad = D.grad;
     float* __restrict__ param = D.param;
+    const int dt = D.dtype;
 
     // slice geometry
     const bool sr = D.split_rows != 0;
@@ -538,8 +576,8 @@ __global__ void __launch_bounds__(kThreads, 4) scalar_cluster_kernel(const ScalH
         // float partials over this thread's elements (at most kClSlice / kThreads), float64 above
         float a0 = 0.0f;
         for_slice([&](int64_t, int64_t, int64_t q, int64_t e) {
-            float f = sgn * __ldg(grad + e);
-            if (wd_on) f = f + wd * param[e];
+            float f = sgn * (dt == CRESSO_DTYPE_F32 ? __ldg(grad + e) : load_elem(grad, e, dt));
+            if (wd_on) f = f + wd * (dt == CRESSO_DTYPE_F32 ? param[e] : load_elem(param, e, dt));
             F[q] = f;
             a0 = fmaf(f, f, a0);
         });
@@ -781,10 +819,14 @@ __global__ void __launch_bounds__(kThreads, 4) scalar_cluster_kernel(const ScalH
     {
         const float cu = sh.c_u, cr = sh.c_root, ctt = sh.c_t, cp = sh.c_pred, cn = sh.c_nov, gain = sh.gain;
         const float neg_lr = (float)(-hp[S_LR]);
+        const float neg_lr16 = neg_lr_in(hp[S_LR], D.dtype);
         for_slice([&](int64_t, int64_t, int64_t q, int64_t e) {
             const Parts P = parts(F[q]);
             const float drive = cu * P.u + cr * P.root + ctt * P.t + cp * qn + cn * P.nov;
-            param[e] = param[e] + neg_lr * (drive * gain);
+            if (dt == CRESSO_DTYPE_F32)
+                param[e] = param[e] + neg_lr * (drive * gain);
+            else
+                apply_update(param, e, dt, neg_lr, neg_lr16, drive * gain);
         });
     }
 }
@@ -821,6 +863,9 @@ static int scal_layout(const cresso_tensor_desc* descs, int64_t n, std::vector<S
     if (out) out->assign(n, ScalTensor{});
     for (int64_t i = 0; i < n; ++i) {
         const cresso_tensor_desc& d = descs[i];
+        CRESSO_REQUIRE(d.dtype == CRESSO_DTYPE_F32 || d.dtype == CRESSO_DTYPE_F16 || d.dtype == CRESSO_DTYPE_BF16,
+                       CRESSO_EUNSUPPORTED, "tensor %lld: dtype code %lld (float32, float16 and bfloat16 are supported)",
+                       (long long)i, (long long)d.dtype);
         CRESSO_REQUIRE(d.ndim >= 0 && d.ndim <= CRESSO_MAX_NDIM, CRESSO_EUNSUPPORTED,
                        "tensor %lld: ndim %lld outside [0, %d]", (long long)i, (long long)d.ndim, CRESSO_MAX_NDIM);
         for (int64_t a = 0; a < d.ndim; ++a)
@@ -846,6 +891,7 @@ static int scal_layout(const cresso_tensor_desc* descs, int64_t n, std::vector<S
             S.nw = nw;
             S.param = (float*)d.param;
             S.grad = (const float*)d.grad;
+            S.dtype = (int32_t)d.dtype;
             S.q = (float*)d.q;
             S.impulse = (float*)d.impulse;
             S.metric_q = (float*)d.metric_q;

@@ -18,6 +18,8 @@
 // per tensor) updates the persistent rank / hash / scalar state and writes
 // the per-tensor constants the next pass needs.  No host synchronisation.
 
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <math.h>
 #include <stdint.h>
@@ -48,6 +50,8 @@ enum : int32_t {
     F_INST1D = 128,
     F_IPOW1 = 256,  // instant_metric_power == 1 (density = rel)
     F_VEC = 512,    // rows 16-byte aligned: streaming tiles are staged with cp.async
+    F_F16 = 1024,   // float16 parameter and gradient (float32 copies in the scratch)
+    F_BF16 = 2048,  // bfloat16 parameter and gradient (float32 copies in the scratch)
 };
 
 struct TensorConsts {
@@ -81,9 +85,11 @@ struct DevTensor {
     int64_t item_base, n_items, step, hidx_n;  // item_base: first item in the class's item list
     int32_t ndim, R, TC, RPI, RB, n_ct, n_bands, flags;
     int32_t cfirst[6], recbase[6], nrec[6], pad0;
-    float* param;
-    const float* grad;
+    float* param;   // float32 parameter (the caller's, or the scratch copy of a 16-bit one)
+    const float* grad;  // float32 gradient (the caller's, or the scratch copy in tbuf)
     float* tbuf;
+    void* param_h;  // the caller's 16-bit parameter and gradient (F_F16 / F_BF16)
+    const void* grad_h;
     const float* rowtab;
     const float* coltab;
     const ModeStats* stats;
@@ -422,6 +428,7 @@ spectral_pass_kernel(const GroupHdr* __restrict__ hdr, const DevTensor* __restri
         float scale = 0.f, inv_scale = 0.f, inst_k = 0.f, inst_gm = 1.f;
         DriveK dk{};
         float c_u = 0.f, c_root = 0.f, c_t = 0.f, c_nov = 0.f, c_hp = 0.f, gain = 0.f, neg_lr = 0.f;
+        float upd_a = 1.f, upd_b = 0.f;
         if constexpr (PASS >= 2 && PASS <= 3) {
             scale = Cp->scale;
             inv_scale = Cp->inv_scale;
@@ -439,6 +446,9 @@ spectral_pass_kernel(const GroupHdr* __restrict__ hdr, const DevTensor* __restri
             c_hp = Cp->c_hp;
             gain = Cp->gain;
             neg_lr = Cp->neg_lr;
+            const bool half = (flags & (F_F16 | F_BF16)) != 0;
+            upd_a = half ? 0.0f : 1.0f;
+            upd_b = half ? 1.0f : neg_lr;
         }
         // reconstruction coefficients of this pass into shared memory
         if constexpr (PASS >= 3) {
@@ -857,7 +867,9 @@ spectral_pass_kernel(const GroupHdr* __restrict__ hdr, const DevTensor* __restri
                         }
                         const DriveParts dp = drive_parts(t, pred, dk);
                         const float drive = c_u * dp.u + c_root * dp.root + c_t * t + comb + c_nov * dp.nov + c_hp * hpv;
-                        param[(int64_t)r * cols32 + col] = pb[o] + neg_lr * (drive * gain);
+                        // float32: p + (-lr) update; 16-bit: the update itself, applied to
+                        // the caller's tensor by half_convert_kernel<false>
+                        param[(int64_t)r * cols32 + col] = fmaf(upd_b, drive * gain, upd_a * pb[o]);
                     }
                 }
                 if constexpr (PASS == 2) {
@@ -1441,6 +1453,7 @@ struct Plan {
     int64_t off_hdr, off_dts, off_items, off_tmap, off_cst, off_htab, off_rowf, off_colf, off_rowpart, off_colpart;
     int64_t off_recs, off_recb, off_red[5], len_red[5], off_tbuf, bytes;
     int64_t n_rec_max;
+    int64_t off_p32, half_elems;  // float32 copies of the 16-bit parameters
     int rm;
 };
 
@@ -1490,6 +1503,9 @@ static int build_plan(const cresso_tensor_desc* descs, int64_t n, const cresso_h
         CRESSO_REQUIRE(d.ndim == 1 || d.ndim == 2, CRESSO_EUNSUPPORTED,
                        "tensor %lld: spectral route supports 1-D and 2-D tensors on the CUDA path (ndim=%lld)",
                        (long long)i, (long long)d.ndim);
+        CRESSO_REQUIRE(d.dtype == CRESSO_DTYPE_F32 || d.dtype == CRESSO_DTYPE_F16 || d.dtype == CRESSO_DTYPE_BF16,
+                       CRESSO_EUNSUPPORTED, "tensor %lld: dtype code %lld (float32, float16 and bfloat16 are supported)",
+                       (long long)i, (long long)d.dtype);
         CRESSO_REQUIRE(d.param && d.grad && d.shape_ws, CRESSO_EINVAL, "tensor %lld: NULL param / grad / workspace",
                        (long long)i);
         CRESSO_REQUIRE(d.rows >= 1 && d.cols >= 1 && d.row0 >= 0 && d.col0 >= 0, CRESSO_EINVAL,
@@ -1514,7 +1530,8 @@ static int build_plan(const cresso_tensor_desc* descs, int64_t n, const cresso_h
         const int64_t gcols = d.ndim == 2 ? d.shape[1] : d.shape[0];
         const int64_t ib = bins <= 256 ? 1 : 2;
         bool ok = d.cols >= 16 && d.cols % 16 == 0 && d.col0 % 16 == 0 && (d.ndim == 1 || gcols % 16 == 0);
-        ok = ok && d.param % 16 == 0 && d.grad % 16 == 0;
+        // 16-bit tensors are read through 256-byte aligned float32 copies in the scratch
+        ok = ok && (d.dtype != CRESSO_DTYPE_F32 || (d.param % 16 == 0 && d.grad % 16 == 0));
         if (d.hash_cache) ok = ok && d.hash_cache % 16 == 0 && (d.hash_cache_n * ib) % 16 == 0;
         vec[i] = ok;
     }
@@ -1586,6 +1603,13 @@ static int build_plan(const cresso_tensor_desc* descs, int64_t n, const cresso_h
         D.hidx_n = d.hash_cache_n;
         D.param = (float*)d.param;
         D.grad = (const float*)d.grad;
+        D.param_h = nullptr;
+        D.grad_h = nullptr;
+        if (d.dtype != CRESSO_DTYPE_F32) {  // rebound to the float32 copies by bind_scratch
+            D.param_h = (void*)d.param;
+            D.grad_h = (const void*)d.grad;
+            D.flags |= d.dtype == CRESSO_DTYPE_F16 ? F_F16 : F_BF16;
+        }
         D.omega = (float*)d.omega;
         D.q_cos = (float*)d.q_cos;
         D.q_sin = (float*)d.q_sin;
@@ -1685,12 +1709,16 @@ static int build_plan(const cresso_tensor_desc* descs, int64_t n, const cresso_h
         P.off_red[p] = take(off, 8 * len);
     }
     P.off_tbuf = take(off, 4 * elems);
+    P.half_elems = 0;
+    for (auto& D : P.dts)
+        if (D.flags & (F_F16 | F_BF16)) P.half_elems += align_up(D.rows * D.cols, 64);
+    P.off_p32 = take(off, 4 * std::max<int64_t>(P.half_elems, 1));
     P.bytes = off;
     return CRESSO_OK;
 }
 
 static void bind_scratch(Plan& P, char* base) {
-    int64_t rows_o = 0, cols_o = 0, rowpart_o = 0, colpart_o = 0, elem_o = 0, red_o[5] = {0, 0, 0, 0, 0};
+    int64_t rows_o = 0, cols_o = 0, rowpart_o = 0, colpart_o = 0, elem_o = 0, red_o[5] = {0, 0, 0, 0, 0}, p32_o = 0;
     const int64_t tbs = std::max<int64_t>(P.hdr.tb, 1);
     for (size_t i = 0; i < P.dts.size(); ++i) {
         DevTensor& D = P.dts[i];
@@ -1701,6 +1729,11 @@ static void bind_scratch(Plan& P, char* base) {
         D.rowpart = reinterpret_cast<float*>(base + P.off_rowpart) + rowpart_o;
         D.colpart = reinterpret_cast<float*>(base + P.off_colpart) + colpart_o;
         D.tbuf = reinterpret_cast<float*>(base + P.off_tbuf) + elem_o;
+        if (D.flags & (F_F16 | F_BF16)) {
+            D.param = reinterpret_cast<float*>(base + P.off_p32) + p32_o;
+            D.grad = D.tbuf;
+            p32_o += align_up(D.rows * D.cols, 64);
+        }
         for (int p = 1; p <= 4; ++p) {
             D.red[p] = reinterpret_cast<double*>(base + P.off_red[p]) + red_o[p];
             red_o[p] += red_len(p, P.rm, P.hdr.tb, D.cols, D.ndim);
@@ -1735,6 +1768,56 @@ static size_t pass_smem(int pass, const GroupHdr& H, int64_t iters, bool tc) {
         b = std::max<size_t>(b, 78 * 1024);
     }
     return b;
+}
+
+// 16-bit tensors: float32 copies of the gradient (into the tangent buffer, which
+// P3 overwrites element by element after reading it) and of the parameter
+// before P1.  After P5, whose output for these tensors is the update u, the
+// caller's parameter becomes round(p + round(-lr) round(u)), every rounding to
+// its type: param.add_(update.to(param.dtype), alpha=-lr) (cresso_v5.py:1353)
+// as PyTorch's vectorised CPU kernel computes it, with alpha converted to the
+// tensor's type and the sum formed in float32.
+template <bool IN>
+__global__ void half_convert_kernel(const DevTensor* __restrict__ dts, int n, double neg_lr) {
+    for (int k = blockIdx.y; k < n; k += gridDim.y) {
+        const DevTensor& D = dts[k];
+        const int fl = D.flags;
+        if (!(fl & (F_F16 | F_BF16))) continue;
+        const bool bf = (fl & F_BF16) != 0;
+        const int64_t N = D.rows * D.cols;
+        for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < N; e += (int64_t)gridDim.x * blockDim.x) {
+            if (IN) {
+                if (bf) {
+                    D.tbuf[e] = __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(D.grad_h)[e]);
+                    D.param[e] = __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(D.param_h)[e]);
+                } else {
+                    D.tbuf[e] = __half2float(reinterpret_cast<const __half*>(D.grad_h)[e]);
+                    D.param[e] = __half2float(reinterpret_cast<const __half*>(D.param_h)[e]);
+                }
+            } else if (bf) {
+                __nv_bfloat16* ph = reinterpret_cast<__nv_bfloat16*>(D.param_h);
+                const float a = __bfloat162float(__double2bfloat16(neg_lr));
+                const float u = __bfloat162float(__float2bfloat16_rn(D.param[e]));
+                ph[e] = __float2bfloat16_rn(__bfloat162float(ph[e]) + a * u);
+            } else {
+                __half* ph = reinterpret_cast<__half*>(D.param_h);
+                const float a = __half2float(__double2half(neg_lr));
+                const float u = __half2float(__float2half_rn(D.param[e]));
+                ph[e] = __float2half_rn(__half2float(ph[e]) + a * u);
+            }
+        }
+    }
+}
+
+template <bool IN>
+static int launch_half_convert(const Plan& P, char* base, cudaStream_t s) {
+    if (P.half_elems == 0) return CRESSO_OK;
+    const DevTensor* dts = reinterpret_cast<const DevTensor*>(base + P.off_dts);
+    const int n = (int)P.hdr.n_tensors;
+    dim3 grid(256, (unsigned)std::min(n, 65535));
+    half_convert_kernel<IN><<<grid, kThreads, 0, s>>>(dts, n, -P.hdr.hp[H_LR]);
+    CRESSO_LAUNCHED("half_convert_kernel");
+    return CRESSO_OK;
 }
 
 template <int RM, int NT>
@@ -1797,8 +1880,13 @@ static int launch_stage(int stage, const Plan& P, char* base, cudaStream_t s) {
             finalize4_kernel<RM><<<n, kThreads, 0, s>>>(hdr, dts);
             CRESSO_LAUNCHED("finalize4_kernel");
             return CRESSO_OK;
-        case 13: return run_pass(spectral_pass_kernel<5, RM, NT, true, RM == 8>, spectral_pass_kernel<5, RM, NT, true, false>,
-                            spectral_pass_kernel<5, RM, NT, false, false>, 5);
+        case 13: {
+            const int st = run_pass(spectral_pass_kernel<5, RM, NT, true, RM == 8>,
+                                    spectral_pass_kernel<5, RM, NT, true, false>,
+                                    spectral_pass_kernel<5, RM, NT, false, false>, 5);
+            if (st) return st;
+            return launch_half_convert<false>(P, base, s);
+        }
         default: return CRESSO_OK;
     }
 }
@@ -1851,6 +1939,8 @@ int cresso_spectral_run(const cresso_tensor_desc* descs, int64_t n, const cresso
                                     cudaMemcpyHostToDevice, s));
         CRESSO_CUDA(cudaMemcpyAsync(base + P.off_tmap, P.tensor_lists.data(), sizeof(int32_t) * n,
                                     cudaMemcpyHostToDevice, s));
+        const int hs = launch_half_convert<true>(P, base, s);
+        if (hs) return hs;
     }
     for (int64_t stage = std::max<int64_t>(stage_begin, 1); stage < stage_end; ++stage) {
         const int nt = P.hdr.tables == 1 ? 1 : (P.hdr.tables == 2 ? 2 : 0);

@@ -39,6 +39,10 @@ from ._host import (
 
 __all__ = ["CRESSO5", "CRESSO", "count_optimizer_state_elements", "theoretical_state_elements"]
 
+# parameter element types of the CUDA path and their descriptor codes; the work and the
+# state are float32 for all three (cresso_v5.py:119-124)
+_DTYPES = {torch.float32: 0, torch.float16: 1, torch.bfloat16: 2}
+
 _SPECTRAL_RANK_STATE = ("q_cos", "q_sin", "p_cos", "p_sin", "metric_cos", "metric_sin", "metric_p_cos",
                         "metric_p_sin", "calcium_cos", "calcium_sin", "mode_confidence")
 
@@ -339,7 +343,6 @@ class CRESSO5(Optimizer):
             route_sig = (group["min_spectral_size"], group["rank"], group.get("thin_matrix_route", "scalar"),
                          group.get("thin_matrix_max_width", 64), group.get("thin_matrix_min_aspect", 4.0))
             micro = int(group.get("micro_field_max_size", 0))
-            f32 = torch.float32
             for param in group["params"]:
                 grad = param.grad  # step() runs under no_grad: no detach needed
                 if grad is None or not torch.is_floating_point(param):
@@ -352,11 +355,12 @@ class CRESSO5(Optimizer):
                 if micro > 0 and param.ndim > 0 and param.numel() <= micro:
                     raise RuntimeError("CRESSO5 micro-field route (micro_field_max_size > 0) is not available on "
                                        "the B200 CUDA path")
-                if param.dtype is not f32:
-                    raise RuntimeError(f"CRESSO5 B200 path supports float32 parameters (got {param.dtype})")
+                if param.dtype not in _DTYPES:
+                    raise RuntimeError("CRESSO5 B200 path supports float32, float16 and bfloat16 parameters "
+                                       f"(got {param.dtype})")
                 if not param.is_contiguous():
                     raise RuntimeError("CRESSO5 B200 path updates parameters in place and needs them contiguous")
-                if grad.dtype is not f32 or grad.device != param.device:
+                if grad.dtype is not param.dtype or grad.device != param.device:
                     raise RuntimeError("CRESSO5: grad must match its parameter's dtype and device")
                 if not grad.is_contiguous():
                     grad = grad.contiguous()
@@ -406,6 +410,7 @@ class CRESSO5(Optimizer):
             d[F["step"]] = int(st["step"])
             d[F["param"]] = p.data_ptr()
             d[F["grad"]] = g.data_ptr()
+            d[F["dtype"]] = _DTYPES[p.dtype]
             d[F["shape_ws"]] = self._workspace(device, shape, group, st["freqs"]).data_ptr()
             if "hash_energy" in st and bins > 0 and hard_enabled(shape, group):
                 buf, cap = self._hash_index_cache(device, bins, tables, numel)
@@ -471,6 +476,7 @@ class CRESSO5(Optimizer):
                 for a, s in enumerate(p.shape):
                     d[F["shape0"] + a] = int(s)
                 d[F["param"]] = p.data_ptr()
+                d[F["dtype"]] = _DTYPES[p.dtype]
                 for name in ("force_rms", "drive_energy", "surprise", "action", "q", "impulse", "metric_q",
                              "metric_impulse"):
                     d[F[name]] = st[name].data_ptr()

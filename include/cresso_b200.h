@@ -72,7 +72,7 @@ typedef struct cresso_tensor_desc {
     int64_t shape[CRESSO_MAX_NDIM];
     int64_t row0, rows, col0, cols;
     int64_t step; /* state["step"] after the increment of this step (1-based) */
-    uint64_t param, grad;           /* float32, contiguous, local block            */
+    uint64_t param, grad;           /* dtype below, contiguous, local block        */
     uint64_t shape_ws;              /* cresso_shape_workspace_init() output       */
     uint64_t hash_cache;            /* cresso_hash_cache_init() output or 0        */
     int64_t hash_cache_n;           /* flat indices covered by hash_cache          */
@@ -83,7 +83,14 @@ typedef struct cresso_tensor_desc {
     uint64_t force_rms, drive_energy, surprise, action;
     /* scalar route 0-d state (float32): */
     uint64_t q, impulse, metric_q, metric_impulse;
+    /* element type of param and grad (CRESSO_DTYPE_*); the work and the state are
+     * float32 for all three, and a float16 / bfloat16 parameter receives the
+     * update rounded to its type first, as param.add_(update.to(param.dtype))
+     * does (cresso_v5.py:119-124, 1353, 1582) */
+    int64_t dtype;
 } cresso_tensor_desc;
+
+enum { CRESSO_DTYPE_F32 = 0, CRESSO_DTYPE_F16 = 1, CRESSO_DTYPE_BF16 = 2 };
 
 /* ---------------------------------------------------------------- info --- */
 

@@ -19,3 +19,11 @@ def golden():
 
     with np.load(ROOT / "tests" / "golden" / "golden_small.npz") as z:
         return {k: z[k] for k in z.files}
+
+
+@pytest.fixture(scope="session")
+def golden_half():
+    import numpy as np
+
+    with np.load(ROOT / "tests" / "golden" / "golden_half.npz") as z:
+        return {k: z[k] for k in z.files}

@@ -1,6 +1,6 @@
 """Generate golden vectors for the CRESSO5 step by running the reference itself.
 
-Usage:  python tests/golden/make_golden.py [path-to-reference-checkout]
+Usage:  python tests/golden/make_golden.py [path-to-reference-checkout] [--half-only]
 
 The reference (win10ogod/cresso, ``cresso_v5.py``) is imported from the given
 checkout and run on CPU with ``cuda_ops='off'`` and one thread, which is its
@@ -9,6 +9,9 @@ PyTorch path.  Outputs are written next to this script:
 * ``golden_small.npz`` - frequency packs, hash indices, hash bin counts at the
   benchmark sizes, basis projections / reconstructions, instant metrics and
   full optimizer steps (inputs, final params, every state tensor).
+* ``golden_half.npz`` - full optimizer steps with float16 / bfloat16
+  parameters (``HALF_CASES``; values stored as float32, which holds every
+  16-bit value exactly).  ``--half-only`` regenerates just this file.
 
 The reference is not available where the tests run, so the vectors are
 committed; the tests only read the ``.npz``.
@@ -67,24 +70,41 @@ STEP_CASES = {
 }
 
 
-def run_steps(ref, shape, kwargs, steps, seed, init_std, grad_std):
+# float16 / bfloat16 parameter cases: name -> (shape, kwargs, steps, seed, init_std, grad_std, dtype).
+# The first four are the shapes and settings of the reference's own 16-bit tests
+# (tests/test_cresso_v5_cuda_ops.py:109-146, 213-250).
+_REF_SPEC16 = dict(lr=1.0e-3, rank=8, max_frequency=5, min_spectral_size=1, hard_channel_min_size=1,
+                   thin_matrix_hard_cutoff=0, hash_bins=37, hash_tables=2, basis_cache_limit_elements=0)
+_REF_SCAL16 = dict(lr=1.0e-3, rank=4, thin_matrix_route="scalar", thin_matrix_max_width=64, min_spectral_size=1)
+HALF_CASES = {
+    "spec16_31x37_f16": ((31, 37), _REF_SPEC16, 2, 8642, 0.05, 0.05, "float16"),
+    "spec16_31x37_bf16": ((31, 37), _REF_SPEC16, 2, 8643, 0.05, 0.05, "bfloat16"),
+    "scal16_64x16_f16": ((64, 16), _REF_SCAL16, 2, 3579, 0.05, 0.05, "float16"),
+    "scal16_64x16_bf16": ((64, 16), _REF_SCAL16, 2, 3580, 0.05, 0.05, "bfloat16"),
+    "spec16_256x256_bf16_wd": ((256, 256), dict(rank=8, hash_bins=64, hash_tables=2, weight_decay=0.01),
+                               3, 31, 0.02, 1e-3, "bfloat16"),
+    "scal16_16x4096_f16": ((16, 4096), dict(rank=4, hash_bins=64, hash_tables=2), 3, 32, 0.01, 1e-3, "float16"),
+}
+
+
+def run_steps(ref, shape, kwargs, steps, seed, init_std, grad_std, dtype=torch.float32):
     gen = torch.Generator().manual_seed(seed)
-    init = (torch.randn(shape, generator=gen) * init_std).float()
-    grads = [(torch.randn(shape, generator=gen) * grad_std).float() for _ in range(steps)]
+    init = (torch.randn(shape, generator=gen) * init_std).float().to(dtype)
+    grads = [(torch.randn(shape, generator=gen) * grad_std).float().to(dtype) for _ in range(steps)]
     p = torch.nn.Parameter(init.clone())
     opt = ref.CRESSO5([p], cuda_ops="off", **kwargs)
     for g in grads:
         p.grad = g.clone()
         opt.step()
     st = opt.state[p]
-    out = {"final": p.detach().numpy().copy(),
+    out = {"final": p.detach().float().numpy().copy(),
            "init_sum": np.asarray(init.double().sum().item()),
            "grad_sum": np.asarray(sum(g.double().abs().sum().item() for g in grads))}
     if init.numel() <= 4096:
         # Small inputs are stored; larger ones are regenerated from the seed and
         # checked against the stored sums.
-        out["init"] = init.numpy()
-        out["grads"] = np.stack([g.numpy() for g in grads])
+        out["init"] = init.float().numpy()
+        out["grads"] = np.stack([g.float().numpy() for g in grads])
     for k, v in st.items():
         if torch.is_tensor(v):
             out["state_" + k] = v.detach().cpu().numpy().copy()
@@ -95,9 +115,21 @@ def run_steps(ref, shape, kwargs, steps, seed, init_std, grad_std):
 
 
 def main() -> None:
-    root = Path(sys.argv[1] if len(sys.argv) > 1 else os.environ.get("CRESSO_REFERENCE", "/root/reference"))
+    args = [a for a in sys.argv[1:] if not a.startswith("--")]
+    root = Path(args[0] if args else os.environ.get("CRESSO_REFERENCE", "/root/reference"))
     ref = load_reference(root)
     torch.set_num_threads(1)
+
+    half: dict[str, np.ndarray] = {}
+    for name, (shape, kwargs, steps, seed, istd, gstd, dt) in HALF_CASES.items():
+        out = run_steps(ref, shape, kwargs, steps, seed, istd, gstd, getattr(torch, dt))
+        for k, v in out.items():
+            half[f"step_{name}_{k}"] = v
+    np.savez_compressed(HERE / "golden_half.npz", **half)
+    print("wrote", HERE / "golden_half.npz", len(half), "arrays")
+    if "--half-only" in sys.argv:
+        return
+
     data: dict[str, np.ndarray] = {}
 
     # Frequency packs (cresso_v5.py:145-227).

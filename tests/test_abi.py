@@ -68,6 +68,7 @@ def _fake_desc(shape, rows=None, row0=0):
             d[0, F[name]] = 4096
     d[0, F["hash_cache"]] = 4096
     d[0, F["hash_cache_n"]] = int(np.prod(shape))
+    d[0, F["dtype"]] = 0  # float32
     return d
 
 
