@@ -249,6 +249,8 @@ def b200_arm(args, world, rank, local):
     torch.cuda.set_device(device)
     shapes, kw, istd = workload_shapes(args.workload)
     params, grads_dev = [], []
+    pdt = {"f32": torch.float32, "bf16": torch.bfloat16, "f16": torch.float16}[args.dtype]
+    bpe = 3 * torch.empty((), dtype=pdt).element_size()  # grad read + param read + param write
     gen = torch.Generator(device=device)
     gen.manual_seed(1234 + rank)
     n_local = 0
@@ -260,7 +262,7 @@ def b200_arm(args, world, rank, local):
             start, local_shape = 0, tuple(s)
         p = torch.empty(local_shape, device=device)
         p.normal_(0.0, istd, generator=gen)
-        p = torch.nn.Parameter(p)
+        p = torch.nn.Parameter(p.to(pdt))
         if world > 1:
             mark_row_shard(p, s, start)
         g = torch.empty(local_shape, device=device)
@@ -268,6 +270,7 @@ def b200_arm(args, world, rank, local):
         if args.workload == "c2":  # BASELINE c2: per-row log-normal(0, 0.5) gradient scale
             row_scale = torch.empty((local_shape[0], 1), device=device).normal_(0.0, 1.0, generator=gen)
             g.mul_(torch.exp(0.5 * row_scale))
+        g = g.to(pdt)
         p.grad = g
         params.append(p)
         grads_dev.append(g)
@@ -302,7 +305,7 @@ def b200_arm(args, world, rank, local):
     launches = _lib.launch_count() - launches0
     ms = e0.elapsed_time(e1) / args.steps
     ms = max_over_ranks(ms, world, device)
-    value = BYTES_PER_ELEM * n_total / (ms * 1e-3) / 1e9
+    value = bpe * n_total / (ms * 1e-3) / 1e9
 
     # ---- per-pass kernel times (CUDA events on the launching stream, same steps)
     pass_ms = time_passes(opt, args, world, device, stream)
@@ -321,7 +324,7 @@ def b200_arm(args, world, rank, local):
     # ---- end to end through the public API with host buffers
     e2e = None
     if not args.skip_e2e:
-        e2e = time_e2e(opt, params, grads_dev, args, world, device, stream, n_total)
+        e2e = time_e2e(opt, params, grads_dev, args, world, device, stream, n_total, bpe)
 
     # ---- CPU baseline (rank 0, N = 1)
     cpu = None
@@ -337,13 +340,14 @@ def b200_arm(args, world, rank, local):
             "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": f"{args.workload}: " + ("7B-shaped fp32 set, 290 tensors, 6,738,411,520 elements"
+            "config": {"workload": f"{args.workload}: " + (f"7B-shaped {args.dtype} set, 290 tensors, 6,738,411,520 elements"
                                                             if args.workload == "c5" else str(shapes[0])),
                        "rank": kw["rank"], "hash_bins": kw["hash_bins"], "hash_tables": kw["hash_tables"],
                        "sharding": f"row-sharded over {world} GPU(s)" if world > 1 else "single GPU",
                        "l2": "no flush: inputs of every step (grads + params) exceed the 126 MB L2"
                              if n_total * 8 > 2 * 126e6 else "inputs fit in L2",
-                       "elements": n_total, "per_pass_ms": {k: round(v, 4) for k, v in pass_ms.items()}},
+                       "elements": n_total, "per_pass_ms": {k: round(v, 4) for k, v in pass_ms.items()},
+                       "param_dtype": args.dtype, "bytes_per_element": bpe},
             "roofline": {"bound": "hbm", "kernel": dom, "achieved": achieved, "peak": peaks["hbm_gbs"],
                          "unit": "GB/s", "frac": achieved / peaks["hbm_gbs"], "traffic": traffic,
                          "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
@@ -408,7 +412,7 @@ def time_passes(opt, args, world, device, stream):
     return {k: v / reps for k, v in acc.items() if v > 0.0}
 
 
-def time_e2e(opt, params, grads_dev, args, world, device, stream, n_total):
+def time_e2e(opt, params, grads_dev, args, world, device, stream, n_total, bpe=BYTES_PER_ELEM):
     """Gradients from pinned host memory each step, drive energies read back each step.
 
     The gradients are double-buffered on the device: step k+1's host -> device
@@ -465,7 +469,7 @@ def time_e2e(opt, params, grads_dev, args, world, device, stream, n_total):
     ms = max_over_ranks(e0.elapsed_time(e1) / args.steps, world, device)
     for p, g in zip(params, grads_dev):
         p.grad = g
-    return {"value": BYTES_PER_ELEM * n_total / (ms * 1e-3) / 1e9, "unit": "GB/s", "ms_per_step": ms,
+    return {"value": bpe * n_total / (ms * 1e-3) / 1e9, "unit": "GB/s", "ms_per_step": ms,
             "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": out_host.numel() * 4,
             "overlap": "step k+1's host->device gradient copy runs on a copy stream under step k"}
 
@@ -478,6 +482,8 @@ def main():
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     ap.add_argument("--workload", default="c5")
     ap.add_argument("--skip-e2e", action="store_true")
+    ap.add_argument("--dtype", choices=["f32", "bf16", "f16"], default="f32",
+                    help="parameter / gradient type (work and state are float32 for all)")
     ap.add_argument("--skip-cpu", action="store_true")
     args = ap.parse_args()
     world, rank, local = dist_setup(args)

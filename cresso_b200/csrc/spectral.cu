@@ -68,15 +68,16 @@ struct TensorConsts {
     double pv[2 * kMaxRank];  // old prediction coefficients on the normalised carriers
 };
 
-// The tensors of a group fall in two launch classes: class 0 ("full") holds
-// the tensors whose every item is a full, 16-byte aligned 256-column tile
-// with 8-bit bin indices; class 1 holds the rest.  Each pass runs one launch
-// per non-empty class over that class's item list.
+// The tensors of a group fall in three launch classes: class 0 ("full") holds
+// the float32 tensors whose every item is a full, 16-byte aligned 256-column
+// tile with 8-bit bin indices; class 2 the 16-bit tensors of that form; class
+// 1 the rest.  Each pass runs one launch per non-empty class over that class's
+// item list; only P5 differs between classes 0 and 2.
 struct GroupHdr {
     int64_t n_tensors, n_items, rm, bins, tables, tb, iters, idx_bytes, rb_max;
     int32_t* status;                  // device word: nonzero when a bounded wait gave up
-    int64_t cls_items[2], cls_nt[2];  // items and tensors of each class
-    int64_t grid[2][6];               // blocks of pass 1..5 per class (index 0 unused)
+    int64_t cls_items[3], cls_nt[3];  // items and tensors of each class
+    int64_t grid[3][6];               // blocks of pass 1..5 per class (index 0 unused)
     double hp[64];                    // cresso_hparams
 };
 
@@ -319,11 +320,11 @@ constexpr uint64_t kTcWaitNs = 1000000000ull;  // bound of one MMA wait (1 s)
 // A_hi B_hi + A_hi B_lo + A_lo B_hi, float32-level accuracy.  The products of
 // item i+1 are issued at the start of item i into the other D buffer, so the
 // tensor core runs under the CUDA-core work of the item.
-template <int PASS, int RM, int NT, bool FULL, bool TCR>
+template <int PASS, int RM, int NT, bool FULL, bool TCR, bool H16 = false>
 __global__ void __launch_bounds__(kThreads, PassCfg<PASS, RM>::kMinBlocks)
 spectral_pass_kernel(const GroupHdr* __restrict__ hdr, const DevTensor* __restrict__ dts,
                      const int64_t* __restrict__ item_lists, const int32_t* __restrict__ tensor_lists,
-                     double* __restrict__ rec_scal, float* __restrict__ rec_bins) {
+                     double* __restrict__ rec_scal, float* __restrict__ rec_bins, int cls) {
     static_assert(!TCR || (FULL && RM == 8 && PASS >= 3), "tensor-core reconstruction: class 0, rank pad 8, P3-P5");
     constexpr int NACC = PassCfg<PASS, RM>::kAccDoubles;
     // rows computed together; P3 keeps two on the CUDA-core form (register budget)
@@ -333,11 +334,12 @@ spectral_pass_kernel(const GroupHdr* __restrict__ hdr, const DevTensor* __restri
 
     // group constants, once per block
     // this launch's class: its item list (prefix sums over its tensors) and tensor indices
-    const int cls = FULL ? 0 : 1;
+    // (item_lists / tensor_lists point at this class's lists; H16: P5 of class 2)
+    static_assert(!H16 || (FULL && PASS == 5), "16-bit kernel form: class-2 P5 only");
     const int64_t n_items = hdr->cls_items[cls];
     const int nt = (int)hdr->cls_nt[cls];
-    const int64_t* __restrict__ item_base = item_lists + (FULL ? 0 : hdr->cls_nt[0] + 1);
-    const int32_t* __restrict__ tmap = tensor_lists + (FULL ? 0 : hdr->cls_nt[0]);
+    const int64_t* __restrict__ item_base = item_lists;
+    const int32_t* __restrict__ tmap = tensor_lists;
     const int TB = (int)hdr->tb, B = (int)hdr->bins;
     const int T = NT > 0 ? NT : (int)hdr->tables;  // hash tables (compile-time 1 or 2 on the fast path)
     const int T2 = T < 2 ? T : 2;                    // tables whose bin bytes are staged
@@ -414,7 +416,12 @@ spectral_pass_kernel(const GroupHdr* __restrict__ hdr, const DevTensor* __restri
         const bool hash_on = (flags & F_HASH) != 0;
         const bool vec = FULL || (flags & F_VEC) != 0;
         const bool wd_on = (flags & F_WD) != 0;
+        // 16-bit parameter: compile-time in class 0 / 2 (H16), run-time in class 1
+        const bool half16 = FULL ? H16 : (flags & (F_F16 | F_BF16)) != 0;
         const bool stage_p = PassCfg<PASS, RM>::kP || (PASS <= 3 && wd_on);
+        // P5 of a 16-bit tensor stages its parameter in that type (16-byte chunks of 8
+        // elements; aligned tensors) or widened to float32 (the per-element path)
+        const bool stage_p16 = PASS == 5 && half16;
         const float* __restrict__ grad = Dp->grad;
         float* __restrict__ param = Dp->param;
         float* __restrict__ tbuf = Dp->tbuf;
@@ -428,7 +435,7 @@ spectral_pass_kernel(const GroupHdr* __restrict__ hdr, const DevTensor* __restri
         float scale = 0.f, inv_scale = 0.f, inst_k = 0.f, inst_gm = 1.f;
         DriveK dk{};
         float c_u = 0.f, c_root = 0.f, c_t = 0.f, c_nov = 0.f, c_hp = 0.f, gain = 0.f, neg_lr = 0.f;
-        float upd_a = 1.f, upd_b = 0.f;
+        float neg_lr16 = 0.f;
         if constexpr (PASS >= 2 && PASS <= 3) {
             scale = Cp->scale;
             inv_scale = Cp->inv_scale;
@@ -446,9 +453,14 @@ spectral_pass_kernel(const GroupHdr* __restrict__ hdr, const DevTensor* __restri
             c_hp = Cp->c_hp;
             gain = Cp->gain;
             neg_lr = Cp->neg_lr;
-            const bool half = (flags & (F_F16 | F_BF16)) != 0;
-            upd_a = half ? 0.0f : 1.0f;
-            upd_b = half ? 1.0f : neg_lr;
+            // -lr in the parameter's 16-bit type (rounded once from double), as
+            // param.add_(update.to(param.dtype), alpha=-lr) converts alpha
+            if constexpr (!FULL || H16) {
+                if (flags & F_BF16)
+                    neg_lr16 = __bfloat162float(__double2bfloat16(-hdr->hp[H_LR]));
+                else if (flags & F_F16)
+                    neg_lr16 = __half2float(__double2half(-hdr->hp[H_LR]));
+            }
         }
         // reconstruction coefficients of this pass into shared memory
         if constexpr (PASS >= 3) {
@@ -512,7 +524,18 @@ spectral_pass_kernel(const GroupHdr* __restrict__ hdr, const DevTensor* __restri
                     const bool ok = FULL || (r < rows32 && col < cols32);
                     const int64_t e = ok ? (int64_t)r * cols32 + col : 0;
                     cp_async16(sb + (lr * TC + 4 * cc) * 4, xsrc + e, ok ? 16 : 0);
-                    if (stage_p) cp_async16(sb + off_p + (lr * TC + 4 * cc) * 4, param + e, ok ? 16 : 0);
+                    if (stage_p && !stage_p16) cp_async16(sb + off_p + (lr * TC + 4 * cc) * 4, param + e, ok ? 16 : 0);
+                }
+                if (stage_p16) {
+                    const int lg_cph = lg_tc - 3;  // 16-byte chunks of 8 elements per tile row
+                    for (int c = tid; c < (RB << lg_cph); c += kThreads) {
+                        const int lr = c >> lg_cph, cc = c & ((1 << lg_cph) - 1);
+                        const int r = rb + lr, col = cb + 8 * cc;
+                        const bool ok = FULL || (r < rows32 && col < cols32);
+                        const int64_t e = ok ? (int64_t)r * cols32 + col : 0;
+                        cp_async16(sb + off_p + (lr * TC + 8 * cc) * 2,
+                                   reinterpret_cast<const unsigned char*>(Dp->param_h) + 2 * e, ok ? 16 : 0);
+                    }
                 }
                 if (PASS >= 2 && hash_on) {
                     for (int c = tid; c < (T2 << lg_rbcprb); c += kThreads) {
@@ -542,7 +565,18 @@ spectral_pass_kernel(const GroupHdr* __restrict__ hdr, const DevTensor* __restri
                     const int64_t e = (int64_t)r * cols32 + col;
                     const int o = lr * TC + lc;
                     reinterpret_cast<float*>(sb)[o] = ok ? xsrc[e] : 0.0f;
-                    if (stage_p) reinterpret_cast<float*>(sb + off_p)[o] = ok ? param[e] : 0.0f;
+                    if (stage_p) {
+                        float pv = 0.0f;
+                        if (ok) {
+                            if (!stage_p16)
+                                pv = param[e];
+                            else if (flags & F_BF16)
+                                pv = __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(Dp->param_h)[e]);
+                            else
+                                pv = __half2float(reinterpret_cast<const __half*>(Dp->param_h)[e]);
+                        }
+                        reinterpret_cast<float*>(sb + off_p)[o] = pv;
+                    }
                     if (PASS >= 2 && hash_on) {
                         const int64_t g = ((int64_t)(row032 + r) * gcols32 + col0 + col);
                         for (int t = 0; t < T2; ++t) {
@@ -867,9 +901,25 @@ spectral_pass_kernel(const GroupHdr* __restrict__ hdr, const DevTensor* __restri
                         }
                         const DriveParts dp = drive_parts(t, pred, dk);
                         const float drive = c_u * dp.u + c_root * dp.root + c_t * t + comb + c_nov * dp.nov + c_hp * hpv;
-                        // float32: p + (-lr) update; 16-bit: the update itself, applied to
-                        // the caller's tensor by half_convert_kernel<false>
-                        param[(int64_t)r * cols32 + col] = fmaf(upd_b, drive * gain, upd_a * pb[o]);
+                        const float upd = drive * gain;
+                        const int64_t pe = (int64_t)r * cols32 + col;
+                        if (!half16) {
+                            param[pe] = pb[o] + neg_lr * upd;
+                        } else {
+                            // round(p + round(-lr) round(u)), every rounding to the 16-bit type
+                            const bool bf = (flags & F_BF16) != 0;
+                            const unsigned short raw = reinterpret_cast<const unsigned short*>(pb)[o];
+                            const float p0 = !vec ? pb[o]
+                                             : (bf ? __bfloat162float(__ushort_as_bfloat16(raw))
+                                                   : __half2float(__ushort_as_half(raw)));
+                            if (bf) {
+                                const float u = __bfloat162float(__float2bfloat16_rn(upd));
+                                reinterpret_cast<__nv_bfloat16*>(Dp->param_h)[pe] = __float2bfloat16_rn(p0 + neg_lr16 * u);
+                            } else {
+                                const float u = __half2float(__float2half_rn(upd));
+                                reinterpret_cast<__half*>(Dp->param_h)[pe] = __float2half_rn(p0 + neg_lr16 * u);
+                            }
+                        }
                     }
                 }
                 if constexpr (PASS == 2) {
@@ -1531,7 +1581,9 @@ static int build_plan(const cresso_tensor_desc* descs, int64_t n, const cresso_h
         const int64_t ib = bins <= 256 ? 1 : 2;
         bool ok = d.cols >= 16 && d.cols % 16 == 0 && d.col0 % 16 == 0 && (d.ndim == 1 || gcols % 16 == 0);
         // 16-bit tensors are read through 256-byte aligned float32 copies in the scratch
-        ok = ok && (d.dtype != CRESSO_DTYPE_F32 || (d.param % 16 == 0 && d.grad % 16 == 0));
+        // (16-bit tensors: the gradient is read through an aligned float32 copy, the
+        // parameter staged in its own type by P5)
+        ok = ok && d.param % 16 == 0 && (d.dtype != CRESSO_DTYPE_F32 || d.grad % 16 == 0);
         if (d.hash_cache) ok = ok && d.hash_cache % 16 == 0 && (d.hash_cache_n * ib) % 16 == 0;
         vec[i] = ok;
     }
@@ -1635,13 +1687,14 @@ static int build_plan(const cresso_tensor_desc* descs, int64_t n, const cresso_h
                        CRESSO_EINVAL, "tensor %lld: NULL state pointer", (long long)i);
     }
     H.n_items = items;
-    // the two launch classes: item lists in tensor order within each class
+    // the three launch classes: item lists in tensor order within each class
     P.item_lists.clear();
     P.tensor_lists.clear();
-    for (int c = 0; c < 2; ++c) {
+    for (int c = 0; c < 3; ++c) {
         int64_t ci = 0, cn = 0;
         for (int64_t i = 0; i < n; ++i) {
-            if ((full[i] ? 0 : 1) != c) continue;
+            const int ci_cls = !full[i] ? 1 : ((P.dts[i].flags & (F_F16 | F_BF16)) ? 2 : 0);
+            if (ci_cls != c) continue;
             P.item_lists.push_back(ci);
             P.tensor_lists.push_back((int32_t)i);
             P.dts[i].item_base = ci;
@@ -1657,12 +1710,14 @@ static int build_plan(const cresso_tensor_desc* descs, int64_t n, const cresso_h
     P.n_rec_max = 0;
     for (int p = 1; p <= 5; ++p) {
         int64_t rb = 0;
-        for (int c = 0; c < 2; ++c) {
+        int64_t tl_off = 0;
+        for (int c = 0; c < 3; ++c) {
             const int64_t ci = H.cls_items[c];
             const int64_t g = ci == 0 ? 0 : std::max<int64_t>(1, std::min<int64_t>(ci, num_sms * (rm > 8 ? 1 : occ[p])));
             H.grid[c][p] = g;
             int64_t b = 0;
-            const int32_t* tl = P.tensor_lists.data() + (c == 0 ? 0 : H.cls_nt[0]);
+            const int32_t* tl = P.tensor_lists.data() + tl_off;
+            tl_off += H.cls_nt[c];
             for (int64_t j = 0; j < H.cls_nt[c]; ++j) {
                 DevTensor& D = P.dts[tl[j]];
                 const int64_t first = D.item_base, last = D.item_base + D.n_items - 1;
@@ -1683,7 +1738,7 @@ static int build_plan(const cresso_tensor_desc* descs, int64_t n, const cresso_h
     int64_t off = 0;
     P.off_hdr = take(off, sizeof(GroupHdr));
     P.off_dts = take(off, sizeof(DevTensor) * n);
-    P.off_items = take(off, sizeof(int64_t) * (n + 2));
+    P.off_items = take(off, sizeof(int64_t) * (n + 3));
     P.off_tmap = take(off, sizeof(int32_t) * n);
     P.off_status = take(off, sizeof(int32_t));
     P.off_cst = take(off, sizeof(TensorConsts) * n);
@@ -1712,7 +1767,8 @@ static int build_plan(const cresso_tensor_desc* descs, int64_t n, const cresso_h
     P.half_elems = 0;
     for (auto& D : P.dts)
         if (D.flags & (F_F16 | F_BF16)) P.half_elems += align_up(D.rows * D.cols, 64);
-    P.off_p32 = take(off, 4 * std::max<int64_t>(P.half_elems, 1));
+    // float32 parameter copies only when weight decay reads the parameter in P1-P3
+    P.off_p32 = take(off, 4 * std::max<int64_t>(hp->weight_decay != 0.0 ? P.half_elems : 0, 1));
     P.bytes = off;
     return CRESSO_OK;
 }
@@ -1730,7 +1786,8 @@ static void bind_scratch(Plan& P, char* base) {
         D.colpart = reinterpret_cast<float*>(base + P.off_colpart) + colpart_o;
         D.tbuf = reinterpret_cast<float*>(base + P.off_tbuf) + elem_o;
         if (D.flags & (F_F16 | F_BF16)) {
-            D.param = reinterpret_cast<float*>(base + P.off_p32) + p32_o;
+            // the float32 parameter copy exists with weight decay only; without it no pass reads D.param
+            D.param = P.hdr.hp[H_WD] != 0.0 ? reinterpret_cast<float*>(base + P.off_p32) + p32_o : nullptr;
             D.grad = D.tbuf;
             p32_o += align_up(D.rows * D.cols, 64);
         }
@@ -1770,53 +1827,60 @@ static size_t pass_smem(int pass, const GroupHdr& H, int64_t iters, bool tc) {
     return b;
 }
 
-// 16-bit tensors: float32 copies of the gradient (into the tangent buffer, which
-// P3 overwrites element by element after reading it) and of the parameter
-// before P1.  After P5, whose output for these tensors is the update u, the
-// caller's parameter becomes round(p + round(-lr) round(u)), every rounding to
-// its type: param.add_(update.to(param.dtype), alpha=-lr) (cresso_v5.py:1353)
-// as PyTorch's vectorised CPU kernel computes it, with alpha converted to the
-// tensor's type and the sum formed in float32.
-template <bool IN>
-__global__ void half_convert_kernel(const DevTensor* __restrict__ dts, int n, double neg_lr) {
+// 16-bit tensors: before P1, float32 copies of the gradient (into the tangent
+// buffer, which P3 overwrites element by element after reading it) and, when
+// weight decay reads it in P1-P3, of the parameter.  P5 updates the 16-bit
+// parameter in place.  Eight elements per thread and step where the tensor
+// allows 16-byte loads.
+template <typename T>
+__device__ __forceinline__ float to_f32(T v);
+template <>
+__device__ __forceinline__ float to_f32<__half>(__half v) { return __half2float(v); }
+template <>
+__device__ __forceinline__ float to_f32<__nv_bfloat16>(__nv_bfloat16 v) { return __bfloat162float(v); }
+
+template <typename T>
+__device__ __forceinline__ void widen(const void* src_v, float* dst, int64_t N) {
+    const T* src = reinterpret_cast<const T*>(src_v);
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    const int64_t t0 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (((uintptr_t)src & 15) == 0 && (N & 7) == 0) {
+        for (int64_t c = t0; c < N / 8; c += stride) {
+            const uint4 raw = reinterpret_cast<const uint4*>(src)[c];
+            const T* h = reinterpret_cast<const T*>(&raw);
+            float4 a = make_float4(to_f32(h[0]), to_f32(h[1]), to_f32(h[2]), to_f32(h[3]));
+            float4 b = make_float4(to_f32(h[4]), to_f32(h[5]), to_f32(h[6]), to_f32(h[7]));
+            reinterpret_cast<float4*>(dst)[2 * c] = a;
+            reinterpret_cast<float4*>(dst)[2 * c + 1] = b;
+        }
+    } else {
+        for (int64_t e = t0; e < N; e += stride) dst[e] = to_f32(src[e]);
+    }
+}
+
+__global__ void half_widen_kernel(const DevTensor* __restrict__ dts, int n, int with_param) {
     for (int k = blockIdx.y; k < n; k += gridDim.y) {
         const DevTensor& D = dts[k];
         const int fl = D.flags;
         if (!(fl & (F_F16 | F_BF16))) continue;
-        const bool bf = (fl & F_BF16) != 0;
         const int64_t N = D.rows * D.cols;
-        for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < N; e += (int64_t)gridDim.x * blockDim.x) {
-            if (IN) {
-                if (bf) {
-                    D.tbuf[e] = __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(D.grad_h)[e]);
-                    D.param[e] = __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(D.param_h)[e]);
-                } else {
-                    D.tbuf[e] = __half2float(reinterpret_cast<const __half*>(D.grad_h)[e]);
-                    D.param[e] = __half2float(reinterpret_cast<const __half*>(D.param_h)[e]);
-                }
-            } else if (bf) {
-                __nv_bfloat16* ph = reinterpret_cast<__nv_bfloat16*>(D.param_h);
-                const float a = __bfloat162float(__double2bfloat16(neg_lr));
-                const float u = __bfloat162float(__float2bfloat16_rn(D.param[e]));
-                ph[e] = __float2bfloat16_rn(__bfloat162float(ph[e]) + a * u);
-            } else {
-                __half* ph = reinterpret_cast<__half*>(D.param_h);
-                const float a = __half2float(__double2half(neg_lr));
-                const float u = __half2float(__float2half_rn(D.param[e]));
-                ph[e] = __float2half_rn(__half2float(ph[e]) + a * u);
-            }
+        if (fl & F_BF16) {
+            widen<__nv_bfloat16>(D.grad_h, D.tbuf, N);
+            if (with_param) widen<__nv_bfloat16>(D.param_h, D.param, N);
+        } else {
+            widen<__half>(D.grad_h, D.tbuf, N);
+            if (with_param) widen<__half>(D.param_h, D.param, N);
         }
     }
 }
 
-template <bool IN>
-static int launch_half_convert(const Plan& P, char* base, cudaStream_t s) {
+static int launch_half_widen(const Plan& P, char* base, cudaStream_t s) {
     if (P.half_elems == 0) return CRESSO_OK;
     const DevTensor* dts = reinterpret_cast<const DevTensor*>(base + P.off_dts);
     const int n = (int)P.hdr.n_tensors;
-    dim3 grid(256, (unsigned)std::min(n, 65535));
-    half_convert_kernel<IN><<<grid, kThreads, 0, s>>>(dts, n, -P.hdr.hp[H_LR]);
-    CRESSO_LAUNCHED("half_convert_kernel");
+    dim3 grid(148, (unsigned)std::min(n, 65535));
+    half_widen_kernel<<<grid, kThreads, 0, s>>>(dts, n, P.hdr.hp[H_WD] != 0.0 ? 1 : 0);
+    CRESSO_LAUNCHED("half_widen_kernel");
     return CRESSO_OK;
 }
 
@@ -1829,16 +1893,23 @@ static int launch_stage(int stage, const Plan& P, char* base, cudaStream_t s) {
     double* recs = reinterpret_cast<double*>(base + P.off_recs);
     float* recb = reinterpret_cast<float*>(base + P.off_recb);
     const int n = (int)P.hdr.n_tensors;
-    // class 0 of P3-P5 at rank pad 8 with 16-row items: the tensor-core kernels
-    auto run_pass = [&](auto kern_tc, auto kern_full, auto kern_gen, int pass) -> int {
-        for (int c = 0; c < 2; ++c) {
+    // classes 0 and 2 of P3-P5 at rank pad 8 with 16-row items: the tensor-core kernels;
+    // class 2 uses the 16-bit forms (which differ from class 0's in P5 only)
+    auto run_pass = [&](auto kern_tc, auto kern_full, auto kern_gen, auto kern_tc16, auto kern_full16,
+                        int pass) -> int {
+        for (int c = 0; c < 3; ++c) {
             if (P.hdr.grid[c][pass] == 0) continue;
-            const bool tc = c == 0 && pass >= 3 && RM == 8 && P.hdr.iters == 16;
+            const bool tc = c != 1 && pass >= 3 && RM == 8 && P.hdr.iters == 16;
             const size_t smem = pass_smem(pass, P.hdr, P.hdr.iters, tc);
-            auto kern = c == 0 ? (tc ? kern_tc : kern_full) : kern_gen;
+            auto kern = c == 1 ? kern_gen : (c == 0 ? (tc ? kern_tc : kern_full) : (tc ? kern_tc16 : kern_full16));
             if (smem > 48 * 1024)
                 CRESSO_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-            kern<<<(unsigned)P.hdr.grid[c][pass], kThreads, smem, s>>>(hdr, dts, items, tmap, recs, recb);
+            int64_t lo = 0, to = 0;  // this class's item and tensor lists
+            for (int k = 0; k < c; ++k) {
+                lo += P.hdr.cls_nt[k] + 1;
+                to += P.hdr.cls_nt[k];
+            }
+            kern<<<(unsigned)P.hdr.grid[c][pass], kThreads, smem, s>>>(hdr, dts, items + lo, tmap + to, recs, recb, c);
             CRESSO_LAUNCHED("spectral_pass_kernel");
         }
         return CRESSO_OK;
@@ -1853,40 +1924,40 @@ static int launch_stage(int stage, const Plan& P, char* base, cudaStream_t s) {
     };
     switch (stage) {
         case 1: return run_pass(spectral_pass_kernel<1, RM, NT, true, false>, spectral_pass_kernel<1, RM, NT, true, false>,
-                            spectral_pass_kernel<1, RM, NT, false, false>, 1);
+                            spectral_pass_kernel<1, RM, NT, false, false>, spectral_pass_kernel<1, RM, NT, true, false>,
+                            spectral_pass_kernel<1, RM, NT, true, false>, 1);
         case 2: return run_reduce(1);
         case 3:
             finalize1_kernel<RM><<<n, kThreads, 0, s>>>(hdr, dts);
             CRESSO_LAUNCHED("finalize1_kernel");
             return CRESSO_OK;
         case 4: return run_pass(spectral_pass_kernel<2, RM, NT, true, false>, spectral_pass_kernel<2, RM, NT, true, false>,
-                            spectral_pass_kernel<2, RM, NT, false, false>, 2);
+                            spectral_pass_kernel<2, RM, NT, false, false>, spectral_pass_kernel<2, RM, NT, true, false>,
+                            spectral_pass_kernel<2, RM, NT, true, false>, 2);
         case 5: return run_reduce(2);
         case 6:
             finalize2_kernel<RM><<<n, kThreads, 0, s>>>(hdr, dts);
             CRESSO_LAUNCHED("finalize2_kernel");
             return CRESSO_OK;
         case 7: return run_pass(spectral_pass_kernel<3, RM, NT, true, RM == 8>, spectral_pass_kernel<3, RM, NT, true, false>,
-                            spectral_pass_kernel<3, RM, NT, false, false>, 3);
+                            spectral_pass_kernel<3, RM, NT, false, false>, spectral_pass_kernel<3, RM, NT, true, RM == 8>,
+                            spectral_pass_kernel<3, RM, NT, true, false>, 3);
         case 8: return run_reduce(3);
         case 9:
             finalize3_kernel<RM><<<n, kThreads, 0, s>>>(hdr, dts);
             CRESSO_LAUNCHED("finalize3_kernel");
             return CRESSO_OK;
         case 10: return run_pass(spectral_pass_kernel<4, RM, NT, true, RM == 8>, spectral_pass_kernel<4, RM, NT, true, false>,
-                            spectral_pass_kernel<4, RM, NT, false, false>, 4);
+                            spectral_pass_kernel<4, RM, NT, false, false>, spectral_pass_kernel<4, RM, NT, true, RM == 8>,
+                            spectral_pass_kernel<4, RM, NT, true, false>, 4);
         case 11: return run_reduce(4);
         case 12:
             finalize4_kernel<RM><<<n, kThreads, 0, s>>>(hdr, dts);
             CRESSO_LAUNCHED("finalize4_kernel");
             return CRESSO_OK;
-        case 13: {
-            const int st = run_pass(spectral_pass_kernel<5, RM, NT, true, RM == 8>,
-                                    spectral_pass_kernel<5, RM, NT, true, false>,
-                                    spectral_pass_kernel<5, RM, NT, false, false>, 5);
-            if (st) return st;
-            return launch_half_convert<false>(P, base, s);
-        }
+        case 13: return run_pass(spectral_pass_kernel<5, RM, NT, true, RM == 8>, spectral_pass_kernel<5, RM, NT, true, false>,
+                            spectral_pass_kernel<5, RM, NT, false, false>, spectral_pass_kernel<5, RM, NT, true, RM == 8, true>,
+                            spectral_pass_kernel<5, RM, NT, true, false, true>, 5);
         default: return CRESSO_OK;
     }
 }
@@ -1911,7 +1982,7 @@ int cresso_spectral_layout(const cresso_tensor_desc* descs, int64_t n, const cre
     if (layout_len >= 10) layout[9] = P.off_status;
     if (layout_len >= 12) {
         layout[10] = P.hdr.iters;
-        layout[11] = (P.hdr.cls_items[0] > 0 && P.rm == 8 && P.hdr.iters == 16) ? ((1 << 3) | (1 << 4) | (1 << 5)) : 0;
+        layout[11] = (P.hdr.cls_items[0] + P.hdr.cls_items[2] > 0 && P.rm == 8 && P.hdr.iters == 16) ? ((1 << 3) | (1 << 4) | (1 << 5)) : 0;
     }
     return CRESSO_OK;
 }
@@ -1935,11 +2006,11 @@ int cresso_spectral_run(const cresso_tensor_desc* descs, int64_t n, const cresso
         CRESSO_CUDA(cudaMemsetAsync(base + P.off_status, 0, sizeof(int32_t), s));
         CRESSO_CUDA(cudaMemcpyAsync(base + P.off_hdr, &P.hdr, sizeof(GroupHdr), cudaMemcpyHostToDevice, s));
         CRESSO_CUDA(cudaMemcpyAsync(base + P.off_dts, P.dts.data(), sizeof(DevTensor) * n, cudaMemcpyHostToDevice, s));
-        CRESSO_CUDA(cudaMemcpyAsync(base + P.off_items, P.item_lists.data(), sizeof(int64_t) * (n + 2),
+        CRESSO_CUDA(cudaMemcpyAsync(base + P.off_items, P.item_lists.data(), sizeof(int64_t) * (n + 3),
                                     cudaMemcpyHostToDevice, s));
         CRESSO_CUDA(cudaMemcpyAsync(base + P.off_tmap, P.tensor_lists.data(), sizeof(int32_t) * n,
                                     cudaMemcpyHostToDevice, s));
-        const int hs = launch_half_convert<true>(P, base, s);
+        const int hs = launch_half_widen(P, base, s);
         if (hs) return hs;
     }
     for (int64_t stage = std::max<int64_t>(stage_begin, 1); stage < stage_end; ++stage) {
