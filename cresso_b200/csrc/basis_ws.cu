@@ -34,15 +34,20 @@ static double hash_unit_host(int64_t n, int64_t salt) {
 
 struct AxisParam {
     double f, chirp, center, width;
-    int32_t active;  // 0: neutral side of a 1-D tensor
-    int32_t pad;
+    int32_t pad0, pad1;
 };
+// A tensor of rank n >= 2 is handled as (product of the n - 1 leading axes) x
+// (last axis): every carrier factorises so, the leading axes composing into
+// the row table (complex products of (cos, sin) pairs, or component-wise
+// products for the product kind).  A 1-D tensor has no leading axis.
 struct ModeParam {
-    int32_t zero, kind, pad0, pad1;
-    AxisParam row, col;
+    int32_t zero, kind, nlead, pad;
+    AxisParam lead[CRESSO_MAX_NDIM - 1];
+    AxisParam col;
 };
 struct ModePack {
     ModeParam m[kMaxRank];
+    int64_t ldim[CRESSO_MAX_NDIM];  // leading axis lengths
 };
 
 static AxisParam axis_param(int64_t mode, int64_t axis, int64_t f) {
@@ -51,27 +56,22 @@ static AxisParam axis_param(int64_t mode, int64_t axis, int64_t f) {
     a.chirp = 0.25 + 1.75 * hash_unit_host(mode, 17 + axis);
     a.center = 0.15 + 0.70 * hash_unit_host(mode, 101 + axis);
     a.width = 0.18 + 0.20 * hash_unit_host(mode, 151 + axis);
-    a.active = 1;
     return a;
 }
 
-static ModePack make_modes(int64_t ndim, int64_t rank, const int64_t* freqs) {
+static ModePack make_modes(int64_t ndim, const int64_t* shape, int64_t rank, const int64_t* freqs) {
     ModePack p;
     memset(&p, 0, sizeof(p));
+    for (int64_t a = 0; a + 1 < ndim; ++a) p.ldim[a] = shape[a];
     for (int64_t k = 0; k < rank; ++k) {
         ModeParam& m = p.m[k];
         int64_t fsum = 0;
         for (int64_t a = 0; a < ndim; ++a) fsum += freqs[k * ndim + a] < 0 ? -freqs[k * ndim + a] : freqs[k * ndim + a];
         m.zero = fsum == 0;
         m.kind = (int32_t)(k % 4);
-        if (ndim == 2) {
-            m.row = axis_param(k, 0, freqs[k * ndim + 0]);
-            m.col = axis_param(k, 1, freqs[k * ndim + 1]);
-        } else {
-            m.row = AxisParam{};
-            m.row.active = 0;
-            m.col = axis_param(k, 0, freqs[k * ndim + 0]);
-        }
+        m.nlead = (int32_t)(ndim - 1);
+        for (int64_t a = 0; a + 1 < ndim; ++a) m.lead[a] = axis_param(k, a, freqs[k * ndim + a]);
+        m.col = axis_param(k, ndim - 1, freqs[k * ndim + ndim - 1]);
     }
     return p;
 }
@@ -87,11 +87,6 @@ __device__ void axis_value(const ModeParam& m, const AxisParam& ax, int64_t idx,
     if (m.zero) {
         x1 = 1.0;
         x2 = 0.0;
-        return;
-    }
-    if (!ax.active) {  // absent axis of a 1-D tensor
-        x1 = 1.0;
-        x2 = m.kind == 1 ? 1.0 : 0.0;
         return;
     }
     const double pi = 3.14159265358979323846;
@@ -125,10 +120,33 @@ __global__ void build_tables_kernel(ModePack modes, int rank, int rm, int64_t gr
         const int64_t idx = t / rm;
         double x1 = 0.0, x2 = 0.0;
         if (k < rank) {
-            if (idx < grows)
-                axis_value(modes.m[k], modes.m[k].row, idx, grows, x1, x2);
-            else
-                axis_value(modes.m[k], modes.m[k].col, idx - grows, gcols, x1, x2);
+            const ModeParam& m = modes.m[k];
+            if (idx >= grows) {
+                axis_value(m, m.col, idx - grows, gcols, x1, x2);
+            } else if (m.zero) {
+                x1 = 1.0;
+                x2 = 0.0;
+            } else {
+                // leading axes, last one fastest; start from the identity of the composition
+                x1 = 1.0;
+                x2 = m.kind == 1 ? 1.0 : 0.0;
+                int64_t rem = idx;
+                for (int a = m.nlead - 1; a >= 0; --a) {
+                    const int64_t dim = modes.ldim[a];
+                    const int64_t coord = rem % dim;
+                    rem /= dim;
+                    double y1, y2;
+                    axis_value(m, m.lead[a], coord, dim, y1, y2);
+                    if (m.kind == 1) {
+                        x1 *= y1;
+                        x2 *= y2;
+                    } else {
+                        const double t1 = x1 * y1 - x2 * y2;
+                        x2 = x1 * y2 + x2 * y1;
+                        x1 = t1;
+                    }
+                }
+            }
         }
         if (idx < grows) {
             rowtab[(idx * rm + k) * 2 + 0] = (float)x1;
@@ -512,11 +530,14 @@ __global__ void instant_metric_kernel(const float* rel, int64_t rows, int64_t co
 
 static int checked_shape(int64_t ndim, const int64_t* shape, int64_t* grows, int64_t* gcols) {
     CRESSO_REQUIRE(shape != nullptr, CRESSO_EINVAL, "shape pointer is NULL");
-    CRESSO_REQUIRE(ndim == 1 || ndim == 2, CRESSO_EUNSUPPORTED,
-                   "spectral carriers support 1-D and 2-D tensors on the CUDA path (got ndim=%lld)", (long long)ndim);
+    CRESSO_REQUIRE(ndim >= 1 && ndim <= CRESSO_MAX_NDIM, CRESSO_EUNSUPPORTED,
+                   "spectral carriers support tensors of rank 1 to %d (got ndim=%lld)", CRESSO_MAX_NDIM, (long long)ndim);
     for (int64_t a = 0; a < ndim; ++a) CRESSO_REQUIRE(shape[a] > 0, CRESSO_EINVAL, "shape[%lld] must be > 0", (long long)a);
-    *grows = ndim == 2 ? shape[0] : 1;
-    *gcols = ndim == 2 ? shape[1] : shape[0];
+    // (product of the leading axes) x (last axis)
+    int64_t lead = 1;
+    for (int64_t a = 0; a + 1 < ndim; ++a) lead *= shape[a];
+    *grows = lead;
+    *gcols = shape[ndim - 1];
     return CRESSO_OK;
 }
 
@@ -638,7 +659,7 @@ int cresso_shape_workspace_init(int64_t ndim, const int64_t* shape, int64_t rank
     ShapeWsHeader h = shape_ws_layout(ndim, grows, gcols, rank, rm, bins, tables);
     cudaStream_t s = (cudaStream_t)stream;
     char* base = (char*)ws;
-    ModePack modes = make_modes(ndim, rank, freqs);
+    ModePack modes = make_modes(ndim, shape, rank, freqs);
     float* rowtab = reinterpret_cast<float*>(base + h.off_rowtab);
     float* coltab = reinterpret_cast<float*>(base + h.off_coltab);
     double* tmp = reinterpret_cast<double*>(base + h.off_tmp);
@@ -711,6 +732,8 @@ int cresso_basis_reconstruct(const float* coef_cos, const float* coef_sin, const
 
 int cresso_instant_axis_metric(const float* rel, int64_t ndim, const int64_t* shape, double power, double coupling,
                                double eps, float* out, cresso_stream_t stream) {
+    CRESSO_REQUIRE(ndim == 1 || ndim == 2, CRESSO_EUNSUPPORTED,
+                   "instant_axis_metric: 1-D and 2-D fields (got ndim=%lld)", (long long)ndim);
     int64_t rows, cols;
     int st = checked_shape(ndim, shape, &rows, &cols);
     if (st) return st;

@@ -38,6 +38,7 @@ namespace cresso {
 constexpr int kStages = 14;  // see launch_stage
 constexpr int kNSRec = 36;  // float64 scalars per block record (>= 2 + 2 * kMaxRank, >= 29)
 constexpr int kGram = 29;   // 28 pair sums of (u, root, t, pred, nov, echo, hp) + sum rat^2
+constexpr int kMaxLeadSum = 4096;  // sum of the leading axis lengths of an N-d tensor with the instant metric
 
 enum : int32_t {
     F_MAXIMIZE = 1,
@@ -83,6 +84,7 @@ struct GroupHdr {
 
 struct DevTensor {
     int64_t rows, cols, row0, col0, gcols, N;
+    int64_t dims[CRESSO_MAX_NDIM];  // global shape (rank >= 3: leading-axis factors of the instant metric)
     int64_t item_base, n_items, step, hidx_n;  // item_base: first item in the class's item list
     int32_t ndim, R, TC, RPI, RB, n_ct, n_bands, flags;
     int32_t cfirst[6], recbase[6], nrec[6], pad0;
@@ -1101,7 +1103,7 @@ spectral_pass_kernel(const GroupHdr* __restrict__ hdr, const DevTensor* __restri
 __host__ __device__ inline int64_t red_len(int pass, int64_t rm, int64_t tb, int64_t cols, int ndim) {
     switch (pass) {
         case 1: return 1;
-        case 2: return 2 + 2 * rm + tb + (ndim == 2 ? cols : 0);
+        case 2: return 2 + 2 * rm + tb + (ndim >= 2 ? cols : 0);
         case 3: return 2 + 2 * rm + tb;
         default: return kGram;
     }
@@ -1261,13 +1263,58 @@ __global__ void finalize2_kernel(const GroupHdr* __restrict__ hdr, const DevTens
     const float pw = fmaxf((float)hp[H_IP], 0.25f);
     const float gmc = fmaxf((float)(sumd / N), eps);
     if (D.flags & F_INST2D) {
-        const float kk = (float)(hp[H_IC] / (2.0 * (double)pw));
-        const int64_t grows = D.ndim == 2 ? (D.N / D.gcols) : 1;
-        for (int64_t r = tid; r < D.rows; r += kThreads) {
-            double s = 0.0;
-            for (int c = 0; c < D.n_ct; ++c) s += (double)D.rowpart[(int64_t)c * D.rows + r];
-            const float rmean = (float)(s / (double)D.gcols);
-            D.rowf[r] = expf(kk * logf(fmaxf(rmean / gmc, eps)));
+        // exp(c / (ndim * p) * sum over axes of log(max(axis mean / mean, eps)))
+        const float kk = (float)(hp[H_IC] / ((double)D.ndim * (double)pw));
+        const int64_t grows = D.N / D.gcols;
+        if (D.ndim == 2) {
+            for (int64_t r = tid; r < D.rows; r += kThreads) {
+                double s = 0.0;
+                for (int c = 0; c < D.n_ct; ++c) s += (double)D.rowpart[(int64_t)c * D.rows + r];
+                const float rmean = (float)(s / (double)D.gcols);
+                D.rowf[r] = expf(kk * logf(fmaxf(rmean / gmc, eps)));
+            }
+        } else {
+            // rank >= 3 (never sharded): the row index is the flattened leading axes.  Row
+            // sums into rowf, then per leading axis a and coordinate c the marginal mean
+            // (a fixed-order float64 sum over the rows with that coordinate), whose log
+            // goes to s_lax; a row's factor is the exponential of its axes' logs.
+            __shared__ float s_lax[kMaxLeadSum];
+            for (int64_t r = tid; r < D.rows; r += kThreads) {
+                double s = 0.0;
+                for (int c = 0; c < D.n_ct; ++c) s += (double)D.rowpart[(int64_t)c * D.rows + r];
+                D.rowf[r] = (float)s;
+            }
+            __syncthreads();
+            const int nl = (int)D.ndim - 1;
+            int lead_sum = 0;
+            for (int a = 0; a < nl; ++a) lead_sum += (int)D.dims[a];
+            for (int j = tid; j < lead_sum; j += kThreads) {
+                int a = 0, c = j;
+                while (c >= D.dims[a]) {
+                    c -= (int)D.dims[a];
+                    ++a;
+                }
+                int64_t inner = 1;
+                for (int b = a + 1; b < nl; ++b) inner *= D.dims[b];
+                const int64_t outer = grows / (D.dims[a] * inner);
+                double m = 0.0;
+                for (int64_t o = 0; o < outer; ++o)
+                    for (int64_t i = 0; i < inner; ++i) m += (double)D.rowf[(o * D.dims[a] + c) * inner + i];
+                const double per = (double)D.N / (double)D.dims[a];
+                s_lax[j] = logf(fmaxf((float)(m / per) / gmc, eps));
+            }
+            __syncthreads();
+            for (int64_t r = tid; r < D.rows; r += kThreads) {
+                float lsum = 0.0f;
+                int64_t rem = r;
+                int off = lead_sum;
+                for (int a = nl - 1; a >= 0; --a) {
+                    off -= (int)D.dims[a];
+                    lsum += s_lax[off + (int)(rem % D.dims[a])];
+                    rem /= D.dims[a];
+                }
+                D.rowf[r] = expf(kk * lsum);
+            }
         }
         const double* cols = red + 2 + 2 * rm + TB;
         for (int64_t c = tid; c < D.cols; c += kThreads) {
@@ -1515,6 +1562,15 @@ static int64_t take(int64_t& off, int64_t bytes) {
     return o;
 }
 
+// A tensor of rank n >= 2 is (product of the n - 1 leading axes) x (last axis);
+// rank 1 is one row.
+static int64_t g_rows(const cresso_tensor_desc& d) {
+    int64_t r = 1;
+    for (int64_t a = 0; a + 1 < d.ndim; ++a) r *= d.shape[a];
+    return r;
+}
+static int64_t g_cols(const cresso_tensor_desc& d) { return d.shape[d.ndim - 1]; }
+
 static int hp_flags_hard(const cresso_tensor_desc& d, const cresso_hparams& hp, int64_t N) {
     const int64_t cutoff = (int64_t)hp.thin_matrix_hard_cutoff;
     bool thin = false;
@@ -1550,9 +1606,9 @@ static int build_plan(const cresso_tensor_desc* descs, int64_t n, const cresso_h
     int64_t total_rows_work = 0;
     for (int64_t i = 0; i < n; ++i) {
         const cresso_tensor_desc& d = descs[i];
-        CRESSO_REQUIRE(d.ndim == 1 || d.ndim == 2, CRESSO_EUNSUPPORTED,
-                       "tensor %lld: spectral route supports 1-D and 2-D tensors on the CUDA path (ndim=%lld)",
-                       (long long)i, (long long)d.ndim);
+        CRESSO_REQUIRE(d.ndim >= 1 && d.ndim <= CRESSO_MAX_NDIM, CRESSO_EUNSUPPORTED,
+                       "tensor %lld: spectral route supports tensors of rank 1 to %d (ndim=%lld)", (long long)i,
+                       CRESSO_MAX_NDIM, (long long)d.ndim);
         CRESSO_REQUIRE(d.dtype == CRESSO_DTYPE_F32 || d.dtype == CRESSO_DTYPE_F16 || d.dtype == CRESSO_DTYPE_BF16,
                        CRESSO_EUNSUPPORTED, "tensor %lld: dtype code %lld (float32, float16 and bfloat16 are supported)",
                        (long long)i, (long long)d.dtype);
@@ -1560,12 +1616,21 @@ static int build_plan(const cresso_tensor_desc* descs, int64_t n, const cresso_h
                        (long long)i);
         CRESSO_REQUIRE(d.rows >= 1 && d.cols >= 1 && d.row0 >= 0 && d.col0 >= 0, CRESSO_EINVAL,
                        "tensor %lld: bad local block", (long long)i);
-        const int64_t grows = d.ndim == 2 ? d.shape[0] : 1;
-        const int64_t gcols = d.ndim == 2 ? d.shape[1] : d.shape[0];
+        const int64_t grows = g_rows(d);
+        const int64_t gcols = g_cols(d);
         CRESSO_REQUIRE(d.row0 + d.rows <= grows && d.col0 + d.cols <= gcols, CRESSO_EINVAL,
                        "tensor %lld: local block outside the global shape", (long long)i);
         CRESSO_REQUIRE(d.ndim == 1 || (d.col0 == 0 && d.cols == gcols), CRESSO_EUNSUPPORTED,
                        "tensor %lld: 2-D tensors are sharded by rows only", (long long)i);
+        CRESSO_REQUIRE(d.ndim <= 2 || (d.row0 == 0 && d.rows == grows), CRESSO_EUNSUPPORTED,
+                       "tensor %lld: tensors of rank >= 3 are not sharded", (long long)i);
+        if (d.ndim >= 3) {
+            int64_t lead_sum = 0;
+            for (int64_t a = 0; a + 1 < d.ndim; ++a) lead_sum += d.shape[a];
+            CRESSO_REQUIRE(lead_sum <= kMaxLeadSum, CRESSO_EUNSUPPORTED,
+                           "tensor %lld: leading axes of a rank-%lld tensor sum to %lld (at most %d)", (long long)i,
+                           (long long)d.ndim, (long long)lead_sum, kMaxLeadSum);
+        }
         CRESSO_REQUIRE(d.step >= 1, CRESSO_EINVAL, "tensor %lld: step must be >= 1", (long long)i);
         CRESSO_REQUIRE(grows * gcols < (1LL << 31), CRESSO_EUNSUPPORTED,
                        "tensor %lld: more than 2^31 - 1 elements per tensor", (long long)i);
@@ -1577,7 +1642,7 @@ static int build_plan(const cresso_tensor_desc* descs, int64_t n, const cresso_h
     std::vector<char> vec(n, 0);
     for (int64_t i = 0; i < n; ++i) {
         const cresso_tensor_desc& d = descs[i];
-        const int64_t gcols = d.ndim == 2 ? d.shape[1] : d.shape[0];
+        const int64_t gcols = g_cols(d);
         const int64_t ib = bins <= 256 ? 1 : 2;
         bool ok = d.cols >= 16 && d.cols % 16 == 0 && d.col0 % 16 == 0 && (d.ndim == 1 || gcols % 16 == 0);
         // 16-bit tensors are read through 256-byte aligned float32 copies in the scratch
@@ -1611,8 +1676,9 @@ static int build_plan(const cresso_tensor_desc* descs, int64_t n, const cresso_h
         D.cols = d.cols;
         D.row0 = d.row0;
         D.col0 = d.col0;
-        D.gcols = d.ndim == 2 ? d.shape[1] : d.shape[0];
-        D.N = d.ndim == 2 ? d.shape[0] * d.shape[1] : d.shape[0];
+        D.gcols = g_cols(d);
+        D.N = g_rows(d) * D.gcols;
+        for (int64_t a = 0; a < CRESSO_MAX_NDIM; ++a) D.dims[a] = a < d.ndim ? d.shape[a] : 0;
         D.step = d.step;
         D.R = (int32_t)rank;
         D.TC = std::min(256, pow2_ceil(d.cols));
@@ -1636,16 +1702,16 @@ static int build_plan(const cresso_tensor_desc* descs, int64_t n, const cresso_h
         if (hp->local_sharpness != 0.0) fl |= F_LOCAL;
         if (hard && hp->echo_mix != 0.0) fl |= F_ECHO;
         const double ic = hard ? hp->instant_metric_coupling : 0.0;
-        if (ic != 0.0 && D.N > 1) fl |= (d.ndim == 2 ? F_INST2D : F_INST1D);
+        if (ic != 0.0 && D.N > 1) fl |= (d.ndim >= 2 ? F_INST2D : F_INST1D);  // rank >= 3: leading-axis factors
         if (fmax(hp->instant_metric_power, 0.25) == 1.0) fl |= F_IPOW1;
         if (vec[i]) fl |= F_VEC;
         full[i] = vec[i] && D.TC == 256 && d.cols % 256 == 0 && d.rows % D.RB == 0 && bins <= 256;
         D.flags = fl;
         // pointers into the caller's objects
         const char* ws = (const char*)d.shape_ws;
-        ShapeWsHeader wh = shape_ws_layout(d.ndim, d.ndim == 2 ? d.shape[0] : 1, D.gcols, rank, rm, bins,
+        ShapeWsHeader wh = shape_ws_layout(d.ndim, g_rows(d), D.gcols, rank, rm, bins,
                                            hash_on || bins > 0 ? tables : 0);
-        if (bins == 0) wh = shape_ws_layout(d.ndim, d.ndim == 2 ? d.shape[0] : 1, D.gcols, rank, rm, 0, 0);
+        if (bins == 0) wh = shape_ws_layout(d.ndim, g_rows(d), D.gcols, rank, rm, 0, 0);
         D.rowtab = (const float*)(ws + wh.off_rowtab);
         D.coltab = (const float*)(ws + wh.off_coltab);
         D.stats = (const ModeStats*)(ws + wh.off_stats);

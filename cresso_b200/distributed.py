@@ -14,8 +14,8 @@ spreading one optimizer step over the GPUs of a box are provided:
     Every rank then holds identical rank / hash / scalar state, and updates its
     own rows.  Hash indices and carrier coordinates use global indices, so the
     result equals the single-GPU step up to the float64 summation order.
-    Small and LoRA-thin (scalar-route) tensors are passed whole and stepped
-    redundantly on every rank.
+    Small and LoRA-thin (scalar-route) tensors and tensors of rank >= 3 are
+    passed whole and stepped redundantly on every rank.
 
 ``ZeroCRESSO5`` (ZeRO-1 partition)
     Whole tensors are assigned to ranks by a longest-processing-time greedy

@@ -230,8 +230,11 @@ class CRESSO5(Optimizer):
         spec = getattr(param, "_cresso_shard", None)
         if spec is None:
             shape = tuple(int(d) for d in param.shape)
-            if len(shape) == 2:
-                return shape, 0, shape[0], 0, shape[1]
+            if len(shape) >= 2:  # rank >= 3: the leading axes flattened into rows
+                rows = 1
+                for d in shape[:-1]:
+                    rows *= d
+                return shape, 0, rows, 0, shape[-1]
             n = shape[-1] if shape else 1
             return shape, 0, 1, 0, n
         gshape, offset = spec

@@ -33,16 +33,17 @@ def case_inputs(golden, name, shape, steps, seed, istd, gstd):
     return init, grads
 
 
-def half_cases():
+def extra_cases():
     spec = importlib.util.spec_from_file_location("make_golden", ROOT / "tests" / "golden" / "make_golden.py")
     mod = importlib.util.module_from_spec(spec)
     spec.loader.exec_module(mod)
-    return mod.HALF_CASES
+    return mod.EXTRA_CASES
 
 
-def half_case_inputs(golden, name, shape, steps, seed, istd, gstd, dtype):
-    """Inputs of a 16-bit golden case, regenerated from its seed exactly as the
-    generator made them (float32 draws rounded to the parameter type)."""
+def extra_case_inputs(golden, name, shape, steps, seed, istd, gstd, dtype):
+    """Inputs of a case of the second golden table (16-bit parameters, tensors of
+    rank >= 3), regenerated from its seed exactly as the generator made them
+    (float32 draws rounded to the parameter type)."""
     dt = getattr(torch, dtype)
     gen = torch.Generator().manual_seed(seed)
     init = (torch.randn(shape, generator=gen) * istd).float().to(dt)

@@ -22,8 +22,8 @@ def golden():
 
 
 @pytest.fixture(scope="session")
-def golden_half():
+def golden_extra():
     import numpy as np
 
-    with np.load(ROOT / "tests" / "golden" / "golden_half.npz") as z:
+    with np.load(ROOT / "tests" / "golden" / "golden_extra.npz") as z:
         return {k: z[k] for k in z.files}

@@ -1,6 +1,6 @@
 """Generate golden vectors for the CRESSO5 step by running the reference itself.
 
-Usage:  python tests/golden/make_golden.py [path-to-reference-checkout] [--half-only]
+Usage:  python tests/golden/make_golden.py [path-to-reference-checkout] [--extra-only]
 
 The reference (win10ogod/cresso, ``cresso_v5.py``) is imported from the given
 checkout and run on CPU with ``cuda_ops='off'`` and one thread, which is its
@@ -9,9 +9,10 @@ PyTorch path.  Outputs are written next to this script:
 * ``golden_small.npz`` - frequency packs, hash indices, hash bin counts at the
   benchmark sizes, basis projections / reconstructions, instant metrics and
   full optimizer steps (inputs, final params, every state tensor).
-* ``golden_half.npz`` - full optimizer steps with float16 / bfloat16
-  parameters (``HALF_CASES``; values stored as float32, which holds every
-  16-bit value exactly).  ``--half-only`` regenerates just this file.
+* ``golden_extra.npz`` - full optimizer steps of ``EXTRA_CASES``: float16 /
+  bfloat16 parameters (values stored as float32, which holds every 16-bit
+  value exactly) and spectral-route tensors of rank 3 to 5.  ``--extra-only``
+  regenerates just this file.
 
 The reference is not available where the tests run, so the vectors are
 committed; the tests only read the ``.npz``.
@@ -70,13 +71,14 @@ STEP_CASES = {
 }
 
 
-# float16 / bfloat16 parameter cases: name -> (shape, kwargs, steps, seed, init_std, grad_std, dtype).
-# The first four are the shapes and settings of the reference's own 16-bit tests
-# (tests/test_cresso_v5_cuda_ops.py:109-146, 213-250).
+# More cases: name -> (shape, kwargs, steps, seed, init_std, grad_std, dtype).  The 16-bit ones
+# start with the shapes and settings of the reference's own 16-bit tests
+# (tests/test_cresso_v5_cuda_ops.py:109-146, 213-250); the N-d ones are spectral-route
+# tensors of rank 3 to 5 (conv-like weights) with the four carrier kinds and the instant metric.
 _REF_SPEC16 = dict(lr=1.0e-3, rank=8, max_frequency=5, min_spectral_size=1, hard_channel_min_size=1,
                    thin_matrix_hard_cutoff=0, hash_bins=37, hash_tables=2, basis_cache_limit_elements=0)
 _REF_SCAL16 = dict(lr=1.0e-3, rank=4, thin_matrix_route="scalar", thin_matrix_max_width=64, min_spectral_size=1)
-HALF_CASES = {
+EXTRA_CASES = {
     "spec16_31x37_f16": ((31, 37), _REF_SPEC16, 2, 8642, 0.05, 0.05, "float16"),
     "spec16_31x37_bf16": ((31, 37), _REF_SPEC16, 2, 8643, 0.05, 0.05, "bfloat16"),
     "scal16_64x16_f16": ((64, 16), _REF_SCAL16, 2, 3579, 0.05, 0.05, "float16"),
@@ -84,6 +86,15 @@ HALF_CASES = {
     "spec16_256x256_bf16_wd": ((256, 256), dict(rank=8, hash_bins=64, hash_tables=2, weight_decay=0.01),
                                3, 31, 0.02, 1e-3, "bfloat16"),
     "scal16_16x4096_f16": ((16, 4096), dict(rank=4, hash_bins=64, hash_tables=2), 3, 32, 0.01, 1e-3, "float16"),
+    "nd_16x8x3x3": ((16, 8, 3, 3), dict(rank=8, hash_bins=64, hash_tables=2), 3, 41, 0.02, 1e-3, "float32"),
+    "nd_8x6x40_wd_local": ((8, 6, 40), dict(rank=8, hash_bins=37, hash_tables=2, weight_decay=0.01,
+                                            local_sharpness=0.3, maximize=True), 3, 42, 0.02, 1e-3, "float32"),
+    "nd_3x4x5x6x7_r16": ((3, 4, 5, 6, 7), dict(rank=16, max_frequency=3, hash_bins=16, hash_tables=3,
+                                               warmup_steps=0), 3, 43, 0.02, 1e-3, "float32"),
+    "nd_4x64x256": ((4, 64, 256), dict(rank=8, hash_bins=64, hash_tables=2, instant_metric_power=0.7), 3, 44,
+                    0.02, 1e-3, "float32"),
+    "nd_32x16x5x5_bf16": ((32, 16, 5, 5), dict(rank=4, hash_bins=64, hash_tables=1), 3, 45, 0.02, 1e-3,
+                          "bfloat16"),
 }
 
 
@@ -120,14 +131,14 @@ def main() -> None:
     ref = load_reference(root)
     torch.set_num_threads(1)
 
-    half: dict[str, np.ndarray] = {}
-    for name, (shape, kwargs, steps, seed, istd, gstd, dt) in HALF_CASES.items():
+    extra: dict[str, np.ndarray] = {}
+    for name, (shape, kwargs, steps, seed, istd, gstd, dt) in EXTRA_CASES.items():
         out = run_steps(ref, shape, kwargs, steps, seed, istd, gstd, getattr(torch, dt))
         for k, v in out.items():
-            half[f"step_{name}_{k}"] = v
-    np.savez_compressed(HERE / "golden_half.npz", **half)
-    print("wrote", HERE / "golden_half.npz", len(half), "arrays")
-    if "--half-only" in sys.argv:
+            extra[f"step_{name}_{k}"] = v
+    np.savez_compressed(HERE / "golden_extra.npz", **extra)
+    print("wrote", HERE / "golden_extra.npz", len(extra), "arrays")
+    if "--extra-only" in sys.argv:
         return
 
     data: dict[str, np.ndarray] = {}

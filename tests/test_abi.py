@@ -44,9 +44,11 @@ def test_argument_errors_are_reported_not_raised():
     assert "bins" in _lib.last_error()
     with pytest.raises(RuntimeError, match="invalid argument"):
         _lib.check(lib.cresso_hash_index(0, -1, 64, 0, None, None), "hash_index")
+    dims = _lib.i64_array([2] * 9)
+    assert lib.cresso_shape_workspace_bytes(9, dims, 8, 64, 2, n.ctypes.data_as(_lib._pi64)) == 2
+    assert "rank 1 to 8" in _lib.last_error()
     dims = _lib.i64_array([4, 5, 6])
-    assert lib.cresso_shape_workspace_bytes(3, dims, 8, 64, 2, n.ctypes.data_as(_lib._pi64)) == 2
-    assert "1-D and 2-D" in _lib.last_error()
+    assert lib.cresso_shape_workspace_bytes(3, dims, 8, 64, 2, n.ctypes.data_as(_lib._pi64)) == 0
     dims = _lib.i64_array([64, 64])
     assert lib.cresso_shape_workspace_bytes(2, dims, 17, 64, 2, n.ctypes.data_as(_lib._pi64)) == 2
     assert lib.cresso_shape_workspace_bytes(2, dims, 8, 64, 2, n.ctypes.data_as(_lib._pi64)) == 0

@@ -96,3 +96,22 @@ def test_projection_large_shape_against_float64(ops):
     scale = float(torch.cat([c64, s64]).abs().max())
     assert float((c.cpu().double() - c64).abs().max()) <= 1e-5 * scale
     assert float((s.cpu().double() - s64).abs().max()) <= 1e-5 * scale
+
+
+@pytest.mark.parametrize("shape,rank", [((6, 5, 7), 8), ((3, 4, 5, 6), 16), ((2, 3, 2, 3, 40), 12)])
+def test_basis_rank3_plus_against_oracle(ops, shape, rank):
+    """Carriers of tensors of rank 3 to 5 (leading axes composed into the row
+    table) against the oracle's direct evaluation, in float64, of the
+    reference formula (cresso_v5.py:295-348); the oracle's full steps on such
+    tensors match the reference bit for bit.  Reference tolerances."""
+    g = torch.Generator().manual_seed(7)
+    x = torch.randn(shape, generator=g) * 0.5 + 0.2
+    freqs = O.freqs_tensor(rank, len(shape), 5)
+    c64, s64 = O.project(x.double(), freqs)
+    c, s = ops.basis_project(x.cuda(), rank, 5)
+    np.testing.assert_allclose(c.cpu().double().numpy(), c64.numpy(), rtol=2e-4, atol=2e-5)
+    np.testing.assert_allclose(s.cpu().double().numpy(), s64.numpy(), rtol=2e-4, atol=2e-5)
+    gates = torch.sigmoid(torch.linspace(-2.0, 2.0, rank))
+    rec64 = O.reconstruct(c64, s64, freqs, shape, torch.float64, gates.double())
+    rec = ops.basis_reconstruct(c64.float().cuda(), s64.float().cuda(), shape, 5, gates.cuda())
+    np.testing.assert_allclose(rec.cpu().double().numpy(), rec64.numpy(), rtol=4e-4, atol=4e-5)

@@ -22,7 +22,7 @@ import torch
 
 import cresso_b200
 from oracle import cresso5_oracle as O
-from tests._cases import case_inputs, golden_cases, half_case_inputs, half_cases, rel_rms, ulp_distance
+from tests._cases import case_inputs, extra_case_inputs, extra_cases, golden_cases, rel_rms, ulp_distance
 
 pytestmark = pytest.mark.gpu
 
@@ -88,24 +88,29 @@ def test_golden_case_parity(golden, name):
     assert cresso_b200.count_optimizer_state_elements(opt) == int(golden[f"step_{name}_state_elements"])
 
 
-HALF_CASES = half_cases()
+EXTRA_CASES = extra_cases()
 
 
-@pytest.mark.parametrize("name", list(HALF_CASES.keys()))
-def test_half_golden_parity(golden_half, name):
-    """float16 / bfloat16 parameters (spectral and scalar routes) against the
-    reference's own output.  Parameters: every element within one unit in the
-    last place of the parameter type per step (at the tensor's scale; a
-    difference feeds the next step's force through weight decay) and a mean distance
-    of at most 0.15 of that unit: the update is rounded to the parameter type
-    before the add and the sum rounded again, so a float32-level difference in
-    an update (the drive mixes terms that partly cancel) can move a rounding by
-    one unit; the reference's own 16-bit tests allow 3e-3 (float16) and 3e-2
+@pytest.mark.parametrize("name", list(EXTRA_CASES.keys()))
+def test_extra_golden_parity(golden_extra, name):
+    """The second golden table against the reference's own output: float16 /
+    bfloat16 parameters (spectral and scalar routes) and spectral tensors of
+    rank 3 to 5 (leading axes flattened into rows, carriers and the instant
+    metric composed over every axis).
+
+    float32 parameters: the criterion of the float32 golden cases.  16-bit
+    parameters: every element within one unit in the last place of the
+    parameter type per step (at the tensor's scale; a difference feeds the
+    next step's force through weight decay) and a mean distance of at most
+    0.15 of that unit: the update is rounded to the parameter type before the
+    add and the sum rounded again, so a float32-level difference in an update
+    (the drive mixes terms that partly cancel) can move a rounding by one
+    unit; the reference's own 16-bit tests allow 3e-3 (float16) and 3e-2
     (bfloat16) absolute on parameters of scale 0.05.  States (float32): the
-    criterion of the float32 tests, against a float64 run from the same 16-bit
+    criterion of the float32 tests, against a float64 run from the same
     inputs."""
-    shape, kw, steps, seed, istd, gstd, dt = HALF_CASES[name]
-    init, grads = half_case_inputs(golden_half, name, shape, steps, seed, istd, gstd, dt)
+    shape, kw, steps, seed, istd, gstd, dt = EXTRA_CASES[name]
+    init, grads = extra_case_inputs(golden_extra, name, shape, steps, seed, istd, gstd, dt)
     p = torch.nn.Parameter(init.clone().cuda())
     opt = cresso_b200.CRESSO5([p], cuda_ops="required", **kw)
     for g in grads:
@@ -114,14 +119,23 @@ def test_half_golden_parity(golden_half, name):
     torch.cuda.synchronize()
     assert p.dtype == getattr(torch, dt)
     assert opt._device_status() == 0
+    ref = golden_extra[f"step_{name}_final"]
+    p64, st64 = run_oracle(kw, init.float(), [g.float() for g in grads], torch.float64)
+    st_ref = {k[len(f"step_{name}_state_"):]: golden_extra[k] for k in golden_extra
+              if k.startswith(f"step_{name}_state_") and k != f"step_{name}_state_elements"}
+    assert set(opt.state[p].keys()) == set(st_ref.keys())
+    assert cresso_b200.count_optimizer_state_elements(opt) == int(golden_extra[f"step_{name}_state_elements"])
+    if dt == "float32":
+        st_ref = {k: (torch.from_numpy(v) if v.ndim > 0 or v.dtype.kind == "f" else int(v)) for k, v in st_ref.items()}
+        st = {k: (v.detach().cpu() if torch.is_tensor(v) else v) for k, v in opt.state[p].items()}
+        check_against(name, init, p.detach().cpu(), st, torch.from_numpy(ref), st_ref, p64, st64)
+        return
     got = p.detach().float().cpu().numpy()
-    ref = golden_half[f"step_{name}_final"]
     ulps = ulp_distance(got, ref, dt)
     assert ulps.max() <= steps, (name, float(ulps.max()))  # at most one unit per step
     assert float(np.mean(ulps)) <= 0.15, (name, float(np.mean(ulps)), float(np.mean(ulps > 0)))
-    _, st64 = run_oracle(kw, init.float(), [g.float() for g in grads], torch.float64)
     for k, v in opt.state[p].items():
-        ref_v = golden_half[f"step_{name}_state_{k}"]
+        ref_v = st_ref[k]
         if not torch.is_tensor(v):
             assert v == int(ref_v), (name, k)
             continue

@@ -6,7 +6,7 @@ import pytest
 import torch
 
 from oracle import cresso5_oracle as O
-from tests._cases import case_inputs, golden_cases, half_case_inputs, half_cases
+from tests._cases import case_inputs, extra_case_inputs, extra_cases, golden_cases
 
 
 def test_frequency_pack_matches_reference(golden):
@@ -87,22 +87,23 @@ def test_full_steps_bit_exact(golden, name):
     assert O.count_state_elements(opt.state) == int(golden[f"step_{name}_state_elements"])
 
 
-@pytest.mark.parametrize("name", list(half_cases().keys()))
-def test_half_steps_bit_exact(golden_half, name):
-    """float16 / bfloat16 parameters: the oracle reproduces the reference bit for bit
-    (fp32 work and state, update rounded to the parameter type before the add)."""
+@pytest.mark.parametrize("name", list(extra_cases().keys()))
+def test_extra_steps_bit_exact(golden_extra, name):
+    """float16 / bfloat16 parameters (fp32 work and state, update rounded to the
+    parameter type before the add) and spectral tensors of rank 3 to 5: the
+    oracle reproduces the reference bit for bit."""
     torch.set_num_threads(1)
-    shape, kw, steps, seed, istd, gstd, dt = half_cases()[name]
-    init, grads = half_case_inputs(golden_half, name, shape, steps, seed, istd, gstd, dt)
+    shape, kw, steps, seed, istd, gstd, dt = extra_cases()[name]
+    init, grads = extra_case_inputs(golden_extra, name, shape, steps, seed, istd, gstd, dt)
     p = torch.nn.Parameter(init.clone())
     opt = O.OracleCRESSO5([p], **kw)
     for g in grads:
         p.grad = g.clone()
         opt.step()
     assert p.dtype == getattr(torch, dt)
-    np.testing.assert_array_equal(p.detach().float().numpy(), golden_half[f"step_{name}_final"])
+    np.testing.assert_array_equal(p.detach().float().numpy(), golden_extra[f"step_{name}_final"])
     for k, v in opt.state[p].items():
-        ref = golden_half[f"step_{name}_state_{k}"]
+        ref = golden_extra[f"step_{name}_state_{k}"]
         got = v.numpy() if torch.is_tensor(v) else np.asarray(v)
         if torch.is_tensor(v) and torch.is_floating_point(v):
             assert v.dtype == torch.float32, k
