@@ -26,7 +26,7 @@ HPARAM_FIELDS = (
     "confidence_decay", "confidence_gain", "surprise_gain", "surprise_decay", "prediction_mix", "novelty_mix",
     "warmup_steps", "surprise_brake", "target_update_rms", "min_gain", "max_gain", "drive_clip", "spike_mix",
     "eps", "maximize", "rank", "max_frequency", "hash_bins", "hash_tables", "hard_channel_min_size",
-    "thin_matrix_hard_cutoff",
+    "thin_matrix_hard_cutoff", "micro_decay", "micro_impulse_decay", "micro_drive_mix",
 )
 
 MAX_NDIM = 8
@@ -42,7 +42,8 @@ DESC_FIELDS = (
     + ["row0", "rows", "col0", "cols", "step", "param", "grad", "shape_ws", "hash_cache", "hash_cache_n",
        "omega", "q_cos", "q_sin", "p_cos", "p_sin", "metric_cos", "metric_sin", "metric_p_cos", "metric_p_sin",
        "calcium_cos", "calcium_sin", "mode_confidence", "hash_energy", "hash_impulse", "hash_refractory",
-       "force_rms", "drive_energy", "surprise", "action", "q", "impulse", "metric_q", "metric_impulse", "dtype"]
+       "force_rms", "drive_energy", "surprise", "action", "q", "impulse", "metric_q", "metric_impulse", "dtype",
+       "micro_energy", "micro_impulse", "micro_refractory"]
 )
 DTYPE_CODES = {"float32": 0, "float16": 1, "bfloat16": 2}
 DESC_INDEX = {name: i for i, name in enumerate(DESC_FIELDS)}
@@ -56,7 +57,7 @@ EXPORTS = (
     "cresso_hash_cache_init", "cresso_shape_workspace_bytes", "cresso_shape_workspace_init",
     "cresso_basis_project", "cresso_basis_reconstruct", "cresso_instant_axis_metric",
     "cresso_spectral_layout", "cresso_spectral_run", "cresso_scalar_scratch_bytes", "cresso_scalar_run",
-    "cresso_scalar_run_noalloc",
+    "cresso_scalar_run_noalloc", "cresso_micro_scratch_bytes", "cresso_micro_run",
 )
 
 _lock = threading.Lock()
@@ -91,6 +92,8 @@ def _declare(lib) -> None:
         "cresso_scalar_scratch_bytes": (ctypes.c_int, [_p, _i64, _pi64]),
         "cresso_scalar_run": (ctypes.c_int, [_p, _i64, _p, _p, _i64, _p]),
         "cresso_scalar_run_noalloc": (ctypes.c_int, [_p, _i64, _p, _p]),
+        "cresso_micro_scratch_bytes": (ctypes.c_int, [_p, _i64, _pi64]),
+        "cresso_micro_run": (ctypes.c_int, [_p, _i64, _p, _p, _i64, _p]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)

@@ -1,10 +1,14 @@
 // Shared device / host helpers of the B200 CRESSO5 kernels.
 #pragma once
 
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
 #include <cmath>
+
+#include "../../include/cresso_b200.h"
 
 namespace cresso {
 
@@ -187,6 +191,40 @@ __device__ __forceinline__ float sqrt_sfu(float x) {
 __device__ __forceinline__ float reservoir(float old, float cur, double decay, int64_t step) {
     if (step <= 1) return cur;
     return old * (float)decay + cur * (float)(1.0 - decay);
+}
+
+// Element e of a parameter / gradient of type dt (float32 work, cresso_v5.py:119-124).
+// -lr rounded (once, from double) to the parameter type dt; float32: -lr.
+__device__ __forceinline__ float neg_lr_in(double lr, int dt) {
+    if (dt == CRESSO_DTYPE_F16) return __half2float(__double2half(-lr));
+    if (dt == CRESSO_DTYPE_BF16) return __bfloat162float(__double2bfloat16(-lr));
+    return (float)(-lr);
+}
+
+__device__ __forceinline__ float load_elem(const void* p, int64_t e, int dt) {
+    if (dt == CRESSO_DTYPE_F16) return __half2float(reinterpret_cast<const __half*>(p)[e]);
+    if (dt == CRESSO_DTYPE_BF16) return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p)[e]);
+    return __ldg(reinterpret_cast<const float*>(p) + e);
+}
+// param.add_(update.to(param.dtype), alpha=-lr)  (cresso_v5.py:1582).  float32:
+// p + (-lr) u.  16-bit: round(p + round(-lr) round(u)), every rounding to the
+// parameter's type, as PyTorch's vectorised CPU kernel computes it (alpha
+// converted to the tensor's type, the sum formed in float32); neg_lr16 is
+// -lr rounded to that type.
+__device__ __forceinline__ void apply_update(void* p, int64_t e, int dt, float neg_lr, float neg_lr16,
+                                             float update) {
+    if (dt == CRESSO_DTYPE_F16) {
+        __half* h = reinterpret_cast<__half*>(p);
+        const float u = __half2float(__float2half_rn(update));
+        h[e] = __float2half_rn(__half2float(h[e]) + neg_lr16 * u);
+    } else if (dt == CRESSO_DTYPE_BF16) {
+        __nv_bfloat16* h = reinterpret_cast<__nv_bfloat16*>(p);
+        const float u = __bfloat162float(__float2bfloat16_rn(update));
+        h[e] = __float2bfloat16_rn(__bfloat162float(h[e]) + neg_lr16 * u);
+    } else {
+        float* f = reinterpret_cast<float*>(p);
+        f[e] = f[e] + neg_lr * update;
+    }
 }
 
 }  // namespace cresso

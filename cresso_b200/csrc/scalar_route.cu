@@ -40,40 +40,6 @@ struct ScalTensor {
     int32_t split_rows, ctc, crpi, dtype;
 };
 
-// Element e of a parameter / gradient of type dt (float32 work, cresso_v5.py:119-124).
-// -lr rounded (once, from double) to the parameter type dt; float32: -lr.
-__device__ __forceinline__ float neg_lr_in(double lr, int dt) {
-    if (dt == CRESSO_DTYPE_F16) return __half2float(__double2half(-lr));
-    if (dt == CRESSO_DTYPE_BF16) return __bfloat162float(__double2bfloat16(-lr));
-    return (float)(-lr);
-}
-
-__device__ __forceinline__ float load_elem(const void* p, int64_t e, int dt) {
-    if (dt == CRESSO_DTYPE_F16) return __half2float(reinterpret_cast<const __half*>(p)[e]);
-    if (dt == CRESSO_DTYPE_BF16) return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p)[e]);
-    return __ldg(reinterpret_cast<const float*>(p) + e);
-}
-// param.add_(update.to(param.dtype), alpha=-lr)  (cresso_v5.py:1582).  float32:
-// p + (-lr) u.  16-bit: round(p + round(-lr) round(u)), every rounding to the
-// parameter's type, as PyTorch's vectorised CPU kernel computes it (alpha
-// converted to the tensor's type, the sum formed in float32); neg_lr16 is
-// -lr rounded to that type.
-__device__ __forceinline__ void apply_update(void* p, int64_t e, int dt, float neg_lr, float neg_lr16,
-                                             float update) {
-    if (dt == CRESSO_DTYPE_F16) {
-        __half* h = reinterpret_cast<__half*>(p);
-        const float u = __half2float(__float2half_rn(update));
-        h[e] = __float2half_rn(__half2float(h[e]) + neg_lr16 * u);
-    } else if (dt == CRESSO_DTYPE_BF16) {
-        __nv_bfloat16* h = reinterpret_cast<__nv_bfloat16*>(p);
-        const float u = __bfloat162float(__float2bfloat16_rn(update));
-        h[e] = __float2bfloat16_rn(__bfloat162float(h[e]) + neg_lr16 * u);
-    } else {
-        float* f = reinterpret_cast<float*>(p);
-        f[e] = f[e] + neg_lr * update;
-    }
-}
-
 struct ScalHdr {
     int64_t n;
     double hp[64];

@@ -115,7 +115,7 @@ enum HP {
     H_LR, H_WD, H_EP, H_DT, H_IF, H_CG, H_REST, H_CUBIC, H_MDT, H_MF, H_MC, H_LS, H_IC, H_IP, H_RCM, H_EM, H_TM,
     H_HD, H_HID, H_HMC, H_HDM, H_DFM, H_RFM, H_RD, H_REFD, H_RG, H_CD, H_CONFG, H_SG, H_SD, H_PM, H_NM, H_WS, H_SB,
     H_TGT, H_MING, H_MAXG, H_CLIP, H_SPIKE, H_EPS, H_MAX, H_RANK, H_MAXF, H_BINS, H_TABLES, H_HARDMIN, H_THINCUT,
-    H_COUNT
+    H_MD, H_MID, H_MDM, H_COUNT
 };
 static_assert(sizeof(cresso_hparams) == H_COUNT * sizeof(double), "cresso_hparams field order");
 

@@ -213,6 +213,7 @@ class CRESSO5(Optimizer):
         # table of the last step with the identities it was built from
         self._route_cache: Dict[tuple, bool] = {}
         self._scalar_descs: Dict[object, tuple] = {}
+        self._micro_descs: Dict[object, tuple] = {}
 
     # ------------------------------------------------------------------ state
     def _init_common(self, state: dict, device, dtype) -> None:
@@ -277,6 +278,14 @@ class CRESSO5(Optimizer):
         self._init_common(state, param.device, dtype)
         for name in ("q", "impulse", "metric_q", "metric_impulse"):
             state[name] = torch.zeros((), device=param.device, dtype=dtype)
+
+    def _init_micro(self, param: Tensor, dtype) -> None:
+        """cresso_v5.py:893-898: per-element float32 fields of the parameter's shape."""
+        state = self.state[param]
+        self._init_common(state, param.device, dtype)
+        state["micro_energy"] = torch.ones_like(param, dtype=dtype, memory_format=torch.preserve_format)
+        state["micro_impulse"] = torch.zeros_like(param, dtype=dtype, memory_format=torch.preserve_format)
+        state["micro_refractory"] = torch.zeros_like(param, dtype=dtype, memory_format=torch.preserve_format)
 
     def _use_spectral_route(self, param: Tensor, group: dict) -> bool:
         return uses_spectral_route(self._geometry(param)[0], group)
@@ -343,6 +352,7 @@ class CRESSO5(Optimizer):
         for group in self.param_groups:
             spectral: Dict[torch.device, list] = {}
             scalar: Dict[torch.device, list] = {}
+            micro_items: Dict[torch.device, list] = {}
             route_sig = (group["min_spectral_size"], group["rank"], group.get("thin_matrix_route", "scalar"),
                          group.get("thin_matrix_max_width", 64), group.get("thin_matrix_min_aspect", 4.0))
             micro = int(group.get("micro_field_max_size", 0))
@@ -355,9 +365,6 @@ class CRESSO5(Optimizer):
                 if not param.is_cuda:
                     raise RuntimeError(
                         "CRESSO5 cuda_ops='required' requires every optimized parameter to be a CUDA parameter")
-                if micro > 0 and param.ndim > 0 and param.numel() <= micro:
-                    raise RuntimeError("CRESSO5 micro-field route (micro_field_max_size > 0) is not available on "
-                                       "the B200 CUDA path")
                 if param.dtype not in _DTYPES:
                     raise RuntimeError("CRESSO5 B200 path supports float32, float16 and bfloat16 parameters "
                                        f"(got {param.dtype})")
@@ -368,6 +375,14 @@ class CRESSO5(Optimizer):
                 if not grad.is_contiguous():
                     grad = grad.contiguous()
                 state = self.state[param]
+                if micro > 0 and param.ndim > 0 and param.numel() <= micro:  # cresso_v5.py:839-840
+                    if getattr(param, "_cresso_shard", None) is not None:
+                        raise RuntimeError("micro-field tensors are not sharded: pass them whole")
+                    if len(state) == 0:
+                        self._init_micro(param, torch.float32)
+                    state["step"] += 1
+                    micro_items.setdefault(param.device, []).append((param, grad, state))
+                    continue
                 rkey = (param.shape, getattr(param, "_cresso_shard", None), route_sig)
                 spectral_route = self._route_cache.get(rkey)
                 if spectral_route is None:
@@ -391,6 +406,9 @@ class CRESSO5(Optimizer):
             for device, items in scalar.items():
                 hp = _lib.pack_hparams(group) if hp is None else hp
                 self._run_scalar(hp, device, items)
+            for device, items in micro_items.items():
+                hp = _lib.pack_hparams(group) if hp is None else hp
+                self._run_micro(hp, device, items)
         return loss
 
     def _spectral_descs(self, group: dict, device, items: list) -> np.ndarray:
@@ -460,42 +478,64 @@ class CRESSO5(Optimizer):
         off, length = int(layout[2 * k - 1]), int(layout[2 * k])
         return scratch[off:off + 8 * length].view(torch.float64)
 
-    def _run_scalar(self, hp: np.ndarray, device, items: list) -> None:
-        L = _lib.lib()
+    def _small_route_descs(self, cache: dict, device, items: list, state_names: Tuple[str, ...],
+                           bytes_fn: Callable, what: str) -> Tuple[np.ndarray, int]:
+        """Descriptor table of the scalar or the micro route.  It depends on the
+        parameters, their storage and their state tensors and is reused while those
+        stay the same; the gradient pointers and step counters change from step to
+        step and are refreshed every time.  The cache entry holds references to the
+        parameters, state dicts and state tensors it points at, so none of them can
+        be freed (and its id or device address reused) while the entry lives."""
         F = _lib.DESC_INDEX
         n = len(items)
-        # the descriptor table depends on the parameters, their storage and their state
-        # tensors; reuse it while those stay the same and refresh the gradient pointers and
-        # step counters, which change from step to step
         ident = tuple((id(p), p.data_ptr(), p.shape, id(st)) for p, g, st in items)
-        cached = self._scalar_descs.get(device)
+        cached = cache.get(device)
         if cached is not None and cached[0] == ident:
             descs, nbytes = cached[1], cached[2]
         else:
             descs = _lib.new_descs(n)
+            keep = []
             for i, (p, g, st) in enumerate(items):
                 d = descs[i]
                 d[F["ndim"]] = p.ndim
-                for a, s in enumerate(p.shape):
-                    d[F["shape0"] + a] = int(s)
+                for a, sz in enumerate(p.shape):
+                    d[F["shape0"] + a] = int(sz)
                 d[F["param"]] = p.data_ptr()
                 d[F["dtype"]] = _DTYPES[p.dtype]
-                for name in ("force_rms", "drive_energy", "surprise", "action", "q", "impulse", "metric_q",
-                             "metric_impulse"):
+                for name in state_names:
                     d[F[name]] = st[name].data_ptr()
+                keep.append((p, st, [st[name] for name in state_names]))
             descs[:, F["grad"]] = [g.data_ptr() for _, g, _ in items]
             descs[:, F["step"]] = [int(st["step"]) for _, _, st in items]
             nb = np.zeros(1, dtype=np.int64)
-            _lib.check(L.cresso_scalar_scratch_bytes(_lib.ptr(descs), n, nb.ctypes.data_as(_lib._pi64)),
-                       "scalar_scratch_bytes")
+            _lib.check(bytes_fn(_lib.ptr(descs), n, nb.ctypes.data_as(_lib._pi64)), what)
             nbytes = int(nb[0])
-            self._scalar_descs[device] = (ident, descs, nbytes)
+            cache[device] = (ident, descs, nbytes, keep)
         descs[:, F["grad"]] = [g.data_ptr() for _, g, _ in items]
         descs[:, F["step"]] = [st["step"] for _, _, st in items]
+        return descs, nbytes
+
+    def _run_scalar(self, hp: np.ndarray, device, items: list) -> None:
+        L = _lib.lib()
+        descs, nbytes = self._small_route_descs(
+            self._scalar_descs, device, items,
+            ("force_rms", "drive_energy", "surprise", "action", "q", "impulse", "metric_q", "metric_impulse"),
+            L.cresso_scalar_scratch_bytes, "scalar_scratch_bytes")
         scratch = self._scratch_buffer(device, "scalar", nbytes)
         stream = torch.cuda.current_stream(device).cuda_stream
-        _lib.check(L.cresso_scalar_run(_lib.ptr(descs), n, _lib.ptr(hp), _lib.ptr(scratch), scratch.numel(), stream),
-                   "scalar_run")
+        _lib.check(L.cresso_scalar_run(_lib.ptr(descs), len(items), _lib.ptr(hp), _lib.ptr(scratch), scratch.numel(),
+                                       stream), "scalar_run")
+
+    def _run_micro(self, hp: np.ndarray, device, items: list) -> None:
+        L = _lib.lib()
+        descs, nbytes = self._small_route_descs(
+            self._micro_descs, device, items,
+            ("force_rms", "drive_energy", "surprise", "micro_energy", "micro_impulse", "micro_refractory"),
+            L.cresso_micro_scratch_bytes, "micro_scratch_bytes")
+        scratch = self._scratch_buffer(device, "micro", nbytes)
+        stream = torch.cuda.current_stream(device).cuda_stream
+        _lib.check(L.cresso_micro_run(_lib.ptr(descs), len(items), _lib.ptr(hp), _lib.ptr(scratch), scratch.numel(),
+                                      stream), "micro_run")
 
 
 CRESSO = CRESSO5

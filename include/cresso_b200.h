@@ -48,7 +48,7 @@ enum { CRESSO_MAX_NDIM = 8, CRESSO_MAX_RANK = 16 };
 /* Hyper-parameters of one parameter group.  Mirrors the `defaults` dict of
  * CRESSO5.__init__ (reference cresso_v5.py:760-818); integer options are
  * stored as doubles.  Keys that only steer host routing (min_spectral_size,
- * thin_matrix_* and the micro-field keys) are not read by the kernels. */
+ * thin_matrix_*, micro_field_max_size) are not read by the kernels. */
 typedef struct cresso_hparams {
     double lr, weight_decay, energy_power, dt, impulse_friction, contact_gain, restoring, cubic;
     double metric_dt, metric_friction, metric_coupling, local_sharpness;
@@ -59,6 +59,7 @@ typedef struct cresso_hparams {
     double warmup_steps, surprise_brake, target_update_rms, min_gain, max_gain, drive_clip, spike_mix;
     double eps, maximize, rank, max_frequency, hash_bins, hash_tables, hard_channel_min_size;
     double thin_matrix_hard_cutoff;
+    double micro_decay, micro_impulse_decay, micro_drive_mix; /* micro-field route */
 } cresso_hparams;
 
 /* One parameter tensor handed to a group step.  `shape` is the GLOBAL shape.
@@ -88,6 +89,8 @@ typedef struct cresso_tensor_desc {
      * update rounded to its type first, as param.add_(update.to(param.dtype))
      * does (cresso_v5.py:119-124, 1353, 1582) */
     int64_t dtype;
+    /* micro-field route state: float32 fields of the parameter's shape */
+    uint64_t micro_energy, micro_impulse, micro_refractory;
 } cresso_tensor_desc;
 
 enum { CRESSO_DTYPE_F32 = 0, CRESSO_DTYPE_F16 = 1, CRESSO_DTYPE_BF16 = 2 };
@@ -140,7 +143,9 @@ CRESSO_API int cresso_hash_cache_init(int64_t n, int64_t bins, int64_t tables, v
  * cu:842-932) and the transient per-step _CudaBasisCache (cresso_v5.py:100-107,
  * 380-415); the caller keeps it across steps (never in state_dict).
  * freqs: host int64 [rank][ndim] = state["freqs"].  bins / tables = 0 skips
- * the counts.  Supports ndim 1 and 2, rank 1..CRESSO_MAX_RANK. */
+ * the counts.  Supports ndim 1..CRESSO_MAX_NDIM (a tensor of rank n >= 2 is
+ * laid out as (product of its n - 1 leading axes) x (last axis)), rank
+ * 1..CRESSO_MAX_RANK. */
 CRESSO_API int cresso_shape_workspace_bytes(int64_t ndim, const int64_t* shape, int64_t rank, int64_t bins,
                                  int64_t tables, int64_t* bytes);
 CRESSO_API int cresso_shape_workspace_init(int64_t ndim, const int64_t* shape, int64_t rank, const int64_t* freqs,
@@ -208,6 +213,18 @@ CRESSO_API int cresso_spectral_run(const cresso_tensor_desc* descs, int64_t n, c
 CRESSO_API int cresso_scalar_scratch_bytes(const cresso_tensor_desc* descs, int64_t n, int64_t* bytes);
 CRESSO_API int cresso_scalar_run(const cresso_tensor_desc* descs, int64_t n, const cresso_hparams* hp, void* scratch,
                       int64_t scratch_bytes, cresso_stream_t stream);
+
+/* ------------------------------------------------------- micro route ---- */
+
+/* Fused micro-field step of n small tensors (cresso_v5.py:1355-1432, the
+ * route of every tensor with 0 < numel <= micro_field_max_size and rank >= 1):
+ * per-element energy / impulse / refractory fields (micro_* in the
+ * descriptor), one thread block per tensor, all tensors in one launch.  The
+ * reference has this route on its PyTorch path only.  Tensors are never
+ * sharded. */
+CRESSO_API int cresso_micro_scratch_bytes(const cresso_tensor_desc* descs, int64_t n, int64_t* bytes);
+CRESSO_API int cresso_micro_run(const cresso_tensor_desc* descs, int64_t n, const cresso_hparams* hp, void* scratch,
+                                int64_t scratch_bytes, cresso_stream_t stream);
 
 /* ---------------------------------------------- allocation-free entry ---- */
 

@@ -10,8 +10,8 @@ golden vectors in ``tests/golden`` (made by running the reference itself) pin
 that claim.  It runs on any torch device and in float32 or float64, which gives
 the tests a float64 "truth" run to measure the float32 noise floor.
 
-The micro-field route (``micro_field_max_size > 0``, ``cresso_v5.py:1355-1432``)
-is outside the hot path and is not restated.
+Routes: spectral (``cresso_v5.py:945-1353``), scalar (``:1434-1582``) and the
+micro field (``micro_field_max_size > 0``, ``:1355-1432``).
 """
 
 from __future__ import annotations
@@ -466,6 +466,15 @@ def init_spectral(param: Tensor, hp, dtype) -> Dict:
     return st
 
 
+def init_micro(param: Tensor, dtype) -> Dict:
+    """Per-element energy / impulse / refractory fields.  cresso_v5.py:893-898."""
+    st = init_common(param.device, dtype)
+    st["micro_energy"] = torch.ones_like(param.detach(), dtype=dtype, memory_format=torch.preserve_format)
+    st["micro_impulse"] = torch.zeros_like(param.detach(), dtype=dtype, memory_format=torch.preserve_format)
+    st["micro_refractory"] = torch.zeros_like(param.detach(), dtype=dtype, memory_format=torch.preserve_format)
+    return st
+
+
 def init_scalar(param: Tensor, dtype) -> Dict:
     st = init_common(param.device, dtype)
     for name in ("q", "impulse", "metric_q", "metric_impulse"):
@@ -747,6 +756,68 @@ def scalar_step(param: Tensor, grad: Tensor, st: Dict, hp) -> None:
 
 
 # ---------------------------------------------------------------------------
+# Micro-field route for small tensors (cresso_v5.py:1355-1432)
+# ---------------------------------------------------------------------------
+
+def micro_step(param: Tensor, grad: Tensor, st: Dict, hp) -> None:
+    dtype = work_dtype(param.dtype)
+    if len(st) == 0:
+        st.update(init_micro(param, work_dtype(dtype)))
+    st["step"] += 1
+    step = int(st["step"])
+    eps = float(hp["eps"])
+    force = base_force(param, grad, hp, dtype)
+    frn = torch.sqrt(force.pow(2).mean() + eps)
+    st["force_rms"] = reservoir(st["force_rms"], frn, hp["reservoir_decay"], step)
+    scale = st["force_rms"].to(dtype).clamp_min(eps)
+    rel = (force.abs() / scale + eps).clamp(max=1.0e4)
+
+    # energy field and its metric (cresso_v5.py:1380-1392)
+    e, imp, ref = st["micro_energy"], st["micro_impulse"], st["micro_refractory"]
+    density = rel.pow(float(hp["energy_power"]))
+    if step <= 1:
+        e.copy_(density.to(e.dtype))
+    else:
+        e.mul_(float(hp["micro_decay"])).add_(density.to(e.dtype), alpha=1.0 - float(hp["micro_decay"]))
+    expo = float(hp["hash_metric_coupling"]) / max(0.25, float(hp["energy_power"]))
+    metric = (e.to(dtype) / e.to(dtype).mean().clamp_min(eps)).pow(expo).clamp(0.08, 12.0)
+    instant = instant_axis_metric(rel, float(hp["instant_metric_power"]),
+                                  min(0.35, float(hp["instant_metric_coupling"])), eps)
+    tangent = (force / (scale * metric * instant + eps)).clamp(-1.0e4, 1.0e4)
+
+    # refractory-gated impulse, prediction, surprise (cresso_v5.py:1394-1404)
+    ref.mul_(float(hp["refractory_decay"])).add_(tangent.abs().to(ref.dtype), alpha=1.0 - float(hp["refractory_decay"]))
+    gate = 1.0 / (1.0 + float(hp["refractory_gain"]) * ref.to(dtype))
+    port = tangent * gate
+    imp.mul_(float(hp["micro_impulse_decay"])).add_(port.to(imp.dtype), alpha=1.0 - float(hp["micro_impulse_decay"]))
+    pred = imp.to(dtype)
+    error = tangent - pred
+    sn = torch.sqrt(error.pow(2).mean() + eps)
+    st["surprise"] = reservoir(st["surprise"], sn, hp["surprise_decay"], step)
+
+    # drive and update (cresso_v5.py:1406-1432)
+    clip = float(hp["drive_clip"])
+    bounded = torch.tanh(tangent / clip) * clip
+    rational = tangent / (1.0 + tangent.abs() / clip)
+    s = st["surprise"].to(dtype)
+    spike = float(hp["spike_mix"]) / (1.0 + s)
+    shaped = (1.0 - spike) * rational + spike * bounded
+    pred_norm = rms_normalize(pred, torch.sqrt(shaped.pow(2).mean() + eps), eps)
+    direct_mix = float(hp["direct_force_mix"]) / (1.0 + 0.35 * s)
+    micro_mix = float(hp["micro_drive_mix"]) / (1.0 + 0.25 * s)
+    residual_mix = float(hp["residual_feedback_mix"]) / (1.0 + s)
+    direct = rms_normalize(tangent, torch.sqrt(shaped.pow(2).mean() + eps), eps)
+    residual = rms_normalize(error, torch.sqrt(shaped.pow(2).mean() + eps), eps)
+    core = (1.0 - direct_mix - 0.5 * micro_mix).clamp(0.0, 1.0)
+    drive = core * shaped + direct_mix * direct + micro_mix * pred_norm + residual_mix * residual
+    den = drive.pow(2).mean().to(st["drive_energy"].dtype)
+    st["drive_energy"] = reservoir(st["drive_energy"], den, hp["reservoir_decay"], step)
+    gain = (float(hp["target_update_rms"]) / torch.sqrt(st["drive_energy"].to(dtype) + eps)).clamp(
+        float(hp["min_gain"]), float(hp["max_gain"]))
+    param.add_((drive * gain).to(dtype=param.dtype), alpha=-float(hp["lr"]))
+
+
+# ---------------------------------------------------------------------------
 # Optimizer-shaped driver
 # ---------------------------------------------------------------------------
 
@@ -771,8 +842,8 @@ class OracleCRESSO5:
                 g = -g
             st = self.state.setdefault(p, {})
             if int(self.hp["micro_field_max_size"]) > 0 and p.ndim > 0 and p.numel() <= int(self.hp["micro_field_max_size"]):
-                raise NotImplementedError("micro-field route is outside the restated hot path")
-            if uses_spectral(tuple(p.shape), self.hp):
+                micro_step(p, g, st, self.hp)
+            elif uses_spectral(tuple(p.shape), self.hp):
                 spectral_step(p, g, st, self.hp)
             else:
                 scalar_step(p, g, st, self.hp)

@@ -95,6 +95,20 @@ EXTRA_CASES = {
                     0.02, 1e-3, "float32"),
     "nd_32x16x5x5_bf16": ((32, 16, 5, 5), dict(rank=4, hash_bins=64, hash_tables=1), 3, 45, 0.02, 1e-3,
                           "bfloat16"),
+    # micro-field route (micro_field_max_size > 0): per-element energy / impulse / refractory state
+    "micro_64x32": ((64, 32), dict(micro_field_max_size=4096), 4, 51, 0.02, 1e-3, "float32"),
+    "micro_4096_wd_max": ((4096,), dict(micro_field_max_size=4096, weight_decay=0.01, maximize=True), 3, 52, 0.02,
+                          1e-3, "float32"),
+    "micro_8x6x5_ip": ((8, 6, 5), dict(micro_field_max_size=1000, instant_metric_power=0.7,
+                                       instant_metric_coupling=0.2, micro_drive_mix=0.5), 3, 53, 0.02, 1e-3,
+                       "float32"),
+    "micro_1x1000": ((1, 1000), dict(micro_field_max_size=1000, energy_power=1.0), 3, 54, 0.02, 1e-3, "float32"),
+    "micro_3": ((3,), dict(micro_field_max_size=16), 3, 55, 0.02, 1e-3, "float32"),
+    "micro_1": ((1,), dict(micro_field_max_size=16), 3, 56, 0.02, 1e-3, "float32"),
+    "micro_64x256": ((64, 256), dict(micro_field_max_size=16384, micro_decay=0.8), 3, 57, 0.02, 1e-3, "float32"),
+    "micro_300x7_bf16": ((300, 7), dict(micro_field_max_size=4096), 3, 58, 0.02, 1e-3, "bfloat16"),
+    "micro_2x3x4x5_f16": ((2, 3, 4, 5), dict(micro_field_max_size=4096, weight_decay=0.05), 3, 59, 0.02, 1e-3,
+                          "float16"),
 }
 
 

@@ -21,7 +21,7 @@ def declared_symbols():
 def test_library_exports_every_declared_symbol():
     lib = _lib.lib()
     names = declared_symbols()
-    assert len(names) == 20
+    assert len(names) == 22
     for name in names:
         assert hasattr(lib, name), name
     assert sorted(_lib.EXPORTS) == names
@@ -127,3 +127,24 @@ def test_scalar_scratch_is_host_logic():
     d = _fake_desc((4096, 16))
     assert lib.cresso_scalar_scratch_bytes(_lib.ptr(d), 1, n.ctypes.data_as(_lib._pi64)) == 0
     assert n[0] >= 4 * (4096 + 4096 + 16)
+
+
+def test_micro_scratch_is_host_logic():
+    lib = _lib.lib()
+    F = _lib.DESC_INDEX
+    n = np.zeros(1, dtype=np.int64)
+    for shape, work in (((4096,), 0), ((3, 4, 5), 12), ((1, 1000), 1001)):
+        d = _fake_desc(shape)
+        assert lib.cresso_micro_scratch_bytes(_lib.ptr(d), 1, n.ctypes.data_as(_lib._pi64)) == 0
+        assert n[0] >= 4 * work  # rank >= 2: one log term per axis coordinate
+    d = _fake_desc((3, 4, 5))
+    d[0, F["micro_refractory"]] = 0
+    assert lib.cresso_micro_scratch_bytes(_lib.ptr(d), 1, n.ctypes.data_as(_lib._pi64)) == 1
+    assert "NULL" in _lib.last_error()
+    d = _fake_desc((3, 4, 5))
+    d[0, F["dtype"]] = 7
+    assert lib.cresso_micro_scratch_bytes(_lib.ptr(d), 1, n.ctypes.data_as(_lib._pi64)) == 2
+    d = _fake_desc((2,) * 4)
+    d[0, F["ndim"]] = 0
+    assert lib.cresso_micro_scratch_bytes(_lib.ptr(d), 1, n.ctypes.data_as(_lib._pi64)) == 1
+    assert "rank 1 to 8" in _lib.last_error()

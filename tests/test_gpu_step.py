@@ -350,13 +350,16 @@ def test_state_dict_round_trip_with_oracle_layout():
     assert rel_rms(p.detach().cpu(), pr.detach()) <= 1e-5
 
 
-def test_mixed_routes_in_one_group():
-    """Spectral 2-D, spectral 1-D, LoRA-thin and small tensors in one param group."""
+@pytest.mark.parametrize("micro", [0, 4096])
+def test_mixed_routes_in_one_group(micro):
+    """Spectral 2-D / 1-D / 3-D, LoRA-thin and small tensors in one param group;
+    with micro_field_max_size = 4096 the tensors of 1 to 4096 elements and
+    rank >= 1 take the micro-field route instead."""
     g = torch.Generator().manual_seed(1)
-    shapes = [(300, 200), (4096,), (512, 16), (16, 512), (7, 9), (100,), (), (3, 4, 5)]
+    shapes = [(300, 200), (4096,), (512, 16), (16, 512), (7, 9), (100,), (), (3, 4, 5), (24, 10, 12)]
     inits = [torch.randn(s, generator=g) * 0.02 for s in shapes]
     grads = [[torch.randn(s, generator=g) * 1e-3 for s in shapes] for _ in range(3)]
-    kw = dict(rank=8, hash_bins=64, hash_tables=2)
+    kw = dict(rank=8, hash_bins=64, hash_tables=2, micro_field_max_size=micro)
     ps = [torch.nn.Parameter(x.clone().cuda()) for x in inits]
     rs = [torch.nn.Parameter(x.clone()) for x in inits]
     opt = cresso_b200.CRESSO5(ps, **kw)
@@ -369,6 +372,7 @@ def test_mixed_routes_in_one_group():
         ref.step()
     for p, r, s in zip(ps, rs, shapes):
         assert rel_rms(p.detach().cpu(), r.detach()) <= 1e-5, s
+        assert set(opt.state[p].keys()) == set(ref.state[r].keys()), s
         for k, v in ref.state[r].items():
             if torch.is_tensor(v) and v.dtype.is_floating_point:
                 assert rel_rms(opt.state[p][k].cpu(), v) <= 5e-3, (s, k)
