@@ -667,10 +667,12 @@ spectral_pass_kernel(const GroupHdr* __restrict__ hdr, const DevTensor* __restri
             __syncthreads();
             if ((tid & 63) == 0) tc_issue(0);
         }
-        float z1[RM], z2[RM];
+        // projection partials (a1_q, a2_q) x field, summed over this thread's rows; packed
+        // pairs for the two-lane fp32 FMA of sm_100 (each lane rounds as fmaf)
+        float2 z12[RM];
         float zc = 0.0f;
 #pragma unroll
-        for (int q = 0; q < RM; ++q) z1[q] = z2[q] = 0.0f;
+        for (int q = 0; q < RM; ++q) z12[q] = make_float2(0.0f, 0.0f);
         for (; it < seg_end; ++it) {
             const int col = ct * TC + lc;
             const bool cvalid = FULL || col < cols32;
@@ -782,11 +784,9 @@ spectral_pass_kernel(const GroupHdr* __restrict__ hdr, const DevTensor* __restri
                         s0 += L;
                         s1 += d;
                         colacc += d;
+                        const float2 Lc2 = make_float2(Lc, Lc);
 #pragma unroll
-                        for (int q = 1; q < RM; ++q) {
-                            z1[q] = fmaf(Lc, a1[q], z1[q]);
-                            z2[q] = fmaf(Lc, a2[q], z2[q]);
-                        }
+                        for (int q = 1; q < RM; ++q) z12[q] = __ffma2_rn(make_float2(a1[q], a2[q]), Lc2, z12[q]);
                         zc += Lc;
                         if (hash_on) {
                             // fixed-point path for every value (zero for the large ones), one
@@ -836,11 +836,9 @@ spectral_pass_kernel(const GroupHdr* __restrict__ hdr, const DevTensor* __restri
                         const float err = t - pred;
                         s0 = fmaf(err, err, s0);
                         s1 += t;
+                        const float2 t2 = make_float2(t, t);
 #pragma unroll
-                        for (int q = 1; q < RM; ++q) {
-                            z1[q] = fmaf(t, a1[q], z1[q]);
-                            z2[q] = fmaf(t, a2[q], z2[q]);
-                        }
+                        for (int q = 1; q < RM; ++q) z12[q] = __ffma2_rn(make_float2(a1[q], a2[q]), t2, z12[q]);
                         zc += t;
                         if (hash_on) {
                             const float port = err + tmix * t;
@@ -969,7 +967,7 @@ spectral_pass_kernel(const GroupHdr* __restrict__ hdr, const DevTensor* __restri
                         s_acc[tid] += (double)zc;  // zero mode: sum of the projected field
 #pragma unroll
                         for (int q = 1; q < RM; ++q) {
-                            const double B1 = b1[q], B2 = b2[q], Z1 = z1[q], Z2 = z2[q];
+                            const double B1 = b1[q], B2 = b2[q], Z1 = z12[q].x, Z2 = z12[q].y;
                             double c, s;
                             if (mode_is_product(q)) {
                                 c = B1 * Z1;
@@ -983,7 +981,7 @@ spectral_pass_kernel(const GroupHdr* __restrict__ hdr, const DevTensor* __restri
                         }
                     }
 #pragma unroll
-                    for (int q = 0; q < RM; ++q) z1[q] = z2[q] = 0.0f;
+                    for (int q = 0; q < RM; ++q) z12[q] = make_float2(0.0f, 0.0f);
                     zc = 0.0f;
                     items_since_flush = 0;
                 }
