@@ -45,7 +45,7 @@ DESC_FIELDS = (
        "force_rms", "drive_energy", "surprise", "action", "q", "impulse", "metric_q", "metric_impulse", "dtype",
        "micro_energy", "micro_impulse", "micro_refractory"]
 )
-DTYPE_CODES = {"float32": 0, "float16": 1, "bfloat16": 2}
+DTYPE_CODES = {"float32": 0, "float16": 1, "bfloat16": 2, "float64": 3}
 DESC_INDEX = {name: i for i, name in enumerate(DESC_FIELDS)}
 DESC_WORDS = len(DESC_FIELDS)
 

@@ -184,15 +184,6 @@ __device__ __forceinline__ float sqrt_sfu(float x) {
 }
 
 
-// EMA with a copy on the first step (reference _update_reservoir,
-// cresso_v5.py:900-905): old * decay + cur * (1 - decay).
-// decay is the Python float of the group; torch multiplies a float32 tensor
-// by (float)decay and adds with alpha (float)(1 - decay).
-__device__ __forceinline__ float reservoir(float old, float cur, double decay, int64_t step) {
-    if (step <= 1) return cur;
-    return old * (float)decay + cur * (float)(1.0 - decay);
-}
-
 // Element e of a parameter / gradient of type dt (float32 work, cresso_v5.py:119-124).
 // -lr rounded (once, from double) to the parameter type dt; float32: -lr.
 __device__ __forceinline__ float neg_lr_in(double lr, int dt) {
@@ -225,6 +216,79 @@ __device__ __forceinline__ void apply_update(void* p, int64_t e, int dt, float n
         float* f = reinterpret_cast<float*>(p);
         f[e] = f[e] + neg_lr * update;
     }
+}
+
+// EMA with a copy on the first step (reference _update_reservoir,
+// cresso_v5.py:900-905): old * decay + cur * (1 - decay).
+// decay is the Python float of the group; torch multiplies a float32 tensor
+// by (float)decay and adds with alpha (float)(1 - decay).
+__device__ __forceinline__ float reservoir(float old, float cur, double decay, int64_t step) {
+    if (step <= 1) return cur;
+    return old * (float)decay + cur * (float)(1.0 - decay);
+}
+// float64 state (float64 parameters): the decay and 1 - decay stay float64.
+__device__ __forceinline__ double reservoir(double old, double cur, double decay, int64_t step) {
+    if (step <= 1) return cur;
+    return old * decay + cur * (1.0 - decay);
+}
+
+// Work-type overloads (float: the float32 functions; double: the float64 ones) for
+// the kernels that run in the parameter's work type (float32 for float32 / float16 /
+// bfloat16 parameters, float64 for float64 ones; cresso_v5.py:119-124).
+__device__ __forceinline__ float w_exp(float x) { return expf(x); }
+__device__ __forceinline__ double w_exp(double x) { return exp(x); }
+__device__ __forceinline__ float w_log(float x) { return logf(x); }
+__device__ __forceinline__ double w_log(double x) { return log(x); }
+__device__ __forceinline__ float w_log1p(float x) { return log1pf(x); }
+__device__ __forceinline__ double w_log1p(double x) { return log1p(x); }
+__device__ __forceinline__ float w_pow(float x, float y) { return powf(x, y); }
+__device__ __forceinline__ double w_pow(double x, double y) { return pow(x, y); }
+__device__ __forceinline__ float w_sqrt(float x) { return sqrtf(x); }
+__device__ __forceinline__ double w_sqrt(double x) { return sqrt(x); }
+__device__ __forceinline__ float w_tanh(float x) { return tanhf(x); }
+__device__ __forceinline__ double w_tanh(double x) { return tanh(x); }
+__device__ __forceinline__ float w_abs(float x) { return fabsf(x); }
+__device__ __forceinline__ double w_abs(double x) { return fabs(x); }
+__device__ __forceinline__ float w_min(float x, float y) { return fminf(x, y); }
+__device__ __forceinline__ double w_min(double x, double y) { return fmin(x, y); }
+__device__ __forceinline__ float w_max(float x, float y) { return fmaxf(x, y); }
+__device__ __forceinline__ double w_max(double x, double y) { return fmax(x, y); }
+__device__ __forceinline__ float w_div(float x, float y) { return __fdiv_rn(x, y); }
+__device__ __forceinline__ double w_div(double x, double y) { return __ddiv_rn(x, y); }
+template <typename W>
+__device__ __forceinline__ W clampw(W v, W lo, W hi) { return w_min(w_max(v, lo), hi); }
+template <typename W>
+__device__ __forceinline__ W w_sgn(W x) { return x > W(0) ? W(1) : (x < W(0) ? W(-1) : W(0)); }
+
+// Element e of a float64 parameter / gradient.
+__device__ __forceinline__ double load_f64(const void* p, int64_t e) {
+    return __ldg(reinterpret_cast<const double*>(p) + e);
+}
+template <typename W>
+__device__ __forceinline__ W load_w(const void* p, int64_t e, int dt);
+template <>
+__device__ __forceinline__ float load_w<float>(const void* p, int64_t e, int dt) { return load_elem(p, e, dt); }
+template <>
+__device__ __forceinline__ double load_w<double>(const void* p, int64_t e, int) { return load_f64(p, e); }
+// -lr in the parameter's type: float32 / 16-bit as neg_lr_in, float64: -lr.
+template <typename W>
+__device__ __forceinline__ W neg_lr_w(double lr, int dt);
+template <>
+__device__ __forceinline__ float neg_lr_w<float>(double lr, int dt) { return neg_lr_in(lr, dt); }
+template <>
+__device__ __forceinline__ double neg_lr_w<double>(double lr, int) { return -lr; }
+// param.add_(update, alpha=-lr): float64 parameters p + (-lr) u in float64.
+template <typename W>
+__device__ __forceinline__ void apply_update_w(void* p, int64_t e, int dt, W neg_lr, W neg_lr16, W update);
+template <>
+__device__ __forceinline__ void apply_update_w<float>(void* p, int64_t e, int dt, float neg_lr, float neg_lr16,
+                                                      float update) {
+    apply_update(p, e, dt, neg_lr, neg_lr16, update);
+}
+template <>
+__device__ __forceinline__ void apply_update_w<double>(void* p, int64_t e, int, double neg_lr, double, double update) {
+    double* d = reinterpret_cast<double*>(p);
+    d[e] = d[e] + neg_lr * update;
 }
 
 }  // namespace cresso

@@ -20,6 +20,7 @@
 #include <math.h>
 #include <stdint.h>
 
+#include <algorithm>
 #include <vector>
 
 #include "cresso_common.cuh"
@@ -51,33 +52,41 @@ enum {
 };
 static_assert(sizeof(cresso_hparams) == M_COUNT * sizeof(double), "cresso_hparams field order");
 
+template <typename W>
 struct MicroShared {
     double red[16 * kWarps];
     double tot[16];
-    float scale, emean, gm, kk;
-    float c_rat, c_bnd, c_t, c_pred, c_err, gain;
+    W scale, emean, gm, kk;
+    W c_rat, c_bnd, c_t, c_pred, c_err, gain;
 };
 
 // Gram index of the pair (a, b), a <= b, of five vectors.
 __host__ __device__ constexpr int g5(int a, int b) { return a * 5 - (a * (a - 1)) / 2 + (b - a); }
 
+template <typename W>
 __global__ void __launch_bounds__(kThreads) micro_route_kernel(const MicroHdr* __restrict__ hdr,
                                                                 const MicroTensor* __restrict__ dts) {
-    __shared__ MicroShared sh;
+    __shared__ MicroShared<W> sh;
     const MicroTensor& D = dts[blockIdx.x];
+    // fields and 0-d state in the work type
+    W* energy = reinterpret_cast<W*>(D.energy);
+    W* impulse = reinterpret_cast<W*>(D.impulse);
+    W* refractory = reinterpret_cast<W*>(D.refractory);
+    W* work = reinterpret_cast<W*>(D.work);
+    auto st = [](float* ptr) { return reinterpret_cast<W*>(ptr); };
     const double* hp = hdr->hp;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int dt = D.dtype;
     const int64_t N = D.N;
     const double Nd = (double)N;
-    const float eps = (float)hp[M_EPS];
-    const float sgn = hp[M_MAX] != 0.0 ? -1.0f : 1.0f;
-    const float wd = (float)hp[M_WD];
+    const W eps = (W)hp[M_EPS];
+    const W sgn = hp[M_MAX] != 0.0 ? -W(1.0) : W(1.0);
+    const W wd = (W)hp[M_WD];
     const bool wd_on = hp[M_WD] != 0.0;
     // f = g (+ wd p), with g negated under maximize (cresso_v5.py:833-834, 907-912)
     auto force = [&](int64_t e) {
-        float f = sgn * load_elem(D.grad, e, dt);
-        if (wd_on) f = f + wd * load_elem(D.param, e, dt);
+        W f = sgn * load_w<W>(D.grad, e, dt);
+        if (wd_on) f = f + wd * load_w<W>(D.param, e, dt);
         return f;
     };
 
@@ -85,56 +94,56 @@ __global__ void __launch_bounds__(kThreads) micro_route_kernel(const MicroHdr* _
     {
         double s = 0.0;
         for (int64_t e = tid; e < N; e += kThreads) {
-            const float f = force(e);
+            const W f = force(e);
             s += (double)(f * f);
         }
         double v[1] = {s};
         block_sum_to<1>(v, sh.red, sh.tot);
         if (tid == 0) {
-            const float frn = sqrtf((float)(sh.tot[0] / Nd) + eps);
-            const float fr = reservoir(*D.force_rms, frn, hp[M_RD], D.step);
-            *D.force_rms = fr;
-            sh.scale = fmaxf(fr, eps);
+            const W frn = w_sqrt((W)(sh.tot[0] / Nd) + eps);
+            const W fr = reservoir(*st(D.force_rms), frn, hp[M_RD], D.step);
+            *st(D.force_rms) = fr;
+            sh.scale = w_max(fr, eps);
         }
         __syncthreads();
     }
-    const float scale = sh.scale;
-    auto rel_of = [&](float f) { return fminf(fabsf(f) / scale + eps, 1.0e4f); };
+    const W scale = sh.scale;
+    auto rel_of = [&](W f) { return w_min(w_abs(f) / scale + eps, W(1.0e4)); };
 
     // instant metric of the micro route: coupling min(0.35, c), every axis (cresso_v5.py:1390-1392, 243-262)
     const double ic = fmin(0.35, hp[M_IC]);
-    const float pw = fmaxf((float)hp[M_IP], 0.25f);
+    const W pw = w_max((W)hp[M_IP], W(0.25));
     const bool inst_on = ic != 0.0 && N > 1;
     const bool marg = inst_on && D.ndim >= 2;
-    auto idens = [&](float rel) { return pw == 1.0f ? fmaxf(rel, eps) : fminf(powf(fmaxf(rel, eps), pw), 1.0e6f); };
+    auto idens = [&](W rel) { return pw == W(1.0) ? w_max(rel, eps) : w_min(w_pow(w_max(rel, eps), pw), W(1.0e6)); };
 
     // ---- sweep 2: energy field and the instant-metric density  (cresso_v5.py:1380-1392)
     {
-        const float ep = (float)hp[M_EP];
-        const float md = (float)hp[M_MD], omd = (float)(1.0 - hp[M_MD]);
+        const W ep = (W)hp[M_EP];
+        const W md = (W)hp[M_MD], omd = (W)(1.0 - hp[M_MD]);
         const bool first = D.step <= 1;
         double se = 0.0, sd = 0.0;
         for (int64_t e = tid; e < N; e += kThreads) {
-            const float rel = rel_of(force(e));
-            const float dens = powf(rel, ep);
-            const float en = first ? dens : D.energy[e] * md + omd * dens;
-            D.energy[e] = en;
+            const W rel = rel_of(force(e));
+            const W dens = w_pow(rel, ep);
+            const W en = first ? dens : energy[e] * md + omd * dens;
+            energy[e] = en;
             se += (double)en;
             if (inst_on) sd += (double)idens(rel);
         }
         double v[2] = {se, sd};
         block_sum_to<2>(v, sh.red, sh.tot);
         if (tid == 0) {
-            sh.emean = fmaxf((float)(sh.tot[0] / Nd), eps);
-            sh.gm = fmaxf((float)(sh.tot[1] / Nd), eps);
-            sh.kk = (float)(ic / ((double)D.ndim * (double)pw));
+            sh.emean = w_max((W)(sh.tot[0] / Nd), eps);
+            sh.gm = w_max((W)(sh.tot[1] / Nd), eps);
+            sh.kk = (W)(ic / ((double)D.ndim * (double)pw));
         }
         __syncthreads();
         if (marg) {
             // log(max(axis mean / mean, eps)) per axis and coordinate: the elements of one
             // coordinate (a slab of N / dims[a]) are summed by one thread when the slab is
             // short, else by one warp (lane-strided, then a shuffle tree); fixed order both ways
-            const float gm = sh.gm;
+            const W gm = sh.gm;
             uint32_t off = 0;
             for (int a = 0; a < (int)D.ndim; ++a) {
                 const uint32_t da = (uint32_t)D.dims[a];
@@ -150,14 +159,14 @@ __global__ void __launch_bounds__(kThreads) micro_route_kernel(const MicroHdr* _
                     for (uint32_t c = tid; c < da; c += kThreads) {
                         double m = 0.0;
                         for (uint32_t s = 0; s < slab; ++s) m += (double)idens(rel_of(force(elem(c, s))));
-                        D.work[off + c] = logf(fmaxf((float)(m * inv_slab) / gm, eps));
+                        work[off + c] = w_log(w_max((W)(m * inv_slab) / gm, eps));
                     }
                 } else {
                     for (uint32_t c = warp; c < da; c += kWarps) {
                         double m = 0.0;
                         for (uint32_t s = lane; s < slab; s += 32) m += (double)idens(rel_of(force(elem(c, s))));
                         m = warp_sum(m);
-                        if (lane == 0) D.work[off + c] = logf(fmaxf((float)(m * inv_slab) / gm, eps));
+                        if (lane == 0) work[off + c] = w_log(w_max((W)(m * inv_slab) / gm, eps));
                     }
                 }
                 off += da;
@@ -165,47 +174,47 @@ __global__ void __launch_bounds__(kThreads) micro_route_kernel(const MicroHdr* _
             __syncthreads();
         }
     }
-    const float emean = sh.emean, gm = sh.gm, kk = sh.kk;
-    const float xm = (float)(hp[M_HMC] / fmax(0.25, hp[M_EP]));
-    auto tangent = [&](int64_t e, float f) {
-        const float rel = rel_of(f);
-        const float metric = clampf(powf(D.energy[e] / emean, xm), 0.08f, 12.0f);
-        float inst = 1.0f;
+    const W emean = sh.emean, gm = sh.gm, kk = sh.kk;
+    const W xm = (W)(hp[M_HMC] / fmax(0.25, hp[M_EP]));
+    auto tangent = [&](int64_t e, W f) {
+        const W rel = rel_of(f);
+        const W metric = clampw(w_pow(energy[e] / emean, xm), W(0.08), W(12.0));
+        W inst = W(1.0);
         if (marg) {
             // 32-bit index arithmetic (N < 2^31): 64-bit division is a subroutine call
-            float lsum = 0.0f;
+            W lsum = W(0.0);
             uint32_t rem = (uint32_t)e, off = 0;
             for (int a = 0; a < (int)D.ndim; ++a) off += (uint32_t)D.dims[a];
             for (int a = (int)D.ndim - 1; a >= 0; --a) {
                 const uint32_t da = (uint32_t)D.dims[a];
                 off -= da;
-                lsum += D.work[off + rem % da];
+                lsum += work[off + rem % da];
                 rem /= da;
             }
-            inst = clampf(expf(kk * lsum), 0.08f, 12.0f);
+            inst = clampw(w_exp(kk * lsum), W(0.08), W(12.0));
         } else if (inst_on) {
-            inst = clampf(expf(kk * logf(fmaxf(idens(rel) / gm, eps))), 0.08f, 12.0f);
+            inst = clampw(w_exp(kk * w_log(w_max(idens(rel) / gm, eps))), W(0.08), W(12.0));
         }
-        return clampf(f / (scale * metric * inst + eps), -1.0e4f, 1.0e4f);
+        return clampw(f / (scale * metric * inst + eps), -W(1.0e4), W(1.0e4));
     };
-    const float clip = (float)hp[M_CLIP];
+    const W clip = (W)hp[M_CLIP];
 
     // ---- sweep 3: refractory-gated impulse, prediction error, drive statistics  (cresso_v5.py:1394-1431)
     {
-        const float rd = (float)hp[M_REFD], ord = (float)(1.0 - hp[M_REFD]);
-        const float rg = (float)hp[M_RG];
-        const float mid = (float)hp[M_MID], omid = (float)(1.0 - hp[M_MID]);
+        const W rd = (W)hp[M_REFD], ord = (W)(1.0 - hp[M_REFD]);
+        const W rg = (W)hp[M_RG];
+        const W mid = (W)hp[M_MID], omid = (W)(1.0 - hp[M_MID]);
         double g[15];
 #pragma unroll
         for (int j = 0; j < 15; ++j) g[j] = 0.0;
         for (int64_t e = tid; e < N; e += kThreads) {
-            const float t = tangent(e, force(e));
-            const float rf = D.refractory[e] * rd + ord * fabsf(t);
-            D.refractory[e] = rf;
-            const float gate = 1.0f / (1.0f + rg * rf);
-            const float im = D.impulse[e] * mid + omid * (t * gate);
-            D.impulse[e] = im;
-            const double v[5] = {(double)(t / (1.0f + fabsf(t) / clip)), (double)(tanhf(t / clip) * clip), (double)t,
+            const W t = tangent(e, force(e));
+            const W rf = refractory[e] * rd + ord * w_abs(t);
+            refractory[e] = rf;
+            const W gate = W(1.0) / (W(1.0) + rg * rf);
+            const W im = impulse[e] * mid + omid * (t * gate);
+            impulse[e] = im;
+            const double v[5] = {(double)(t / (W(1.0) + w_abs(t) / clip)), (double)(w_tanh(t / clip) * clip), (double)t,
                                  (double)im, (double)(t - im)};
             int j = 0;
 #pragma unroll
@@ -217,18 +226,18 @@ __global__ void __launch_bounds__(kThreads) micro_route_kernel(const MicroHdr* _
         if (tid == 0) {
             const double* G = sh.tot;
             enum { RAT = 0, BND = 1, TT = 2, PR = 3, ER = 4 };
-            const float sn = sqrtf((float)(G[g5(ER, ER)] / Nd) + eps);
-            const float S = reservoir(*D.surprise, sn, hp[M_SD], D.step);
-            *D.surprise = S;
-            const float sp = (float)hp[M_SPIKE] / (1.0f + S);
-            const double a = (double)(1.0f - sp), b = (double)sp;
+            const W sn = w_sqrt((W)(G[g5(ER, ER)] / Nd) + eps);
+            const W S = reservoir(*st(D.surprise), sn, hp[M_SD], D.step);
+            *st(D.surprise) = S;
+            const W sp = (W)hp[M_SPIKE] / (W(1.0) + S);
+            const double a = (double)(W(1.0) - sp), b = (double)sp;
             const double sh2 = a * a * G[g5(RAT, RAT)] + 2.0 * a * b * G[g5(RAT, BND)] + b * b * G[g5(BND, BND)];
-            const float target = sqrtf((float)(sh2 / Nd) + eps);
-            auto k_of = [&](int i) { return target / fmaxf(sqrtf((float)(G[g5(i, i)] / Nd) + eps), eps); };
-            const float dm = (float)hp[M_DFM] / (1.0f + 0.35f * S);
-            const float mm = (float)hp[M_MDM] / (1.0f + 0.25f * S);
-            const float rm = (float)hp[M_RFM] / (1.0f + S);
-            const float core = clampf(1.0f - dm - 0.5f * mm, 0.0f, 1.0f);
+            const W target = w_sqrt((W)(sh2 / Nd) + eps);
+            auto k_of = [&](int i) { return target / w_max(w_sqrt((W)(G[g5(i, i)] / Nd) + eps), eps); };
+            const W dm = (W)hp[M_DFM] / (W(1.0) + W(0.35) * S);
+            const W mm = (W)hp[M_MDM] / (W(1.0) + W(0.25) * S);
+            const W rm = (W)hp[M_RFM] / (W(1.0) + S);
+            const W core = clampw(W(1.0) - dm - W(0.5) * mm, W(0.0), W(1.0));
             double c[5];
             c[RAT] = (double)core * a;
             c[BND] = (double)core * b;
@@ -240,29 +249,29 @@ __global__ void __launch_bounds__(kThreads) micro_route_kernel(const MicroHdr* _
             for (int i = 0; i < 5; ++i)
 #pragma unroll
                 for (int j = 0; j < 5; ++j) d2 += c[i] * c[j] * G[i <= j ? g5(i, j) : g5(j, i)];
-            const float DE = reservoir(*D.drive_energy, (float)(fmax(d2, 0.0) / Nd), hp[M_RD], D.step);
-            *D.drive_energy = DE;
-            sh.gain = clampf((float)hp[M_TGT] / sqrtf(DE + eps), (float)hp[M_MING], (float)hp[M_MAXG]);
-            sh.c_rat = (float)c[RAT];
-            sh.c_bnd = (float)c[BND];
-            sh.c_t = (float)c[TT];
-            sh.c_pred = (float)c[PR];
-            sh.c_err = (float)c[ER];
+            const W DE = reservoir(*st(D.drive_energy), (W)(fmax(d2, 0.0) / Nd), hp[M_RD], D.step);
+            *st(D.drive_energy) = DE;
+            sh.gain = clampw((W)hp[M_TGT] / w_sqrt(DE + eps), (W)hp[M_MING], (W)hp[M_MAXG]);
+            sh.c_rat = (W)c[RAT];
+            sh.c_bnd = (W)c[BND];
+            sh.c_t = (W)c[TT];
+            sh.c_pred = (W)c[PR];
+            sh.c_err = (W)c[ER];
         }
         __syncthreads();
     }
 
     // ---- sweep 4: parameter update  (cresso_v5.py:1432)
     {
-        const float cr = sh.c_rat, cb = sh.c_bnd, ct = sh.c_t, cp = sh.c_pred, ce = sh.c_err, gain = sh.gain;
-        const float neg_lr = (float)(-hp[M_LR]);
-        const float neg_lr16 = neg_lr_in(hp[M_LR], dt);
+        const W cr = sh.c_rat, cb = sh.c_bnd, ct = sh.c_t, cp = sh.c_pred, ce = sh.c_err, gain = sh.gain;
+        const W neg_lr = (W)(-hp[M_LR]);
+        const W neg_lr16 = neg_lr_w<W>(hp[M_LR], dt);
         for (int64_t e = tid; e < N; e += kThreads) {
-            const float t = tangent(e, force(e));
-            const float im = D.impulse[e];
-            const float drive = cr * (t / (1.0f + fabsf(t) / clip)) + cb * (tanhf(t / clip) * clip) + ct * t +
+            const W t = tangent(e, force(e));
+            const W im = impulse[e];
+            const W drive = cr * (t / (W(1.0) + w_abs(t) / clip)) + cb * (w_tanh(t / clip) * clip) + ct * t +
                                 cp * im + ce * (t - im);
-            apply_update(D.param, e, dt, neg_lr, neg_lr16, drive * gain);
+            apply_update_w<W>(D.param, e, dt, neg_lr, neg_lr16, drive * gain);
         }
     }
 }
@@ -280,8 +289,10 @@ static int micro_layout(const cresso_tensor_desc* descs, int64_t n, std::vector<
         CRESSO_REQUIRE(d.ndim >= 1 && d.ndim <= CRESSO_MAX_NDIM, CRESSO_EINVAL,
                        "tensor %lld: the micro route takes tensors of rank 1 to %d (ndim=%lld)", (long long)i,
                        CRESSO_MAX_NDIM, (long long)d.ndim);
-        CRESSO_REQUIRE(d.dtype == CRESSO_DTYPE_F32 || d.dtype == CRESSO_DTYPE_F16 || d.dtype == CRESSO_DTYPE_BF16,
-                       CRESSO_EUNSUPPORTED, "tensor %lld: dtype code %lld (float32, float16 and bfloat16 are supported)",
+        CRESSO_REQUIRE(d.dtype == CRESSO_DTYPE_F32 || d.dtype == CRESSO_DTYPE_F16 || d.dtype == CRESSO_DTYPE_BF16 ||
+                           d.dtype == CRESSO_DTYPE_F64,
+                       CRESSO_EUNSUPPORTED,
+                       "tensor %lld: dtype code %lld (float32, float16, bfloat16 and float64 are supported)",
                        (long long)i, (long long)d.dtype);
         int64_t N = 1, lead_sum = 0;
         for (int64_t a = 0; a < d.ndim; ++a) {
@@ -314,7 +325,7 @@ static int micro_layout(const cresso_tensor_desc* descs, int64_t n, std::vector<
             M.dtype = (int32_t)d.dtype;
             M.work = d.ndim >= 2 ? (float*)(intptr_t)off : nullptr;  // offset, rebased by the caller
         }
-        if (d.ndim >= 2) off = align_up(off + 4 * lead_sum, 256);
+        if (d.ndim >= 2) off = align_up(off + (d.dtype == CRESSO_DTYPE_F64 ? 8 : 4) * lead_sum, 256);
     }
     *bytes = off;
     return CRESSO_OK;
@@ -345,6 +356,10 @@ int cresso_micro_run(const cresso_tensor_desc* descs, int64_t n, const cresso_hp
     char* base = (char*)scratch;
     for (auto& M : dts)
         if (M.ndim >= 2) M.work = (float*)(base + (intptr_t)M.work);
+    // float32-work tensors first, then the float64 ones (a kernel instantiation each)
+    std::stable_partition(dts.begin(), dts.end(), [](const MicroTensor& M) { return M.dtype != CRESSO_DTYPE_F64; });
+    int64_t n32 = 0;
+    for (const auto& M : dts) n32 += M.dtype != CRESSO_DTYPE_F64;
     MicroHdr h{};
     h.n = n;
     memcpy(h.hp, hp, sizeof(cresso_hparams));
@@ -352,9 +367,16 @@ int cresso_micro_run(const cresso_tensor_desc* descs, int64_t n, const cresso_hp
     cudaStream_t s = (cudaStream_t)stream;
     CRESSO_CUDA(cudaMemcpyAsync(base, &h, sizeof(h), cudaMemcpyHostToDevice, s));
     CRESSO_CUDA(cudaMemcpyAsync(base + off_dts, dts.data(), sizeof(MicroTensor) * n, cudaMemcpyHostToDevice, s));
-    micro_route_kernel<<<(unsigned)n, kThreads, 0, s>>>(reinterpret_cast<const MicroHdr*>(base),
-                                                         reinterpret_cast<const MicroTensor*>(base + off_dts));
-    CRESSO_LAUNCHED("micro_route_kernel");
+    const MicroHdr* dh = reinterpret_cast<const MicroHdr*>(base);
+    const MicroTensor* dd = reinterpret_cast<const MicroTensor*>(base + off_dts);
+    if (n32 > 0) {
+        micro_route_kernel<float><<<(unsigned)n32, kThreads, 0, s>>>(dh, dd);
+        CRESSO_LAUNCHED("micro_route_kernel<float>");
+    }
+    if (n32 < n) {
+        micro_route_kernel<double><<<(unsigned)(n - n32), kThreads, 0, s>>>(dh, dd + n32);
+        CRESSO_LAUNCHED("micro_route_kernel<double>");
+    }
     return CRESSO_OK;
 }
 

@@ -52,11 +52,12 @@ enum {
     S_TGT, S_MING, S_MAXG, S_CLIP, S_SPIKE, S_EPS, S_MAX
 };
 
+template <typename W>
 struct ScalShared {
     double red[16 * kWarps];
     double tot[16];
-    float scale, inv_scale, metric, q_old, q_new, S, gm, inst_k;
-    float c_u, c_root, c_t, c_pred, c_nov, gain, sp, invD;
+    W scale, inv_scale, metric, q_old, q_new, S, gm, inst_k;
+    W c_u, c_root, c_t, c_pred, c_nov, gain, sp, invD;
     int inst_mode;  // 0 none, 1 one axis (per element), 2 rows x cols, 3 N-d marginals
 };
 
@@ -91,8 +92,10 @@ __device__ __forceinline__ void walk_elems(const ScalTensor& D, Fn fn) {
 
 // Product of the per-axis instant factors of element e of an N-d tensor;
 // work holds the factors of axis a at [sum(dims[:a]), sum(dims[:a+1])).
-__device__ __forceinline__ float nd_factor(const ScalTensor& D, int64_t e) {
-    float prod = 1.0f;
+template <typename W>
+__device__ __forceinline__ W nd_factor(const ScalTensor& D, int64_t e) {
+    const W* work = reinterpret_cast<const W*>(D.work);
+    W prod = W(1.0);
     int64_t rem = e;
     int64_t base = 0;
     for (int64_t a = 0; a < D.ndim; ++a) base += D.dims[a];
@@ -100,25 +103,28 @@ __device__ __forceinline__ float nd_factor(const ScalTensor& D, int64_t e) {
         base -= D.dims[a];
         const int64_t coord = rem % D.dims[a];
         rem /= D.dims[a];
-        prod *= D.work[base + coord];
+        prod *= work[base + coord];
     }
     return prod;
 }
 
+template <typename W>
 __global__ void __launch_bounds__(kThreads) scalar_route_kernel(const ScalHdr* __restrict__ hdr,
                                                                  const ScalTensor* __restrict__ dts) {
-    __shared__ ScalShared sh;
+    __shared__ ScalShared<W> sh;
     const ScalTensor& D = dts[blockIdx.x];
+    W* work = reinterpret_cast<W*>(D.work);
+    auto st = [](float* ptr) { return reinterpret_cast<W*>(ptr); };  // 0-d state of the work type
     const double* hp = hdr->hp;
     const int tid = threadIdx.x, lane = tid & 31;
-    const float eps = (float)hp[S_EPS];
-    const float sgn = hp[S_MAX] != 0.0 ? -1.0f : 1.0f;
-    const float wd = (float)hp[S_WD];
+    const W eps = (W)hp[S_EPS];
+    const W sgn = hp[S_MAX] != 0.0 ? -W(1.0) : W(1.0);
+    const W wd = (W)hp[S_WD];
     const bool wd_on = hp[S_WD] != 0.0;
     const double N = (double)D.N;
     auto force = [&](int64_t e) {
-        float f = sgn * load_elem(D.grad, e, D.dtype);
-        if (wd_on) f = f + wd * load_elem(D.param, e, D.dtype);
+        W f = sgn * load_w<W>(D.grad, e, D.dtype);
+        if (wd_on) f = f + wd * load_w<W>(D.param, e, D.dtype);
         return f;
     };
 
@@ -127,39 +133,39 @@ __global__ void __launch_bounds__(kThreads) scalar_route_kernel(const ScalHdr* _
         double s = 0.0;
         walk_elems(D, [&](int64_t e, int64_t, int64_t, int, bool valid) {
             if (valid) {
-                const float f = force(e);
+                const W f = force(e);
                 s += (double)(f * f);
             }
         });
         double v[1] = {s};
         block_sum_to<1>(v, sh.red, sh.tot);
         if (tid == 0) {
-            const float frn = sqrtf((float)(sh.tot[0] / N) + eps);
-            const float fr = reservoir(*D.force_rms, frn, hp[S_RD], D.step);
-            *D.force_rms = fr;
-            sh.scale = fmaxf(fr, eps);
-            sh.inv_scale = 1.0f / sh.scale;
+            const W frn = w_sqrt((W)(sh.tot[0] / N) + eps);
+            const W fr = reservoir(*st(D.force_rms), frn, hp[S_RD], D.step);
+            *st(D.force_rms) = fr;
+            sh.scale = w_max(fr, eps);
+            sh.inv_scale = W(1.0) / sh.scale;
         }
         __syncthreads();
     }
-    const float scale = sh.scale, inv_scale = sh.inv_scale;
-    const float ep = (float)hp[S_EP];
-    const float pw = fmaxf((float)hp[S_IP], 0.25f);
-    const bool ipow1 = pw == 1.0f;
-    const float ic = (float)hp[S_IC];
+    const W scale = sh.scale, inv_scale = sh.inv_scale;
+    const W ep = (W)hp[S_EP];
+    const W pw = w_max((W)hp[S_IP], W(0.25));
+    const bool ipow1 = pw == W(1.0);
+    const W ic = (W)hp[S_IC];
     int inst_mode = 0;
-    if (ic != 0.0f && D.ndim > 0 && D.N > 1) inst_mode = D.ndim == 1 ? 1 : (D.ndim == 2 ? 2 : 3);
-    auto dens = [&](float rel) { return ipow1 ? rel : fminf(powf(fmaxf(rel, eps), pw), 1.0e6f); };
+    if (ic != W(0.0) && D.ndim > 0 && D.N > 1) inst_mode = D.ndim == 1 ? 1 : (D.ndim == 2 ? 2 : 3);
+    auto dens = [&](W rel) { return ipow1 ? rel : w_min(w_pow(w_max(rel, eps), pw), W(1.0e6)); };
 
     // ---- stage 2: density metric and the instant-metric axis sums  (cresso_v5.py:1510-1525)
     {
-        float* rowpart = D.work;  // [n_ct * nw][rows]
+        W* rowpart = work;  // [n_ct * nw][rows]
         const int nw = D.nw;
-        float* colsum = D.work + (int64_t)D.n_ct * nw * D.rows + D.rows;  // [cols]
+        W* colsum = work + (int64_t)D.n_ct * nw * D.rows + D.rows;  // [cols]
         __syncthreads();
         double sL = 0.0, sd = 0.0;
-        float colacc = 0.0f;
-        __shared__ float s_col[kThreads];
+        W colacc = W(0.0);
+        __shared__ W s_col[kThreads];
         const int lc = tid & (D.TC - 1), rs = tid / D.TC;
         int cur_ct = -1;
         walk_elems(D, [&](int64_t e, int64_t r, int64_t c, int ct, bool valid) {
@@ -169,27 +175,27 @@ __global__ void __launch_bounds__(kThreads) scalar_route_kernel(const ScalHdr* _
                     __syncthreads();
                     const int64_t cc = (int64_t)cur_ct * D.TC + lc;
                     if (rs == 0 && cc < D.cols) {
-                        float s = 0.0f;
+                        W s = W(0.0);
                         for (int q = 0; q < D.RPI; ++q) s += s_col[q * D.TC + lc];
                         colsum[cc] = s;
                     }
                     __syncthreads();
                 }
-                colacc = 0.0f;
+                colacc = W(0.0);
                 cur_ct = ct;
             }
-            float d = 0.0f;
+            W d = W(0.0);
             if (valid) {
-                const float f = force(e);
-                const float rel0 = fabsf(f) * inv_scale + eps;
-                sL += (double)log1pf(powf(rel0, ep));
-                const float rel = fminf(rel0, 1.0e4f);
+                const W f = force(e);
+                const W rel0 = w_abs(f) * inv_scale + eps;
+                sL += (double)w_log1p(w_pow(rel0, ep));
+                const W rel = w_min(rel0, W(1.0e4));
                 d = dens(rel);
                 sd += (double)d;
                 colacc += d;
             }
             if (inst_mode == 2) {
-                float v = d;
+                W v = d;
                 const int w = min(D.TC, 32);
                 for (int o = w >> 1; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
                 const bool leader = D.TC <= 32 ? (lc == 0) : (lane == 0);
@@ -202,7 +208,7 @@ __global__ void __launch_bounds__(kThreads) scalar_route_kernel(const ScalHdr* _
             __syncthreads();
             const int64_t cc = (int64_t)cur_ct * D.TC + lc;
             if (rs == 0 && cc < D.cols) {
-                float s = 0.0f;
+                W s = W(0.0);
                 for (int q = 0; q < D.RPI; ++q) s += s_col[q * D.TC + lc];
                 colsum[cc] = s;
             }
@@ -211,32 +217,32 @@ __global__ void __launch_bounds__(kThreads) scalar_route_kernel(const ScalHdr* _
         block_sum_to<2>(v, sh.red, sh.tot);  // includes __syncthreads
         if (tid == 0) {
             // metric oscillator on the scalar density  (cresso_v5.py:1510-1519)
-            const float density = (float)(sh.tot[0] / N);
-            const float mq0 = *D.metric_q;
-            const float port = density - tanhf(mq0);
-            const float mdt = (float)hp[S_MDT];
-            float mp = *D.metric_impulse * (float)fmax(0.0, 1.0 - hp[S_MDT] * hp[S_MF]);
+            const W density = (W)(sh.tot[0] / N);
+            const W mq0 = *st(D.metric_q);
+            const W port = density - w_tanh(mq0);
+            const W mdt = (W)hp[S_MDT];
+            W mp = *st(D.metric_impulse) * (W)fmax(0.0, 1.0 - hp[S_MDT] * hp[S_MF]);
             mp = mp + mdt * (port - mq0);
-            const float mq = clampf(mq0 + mdt * mp, -3.0f, 3.0f);
-            *D.metric_impulse = mp;
-            *D.metric_q = mq;
-            sh.metric = clampf(expf((float)hp[S_MC] * mq), 0.06f, 16.0f);
-            sh.gm = fmaxf((float)(sh.tot[1] / N), eps);
-            sh.inst_k = ic / ((float)(D.ndim > 1 ? D.ndim : 1) * pw);
-            sh.q_old = *D.q;
+            const W mq = clampw(mq0 + mdt * mp, -W(3.0), W(3.0));
+            *st(D.metric_impulse) = mp;
+            *st(D.metric_q) = mq;
+            sh.metric = clampw(w_exp((W)hp[S_MC] * mq), W(0.06), W(16.0));
+            sh.gm = w_max((W)(sh.tot[1] / N), eps);
+            sh.inst_k = ic / ((W)(D.ndim > 1 ? D.ndim : 1) * pw);
+            sh.q_old = *st(D.q);
         }
         __syncthreads();
         // per-axis factors exp(k * log(max(mean / gmean, eps)))  (cresso_v5.py:243-262)
-        const float gm = sh.gm, kk = sh.inst_k;
+        const W gm = sh.gm, kk = sh.inst_k;
         if (inst_mode == 2) {
-            float* rowf = D.work + (int64_t)D.n_ct * nw * D.rows;
+            W* rowf = work + (int64_t)D.n_ct * nw * D.rows;
             for (int64_t r = tid; r < D.rows; r += kThreads) {
                 double s = 0.0;
                 for (int64_t j = 0; j < (int64_t)D.n_ct * nw; ++j) s += (double)rowpart[j * D.rows + r];
-                rowf[r] = expf(kk * logf(fmaxf((float)(s / (double)D.cols) / gm, eps)));
+                rowf[r] = w_exp(kk * w_log(w_max((W)(s / (double)D.cols) / gm, eps)));
             }
             for (int64_t c = tid; c < D.cols; c += kThreads)
-                colsum[c] = expf(kk * logf(fmaxf((float)((double)colsum[c] / (double)D.rows) / gm, eps)));
+                colsum[c] = w_exp(kk * w_log(w_max((W)((double)colsum[c] / (double)D.rows) / gm, eps)));
         } else if (inst_mode == 3) {
             // N-d marginals: one thread per (axis, coordinate) sums its slab in a fixed
             // order (deterministic), then turns the mean into the axis factor.
@@ -255,43 +261,43 @@ __global__ void __launch_bounds__(kThreads) scalar_route_kernel(const ScalHdr* _
                 for (int64_t o = 0; o < outer; ++o)
                     for (int64_t i = 0; i < inner; ++i) {
                         const int64_t e = (o * D.dims[a] + c) * inner + i;
-                        const float f = force(e);
-                        m += (double)dens(fminf(fabsf(f) * inv_scale + eps, 1.0e4f));
+                        const W f = force(e);
+                        m += (double)dens(w_min(w_abs(f) * inv_scale + eps, W(1.0e4)));
                     }
                 const double per = N / (double)D.dims[a];
-                D.work[j] = expf(kk * logf(fmaxf((float)(m / per) / gm, eps)));
+                work[j] = w_exp(kk * w_log(w_max((W)(m / per) / gm, eps)));
             }
         }
         __syncthreads();
     }
 
-    const float metric = sh.metric, gm = sh.gm, kk = sh.inst_k;
-    const float ls = (float)hp[S_LS];
+    const W metric = sh.metric, gm = sh.gm, kk = sh.inst_k;
+    const W ls = (W)hp[S_LS];
     const bool local_on = hp[S_LS] != 0.0;
-    const float* rowf = D.work + (int64_t)D.n_ct * D.nw * D.rows;
-    const float* colf = rowf + D.rows;
+    const W* rowf = work + (int64_t)D.n_ct * D.nw * D.rows;
+    const W* colf = rowf + D.rows;
     auto tangent = [&](int64_t e, int64_t r, int64_t c) {
-        const float f = force(e);
-        const float rel = fminf(fabsf(f) * inv_scale + eps, 1.0e4f);
-        float den = scale * metric;
-        if (local_on) den = den * clampf(1.0f + ls * sqrtf(fminf(rel, 100.0f)), 1.0f, 8.0f);
+        const W f = force(e);
+        const W rel = w_min(w_abs(f) * inv_scale + eps, W(1.0e4));
+        W den = scale * metric;
+        if (local_on) den = den * clampw(W(1.0) + ls * w_sqrt(w_min(rel, W(100.0))), W(1.0), W(8.0));
         if (inst_mode == 1) {
-            den = den * clampf(expf(kk * logf(fmaxf(dens(rel) / gm, eps))), 0.08f, 12.0f);
+            den = den * clampw(w_exp(kk * w_log(w_max(dens(rel) / gm, eps))), W(0.08), W(12.0));
         } else if (inst_mode == 2) {
-            den = den * clampf(rowf[r] * colf[c], 0.08f, 12.0f);
+            den = den * clampw(rowf[r] * colf[c], W(0.08), W(12.0));
         } else if (inst_mode == 3) {
-            den = den * clampf(nd_factor(D, e), 0.08f, 12.0f);
+            den = den * clampw(nd_factor<W>(D, e), W(0.08), W(12.0));
         }
-        return clampf(__fdiv_rn(f, den + eps), -1.0e4f, 1.0e4f);
+        return clampw(w_div(f, den + eps), -W(1.0e4), W(1.0e4));
     };
 
     // ---- stage 3: prediction error, surprise, scalar contact  (cresso_v5.py:1526-1546)
     {
-        const float q0 = sh.q_old;
+        const W q0 = sh.q_old;
         double se = 0.0, se2 = 0.0;
         walk_elems(D, [&](int64_t e, int64_t r, int64_t c, int, bool valid) {
             if (valid) {
-                const float err = tangent(e, r, c) - q0;
+                const W err = tangent(e, r, c) - q0;
                 se += (double)err;
                 se2 += (double)(err * err);
             }
@@ -299,46 +305,46 @@ __global__ void __launch_bounds__(kThreads) scalar_route_kernel(const ScalHdr* _
         double v[2] = {se, se2};
         block_sum_to<2>(v, sh.red, sh.tot);
         if (tid == 0) {
-            const float sn = sqrtf((float)(sh.tot[1] / N) + eps);
-            const float S = reservoir(*D.surprise, sn, hp[S_SD], D.step);
-            *D.surprise = S;
-            const float port = (float)(sh.tot[0] / N);
-            const float dt = (float)hp[S_DT];
-            const float plast = 1.0f + (float)hp[S_SG] * S / (1.0f + S);
-            const float brake = 1.0f / (1.0f + (float)hp[S_SB] * S);
-            float imp = *D.impulse, q = q0, action = *D.action;
-            const float energy = 0.5f * (imp * imp + q * q);
-            action = action * 0.985f + (port * imp - energy) * dt;
-            const float fr = (float)hp[S_IF] + (float)hp[S_CG] * tanhf(fabsf(action));
-            imp = imp * fmaxf(1.0f - dt * fr, 0.0f);
-            imp = imp + dt * (plast * brake * port - (float)hp[S_REST] * q - (float)hp[S_CUBIC] * (q * q * q));
-            q = clampf(q + dt * imp, -8.0f, 8.0f);
-            *D.impulse = imp;
-            *D.action = action;
-            *D.q = q;
+            const W sn = w_sqrt((W)(sh.tot[1] / N) + eps);
+            const W S = reservoir(*st(D.surprise), sn, hp[S_SD], D.step);
+            *st(D.surprise) = S;
+            const W port = (W)(sh.tot[0] / N);
+            const W dt = (W)hp[S_DT];
+            const W plast = W(1.0) + (W)hp[S_SG] * S / (W(1.0) + S);
+            const W brake = W(1.0) / (W(1.0) + (W)hp[S_SB] * S);
+            W imp = *st(D.impulse), q = q0, action = *st(D.action);
+            const W energy = W(0.5) * (imp * imp + q * q);
+            action = action * W(0.985) + (port * imp - energy) * dt;
+            const W fr = (W)hp[S_IF] + (W)hp[S_CG] * w_tanh(w_abs(action));
+            imp = imp * w_max(W(1.0) - dt * fr, W(0.0));
+            imp = imp + dt * (plast * brake * port - (W)hp[S_REST] * q - (W)hp[S_CUBIC] * (q * q * q));
+            q = clampw(q + dt * imp, -W(8.0), W(8.0));
+            *st(D.impulse) = imp;
+            *st(D.action) = action;
+            *st(D.q) = q;
             sh.q_new = q;
             sh.S = S;
-            const float clip = (float)hp[S_CLIP];
-            sh.sp = (float)hp[S_SPIKE] / (1.0f + S);
-            sh.invD = 1.0f / (clip * (1.0f + S));
+            const W clip = (W)hp[S_CLIP];
+            sh.sp = (W)hp[S_SPIKE] / (W(1.0) + S);
+            sh.invD = W(1.0) / (clip * (W(1.0) + S));
         }
         __syncthreads();
     }
 
-    const float qn = sh.q_new, S = sh.S, sp = sh.sp, invD = sh.invD;
-    const float clip = (float)hp[S_CLIP], inv_clip = 1.0f / clip, clip2 = (float)(hp[S_CLIP] * hp[S_CLIP]);
+    const W qn = sh.q_new, S = sh.S, sp = sh.sp, invD = sh.invD;
+    const W clip = (W)hp[S_CLIP], inv_clip = W(1.0) / clip, clip2 = (W)(hp[S_CLIP] * hp[S_CLIP]);
     struct Parts {
-        float u, root, t, nov, rat;
+        W u, root, t, nov, rat;
     };
     auto parts = [&](int64_t e, int64_t r, int64_t c) {
         Parts P;
         P.t = tangent(e, r, c);
-        const float at = fabsf(P.t);
-        P.rat = P.t / (1.0f + at * inv_clip);
-        const float bnd = tanhf(P.t * inv_clip) * clip;
-        P.root = sgnf_s(P.t) * sqrtf(fminf(at, clip2) + eps);
-        P.u = (1.0f - sp) * P.rat + sp * bnd;
-        P.nov = tanhf((P.t - qn) * invD) * clip;
+        const W at = w_abs(P.t);
+        P.rat = P.t / (W(1.0) + at * inv_clip);
+        const W bnd = w_tanh(P.t * inv_clip) * clip;
+        P.root = w_sgn(P.t) * w_sqrt(w_min(at, clip2) + eps);
+        P.u = (W(1.0) - sp) * P.rat + sp * bnd;
+        P.nov = w_tanh((P.t - qn) * invD) * clip;
         return P;
     };
 
@@ -350,7 +356,7 @@ __global__ void __launch_bounds__(kThreads) scalar_route_kernel(const ScalHdr* _
         walk_elems(D, [&](int64_t e, int64_t r, int64_t c, int, bool valid) {
             if (valid) {
                 const Parts P = parts(e, r, c);
-                const float v[5] = {P.u, P.root, P.t, qn, P.nov};
+                const W v[5] = {P.u, P.root, P.t, qn, P.nov};
                 int j = 0;
 #pragma unroll
                 for (int a = 0; a < 5; ++a)
@@ -367,29 +373,29 @@ __global__ void __launch_bounds__(kThreads) scalar_route_kernel(const ScalHdr* _
                 return G[a * 5 - (a * (a - 1)) / 2 + (b - a)];
             };
             enum { U = 0, RT = 1, TT = 2, PR = 3, NV = 4 };
-            const float frms = sqrtf((float)(Gm(TT, TT) / N) + eps);
-            const float prms = sqrtf((float)(Gm(PR, PR) / N) + eps);
-            const float align = clampf((float)(Gm(TT, PR) / N) / (frms * prms + eps), -1.0f, 1.0f);
-            const float align_gate = prms > (float)sqrt(hp[S_EPS]) ? clampf((align + 1.0f) * 0.5f, 0.0f, 1.0f) : 0.0f;
+            const W frms = w_sqrt((W)(Gm(TT, TT) / N) + eps);
+            const W prms = w_sqrt((W)(Gm(PR, PR) / N) + eps);
+            const W align = clampw((W)(Gm(TT, PR) / N) / (frms * prms + eps), -W(1.0), W(1.0));
+            const W align_gate = prms > (W)sqrt(hp[S_EPS]) ? clampw((align + W(1.0)) * W(0.5), W(0.0), W(1.0)) : W(0.0);
             const int ws = (int)hp[S_WS];
             const double warm = ws == 0 ? 1.0 : (1.0 - exp(-(double)D.step / (double)(ws > 1 ? ws : 1)));
-            const float mix = (float)(hp[S_PM] * warm) * align_gate / (1.0f + S);
-            const float rat_rms = sqrtf((float)(G[15] / N) + eps);
-            const float root_rms = sqrtf((float)(Gm(RT, RT) / N) + eps);
-            const float k_root = rat_rms / fmaxf(root_rms, eps);
-            const float root_mix = (float)hp[S_RCM] / (1.0f + 0.5f * S);
+            const W mix = (W)(hp[S_PM] * warm) * align_gate / (W(1.0) + S);
+            const W rat_rms = w_sqrt((W)(G[15] / N) + eps);
+            const W root_rms = w_sqrt((W)(Gm(RT, RT) / N) + eps);
+            const W k_root = rat_rms / w_max(root_rms, eps);
+            const W root_mix = (W)hp[S_RCM] / (W(1.0) + W(0.5) * S);
             const double a = 1.0 - (double)root_mix, b = (double)root_mix * (double)k_root;
             const double sh2 = a * a * Gm(U, U) + 2.0 * a * b * Gm(U, RT) + b * b * Gm(RT, RT);
-            const float shaped_rms = sqrtf((float)(sh2 / N) + eps);
-            const float dm = (float)hp[S_DFM] / (1.0f + 0.35f * S);
-            const float k_d = shaped_rms / fmaxf(frms, eps);
+            const W shaped_rms = w_sqrt((W)(sh2 / N) + eps);
+            const W dm = (W)hp[S_DFM] / (W(1.0) + W(0.35) * S);
+            const W k_d = shaped_rms / w_max(frms, eps);
             const double cu = (1.0 - dm) * a, cr = (1.0 - dm) * b, ctt = (double)dm * k_d;
             const double core2 = cu * cu * Gm(U, U) + cr * cr * Gm(RT, RT) + ctt * ctt * Gm(TT, TT) +
                                  2.0 * (cu * cr * Gm(U, RT) + cu * ctt * Gm(U, TT) + cr * ctt * Gm(RT, TT));
-            const float core_rms = sqrtf((float)(core2 / N) + eps);
-            const float resm = (float)hp[S_RFM] / (1.0f + S);
+            const W core_rms = w_sqrt((W)(core2 / N) + eps);
+            const W resm = (W)hp[S_RFM] / (W(1.0) + S);
             const double err2 = Gm(TT, TT) - 2.0 * Gm(TT, PR) + Gm(PR, PR);
-            const float k_r = core_rms / fmaxf(sqrtf((float)(fmax(err2, 0.0) / N) + eps), eps);
+            const W k_r = core_rms / w_max(w_sqrt((W)(fmax(err2, 0.0) / N) + eps), eps);
             double c[5];
             c[U] = (1.0 - mix) * cu;
             c[RT] = (1.0 - mix) * cr;
@@ -399,29 +405,29 @@ __global__ void __launch_bounds__(kThreads) scalar_route_kernel(const ScalHdr* _
             double d2 = 0.0;
             for (int i = 0; i < 5; ++i)
                 for (int j = 0; j < 5; ++j) d2 += c[i] * c[j] * Gm(i, j);
-            const float den = (float)(fmax(d2, 0.0) / N);
-            const float DE = reservoir(*D.drive_energy, den, hp[S_RD], D.step);
-            *D.drive_energy = DE;
-            sh.gain = clampf((float)hp[S_TGT] / sqrtf(DE + eps), (float)hp[S_MING], (float)hp[S_MAXG]);
-            sh.c_u = (float)c[U];
-            sh.c_root = (float)c[RT];
-            sh.c_t = (float)c[TT];
-            sh.c_pred = (float)c[PR];
-            sh.c_nov = (float)c[NV];
+            const W den = (W)(fmax(d2, 0.0) / N);
+            const W DE = reservoir(*st(D.drive_energy), den, hp[S_RD], D.step);
+            *st(D.drive_energy) = DE;
+            sh.gain = clampw((W)hp[S_TGT] / w_sqrt(DE + eps), (W)hp[S_MING], (W)hp[S_MAXG]);
+            sh.c_u = (W)c[U];
+            sh.c_root = (W)c[RT];
+            sh.c_t = (W)c[TT];
+            sh.c_pred = (W)c[PR];
+            sh.c_nov = (W)c[NV];
         }
         __syncthreads();
     }
 
     // ---- stage 5: parameter update  (cresso_v5.py:1582)
     {
-        const float cu = sh.c_u, cr = sh.c_root, ctt = sh.c_t, cp = sh.c_pred, cn = sh.c_nov, gain = sh.gain;
-        const float neg_lr = (float)(-hp[S_LR]);
-        const float neg_lr16 = neg_lr_in(hp[S_LR], D.dtype);
+        const W cu = sh.c_u, cr = sh.c_root, ctt = sh.c_t, cp = sh.c_pred, cn = sh.c_nov, gain = sh.gain;
+        const W neg_lr = (W)(-hp[S_LR]);
+        const W neg_lr16 = neg_lr_w<W>(hp[S_LR], D.dtype);
         walk_elems(D, [&](int64_t e, int64_t r, int64_t c, int, bool valid) {
             if (valid) {
                 const Parts P = parts(e, r, c);
-                const float drive = cu * P.u + cr * P.root + ctt * P.t + cp * qn + cn * P.nov;
-                apply_update(D.param, e, D.dtype, neg_lr, neg_lr16, drive * gain);
+                const W drive = cu * P.u + cr * P.root + ctt * P.t + cp * qn + cn * P.nov;
+                apply_update_w<W>(D.param, e, D.dtype, neg_lr, neg_lr16, drive * gain);
             }
         });
     }
@@ -829,8 +835,10 @@ static int scal_layout(const cresso_tensor_desc* descs, int64_t n, std::vector<S
     if (out) out->assign(n, ScalTensor{});
     for (int64_t i = 0; i < n; ++i) {
         const cresso_tensor_desc& d = descs[i];
-        CRESSO_REQUIRE(d.dtype == CRESSO_DTYPE_F32 || d.dtype == CRESSO_DTYPE_F16 || d.dtype == CRESSO_DTYPE_BF16,
-                       CRESSO_EUNSUPPORTED, "tensor %lld: dtype code %lld (float32, float16 and bfloat16 are supported)",
+        CRESSO_REQUIRE(d.dtype == CRESSO_DTYPE_F32 || d.dtype == CRESSO_DTYPE_F16 || d.dtype == CRESSO_DTYPE_BF16 ||
+                           d.dtype == CRESSO_DTYPE_F64,
+                       CRESSO_EUNSUPPORTED,
+                       "tensor %lld: dtype code %lld (float32, float16, bfloat16 and float64 are supported)",
                        (long long)i, (long long)d.dtype);
         CRESSO_REQUIRE(d.ndim >= 0 && d.ndim <= CRESSO_MAX_NDIM, CRESSO_EUNSUPPORTED,
                        "tensor %lld: ndim %lld outside [0, %d]", (long long)i, (long long)d.ndim, CRESSO_MAX_NDIM);
@@ -838,7 +846,8 @@ static int scal_layout(const cresso_tensor_desc* descs, int64_t n, std::vector<S
             CRESSO_REQUIRE(d.shape[a] >= 1, CRESSO_EINVAL, "tensor %lld: empty dimension", (long long)i);
         int TC, RPI, n_ct, nw;
         int64_t rows, cols;
-        const int64_t wf = scal_work_floats(d, &TC, &RPI, &n_ct, &nw, &rows, &cols);
+        // float64 tensors keep their work values in float64: two float slots each
+        const int64_t wf = scal_work_floats(d, &TC, &RPI, &n_ct, &nw, &rows, &cols) * (d.dtype == CRESSO_DTYPE_F64 ? 2 : 1);
         if (out) {
             ScalTensor& S = (*out)[i];
             S.ndim = d.ndim;
@@ -887,7 +896,7 @@ struct ClGeom {
     int64_t chunk, lrows, lcols, ld, shortlen;
 };
 static bool cl_geometry(const ScalTensor& S, int cs, ClGeom* g) {
-    if (S.ndim > 2) return false;
+    if (S.ndim > 2 || S.dtype == CRESSO_DTYPE_F64) return false;  // the cluster form works in float32
     g->sr = S.ndim == 2 && S.rows >= S.cols;
     const int64_t longlen = g->sr ? S.rows : S.cols;
     g->shortlen = g->sr ? S.cols : S.rows;
@@ -939,8 +948,14 @@ static int scal_launch(std::vector<ScalTensor>& dts, const cresso_hparams* hp, c
         short_cap = std::max(short_cap, g.shortlen);
         ord.push_back(S);
     }
+    int64_t n_f32 = 0;  // general-form tensors of float32 work, then the float64 ones
     for (int64_t i = 0; i < n; ++i)
-        if (!fits[i]) ord.push_back(dts[i]);
+        if (!fits[i] && dts[i].dtype != CRESSO_DTYPE_F64) {
+            ord.push_back(dts[i]);
+            ++n_f32;
+        }
+    for (int64_t i = 0; i < n; ++i)
+        if (!fits[i] && dts[i].dtype == CRESSO_DTYPE_F64) ord.push_back(dts[i]);
     ScalHdr h{};
     h.n = n;
     memcpy(h.hp, hp, sizeof(cresso_hparams));
@@ -968,9 +983,13 @@ static int scal_launch(std::vector<ScalTensor>& dts, const cresso_hparams* hp, c
         CRESSO_CUDA(cudaLaunchKernelEx(&cfg, scalar_cluster_kernel, dh, dd, (int)slice_cap, (int)loc_cap, (int)short_cap));
         CRESSO_LAUNCHED("scalar_cluster_kernel");
     }
-    if (n_cl < n) {
-        scalar_route_kernel<<<(unsigned)(n - n_cl), kThreads, 0, s>>>(dh, dd + n_cl);
-        CRESSO_LAUNCHED("scalar_route_kernel");
+    if (n_f32 > 0) {
+        scalar_route_kernel<float><<<(unsigned)n_f32, kThreads, 0, s>>>(dh, dd + n_cl);
+        CRESSO_LAUNCHED("scalar_route_kernel<float>");
+    }
+    if (n_cl + n_f32 < n) {
+        scalar_route_kernel<double><<<(unsigned)(n - n_cl - n_f32), kThreads, 0, s>>>(dh, dd + n_cl + n_f32);
+        CRESSO_LAUNCHED("scalar_route_kernel<double>");
     }
     return CRESSO_OK;
 }

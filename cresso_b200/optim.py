@@ -41,7 +41,7 @@ __all__ = ["CRESSO5", "CRESSO", "count_optimizer_state_elements", "theoretical_s
 
 # parameter element types of the CUDA path and their descriptor codes; the work and the
 # state are float32 for all three (cresso_v5.py:119-124)
-_DTYPES = {torch.float32: 0, torch.float16: 1, torch.bfloat16: 2}
+_DTYPES = {torch.float32: 0, torch.float16: 1, torch.bfloat16: 2, torch.float64: 3}
 
 _SPECTRAL_RANK_STATE = ("q_cos", "q_sin", "p_cos", "p_sin", "metric_cos", "metric_sin", "metric_p_cos",
                         "metric_p_sin", "calcium_cos", "calcium_sin", "mode_confidence")
@@ -366,8 +366,8 @@ class CRESSO5(Optimizer):
                     raise RuntimeError(
                         "CRESSO5 cuda_ops='required' requires every optimized parameter to be a CUDA parameter")
                 if param.dtype not in _DTYPES:
-                    raise RuntimeError("CRESSO5 B200 path supports float32, float16 and bfloat16 parameters "
-                                       f"(got {param.dtype})")
+                    raise RuntimeError("CRESSO5 B200 path supports float32, float16, bfloat16 and float64 "
+                                       f"parameters (got {param.dtype})")
                 if not param.is_contiguous():
                     raise RuntimeError("CRESSO5 B200 path updates parameters in place and needs them contiguous")
                 if grad.dtype is not param.dtype or grad.device != param.device:
@@ -375,11 +375,13 @@ class CRESSO5(Optimizer):
                 if not grad.is_contiguous():
                     grad = grad.contiguous()
                 state = self.state[param]
+                # work and state type: float64 for float64 parameters, else float32 (cresso_v5.py:119-124)
+                wdt = torch.float64 if param.dtype is torch.float64 else torch.float32
                 if micro > 0 and param.ndim > 0 and param.numel() <= micro:  # cresso_v5.py:839-840
                     if getattr(param, "_cresso_shard", None) is not None:
                         raise RuntimeError("micro-field tensors are not sharded: pass them whole")
                     if len(state) == 0:
-                        self._init_micro(param, torch.float32)
+                        self._init_micro(param, wdt)
                     state["step"] += 1
                     micro_items.setdefault(param.device, []).append((param, grad, state))
                     continue
@@ -388,6 +390,9 @@ class CRESSO5(Optimizer):
                 if spectral_route is None:
                     spectral_route = self._route_cache[rkey] = self._use_spectral_route(param, group)
                 if spectral_route:
+                    if param.dtype is torch.float64:
+                        raise RuntimeError("CRESSO5 B200 path: float64 parameters are supported on the scalar and "
+                                           "micro-field routes, not on the spectral route")
                     if len(state) == 0:
                         self._init_spectral(param, group, torch.float32, self._geometry(param)[0])
                     state["step"] += 1
@@ -396,7 +401,7 @@ class CRESSO5(Optimizer):
                     if getattr(param, "_cresso_shard", None) is not None:
                         raise RuntimeError("scalar-route (small / LoRA-thin) tensors are not sharded: pass them whole")
                     if len(state) == 0:
-                        self._init_scalar(param, torch.float32)
+                        self._init_scalar(param, wdt)
                     state["step"] += 1
                     scalar.setdefault(param.device, []).append((param, grad, state))
             hp = None

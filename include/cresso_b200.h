@@ -85,15 +85,17 @@ typedef struct cresso_tensor_desc {
     /* scalar route 0-d state (float32): */
     uint64_t q, impulse, metric_q, metric_impulse;
     /* element type of param and grad (CRESSO_DTYPE_*); the work and the state are
-     * float32 for all three, and a float16 / bfloat16 parameter receives the
-     * update rounded to its type first, as param.add_(update.to(param.dtype))
-     * does (cresso_v5.py:119-124, 1353, 1582) */
+     * float32 for float32 / float16 / bfloat16 parameters, and a float16 / bfloat16
+     * parameter receives the update rounded to its type first, as
+     * param.add_(update.to(param.dtype)) does (cresso_v5.py:119-124, 1353, 1582).
+     * float64 parameters (scalar and micro routes only) work in float64 and their
+     * state pointers point at float64 values. */
     int64_t dtype;
     /* micro-field route state: float32 fields of the parameter's shape */
     uint64_t micro_energy, micro_impulse, micro_refractory;
 } cresso_tensor_desc;
 
-enum { CRESSO_DTYPE_F32 = 0, CRESSO_DTYPE_F16 = 1, CRESSO_DTYPE_BF16 = 2 };
+enum { CRESSO_DTYPE_F32 = 0, CRESSO_DTYPE_F16 = 1, CRESSO_DTYPE_BF16 = 2, CRESSO_DTYPE_F64 = 3 };
 
 /* ---------------------------------------------------------------- info --- */
 

@@ -109,6 +109,14 @@ EXTRA_CASES = {
     "micro_300x7_bf16": ((300, 7), dict(micro_field_max_size=4096), 3, 58, 0.02, 1e-3, "bfloat16"),
     "micro_2x3x4x5_f16": ((2, 3, 4, 5), dict(micro_field_max_size=4096, weight_decay=0.05), 3, 59, 0.02, 1e-3,
                           "float16"),
+    # float64 parameters: float64 work and state on the scalar and micro-field routes
+    "scal64_256x16": ((256, 16), dict(rank=4, hash_bins=64, hash_tables=2), 3, 61, 0.02, 1e-3, "float64"),
+    "scal64_7x9_wd": ((7, 9), dict(weight_decay=0.01, maximize=True), 3, 62, 0.02, 1e-3, "float64"),
+    "scal64_3x4x5": ((3, 4, 5), dict(instant_metric_power=0.7), 3, 63, 0.02, 1e-3, "float64"),
+    "scal64_1024x16": ((1024, 16), dict(rank=4), 3, 64, 0.01, 1e-3, "float64"),
+    "micro64_30x20": ((30, 20), dict(micro_field_max_size=1000), 3, 65, 0.02, 1e-3, "float64"),
+    "micro64_2x3x4": ((2, 3, 4), dict(micro_field_max_size=100, maximize=True, weight_decay=0.02), 3, 66, 0.02, 1e-3,
+                      "float64"),
 }
 
 
@@ -122,7 +130,9 @@ def run_steps(ref, shape, kwargs, steps, seed, init_std, grad_std, dtype=torch.f
         p.grad = g.clone()
         opt.step()
     st = opt.state[p]
-    out = {"final": p.detach().float().numpy().copy(),
+    # float64 results stay float64; the other types are stored as float32, which holds them exactly
+    final = p.detach().numpy() if dtype == torch.float64 else p.detach().float().numpy()
+    out = {"final": final.copy(),
            "init_sum": np.asarray(init.double().sum().item()),
            "grad_sum": np.asarray(sum(g.double().abs().sum().item() for g in grads))}
     if init.numel() <= 4096:

@@ -94,9 +94,10 @@ EXTRA_CASES = extra_cases()
 @pytest.mark.parametrize("name", list(EXTRA_CASES.keys()))
 def test_extra_golden_parity(golden_extra, name):
     """The second golden table against the reference's own output: float16 /
-    bfloat16 parameters (spectral and scalar routes) and spectral tensors of
+    bfloat16 parameters (spectral and scalar routes), spectral tensors of
     rank 3 to 5 (leading axes flattened into rows, carriers and the instant
-    metric composed over every axis).
+    metric composed over every axis), the micro-field route and float64
+    parameters (scalar and micro-field routes, float64 work and state).
 
     float32 parameters: the criterion of the float32 golden cases.  16-bit
     parameters: every element within one unit in the last place of the
@@ -125,6 +126,20 @@ def test_extra_golden_parity(golden_extra, name):
               if k.startswith(f"step_{name}_state_") and k != f"step_{name}_state_elements"}
     assert set(opt.state[p].keys()) == set(st_ref.keys())
     assert cresso_b200.count_optimizer_state_elements(opt) == int(golden_extra[f"step_{name}_state_elements"])
+    if dt == "float64":
+        # float64 work and state: every value within 1e-9 relative RMS of the reference's
+        # (float32 arithmetic would be ~1e-7 off); the update within 1e-8 of its own size
+        got = p.detach().cpu().numpy()
+        init64 = init.double().numpy()
+        assert rel_rms(got, ref) <= 1e-12, name
+        assert rel_rms(got - init64, ref - init64) <= 1e-8, (name, rel_rms(got - init64, ref - init64))
+        for k, v in opt.state[p].items():
+            if not torch.is_tensor(v):
+                assert v == int(st_ref[k]), (name, k)
+                continue
+            assert v.dtype == torch.float64, (name, k)
+            assert rel_rms(v.cpu().numpy(), st_ref[k]) <= 1e-9, (name, k, rel_rms(v.cpu().numpy(), st_ref[k]))
+        return
     if dt == "float32":
         st_ref = {k: (torch.from_numpy(v) if v.ndim > 0 or v.dtype.kind == "f" else int(v)) for k, v in st_ref.items()}
         st = {k: (v.detach().cpu() if torch.is_tensor(v) else v) for k, v in opt.state[p].items()}
@@ -376,3 +391,18 @@ def test_mixed_routes_in_one_group(micro):
         for k, v in ref.state[r].items():
             if torch.is_tensor(v) and v.dtype.is_floating_point:
                 assert rel_rms(opt.state[p][k].cpu(), v) <= 5e-3, (s, k)
+
+
+def test_float64_spectral_route_is_rejected():
+    """float64 parameters run on the scalar and micro-field routes; a float64
+    tensor that routes to the spectral path is refused with a clear error."""
+    p = torch.nn.Parameter(torch.zeros((64, 64), dtype=torch.float64, device="cuda"))
+    p.grad = torch.ones_like(p)
+    opt = cresso_b200.CRESSO5([p])
+    with pytest.raises(RuntimeError, match="float64"):
+        opt.step()
+    q = torch.nn.Parameter(torch.zeros((64, 64), dtype=torch.float64, device="cuda"))
+    q.grad = torch.full_like(q, 1e-3)
+    opt = cresso_b200.CRESSO5([q], micro_field_max_size=4096)
+    opt.step()
+    assert opt.state[q]["micro_energy"].dtype == torch.float64 and float(q.detach().abs().max()) > 0

@@ -90,8 +90,9 @@ def test_full_steps_bit_exact(golden, name):
 @pytest.mark.parametrize("name", list(extra_cases().keys()))
 def test_extra_steps_bit_exact(golden_extra, name):
     """float16 / bfloat16 parameters (fp32 work and state, update rounded to the
-    parameter type before the add) and spectral tensors of rank 3 to 5: the
-    oracle reproduces the reference bit for bit."""
+    parameter type before the add), float64 parameters (float64 work and state),
+    spectral tensors of rank 3 to 5 and the micro-field route: the oracle
+    reproduces the reference bit for bit."""
     torch.set_num_threads(1)
     shape, kw, steps, seed, istd, gstd, dt = extra_cases()[name]
     init, grads = extra_case_inputs(golden_extra, name, shape, steps, seed, istd, gstd, dt)
@@ -101,10 +102,10 @@ def test_extra_steps_bit_exact(golden_extra, name):
         p.grad = g.clone()
         opt.step()
     assert p.dtype == getattr(torch, dt)
-    np.testing.assert_array_equal(p.detach().float().numpy(), golden_extra[f"step_{name}_final"])
+    np.testing.assert_array_equal(p.detach().double().numpy(), golden_extra[f"step_{name}_final"].astype(np.float64))
     for k, v in opt.state[p].items():
         ref = golden_extra[f"step_{name}_state_{k}"]
         got = v.numpy() if torch.is_tensor(v) else np.asarray(v)
         if torch.is_tensor(v) and torch.is_floating_point(v):
-            assert v.dtype == torch.float32, k
+            assert v.dtype == (torch.float64 if dt == "float64" else torch.float32), k
         np.testing.assert_array_equal(got.astype(ref.dtype), ref, err_msg=k)
