@@ -10,7 +10,10 @@ gate, up (11008, 4096), down (4096, 11008) and two (4096,) norms --
 rank 8, 64 hash bins, 2 tables, init N(0, 0.02), grads N(0, 1e-3), synthetic.
 With N GPUs every tensor is row-sharded over the ranks (RowShardedCRESSO5: a
 float64 NCCL all-reduce of the per-pass partial sums between passes), so the
-total work is fixed ("scaling": "strong").
+total work is fixed ("scaling": "strong").  `--sharding zero` instead gives
+every rank the full (replicated) set and partitions whole tensors
+(ZeroCRESSO5; `--bucket-elements` > 0 overlaps each bucket's all-gather with
+the next bucket's compute).
 
 Metric: CRESSO5 ms/step and achieved HBM GB/s; `value` is the
 whole-job algorithmic bandwidth 12 B x parameter elements / step time
@@ -243,19 +246,20 @@ def reference_arm(args, world, rank):
 def b200_arm(args, world, rank, local):
     import cresso_b200
     from cresso_b200 import _lib
-    from cresso_b200.distributed import RowShardedCRESSO5, mark_row_shard, row_block
+    from cresso_b200.distributed import RowShardedCRESSO5, ZeroCRESSO5, mark_row_shard, row_block
 
     device = torch.device("cuda", local)
+    zero = world > 1 and args.sharding == "zero"  # ZeRO-1: whole tensors, replicated inputs
     torch.cuda.set_device(device)
     shapes, kw, istd = workload_shapes(args.workload)
     params, grads_dev = [], []
     pdt = {"f32": torch.float32, "bf16": torch.bfloat16, "f16": torch.float16}[args.dtype]
     bpe = 3 * torch.empty((), dtype=pdt).element_size()  # grad read + param read + param write
     gen = torch.Generator(device=device)
-    gen.manual_seed(1234 + rank)
+    gen.manual_seed(1234 + (0 if zero else rank))
     n_local = 0
     for i, s in enumerate(shapes):
-        if world > 1:
+        if world > 1 and not zero:
             start, stop = row_block(s[0], rank, world)
             local_shape = (stop - start,) + tuple(s[1:])
         else:
@@ -263,7 +267,7 @@ def b200_arm(args, world, rank, local):
         p = torch.empty(local_shape, device=device)
         p.normal_(0.0, istd, generator=gen)
         p = torch.nn.Parameter(p.to(pdt))
-        if world > 1:
+        if world > 1 and not zero:
             mark_row_shard(p, s, start)
         g = torch.empty(local_shape, device=device)
         g.normal_(0.0, 1e-3, generator=gen)
@@ -276,7 +280,12 @@ def b200_arm(args, world, rank, local):
         grads_dev.append(g)
         n_local += numel(local_shape)
     n_total = sum(numel(s) for s in shapes)
-    opt = RowShardedCRESSO5(params, **kw) if world > 1 else cresso_b200.CRESSO5(params, **kw)
+    if zero:
+        opt = ZeroCRESSO5(params, bucket_elements=args.bucket_elements, **kw)
+        n_local = sum(p.numel() for p in params if opt.owner[p] == rank)
+        args.skip_e2e = True  # non-owned tensors carry no state to read back
+    else:
+        opt = RowShardedCRESSO5(params, **kw) if world > 1 else cresso_b200.CRESSO5(params, **kw)
     stream = torch.cuda.current_stream(device)
 
     for _ in range(args.warmup):
@@ -343,7 +352,10 @@ def b200_arm(args, world, rank, local):
             "config": {"workload": f"{args.workload}: " + (f"7B-shaped {args.dtype} set, 290 tensors, 6,738,411,520 elements"
                                                             if args.workload == "c5" else str(shapes[0])),
                        "rank": kw["rank"], "hash_bins": kw["hash_bins"], "hash_tables": kw["hash_tables"],
-                       "sharding": f"row-sharded over {world} GPU(s)" if world > 1 else "single GPU",
+                       "sharding": (f"ZeRO-1 over {world} GPU(s), {len(opt.buckets)} bucket(s) of >= "
+                                    f"{args.bucket_elements} elements, all-gather of bucket k under the compute of "
+                                    f"bucket k + 1" if zero else
+                                    f"row-sharded over {world} GPU(s)" if world > 1 else "single GPU"),
                        "l2": "no flush: inputs of every step (grads + params) exceed the 126 MB L2"
                              if n_total * 8 > 2 * 126e6 else "inputs fit in L2",
                        "elements": n_total, "per_pass_ms": {k: round(v, 4) for k, v in pass_ms.items()},
@@ -367,6 +379,9 @@ def time_passes(opt, args, world, device, stream):
     from cresso_b200 import _lib
     import torch.distributed as dist
 
+    from cresso_b200.distributed import RowShardedCRESSO5
+
+    exchange = isinstance(opt, RowShardedCRESSO5)  # row sharding all-reduces between passes
     acc = {k: 0.0 for k in PASS_STAGE}
     acc["SCALAR"] = 0.0
     reps = max(1, min(args.steps, 3))
@@ -393,7 +408,7 @@ def time_passes(opt, args, world, device, stream):
                 events.append((name, a, b))
             else:
                 run(st, st + 1)
-            if st + 1 in bounds and world > 1:
+            if st + 1 in bounds and world > 1 and exchange:
                 k += 1
                 dist.all_reduce(opt._reduction_view(scratch, layout, k))
 
@@ -485,6 +500,10 @@ def main():
     ap.add_argument("--dtype", choices=["f32", "bf16", "f16"], default="f32",
                     help="parameter / gradient type (work and state are float32 for all)")
     ap.add_argument("--skip-cpu", action="store_true")
+    ap.add_argument("--sharding", choices=["row", "zero"], default="row",
+                    help="N > 1: row sharding (default) or ZeRO-1 whole-tensor partition")
+    ap.add_argument("--bucket-elements", type=int, default=0,
+                    help="ZeRO-1: elements per all-gather bucket (0: one bucket after the step)")
     args = ap.parse_args()
     world, rank, local = dist_setup(args)
     try:

@@ -21,7 +21,9 @@ spreading one optimizer step over the GPUs of a box are provided:
     Whole tensors are assigned to ranks by a longest-processing-time greedy
     partition on element counts.  A rank steps only the tensors it owns (no
     collective during the step) and the updated tensors are then
-    all-gathered, so every rank ends with the full updated parameters.
+    all-gathered, so every rank ends with the full updated parameters.  With
+    ``bucket_elements`` the owned tensors go in buckets whose all-gather runs
+    while the next bucket computes.
 """
 
 from __future__ import annotations
@@ -95,9 +97,17 @@ class RowShardedCRESSO5(CRESSO5):
 
 class ZeroCRESSO5(CRESSO5):
     """ZeRO-1 style CRESSO5: each rank steps the whole tensors it owns, then
-    the updated parameters are all-gathered."""
+    the updated parameters are all-gathered.
 
-    def __init__(self, params: Iterable[Tensor], process_group=None, **kwargs):
+    With ``bucket_elements > 0`` the owned tensors of every rank are cut, in
+    parameter order, into runs of at least that many elements; bucket k is the
+    k-th run of every rank.  The step computes bucket k, starts its all-gather
+    asynchronously (NCCL runs it on its own stream) and goes on with bucket
+    k + 1, so the exchange of one bucket overlaps the compute of the next;
+    the gathered values are copied into the parameters at the end of the step.
+    Every rank derives the same plan from the shapes alone."""
+
+    def __init__(self, params: Iterable[Tensor], process_group=None, bucket_elements: int = 0, **kwargs):
         super().__init__(params, **kwargs)
         self.process_group = process_group
         world = dist.get_world_size(process_group) if dist.is_initialized() else 1
@@ -107,49 +117,101 @@ class ZeroCRESSO5(CRESSO5):
         self.owner: Dict[Tensor, int] = {}
         for p, r in zip(all_params, lpt_partition([p.numel() for p in all_params], world)):
             self.owner[p] = r
+        self.bucket_elements = int(bucket_elements)
+        self.buckets = self._plan_buckets(all_params)
+
+    def _plan_buckets(self, all_params: List[Tensor]) -> List[List[List[Tensor]]]:
+        """buckets[k][r]: rank r's tensors of bucket k (possibly none)."""
+        chunks = []
+        for r in range(self.world):
+            runs: List[List[Tensor]] = []
+            cur: List[Tensor] = []
+            n = 0
+            for p in all_params:
+                if self.owner[p] != r:
+                    continue
+                cur.append(p)
+                n += p.numel()
+                if self.bucket_elements > 0 and n >= self.bucket_elements:
+                    runs.append(cur)
+                    cur, n = [], 0
+            if cur or not runs:
+                runs.append(cur)
+            chunks.append(runs)
+        k_max = max(len(c) for c in chunks)
+        return [[chunks[r][k] if k < len(chunks[r]) else [] for r in range(self.world)] for k in range(k_max)]
 
     @torch.no_grad()
     def step(self, closure=None):  # type: ignore[override]
-        hidden = []
-        for g in self.param_groups:
-            for p in g["params"]:
-                if self.owner[p] != self.rank and p.grad is not None:
-                    hidden.append((p, p.grad))
-                    p.grad = None
-        try:
-            loss = super().step(closure)
-        finally:
-            for p, gr in hidden:
-                p.grad = gr
-        if self.world > 1:
-            self.gather_params()
+        loss = None
+        if closure is not None:
+            with torch.enable_grad():
+                loss = closure()
+        pending: list = []  # all-gathers of the previous bucket, still in flight
+        for bucket in self.buckets:
+            mine = {id(p) for p in bucket[self.rank]}
+            hidden = []
+            for g in self.param_groups:
+                for p in g["params"]:
+                    if id(p) not in mine and p.grad is not None:
+                        hidden.append((p, p.grad))
+                        p.grad = None
+            try:
+                super().step()
+            finally:
+                for p, gr in hidden:
+                    p.grad = gr
+            if self.world > 1:
+                started = self._gather_bucket_async(bucket)
+                # the previous bucket's exchange ran while this bucket computed; its
+                # values go into the parameters now (at most two buckets in flight)
+                for item in pending:
+                    self._finish_gather(item)
+                pending = started
+        for item in pending:
+            self._finish_gather(item)
         return loss
 
-    @torch.no_grad()
-    def gather_params(self) -> None:
-        """All-gathers every rank's owned parameters into all ranks."""
-        groups: Dict[torch.dtype, List[Tensor]] = {}
-        for g in self.param_groups:
-            for p in g["params"]:
-                groups.setdefault(p.dtype, []).append(p)
-        for dtype, params in groups.items():
-            per_rank = [[p for p in params if self.owner[p] == r] for r in range(self.world)]
-            sizes = [sum(p.numel() for p in ps) for ps in per_rank]
-            width = max(max(sizes), 1)
-            dev = params[0].device
+    def _gather_bucket_async(self, bucket: List[List[Tensor]]) -> list:
+        """Starts the all-gathers of one bucket (one per dtype); returns their handles."""
+        dtypes = []
+        for ps in bucket:
+            for p in ps:
+                if p.dtype not in dtypes:
+                    dtypes.append(p.dtype)
+        out_items = []
+        for dtype in dtypes:
+            per_rank = [[p for p in ps if p.dtype == dtype] for ps in bucket]
+            width = max(max(sum(p.numel() for p in ps) for ps in per_rank), 1)
+            dev = next(p for ps in per_rank for p in ps).device
             local = torch.zeros(width, dtype=dtype, device=dev)
             if per_rank[self.rank]:
-                flat = torch.cat([p.reshape(-1) for p in per_rank[self.rank]])
+                flat = torch.cat([p.detach().reshape(-1) for p in per_rank[self.rank]])
                 local[: flat.numel()].copy_(flat)
             out = torch.empty(width * self.world, dtype=dtype, device=dev)
             if dist.get_backend(self.process_group) == "nccl":
-                dist.all_gather_into_tensor(out, local, group=self.process_group)
+                work = dist.all_gather_into_tensor(out, local, group=self.process_group, async_op=True)
             else:
-                dist.all_gather(list(out.chunk(self.world)), local, group=self.process_group)
-            for r, ps in enumerate(per_rank):
-                if r == self.rank:
-                    continue
-                off = r * width
-                for p in ps:
-                    p.copy_(out[off:off + p.numel()].view_as(p))
-                    off += p.numel()
+                work = dist.all_gather(list(out.chunk(self.world)), local, group=self.process_group, async_op=True)
+            out_items.append((per_rank, width, out, local, work))
+        return out_items
+
+    def _finish_gather(self, item) -> None:
+        per_rank, width, out, _local, work = item
+        work.wait()
+        for r, ps in enumerate(per_rank):
+            if r == self.rank:
+                continue
+            off = r * width
+            for p in ps:
+                p.detach().copy_(out[off:off + p.numel()].view_as(p))
+                off += p.numel()
+
+    @torch.no_grad()
+    def gather_params(self) -> None:
+        """All-gathers every rank's owned parameters into all ranks, bucket by bucket."""
+        pending = []
+        for bucket in self.buckets:
+            pending.extend(self._gather_bucket_async(bucket))
+        for item in pending:
+            self._finish_gather(item)

@@ -54,19 +54,63 @@ def stages_worker(rank, world, port, outdir):
     dist.destroy_process_group()
 
 
-def zero_gather_worker(rank, world, port, outdir):
+def zero_gather_worker(rank, world, port, outdir, bucket_elements=0):
     from cresso_b200.distributed import ZeroCRESSO5
 
     _init(rank, world, port, "gloo")
-    shapes = [(7, 5), (13,), (4, 4), (30,), (2, 3)]
+    shapes = [(7, 5), (13,), (4, 4), (30,), (2, 3), (3, 3, 3), (11,), (5, 8)]
     ps = [torch.nn.Parameter(torch.full(s, -1.0)) for s in shapes]
-    opt = ZeroCRESSO5(ps)
+    ps[6].data = ps[6].data.double()  # a second dtype: one all-gather per (bucket, dtype)
+    opt = ZeroCRESSO5(ps, bucket_elements=bucket_elements)
     for i, p in enumerate(ps):
         if opt.owner[p] == rank:
             p.data.fill_(float(100 * i + 7))
     opt.gather_params()
-    torch.save({"vals": [p.detach().clone() for p in ps], "owner": [opt.owner[p] for p in ps]},
-               os.path.join(outdir, f"zero_{rank}.pt"))
+    index = {id(p): j for j, p in enumerate(ps)}
+    plan = [[[index[id(p)] for p in run] for run in bucket] for bucket in opt.buckets]
+    torch.save({"vals": [p.detach().clone() for p in ps], "owner": [opt.owner[p] for p in ps], "plan": plan},
+               os.path.join(outdir, f"zero_{rank}_{bucket_elements}.pt"))
+    dist.destroy_process_group()
+
+
+def zero_gather_bucketed_worker(rank, world, port, outdir):
+    zero_gather_worker(rank, world, port, outdir, bucket_elements=20)
+
+
+def gpu_zero_worker(rank, world, port, outdir):
+    """Bucketed ZeRO-1 CUDA step on `world` GPUs against the single-GPU step."""
+    import cresso_b200
+    from cresso_b200.distributed import ZeroCRESSO5
+
+    torch.cuda.set_device(rank)
+    _init(rank, world, port, "nccl", timeout_s=120)
+    dev = torch.device("cuda", rank)
+    g = torch.Generator().manual_seed(4)
+    shapes = [(256, 192), (1536,), (96, 64), (512, 16), (7, 9), (128, 128), (4, 8, 3, 3)]
+    inits = [torch.randn(s, generator=g) * 0.02 for s in shapes]
+    grads = [[torch.randn(s, generator=g) * 1e-3 for s in shapes] for _ in range(3)]
+    kw = dict(rank=8, hash_bins=64, hash_tables=2)
+    ps = [torch.nn.Parameter(x.clone().to(dev)) for x in inits]
+    opt = ZeroCRESSO5(ps, bucket_elements=20000, **kw)
+    for gs in grads:
+        for p, gg in zip(ps, gs):
+            p.grad = gg.clone().to(dev)
+        opt.step()
+    torch.cuda.synchronize()
+    out = [p.detach().cpu() for p in ps]
+    ref_out = None
+    if rank == 0:
+        full = [torch.nn.Parameter(x.clone().to(dev)) for x in inits]
+        ref = cresso_b200.CRESSO5(full, **kw)
+        for gs in grads:
+            for p, gg in zip(full, gs):
+                p.grad = gg.to(dev)
+            ref.step()
+        torch.cuda.synchronize()
+        ref_out = [p.detach().cpu() for p in full]
+    torch.save({"params": out, "ref": ref_out, "n_buckets": len(opt.buckets),
+                "owned": [opt.owner[p] == rank for p in ps]}, os.path.join(outdir, f"gpu_zero_{rank}.pt"))
+    dist.barrier()
     dist.destroy_process_group()
 
 

@@ -54,13 +54,21 @@ def test_row_sharded_stage_orchestration_gloo(tmp_path):
         assert torch.all(a == 3.0 * k)
 
 
-def test_zero_partition_gathers_owned_params_gloo(tmp_path):
-    spawn(W.zero_gather_worker, 2, tmp_path)
-    r0 = torch.load(tmp_path / "zero_0.pt")
-    r1 = torch.load(tmp_path / "zero_1.pt")
+@pytest.mark.parametrize("bucketed", [False, True])
+def test_zero_partition_gathers_owned_params_gloo(tmp_path, bucketed):
+    spawn(W.zero_gather_bucketed_worker if bucketed else W.zero_gather_worker, 2, tmp_path)
+    be = 20 if bucketed else 0
+    r0 = torch.load(tmp_path / f"zero_0_{be}.pt")
+    r1 = torch.load(tmp_path / f"zero_1_{be}.pt")
     assert set(r0["owner"]) == {0, 1}
+    assert r0["plan"] == r1["plan"]  # every rank derives the same bucket plan
+    assert (len(r0["plan"]) > 1) == bucketed
     for i, (a, b) in enumerate(zip(r0["vals"], r1["vals"])):
         assert torch.all(a == 100 * i + 7) and torch.equal(a, b)
+    # each tensor is in exactly one bucket, under its owner
+    seen = sorted(i for bucket in r0["plan"] for r, run in enumerate(bucket) for i in run
+                  if r0["owner"][i] == r)
+    assert seen == list(range(len(r0["vals"])))
 
 
 def test_failed_rank_surfaces_as_an_error_not_a_hang_gloo(tmp_path):
@@ -101,3 +109,17 @@ def test_row_sharded_step_matches_single_gpu(tmp_path):
                     assert d <= 1e-4 * max(float(v.double().abs().max()), 1e-6), (i, k, d)
             else:
                 assert a == v == b
+
+
+@pytest.mark.gpu
+def test_zero_bucketed_step_matches_single_gpu(tmp_path):
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    spawn(W.gpu_zero_worker, 2, tmp_path)
+    r = [torch.load(tmp_path / f"gpu_zero_{k}.pt") for k in range(2)]
+    assert r[0]["n_buckets"] > 1
+    for i, full in enumerate(r[0]["ref"]):
+        a, b = r[0]["params"][i], r[1]["params"][i]
+        assert torch.equal(a, b), i  # every rank ends with the owner's values
+        rel = float((a.double() - full.double()).pow(2).mean().sqrt() / full.double().pow(2).mean().sqrt())
+        assert rel <= 1e-6, (i, rel)
