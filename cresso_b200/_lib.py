@@ -57,7 +57,7 @@ EXPORTS = (
     "cresso_hash_cache_init", "cresso_shape_workspace_bytes", "cresso_shape_workspace_init",
     "cresso_basis_project", "cresso_basis_reconstruct", "cresso_instant_axis_metric",
     "cresso_spectral_layout", "cresso_spectral_run", "cresso_scalar_scratch_bytes", "cresso_scalar_run",
-    "cresso_scalar_run_noalloc", "cresso_micro_scratch_bytes", "cresso_micro_run",
+    "cresso_scalar_run_noalloc", "cresso_micro_scratch_bytes", "cresso_micro_run", "cresso_selftest_bounded_wait",
 )
 
 _lock = threading.Lock()
@@ -94,6 +94,7 @@ def _declare(lib) -> None:
         "cresso_scalar_run_noalloc": (ctypes.c_int, [_p, _i64, _p, _p]),
         "cresso_micro_scratch_bytes": (ctypes.c_int, [_p, _i64, _pi64]),
         "cresso_micro_run": (ctypes.c_int, [_p, _i64, _p, _p, _i64, _p]),
+        "cresso_selftest_bounded_wait": (ctypes.c_int, [_i64, _i64, _p, _p]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)

@@ -7,9 +7,32 @@
 
 #include <atomic>
 
+#include <stdlib.h>
+
+#include <nvtx3/nvToolsExt.h>
+
 #include "cresso_status.h"
 
 namespace cresso {
+
+bool nvtx_enabled() {
+    static const bool on = [] {
+        const char* v = getenv("CRESSO_B200_NVTX");
+        return v != nullptr && v[0] != '\0' && !(v[0] == '0' && v[1] == '\0');
+    }();
+    return on;
+}
+
+void nvtx_push(const char* fmt, ...) {
+    char name[160];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(name, sizeof(name), fmt, ap);
+    va_end(ap);
+    nvtxRangePushA(name);
+}
+
+void nvtx_pop() { nvtxRangePop(); }
 
 static thread_local char g_last_error[1024] = {0};
 static std::atomic<int64_t> g_launches{0};

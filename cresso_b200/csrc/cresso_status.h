@@ -14,6 +14,25 @@ int check_cuda(cudaError_t e, const char* what);
 // Status of the last kernel launch on this thread (cudaGetLastError).
 int check_launch(const char* what);
 
+// NVTX ranges around the library's launches, on when the environment variable
+// CRESSO_B200_NVTX is set to a value other than "0" when the library first
+// checks it (a profiler then shows one range per entry call and per stage).
+bool nvtx_enabled();
+void nvtx_push(const char* fmt, ...);
+void nvtx_pop();
+struct NvtxRange {
+    bool on;
+    template <typename... Args>
+    explicit NvtxRange(const char* fmt, Args... args) : on(nvtx_enabled()) {
+        if (on) nvtx_push(fmt, args...);
+    }
+    ~NvtxRange() {
+        if (on) nvtx_pop();
+    }
+    NvtxRange(const NvtxRange&) = delete;
+    NvtxRange& operator=(const NvtxRange&) = delete;
+};
+
 }  // namespace cresso
 
 #define CRESSO_REQUIRE(cond, code, ...)                    \

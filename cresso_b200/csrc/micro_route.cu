@@ -360,6 +360,7 @@ int cresso_micro_run(const cresso_tensor_desc* descs, int64_t n, const cresso_hp
     std::stable_partition(dts.begin(), dts.end(), [](const MicroTensor& M) { return M.dtype != CRESSO_DTYPE_F64; });
     int64_t n32 = 0;
     for (const auto& M : dts) n32 += M.dtype != CRESSO_DTYPE_F64;
+    NvtxRange range("cresso_micro_run %lld tensors", (long long)n);
     MicroHdr h{};
     h.n = n;
     memcpy(h.hp, hp, sizeof(cresso_hparams));

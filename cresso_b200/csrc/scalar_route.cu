@@ -1017,6 +1017,7 @@ int cresso_scalar_run(const cresso_tensor_desc* descs, int64_t n, const cresso_h
                    (long long)scratch_bytes, (long long)bytes);
     char* base = (char*)scratch;
     for (auto& S : dts) S.work = (float*)(base + (intptr_t)S.work);
+    NvtxRange range("cresso_scalar_run %lld tensors", (long long)n);
     return scal_launch(dts, hp, base, (cudaStream_t)stream);
 }
 

@@ -1948,6 +1948,26 @@ static int launch_half_widen(const Plan& P, char* base, cudaStream_t s) {
     return CRESSO_OK;
 }
 
+// The bounded mbarrier wait of the tensor-core passes, on an mbarrier that
+// completes only when `arrive` is set (one arrival by lane 0 before the wait):
+// without it nothing ever arrives, the wait runs out after limit_ns and the
+// kernel stores 1 in *status (0 when the phase completed).  No tensor-core
+// work and no TMEM are involved, so running out leaves nothing in flight.
+__global__ void bounded_wait_selftest_kernel(uint64_t limit_ns, bool arrive, int32_t* status) {
+    __shared__ __align__(8) uint64_t bar;
+    if (threadIdx.x == 0) mbar_init(&bar, 1);
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        if (arrive) {
+            uint64_t token;
+            asm volatile("mbarrier.arrive.shared::cta.b64 %0, [%1];" : "=l"(token) : "r"(smem_u32(&bar)) : "memory");
+            (void)token;
+        }
+        const bool ok = mbar_wait_bounded(smem_u32(&bar), 0, limit_ns);
+        *status = ok ? 0 : 1;
+    }
+}
+
 template <int RM, int NT>
 static int launch_stage(int stage, const Plan& P, char* base, cudaStream_t s) {
     const GroupHdr* hdr = reinterpret_cast<const GroupHdr*>(base + P.off_hdr);
@@ -2051,6 +2071,16 @@ int cresso_spectral_layout(const cresso_tensor_desc* descs, int64_t n, const cre
     return CRESSO_OK;
 }
 
+int cresso_selftest_bounded_wait(int64_t limit_ns, int64_t arrive, void* status_word, cresso_stream_t stream) {
+    CRESSO_REQUIRE(status_word != nullptr, CRESSO_EINVAL, "selftest_bounded_wait: NULL status word");
+    CRESSO_REQUIRE(limit_ns >= 0 && limit_ns <= 2000000000LL, CRESSO_EINVAL,
+                   "selftest_bounded_wait: limit must be in [0, 2 s]");
+    bounded_wait_selftest_kernel<<<1, 32, 0, (cudaStream_t)stream>>>((uint64_t)limit_ns, arrive != 0,
+                                                                      reinterpret_cast<int32_t*>(status_word));
+    CRESSO_LAUNCHED("bounded_wait_selftest_kernel");
+    return CRESSO_OK;
+}
+
 int cresso_spectral_run(const cresso_tensor_desc* descs, int64_t n, const cresso_hparams* hp, void* scratch,
                         int64_t scratch_bytes, int64_t stage_begin, int64_t stage_end, int64_t num_sms,
                         cresso_stream_t stream) {
@@ -2064,6 +2094,8 @@ int cresso_spectral_run(const cresso_tensor_desc* descs, int64_t n, const cresso
                    "spectral_run: stages must satisfy 0 <= begin <= end <= %d", kStages);
     char* base = (char*)scratch;
     cudaStream_t s = (cudaStream_t)stream;
+    NvtxRange range("cresso_spectral_run %lld tensors, stages [%lld, %lld)", (long long)n, (long long)stage_begin,
+                    (long long)stage_end);
     bind_scratch(P, base);
     P.hdr.status = reinterpret_cast<int32_t*>(base + P.off_status);
     if (stage_begin == 0) {
@@ -2077,7 +2109,12 @@ int cresso_spectral_run(const cresso_tensor_desc* descs, int64_t n, const cresso
         const int hs = launch_half_widen(P, base, s);
         if (hs) return hs;
     }
+    static const char* const kStageName[kStages] = {
+        "upload",     "P1 force energy", "reduce 1", "finalize 1", "P2 density / bins / projection",
+        "reduce 2",   "finalize 2",      "P3 tangent / port", "reduce 3", "finalize 3",
+        "P4 drive Gram", "reduce 4",     "finalize 4", "P5 update"};
     for (int64_t stage = std::max<int64_t>(stage_begin, 1); stage < stage_end; ++stage) {
+        NvtxRange stage_range("cresso stage %lld: %s", (long long)stage, kStageName[stage]);
         const int nt = P.hdr.tables == 1 ? 1 : (P.hdr.tables == 2 ? 2 : 0);
         switch (P.rm * 4 + nt) {
             case 16: st = launch_stage<4, 0>((int)stage, P, base, s); break;

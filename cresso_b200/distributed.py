@@ -207,6 +207,25 @@ class ZeroCRESSO5(CRESSO5):
                 p.detach().copy_(out[off:off + p.numel()].view_as(p))
                 off += p.numel()
 
+    def consolidate_state_dict(self, to: int = 0) -> Optional[dict]:
+        """The optimizer state of all ranks (each holds the state of the tensors it
+        owns) as one ``state_dict`` in the reference layout, on rank ``to``; the
+        other ranks get None.  It loads into CRESSO5 (or the reference's
+        optimizer) like a single-process state_dict."""
+        sd = self.state_dict()
+        if self.world == 1:
+            return sd
+        local = {k: {n: (v.detach().cpu() if torch.is_tensor(v) else v) for n, v in st.items()}
+                 for k, st in sd["state"].items()}
+        parts = [None] * self.world if self.rank == to else None
+        dist.gather_object(local, parts, dst=to, group=self.process_group)
+        if self.rank != to:
+            return None
+        merged: Dict[int, dict] = {}
+        for part in parts:
+            merged.update(part)
+        return {"state": {k: merged[k] for k in sorted(merged)}, "param_groups": sd["param_groups"]}
+
     @torch.no_grad()
     def gather_params(self) -> None:
         """All-gathers every rank's owned parameters into all ranks, bucket by bucket."""

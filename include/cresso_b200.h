@@ -199,6 +199,15 @@ CRESSO_API int cresso_instant_axis_metric(const float* rel, int64_t ndim, const 
  * layout[11] = bit p set when pass Pp of the full-tile tensors runs on the
  *              tcgen05 tensor cores (p = 3, 4, 5). */
 enum { CRESSO_SPECTRAL_STAGES = 14 };
+
+/* Self-test of the bounded in-kernel wait that guards the tensor-core passes
+ * (no counterpart in the reference): one block waits on an mbarrier that
+ * completes only if `arrive` is nonzero, for at most limit_ns (<= 2 s), then
+ * stores 1 in the device int32 *status_word if the wait ran out, else 0.  It
+ * shows on a live GPU that a wait which nothing satisfies ends with an error
+ * status the host reads, and the context stays usable. */
+CRESSO_API int cresso_selftest_bounded_wait(int64_t limit_ns, int64_t arrive, void* status_word,
+                                            cresso_stream_t stream);
 CRESSO_API int cresso_spectral_layout(const cresso_tensor_desc* descs, int64_t n, const cresso_hparams* hp,
                            int64_t num_sms, int64_t* layout, int64_t layout_len);
 CRESSO_API int cresso_spectral_run(const cresso_tensor_desc* descs, int64_t n, const cresso_hparams* hp, void* scratch,

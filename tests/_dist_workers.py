@@ -184,3 +184,20 @@ def gpu_row_shard_worker(rank, world, port, outdir):
     torch.save({"shard": shard, "states": states, "ref": ref_out}, os.path.join(outdir, f"gpu_rs_{rank}.pt"))
     dist.barrier()
     dist.destroy_process_group()
+
+
+def zero_consolidate_worker(rank, world, port, outdir):
+    """consolidate_state_dict on CPU ranks: each rank fakes the state of the
+    tensors it owns (as a step would leave it); rank 0 collects all of them."""
+    from cresso_b200.distributed import ZeroCRESSO5
+
+    _init(rank, world, port, "gloo")
+    shapes = [(7, 5), (13,), (4, 4), (30,), (2, 3)]
+    ps = [torch.nn.Parameter(torch.zeros(s)) for s in shapes]
+    opt = ZeroCRESSO5(ps)
+    for i, p in enumerate(ps):
+        if opt.owner[p] == rank:
+            opt.state[p] = {"step": 3, "force_rms": torch.tensor(float(i)), "q": torch.full((2,), float(10 * i))}
+    sd = opt.consolidate_state_dict(to=0)
+    torch.save({"sd": sd, "owner": [opt.owner[p] for p in ps]}, os.path.join(outdir, f"consolidate_{rank}.pt"))
+    dist.destroy_process_group()

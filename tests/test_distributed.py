@@ -71,6 +71,19 @@ def test_zero_partition_gathers_owned_params_gloo(tmp_path, bucketed):
     assert seen == list(range(len(r0["vals"])))
 
 
+def test_zero_consolidate_state_dict_gloo(tmp_path):
+    spawn(W.zero_consolidate_worker, 2, tmp_path)
+    r0 = torch.load(tmp_path / "consolidate_0.pt")
+    r1 = torch.load(tmp_path / "consolidate_1.pt")
+    assert r1["sd"] is None
+    sd = r0["sd"]
+    assert sorted(sd["state"].keys()) == list(range(5))  # every tensor, whichever rank owned it
+    for i, st in sd["state"].items():
+        assert st["step"] == 3 and float(st["force_rms"]) == float(i) and torch.all(st["q"] == 10 * i)
+    assert set(r0["owner"]) == {0, 1}
+    assert len(sd["param_groups"]) == 1 and sd["param_groups"][0]["params"] == list(range(5))
+
+
 def test_failed_rank_surfaces_as_an_error_not_a_hang_gloo(tmp_path):
     ctx = mp.get_context("spawn")
     port = free_port()

@@ -15,6 +15,7 @@ Tolerances (stated per check):
 """
 
 import copy
+import os
 
 import numpy as np
 import pytest
@@ -22,7 +23,7 @@ import torch
 
 import cresso_b200
 from oracle import cresso5_oracle as O
-from tests._cases import case_inputs, extra_case_inputs, extra_cases, golden_cases, rel_rms, ulp_distance
+from tests._cases import ROOT, case_inputs, extra_case_inputs, extra_cases, golden_cases, rel_rms, ulp_distance
 
 pytestmark = pytest.mark.gpu
 
@@ -406,3 +407,50 @@ def test_float64_spectral_route_is_rejected():
     opt = cresso_b200.CRESSO5([q], micro_field_max_size=4096)
     opt.step()
     assert opt.state[q]["micro_energy"].dtype == torch.float64 and float(q.detach().abs().max()) > 0
+
+
+def test_bounded_wait_runs_out_and_reports_status():
+    """The bounded in-kernel wait that guards the tensor-core passes, on a GPU:
+    an mbarrier nothing arrives on makes the wait give up after its limit and
+    report status 1; with the arrival it reports 0; the context stays usable."""
+    from cresso_b200 import _lib, ops
+    L = _lib.lib()
+    st = torch.full((2,), 7, dtype=torch.int32, device="cuda")
+    stream = torch.cuda.current_stream().cuda_stream
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    _lib.check(L.cresso_selftest_bounded_wait(2_000_000, 0, st[0:1].data_ptr(), stream), "selftest")
+    e1.record()
+    _lib.check(L.cresso_selftest_bounded_wait(2_000_000, 1, st[1:2].data_ptr(), stream), "selftest")
+    torch.cuda.synchronize()
+    assert st.tolist() == [1, 0]
+    assert 2.0 <= e0.elapsed_time(e1) < 1000.0  # gave up after its 2 ms limit, not before
+    idx = ops.hash_index((1024,), 64, 0, "cuda")  # the context still runs work
+    assert int(idx.max()) < 64
+
+
+def test_nvtx_ranges_switch_on_without_changing_results():
+    """CRESSO_B200_NVTX=1 wraps the entry calls and stages in NVTX ranges; the
+    step is unchanged (a child process, so the switch is read at load)."""
+    import subprocess
+    import sys
+    code = (
+        "import torch, cresso_b200\n"
+        "g = torch.Generator().manual_seed(0)\n"
+        "ps = [torch.nn.Parameter((torch.randn(s, generator=g) * 0.02).cuda()) for s in [(256, 256), (512, 16), (9,)]]\n"
+        "opt = cresso_b200.CRESSO5(ps, rank=8, hash_bins=64, micro_field_max_size=16)\n"
+        "for _ in range(2):\n"
+        "    for p in ps: p.grad = torch.full_like(p, 1e-3)\n"
+        "    opt.step()\n"
+        "torch.cuda.synchronize()\n"
+        "print(repr([float(p.double().sum()) for p in ps]))\n"
+    )
+    env = dict(os.environ)
+    outs = []
+    for flag in ("0", "1"):
+        env["CRESSO_B200_NVTX"] = flag
+        r = subprocess.run([sys.executable, "-c", code], env=env, cwd=str(ROOT), capture_output=True, text=True,
+                           timeout=300)
+        assert r.returncode == 0, r.stderr[-2000:]
+        outs.append(r.stdout.strip().splitlines()[-1])
+    assert outs[0] == outs[1]
