@@ -58,6 +58,8 @@ EXPORTS = (
     "cresso_basis_project", "cresso_basis_reconstruct", "cresso_instant_axis_metric",
     "cresso_spectral_layout", "cresso_spectral_run", "cresso_scalar_scratch_bytes", "cresso_scalar_run",
     "cresso_scalar_run_noalloc", "cresso_micro_scratch_bytes", "cresso_micro_run", "cresso_selftest_bounded_wait",
+    "cresso_shape_workspace64_bytes", "cresso_shape_workspace64_init", "cresso_spectral64_scratch_bytes",
+    "cresso_spectral64_run",
 )
 
 _lock = threading.Lock()
@@ -95,6 +97,10 @@ def _declare(lib) -> None:
         "cresso_micro_scratch_bytes": (ctypes.c_int, [_p, _i64, _pi64]),
         "cresso_micro_run": (ctypes.c_int, [_p, _i64, _p, _p, _i64, _p]),
         "cresso_selftest_bounded_wait": (ctypes.c_int, [_i64, _i64, _p, _p]),
+        "cresso_shape_workspace64_bytes": (ctypes.c_int, [_i64, _pi64, _i64, _pi64]),
+        "cresso_shape_workspace64_init": (ctypes.c_int, [_i64, _pi64, _i64, _pi64, _p, _p]),
+        "cresso_spectral64_scratch_bytes": (ctypes.c_int, [_p, _i64, _p, _pi64]),
+        "cresso_spectral64_run": (ctypes.c_int, [_p, _i64, _p, _p, _i64, _p]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)

@@ -112,8 +112,10 @@ __device__ void axis_value(const ModeParam& m, const AxisParam& ax, int64_t idx,
     }
 }
 
-__global__ void build_tables_kernel(ModePack modes, int rank, int rm, int64_t grows, int64_t gcols, float* rowtab,
-                                    float* coltab) {
+// Axis tables in T (float for the float32 path, double for float64 tensors).
+template <typename T>
+__global__ void build_tables_kernel(ModePack modes, int rank, int rm, int64_t grows, int64_t gcols, T* rowtab,
+                                    T* coltab) {
     const int64_t total = (grows + gcols) * rm;
     for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < total; t += (int64_t)gridDim.x * blockDim.x) {
         const int k = (int)(t % rm);
@@ -149,19 +151,20 @@ __global__ void build_tables_kernel(ModePack modes, int rank, int rm, int64_t gr
             }
         }
         if (idx < grows) {
-            rowtab[(idx * rm + k) * 2 + 0] = (float)x1;
-            rowtab[(idx * rm + k) * 2 + 1] = (float)x2;
+            rowtab[(idx * rm + k) * 2 + 0] = (T)x1;
+            rowtab[(idx * rm + k) * 2 + 1] = (T)x2;
         } else {
             const int64_t j = idx - grows;
-            coltab[(2 * k) * gcols + j] = (float)x1;
-            coltab[(2 * k + 1) * gcols + j] = (float)x2;
+            coltab[(2 * k) * gcols + j] = (T)x1;
+            coltab[(2 * k + 1) * gcols + j] = (T)x2;
         }
     }
 }
 
 // Block 0 sums the row table, block 1 the column table: S1[p] = sum x_p and
 // S2[p][q] = sum x_p x_q over the axis, p = 2k + (0 | 1), in float64.
-__global__ void table_sums_kernel(const float* rowtab, const float* coltab, int rm, int64_t grows, int64_t gcols,
+template <typename T>
+__global__ void table_sums_kernel(const T* rowtab, const T* coltab, int rm, int64_t grows, int64_t gcols,
                                   double* tmp) {
     const int P = 2 * rm;
     const bool rows = blockIdx.x == 0;
@@ -664,10 +667,10 @@ int cresso_shape_workspace_init(int64_t ndim, const int64_t* shape, int64_t rank
     float* coltab = reinterpret_cast<float*>(base + h.off_coltab);
     double* tmp = reinterpret_cast<double*>(base + h.off_tmp);
     const int64_t cells = (grows + gcols) * rm;
-    build_tables_kernel<<<(int)std::min<int64_t>(ceil_div(cells, kThreads), 4096), kThreads, 0, s>>>(
+    build_tables_kernel<float><<<(int)std::min<int64_t>(ceil_div(cells, kThreads), 4096), kThreads, 0, s>>>(
         modes, (int)rank, rm, grows, gcols, rowtab, coltab);
     CRESSO_LAUNCHED("build_tables_kernel");
-    table_sums_kernel<<<2, kThreads, 0, s>>>(rowtab, coltab, rm, grows, gcols, tmp);
+    table_sums_kernel<float><<<2, kThreads, 0, s>>>(rowtab, coltab, rm, grows, gcols, tmp);
     CRESSO_LAUNCHED("table_sums_kernel");
     stats_gram_kernel<<<1, kThreads, 0, s>>>(modes, (int)rank, rm, (double)grows * (double)gcols, tmp,
                                               reinterpret_cast<ModeStats*>(base + h.off_stats),
@@ -687,6 +690,49 @@ int cresso_shape_workspace_init(int64_t ndim, const int64_t* shape, int64_t rank
         counts_to_float_kernel<<<1, kThreads, 0, s>>>(bins * tables, counts);
         CRESSO_LAUNCHED("counts_to_float_kernel");
     }
+    CRESSO_CUDA(cudaMemcpyAsync(ws, &h, sizeof(h), cudaMemcpyHostToDevice, s));
+    // the header lives on this stack frame: finish the copy before returning
+    CRESSO_CUDA(cudaStreamSynchronize(s));
+    return CRESSO_OK;
+}
+
+int cresso_shape_workspace64_bytes(int64_t ndim, const int64_t* shape, int64_t rank, int64_t* bytes) {
+    int64_t grows, gcols;
+    int st = checked_shape(ndim, shape, &grows, &gcols);
+    if (st) return st;
+    CRESSO_REQUIRE(bytes != nullptr, CRESSO_EINVAL, "shape_workspace64_bytes: NULL output");
+    CRESSO_REQUIRE(rank >= 1 && rank <= kMaxRank, CRESSO_EUNSUPPORTED,
+                   "rank must be in [1, %d] on the CUDA path (got %lld)", kMaxRank, (long long)rank);
+    *bytes = shape_ws64_layout(ndim, grows, gcols, rank, rank_pad(rank)).bytes;
+    return CRESSO_OK;
+}
+
+int cresso_shape_workspace64_init(int64_t ndim, const int64_t* shape, int64_t rank, const int64_t* freqs, void* ws,
+                                  cresso_stream_t stream) {
+    int64_t grows, gcols;
+    int st = checked_shape(ndim, shape, &grows, &gcols);
+    if (st) return st;
+    CRESSO_REQUIRE(rank >= 1 && rank <= kMaxRank, CRESSO_EUNSUPPORTED,
+                   "rank must be in [1, %d] on the CUDA path (got %lld)", kMaxRank, (long long)rank);
+    CRESSO_REQUIRE(freqs != nullptr && ws != nullptr, CRESSO_EINVAL, "shape_workspace64_init: NULL pointer");
+    const int rm = rank_pad(rank);
+    ShapeWsHeader h = shape_ws64_layout(ndim, grows, gcols, rank, rm);
+    cudaStream_t s = (cudaStream_t)stream;
+    char* base = (char*)ws;
+    ModePack modes = make_modes(ndim, shape, rank, freqs);
+    double* rowtab = reinterpret_cast<double*>(base + h.off_rowtab);
+    double* coltab = reinterpret_cast<double*>(base + h.off_coltab);
+    double* tmp = reinterpret_cast<double*>(base + h.off_tmp);
+    const int64_t cells = (grows + gcols) * rm;
+    build_tables_kernel<double><<<(int)std::min<int64_t>(ceil_div(cells, kThreads), 4096), kThreads, 0, s>>>(
+        modes, (int)rank, rm, grows, gcols, rowtab, coltab);
+    CRESSO_LAUNCHED("build_tables_kernel<double>");
+    table_sums_kernel<double><<<2, kThreads, 0, s>>>(rowtab, coltab, rm, grows, gcols, tmp);
+    CRESSO_LAUNCHED("table_sums_kernel<double>");
+    stats_gram_kernel<<<1, kThreads, 0, s>>>(modes, (int)rank, rm, (double)grows * (double)gcols, tmp,
+                                              reinterpret_cast<ModeStats*>(base + h.off_stats),
+                                              reinterpret_cast<double*>(base + h.off_gram));
+    CRESSO_LAUNCHED("stats_gram_kernel");
     CRESSO_CUDA(cudaMemcpyAsync(ws, &h, sizeof(h), cudaMemcpyHostToDevice, s));
     // the header lives on this stack frame: finish the copy before returning
     CRESSO_CUDA(cudaStreamSynchronize(s));

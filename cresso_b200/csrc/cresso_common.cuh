@@ -99,6 +99,35 @@ __host__ inline ShapeWsHeader shape_ws_layout(int64_t ndim, int64_t grows, int64
     return h;
 }
 
+// Float64 shape workspace (float64 parameters on the spectral route): float64
+// axis tables rowtab [grows][rm][2] and coltab [2 rm][gcols], the carrier stats
+// and Gram from them; no hash counts.
+constexpr int64_t kShapeWs64Magic = 0x43524553534f3544LL;  // "CRESSO5D"
+__host__ inline ShapeWsHeader shape_ws64_layout(int64_t ndim, int64_t grows, int64_t gcols, int64_t rank, int64_t rm) {
+    ShapeWsHeader h{};
+    h.magic = kShapeWs64Magic;
+    h.ndim = ndim;
+    h.grows = grows;
+    h.gcols = gcols;
+    h.rank = rank;
+    h.rm = rm;
+    h.n = grows * gcols;
+    int64_t off = align_up((int64_t)sizeof(ShapeWsHeader), 256);
+    h.off_rowtab = off;
+    off = align_up(off + grows * rm * 2 * 8, 256);
+    h.off_coltab = off;
+    off = align_up(off + 2 * rm * gcols * 8, 256);
+    h.off_stats = off;
+    off = align_up(off + 64 * kMaxRank, 256);  // ModeStats: 8 doubles per mode
+    h.off_gram = off;
+    off = align_up(off + (2 * rm) * (2 * rm) * 8, 256);
+    h.off_tmp = off;
+    off = align_up(off + 2 * (2 * rm + 4 * rm * rm) * 8, 256);
+    h.off_counts = off;
+    h.bytes = off;
+    return h;
+}
+
 __host__ __device__ inline int rank_pad(int64_t rank) { return rank <= 4 ? 4 : (rank <= 8 ? 8 : 16); }
 
 // ---------------------------------------------------------------------------

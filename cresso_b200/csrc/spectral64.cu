@@ -1,0 +1,862 @@
+// Spectral-route CRESSO5 step for float64 parameters (cresso_v5.py:945-1353
+// with float64 work and state, cresso_v5.py:119-124).
+//
+// The float32 path (spectral.cu) is built around float32 tiles, tf32 tensor-core
+// reconstructions and fixed-point bin sums; a float64 tensor instead runs this
+// plain float64 pipeline, one tensor after another, with the same five passes
+// and the same reductions between them:
+//   P1 force energy | fin1 scale
+//   P2 density, hash-bin sums and counts, density projections
+//      (+ row sums / column sums of the instant-metric density, rank >= 2)
+//      | fin2 hash energy and bin log-metric, metric oscillator, instant factors
+//   P3 tangent (kept in the scratch), error, port and tangent projections,
+//      port bin sums | fin3 surprise, hash impulse, confidence, contact
+//      oscillators, second prediction and echo coefficients
+//   P4 drive Gram of (rational, bounded, root, tangent, prediction, novelty,
+//      echo, hash prediction) | fin4 drive coefficients, drive energy, gain
+//   P5 parameter update
+// Carriers come from the float64 axis tables of a float64 shape workspace
+// (cresso_shape_workspace64_init).  Block partial sums are written per block and
+// added in block order by the one-block finalize kernels; the bin sums inside a
+// block use shared-memory float64 atomics (their order, and so the last bit of
+// a bin sum, can vary from run to run).
+#include <cuda_runtime.h>
+#include <math.h>
+#include <stdint.h>
+
+#include <algorithm>
+#include <vector>
+
+#include "basis_dev.cuh"
+#include "cresso_common.cuh"
+#include "cresso_status.h"
+
+namespace cresso {
+
+namespace {
+
+constexpr int kMaxTB64 = 2048;  // hash_bins * hash_tables on the float64 path
+constexpr int kGram64 = 36;     // pair sums of 8 drive vectors
+constexpr int kMaxBlocks64 = 256;
+constexpr int kMaxLeadSum64 = 4096;  // sum of the leading axis lengths (rank >= 3)
+
+enum {
+    Q_LR, Q_WD, Q_EP, Q_DT, Q_IF, Q_CG, Q_REST, Q_CUBIC, Q_MDT, Q_MF, Q_MC, Q_LS, Q_IC, Q_IP, Q_RCM, Q_EM, Q_TM,
+    Q_HD, Q_HID, Q_HMC, Q_HDM, Q_DFM, Q_RFM, Q_RD, Q_REFD, Q_RG, Q_CD, Q_CONFG, Q_SG, Q_SD, Q_PM, Q_NM, Q_WS, Q_SB,
+    Q_TGT, Q_MING, Q_MAXG, Q_CLIP, Q_SPIKE, Q_EPS, Q_MAX, Q_RANK, Q_MAXF, Q_BINS, Q_TABLES, Q_HARDMIN, Q_THINCUT,
+    Q_MD, Q_MID, Q_MDM, Q_COUNT
+};
+static_assert(sizeof(cresso_hparams) == Q_COUNT * sizeof(double), "cresso_hparams field order");
+
+struct T64 {
+    int64_t ndim, N, rows, cols, step;
+    int64_t dims[CRESSO_MAX_NDIM];
+    double* param;
+    const double* grad;
+    const double* rowtab;  // [rows][rm][2]
+    const double* coltab;  // [2 rm][cols]
+    const ModeStats* stats;
+    double *omega, *q_cos, *q_sin, *p_cos, *p_sin, *m_cos, *m_sin, *mp_cos, *mp_sin, *ca_cos, *ca_sin, *conf;
+    double *h_energy, *h_impulse, *h_refractory, *force_rms, *drive_energy, *surprise, *action;
+    int32_t R, T, B, hard, hash_on, echo_on, inst, local_on;
+    double hp[64];
+};
+
+// Per-tensor values passed from the finalize kernels to the pass kernels.
+struct C64 {
+    double scale, gm, kk, meanL, S, clip;
+    double m_al[kMaxRank], m_be[kMaxRank];  // log-metric reconstruction (shrink * metric oscillator)
+    double p_al[kMaxRank], p_be[kMaxRank];  // prediction (shrink * gate * q), P3: old q, P4/P5: new q
+    double e_al[kMaxRank], e_be[kMaxRank];  // echo reconstruction (shrink * tangent projection)
+    double c[8], gain;                      // drive = sum c_i v_i
+};
+
+struct Buf64 {
+    C64* cst;
+    double* rec;     // [blocks][L]
+    double* lterm;   // [T * B] per-bin log hash metric (P3)
+    double* impv;    // [T * B] hash impulse per bin (P4 / P5)
+    double* counts;  // [T * B] elements per bin
+    double* rowsum;  // [rows] instant-metric density per row, then its log factor
+    double* colsum;  // [cols] same per column
+    double* tbuf;    // [N] tangent
+    int blocks;
+};
+
+__device__ __forceinline__ double clampd(double v, double lo, double hi) { return fmin(fmax(v, lo), hi); }
+__device__ __forceinline__ double sigmoidd(double x) { return 1.0 / (1.0 + exp(-x)); }
+__device__ __forceinline__ double sgnd(double x) { return x > 0.0 ? 1.0 : (x < 0.0 ? -1.0 : 0.0); }
+
+// Normalised carriers (cos, sin) of modes 0..RM-1 at row r, column c.
+template <int RM>
+__device__ __forceinline__ void carriers(const T64& D, int64_t r, int64_t c, double (&ch)[RM], double (&sh)[RM]) {
+#pragma unroll
+    for (int k = 0; k < RM; ++k) {
+        const double a1 = D.rowtab[(r * RM + k) * 2], a2 = D.rowtab[(r * RM + k) * 2 + 1];
+        const double b1 = D.coltab[(int64_t)(2 * k) * D.cols + c], b2 = D.coltab[(int64_t)(2 * k + 1) * D.cols + c];
+        double rc, rs;
+        if (mode_is_product(k)) {
+            rc = a1 * b1;
+            rs = a2 * b2;
+        } else {
+            rc = a1 * b1 - a2 * b2;
+            rs = a1 * b2 + a2 * b1;
+        }
+        const ModeStats& m = D.stats[k];
+        ch[k] = (rc - m.mu_c) * m.inv_c;
+        sh[k] = (rs - m.mu_s) * m.inv_s;
+    }
+}
+
+template <int RM>
+__device__ __forceinline__ double recon(const double* al, const double* be, const double (&ch)[RM],
+                                        const double (&sh)[RM]) {
+    double out = 0.0;
+#pragma unroll
+    for (int k = 0; k < RM; ++k) {
+        out += ch[k] * al[k];
+        out += sh[k] * be[k];
+    }
+    return out;
+}
+
+__device__ __forceinline__ double force_of(const T64& D, int64_t e) {
+    double f = (D.hp[Q_MAX] != 0.0 ? -1.0 : 1.0) * D.grad[e];
+    if (D.hp[Q_WD] != 0.0) f = f + D.hp[Q_WD] * D.param[e];
+    return f;
+}
+
+__device__ __forceinline__ double rel_of(const T64& D, double scale, double f) {
+    return fmin(fabs(f) / scale + D.hp[Q_EPS], 1.0e4);
+}
+
+__device__ __forceinline__ double idens_of(const T64& D, double rel) {
+    const double pw = fmax(D.hp[Q_IP], 0.25);
+    return fmin(pow(fmax(rel, D.hp[Q_EPS]), pw), 1.0e6);
+}
+
+// Block sum of v[0..L) into rec[blockIdx.x * L ...]; every thread calls.
+template <int L>
+__device__ __forceinline__ void block_record(double (&v)[L], double* red, double* rec) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    for (int j = 0; j < L; ++j) {
+        const double s = warp_sum(v[j]);
+        if (lane == 0) red[warp] = s;
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            double t = 0.0;
+            for (int w = 0; w < kWarps; ++w) t += red[w];
+            rec[j] = t;
+        }
+        __syncthreads();
+    }
+}
+
+// ---- P1: force energy
+__global__ void __launch_bounds__(kThreads) s64_p1(T64 D, Buf64 Bf) {
+    __shared__ double red[kWarps];
+    double v[1] = {0.0};
+    for (int64_t e = blockIdx.x * (int64_t)kThreads + threadIdx.x; e < D.N; e += (int64_t)gridDim.x * kThreads) {
+        const double f = force_of(D, e);
+        v[0] += f * f;
+    }
+    block_record<1>(v, red, Bf.rec + (int64_t)blockIdx.x * 1);
+}
+
+__global__ void s64_fin1(T64 D, Buf64 Bf) {
+    if (threadIdx.x != 0) return;
+    double s = 0.0;
+    for (int b = 0; b < Bf.blocks; ++b) s += Bf.rec[b];
+    const double eps = D.hp[Q_EPS];
+    const double frn = sqrt(s / (double)D.N + eps);
+    const double fr = reservoir(*D.force_rms, frn, D.hp[Q_RD], D.step);
+    *D.force_rms = fr;
+    Bf.cst->scale = fmax(fr, eps);
+}
+
+// ---- P2: density, bins, projections.  Record: [sum L, sum dens, sum L c_k (RM), sum L s_k (RM),
+// bin sums (TB), bin counts (TB)]
+template <int RM>
+__global__ void __launch_bounds__(kThreads) s64_p2(T64 D, Buf64 Bf) {
+    __shared__ double red[kWarps];
+    extern __shared__ double sbin[];  // [TB] sums, then [TB] counts
+    const int TB = D.T * D.B;
+    const bool hash_on = D.hash_on != 0;
+    if (hash_on)
+        for (int i = threadIdx.x; i < 2 * TB; i += kThreads) sbin[i] = 0.0;
+    __syncthreads();
+    const double scale = Bf.cst->scale, ep = D.hp[Q_EP];
+    double v[2 + 2 * RM];
+#pragma unroll
+    for (int j = 0; j < 2 + 2 * RM; ++j) v[j] = 0.0;
+    for (int64_t e = blockIdx.x * (int64_t)kThreads + threadIdx.x; e < D.N; e += (int64_t)gridDim.x * kThreads) {
+        const double rel = rel_of(D, scale, force_of(D, e));
+        const double ds = pow(rel, ep);
+        const double L = log1p(ds);
+        v[0] += L;
+        if (D.inst) v[1] += idens_of(D, rel);
+        double ch[RM], sh[RM];
+        carriers<RM>(D, e / D.cols, e % D.cols, ch, sh);
+#pragma unroll
+        for (int k = 0; k < RM; ++k) {
+            v[2 + k] += L * ch[k];
+            v[2 + RM + k] += L * sh[k];
+        }
+        if (hash_on)
+            for (int t = 0; t < D.T; ++t) {
+                const int b = (int)hash_bin(e, D.B, t);
+                atomicAdd(&sbin[t * D.B + b], ds);
+                atomicAdd(&sbin[TB + t * D.B + b], 1.0);
+            }
+    }
+    const int RL = 2 + 2 * RM + 2 * TB;
+    double* rec = Bf.rec + (int64_t)blockIdx.x * RL;
+    block_record<2 + 2 * RM>(v, red, rec);
+    if (hash_on)
+        for (int i = threadIdx.x; i < 2 * TB; i += kThreads) rec[2 + 2 * RM + i] = sbin[i];
+}
+
+// Row sums of the instant-metric density: one warp per row (rank >= 2).
+__global__ void __launch_bounds__(kThreads) s64_rowsum(T64 D, Buf64 Bf) {
+    const int lane = threadIdx.x & 31;
+    const double scale = Bf.cst->scale;
+    for (int64_t r = blockIdx.x * (int64_t)kWarps + (threadIdx.x >> 5); r < D.rows; r += (int64_t)gridDim.x * kWarps) {
+        double s = 0.0;
+        for (int64_t c = lane; c < D.cols; c += 32) s += idens_of(D, rel_of(D, scale, force_of(D, r * D.cols + c)));
+        s = warp_sum(s);
+        if (lane == 0) Bf.rowsum[r] = s;
+    }
+}
+
+// Column sums of the instant-metric density: one thread per column (rank >= 2).
+__global__ void __launch_bounds__(kThreads) s64_colsum(T64 D, Buf64 Bf) {
+    const double scale = Bf.cst->scale;
+    for (int64_t c = blockIdx.x * (int64_t)kThreads + threadIdx.x; c < D.cols; c += (int64_t)gridDim.x * kThreads) {
+        double s = 0.0;
+        for (int64_t r = 0; r < D.rows; ++r) s += idens_of(D, rel_of(D, scale, force_of(D, r * D.cols + c)));
+        Bf.colsum[c] = s;
+    }
+}
+
+template <int RM>
+__global__ void __launch_bounds__(kThreads) s64_fin2(T64 D, Buf64 Bf) {
+    __shared__ double tot[2 + 2 * RM];
+    __shared__ double emean[8];
+    __shared__ double s_lax[kMaxLeadSum64];
+    const int tid = threadIdx.x;
+    const int TB = D.T * D.B;
+    const int L = 2 + 2 * RM + 2 * TB;
+    const double N = (double)D.N, eps = D.hp[Q_EPS];
+    C64& C = *Bf.cst;
+    for (int j = tid; j < 2 + 2 * RM; j += kThreads) {
+        double s = 0.0;
+        for (int b = 0; b < Bf.blocks; ++b) s += Bf.rec[(int64_t)b * L + j];
+        tot[j] = s;
+    }
+    // ---- hash energy and the per-bin log metric (cresso_v5.py:995-1056)
+    if (D.hash_on) {
+        for (int i = tid; i < TB; i += kThreads) {
+            double s = 0.0, n = 0.0;
+            for (int b = 0; b < Bf.blocks; ++b) {
+                s += Bf.rec[(int64_t)b * L + 2 + 2 * RM + i];
+                n += Bf.rec[(int64_t)b * L + 2 + 2 * RM + TB + i];
+            }
+            Bf.counts[i] = n;
+            const double cell = s / fmax(n, 1.0);
+            D.h_energy[i] = reservoir(D.h_energy[i], cell, D.hp[Q_HD], D.step);
+        }
+        __syncthreads();
+        if (tid < D.T) {
+            double s = 0.0;
+            for (int b = 0; b < D.B; ++b) s += D.h_energy[tid * D.B + b];
+            emean[tid] = fmax(s / (double)D.B, eps);
+        }
+        __syncthreads();
+        const double xp = D.hp[Q_HMC] / fmax(0.25, D.hp[Q_EP]);
+        for (int i = tid; i < TB; i += kThreads) {
+            const double hm = fmax(D.h_energy[i] / emean[i / D.B], eps);
+            Bf.lterm[i] = log(fmax(clampd(pow(hm, xp), 0.08, 12.0), eps));
+        }
+    }
+    __syncthreads();
+    // ---- metric oscillator and the log-metric coefficients (cresso_v5.py:1057-1093)
+    const double shrink = 1.0 / sqrt(fmax(1.0, 0.7 * log2((double)D.R + 1.0)));
+    if (tid == 0) {
+        C.meanL = fmax(tot[0] / N, eps);
+        C.gm = fmax(tot[1] / N, eps);
+        const double pw = fmax(D.hp[Q_IP], 0.25);
+        const double ic = D.hard ? D.hp[Q_IC] : 0.0;
+        C.kk = ic / ((double)D.ndim * pw);
+    }
+    __syncthreads();
+    if (tid < RM) {
+        const int k = tid;
+        if (k < D.R) {
+            const ModeStats& m = D.stats[k];
+            const double pc = tot[2 + k] / N / C.meanL - m.mhat_c;
+            const double ps = tot[2 + RM + k] / N / C.meanL - m.mhat_s;
+            const double mdt = D.hp[Q_MDT];
+            const double damp = fmax(0.0, 1.0 - mdt * D.hp[Q_MF]);
+            const double om2 = D.omega[k] * D.omega[k];
+            double mp = D.mp_cos[k] * damp + mdt * (pc - om2 * D.m_cos[k]);
+            double mq = clampd(D.m_cos[k] + mdt * mp, -3.0, 3.0);
+            D.mp_cos[k] = mp;
+            D.m_cos[k] = mq;
+            C.m_al[k] = mq * shrink;
+            mp = D.mp_sin[k] * damp + mdt * (ps - om2 * D.m_sin[k]);
+            mq = clampd(D.m_sin[k] + mdt * mp, -3.0, 3.0);
+            D.mp_sin[k] = mp;
+            D.m_sin[k] = mq;
+            C.m_be[k] = mq * shrink;
+            // prediction from the old oscillators (cresso_v5.py:1125-1129)
+            const double g = sigmoidd(D.hp[Q_CONFG] * D.conf[k]);
+            C.p_al[k] = D.q_cos[k] * shrink * g;
+            C.p_be[k] = D.q_sin[k] * shrink * g;
+        } else {
+            C.m_al[k] = C.m_be[k] = C.p_al[k] = C.p_be[k] = 0.0;
+        }
+    }
+    // ---- instant metric factors (cresso_v5.py:243-262): logs of the axis means over the mean
+    if (D.inst && D.ndim >= 2) {
+        __syncthreads();
+        const double gm = C.gm;
+        for (int64_t c = tid; c < D.cols; c += kThreads)
+            Bf.colsum[c] = log(fmax((Bf.colsum[c] / (double)D.rows) / gm, eps));
+        if (D.ndim == 2) {
+            for (int64_t r = tid; r < D.rows; r += kThreads)
+                Bf.rowsum[r] = log(fmax((Bf.rowsum[r] / (double)D.cols) / gm, eps));
+            return;
+        }
+        // rank >= 3: per leading axis and coordinate the marginal mean (a fixed-order sum of
+        // the row sums with that coordinate); a row's log factor sums its axes' logs
+        const int nl = (int)D.ndim - 1;
+        int lead_sum = 0;
+        for (int a = 0; a < nl; ++a) lead_sum += (int)D.dims[a];
+        for (int j = tid; j < lead_sum; j += kThreads) {
+            int a = 0, c = j;
+            while (c >= D.dims[a]) {
+                c -= (int)D.dims[a];
+                ++a;
+            }
+            int64_t inner = 1;
+            for (int b = a + 1; b < nl; ++b) inner *= D.dims[b];
+            const int64_t outer = D.rows / (D.dims[a] * inner);
+            double m = 0.0;
+            for (int64_t o = 0; o < outer; ++o)
+                for (int64_t i = 0; i < inner; ++i) m += Bf.rowsum[(o * D.dims[a] + c) * inner + i];
+            s_lax[j] = log(fmax((m / (N / (double)D.dims[a])) / gm, eps));
+        }
+        __syncthreads();
+        for (int64_t r = tid; r < D.rows; r += kThreads) {
+            double lsum = 0.0;
+            int64_t rem = r;
+            int off = lead_sum;
+            for (int a = nl - 1; a >= 0; --a) {
+                off -= (int)D.dims[a];
+                lsum += s_lax[off + (int)(rem % D.dims[a])];
+                rem /= D.dims[a];
+            }
+            Bf.rowsum[r] = lsum;
+        }
+    }
+}
+
+// ---- P3: tangent, error, projections of the port and of the tangent, port bins.
+// Record: [sum err^2, sum port c_k (RM), sum port s_k (RM), sum t c_k (RM), sum t s_k (RM), port bins (TB)]
+template <int RM>
+__global__ void __launch_bounds__(kThreads) s64_p3(T64 D, Buf64 Bf) {
+    __shared__ double red[kWarps];
+    extern __shared__ double sbin[];
+    const int TB = D.T * D.B;
+    const bool hash_on = D.hash_on != 0;
+    if (hash_on)
+        for (int i = threadIdx.x; i < TB; i += kThreads) sbin[i] = 0.0;
+    __syncthreads();
+    const C64& C = *Bf.cst;
+    const double scale = C.scale, eps = D.hp[Q_EPS], mc = D.hp[Q_MC], ls = D.hp[Q_LS], tm = D.hp[Q_TM];
+    double v[1 + 4 * RM];
+#pragma unroll
+    for (int j = 0; j < 1 + 4 * RM; ++j) v[j] = 0.0;
+    for (int64_t e = blockIdx.x * (int64_t)kThreads + threadIdx.x; e < D.N; e += (int64_t)gridDim.x * kThreads) {
+        const int64_t r = e / D.cols, c = e % D.cols;
+        const double f = force_of(D, e);
+        const double rel = rel_of(D, scale, f);
+        double ch[RM], sh[RM];
+        carriers<RM>(D, r, c, ch, sh);
+        const double lm = clampd(recon<RM>(C.m_al, C.m_be, ch, sh), -3.0, 3.0);
+        const double metric = clampd(exp(mc * lm), 0.06, 16.0);
+        const double local = D.local_on ? clampd(1.0 + ls * sqrt(fmin(rel, 100.0)), 1.0, 8.0) : 1.0;
+        double inst = 1.0;
+        if (D.inst) {
+            const double lg = D.ndim >= 2 ? Bf.rowsum[r] + Bf.colsum[c] : log(fmax(idens_of(D, rel) / C.gm, eps));
+            inst = clampd(exp(C.kk * lg), 0.08, 12.0);
+        }
+        double hm = 1.0;
+        if (hash_on) {
+            double lsum = 0.0;
+            for (int t = 0; t < D.T; ++t) lsum += Bf.lterm[t * D.B + (int)hash_bin(e, D.B, t)];
+            hm = clampd(exp(lsum / (double)D.T), 0.08, 12.0);
+        }
+        const double t = clampd(f / (scale * metric * local * inst * hm + eps), -1.0e4, 1.0e4);
+        Bf.tbuf[e] = t;
+        const double err = t - recon<RM>(C.p_al, C.p_be, ch, sh);
+        v[0] += err * err;
+        const double port = err + tm * t;
+#pragma unroll
+        for (int k = 0; k < RM; ++k) {
+            v[1 + k] += port * ch[k];
+            v[1 + RM + k] += port * sh[k];
+            v[1 + 2 * RM + k] += t * ch[k];
+            v[1 + 3 * RM + k] += t * sh[k];
+        }
+        if (hash_on)
+            for (int tb = 0; tb < D.T; ++tb) atomicAdd(&sbin[tb * D.B + (int)hash_bin(e, D.B, tb)], port);
+    }
+    const int RL = 1 + 4 * RM + TB;
+    double* rec = Bf.rec + (int64_t)blockIdx.x * RL;
+    block_record<1 + 4 * RM>(v, red, rec);
+    if (hash_on)
+        for (int i = threadIdx.x; i < TB; i += kThreads) rec[1 + 4 * RM + i] = sbin[i];
+}
+
+template <int RM>
+__global__ void __launch_bounds__(kThreads) s64_fin3(T64 D, Buf64 Bf) {
+    __shared__ double tot[1 + 4 * RM];
+    const int tid = threadIdx.x;
+    const int TB = D.T * D.B;
+    const int L = 1 + 4 * RM + TB;
+    const double N = (double)D.N, eps = D.hp[Q_EPS];
+    C64& C = *Bf.cst;
+    for (int j = tid; j < 1 + 4 * RM; j += kThreads) {
+        double s = 0.0;
+        for (int b = 0; b < Bf.blocks; ++b) s += Bf.rec[(int64_t)b * L + j];
+        tot[j] = s;
+    }
+    // ---- hash impulse reservoirs (cresso_v5.py:1140-1184)
+    if (D.hash_on) {
+        const double hd = D.hp[Q_HD], hid = D.hp[Q_HID], rg = D.hp[Q_RG];
+        for (int i = tid; i < TB; i += kThreads) {
+            double s = 0.0;
+            for (int b = 0; b < Bf.blocks; ++b) s += Bf.rec[(int64_t)b * L + 1 + 4 * RM + i];
+            const double cell = s / fmax(Bf.counts[i], 1.0);
+            const double href = D.h_refractory[i] * hd + (1.0 - hd) * fabs(cell);
+            D.h_refractory[i] = href;
+            const double hg = 1.0 / (1.0 + rg * href);
+            const double himp = D.h_impulse[i] * hid + (1.0 - hid) * (cell * hg);
+            D.h_impulse[i] = himp;
+            Bf.impv[i] = himp;
+        }
+    }
+    __syncthreads();
+    if (tid != 0) return;
+    // ---- surprise (cresso_v5.py:1132-1134)
+    const double S = reservoir(*D.surprise, sqrt(tot[0] / N + eps), D.hp[Q_SD], D.step);
+    *D.surprise = S;
+    C.S = S;
+    const int R = D.R;
+    const double shrink = 1.0 / sqrt(fmax(1.0, 0.7 * log2((double)R + 1.0)));
+    double pc[kMaxRank], ps[kMaxRank];
+    for (int k = 0; k < R; ++k) {
+        pc[k] = tot[1 + k] / N;
+        ps[k] = tot[1 + RM + k] / N;
+    }
+    // ---- confidence from the old oscillators (cresso_v5.py:1186-1202)
+    const double cd = D.hp[Q_CD];
+    for (int k = 0; k < R; ++k) {
+        const double qc = D.q_cos[k], qs = D.q_sin[k];
+        const double pe = sqrt(pc[k] * pc[k] + ps[k] * ps[k] + eps);
+        const double support = (pc[k] * qc + ps[k] * qs) / (pe * sqrt(qc * qc + qs * qs + eps) + eps);
+        D.conf[k] = clampd(D.conf[k] * cd + (1.0 - cd) * clampd(support, -1.0, 1.0), -4.0, 4.0);
+    }
+    // ---- contact oscillators, cos half then sin half (cresso_v5.py:914-943, 1204-1250)
+    const double dt = D.hp[Q_DT], rd = D.hp[Q_REFD], rg = D.hp[Q_RG];
+    const double plast = 1.0 + D.hp[Q_SG] * S / (1.0 + S);
+    const double brake = 1.0 / (1.0 + D.hp[Q_SB] * S);
+    double action = *D.action;
+    for (int half = 0; half < 2; ++half) {
+        double* q = half ? D.q_sin : D.q_cos;
+        double* p = half ? D.p_sin : D.p_cos;
+        double* ca = half ? D.ca_sin : D.ca_cos;
+        const double* port = half ? ps : pc;
+        double gp[kMaxRank];
+        double p2 = 0.0, oq2 = 0.0, pp = 0.0;
+        for (int k = 0; k < R; ++k) {
+            ca[k] = ca[k] * rd + (1.0 - rd) * fabs(port[k]);
+            const double rgate = 1.0 / (1.0 + rg * ca[k]);
+            gp[k] = port[k] * rgate * plast * brake;
+            p2 += p[k] * p[k];
+            const double oq = D.omega[k] * q[k];
+            oq2 += oq * oq;
+            pp += gp[k] * p[k];
+        }
+        const double energy = 0.5 * (p2 / R + oq2 / R);
+        action = action * 0.985 + dt * (pp / R - energy);
+        const double fr = D.hp[Q_IF] + D.hp[Q_CG] * tanh(fabs(action));
+        const double damp = fmax(1.0 - dt * fr, 0.0);
+        for (int k = 0; k < R; ++k) {
+            const double om2 = D.omega[k] * D.omega[k];
+            p[k] = p[k] * damp + dt * (gp[k] - D.hp[Q_REST] * om2 * q[k] - D.hp[Q_CUBIC] * (q[k] * q[k] * q[k]));
+            q[k] = clampd(q[k] + dt * p[k], -8.0, 8.0);
+        }
+    }
+    *D.action = action;
+    // ---- second prediction and echo coefficients (cresso_v5.py:1252-1258)
+    for (int k = 0; k < RM; ++k) {
+        if (k < R) {
+            const double g = sigmoidd(D.hp[Q_CONFG] * D.conf[k]);
+            C.p_al[k] = D.q_cos[k] * shrink * g;
+            C.p_be[k] = D.q_sin[k] * shrink * g;
+            C.e_al[k] = D.echo_on ? (tot[1 + 2 * RM + k] / N) * shrink : 0.0;
+            C.e_be[k] = D.echo_on ? (tot[1 + 3 * RM + k] / N) * shrink : 0.0;
+        } else {
+            C.p_al[k] = C.p_be[k] = C.e_al[k] = C.e_be[k] = 0.0;
+        }
+    }
+    C.clip = D.hp[Q_CLIP];
+}
+
+// The eight drive vectors of one element (cresso_v5.py:1303-1326):
+// rational, bounded, root (before its normalisation), tangent, prediction,
+// novelty, echo (raw), hash prediction (raw).
+template <int RM>
+__device__ __forceinline__ void drive_vectors(const T64& D, const Buf64& Bf, int64_t e, double (&v)[8]) {
+    const C64& C = *Bf.cst;
+    const double eps = D.hp[Q_EPS], clip = C.clip;
+    double ch[RM], sh[RM];
+    carriers<RM>(D, e / D.cols, e % D.cols, ch, sh);
+    const double t = Bf.tbuf[e];
+    const double pred = recon<RM>(C.p_al, C.p_be, ch, sh);
+    v[0] = t / (1.0 + fabs(t) / clip);
+    v[1] = tanh(t / clip) * clip;
+    v[2] = sgnd(t) * sqrt(fmin(fabs(t), clip * clip) + eps);
+    v[3] = t;
+    v[4] = pred;
+    v[5] = tanh((t - pred) / (clip * (1.0 + C.S))) * clip;
+    v[6] = D.echo_on ? recon<RM>(C.e_al, C.e_be, ch, sh) : 0.0;
+    double hp = 0.0;
+    if (D.hash_on) {
+        for (int t2 = 0; t2 < D.T; ++t2) hp += Bf.impv[t2 * D.B + (int)hash_bin(e, D.B, t2)];
+        hp = hp / (double)D.T;
+    }
+    v[7] = hp;
+}
+
+__host__ __device__ constexpr int g8(int a, int b) { return a * 8 - (a * (a - 1)) / 2 + (b - a); }
+
+template <int RM>
+__global__ void __launch_bounds__(kThreads) s64_p4(T64 D, Buf64 Bf) {
+    __shared__ double red[kWarps];
+    double g[kGram64];
+#pragma unroll
+    for (int j = 0; j < kGram64; ++j) g[j] = 0.0;
+    for (int64_t e = blockIdx.x * (int64_t)kThreads + threadIdx.x; e < D.N; e += (int64_t)gridDim.x * kThreads) {
+        double v[8];
+        drive_vectors<RM>(D, Bf, e, v);
+#pragma unroll
+        for (int a = 0; a < 8; ++a)
+#pragma unroll
+            for (int b = a; b < 8; ++b) g[g8(a, b)] += v[a] * v[b];
+    }
+    block_record<kGram64>(g, red, Bf.rec + (int64_t)blockIdx.x * kGram64);
+}
+
+// Drive coefficients from the Gram (cresso_v5.py:1303-1353).
+__global__ void s64_fin4(T64 D, Buf64 Bf) {
+    __shared__ double G[kGram64];
+    const int tid = threadIdx.x;
+    for (int j = tid; j < kGram64; j += kThreads) {
+        double s = 0.0;
+        for (int b = 0; b < Bf.blocks; ++b) s += Bf.rec[(int64_t)b * kGram64 + j];
+        G[j] = s;
+    }
+    __syncthreads();
+    if (tid != 0) return;
+    C64& C = *Bf.cst;
+    const double N = (double)D.N, eps = D.hp[Q_EPS], S = C.S;
+    auto Gm = [&](int a, int b) { return a <= b ? G[g8(a, b)] : G[g8(b, a)]; };
+    enum { RAT, BND, ROOT, TT, PR, NOV, ECHO, HASH };
+    auto rms_of = [&](const double* c8) {  // sqrt(mean((sum c_i v_i)^2) + eps)
+        double s = 0.0;
+        for (int i = 0; i < 8; ++i)
+            for (int j = 0; j < 8; ++j) s += c8[i] * c8[j] * Gm(i, j);
+        return sqrt(fmax(s, 0.0) / N + eps);
+    };
+    const double frms = sqrt(Gm(TT, TT) / N + eps);
+    const double prms = sqrt(Gm(PR, PR) / N + eps);
+    const double align = clampd((Gm(TT, PR) / N) / (frms * prms + eps), -1.0, 1.0);
+    const double align_gate = prms > sqrt(eps) ? clampd((align + 1.0) * 0.5, 0.0, 1.0) : 0.0;
+    const int ws = (int)D.hp[Q_WS];
+    const double warm = ws == 0 ? 1.0 : (1.0 - exp(-(double)D.step / (double)(ws > 1 ? ws : 1)));
+    const double mix = D.hp[Q_PM] * warm * align_gate * (1.0 / (1.0 + S));
+    const double rat_rms = sqrt(Gm(RAT, RAT) / N + eps);
+    const double k_root = rat_rms / fmax(sqrt(Gm(ROOT, ROOT) / N + eps), eps);
+    const double spike = D.hp[Q_SPIKE] / (1.0 + S);
+    const double root_mix = (D.hard ? D.hp[Q_RCM] : 0.0) / (1.0 + 0.5 * S);
+    double shaped[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    shaped[RAT] = (1.0 - root_mix) * (1.0 - spike);
+    shaped[BND] = (1.0 - root_mix) * spike;
+    shaped[ROOT] = root_mix * k_root;
+    const double shaped_rms = rms_of(shaped);
+    const double dm = D.hp[Q_DFM] / (1.0 + 0.35 * S);
+    double core[8];
+    for (int i = 0; i < 8; ++i) core[i] = (1.0 - dm) * shaped[i];
+    core[TT] += dm * (shaped_rms / fmax(frms, eps));
+    const double core_rms = rms_of(core);
+    const double resm = D.hp[Q_RFM] / (1.0 + S);
+    const double err_rms = sqrt(fmax(Gm(TT, TT) - 2.0 * Gm(TT, PR) + Gm(PR, PR), 0.0) / N + eps);
+    const double k_res = core_rms / fmax(err_rms, eps);
+    double c[8];
+    for (int i = 0; i < 8; ++i) c[i] = (1.0 - mix) * core[i];
+    c[PR] += mix;
+    c[NOV] += D.hp[Q_NM];
+    c[TT] += resm * k_res;
+    c[PR] -= resm * k_res;
+    if (D.hard && D.echo_on) {
+        const double k_e = shaped_rms / fmax(sqrt(Gm(ECHO, ECHO) / N + eps), eps);
+        c[ECHO] += D.hp[Q_EM] * k_e;
+    }
+    if (D.hard && D.hash_on) {
+        const double k_h = shaped_rms / fmax(sqrt(Gm(HASH, HASH) / N + eps), eps);
+        c[HASH] += D.hp[Q_HDM] * k_h;
+    }
+    double d2 = 0.0;
+    for (int i = 0; i < 8; ++i)
+        for (int j = 0; j < 8; ++j) d2 += c[i] * c[j] * Gm(i, j);
+    const double DE = reservoir(*D.drive_energy, fmax(d2, 0.0) / N, D.hp[Q_RD], D.step);
+    *D.drive_energy = DE;
+    C.gain = clampd(D.hp[Q_TGT] / sqrt(DE + eps), D.hp[Q_MING], D.hp[Q_MAXG]);
+    for (int i = 0; i < 8; ++i) C.c[i] = c[i];
+}
+
+template <int RM>
+__global__ void __launch_bounds__(kThreads) s64_p5(T64 D, Buf64 Bf) {
+    const C64& C = *Bf.cst;
+    const double neg_lr = -D.hp[Q_LR], gain = C.gain;
+    for (int64_t e = blockIdx.x * (int64_t)kThreads + threadIdx.x; e < D.N; e += (int64_t)gridDim.x * kThreads) {
+        double v[8];
+        drive_vectors<RM>(D, Bf, e, v);
+        double drive = 0.0;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) drive += C.c[i] * v[i];
+        D.param[e] = D.param[e] + neg_lr * (drive * gain);
+    }
+}
+
+struct Plan64 {
+    std::vector<T64> ts;
+    int64_t bytes, off_cst, off_rec, off_lterm, off_impv, off_counts, off_row, off_col, off_tbuf;
+    int blocks;
+};
+
+int plan64(const cresso_tensor_desc* descs, int64_t n, const cresso_hparams* hp, Plan64& P) {
+    CRESSO_REQUIRE(descs != nullptr && hp != nullptr && n >= 1, CRESSO_EINVAL, "spectral64: need tensors and hparams");
+    const int64_t rank = (int64_t)hp->rank, bins = (int64_t)hp->hash_bins, tables = (int64_t)hp->hash_tables;
+    CRESSO_REQUIRE(rank >= 1 && rank <= kMaxRank, CRESSO_EUNSUPPORTED,
+                   "rank must be in [1, %d] on the CUDA spectral path (got %lld)", kMaxRank, (long long)rank);
+    CRESSO_REQUIRE(bins >= 0 && tables >= 1, CRESSO_EINVAL, "hash_bins must be >= 0, hash_tables >= 1");
+    CRESSO_REQUIRE(bins * tables <= kMaxTB64, CRESSO_EUNSUPPORTED,
+                   "hash_bins * hash_tables must be <= %d for float64 parameters", kMaxTB64);
+    const int rm = rank_pad(rank);
+    int64_t max_rows = 1, max_cols = 1, max_n = 1;
+    P.ts.assign(n, T64{});
+    for (int64_t i = 0; i < n; ++i) {
+        const cresso_tensor_desc& d = descs[i];
+        CRESSO_REQUIRE(d.dtype == CRESSO_DTYPE_F64, CRESSO_EINVAL, "tensor %lld: spectral64 takes float64 tensors",
+                       (long long)i);
+        CRESSO_REQUIRE(d.ndim >= 1 && d.ndim <= CRESSO_MAX_NDIM, CRESSO_EUNSUPPORTED,
+                       "tensor %lld: spectral route supports tensors of rank 1 to %d", (long long)i, CRESSO_MAX_NDIM);
+        int64_t rows = 1, lead_sum = 0;
+        for (int64_t a = 0; a < d.ndim; ++a)
+            CRESSO_REQUIRE(d.shape[a] >= 1, CRESSO_EINVAL, "tensor %lld: empty dimension", (long long)i);
+        for (int64_t a = 0; a + 1 < d.ndim; ++a) {
+            rows *= d.shape[a];
+            lead_sum += d.shape[a];
+        }
+        const int64_t cols = d.shape[d.ndim - 1];
+        CRESSO_REQUIRE(d.row0 == 0 && d.col0 == 0 && d.rows == rows && d.cols == cols, CRESSO_EUNSUPPORTED,
+                       "tensor %lld: float64 tensors are not sharded", (long long)i);
+        CRESSO_REQUIRE(rows * cols < (1LL << 40), CRESSO_EUNSUPPORTED, "tensor %lld: too many elements", (long long)i);
+        CRESSO_REQUIRE(d.ndim <= 2 || lead_sum <= kMaxLeadSum64, CRESSO_EUNSUPPORTED,
+                       "tensor %lld: leading axes sum to %lld (at most %d)", (long long)i, (long long)lead_sum,
+                       kMaxLeadSum64);
+        CRESSO_REQUIRE(d.step >= 1, CRESSO_EINVAL, "tensor %lld: step must be >= 1", (long long)i);
+        CRESSO_REQUIRE(d.param && d.grad && d.shape_ws && d.omega && d.q_cos && d.q_sin && d.p_cos && d.p_sin &&
+                           d.metric_cos && d.metric_sin && d.metric_p_cos && d.metric_p_sin && d.calcium_cos &&
+                           d.calcium_sin && d.mode_confidence && d.force_rms && d.drive_energy && d.surprise && d.action,
+                       CRESSO_EINVAL, "tensor %lld: NULL param / grad / workspace / state pointer", (long long)i);
+        T64& T = P.ts[i];
+        T.ndim = d.ndim;
+        T.rows = rows;
+        T.cols = cols;
+        T.N = rows * cols;
+        T.step = d.step;
+        for (int64_t a = 0; a < CRESSO_MAX_NDIM; ++a) T.dims[a] = a < d.ndim ? d.shape[a] : 0;
+        T.param = (double*)d.param;
+        T.grad = (const double*)d.grad;
+        const ShapeWsHeader wh = shape_ws64_layout(d.ndim, rows, cols, rank, rm);
+        const char* ws = (const char*)d.shape_ws;
+        T.rowtab = (const double*)(ws + wh.off_rowtab);
+        T.coltab = (const double*)(ws + wh.off_coltab);
+        T.stats = (const ModeStats*)(ws + wh.off_stats);
+        T.omega = (double*)d.omega;
+        T.q_cos = (double*)d.q_cos;
+        T.q_sin = (double*)d.q_sin;
+        T.p_cos = (double*)d.p_cos;
+        T.p_sin = (double*)d.p_sin;
+        T.m_cos = (double*)d.metric_cos;
+        T.m_sin = (double*)d.metric_sin;
+        T.mp_cos = (double*)d.metric_p_cos;
+        T.mp_sin = (double*)d.metric_p_sin;
+        T.ca_cos = (double*)d.calcium_cos;
+        T.ca_sin = (double*)d.calcium_sin;
+        T.conf = (double*)d.mode_confidence;
+        T.h_energy = (double*)d.hash_energy;
+        T.h_impulse = (double*)d.hash_impulse;
+        T.h_refractory = (double*)d.hash_refractory;
+        T.force_rms = (double*)d.force_rms;
+        T.drive_energy = (double*)d.drive_energy;
+        T.surprise = (double*)d.surprise;
+        T.action = (double*)d.action;
+        T.R = (int32_t)rank;
+        T.T = (int32_t)tables;
+        T.B = (int32_t)bins;
+        // hard channel: numel >= hard_channel_min_size and not a thin 2-D matrix (cresso_v5.py:983-989)
+        const int64_t cutoff = (int64_t)hp->thin_matrix_hard_cutoff;
+        const bool thin = d.ndim == 2 && cutoff > 0 && std::min(d.shape[0], d.shape[1]) <= cutoff;
+        const bool hard = T.N >= (int64_t)hp->hard_channel_min_size && !thin;
+        T.hard = hard;
+        T.hash_on = hard && bins > 0 && d.hash_energy && d.hash_impulse && d.hash_refractory;
+        if (!T.hash_on) T.T = 1, T.B = 0;
+        T.echo_on = hard && hp->echo_mix != 0.0;
+        T.inst = hard && hp->instant_metric_coupling != 0.0 && T.N > 1;
+        T.local_on = hp->local_sharpness != 0.0;
+        memcpy(T.hp, hp, sizeof(cresso_hparams));
+        max_rows = std::max(max_rows, rows);
+        max_cols = std::max(max_cols, cols);
+        max_n = std::max(max_n, T.N);
+    }
+    int dev = 0, sms = 148;
+    CRESSO_CUDA(cudaGetDevice(&dev));
+    CRESSO_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+    P.blocks = (int)std::min<int64_t>(std::min<int64_t>(ceil_div(max_n, kThreads * 4), kMaxBlocks64), 2 * sms);
+    P.blocks = std::max(P.blocks, 1);
+    const int64_t TB = bins * tables;
+    const int64_t L = std::max<int64_t>(std::max<int64_t>(2 + 2 * rm + 2 * TB, 1 + 4 * rm + TB), kGram64);
+    int64_t off = 0;
+    P.off_cst = off;
+    off = align_up(off + (int64_t)sizeof(C64), 256);
+    P.off_rec = off;
+    off = align_up(off + 8 * L * P.blocks, 256);
+    P.off_lterm = off;
+    off = align_up(off + 8 * std::max<int64_t>(TB, 1), 256);
+    P.off_impv = off;
+    off = align_up(off + 8 * std::max<int64_t>(TB, 1), 256);
+    P.off_counts = off;
+    off = align_up(off + 8 * std::max<int64_t>(TB, 1), 256);
+    P.off_row = off;
+    off = align_up(off + 8 * max_rows, 256);
+    P.off_col = off;
+    off = align_up(off + 8 * max_cols, 256);
+    P.off_tbuf = off;
+    off = align_up(off + 8 * max_n, 256);
+    P.bytes = off;
+    return CRESSO_OK;
+}
+
+template <int RM>
+int run_tensor(const T64& T, Buf64 Bf, cudaStream_t s) {
+    const int g = Bf.blocks;
+    const size_t smem2 = T.hash_on ? (size_t)2 * T.T * T.B * 8 : 0;
+    const size_t smem3 = T.hash_on ? (size_t)T.T * T.B * 8 : 0;
+    {
+        NvtxRange r("cresso64 P1 force energy");
+        s64_p1<<<g, kThreads, 0, s>>>(T, Bf);
+        CRESSO_LAUNCHED("s64_p1");
+        s64_fin1<<<1, 32, 0, s>>>(T, Bf);
+        CRESSO_LAUNCHED("s64_fin1");
+    }
+    {
+        NvtxRange r("cresso64 P2 density / bins / projection");
+        s64_p2<RM><<<g, kThreads, smem2, s>>>(T, Bf);
+        CRESSO_LAUNCHED("s64_p2");
+        if (T.inst && T.ndim >= 2) {
+            s64_rowsum<<<(int)std::min<int64_t>(ceil_div(T.rows, kWarps), 4096), kThreads, 0, s>>>(T, Bf);
+            CRESSO_LAUNCHED("s64_rowsum");
+            s64_colsum<<<(int)std::min<int64_t>(ceil_div(T.cols, kThreads), 4096), kThreads, 0, s>>>(T, Bf);
+            CRESSO_LAUNCHED("s64_colsum");
+        }
+        s64_fin2<RM><<<1, kThreads, 0, s>>>(T, Bf);
+        CRESSO_LAUNCHED("s64_fin2");
+    }
+    {
+        NvtxRange r("cresso64 P3 tangent / port");
+        s64_p3<RM><<<g, kThreads, smem3, s>>>(T, Bf);
+        CRESSO_LAUNCHED("s64_p3");
+        s64_fin3<RM><<<1, kThreads, 0, s>>>(T, Bf);
+        CRESSO_LAUNCHED("s64_fin3");
+    }
+    {
+        NvtxRange r("cresso64 P4 drive Gram / P5 update");
+        s64_p4<RM><<<g, kThreads, 0, s>>>(T, Bf);
+        CRESSO_LAUNCHED("s64_p4");
+        s64_fin4<<<1, kThreads, 0, s>>>(T, Bf);
+        CRESSO_LAUNCHED("s64_fin4");
+        s64_p5<RM><<<g, kThreads, 0, s>>>(T, Bf);
+        CRESSO_LAUNCHED("s64_p5");
+    }
+    return CRESSO_OK;
+}
+
+}  // namespace
+
+}  // namespace cresso
+
+using namespace cresso;
+
+extern "C" {
+
+int cresso_spectral64_scratch_bytes(const cresso_tensor_desc* descs, int64_t n, const cresso_hparams* hp,
+                                    int64_t* bytes) {
+    CRESSO_REQUIRE(bytes != nullptr, CRESSO_EINVAL, "spectral64_scratch_bytes: NULL output");
+    Plan64 P;
+    int st = plan64(descs, n, hp, P);
+    if (st) return st;
+    *bytes = P.bytes;
+    return CRESSO_OK;
+}
+
+int cresso_spectral64_run(const cresso_tensor_desc* descs, int64_t n, const cresso_hparams* hp, void* scratch,
+                          int64_t scratch_bytes, cresso_stream_t stream) {
+    Plan64 P;
+    int st = plan64(descs, n, hp, P);
+    if (st) return st;
+    CRESSO_REQUIRE(scratch != nullptr, CRESSO_EINVAL, "spectral64_run: NULL scratch");
+    CRESSO_REQUIRE(scratch_bytes >= P.bytes, CRESSO_ESCRATCH, "spectral64_run: scratch of %lld bytes, need %lld",
+                   (long long)scratch_bytes, (long long)P.bytes);
+    NvtxRange range("cresso_spectral64_run %lld tensors", (long long)n);
+    char* base = (char*)scratch;
+    Buf64 Bf;
+    Bf.cst = reinterpret_cast<C64*>(base + P.off_cst);
+    Bf.rec = reinterpret_cast<double*>(base + P.off_rec);
+    Bf.lterm = reinterpret_cast<double*>(base + P.off_lterm);
+    Bf.impv = reinterpret_cast<double*>(base + P.off_impv);
+    Bf.counts = reinterpret_cast<double*>(base + P.off_counts);
+    Bf.rowsum = reinterpret_cast<double*>(base + P.off_row);
+    Bf.colsum = reinterpret_cast<double*>(base + P.off_col);
+    Bf.tbuf = reinterpret_cast<double*>(base + P.off_tbuf);
+    Bf.blocks = P.blocks;
+    cudaStream_t s = (cudaStream_t)stream;
+    const int rm = rank_pad((int64_t)hp->rank);
+    // tensors one after another on the stream: each reuses the same scratch
+    for (const T64& T : P.ts) {
+        switch (rm) {
+            case 4: st = run_tensor<4>(T, Bf, s); break;
+            case 8: st = run_tensor<8>(T, Bf, s); break;
+            default: st = run_tensor<16>(T, Bf, s); break;
+        }
+        if (st) return st;
+    }
+    return CRESSO_OK;
+}
+
+}  // extern "C"

@@ -318,6 +318,29 @@ class CRESSO5(Optimizer):
         self._shape_ws[key] = ws
         return ws
 
+    def _workspace64(self, device, shape: tuple, group: dict, freqs: Tensor) -> Tensor:
+        """Float64 carrier tables and stats of a shape (float64 parameters), kept across steps."""
+        rank, maxf = int(group["rank"]), int(group["max_frequency"])
+        key = (device, shape, rank, maxf, "f64")
+        ws = self._shape_ws.get(key)
+        if ws is not None:
+            return ws
+        L = _lib.lib()
+        dims = _lib.i64_array(shape)
+        nbytes = np.zeros(1, dtype=np.int64)
+        _lib.check(L.cresso_shape_workspace64_bytes(len(shape), dims, rank, nbytes.ctypes.data_as(_lib._pi64)),
+                   "shape_workspace64_bytes")
+        ws = torch.empty(int(nbytes[0]), dtype=torch.uint8, device=device)
+        fr = np.ascontiguousarray(np.asarray(multiscale_frequencies(rank, len(shape), maxf), dtype=np.int64))
+        stored = freqs.detach().to("cpu", torch.int64).numpy()
+        if stored.shape != fr.shape or not np.array_equal(stored, fr):
+            raise RuntimeError("state['freqs'] differs from the deterministic CRESSO5 frequency pack")
+        stream = torch.cuda.current_stream(device).cuda_stream
+        _lib.check(L.cresso_shape_workspace64_init(len(shape), dims, rank, fr.ctypes.data_as(_lib._pi64),
+                                                   _lib.ptr(ws), stream), "shape_workspace64_init")
+        self._shape_ws[key] = ws
+        return ws
+
     def _hash_index_cache(self, device, bins: int, tables: int, n: int) -> Tuple[Tensor, int]:
         key = (device, bins, tables)
         cur = self._hash_cache.get(key)
@@ -353,6 +376,7 @@ class CRESSO5(Optimizer):
             spectral: Dict[torch.device, list] = {}
             scalar: Dict[torch.device, list] = {}
             micro_items: Dict[torch.device, list] = {}
+            spectral64: Dict[torch.device, list] = {}
             route_sig = (group["min_spectral_size"], group["rank"], group.get("thin_matrix_route", "scalar"),
                          group.get("thin_matrix_max_width", 64), group.get("thin_matrix_min_aspect", 4.0))
             micro = int(group.get("micro_field_max_size", 0))
@@ -390,9 +414,14 @@ class CRESSO5(Optimizer):
                 if spectral_route is None:
                     spectral_route = self._route_cache[rkey] = self._use_spectral_route(param, group)
                 if spectral_route:
-                    if param.dtype is torch.float64:
-                        raise RuntimeError("CRESSO5 B200 path: float64 parameters are supported on the scalar and "
-                                           "micro-field routes, not on the spectral route")
+                    if param.dtype is torch.float64:  # float64 work and state: the float64 pipeline
+                        if getattr(param, "_cresso_shard", None) is not None:
+                            raise RuntimeError("float64 spectral tensors are not sharded: pass them whole")
+                        if len(state) == 0:
+                            self._init_spectral(param, group, torch.float64)
+                        state["step"] += 1
+                        spectral64.setdefault(param.device, []).append((param, grad, state))
+                        continue
                     if len(state) == 0:
                         self._init_spectral(param, group, torch.float32, self._geometry(param)[0])
                     state["step"] += 1
@@ -414,6 +443,9 @@ class CRESSO5(Optimizer):
             for device, items in micro_items.items():
                 hp = _lib.pack_hparams(group) if hp is None else hp
                 self._run_micro(hp, device, items)
+            for device, items in spectral64.items():
+                hp = _lib.pack_hparams(group) if hp is None else hp
+                self._run_spectral64(group, hp, device, items)
         return loss
 
     def _spectral_descs(self, group: dict, device, items: list) -> np.ndarray:
@@ -467,6 +499,42 @@ class CRESSO5(Optimizer):
                                              begin, end, num_sms, stream), "spectral_run")
 
         self._spectral_stages(run, scratch, layout)
+
+    def _run_spectral64(self, group: dict, hp: np.ndarray, device, items: list) -> None:
+        """Float64 spectral tensors: the float64 pipeline, whole tensors."""
+        if int(group["rank"]) > _lib.MAX_RANK:
+            raise RuntimeError(f"CRESSO5 B200 path supports rank <= {_lib.MAX_RANK} (got {group['rank']})")
+        L = _lib.lib()
+        F = _lib.DESC_INDEX
+        descs = _lib.new_descs(len(items))
+        for i, (p, g, st) in enumerate(items):
+            shape = tuple(int(d) for d in p.shape)
+            rows = 1
+            for dd in shape[:-1]:
+                rows *= dd
+            d = descs[i]
+            d[F["ndim"]] = len(shape)
+            for a, sz in enumerate(shape):
+                d[F["shape0"] + a] = sz
+            d[F["rows"]] = rows
+            d[F["cols"]] = shape[-1]
+            d[F["step"]] = int(st["step"])
+            d[F["param"]] = p.data_ptr()
+            d[F["grad"]] = g.data_ptr()
+            d[F["dtype"]] = _DTYPES[p.dtype]
+            d[F["shape_ws"]] = self._workspace64(device, shape, group, st["freqs"]).data_ptr()
+            if "hash_energy" in st:
+                for name in ("hash_energy", "hash_impulse", "hash_refractory"):
+                    d[F[name]] = st[name].data_ptr()
+            for name in ("omega",) + _SPECTRAL_RANK_STATE + ("force_rms", "drive_energy", "surprise", "action"):
+                d[F[name]] = st[name].data_ptr()
+        nb = np.zeros(1, dtype=np.int64)
+        _lib.check(L.cresso_spectral64_scratch_bytes(_lib.ptr(descs), len(items), _lib.ptr(hp),
+                                                     nb.ctypes.data_as(_lib._pi64)), "spectral64_scratch_bytes")
+        scratch = self._scratch_buffer(device, "spectral64", int(nb[0]))
+        stream = torch.cuda.current_stream(device).cuda_stream
+        _lib.check(L.cresso_spectral64_run(_lib.ptr(descs), len(items), _lib.ptr(hp), _lib.ptr(scratch),
+                                           scratch.numel(), stream), "spectral64_run")
 
     def _device_status(self) -> int:
         """Status word of the last spectral step on each device (synchronises):

@@ -88,8 +88,8 @@ typedef struct cresso_tensor_desc {
      * float32 for float32 / float16 / bfloat16 parameters, and a float16 / bfloat16
      * parameter receives the update rounded to its type first, as
      * param.add_(update.to(param.dtype)) does (cresso_v5.py:119-124, 1353, 1582).
-     * float64 parameters (scalar and micro routes only) work in float64 and their
-     * state pointers point at float64 values. */
+     * float64 parameters work in float64 and their state pointers point at
+     * float64 values (spectral route: cresso_spectral64_run). */
     int64_t dtype;
     /* micro-field route state: float32 fields of the parameter's shape */
     uint64_t micro_energy, micro_impulse, micro_refractory;
@@ -213,6 +213,20 @@ CRESSO_API int cresso_spectral_layout(const cresso_tensor_desc* descs, int64_t n
 CRESSO_API int cresso_spectral_run(const cresso_tensor_desc* descs, int64_t n, const cresso_hparams* hp, void* scratch,
                         int64_t scratch_bytes, int64_t stage_begin, int64_t stage_end, int64_t num_sms,
                         cresso_stream_t stream);
+
+/* Float64 parameters on the spectral route (cresso_v5.py:945-1353 with the
+ * float64 work and state of cresso_v5.py:119-124).  The shape workspace holds
+ * float64 axis tables and the carrier stats built from them; state pointers of
+ * the descriptors point at float64 values, `shape_ws` at this workspace.  The
+ * step runs the same five passes as cresso_spectral_run in float64, tensor by
+ * tensor; tensors are whole (not sharded), hash_bins * hash_tables <= 2048. */
+CRESSO_API int cresso_shape_workspace64_bytes(int64_t ndim, const int64_t* shape, int64_t rank, int64_t* bytes);
+CRESSO_API int cresso_shape_workspace64_init(int64_t ndim, const int64_t* shape, int64_t rank, const int64_t* freqs,
+                                             void* ws, cresso_stream_t stream);
+CRESSO_API int cresso_spectral64_scratch_bytes(const cresso_tensor_desc* descs, int64_t n, const cresso_hparams* hp,
+                                               int64_t* bytes);
+CRESSO_API int cresso_spectral64_run(const cresso_tensor_desc* descs, int64_t n, const cresso_hparams* hp,
+                                     void* scratch, int64_t scratch_bytes, cresso_stream_t stream);
 
 /* ------------------------------------------------------ scalar route ---- */
 

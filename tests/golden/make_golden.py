@@ -117,6 +117,15 @@ EXTRA_CASES = {
     "micro64_30x20": ((30, 20), dict(micro_field_max_size=1000), 3, 65, 0.02, 1e-3, "float64"),
     "micro64_2x3x4": ((2, 3, 4), dict(micro_field_max_size=100, maximize=True, weight_decay=0.02), 3, 66, 0.02, 1e-3,
                       "float64"),
+    # float64 parameters on the spectral route
+    "spec64_96x80": ((96, 80), dict(), 3, 71, 0.02, 1e-3, "float64"),
+    "spec64_64x64_wd_local_max": ((64, 64), dict(rank=8, hash_bins=64, hash_tables=2, weight_decay=0.01,
+                                                 local_sharpness=0.3, maximize=True), 3, 72, 0.02, 1e-3, "float64"),
+    "spec64_2048": ((2048,), dict(rank=8, hash_bins=64, hash_tables=2), 3, 73, 0.02, 1e-3, "float64"),
+    "spec64_8x6x40": ((8, 6, 40), dict(rank=4, hash_bins=32, hash_tables=1), 3, 74, 0.02, 1e-3, "float64"),
+    "spec64_128x40_r16": ((128, 40), dict(rank=16, hash_bins=37, hash_tables=3, instant_metric_power=0.7,
+                                          warmup_steps=0), 3, 75, 0.02, 1e-3, "float64"),
+    "spec64_thin_8x512": ((8, 512), dict(rank=8, thin_matrix_route="spectral"), 3, 76, 0.02, 1e-3, "float64"),
 }
 
 

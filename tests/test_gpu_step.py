@@ -138,6 +138,9 @@ def test_extra_golden_parity(golden_extra, name):
             if not torch.is_tensor(v):
                 assert v == int(st_ref[k]), (name, k)
                 continue
+            if v.dtype == torch.int64:
+                assert np.array_equal(v.cpu().numpy(), st_ref[k]), (name, k)
+                continue
             assert v.dtype == torch.float64, (name, k)
             assert rel_rms(v.cpu().numpy(), st_ref[k]) <= 1e-9, (name, k, rel_rms(v.cpu().numpy(), st_ref[k]))
         return
@@ -394,19 +397,35 @@ def test_mixed_routes_in_one_group(micro):
                 assert rel_rms(opt.state[p][k].cpu(), v) <= 5e-3, (s, k)
 
 
-def test_float64_spectral_route_is_rejected():
-    """float64 parameters run on the scalar and micro-field routes; a float64
-    tensor that routes to the spectral path is refused with a clear error."""
-    p = torch.nn.Parameter(torch.zeros((64, 64), dtype=torch.float64, device="cuda"))
-    p.grad = torch.ones_like(p)
-    opt = cresso_b200.CRESSO5([p])
-    with pytest.raises(RuntimeError, match="float64"):
+def test_float64_spectral_route_in_a_mixed_group():
+    """float64 tensors of every route in one group next to float32 ones: the
+    float64 spectral tensors run the float64 pipeline (float64 state), and the
+    whole group matches the oracle run in float64 / float32."""
+    g = torch.Generator().manual_seed(8)
+    specs = [((96, 64), torch.float64), ((3000,), torch.float64), ((9, 7), torch.float64), ((96, 64), torch.float32),
+             ((4, 6, 50), torch.float64)]
+    inits = [torch.randn(s, generator=g) * 0.02 for s, _ in specs]
+    grads = [[torch.randn(s, generator=g) * 1e-3 for s, _ in specs] for _ in range(3)]
+    kw = dict(rank=8, hash_bins=64, hash_tables=2)
+    ps = [torch.nn.Parameter(x.clone().to("cuda", dt)) for x, (_, dt) in zip(inits, specs)]
+    rs = [torch.nn.Parameter(x.clone().to(dt)) for x, (_, dt) in zip(inits, specs)]
+    opt = cresso_b200.CRESSO5(ps, **kw)
+    ref = O.OracleCRESSO5(rs, **kw)
+    for gs in grads:
+        for p, r, gg in zip(ps, rs, gs):
+            p.grad = gg.to("cuda", p.dtype)
+            r.grad = gg.to(r.dtype)
         opt.step()
-    q = torch.nn.Parameter(torch.zeros((64, 64), dtype=torch.float64, device="cuda"))
-    q.grad = torch.full_like(q, 1e-3)
-    opt = cresso_b200.CRESSO5([q], micro_field_max_size=4096)
-    opt.step()
-    assert opt.state[q]["micro_energy"].dtype == torch.float64 and float(q.detach().abs().max()) > 0
+        ref.step()
+    torch.cuda.synchronize()
+    for (shape, dt), p, r in zip(specs, ps, rs):
+        tol = 1e-12 if dt == torch.float64 else 1e-5
+        assert rel_rms(p.detach().cpu().double(), r.detach().double()) <= tol, shape
+        for k, v in ref.state[r].items():
+            if torch.is_tensor(v) and v.dtype.is_floating_point:
+                assert opt.state[p][k].dtype == v.dtype, (shape, k)
+                stol = 1e-9 if dt == torch.float64 else 5e-3
+                assert rel_rms(opt.state[p][k].cpu().double(), v.double()) <= stol, (shape, k)
 
 
 def test_bounded_wait_runs_out_and_reports_status():
