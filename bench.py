@@ -253,7 +253,7 @@ def b200_arm(args, world, rank, local):
     torch.cuda.set_device(device)
     shapes, kw, istd = workload_shapes(args.workload)
     params, grads_dev = [], []
-    pdt = {"f32": torch.float32, "bf16": torch.bfloat16, "f16": torch.float16}[args.dtype]
+    pdt = {"f32": torch.float32, "bf16": torch.bfloat16, "f16": torch.float16, "f64": torch.float64}[args.dtype]
     bpe = 3 * torch.empty((), dtype=pdt).element_size()  # grad read + param read + param write
     gen = torch.Generator(device=device)
     gen.manual_seed(1234 + (0 if zero else rank))
@@ -318,10 +318,14 @@ def b200_arm(args, world, rank, local):
 
     # ---- per-pass kernel times (CUDA events on the launching stream, same steps)
     pass_ms = time_passes(opt, args, world, device, stream)
-    dom = max(pass_ms, key=pass_ms.get)
-    dom_ms = max_over_ranks(pass_ms[dom], world, device)
+    if pass_ms:
+        dom = max(pass_ms, key=pass_ms.get)
+        dom_ms = max_over_ranks(pass_ms[dom], world, device)
+        dom_bytes = PASS_BYTES[dom]
+    else:  # float64: its own pipeline, timed as a whole step
+        dom, dom_ms, dom_bytes = "step", ms, bpe
     peaks, peak_kind = measured_peaks()
-    achieved = PASS_BYTES[dom] * n_local / (dom_ms * 1e-3) / 1e9
+    achieved = dom_bytes * n_local / (dom_ms * 1e-3) / 1e9
     traffic = None
     try:
         tr = json.loads((ROOT / "profiles" / "traffic_per_element.json").read_text())
@@ -348,7 +352,7 @@ def b200_arm(args, world, rank, local):
         line = {
             "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
-            "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "vs_baseline": None, "dtype": "f64" if args.dtype == "f64" else "f32", "data": "synthetic",
             "config": {"workload": f"{args.workload}: " + (f"7B-shaped {args.dtype} set, 290 tensors, 6,738,411,520 elements"
                                                             if args.workload == "c5" else str(shapes[0])),
                        "rank": kw["rank"], "hash_bins": kw["hash_bins"], "hash_tables": kw["hash_tables"],
@@ -364,7 +368,7 @@ def b200_arm(args, world, rank, local):
                          "unit": "GB/s", "frac": achieved / peaks["hbm_gbs"], "traffic": traffic,
                          "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
                          else "fallback 6.65 TB/s",
-                         "algorithmic_bytes_per_element": PASS_BYTES[dom],
+                         "algorithmic_bytes_per_element": dom_bytes,
                          "step_frac": value / world / peaks["hbm_gbs"]},
             "clocks": clk.summary(),
             "gpu_launches": launches,
@@ -497,8 +501,8 @@ def main():
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     ap.add_argument("--workload", default="c5")
     ap.add_argument("--skip-e2e", action="store_true")
-    ap.add_argument("--dtype", choices=["f32", "bf16", "f16"], default="f32",
-                    help="parameter / gradient type (work and state are float32 for all)")
+    ap.add_argument("--dtype", choices=["f32", "bf16", "f16", "f64"], default="f32",
+                    help="parameter / gradient type (work and state: float64 for f64, else float32)")
     ap.add_argument("--skip-cpu", action="store_true")
     ap.add_argument("--sharding", choices=["row", "zero"], default="row",
                     help="N > 1: row sharding (default) or ZeRO-1 whole-tensor partition")

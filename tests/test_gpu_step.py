@@ -98,7 +98,7 @@ def test_extra_golden_parity(golden_extra, name):
     bfloat16 parameters (spectral and scalar routes), spectral tensors of
     rank 3 to 5 (leading axes flattened into rows, carriers and the instant
     metric composed over every axis), the micro-field route and float64
-    parameters (scalar and micro-field routes, float64 work and state).
+    parameters (every route, float64 work and state).
 
     float32 parameters: the criterion of the float32 golden cases.  16-bit
     parameters: every element within one unit in the last place of the
@@ -230,6 +230,43 @@ def test_benchmark_config_ten_steps(cfg):
                       upd_tol=5e-4)
         if i >= 3:
             break
+
+
+def test_c5_shapes_full_size_parity():
+    """The four distinct tensor shapes of the 7B-shaped benchmark set (c5) at
+    full size in one group -- (32000, 4096), (11008, 4096), (4096, 11008),
+    (4096,) -- two steps against the float32 and float64 oracle run by torch
+    on the same GPU, with the criterion of the golden cases."""
+    shapes = [(32000, 4096), (11008, 4096), (4096, 11008), (4096,)]
+    kw = dict(lr=2e-3, rank=8, max_frequency=5, hash_bins=64, hash_tables=2)
+    dev = torch.device("cuda")
+    g = torch.Generator(device=dev).manual_seed(5)
+    inits = [torch.randn(s, generator=g, device=dev) * 0.02 for s in shapes]
+    grads = [[torch.randn(s, generator=g, device=dev) * 1e-3 for s in shapes] for _ in range(2)]
+    ps = [torch.nn.Parameter(x.clone()) for x in inits]
+    opt = cresso_b200.CRESSO5(ps, **kw)
+    for gs in grads:
+        for p, gg in zip(ps, gs):
+            p.grad = gg.clone()
+        opt.step()
+    torch.cuda.synchronize()
+    assert opt._device_status() == 0
+    for i, (p, x0) in enumerate(zip(ps, inits)):
+        r = torch.nn.Parameter(x0.clone())
+        r64 = torch.nn.Parameter(x0.double())
+        ref32, ref64 = O.OracleCRESSO5([r], **kw), O.OracleCRESSO5([r64], **kw)
+        for gs in grads:
+            r.grad = gs[i].clone()
+            r64.grad = gs[i].double()
+            ref32.step()
+            ref64.step()
+        st = {k: (v.cpu() if torch.is_tensor(v) else v) for k, v in opt.state[p].items()}
+        st32 = {k: (v.cpu() if torch.is_tensor(v) else v) for k, v in ref32.state[r].items()}
+        st64 = {k: (v.cpu() if torch.is_tensor(v) else v) for k, v in ref64.state[r64].items()}
+        check_against(f"c5{shapes[i]}", x0.cpu(), p.detach().cpu(), st, r.detach().cpu(), st32, r64.detach().cpu(),
+                      st64, upd_tol=5e-4)
+        del r, r64, ref32, ref64
+        torch.cuda.empty_cache()
 
 
 # Hyper-parameter variants on a shape that takes the tensor-core (tcgen05) form
