@@ -46,7 +46,7 @@ struct ModeParam {
     AxisParam col;
 };
 struct ModePack {
-    ModeParam m[kMaxRank];
+    ModeParam m[kMaxRankPlain];
     int64_t ldim[CRESSO_MAX_NDIM];  // leading axis lengths
 };
 
@@ -247,7 +247,7 @@ __global__ void stats_gram_kernel(ModePack modes, int rank, int rm, double n, co
     const double* A2 = tmp + P;
     const double* B1 = tmp + P + P * P;
     const double* B2 = B1 + P;
-    __shared__ double mu[2 * kMaxRank], inv[2 * kMaxRank], ex2[2 * kMaxRank];
+    __shared__ double mu[2 * kMaxRankPlain], inv[2 * kMaxRankPlain], ex2[2 * kMaxRankPlain];
     for (int X = threadIdx.x; X < P; X += blockDim.x) {
         const int k = X >> 1;
         Term t[2];
@@ -701,8 +701,8 @@ int cresso_shape_workspace64_bytes(int64_t ndim, const int64_t* shape, int64_t r
     int st = checked_shape(ndim, shape, &grows, &gcols);
     if (st) return st;
     CRESSO_REQUIRE(bytes != nullptr, CRESSO_EINVAL, "shape_workspace64_bytes: NULL output");
-    CRESSO_REQUIRE(rank >= 1 && rank <= kMaxRank, CRESSO_EUNSUPPORTED,
-                   "rank must be in [1, %d] on the CUDA path (got %lld)", kMaxRank, (long long)rank);
+    CRESSO_REQUIRE(rank >= 1 && rank <= kMaxRankPlain, CRESSO_EUNSUPPORTED,
+                   "rank must be in [1, %d] on the CUDA path (got %lld)", kMaxRankPlain, (long long)rank);
     *bytes = shape_ws64_layout(ndim, grows, gcols, rank, rank_pad(rank)).bytes;
     return CRESSO_OK;
 }
@@ -712,8 +712,8 @@ int cresso_shape_workspace64_init(int64_t ndim, const int64_t* shape, int64_t ra
     int64_t grows, gcols;
     int st = checked_shape(ndim, shape, &grows, &gcols);
     if (st) return st;
-    CRESSO_REQUIRE(rank >= 1 && rank <= kMaxRank, CRESSO_EUNSUPPORTED,
-                   "rank must be in [1, %d] on the CUDA path (got %lld)", kMaxRank, (long long)rank);
+    CRESSO_REQUIRE(rank >= 1 && rank <= kMaxRankPlain, CRESSO_EUNSUPPORTED,
+                   "rank must be in [1, %d] on the CUDA path (got %lld)", kMaxRankPlain, (long long)rank);
     CRESSO_REQUIRE(freqs != nullptr && ws != nullptr, CRESSO_EINVAL, "shape_workspace64_init: NULL pointer");
     const int rm = rank_pad(rank);
     ShapeWsHeader h = shape_ws64_layout(ndim, grows, gcols, rank, rm);

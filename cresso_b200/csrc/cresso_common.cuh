@@ -14,7 +14,8 @@ namespace cresso {
 
 constexpr int kThreads = 256;  // every kernel of the library runs 256-thread blocks
 constexpr int kWarps = kThreads / 32;
-constexpr int kMaxRank = 16;
+constexpr int kMaxRank = 16;       // the fused float32 spectral path
+constexpr int kMaxRankPlain = 32;  // the float64-arithmetic spectral path and its shape workspace
 constexpr int kMaxTB = 8192;   // hash_tables * hash_bins held in shared memory
 constexpr int kMaxBins = 4096; // same bound as the reference CUDA hash path (cresso_v5.py:1002)
 
@@ -118,7 +119,7 @@ __host__ inline ShapeWsHeader shape_ws64_layout(int64_t ndim, int64_t grows, int
     h.off_coltab = off;
     off = align_up(off + 2 * rm * gcols * 8, 256);
     h.off_stats = off;
-    off = align_up(off + 64 * kMaxRank, 256);  // ModeStats: 8 doubles per mode
+    off = align_up(off + 64 * kMaxRankPlain, 256);  // ModeStats: 8 doubles per mode
     h.off_gram = off;
     off = align_up(off + (2 * rm) * (2 * rm) * 8, 256);
     h.off_tmp = off;
@@ -128,7 +129,9 @@ __host__ inline ShapeWsHeader shape_ws64_layout(int64_t ndim, int64_t grows, int
     return h;
 }
 
-__host__ __device__ inline int rank_pad(int64_t rank) { return rank <= 4 ? 4 : (rank <= 8 ? 8 : 16); }
+__host__ __device__ inline int rank_pad(int64_t rank) {
+    return rank <= 4 ? 4 : (rank <= 8 ? 8 : (rank <= 16 ? 16 : 32));
+}
 
 // ---------------------------------------------------------------------------
 // Warp / block reductions (fixed order => run-to-run deterministic)

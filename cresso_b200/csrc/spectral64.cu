@@ -24,6 +24,8 @@
 #include <math.h>
 #include <stdint.h>
 
+#include <string.h>
+
 #include <algorithm>
 #include <vector>
 
@@ -48,26 +50,29 @@ enum {
 };
 static_assert(sizeof(cresso_hparams) == Q_COUNT * sizeof(double), "cresso_hparams field order");
 
+// P: storage type of the parameter, gradient and state (double for float64
+// tensors, float for float32 tensors of rank > 16); the arithmetic is float64.
+template <typename P>
 struct T64 {
     int64_t ndim, N, rows, cols, step;
     int64_t dims[CRESSO_MAX_NDIM];
-    double* param;
-    const double* grad;
+    P* param;
+    const P* grad;
     const double* rowtab;  // [rows][rm][2]
     const double* coltab;  // [2 rm][cols]
     const ModeStats* stats;
-    double *omega, *q_cos, *q_sin, *p_cos, *p_sin, *m_cos, *m_sin, *mp_cos, *mp_sin, *ca_cos, *ca_sin, *conf;
-    double *h_energy, *h_impulse, *h_refractory, *force_rms, *drive_energy, *surprise, *action;
-    int32_t R, T, B, hard, hash_on, echo_on, inst, local_on;
+    P *omega, *q_cos, *q_sin, *p_cos, *p_sin, *m_cos, *m_sin, *mp_cos, *mp_sin, *ca_cos, *ca_sin, *conf;
+    P *h_energy, *h_impulse, *h_refractory, *force_rms, *drive_energy, *surprise, *action;
+    int32_t R, T, B, hard, hash_on, echo_on, inst, local_on, f32, pad;
     double hp[64];
 };
 
 // Per-tensor values passed from the finalize kernels to the pass kernels.
 struct C64 {
     double scale, gm, kk, meanL, S, clip;
-    double m_al[kMaxRank], m_be[kMaxRank];  // log-metric reconstruction (shrink * metric oscillator)
-    double p_al[kMaxRank], p_be[kMaxRank];  // prediction (shrink * gate * q), P3: old q, P4/P5: new q
-    double e_al[kMaxRank], e_be[kMaxRank];  // echo reconstruction (shrink * tangent projection)
+    double m_al[kMaxRankPlain], m_be[kMaxRankPlain];  // log-metric reconstruction (shrink * metric oscillator)
+    double p_al[kMaxRankPlain], p_be[kMaxRankPlain];  // prediction (shrink * gate * q), P3: old q, P4/P5: new q
+    double e_al[kMaxRankPlain], e_be[kMaxRankPlain];  // echo reconstruction (shrink * tangent projection)
     double c[8], gain;                      // drive = sum c_i v_i
 };
 
@@ -88,8 +93,8 @@ __device__ __forceinline__ double sigmoidd(double x) { return 1.0 / (1.0 + exp(-
 __device__ __forceinline__ double sgnd(double x) { return x > 0.0 ? 1.0 : (x < 0.0 ? -1.0 : 0.0); }
 
 // Normalised carriers (cos, sin) of modes 0..RM-1 at row r, column c.
-template <int RM>
-__device__ __forceinline__ void carriers(const T64& D, int64_t r, int64_t c, double (&ch)[RM], double (&sh)[RM]) {
+template <int RM, typename P>
+__device__ __forceinline__ void carriers(const T64<P>& D, int64_t r, int64_t c, double (&ch)[RM], double (&sh)[RM]) {
 #pragma unroll
     for (int k = 0; k < RM; ++k) {
         const double a1 = D.rowtab[(r * RM + k) * 2], a2 = D.rowtab[(r * RM + k) * 2 + 1];
@@ -120,17 +125,20 @@ __device__ __forceinline__ double recon(const double* al, const double* be, cons
     return out;
 }
 
-__device__ __forceinline__ double force_of(const T64& D, int64_t e) {
+template <typename P>
+__device__ __forceinline__ double force_of(const T64<P>& D, int64_t e) {
     double f = (D.hp[Q_MAX] != 0.0 ? -1.0 : 1.0) * D.grad[e];
     if (D.hp[Q_WD] != 0.0) f = f + D.hp[Q_WD] * D.param[e];
     return f;
 }
 
-__device__ __forceinline__ double rel_of(const T64& D, double scale, double f) {
+template <typename P>
+__device__ __forceinline__ double rel_of(const T64<P>& D, double scale, double f) {
     return fmin(fabs(f) / scale + D.hp[Q_EPS], 1.0e4);
 }
 
-__device__ __forceinline__ double idens_of(const T64& D, double rel) {
+template <typename P>
+__device__ __forceinline__ double idens_of(const T64<P>& D, double rel) {
     const double pw = fmax(D.hp[Q_IP], 0.25);
     return fmin(pow(fmax(rel, D.hp[Q_EPS]), pw), 1.0e6);
 }
@@ -153,7 +161,8 @@ __device__ __forceinline__ void block_record(double (&v)[L], double* red, double
 }
 
 // ---- P1: force energy
-__global__ void __launch_bounds__(kThreads) s64_p1(T64 D, Buf64 Bf) {
+template <typename P>
+__global__ void __launch_bounds__(kThreads) s64_p1(T64<P> D, Buf64 Bf) {
     __shared__ double red[kWarps];
     double v[1] = {0.0};
     for (int64_t e = blockIdx.x * (int64_t)kThreads + threadIdx.x; e < D.N; e += (int64_t)gridDim.x * kThreads) {
@@ -163,21 +172,22 @@ __global__ void __launch_bounds__(kThreads) s64_p1(T64 D, Buf64 Bf) {
     block_record<1>(v, red, Bf.rec + (int64_t)blockIdx.x * 1);
 }
 
-__global__ void s64_fin1(T64 D, Buf64 Bf) {
+template <typename P>
+__global__ void s64_fin1(T64<P> D, Buf64 Bf) {
     if (threadIdx.x != 0) return;
     double s = 0.0;
     for (int b = 0; b < Bf.blocks; ++b) s += Bf.rec[b];
     const double eps = D.hp[Q_EPS];
     const double frn = sqrt(s / (double)D.N + eps);
-    const double fr = reservoir(*D.force_rms, frn, D.hp[Q_RD], D.step);
+    const double fr = reservoir((double)*D.force_rms, frn, D.hp[Q_RD], D.step);
     *D.force_rms = fr;
     Bf.cst->scale = fmax(fr, eps);
 }
 
 // ---- P2: density, bins, projections.  Record: [sum L, sum dens, sum L c_k (RM), sum L s_k (RM),
 // bin sums (TB), bin counts (TB)]
-template <int RM>
-__global__ void __launch_bounds__(kThreads) s64_p2(T64 D, Buf64 Bf) {
+template <int RM, typename P>
+__global__ void __launch_bounds__(kThreads) s64_p2(T64<P> D, Buf64 Bf) {
     __shared__ double red[kWarps];
     extern __shared__ double sbin[];  // [TB] sums, then [TB] counts
     const int TB = D.T * D.B;
@@ -217,7 +227,8 @@ __global__ void __launch_bounds__(kThreads) s64_p2(T64 D, Buf64 Bf) {
 }
 
 // Row sums of the instant-metric density: one warp per row (rank >= 2).
-__global__ void __launch_bounds__(kThreads) s64_rowsum(T64 D, Buf64 Bf) {
+template <typename P>
+__global__ void __launch_bounds__(kThreads) s64_rowsum(T64<P> D, Buf64 Bf) {
     const int lane = threadIdx.x & 31;
     const double scale = Bf.cst->scale;
     for (int64_t r = blockIdx.x * (int64_t)kWarps + (threadIdx.x >> 5); r < D.rows; r += (int64_t)gridDim.x * kWarps) {
@@ -229,7 +240,8 @@ __global__ void __launch_bounds__(kThreads) s64_rowsum(T64 D, Buf64 Bf) {
 }
 
 // Column sums of the instant-metric density: one thread per column (rank >= 2).
-__global__ void __launch_bounds__(kThreads) s64_colsum(T64 D, Buf64 Bf) {
+template <typename P>
+__global__ void __launch_bounds__(kThreads) s64_colsum(T64<P> D, Buf64 Bf) {
     const double scale = Bf.cst->scale;
     for (int64_t c = blockIdx.x * (int64_t)kThreads + threadIdx.x; c < D.cols; c += (int64_t)gridDim.x * kThreads) {
         double s = 0.0;
@@ -238,8 +250,8 @@ __global__ void __launch_bounds__(kThreads) s64_colsum(T64 D, Buf64 Bf) {
     }
 }
 
-template <int RM>
-__global__ void __launch_bounds__(kThreads) s64_fin2(T64 D, Buf64 Bf) {
+template <int RM, typename P>
+__global__ void __launch_bounds__(kThreads) s64_fin2(T64<P> D, Buf64 Bf) {
     __shared__ double tot[2 + 2 * RM];
     __shared__ double emean[8];
     __shared__ double s_lax[kMaxLeadSum64];
@@ -263,7 +275,7 @@ __global__ void __launch_bounds__(kThreads) s64_fin2(T64 D, Buf64 Bf) {
             }
             Bf.counts[i] = n;
             const double cell = s / fmax(n, 1.0);
-            D.h_energy[i] = reservoir(D.h_energy[i], cell, D.hp[Q_HD], D.step);
+            D.h_energy[i] = reservoir((double)D.h_energy[i], cell, D.hp[Q_HD], D.step);
         }
         __syncthreads();
         if (tid < D.T) {
@@ -363,8 +375,8 @@ __global__ void __launch_bounds__(kThreads) s64_fin2(T64 D, Buf64 Bf) {
 
 // ---- P3: tangent, error, projections of the port and of the tangent, port bins.
 // Record: [sum err^2, sum port c_k (RM), sum port s_k (RM), sum t c_k (RM), sum t s_k (RM), port bins (TB)]
-template <int RM>
-__global__ void __launch_bounds__(kThreads) s64_p3(T64 D, Buf64 Bf) {
+template <int RM, typename P>
+__global__ void __launch_bounds__(kThreads) s64_p3(T64<P> D, Buf64 Bf) {
     __shared__ double red[kWarps];
     extern __shared__ double sbin[];
     const int TB = D.T * D.B;
@@ -419,8 +431,8 @@ __global__ void __launch_bounds__(kThreads) s64_p3(T64 D, Buf64 Bf) {
         for (int i = threadIdx.x; i < TB; i += kThreads) rec[1 + 4 * RM + i] = sbin[i];
 }
 
-template <int RM>
-__global__ void __launch_bounds__(kThreads) s64_fin3(T64 D, Buf64 Bf) {
+template <int RM, typename P>
+__global__ void __launch_bounds__(kThreads) s64_fin3(T64<P> D, Buf64 Bf) {
     __shared__ double tot[1 + 4 * RM];
     const int tid = threadIdx.x;
     const int TB = D.T * D.B;
@@ -450,12 +462,12 @@ __global__ void __launch_bounds__(kThreads) s64_fin3(T64 D, Buf64 Bf) {
     __syncthreads();
     if (tid != 0) return;
     // ---- surprise (cresso_v5.py:1132-1134)
-    const double S = reservoir(*D.surprise, sqrt(tot[0] / N + eps), D.hp[Q_SD], D.step);
+    const double S = reservoir((double)*D.surprise, sqrt(tot[0] / N + eps), D.hp[Q_SD], D.step);
     *D.surprise = S;
     C.S = S;
     const int R = D.R;
     const double shrink = 1.0 / sqrt(fmax(1.0, 0.7 * log2((double)R + 1.0)));
-    double pc[kMaxRank], ps[kMaxRank];
+    double pc[kMaxRankPlain], ps[kMaxRankPlain];
     for (int k = 0; k < R; ++k) {
         pc[k] = tot[1 + k] / N;
         ps[k] = tot[1 + RM + k] / N;
@@ -474,11 +486,11 @@ __global__ void __launch_bounds__(kThreads) s64_fin3(T64 D, Buf64 Bf) {
     const double brake = 1.0 / (1.0 + D.hp[Q_SB] * S);
     double action = *D.action;
     for (int half = 0; half < 2; ++half) {
-        double* q = half ? D.q_sin : D.q_cos;
-        double* p = half ? D.p_sin : D.p_cos;
-        double* ca = half ? D.ca_sin : D.ca_cos;
+        P* q = half ? D.q_sin : D.q_cos;
+        P* p = half ? D.p_sin : D.p_cos;
+        P* ca = half ? D.ca_sin : D.ca_cos;
         const double* port = half ? ps : pc;
-        double gp[kMaxRank];
+        double gp[kMaxRankPlain];
         double p2 = 0.0, oq2 = 0.0, pp = 0.0;
         for (int k = 0; k < R; ++k) {
             ca[k] = ca[k] * rd + (1.0 - rd) * fabs(port[k]);
@@ -518,8 +530,8 @@ __global__ void __launch_bounds__(kThreads) s64_fin3(T64 D, Buf64 Bf) {
 // The eight drive vectors of one element (cresso_v5.py:1303-1326):
 // rational, bounded, root (before its normalisation), tangent, prediction,
 // novelty, echo (raw), hash prediction (raw).
-template <int RM>
-__device__ __forceinline__ void drive_vectors(const T64& D, const Buf64& Bf, int64_t e, double (&v)[8]) {
+template <int RM, typename P>
+__device__ __forceinline__ void drive_vectors(const T64<P>& D, const Buf64& Bf, int64_t e, double (&v)[8]) {
     const C64& C = *Bf.cst;
     const double eps = D.hp[Q_EPS], clip = C.clip;
     double ch[RM], sh[RM];
@@ -543,8 +555,8 @@ __device__ __forceinline__ void drive_vectors(const T64& D, const Buf64& Bf, int
 
 __host__ __device__ constexpr int g8(int a, int b) { return a * 8 - (a * (a - 1)) / 2 + (b - a); }
 
-template <int RM>
-__global__ void __launch_bounds__(kThreads) s64_p4(T64 D, Buf64 Bf) {
+template <int RM, typename P>
+__global__ void __launch_bounds__(kThreads) s64_p4(T64<P> D, Buf64 Bf) {
     __shared__ double red[kWarps];
     double g[kGram64];
 #pragma unroll
@@ -561,7 +573,8 @@ __global__ void __launch_bounds__(kThreads) s64_p4(T64 D, Buf64 Bf) {
 }
 
 // Drive coefficients from the Gram (cresso_v5.py:1303-1353).
-__global__ void s64_fin4(T64 D, Buf64 Bf) {
+template <typename P>
+__global__ void s64_fin4(T64<P> D, Buf64 Bf) {
     __shared__ double G[kGram64];
     const int tid = threadIdx.x;
     for (int j = tid; j < kGram64; j += kThreads) {
@@ -622,14 +635,14 @@ __global__ void s64_fin4(T64 D, Buf64 Bf) {
     double d2 = 0.0;
     for (int i = 0; i < 8; ++i)
         for (int j = 0; j < 8; ++j) d2 += c[i] * c[j] * Gm(i, j);
-    const double DE = reservoir(*D.drive_energy, fmax(d2, 0.0) / N, D.hp[Q_RD], D.step);
+    const double DE = reservoir((double)*D.drive_energy, fmax(d2, 0.0) / N, D.hp[Q_RD], D.step);
     *D.drive_energy = DE;
     C.gain = clampd(D.hp[Q_TGT] / sqrt(DE + eps), D.hp[Q_MING], D.hp[Q_MAXG]);
     for (int i = 0; i < 8; ++i) C.c[i] = c[i];
 }
 
-template <int RM>
-__global__ void __launch_bounds__(kThreads) s64_p5(T64 D, Buf64 Bf) {
+template <int RM, typename P>
+__global__ void __launch_bounds__(kThreads) s64_p5(T64<P> D, Buf64 Bf) {
     const C64& C = *Bf.cst;
     const double neg_lr = -D.hp[Q_LR], gain = C.gain;
     for (int64_t e = blockIdx.x * (int64_t)kThreads + threadIdx.x; e < D.N; e += (int64_t)gridDim.x * kThreads) {
@@ -642,8 +655,17 @@ __global__ void __launch_bounds__(kThreads) s64_p5(T64 D, Buf64 Bf) {
     }
 }
 
+// Both storage types have the same layout (every pointer the same size), so the
+// plan keeps T64<double> and a float32 tensor is launched as its T64<float> copy.
+static_assert(sizeof(T64<float>) == sizeof(T64<double>), "T64 layout");
+T64<float> as_f32(const T64<double>& d) {
+    T64<float> f;
+    memcpy(&f, &d, sizeof(f));
+    return f;
+}
+
 struct Plan64 {
-    std::vector<T64> ts;
+    std::vector<T64<double>> ts;
     int64_t bytes, off_cst, off_rec, off_lterm, off_impv, off_counts, off_row, off_col, off_tbuf;
     int blocks;
 };
@@ -651,18 +673,19 @@ struct Plan64 {
 int plan64(const cresso_tensor_desc* descs, int64_t n, const cresso_hparams* hp, Plan64& P) {
     CRESSO_REQUIRE(descs != nullptr && hp != nullptr && n >= 1, CRESSO_EINVAL, "spectral64: need tensors and hparams");
     const int64_t rank = (int64_t)hp->rank, bins = (int64_t)hp->hash_bins, tables = (int64_t)hp->hash_tables;
-    CRESSO_REQUIRE(rank >= 1 && rank <= kMaxRank, CRESSO_EUNSUPPORTED,
-                   "rank must be in [1, %d] on the CUDA spectral path (got %lld)", kMaxRank, (long long)rank);
+    CRESSO_REQUIRE(rank >= 1 && rank <= kMaxRankPlain, CRESSO_EUNSUPPORTED,
+                   "rank must be in [1, %d] on the CUDA spectral path (got %lld)", kMaxRankPlain, (long long)rank);
     CRESSO_REQUIRE(bins >= 0 && tables >= 1, CRESSO_EINVAL, "hash_bins must be >= 0, hash_tables >= 1");
     CRESSO_REQUIRE(bins * tables <= kMaxTB64, CRESSO_EUNSUPPORTED,
                    "hash_bins * hash_tables must be <= %d for float64 parameters", kMaxTB64);
     const int rm = rank_pad(rank);
     int64_t max_rows = 1, max_cols = 1, max_n = 1;
-    P.ts.assign(n, T64{});
+    P.ts.assign(n, T64<double>{});
     for (int64_t i = 0; i < n; ++i) {
         const cresso_tensor_desc& d = descs[i];
-        CRESSO_REQUIRE(d.dtype == CRESSO_DTYPE_F64, CRESSO_EINVAL, "tensor %lld: spectral64 takes float64 tensors",
-                       (long long)i);
+        CRESSO_REQUIRE(d.dtype == CRESSO_DTYPE_F64 || (d.dtype == CRESSO_DTYPE_F32 && rank > kMaxRank), CRESSO_EINVAL,
+                       "tensor %lld: spectral64 takes float64 tensors, and float32 tensors when rank > %d",
+                       (long long)i, kMaxRank);
         CRESSO_REQUIRE(d.ndim >= 1 && d.ndim <= CRESSO_MAX_NDIM, CRESSO_EUNSUPPORTED,
                        "tensor %lld: spectral route supports tensors of rank 1 to %d", (long long)i, CRESSO_MAX_NDIM);
         int64_t rows = 1, lead_sum = 0;
@@ -684,15 +707,16 @@ int plan64(const cresso_tensor_desc* descs, int64_t n, const cresso_hparams* hp,
                            d.metric_cos && d.metric_sin && d.metric_p_cos && d.metric_p_sin && d.calcium_cos &&
                            d.calcium_sin && d.mode_confidence && d.force_rms && d.drive_energy && d.surprise && d.action,
                        CRESSO_EINVAL, "tensor %lld: NULL param / grad / workspace / state pointer", (long long)i);
-        T64& T = P.ts[i];
+        T64<double>& T = P.ts[i];
         T.ndim = d.ndim;
         T.rows = rows;
         T.cols = cols;
         T.N = rows * cols;
         T.step = d.step;
         for (int64_t a = 0; a < CRESSO_MAX_NDIM; ++a) T.dims[a] = a < d.ndim ? d.shape[a] : 0;
-        T.param = (double*)d.param;
+        T.param = (double*)d.param;  // storage type: double, or float when f32 (see as_f32)
         T.grad = (const double*)d.grad;
+        T.f32 = d.dtype == CRESSO_DTYPE_F32;
         const ShapeWsHeader wh = shape_ws64_layout(d.ndim, rows, cols, rank, rm);
         const char* ws = (const char*)d.shape_ws;
         T.rowtab = (const double*)(ws + wh.off_rowtab);
@@ -763,45 +787,45 @@ int plan64(const cresso_tensor_desc* descs, int64_t n, const cresso_hparams* hp,
     return CRESSO_OK;
 }
 
-template <int RM>
-int run_tensor(const T64& T, Buf64 Bf, cudaStream_t s) {
+template <int RM, typename P>
+int run_tensor(const T64<P>& T, Buf64 Bf, cudaStream_t s) {
     const int g = Bf.blocks;
     const size_t smem2 = T.hash_on ? (size_t)2 * T.T * T.B * 8 : 0;
     const size_t smem3 = T.hash_on ? (size_t)T.T * T.B * 8 : 0;
     {
         NvtxRange r("cresso64 P1 force energy");
-        s64_p1<<<g, kThreads, 0, s>>>(T, Bf);
+        s64_p1<P><<<g, kThreads, 0, s>>>(T, Bf);
         CRESSO_LAUNCHED("s64_p1");
-        s64_fin1<<<1, 32, 0, s>>>(T, Bf);
+        s64_fin1<P><<<1, 32, 0, s>>>(T, Bf);
         CRESSO_LAUNCHED("s64_fin1");
     }
     {
         NvtxRange r("cresso64 P2 density / bins / projection");
-        s64_p2<RM><<<g, kThreads, smem2, s>>>(T, Bf);
+        s64_p2<RM, P><<<g, kThreads, smem2, s>>>(T, Bf);
         CRESSO_LAUNCHED("s64_p2");
         if (T.inst && T.ndim >= 2) {
-            s64_rowsum<<<(int)std::min<int64_t>(ceil_div(T.rows, kWarps), 4096), kThreads, 0, s>>>(T, Bf);
+            s64_rowsum<P><<<(int)std::min<int64_t>(ceil_div(T.rows, kWarps), 4096), kThreads, 0, s>>>(T, Bf);
             CRESSO_LAUNCHED("s64_rowsum");
-            s64_colsum<<<(int)std::min<int64_t>(ceil_div(T.cols, kThreads), 4096), kThreads, 0, s>>>(T, Bf);
+            s64_colsum<P><<<(int)std::min<int64_t>(ceil_div(T.cols, kThreads), 4096), kThreads, 0, s>>>(T, Bf);
             CRESSO_LAUNCHED("s64_colsum");
         }
-        s64_fin2<RM><<<1, kThreads, 0, s>>>(T, Bf);
+        s64_fin2<RM, P><<<1, kThreads, 0, s>>>(T, Bf);
         CRESSO_LAUNCHED("s64_fin2");
     }
     {
         NvtxRange r("cresso64 P3 tangent / port");
-        s64_p3<RM><<<g, kThreads, smem3, s>>>(T, Bf);
+        s64_p3<RM, P><<<g, kThreads, smem3, s>>>(T, Bf);
         CRESSO_LAUNCHED("s64_p3");
-        s64_fin3<RM><<<1, kThreads, 0, s>>>(T, Bf);
+        s64_fin3<RM, P><<<1, kThreads, 0, s>>>(T, Bf);
         CRESSO_LAUNCHED("s64_fin3");
     }
     {
         NvtxRange r("cresso64 P4 drive Gram / P5 update");
-        s64_p4<RM><<<g, kThreads, 0, s>>>(T, Bf);
+        s64_p4<RM, P><<<g, kThreads, 0, s>>>(T, Bf);
         CRESSO_LAUNCHED("s64_p4");
-        s64_fin4<<<1, kThreads, 0, s>>>(T, Bf);
+        s64_fin4<P><<<1, kThreads, 0, s>>>(T, Bf);
         CRESSO_LAUNCHED("s64_fin4");
-        s64_p5<RM><<<g, kThreads, 0, s>>>(T, Bf);
+        s64_p5<RM, P><<<g, kThreads, 0, s>>>(T, Bf);
         CRESSO_LAUNCHED("s64_p5");
     }
     return CRESSO_OK;
@@ -848,11 +872,22 @@ int cresso_spectral64_run(const cresso_tensor_desc* descs, int64_t n, const cres
     cudaStream_t s = (cudaStream_t)stream;
     const int rm = rank_pad((int64_t)hp->rank);
     // tensors one after another on the stream: each reuses the same scratch
-    for (const T64& T : P.ts) {
-        switch (rm) {
-            case 4: st = run_tensor<4>(T, Bf, s); break;
-            case 8: st = run_tensor<8>(T, Bf, s); break;
-            default: st = run_tensor<16>(T, Bf, s); break;
+    for (const T64<double>& T : P.ts) {
+        if (T.f32) {
+            const T64<float> F = as_f32(T);
+            switch (rm) {
+                case 4: st = run_tensor<4>(F, Bf, s); break;
+                case 8: st = run_tensor<8>(F, Bf, s); break;
+                case 16: st = run_tensor<16>(F, Bf, s); break;
+                default: st = run_tensor<32>(F, Bf, s); break;
+            }
+        } else {
+            switch (rm) {
+                case 4: st = run_tensor<4>(T, Bf, s); break;
+                case 8: st = run_tensor<8>(T, Bf, s); break;
+                case 16: st = run_tensor<16>(T, Bf, s); break;
+                default: st = run_tensor<32>(T, Bf, s); break;
+            }
         }
         if (st) return st;
     }

@@ -414,11 +414,17 @@ class CRESSO5(Optimizer):
                 if spectral_route is None:
                     spectral_route = self._route_cache[rkey] = self._use_spectral_route(param, group)
                 if spectral_route:
-                    if param.dtype is torch.float64:  # float64 work and state: the float64 pipeline
+                    # float64 tensors, and float32 tensors of rank > 16: the float64-arithmetic pipeline
+                    wide = int(group["rank"]) > _lib.MAX_RANK
+                    if param.dtype is torch.float64 or (wide and param.dtype is torch.float32):
+                        if wide and int(group["rank"]) > _lib.MAX_RANK_PLAIN:
+                            raise RuntimeError(f"CRESSO5 B200 path supports rank <= {_lib.MAX_RANK_PLAIN} "
+                                               f"(got {group['rank']})")
                         if getattr(param, "_cresso_shard", None) is not None:
-                            raise RuntimeError("float64 spectral tensors are not sharded: pass them whole")
+                            raise RuntimeError("float64 and rank > 16 spectral tensors are not sharded: pass them "
+                                               "whole")
                         if len(state) == 0:
-                            self._init_spectral(param, group, torch.float64)
+                            self._init_spectral(param, group, wdt)
                         state["step"] += 1
                         spectral64.setdefault(param.device, []).append((param, grad, state))
                         continue
@@ -481,8 +487,10 @@ class CRESSO5(Optimizer):
         return descs
 
     def _run_spectral(self, group: dict, hp: np.ndarray, device, items: list) -> None:
-        if int(group["rank"]) > _lib.MAX_RANK:
-            raise RuntimeError(f"CRESSO5 B200 path supports rank <= {_lib.MAX_RANK} (got {group['rank']})")
+        if int(group["rank"]) > _lib.MAX_RANK:  # float16 / bfloat16 tensors on the fused path
+            raise RuntimeError(f"CRESSO5 B200 path supports rank <= {_lib.MAX_RANK} for float16 / bfloat16 "
+                               f"spectral tensors (got {group['rank']}); float32 and float64 take up to "
+                               f"{_lib.MAX_RANK_PLAIN}")
         L = _lib.lib()
         descs = self._spectral_descs(group, device, items)
         n = len(items)
@@ -501,9 +509,8 @@ class CRESSO5(Optimizer):
         self._spectral_stages(run, scratch, layout)
 
     def _run_spectral64(self, group: dict, hp: np.ndarray, device, items: list) -> None:
-        """Float64 spectral tensors: the float64 pipeline, whole tensors."""
-        if int(group["rank"]) > _lib.MAX_RANK:
-            raise RuntimeError(f"CRESSO5 B200 path supports rank <= {_lib.MAX_RANK} (got {group['rank']})")
+        """Float64 spectral tensors and float32 ones of rank > 16: the float64-arithmetic
+        pipeline, whole tensors."""
         L = _lib.lib()
         F = _lib.DESC_INDEX
         descs = _lib.new_descs(len(items))

@@ -126,6 +126,12 @@ EXTRA_CASES = {
     "spec64_128x40_r16": ((128, 40), dict(rank=16, hash_bins=37, hash_tables=3, instant_metric_power=0.7,
                                           warmup_steps=0), 3, 75, 0.02, 1e-3, "float64"),
     "spec64_thin_8x512": ((8, 512), dict(rank=8, thin_matrix_route="spectral"), 3, 76, 0.02, 1e-3, "float64"),
+    # rank above 16 (the float64-arithmetic spectral path for float32 tensors)
+    "r32_96x80": ((96, 80), dict(rank=32, hash_bins=64, hash_tables=2), 3, 81, 0.02, 1e-3, "float32"),
+    "r24_3000_wd": ((3000,), dict(rank=24, weight_decay=0.01, max_frequency=7), 3, 82, 0.02, 1e-3, "float32"),
+    "r20_6x8x30": ((6, 8, 30), dict(rank=20, hash_bins=37, hash_tables=1, local_sharpness=0.2), 3, 83, 0.02, 1e-3,
+                   "float32"),
+    "r32_f64_64x48": ((64, 48), dict(rank=32), 3, 84, 0.02, 1e-3, "float64"),
 }
 
 
