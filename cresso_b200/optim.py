@@ -52,7 +52,10 @@ class CRESSO5(Optimizer):
 
     Large tensors evolve a compact contact-dissipative multiwave state
     (rank-R spectral oscillators, T x B hash-cell reservoirs, four scalars);
-    LoRA-thin and small tensors use the scalar contact route.
+    LoRA-thin and small tensors use the scalar contact route, and with
+    ``micro_field_max_size > 0`` tensors up to that size keep per-element
+    micro fields.  Parameters may be float32, float16, bfloat16 (float32 work
+    and state) or float64 (float64 work and state), on CUDA devices only.
     """
 
     def __init__(
