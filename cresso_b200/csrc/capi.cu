@@ -34,6 +34,39 @@ void nvtx_push(const char* fmt, ...) {
 
 void nvtx_pop() { nvtxRangePop(); }
 
+constexpr int kUploadBytes = 16384;
+struct UploadBlob {
+    uint32_t w[kUploadBytes / 4];
+};
+
+// The blob is read in place from the parameter space (__grid_constant__).
+__global__ void upload_kernel(const __grid_constant__ UploadBlob blob, unsigned char* __restrict__ dst, int n) {
+    if ((reinterpret_cast<uintptr_t>(dst) & 3) == 0 && (n & 3) == 0) {
+        uint32_t* d = reinterpret_cast<uint32_t*>(dst);
+        for (int i = threadIdx.x; i < (n >> 2); i += blockDim.x) d[i] = blob.w[i];
+    } else {
+        const unsigned char* src = reinterpret_cast<const unsigned char*>(blob.w);
+        for (int i = threadIdx.x; i < n; i += blockDim.x) dst[i] = src[i];
+    }
+}
+
+int upload_async(void* dst, const void* src, size_t bytes, cudaStream_t stream) {
+    const unsigned char* p = static_cast<const unsigned char*>(src);
+    unsigned char* d = static_cast<unsigned char*>(dst);
+    UploadBlob blob;
+    while (bytes > 0) {
+        const size_t c = bytes < (size_t)kUploadBytes ? bytes : (size_t)kUploadBytes;
+        memcpy(blob.w, p, c);
+        upload_kernel<<<1, 256, 0, stream>>>(blob, d, (int)c);
+        const int st = check_launch("upload_kernel");
+        if (st != CRESSO_OK) return st;
+        p += c;
+        d += c;
+        bytes -= c;
+    }
+    return CRESSO_OK;
+}
+
 static thread_local char g_last_error[1024] = {0};
 static std::atomic<int64_t> g_launches{0};
 

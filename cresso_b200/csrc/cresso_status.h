@@ -14,6 +14,13 @@ int check_cuda(cudaError_t e, const char* what);
 // Status of the last kernel launch on this thread (cudaGetLastError).
 int check_launch(const char* what);
 
+// Copies `bytes` of host memory to device memory in stream order, carried as the
+// parameters of kernel launches (16 KB per launch) instead of a DMA copy: the
+// per-step plan uploads then never wait behind large host-to-device copies that
+// other streams have queued on the copy engine (a caller prefetching the next
+// step's gradients, for instance).  The host buffer may be released on return.
+int upload_async(void* dst, const void* src, size_t bytes, cudaStream_t stream);
+
 // NVTX ranges around the library's launches, on when the environment variable
 // CRESSO_B200_NVTX is set to a value other than "0" when the library first
 // checks it (a profiler then shows one range per entry call and per stage).

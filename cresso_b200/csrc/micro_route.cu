@@ -366,8 +366,9 @@ int cresso_micro_run(const cresso_tensor_desc* descs, int64_t n, const cresso_hp
     memcpy(h.hp, hp, sizeof(cresso_hparams));
     const int64_t off_dts = align_up((int64_t)sizeof(MicroHdr), 256);
     cudaStream_t s = (cudaStream_t)stream;
-    CRESSO_CUDA(cudaMemcpyAsync(base, &h, sizeof(h), cudaMemcpyHostToDevice, s));
-    CRESSO_CUDA(cudaMemcpyAsync(base + off_dts, dts.data(), sizeof(MicroTensor) * n, cudaMemcpyHostToDevice, s));
+    int ust = upload_async(base, &h, sizeof(h), s);
+    if (!ust) ust = upload_async(base + off_dts, dts.data(), sizeof(MicroTensor) * n, s);
+    if (ust) return ust;
     const MicroHdr* dh = reinterpret_cast<const MicroHdr*>(base);
     const MicroTensor* dd = reinterpret_cast<const MicroTensor*>(base + off_dts);
     if (n32 > 0) {

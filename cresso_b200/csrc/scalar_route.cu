@@ -960,8 +960,9 @@ static int scal_launch(std::vector<ScalTensor>& dts, const cresso_hparams* hp, c
     h.n = n;
     memcpy(h.hp, hp, sizeof(cresso_hparams));
     const int64_t off_dts = align_up((int64_t)sizeof(ScalHdr), 256);
-    CRESSO_CUDA(cudaMemcpyAsync(base, &h, sizeof(h), cudaMemcpyHostToDevice, s));
-    CRESSO_CUDA(cudaMemcpyAsync(base + off_dts, ord.data(), sizeof(ScalTensor) * n, cudaMemcpyHostToDevice, s));
+    int ust = upload_async(base, &h, sizeof(h), s);
+    if (!ust) ust = upload_async(base + off_dts, ord.data(), sizeof(ScalTensor) * n, s);
+    if (ust) return ust;
     const ScalHdr* dh = reinterpret_cast<const ScalHdr*>(base);
     const ScalTensor* dd = reinterpret_cast<const ScalTensor*>(base + off_dts);
     if (n_cl > 0) {

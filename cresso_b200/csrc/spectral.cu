@@ -2099,13 +2099,13 @@ int cresso_spectral_run(const cresso_tensor_desc* descs, int64_t n, const cresso
     bind_scratch(P, base);
     P.hdr.status = reinterpret_cast<int32_t*>(base + P.off_status);
     if (stage_begin == 0) {
-        CRESSO_CUDA(cudaMemsetAsync(base + P.off_status, 0, sizeof(int32_t), s));
-        CRESSO_CUDA(cudaMemcpyAsync(base + P.off_hdr, &P.hdr, sizeof(GroupHdr), cudaMemcpyHostToDevice, s));
-        CRESSO_CUDA(cudaMemcpyAsync(base + P.off_dts, P.dts.data(), sizeof(DevTensor) * n, cudaMemcpyHostToDevice, s));
-        CRESSO_CUDA(cudaMemcpyAsync(base + P.off_items, P.item_lists.data(), sizeof(int64_t) * (n + 3),
-                                    cudaMemcpyHostToDevice, s));
-        CRESSO_CUDA(cudaMemcpyAsync(base + P.off_tmap, P.tensor_lists.data(), sizeof(int32_t) * n,
-                                    cudaMemcpyHostToDevice, s));
+        const int32_t zero = 0;
+        int ust = upload_async(base + P.off_status, &zero, sizeof(zero), s);
+        if (!ust) ust = upload_async(base + P.off_hdr, &P.hdr, sizeof(GroupHdr), s);
+        if (!ust) ust = upload_async(base + P.off_dts, P.dts.data(), sizeof(DevTensor) * n, s);
+        if (!ust) ust = upload_async(base + P.off_items, P.item_lists.data(), sizeof(int64_t) * (n + 3), s);
+        if (!ust) ust = upload_async(base + P.off_tmap, P.tensor_lists.data(), sizeof(int32_t) * n, s);
+        if (ust) return ust;
         const int hs = launch_half_widen(P, base, s);
         if (hs) return hs;
     }
@@ -2129,8 +2129,8 @@ int cresso_spectral_run(const cresso_tensor_desc* descs, int64_t n, const cresso
         }
         if (st) return st;
     }
-    // The upload reads pageable host memory, which cudaMemcpyAsync stages
-    // before returning, so the plan's host vectors may be released here.
+    // The upload carried the plan in kernel parameters, copied at launch, so the
+    // plan's host vectors may be released here.
     return CRESSO_OK;
 }
 
