@@ -217,6 +217,9 @@ class CRESSO5(Optimizer):
         self._route_cache: Dict[tuple, bool] = {}
         self._scalar_descs: Dict[object, tuple] = {}
         self._micro_descs: Dict[object, tuple] = {}
+        self._fast: Dict[int, tuple] = {}  # per param group: the routing of the last full pass
+        self._spectral_desc_cache: Dict[object, tuple] = {}
+        self._num_sms: Dict[object, int] = {}
 
     # ------------------------------------------------------------------ state
     def _init_common(self, state: dict, device, dtype) -> None:
@@ -375,43 +378,93 @@ class CRESSO5(Optimizer):
         if closure is not None:
             with torch.enable_grad():
                 loss = closure()
-        for group in self.param_groups:
-            spectral: Dict[torch.device, list] = {}
-            scalar: Dict[torch.device, list] = {}
-            micro_items: Dict[torch.device, list] = {}
-            spectral64: Dict[torch.device, list] = {}
+        for gi, group in enumerate(self.param_groups):
             route_sig = (group["min_spectral_size"], group["rank"], group.get("thin_matrix_route", "scalar"),
-                         group.get("thin_matrix_max_width", 64), group.get("thin_matrix_min_aspect", 4.0))
-            micro = int(group.get("micro_field_max_size", 0))
-            for param in group["params"]:
-                grad = param.grad  # step() runs under no_grad: no detach needed
-                if grad is None or not torch.is_floating_point(param):
-                    continue
-                if grad.is_sparse:
-                    raise RuntimeError("CRESSO5 does not support sparse gradients")
-                if not param.is_cuda:
-                    raise RuntimeError(
-                        "CRESSO5 cuda_ops='required' requires every optimized parameter to be a CUDA parameter")
-                if param.dtype not in _DTYPES:
-                    raise RuntimeError("CRESSO5 B200 path supports float32, float16, bfloat16 and float64 "
-                                       f"parameters (got {param.dtype})")
-                if not param.is_contiguous():
-                    raise RuntimeError("CRESSO5 B200 path updates parameters in place and needs them contiguous")
-                if grad.dtype is not param.dtype or grad.device != param.device:
-                    raise RuntimeError("CRESSO5: grad must match its parameter's dtype and device")
-                if not grad.is_contiguous():
-                    grad = grad.contiguous()
-                state = self.state[param]
-                # work and state type: float64 for float64 parameters, else float32 (cresso_v5.py:119-124)
-                wdt = torch.float64 if param.dtype is torch.float64 else torch.float32
-                if micro > 0 and param.ndim > 0 and param.numel() <= micro:  # cresso_v5.py:839-840
-                    if getattr(param, "_cresso_shard", None) is not None:
-                        raise RuntimeError("micro-field tensors are not sharded: pass them whole")
-                    if len(state) == 0:
-                        self._init_micro(param, wdt)
-                    state["step"] += 1
-                    micro_items.setdefault(param.device, []).append((param, grad, state))
-                    continue
+                         group.get("thin_matrix_max_width", 64), group.get("thin_matrix_min_aspect", 4.0),
+                         group.get("micro_field_max_size", 0))
+            routed = self._route_fast(gi, group, route_sig)
+            if routed is None:
+                routed = self._route_full(gi, group, route_sig)
+            spectral, scalar, micro_items, spectral64 = routed
+            hp = None
+            for device, items in spectral.items():
+                hp = _lib.pack_hparams(group) if hp is None else hp
+                self._run_spectral(group, hp, device, items)
+            for device, items in scalar.items():
+                hp = _lib.pack_hparams(group) if hp is None else hp
+                self._run_scalar(hp, device, items)
+            for device, items in micro_items.items():
+                hp = _lib.pack_hparams(group) if hp is None else hp
+                self._run_micro(hp, device, items)
+            for device, items in spectral64.items():
+                hp = _lib.pack_hparams(group) if hp is None else hp
+                self._run_spectral64(group, hp, device, items)
+        return loss
+
+    def _route_fast(self, gi: int, group: dict, route_sig: tuple):
+        """The routing of the group's last full pass, reused when nothing it depends on
+        has changed: the same parameter objects (contiguous, same dtype) with the same
+        state dicts, every parameter with a contiguous strided gradient of its dtype on
+        its device, and the same routing settings.  Anything else returns None (before
+        any state is touched) and the full pass runs."""
+        cached = self._fast.get(gi)
+        if cached is None:
+            return None
+        sig, ids, params, states, dtypes, devices, slots = cached
+        plist = group["params"]
+        if sig != route_sig or len(plist) != len(params) or tuple(map(id, plist)) != ids:
+            return None
+        grads = [p.grad for p in params]
+        state = self.state
+        for p, g, st, dt, dev in zip(params, grads, states, dtypes, devices):
+            if (g is None or g.dtype is not dt or g.layout is not torch.strided or not g.is_contiguous()
+                    or g.device != dev or not p.is_contiguous() or state.get(p) is not st):
+                return None
+        for st in states:
+            st["step"] += 1
+        routed: Tuple[Dict[torch.device, list], ...] = ({}, {}, {}, {})
+        for (kind, i), p, g, st, dev in zip(slots, params, grads, states, devices):
+            routed[kind].setdefault(dev, []).append((p, g, st))
+        return routed
+
+    def _route_full(self, gi: int, group: dict, route_sig: tuple):
+        """Checks and routes every parameter of the group (cresso_v5.py:822-845) and
+        creates missing state; records the routing for _route_fast when every
+        parameter took part."""
+        routed: Tuple[Dict[torch.device, list], ...] = ({}, {}, {}, {})  # spectral, scalar, micro, spectral64
+        SPEC, SCAL, MICRO, SPEC64 = 0, 1, 2, 3
+        micro = int(group.get("micro_field_max_size", 0))
+        slots = []
+        complete = True
+        for param in group["params"]:
+            grad = param.grad  # step() runs under no_grad: no detach needed
+            if grad is None or not torch.is_floating_point(param):
+                complete = False
+                continue
+            if grad.is_sparse:
+                raise RuntimeError("CRESSO5 does not support sparse gradients")
+            if not param.is_cuda:
+                raise RuntimeError(
+                    "CRESSO5 cuda_ops='required' requires every optimized parameter to be a CUDA parameter")
+            if param.dtype not in _DTYPES:
+                raise RuntimeError("CRESSO5 B200 path supports float32, float16, bfloat16 and float64 "
+                                   f"parameters (got {param.dtype})")
+            if not param.is_contiguous():
+                raise RuntimeError("CRESSO5 B200 path updates parameters in place and needs them contiguous")
+            if grad.dtype is not param.dtype or grad.device != param.device:
+                raise RuntimeError("CRESSO5: grad must match its parameter's dtype and device")
+            if not grad.is_contiguous():
+                grad = grad.contiguous()
+            state = self.state[param]
+            # work and state type: float64 for float64 parameters, else float32 (cresso_v5.py:119-124)
+            wdt = torch.float64 if param.dtype is torch.float64 else torch.float32
+            if micro > 0 and param.ndim > 0 and param.numel() <= micro:  # cresso_v5.py:839-840
+                if getattr(param, "_cresso_shard", None) is not None:
+                    raise RuntimeError("micro-field tensors are not sharded: pass them whole")
+                if len(state) == 0:
+                    self._init_micro(param, wdt)
+                kind = MICRO
+            else:
                 rkey = (param.shape, getattr(param, "_cresso_shard", None), route_sig)
                 spectral_route = self._route_cache.get(rkey)
                 if spectral_route is None:
@@ -428,38 +481,55 @@ class CRESSO5(Optimizer):
                                                "whole")
                         if len(state) == 0:
                             self._init_spectral(param, group, wdt)
-                        state["step"] += 1
-                        spectral64.setdefault(param.device, []).append((param, grad, state))
-                        continue
-                    if len(state) == 0:
-                        self._init_spectral(param, group, torch.float32, self._geometry(param)[0])
-                    state["step"] += 1
-                    spectral.setdefault(param.device, []).append((param, grad, state))
+                        kind = SPEC64
+                    else:
+                        if len(state) == 0:
+                            self._init_spectral(param, group, torch.float32, self._geometry(param)[0])
+                        kind = SPEC
                 else:
                     if getattr(param, "_cresso_shard", None) is not None:
-                        raise RuntimeError("scalar-route (small / LoRA-thin) tensors are not sharded: pass them whole")
+                        raise RuntimeError("scalar-route (small / LoRA-thin) tensors are not sharded: pass them "
+                                           "whole")
                     if len(state) == 0:
                         self._init_scalar(param, wdt)
-                    state["step"] += 1
-                    scalar.setdefault(param.device, []).append((param, grad, state))
-            hp = None
-            for device, items in spectral.items():
-                hp = _lib.pack_hparams(group) if hp is None else hp
-                self._run_spectral(group, hp, device, items)
-            for device, items in scalar.items():
-                hp = _lib.pack_hparams(group) if hp is None else hp
-                self._run_scalar(hp, device, items)
-            for device, items in micro_items.items():
-                hp = _lib.pack_hparams(group) if hp is None else hp
-                self._run_micro(hp, device, items)
-            for device, items in spectral64.items():
-                hp = _lib.pack_hparams(group) if hp is None else hp
-                self._run_spectral64(group, hp, device, items)
-        return loss
+                    kind = SCAL
+            state["step"] += 1
+            routed[kind].setdefault(param.device, []).append((param, grad, state))
+            slots.append((kind, param, state))
+        if complete and slots:
+            params = tuple(p for _, p, _ in slots)
+            self._fast[gi] = (route_sig, tuple(map(id, group["params"])), params, tuple(st for _, _, st in slots),
+                              tuple(p.dtype for p in params), tuple(p.device for p in params),
+                              tuple((k, i) for i, (k, _, _) in enumerate(slots)))
+        else:
+            self._fast.pop(gi, None)
+        return routed
 
     def _spectral_descs(self, group: dict, device, items: list) -> np.ndarray:
+        """Descriptor table of the spectral group.  Like the small-route tables it is
+        reused while the parameters, their storage, their state dicts and the settings
+        it depends on stay the same, refreshing gradient pointers and step counters;
+        the entry holds every object whose memory it points at."""
+        F = _lib.DESC_INDEX
+        bins, tables = int(group["hash_bins"]), int(group["hash_tables"])
+        settings = (group["rank"], group["max_frequency"], bins, tables, group.get("hard_channel_min_size"),
+                    group.get("thin_matrix_hard_cutoff"))
+        ident = (settings, tuple((id(p), p.data_ptr(), p.shape, id(st)) for p, g, st in items))
+        key = (device, id(group))
+        cached = self._spectral_desc_cache.get(key)
+        if cached is not None and cached[0] == ident:
+            descs = cached[1]
+        else:
+            descs, keep = self._build_spectral_descs(group, device, items)
+            self._spectral_desc_cache[key] = (ident, descs, keep, group)
+        descs[:, F["grad"]] = [g.data_ptr() for _, g, _ in items]
+        descs[:, F["step"]] = [st["step"] for _, _, st in items]
+        return descs
+
+    def _build_spectral_descs(self, group: dict, device, items: list):
         F = _lib.DESC_INDEX
         descs = _lib.new_descs(len(items))
+        keep = []
         bins, tables = int(group["hash_bins"]), int(group["hash_tables"])
         for i, (p, g, st) in enumerate(items):
             shape, row0, rows, col0, cols = self._geometry(p)
@@ -478,16 +548,22 @@ class CRESSO5(Optimizer):
             d[F["param"]] = p.data_ptr()
             d[F["grad"]] = g.data_ptr()
             d[F["dtype"]] = _DTYPES[p.dtype]
-            d[F["shape_ws"]] = self._workspace(device, shape, group, st["freqs"]).data_ptr()
+            ws = self._workspace(device, shape, group, st["freqs"])
+            d[F["shape_ws"]] = ws.data_ptr()
+            held = [p, st, ws]
             if "hash_energy" in st and bins > 0 and hard_enabled(shape, group):
                 buf, cap = self._hash_index_cache(device, bins, tables, numel)
                 d[F["hash_cache"]] = buf.data_ptr()
                 d[F["hash_cache_n"]] = cap
+                held.append(buf)
                 for name in ("hash_energy", "hash_impulse", "hash_refractory"):
                     d[F[name]] = st[name].data_ptr()
+                    held.append(st[name])
             for name in ("omega",) + _SPECTRAL_RANK_STATE + ("force_rms", "drive_energy", "surprise", "action"):
                 d[F[name]] = st[name].data_ptr()
-        return descs
+                held.append(st[name])
+            keep.append(held)
+        return descs, keep
 
     def _run_spectral(self, group: dict, hp: np.ndarray, device, items: list) -> None:
         if int(group["rank"]) > _lib.MAX_RANK:  # float16 / bfloat16 tensors on the fused path
@@ -497,7 +573,9 @@ class CRESSO5(Optimizer):
         L = _lib.lib()
         descs = self._spectral_descs(group, device, items)
         n = len(items)
-        num_sms = torch.cuda.get_device_properties(device).multi_processor_count
+        num_sms = self._num_sms.get(device)
+        if num_sms is None:
+            num_sms = self._num_sms[device] = torch.cuda.get_device_properties(device).multi_processor_count
         layout = np.zeros(10, dtype=np.int64)
         _lib.check(L.cresso_spectral_layout(_lib.ptr(descs), n, _lib.ptr(hp), num_sms,
                                             layout.ctypes.data_as(_lib._pi64), 10), "spectral_layout")
