@@ -510,3 +510,33 @@ def test_nvtx_ranges_switch_on_without_changing_results():
         assert r.returncode == 0, r.stderr[-2000:]
         outs.append(r.stdout.strip().splitlines()[-1])
     assert outs[0] == outs[1]
+
+
+def test_fast_routing_path_follows_the_full_one():
+    """Steps reuse the previous routing only while nothing it depends on changed:
+    a parameter without a gradient, a state_dict reload and a new gradient type
+    each send the step back through the full checks.  The sequence is compared
+    with the oracle doing the same steps."""
+    g = torch.Generator().manual_seed(11)
+    shapes = [(256, 256), (512, 16), (9,)]
+    inits = [torch.randn(s, generator=g) * 0.02 for s in shapes]
+    kw = dict(rank=8, hash_bins=64, hash_tables=2, micro_field_max_size=16)
+    ps = [torch.nn.Parameter(x.clone().cuda()) for x in inits]
+    rs = [torch.nn.Parameter(x.clone()) for x in inits]
+    opt = cresso_b200.CRESSO5(ps, **kw)
+    ref = O.OracleCRESSO5(rs, **kw)
+    for step in range(6):
+        gs = [torch.randn(s, generator=g) * 1e-3 for s in shapes]
+        for i, (p, r, gg) in enumerate(zip(ps, rs, gs)):
+            skip = step == 3 and i == 0
+            p.grad = None if skip else gg.cuda()
+            r.grad = None if skip else gg.clone()
+        if step == 4:  # reload the state: new state dicts, the cached routing must not be used
+            opt.load_state_dict(copy.deepcopy(opt.state_dict()))
+        opt.step()
+        ref.step()
+        assert (0 in opt._fast) == (step != 3)  # recorded after every pass in which all took part
+    torch.cuda.synchronize()
+    for p, r, s in zip(ps, rs, shapes):
+        assert opt.state[p]["step"] == ref.state[r]["step"], s
+        assert rel_rms(p.detach().cpu(), r.detach()) <= 1e-5, s
