@@ -438,14 +438,23 @@ def time_e2e(opt, params, grads_dev, args, world, device, stream, n_total, bpe=B
     copy runs on a copy stream while step k computes (input prefetch, as a
     training loop's loader does), so a step costs max(copy, compute).  Every
     step's full gradient copy and result read lies inside the timed region."""
-    host = []
-    for g in grads_dev:
-        h = torch.empty(g.shape, dtype=g.dtype, pin_memory=True)
-        h.copy_(g)
-        host.append(h)
-    h2d = sum(h.numel() * h.element_size() for h in host)
+    # all gradients of a step in one flat pinned host buffer (as a training loop's
+    # gradient buckets hold them) and two flat device buffers; the gradients are views
+    dtype = grads_dev[0].dtype
+    sizes = [g.numel() for g in grads_dev]
+    offs, total = [], 0
+    for n in sizes:  # each gradient starts on a 256-byte boundary
+        offs.append(total)
+        total += (n + 63) // 64 * 64
+    host_flat = torch.zeros(total, dtype=dtype, pin_memory=True)
+    for g, n, off in zip(grads_dev, sizes, offs):
+        host_flat[off:off + n].copy_(g.reshape(-1))
+    h2d = total * host_flat.element_size()
     out_host = torch.empty(len(params), dtype=torch.float32, pin_memory=True)
-    bufs = [list(grads_dev), [torch.empty_like(g) for g in grads_dev]]
+    dev_flat = [torch.empty(total, dtype=dtype, device=device) for _ in range(2)]
+    bufs = []
+    for flat in dev_flat:
+        bufs.append([flat[off:off + n].view(g.shape) for g, n, off in zip(grads_dev, sizes, offs)])
     copy_stream = torch.cuda.Stream(device)
     copied = [torch.cuda.Event(), torch.cuda.Event()]
     stepped = [torch.cuda.Event(), torch.cuda.Event()]
@@ -454,8 +463,7 @@ def time_e2e(opt, params, grads_dev, args, world, device, stream, n_total, bpe=B
         b = k % 2
         with torch.cuda.stream(copy_stream):
             copy_stream.wait_event(stepped[b])
-            for d, h in zip(bufs[b], host):
-                d.copy_(h, non_blocking=True)
+            dev_flat[b].copy_(host_flat, non_blocking=True)
             copied[b].record(copy_stream)
 
     def run(n):
