@@ -356,9 +356,10 @@ def b200_arm(args, world, rank, local):
             "config": {"workload": f"{args.workload}: " + (f"7B-shaped {args.dtype} set, 290 tensors, 6,738,411,520 elements"
                                                             if args.workload == "c5" else str(shapes[0])),
                        "rank": kw["rank"], "hash_bins": kw["hash_bins"], "hash_tables": kw["hash_tables"],
-                       "sharding": (f"ZeRO-1 over {world} GPU(s), {len(opt.buckets)} bucket(s) of >= "
-                                    f"{args.bucket_elements} elements, all-gather of bucket k under the compute of "
-                                    f"bucket k + 1" if zero else
+                       "sharding": ((f"ZeRO-1 over {world} GPU(s), {len(opt.buckets)} buckets of >= "
+                                     f"{args.bucket_elements} elements, all-gather of bucket k under the compute of "
+                                     f"bucket k + 1" if args.bucket_elements > 0 else
+                                     f"ZeRO-1 over {world} GPU(s), one all-gather after the step") if zero else
                                     f"row-sharded over {world} GPU(s)" if world > 1 else "single GPU"),
                        "l2": "no flush: inputs of every step (grads + params) exceed the 126 MB L2"
                              if n_total * 8 > 2 * 126e6 else "inputs fit in L2",
