@@ -23,10 +23,20 @@ optimizer API with the gradients copied host -> device from pinned memory
 every step (double-buffered: the next step's copy overlaps the current step)
 and a per-tensor drive-energy vector read back.
 
---impl reference times the reference algorithm's PyTorch CPU path (the
-oracle restatement in oracle/, the same torch operations as
-cresso_v5.CRESSO5(cuda_ops='off')) on the host cores, on a bounded sample of
-the workload (one tensor of the set per step), in the same unit.
+--impl reference times the reference's own PyTorch CPU path
+(cresso_v5.CRESSO5(cuda_ops='off') of the unmodified reference installed into
+baseline/_ref; the oracle restatement of the same torch operations if that is
+absent) on all host cores, on a bounded sample of the workload (c5: one
+(4096, 4096) weight of the set per step; c1-c4: the whole set), in the same
+unit and with the same `config`.
+
+The default run (c5, one GPU) adds `per_config`: c1, c2, c3, c4 and c4s (the
+840 thin tensors on thin_matrix_route="spectral") timed the same way.  With
+N > 1 row-sharded GPUs the run first checks the sharded step against the
+single-GPU step on this box (`parity` in the line; it exits non-zero above
+1e-6 relative RMS or if the ranks' states differ) and reports the time of the
+all-reduces between the passes (`exchange_ms`) and of the reduce / finalize
+stages (`reduce_finalize_ms`) per step.
 """
 
 from __future__ import annotations
@@ -185,80 +195,139 @@ def barrier(world):
 
 
 # ---------------------------------------------------------------------------
-# reference arm / CPU baseline: the reference algorithm's PyTorch CPU path
+# reference arm / CPU baseline: the reference's PyTorch CPU path
 # ---------------------------------------------------------------------------
-def cpu_reference_steps(shape, kw, istd, steps, warmup, budget_s=None):
-    """Times `steps` CPU steps of the oracle restatement on one tensor; returns
-    (seconds per step, elements per step, threads, sample description)."""
+REF_DIR = ROOT / "baseline" / "_ref"
+
+
+def reference_optimizer_class():
+    """(CRESSO5 class, kind): the unmodified reference package installed under
+    baseline/_ref (cresso_v5.CRESSO5 with cuda_ops='off', kind "reference"); if it
+    is not installed, the oracle restatement of the same torch operations
+    (kind "port")."""
+    if (REF_DIR / "cresso_v5.py").exists():
+        if str(REF_DIR) not in sys.path:
+            sys.path.insert(0, str(REF_DIR))
+        import cresso_v5
+
+        def make(params, **kw):
+            return cresso_v5.CRESSO5(params, cuda_ops="off", **kw)
+        return make, "reference"
     from oracle import cresso5_oracle as O
 
+    return O.OracleCRESSO5, "port"
+
+
+def cpu_model() -> str:
+    try:
+        for ln in subprocess.run(["lscpu"], capture_output=True, text=True, timeout=10).stdout.splitlines():
+            if ln.startswith("Model name:"):
+                return ln.split(":", 1)[1].strip()
+    except Exception:
+        pass
+    return "unknown"
+
+
+def cpu_reference_steps(shapes, kw, istd, steps, warmup, budget_s=None, row_scale=False):
+    """Times `steps` CPU steps of the reference path on a set of tensors (one
+    optimizer over all of them, BASELINE inputs: init seed 0, fresh gradients
+    each step); returns (seconds per step, elements per step, threads, steps
+    timed, kind)."""
+    make, kind = reference_optimizer_class()
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
     g = torch.Generator().manual_seed(0)
-    p = torch.nn.Parameter(torch.randn(shape, generator=g) * istd)
-    grads = [torch.randn(shape, generator=g) * 1e-3 for _ in range(2)]
-    opt = O.OracleCRESSO5([p], **kw)
+    ps = [torch.nn.Parameter(torch.randn(s, generator=g) * istd) for s in shapes]
+    rs = None
+    if row_scale:  # BASELINE c2: per-row log-normal(0, 0.5) gradient scale, drawn once (seed 7)
+        rs = torch.exp(0.5 * torch.randn((shapes[0][0], 1), generator=torch.Generator().manual_seed(7)))
+    opt = make(ps, **kw)
+
+    def grads(step):
+        gg = torch.Generator().manual_seed(1000 + step)
+        for p in ps:
+            x = torch.randn(p.shape, generator=gg) * 1e-3
+            p.grad = x * rs if rs is not None else x
+
     for i in range(warmup):
-        p.grad = grads[i % 2]
+        grads(i)
         opt.step()
     times = []
     for i in range(steps):
-        p.grad = grads[i % 2]
+        grads(warmup + i)
         t0 = time.perf_counter()
         opt.step()
         times.append(time.perf_counter() - t0)
         if budget_s is not None and sum(times) > budget_s:
             break
-    return sum(times) / len(times), numel(shape), threads, len(times)
+    return sum(times) / len(times), sum(numel(s) for s in shapes), threads, len(times), kind
+
+
+def reference_sample(workload: str):
+    """The bounded CPU sample of a workload: the whole set where a step takes
+    seconds (c1-c4), one (4096, 4096) weight of the set per step for c5 (its
+    per-element rate stands for the set: 226 of its 290 tensors are 4096-wide
+    matrices)."""
+    shapes, kw, istd = workload_shapes(workload)
+    if workload == "c5":
+        return [(4096, 4096)], kw, istd, "one (4096, 4096) weight of the 7B-shaped set per step"
+    return shapes, kw, istd, f"the whole {workload} set per step"
 
 
 def reference_arm(args, world, rank):
     if rank != 0:
         return
-    shapes, kw, istd = workload_shapes(args.workload)
-    # bounded sample: one tensor of the set per step, shrunk until a step is a few seconds
-    sample = max(shapes, key=lambda s: (numel(s) if numel(s) <= 4096 * 4096 else 0))
-    t_probe, _, _, _ = cpu_reference_steps((min(sample[0], 1024),) + tuple(sample[1:]), kw, istd, 1, 0)
-    per_elem = t_probe / numel((min(sample[0], 1024),) + tuple(sample[1:]))
-    rows = sample[0]
-    while rows > 256 and per_elem * rows * numel(sample[1:]) > 6.0:
-        rows //= 2
-    shape = (rows,) + tuple(sample[1:])
-    sec, n, threads, done = cpu_reference_steps(shape, kw, istd, args.steps, args.warmup)
+    shapes, kw, istd, what = reference_sample(args.workload)
+    sec, n, threads, done, kind = cpu_reference_steps(shapes, kw, istd, args.steps, args.warmup, budget_s=240.0,
+                                                      row_scale=args.workload == "c2")
     value = BYTES_PER_ELEM * n / sec / 1e9
+    path = ("reference cresso_v5.CRESSO5(cuda_ops='off') from baseline/_ref, PyTorch CPU path" if kind == "reference"
+            else "oracle restatement of the reference PyTorch CPU path")
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": args.gpus,
         "steps": done, "warmup": args.warmup, "ms_per_step": sec * 1e3, "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": f"{args.workload} sample {shape}", "rank": kw["rank"], "hash_bins": kw["hash_bins"],
-                   "hash_tables": kw["hash_tables"], "path": "reference PyTorch CPU path (oracle restatement)"},
-        "cpu_baseline": {"value": value, "unit": "GB/s", "cores": threads, "kind": "port",
-                         "sample": f"one {shape} tensor of {args.workload} per step, {done} steps after "
-                                   f"{args.warmup} warm-up"},
+        "config": workload_config(args.workload, shapes_of(args.workload), kw, "f32"),
+        "cpu_baseline": {"value": value, "unit": "GB/s", "cores": threads, "kind": kind, "cpu": cpu_model(),
+                         "sample": f"{what}, {done} steps after {args.warmup} warm-up; {path}"},
         "e2e": {"value": value, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
 
 
+def shapes_of(workload):
+    return workload_shapes(workload)[0]
+
+
+def workload_config(workload, shapes, kw, dtype):
+    """The `config` object of a workload (identical for both arms)."""
+    n_total = sum(numel(s) for s in shapes)
+    desc = {"c5": f"7B-shaped {dtype} set, 290 tensors, 6,738,411,520 elements",
+            "c3": "64 LoRA-thin (4096, 16) / (16, 4096), scalar route",
+            "c4": "840 LoRA-thin (4096, 16) / (16, 4096), scalar route",
+            "c4s": "840 LoRA-thin (4096, 16) / (16, 4096), thin_matrix_route='spectral'"}.get(workload, str(shapes[0]))
+    return {"workload": f"{workload}: {desc}", "rank": kw["rank"], "hash_bins": kw["hash_bins"],
+            "hash_tables": kw["hash_tables"], "elements": n_total,
+            "l2": "no flush: inputs of every step (grads + params) exceed the 126 MB L2"
+                  if n_total * 8 > 2 * 126e6 else "inputs fit in the 126 MB L2 (no flush)"}
+
+
 # ---------------------------------------------------------------------------
 # B200 arm
 # ---------------------------------------------------------------------------
-def b200_arm(args, world, rank, local):
-    import cresso_b200
-    from cresso_b200 import _lib
-    from cresso_b200.distributed import RowShardedCRESSO5, ZeroCRESSO5, mark_row_shard, row_block
+def make_inputs(name, args, world, rank, device, zero):
+    """Parameters (with gradients attached) of a workload on this rank: row blocks of
+    every tensor under row sharding, the whole set otherwise.  Returns (shapes, kw,
+    params, device gradients, local elements, total elements, bytes per element)."""
+    from cresso_b200.distributed import mark_row_shard, row_block
 
-    device = torch.device("cuda", local)
-    zero = world > 1 and args.sharding == "zero"  # ZeRO-1: whole tensors, replicated inputs
-    torch.cuda.set_device(device)
-    shapes, kw, istd = workload_shapes(args.workload)
-    params, grads_dev = [], []
+    shapes, kw, istd = workload_shapes(name)
     pdt = {"f32": torch.float32, "bf16": torch.bfloat16, "f16": torch.float16, "f64": torch.float64}[args.dtype]
     bpe = 3 * torch.empty((), dtype=pdt).element_size()  # grad read + param read + param write
     gen = torch.Generator(device=device)
     gen.manual_seed(1234 + (0 if zero else rank))
-    n_local = 0
-    for i, s in enumerate(shapes):
+    params, grads_dev, n_local = [], [], 0
+    for s in shapes:
         if world > 1 and not zero:
             start, stop = row_block(s[0], rank, world)
             local_shape = (stop - start,) + tuple(s[1:])
@@ -271,7 +340,7 @@ def b200_arm(args, world, rank, local):
             mark_row_shard(p, s, start)
         g = torch.empty(local_shape, device=device)
         g.normal_(0.0, 1e-3, generator=gen)
-        if args.workload == "c2":  # BASELINE c2: per-row log-normal(0, 0.5) gradient scale
+        if name == "c2":  # BASELINE c2: per-row log-normal(0, 0.5) gradient scale
             row_scale = torch.empty((local_shape[0], 1), device=device).normal_(0.0, 1.0, generator=gen)
             g.mul_(torch.exp(0.5 * row_scale))
         g = g.to(pdt)
@@ -279,14 +348,147 @@ def b200_arm(args, world, rank, local):
         params.append(p)
         grads_dev.append(g)
         n_local += numel(local_shape)
-    n_total = sum(numel(s) for s in shapes)
+    return shapes, kw, params, grads_dev, n_local, sum(numel(s) for s in shapes), bpe
+
+
+def time_steps(opt, steps, device, stream, world):
+    """Device time of exactly `steps` steps (CUDA events, barrier and synchronize on
+    both sides, max over ranks), in ms per step."""
+    barrier(world)
+    torch.cuda.synchronize(device)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(steps):
+        opt.step()
+    e1.record(stream)
+    torch.cuda.synchronize(device)
+    barrier(world)
+    return max_over_ranks(e0.elapsed_time(e1) / steps, world, device)
+
+
+def sharded_parity_check(world, rank, device, steps=3):
+    """Correctness of the row-sharded step on this box, before anything is timed:
+    every rank steps its row block of one (4096, 4096) and one (4096,) tensor for
+    `steps` steps (RowShardedCRESSO5), rank 0 steps the same whole tensors with
+    the single-GPU CRESSO5, and the blocks are gathered (each rank adds its rows
+    into a zero tensor, SUM-all-reduced: exact).  Returns the relative RMS of the
+    parameters, the largest relative RMS of a state tensor against the
+    single-GPU state, and whether every rank holds bitwise the same state."""
+    import cresso_b200
+    import torch.distributed as dist
+
+    from cresso_b200.distributed import RowShardedCRESSO5, mark_row_shard, row_block
+
+    shapes = [(4096, 4096), (4096,)]
+    kw = dict(lr=2e-3, rank=8, max_frequency=5, hash_bins=64, hash_tables=2)
+    g = torch.Generator(device=device).manual_seed(77)  # the same inputs on every rank
+    inits = [torch.randn(s, generator=g, device=device) * 0.02 for s in shapes]
+    grads = [[torch.randn(s, generator=g, device=device) * 1e-3 for s in shapes] for _ in range(steps)]
+    local = []
+    for s, x in zip(shapes, inits):
+        a, b = row_block(s[0], rank, world)
+        p = torch.nn.Parameter(x[a:b].clone())
+        mark_row_shard(p, s, a)
+        local.append((p, a, b))
+    opt = RowShardedCRESSO5([p for p, _, _ in local], **kw)
+    for gs in grads:
+        for (p, a, b), gg in zip(local, gs):
+            p.grad = gg[a:b].clone()
+        opt.step()
+    opt.check_device_status()
+    full = []
+    for (p, a, b), s in zip(local, shapes):
+        t = torch.zeros(s, device=device)
+        t[a:b] = p.detach()
+        dist.all_reduce(t)
+        full.append(t)
+    identical = True
+    states = [opt.state[p] for p, _, _ in local]
+    for st in states:
+        for k, v in sorted(st.items()):
+            if torch.is_tensor(v) and v.is_floating_point():
+                hi, lo = v.detach().clone(), v.detach().clone()
+                dist.all_reduce(hi, op=dist.ReduceOp.MAX)
+                dist.all_reduce(lo, op=dist.ReduceOp.MIN)
+                identical = identical and bool(torch.equal(hi, lo))
+    flag = torch.tensor([1.0 if identical else 0.0], device=device)
+    dist.all_reduce(flag, op=dist.ReduceOp.MIN)
+    out = {"param_rel_rms": None, "state_max_rel": None, "state_identical_across_ranks": bool(flag.item() == 1.0),
+           "shapes": [list(s) for s in shapes], "steps": steps}
+    bad = torch.zeros(1, device=device)
+    if rank == 0:
+        ps = [torch.nn.Parameter(x.clone()) for x in inits]
+        ref = cresso_b200.CRESSO5(ps, **kw)
+        for gs in grads:
+            for p, gg in zip(ps, gs):
+                p.grad = gg.clone()
+            ref.step()
+        torch.cuda.synchronize(device)
+
+        def rel(a, b):
+            a, b = a.double(), b.double()
+            return float(torch.sqrt(torch.mean((a - b) ** 2)) / (torch.sqrt(torch.mean(b * b)) + 1e-30))
+
+        out["param_rel_rms"] = max(rel(f, p.detach()) for f, p in zip(full, ps))
+        out["state_max_rel"] = max(rel(st[k], ref.state[p][k]) for st, p in zip(states, ps)
+                                   for k, v in st.items() if torch.is_tensor(v) and v.is_floating_point())
+        if out["param_rel_rms"] > 1e-6 or not out["state_identical_across_ranks"]:
+            bad.fill_(1.0)
+    dist.all_reduce(bad)  # every rank learns the verdict
+    out["ok"] = bool(bad.item() == 0.0)
+    del opt, local, full
+    torch.cuda.empty_cache()
+    return out
+
+
+def quick_config(name, args, device, stream):
+    """One more BASELINE config on this GPU (N = 1): device time of args.steps steps
+    after args.warmup, and the end-to-end time through CRESSO5.step() with host
+    gradients."""
+    import cresso_b200
+
+    shapes, kw, params, grads_dev, n_local, n_total, bpe = make_inputs(name, args, 1, 0, device, False)
+    opt = cresso_b200.CRESSO5(params, **kw)
+    for _ in range(args.warmup):
+        opt.step()
+    torch.cuda.synchronize(device)
+    ms = time_steps(opt, args.steps, device, stream, 1)
+    e2e = time_e2e(opt, params, grads_dev, args, 1, device, stream, n_total, bpe)
+    opt.check_device_status()
+    out = {"ms_per_step": round(ms, 5), "value": round(bpe * n_total / (ms * 1e-3) / 1e9, 3), "unit": "GB/s",
+           "elements": n_total, "workload": workload_config(name, shapes, kw, args.dtype)["workload"],
+           "e2e": {"value": round(e2e["value"], 3), "ms_per_step": round(e2e["ms_per_step"], 5)}}
+    del opt, params, grads_dev
+    torch.cuda.empty_cache()
+    return out
+
+
+def b200_arm(args, world, rank, local):
+    from cresso_b200 import _lib
+    import cresso_b200
+    from cresso_b200.distributed import RowShardedCRESSO5, ZeroCRESSO5
+
+    device = torch.device("cuda", local)
+    zero = world > 1 and args.sharding == "zero"  # ZeRO-1: whole tensors, replicated inputs
+    torch.cuda.set_device(device)
+    stream = torch.cuda.current_stream(device)
+
+    # ---- multi-GPU: correctness of the sharded step on this box before any timing
+    parity = None
+    if world > 1 and not zero:
+        parity = sharded_parity_check(world, rank, device)
+        if rank == 0:
+            print(json.dumps({"sharded_parity": parity}), file=sys.stderr, flush=True)
+        if not parity["ok"]:
+            raise SystemExit(f"row-sharded step differs from the single-GPU step: {parity}")
+
+    shapes, kw, params, grads_dev, n_local, n_total, bpe = make_inputs(args.workload, args, world, rank, device, zero)
     if zero:
         opt = ZeroCRESSO5(params, bucket_elements=args.bucket_elements, **kw)
         n_local = sum(p.numel() for p in params if opt.owner[p] == rank)
         args.skip_e2e = True  # non-owned tensors carry no state to read back
     else:
         opt = RowShardedCRESSO5(params, **kw) if world > 1 else cresso_b200.CRESSO5(params, **kw)
-    stream = torch.cuda.current_stream(device)
 
     for _ in range(args.warmup):
         opt.step()
@@ -302,22 +504,13 @@ def b200_arm(args, world, rank, local):
             pass
     launches0 = _lib.launch_count()
     with ClockSampler(rank == 0, uuids) as clk:
-        barrier(world)
-        torch.cuda.synchronize(device)
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record(stream)
-        for _ in range(args.steps):
-            opt.step()
-        e1.record(stream)
-        torch.cuda.synchronize(device)
-        barrier(world)
+        ms = time_steps(opt, args.steps, device, stream, world)
     launches = _lib.launch_count() - launches0
-    ms = e0.elapsed_time(e1) / args.steps
-    ms = max_over_ranks(ms, world, device)
+    opt.check_device_status()
     value = bpe * n_total / (ms * 1e-3) / 1e9
 
     # ---- per-pass kernel times (CUDA events on the launching stream, same steps)
-    pass_ms = time_passes(opt, args, world, device, stream)
+    pass_ms, extra_ms = time_passes(opt, args, world, device, stream)
     if pass_ms:
         dom = max(pass_ms, key=pass_ms.get)
         dom_ms = max_over_ranks(pass_ms[dom], world, device)
@@ -339,32 +532,42 @@ def b200_arm(args, world, rank, local):
     if not args.skip_e2e:
         e2e = time_e2e(opt, params, grads_dev, args, world, device, stream, n_total, bpe)
 
-    # ---- CPU baseline (rank 0, N = 1)
+    # ---- the other BASELINE configs on one GPU (default run only)
+    per_config = None
+    if world == 1 and args.workload == "c5" and not args.skip_configs:
+        del opt, params, grads_dev
+        torch.cuda.empty_cache()
+        per_config = {name: quick_config(name, args, device, stream) for name in ("c1", "c2", "c3", "c4", "c4s")}
+
+    # ---- CPU baseline (rank 0, N = 1): the reference PyTorch CPU path on a bounded sample
     cpu = None
     if world == 1 and not args.skip_cpu:
-        sample = (1024, 4096)
-        sec, n, threads, done = cpu_reference_steps(sample, kw, istd, 2, 1, budget_s=30.0)
-        cpu = {"value": BYTES_PER_ELEM * n / sec / 1e9, "unit": "GB/s", "cores": threads, "kind": "port",
-               "sample": f"one {sample} tensor of {args.workload}, {done} steps after 1 warm-up, "
-                         f"reference PyTorch CPU path (oracle restatement)"}
+        cshapes, ckw, cistd, what = reference_sample(args.workload)
+        sec, n, threads, done, kind = cpu_reference_steps(cshapes, ckw, cistd, 2, 1, budget_s=30.0,
+                                                          row_scale=args.workload == "c2")
+        cpu = {"value": BYTES_PER_ELEM * n / sec / 1e9, "unit": "GB/s", "cores": threads, "kind": kind,
+               "cpu": cpu_model(),
+               "sample": f"{what}, {done} steps after 1 warm-up, "
+                         + ("reference cresso_v5.CRESSO5(cuda_ops='off') from baseline/_ref" if kind == "reference"
+                            else "oracle restatement of the reference PyTorch CPU path")}
 
     if rank == 0:
+        config = workload_config(args.workload, shapes, kw, args.dtype)
+        config.update({
+            "sharding": ((f"ZeRO-1 over {world} GPU(s), {len(opt.buckets)} buckets of >= "
+                          f"{args.bucket_elements} elements, all-gather of bucket k under the compute of "
+                          f"bucket k + 1" if args.bucket_elements > 0 else
+                          f"ZeRO-1 over {world} GPU(s), one all-gather after the step") if zero else
+                         f"row-sharded over {world} GPU(s)" if world > 1 else "single GPU"),
+            "per_pass_ms": {k: round(v, 4) for k, v in pass_ms.items()},
+            "param_dtype": args.dtype, "bytes_per_element": bpe})
+        if extra_ms:
+            config.update({k: round(v, 4) for k, v in extra_ms.items()})
         line = {
             "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "f64" if args.dtype == "f64" else "f32", "data": "synthetic",
-            "config": {"workload": f"{args.workload}: " + (f"7B-shaped {args.dtype} set, 290 tensors, 6,738,411,520 elements"
-                                                            if args.workload == "c5" else str(shapes[0])),
-                       "rank": kw["rank"], "hash_bins": kw["hash_bins"], "hash_tables": kw["hash_tables"],
-                       "sharding": ((f"ZeRO-1 over {world} GPU(s), {len(opt.buckets)} buckets of >= "
-                                     f"{args.bucket_elements} elements, all-gather of bucket k under the compute of "
-                                     f"bucket k + 1" if args.bucket_elements > 0 else
-                                     f"ZeRO-1 over {world} GPU(s), one all-gather after the step") if zero else
-                                    f"row-sharded over {world} GPU(s)" if world > 1 else "single GPU"),
-                       "l2": "no flush: inputs of every step (grads + params) exceed the 126 MB L2"
-                             if n_total * 8 > 2 * 126e6 else "inputs fit in L2",
-                       "elements": n_total, "per_pass_ms": {k: round(v, 4) for k, v in pass_ms.items()},
-                       "param_dtype": args.dtype, "bytes_per_element": bpe},
+            "config": config,
             "roofline": {"bound": "hbm", "kernel": dom, "achieved": achieved, "peak": peaks["hbm_gbs"],
                          "unit": "GB/s", "frac": achieved / peaks["hbm_gbs"], "traffic": traffic,
                          "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
@@ -376,19 +579,26 @@ def b200_arm(args, world, rank, local):
             "e2e": e2e,
             "cpu_baseline": cpu,
         }
+        if per_config is not None:
+            line["per_config"] = per_config
+        if parity is not None:
+            line["parity"] = parity
         print(json.dumps(line), flush=True)
 
 
 def time_passes(opt, args, world, device, stream):
-    """Runs min(K, 3) more steps stage by stage with events around the five pass kernels."""
+    """Runs min(K, 3) more steps stage by stage with events around the five pass
+    kernels, the reduce / finalize stages between them, and (row sharding) the
+    all-reduces of the reduction vectors.  Returns (per-pass ms, other ms)."""
     from cresso_b200 import _lib
     import torch.distributed as dist
 
     from cresso_b200.distributed import RowShardedCRESSO5
 
-    exchange = isinstance(opt, RowShardedCRESSO5)  # row sharding all-reduces between passes
+    exchange = isinstance(opt, RowShardedCRESSO5) and world > 1  # row sharding all-reduces between passes
     acc = {k: 0.0 for k in PASS_STAGE}
     acc["SCALAR"] = 0.0
+    other = {"reduce_finalize_ms": 0.0, "exchange_ms": 0.0}
     reps = max(1, min(args.steps, 3))
     orig = opt._spectral_stages
     orig_scalar = opt._run_scalar
@@ -400,22 +610,23 @@ def time_passes(opt, args, world, device, stream):
         ev1.record(stream)
         events.append(("SCALAR", ev0, ev1))
 
+    def timed(name, fn):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        fn()
+        b.record(stream)
+        events.append((name, a, b))
+
     def instrumented(run, scratch, layout):
         bounds = set(_lib.REDUCTION_BOUNDARIES)
         k = 0
         for st in range(_lib.SPECTRAL_STAGES):
             name = next((n for n, s in PASS_STAGE.items() if s == st), None)
-            if name is not None:
-                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-                a.record(stream)
-                run(st, st + 1)
-                b.record(stream)
-                events.append((name, a, b))
-            else:
-                run(st, st + 1)
-            if st + 1 in bounds and world > 1 and exchange:
+            timed(name if name is not None else "reduce_finalize_ms", lambda st=st: run(st, st + 1))
+            if st + 1 in bounds and exchange:
                 k += 1
-                dist.all_reduce(opt._reduction_view(scratch, layout, k))
+                view = opt._reduction_view(scratch, layout, k)
+                timed("exchange_ms", lambda view=view: dist.all_reduce(view, group=opt.process_group))
 
     opt._spectral_stages = instrumented
     opt._run_scalar = scalar_timed
@@ -425,11 +636,15 @@ def time_passes(opt, args, world, device, stream):
             opt.step()
             torch.cuda.synchronize(device)
             for name, a, b in events:
-                acc[name] += a.elapsed_time(b)
+                if name in other:
+                    other[name] += a.elapsed_time(b)
+                else:
+                    acc[name] += a.elapsed_time(b)
     finally:
         opt._spectral_stages = orig
         opt._run_scalar = orig_scalar
-    return {k: v / reps for k, v in acc.items() if v > 0.0}
+    extra = {k: max_over_ranks(v / reps, world, device) for k, v in other.items() if v > 0.0}
+    return {k: v / reps for k, v in acc.items() if v > 0.0}, extra
 
 
 def time_e2e(opt, params, grads_dev, args, world, device, stream, n_total, bpe=BYTES_PER_ELEM):
@@ -513,6 +728,7 @@ def main():
     ap.add_argument("--dtype", choices=["f32", "bf16", "f16", "f64"], default="f32",
                     help="parameter / gradient type (work and state: float64 for f64, else float32)")
     ap.add_argument("--skip-cpu", action="store_true")
+    ap.add_argument("--skip-configs", action="store_true", help="default c5 run: leave out the c1-c4 lines")
     ap.add_argument("--sharding", choices=["row", "zero"], default="row",
                     help="N > 1: row sharding (default) or ZeRO-1 whole-tensor partition")
     ap.add_argument("--bucket-elements", type=int, default=0,

@@ -51,6 +51,9 @@ DESC_INDEX = {name: i for i, name in enumerate(DESC_FIELDS)}
 DESC_WORDS = len(DESC_FIELDS)
 
 STATUS = {0: "ok", 1: "invalid argument", 2: "unsupported on the CUDA path", 3: "CUDA error", 4: "scratch too small"}
+# failure bits of the device status word of cresso_spectral_run_status
+DEVICE_STATUS = {1: "a bounded wait inside a spectral pass kernel gave up (that step's results and state are invalid)",
+                 2: "tensor-core work was still in flight when a block gave up (later steps are not to be trusted)"}
 
 EXPORTS = (
     "cresso_version", "cresso_arch", "cresso_last_error", "cresso_abi_layout", "cresso_launch_count",
@@ -60,7 +63,7 @@ EXPORTS = (
     "cresso_spectral_layout", "cresso_spectral_run", "cresso_scalar_scratch_bytes", "cresso_scalar_run",
     "cresso_scalar_run_noalloc", "cresso_micro_scratch_bytes", "cresso_micro_run", "cresso_selftest_bounded_wait",
     "cresso_shape_workspace64_bytes", "cresso_shape_workspace64_init", "cresso_spectral64_scratch_bytes",
-    "cresso_spectral64_run",
+    "cresso_spectral64_run", "cresso_spectral_run_status",
 )
 
 _lock = threading.Lock()
@@ -92,6 +95,7 @@ def _declare(lib) -> None:
         "cresso_instant_axis_metric": (ctypes.c_int, [_p, _i64, _pi64, _dbl, _dbl, _dbl, _p, _p]),
         "cresso_spectral_layout": (ctypes.c_int, [_p, _i64, _p, _i64, _pi64, _i64]),
         "cresso_spectral_run": (ctypes.c_int, [_p, _i64, _p, _p, _i64, _i64, _i64, _i64, _p]),
+        "cresso_spectral_run_status": (ctypes.c_int, [_p, _i64, _p, _p, _i64, _i64, _i64, _i64, _p, _p]),
         "cresso_scalar_scratch_bytes": (ctypes.c_int, [_p, _i64, _pi64]),
         "cresso_scalar_run": (ctypes.c_int, [_p, _i64, _p, _p, _i64, _p]),
         "cresso_scalar_run_noalloc": (ctypes.c_int, [_p, _i64, _p, _p]),

@@ -18,7 +18,6 @@
 #include <cooperative_groups.h>
 
 #include <algorithm>
-#include <mutex>
 #include <vector>
 
 #include "cresso_common.cuh"
@@ -1031,24 +1030,18 @@ int cresso_scalar_run(const cresso_tensor_desc* descs, int64_t n, const cresso_h
 // ---------------------------------------------------------------------------
 static __device__ __align__(256) unsigned char g_noalloc_scratch[CRESSO_NOALLOC_SCRATCH_BYTES];
 
-static std::mutex g_noalloc_mutex;
-static void* g_noalloc_addr[256] = {nullptr};  // device address of the array, per device ordinal
-
-// Device address of g_noalloc_scratch on the current device.  In host code the
-// array's name is only a host-side stand-in, so the address is looked up once
-// per device with cudaGetSymbolAddress (with that device current) and cached.
+// Device address of g_noalloc_scratch in the current device's current context.
+// In host code the array's name is only a host-side stand-in, so the address is
+// asked of the runtime (cudaGetSymbolAddress, with the target device current)
+// on every call: a cached address would go stale after cudaDeviceReset or when
+// an FFI host drives the device through a context of its own, and the lookup is
+// cheap next to the launch.  The first lookup on a device loads the library's
+// module there.
 static int noalloc_scratch_address(void** out) {
-    int dev = -1;
-    CRESSO_CUDA(cudaGetDevice(&dev));
-    CRESSO_REQUIRE(dev >= 0 && dev < 256, CRESSO_EUNSUPPORTED, "scalar_run_noalloc: device ordinal %d out of range", dev);
-    std::lock_guard<std::mutex> lock(g_noalloc_mutex);
-    if (g_noalloc_addr[dev] == nullptr) {
-        void* ptr = nullptr;
-        CRESSO_CUDA(cudaGetSymbolAddress(&ptr, g_noalloc_scratch));
-        CRESSO_REQUIRE(ptr != nullptr, CRESSO_ECUDA, "scalar_run_noalloc: cudaGetSymbolAddress returned NULL");
-        g_noalloc_addr[dev] = ptr;
-    }
-    *out = g_noalloc_addr[dev];
+    void* ptr = nullptr;
+    CRESSO_CUDA(cudaGetSymbolAddress(&ptr, g_noalloc_scratch));
+    CRESSO_REQUIRE(ptr != nullptr, CRESSO_ECUDA, "scalar_run_noalloc: cudaGetSymbolAddress returned NULL");
+    *out = ptr;
     return CRESSO_OK;
 }
 

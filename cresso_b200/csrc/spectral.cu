@@ -76,7 +76,8 @@ struct TensorConsts {
 // item list; only P5 differs between classes 0 and 2.
 struct GroupHdr {
     int64_t n_tensors, n_items, rm, bins, tables, tb, iters, idx_bytes, rb_max;
-    int32_t* status;                  // device word: nonzero when a bounded wait gave up
+    int32_t* status;                  // device word, OR of failure bits (1: a bounded wait gave up,
+                                      // 2: products still in flight when the block freed its TMEM)
     int64_t cls_items[3], cls_nt[3];  // items and tensors of each class
     int64_t grid[3][6];               // blocks of pass 1..5 per class (index 0 unused)
     double hp[64];                    // cresso_hparams
@@ -721,7 +722,7 @@ spectral_pass_kernel(const GroupHdr* __restrict__ hdr, const DevTensor* __restri
             // TCR: this item's two reconstructions are in D buffer tcb (read per row group below)
             if constexpr (TCR) {
                 if (*s_tcflag) {  // a product never completed: stop this block (uniform after the barrier)
-                    if (tid == 0) atomicExch(hdr->status, 1);
+                    if (tid == 0) atomicOr(hdr->status, 1);
                     tc_abort = true;
                     break;
                 }
@@ -1085,7 +1086,11 @@ spectral_pass_kernel(const GroupHdr* __restrict__ hdr, const DevTensor* __restri
     }
     if constexpr (TCR) {
         cp_async_wait<0>();
-        if (tc_abort && tid == 0) mbar_wait_bounded(smem_u32(s_tcbar), tc_parity ^ 1, kTcWaitNs);
+        // after a give-up, the products of the next item may still be in flight: wait for
+        // them (bounded) before the TMEM is freed, and record bit 2 if they never completed
+        // (the tensor core may then still write TMEM that another block can claim)
+        if (tc_abort && tid == 0 && !mbar_wait_bounded(smem_u32(s_tcbar), tc_parity ^ 1, kTcWaitNs))
+            atomicOr(hdr->status, 2);
         tc_fence_before();
         __syncthreads();
         if (warp == 0) {
@@ -2084,6 +2089,15 @@ int cresso_selftest_bounded_wait(int64_t limit_ns, int64_t arrive, void* status_
 int cresso_spectral_run(const cresso_tensor_desc* descs, int64_t n, const cresso_hparams* hp, void* scratch,
                         int64_t scratch_bytes, int64_t stage_begin, int64_t stage_end, int64_t num_sms,
                         cresso_stream_t stream) {
+    return cresso_spectral_run_status(descs, n, hp, scratch, scratch_bytes, stage_begin, stage_end, num_sms, nullptr,
+                                      stream);
+}
+
+int cresso_spectral_run_status(const cresso_tensor_desc* descs, int64_t n, const cresso_hparams* hp, void* scratch,
+                               int64_t scratch_bytes, int64_t stage_begin, int64_t stage_end, int64_t num_sms,
+                               void* status_word, cresso_stream_t stream) {
+    CRESSO_REQUIRE(status_word == nullptr || ((uintptr_t)status_word & 3) == 0, CRESSO_EINVAL,
+                   "spectral_run: status word not 4-byte aligned");
     Plan P;
     int st = build_plan(descs, n, hp, num_sms, P);
     if (st) return st;
@@ -2097,7 +2111,9 @@ int cresso_spectral_run(const cresso_tensor_desc* descs, int64_t n, const cresso
     NvtxRange range("cresso_spectral_run %lld tensors, stages [%lld, %lld)", (long long)n, (long long)stage_begin,
                     (long long)stage_end);
     bind_scratch(P, base);
-    P.hdr.status = reinterpret_cast<int32_t*>(base + P.off_status);
+    // failure bits go to the caller's word (never cleared here) or to the scratch word,
+    // which stage 0 clears
+    P.hdr.status = status_word ? reinterpret_cast<int32_t*>(status_word) : reinterpret_cast<int32_t*>(base + P.off_status);
     if (stage_begin == 0) {
         const int32_t zero = 0;
         int ust = upload_async(base + P.off_status, &zero, sizeof(zero), s);

@@ -71,12 +71,38 @@ def lpt_partition(sizes: Sequence[int], world: int) -> List[int]:
     return owner
 
 
+def exchange_status(opt: CRESSO5, group=None) -> None:
+    """Spreads a device-side failure report of any rank to every rank: the failure
+    words are MAX-all-reduced once per step (every rank takes this collective in
+    every step, so it cannot unbalance the collective order) and the host copies
+    re-queued, so all ranks raise together at a later step().  The words only
+    take the values 0, 1 and 3 (bit 2 is only ever set with bit 1), so MAX is
+    their union."""
+    if not dist.is_available() or not dist.is_initialized() or dist.get_world_size(group) == 1:
+        return
+    if dist.get_backend(group) == "nccl":
+        device = torch.device("cuda", torch.cuda.current_device())
+    else:
+        device = torch.device("cpu")
+    word = opt._status_word(device)
+    dist.all_reduce(word, op=dist.ReduceOp.MAX, group=group)
+    opt._publish_status([device])
+
+
 class RowShardedCRESSO5(CRESSO5):
     """CRESSO5 over row-sharded tensors with one float64 all-reduce per pass."""
 
     def __init__(self, params: Iterable[Tensor], process_group=None, **kwargs):
         super().__init__(params, **kwargs)
         self.process_group = process_group
+
+    @torch.no_grad()
+    def step(self, closure=None):  # type: ignore[override]
+        loss = super().step(closure)
+        # a rank whose kernel gave up fed partial sums into the exchange, which spoils
+        # every rank's state: every rank learns of it
+        exchange_status(self, self.process_group)
+        return loss
 
     def _world(self) -> int:
         if not dist.is_available() or not dist.is_initialized():
@@ -170,6 +196,7 @@ class ZeroCRESSO5(CRESSO5):
                 pending = started
         for item in pending:
             self._finish_gather(item)
+        exchange_status(self, self.process_group)
         return loss
 
     def _gather_bucket_async(self, bucket: List[List[Tensor]]) -> list:

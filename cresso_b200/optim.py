@@ -210,7 +210,11 @@ class CRESSO5(Optimizer):
         self._shape_ws: Dict[tuple, Tensor] = {}
         self._hash_cache: Dict[tuple, Tuple[Tensor, int]] = {}
         self._scratch: Dict[tuple, Tensor] = {}
-        self._status_words: Dict[object, Tensor] = {}
+        # device-side failure reports: per device an int32 word that the spectral kernels OR
+        # failure bits into (never cleared), and a pinned host copy of it taken after every
+        # step, read without synchronising at the start of the next step
+        self._status_dev: Dict[object, Tensor] = {}
+        self._status_host: Dict[object, tuple] = {}
         # host-side caches for groups of many small tensors (LoRA adapters): the route of
         # each (shape, shard, routing settings), and per device the scalar-route descriptor
         # table of the last step with the identities it was built from
@@ -378,6 +382,8 @@ class CRESSO5(Optimizer):
         if closure is not None:
             with torch.enable_grad():
                 loss = closure()
+        self.check_device_status(block=False)
+        spectral_devices = set()
         for gi, group in enumerate(self.param_groups):
             route_sig = (group["min_spectral_size"], group["rank"], group.get("thin_matrix_route", "scalar"),
                          group.get("thin_matrix_max_width", 64), group.get("thin_matrix_min_aspect", 4.0),
@@ -390,6 +396,7 @@ class CRESSO5(Optimizer):
             for device, items in spectral.items():
                 hp = _lib.pack_hparams(group) if hp is None else hp
                 self._run_spectral(group, hp, device, items)
+                spectral_devices.add(device)
             for device, items in scalar.items():
                 hp = _lib.pack_hparams(group) if hp is None else hp
                 self._run_scalar(hp, device, items)
@@ -399,7 +406,52 @@ class CRESSO5(Optimizer):
             for device, items in spectral64.items():
                 hp = _lib.pack_hparams(group) if hp is None else hp
                 self._run_spectral64(group, hp, device, items)
+        self._publish_status(spectral_devices)
         return loss
+
+    # ------------------------------------------------------- failure reports
+    def _status_word(self, device) -> Tensor:
+        """The device's int32 failure word (zeroed once, never cleared afterwards)."""
+        w = self._status_dev.get(device)
+        if w is None:
+            w = self._status_dev[device] = torch.zeros(1, dtype=torch.int32, device=device)
+        return w
+
+    def _publish_status(self, devices) -> None:
+        """Queues, after this step's work on each device, a copy of its failure word
+        into pinned host memory; check_device_status reads it."""
+        for device in devices:
+            word = self._status_word(device)
+            if word.device.type != "cuda":  # host-side word (multi-process tests on CPU ranks)
+                self._status_host[device] = (word.clone(), None)
+                continue
+            entry = self._status_host.get(device)
+            if entry is None:
+                entry = self._status_host[device] = (torch.zeros(1, dtype=torch.int32, pin_memory=True),
+                                                     torch.cuda.Event())
+            host, ev = entry
+            host.copy_(word, non_blocking=True)
+            ev.record(torch.cuda.current_stream(device))
+
+    def check_device_status(self, block: bool = True) -> None:
+        """Raises RuntimeError if a spectral kernel of an earlier step reported a
+        device-side failure: a bounded wait inside a pass kernel that gave up (the
+        results and state of that step are invalid; bit 1), or tensor-core work still
+        in flight after such a give-up (later steps are not to be trusted either;
+        bit 2).  step() calls it without blocking, so a failure surfaces at the first
+        step() after the failed step's copy of the word reached the host; with
+        block=True (the default) it waits for the last step's copy."""
+        for device, (host, ev) in self._status_host.items():
+            if ev is None:
+                pass
+            elif block:
+                ev.synchronize()
+            elif not ev.query():
+                continue
+            v = int(host[0])
+            if v:
+                what = "; ".join(msg for bit, msg in _lib.DEVICE_STATUS.items() if v & bit)
+                raise RuntimeError(f"CRESSO5 device failure on {device} (status {v}): {what}")
 
     def _route_fast(self, gi: int, group: dict, route_sig: tuple):
         """The routing of the group's last full pass, reused when nothing it depends on
@@ -580,12 +632,13 @@ class CRESSO5(Optimizer):
         _lib.check(L.cresso_spectral_layout(_lib.ptr(descs), n, _lib.ptr(hp), num_sms,
                                             layout.ctypes.data_as(_lib._pi64), 10), "spectral_layout")
         scratch = self._scratch_buffer(device, "spectral", int(layout[0]))
-        self._status_words[device] = scratch[int(layout[9]):int(layout[9]) + 4].view(torch.int32)
+        status = self._status_word(device)
         stream = torch.cuda.current_stream(device).cuda_stream
 
         def run(begin: int, end: int) -> None:
-            _lib.check(L.cresso_spectral_run(_lib.ptr(descs), n, _lib.ptr(hp), _lib.ptr(scratch), scratch.numel(),
-                                             begin, end, num_sms, stream), "spectral_run")
+            _lib.check(L.cresso_spectral_run_status(_lib.ptr(descs), n, _lib.ptr(hp), _lib.ptr(scratch),
+                                                    scratch.numel(), begin, end, num_sms, _lib.ptr(status), stream),
+                       "spectral_run")
 
         self._spectral_stages(run, scratch, layout)
 
@@ -625,9 +678,12 @@ class CRESSO5(Optimizer):
                                            scratch.numel(), stream), "spectral64_run")
 
     def _device_status(self) -> int:
-        """Status word of the last spectral step on each device (synchronises):
-        nonzero when a bounded wait inside a kernel gave up."""
-        return max((int(w.item()) for w in self._status_words.values()), default=0)
+        """OR of the failure words of every device (synchronises); 0 when no bounded
+        wait inside a kernel gave up in any step so far."""
+        v = 0
+        for w in self._status_dev.values():
+            v |= int(w.item())
+        return v
 
     def _spectral_stages(self, run: Callable[[int, int], None], scratch: Tensor, layout: np.ndarray) -> None:
         """Runs the kernel stages of a group step; one GPU needs no exchange."""

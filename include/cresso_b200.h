@@ -213,6 +213,21 @@ CRESSO_API int cresso_spectral_layout(const cresso_tensor_desc* descs, int64_t n
 CRESSO_API int cresso_spectral_run(const cresso_tensor_desc* descs, int64_t n, const cresso_hparams* hp, void* scratch,
                         int64_t scratch_bytes, int64_t stage_begin, int64_t stage_end, int64_t num_sms,
                         cresso_stream_t stream);
+/* cresso_spectral_run reporting device-side failures into a caller-owned
+ * int32 device word (no counterpart in the reference, whose kernels have no
+ * in-kernel waits).  Kernels OR failure bits into *status_word and nothing
+ * in the library clears it: bit 0 (1) = a bounded wait inside a pass kernel
+ * gave up and that group's results and state of this step are invalid; bit 1
+ * (2) = after such a give-up the in-flight tensor-core work did not finish
+ * within its bound either, so later steps in this process are not to be
+ * trusted.  The caller zeroes the word once, keeps it across steps and groups,
+ * and reads it asynchronously (e.g. copied to pinned host memory after the
+ * step).  status_word = NULL is cresso_spectral_run (the scratch word of
+ * layout[9], cleared by stage 0). */
+CRESSO_API int cresso_spectral_run_status(const cresso_tensor_desc* descs, int64_t n, const cresso_hparams* hp,
+                                          void* scratch, int64_t scratch_bytes, int64_t stage_begin,
+                                          int64_t stage_end, int64_t num_sms, void* status_word,
+                                          cresso_stream_t stream);
 
 /* Float64 parameters on the spectral route (cresso_v5.py:945-1353 with the
  * float64 work and state of cresso_v5.py:119-124).  The shape workspace holds
@@ -266,9 +281,10 @@ CRESSO_API int cresso_micro_run(const cresso_tensor_desc* descs, int64_t n, cons
  * CRESSO_NOALLOC_SCRATCH_BYTES that every GPU loading the library holds until
  * the process exits.  Tensor lists whose scratch (cresso_scalar_scratch_bytes)
  * exceeds that size are rejected with CRESSO_ESCRATCH: split them over several
- * calls.  The first call on a device looks up the array's device address
- * (with that device current) and caches it; make that first call before any
- * stream capture.  All calls share the one array, so calls that may overlap
+ * calls.  Every call looks up the array's device address in the current
+ * context (cudaGetSymbolAddress, with the target device current); the first
+ * call on a device also loads the library's module there, so make that first
+ * call before any stream capture.  All calls share the one array, so calls that may overlap
  * on the GPU (other streams, other host threads, same device) race: order
  * them on one stream or serialise them. */
 CRESSO_API int cresso_scalar_run_noalloc(const cresso_tensor_desc* descs, int64_t n, const cresso_hparams* hp,

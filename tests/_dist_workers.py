@@ -201,3 +201,27 @@ def zero_consolidate_worker(rank, world, port, outdir):
     sd = opt.consolidate_state_dict(to=0)
     torch.save({"sd": sd, "owner": [opt.owner[p] for p in ps]}, os.path.join(outdir, f"consolidate_{rank}.pt"))
     dist.destroy_process_group()
+
+
+def status_exchange_worker(rank, world, port, outdir):
+    """A device-side failure reported on rank 1 only reaches every rank after the
+    per-step status exchange, and every rank's next check raises (gloo; the
+    failure word is a host tensor here, set as a kernel would set it)."""
+    from cresso_b200.distributed import RowShardedCRESSO5, exchange_status
+
+    _init(rank, world, port, "gloo")
+    opt = RowShardedCRESSO5([torch.nn.Parameter(torch.zeros(4))])
+    word = opt._status_word(torch.device("cpu"))
+    if rank == 1:
+        word.fill_(1)  # as the kernels OR bit 1 in after a bounded wait gave up
+    before = int(word.item())
+    exchange_status(opt)
+    after = int(word.item())
+    raised = ""
+    try:
+        opt.check_device_status()
+    except RuntimeError as exc:
+        raised = str(exc)[:300]
+    with open(os.path.join(outdir, f"status_{rank}.txt"), "w") as f:
+        f.write(f"{before}\n{after}\n{raised}\n")
+    dist.destroy_process_group()

@@ -43,6 +43,15 @@ def test_lpt_partition_is_balanced_and_deterministic():
     assert load.max() / load.mean() < 1.02
 
 
+def test_device_failure_report_reaches_every_rank_gloo(tmp_path):
+    spawn(W.status_exchange_worker, 2, tmp_path)
+    rows = [(tmp_path / f"status_{r}.txt").read_text().splitlines() for r in range(2)]
+    assert [int(r[0]) for r in rows] == [0, 1]  # only rank 1 saw the failure itself
+    for r in rows:
+        assert int(r[1]) == 1  # after the exchange every rank holds it
+        assert "bounded wait" in r[2]  # and every rank's check raises
+
+
 def test_row_sharded_stage_orchestration_gloo(tmp_path):
     spawn(W.stages_worker, 2, tmp_path)
     r0 = torch.load(tmp_path / "stages_0.pt")

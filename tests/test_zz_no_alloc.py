@@ -6,9 +6,10 @@ reserved at start-up that forbids raw cudaMalloc later), or they are thin FFI
 hosts with no device allocator of their own.  For them the library offers one
 entry point whose scratch is a built-in device array instead of caller memory.
 This test drives it through the C ABI and checks it against the regular entry
-point (cresso_scalar_run with caller scratch) on two consecutive steps, with
-the parameter tolerance the other parity tests use (relative RMS <= 1e-6 here;
-both calls run the same kernel, so the results agree bit for bit in practice).
+point (cresso_scalar_run with caller scratch) on two consecutive steps
+(relative RMS <= 1e-6 here; both calls run the same kernel, so the results
+agree bit for bit in practice), and the result against the oracle with the
+parameter tolerance of the other parity tests (relative RMS <= 1e-5).
 The file is named so that pytest collects it last.
 """
 
@@ -77,6 +78,19 @@ def test_noalloc_entry_matches_regular_entry_on_two_steps():
         for sa, sb in zip(s_na, s_reg):
             for k in sa:
                 assert abs(float(sa[k]) - float(sb[k])) <= 1e-6 * max(abs(float(sb[k])), 1e-6), (step, k)
+    # and against the oracle (the reference's PyTorch scalar route restated), so that a
+    # defect shared by both entry points through their common launch would not pass
+    from oracle.cresso5_oracle import OracleCRESSO5
+    refs = [torch.nn.Parameter(x.clone()) for x in inits]
+    opt = OracleCRESSO5(refs, rank=4, weight_decay=0.01)
+    for gs in grads:
+        for r, g in zip(refs, gs):
+            r.grad = g.cpu()
+        opt.step()
+    for a, r in zip(p_na, refs):
+        rel = float((a.cpu().double() - r.detach().double()).pow(2).mean().sqrt()
+                    / r.detach().double().pow(2).mean().sqrt())
+        assert rel <= 1e-5, rel
 
 
 def test_noalloc_entry_rejects_lists_beyond_its_array():
