@@ -295,6 +295,68 @@ def reference_arm(args, world, rank):
     print(json.dumps(line), flush=True)
 
 
+def reference_cuda_arm(args, world, rank):
+    """The reference's own CUDA extension on one GPU: the unmodified package in
+    baseline/_ref, its stock JIT loader (cresso_cuda_ext.load_cuda_ops, built for
+    sm_100 with TORCH_CUDA_ARCH_LIST=10.0, which its arch check accepts) and
+    cresso_v5.CRESSO5(cuda_ops='required'), timed with CUDA events on the same
+    BASELINE inputs, config by config.  Prints one JSON line with ms/step per
+    config (c5: a few steps, its reference step takes seconds)."""
+    if rank != 0:
+        return
+    os.environ["TORCH_CUDA_ARCH_LIST"] = "10.0"
+    os.environ.setdefault("CRESSO_CUDA_BUILD_ROOT", str(ROOT / "baseline" / "_ref_build"))
+    os.environ.setdefault("CRESSO_CUDA_MAX_JOBS", str(min(16, os.cpu_count() or 1)))
+    if not (REF_DIR / "cresso_v5.py").exists():
+        print(json.dumps({"impl": "reference-cuda", "unavailable": "reference not installed into baseline/_ref"}))
+        return
+    if str(REF_DIR) not in sys.path:
+        sys.path.insert(0, str(REF_DIR))
+    import cresso_v5
+
+    device = torch.device("cuda", 0)
+    t0 = time.perf_counter()
+    cresso_v5._load_cuda_ops(required=True)
+    build_s = time.perf_counter() - t0
+    stream = torch.cuda.current_stream(device)
+    out = {}
+    names = [w.strip() for w in args.ref_configs.split(",") if w.strip()]
+    for name in names:
+        shapes, kw, istd = workload_shapes(name)
+        g = torch.Generator(device=device).manual_seed(1234)
+        ps = []
+        for shp in shapes:
+            p = torch.nn.Parameter(torch.empty(shp, device=device).normal_(0.0, istd, generator=g))
+            gr = torch.empty(shp, device=device).normal_(0.0, 1e-3, generator=g)
+            if name == "c2":
+                gr.mul_(torch.exp(0.5 * torch.empty((shp[0], 1), device=device).normal_(0.0, 1.0, generator=g)))
+            p.grad = gr
+            ps.append(p)
+        opt = cresso_v5.CRESSO5(ps, cuda_ops="required", **kw)
+        steps, warm = (2, 1) if name == "c5" else (args.steps, args.warmup)
+        for _ in range(warm):
+            opt.step()
+        torch.cuda.synchronize(device)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(steps):
+            opt.step()
+        e1.record(stream)
+        torch.cuda.synchronize(device)
+        ms = e0.elapsed_time(e1) / steps
+        n = sum(numel(x) for x in shapes)
+        out[name] = {"ms_per_step": round(ms, 4), "value": round(BYTES_PER_ELEM * n / (ms * 1e-3) / 1e9, 3),
+                     "unit": "GB/s", "steps": steps, "warmup": warm}
+        print(json.dumps({"reference_cuda": name, **out[name]}), file=sys.stderr, flush=True)
+        del opt, ps
+        torch.cuda.empty_cache()
+    line = {"impl": "reference-cuda", "metric": METRIC, "per_config": out, "n_gpus": 1,
+            "path": "reference cresso_v5.CRESSO5(cuda_ops='required') from baseline/_ref, its JIT-built CUDA "
+                    "extension (cresso_cuda_ext.load_cuda_ops) for sm_100",
+            "build_or_load_s": round(build_s, 1), "torch_cuda_arch_list": os.environ["TORCH_CUDA_ARCH_LIST"]}
+    print(json.dumps(line), flush=True)
+
+
 def shapes_of(workload):
     return workload_shapes(workload)[0]
 
@@ -722,7 +784,9 @@ def main():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
-    ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
+    ap.add_argument("--impl", choices=["b200", "reference", "reference-cuda"], default="b200")
+    ap.add_argument("--ref-configs", default="c1,c2,c3,c4,c4s,c5",
+                    help="--impl reference-cuda: the BASELINE configs to time")
     ap.add_argument("--workload", default="c5")
     ap.add_argument("--skip-e2e", action="store_true")
     ap.add_argument("--dtype", choices=["f32", "bf16", "f16", "f64"], default="f32",
@@ -738,6 +802,8 @@ def main():
     try:
         if args.impl == "reference":
             reference_arm(args, world, rank)
+        elif args.impl == "reference-cuda":
+            reference_cuda_arm(args, world, rank)
         else:
             b200_arm(args, world, rank, local)
     finally:
