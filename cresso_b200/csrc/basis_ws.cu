@@ -333,6 +333,13 @@ __global__ void hash_cache_kernel(int64_t n, int64_t bins, int64_t tables, IdxT*
         for (int64_t t = 0; t < tables; ++t) cache[t * n + i] = (IdxT)hash_bin(i, bins, t);
 }
 
+// Joint section of a two-table cache with at most 64 bins: j = b0 + 64 b1 per
+// flat index, one 16-bit load for both bins.
+__global__ void hash_joint_kernel(int64_t n, int64_t bins, uint16_t* joint) {
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+        joint[i] = (uint16_t)(hash_bin(i, bins, 0) + 64 * hash_bin(i, bins, 1));
+}
+
 // ---------------------------------------------------------------------------
 // Op-level kernels (single-block reductions: they back the op parity tests)
 // ---------------------------------------------------------------------------
@@ -619,6 +626,7 @@ int cresso_hash_cache_bytes(int64_t n, int64_t bins, int64_t tables, int64_t* by
     CRESSO_REQUIRE(n >= 0 && bins > 0 && bins <= 65536 && tables >= 1, CRESSO_EINVAL,
                    "hash_cache_bytes: need n >= 0, 1 <= bins <= 65536, tables >= 1");
     *bytes = align_up(n * tables * (bins <= 256 ? 1 : 2), 256);
+    if (tables == 2 && bins <= 64) *bytes += align_up(2 * n, 256);  // the joint section
     return CRESSO_OK;
 }
 
@@ -633,6 +641,11 @@ int cresso_hash_cache_init(int64_t n, int64_t bins, int64_t tables, void* cache,
     else
         hash_cache_kernel<uint16_t><<<blocks, kThreads, 0, (cudaStream_t)stream>>>(n, bins, tables, (uint16_t*)cache);
     CRESSO_LAUNCHED("hash_cache_kernel");
+    if (tables == 2 && bins <= 64) {
+        uint16_t* joint = reinterpret_cast<uint16_t*>((char*)cache + align_up(2 * n, 256));
+        hash_joint_kernel<<<blocks, kThreads, 0, (cudaStream_t)stream>>>(n, bins, joint);
+        CRESSO_LAUNCHED("hash_joint_kernel");
+    }
     return CRESSO_OK;
 }
 

@@ -1100,6 +1100,12 @@ spectral_pass_kernel(const GroupHdr* __restrict__ hdr, const DevTensor* __restri
     }
 }
 
+}  // namespace cresso
+
+#include "spectral_fast.cuh"
+
+namespace cresso {
+
 // ---------------------------------------------------------------------------
 // Reduce: fixed-order sums of block records into the reduction vectors
 // ---------------------------------------------------------------------------
@@ -1555,6 +1561,7 @@ struct Plan {
     int64_t n_rec_max;
     int64_t off_p32, half_elems;  // float32 copies of the 16-bit parameters
     int rm;
+    bool fast;  // class 0 runs P2-P5 on fast_pass_kernel
 };
 
 static size_t pass_smem(int pass, const GroupHdr& H, int64_t iters, bool tc = false);
@@ -1756,6 +1763,14 @@ static int build_plan(const cresso_tensor_desc* descs, int64_t n, const cresso_h
                        CRESSO_EINVAL, "tensor %lld: NULL state pointer", (long long)i);
     }
     H.n_items = items;
+    // the lean kernels of the full-tile class (spectral_fast.cuh): default hyper-parameters,
+    // two tables of <= 64 bins (joint cache section), rank pad 8, 16-row items, and every
+    // class-0 tensor with the hash and the axial instant metric on
+    P.fast = rm == 8 && tables == 2 && bins >= 1 && bins <= 64 && iters == 16 && hp->weight_decay == 0.0 &&
+             hp->local_sharpness == 0.0 && fmax(hp->instant_metric_power, 0.25) == 1.0;
+    for (int64_t i = 0; i < n; ++i)
+        if (full[i] && !(P.dts[i].flags & (F_F16 | F_BF16)))
+            P.fast = P.fast && (P.dts[i].flags & F_HASH) && (P.dts[i].flags & F_INST2D);
     // the three launch classes: item lists in tensor order within each class
     P.item_lists.clear();
     P.tensor_lists.clear();
@@ -1988,6 +2003,17 @@ static int launch_stage(int stage, const Plan& P, char* base, cudaStream_t s) {
                         int pass) -> int {
         for (int c = 0; c < 3; ++c) {
             if (P.hdr.grid[c][pass] == 0) continue;
+            if (c == 0 && P.fast && pass >= 2 && RM == 8 && NT == 2) {
+                size_t off[13];
+                size_t smem = fast_smem_layout(pass, (int)P.hdr.tb, off);
+                if (pass >= 3) smem = std::max<size_t>(smem, 78 * 1024);  // two blocks per SM at most (TMEM)
+                auto fk = pass == 2 ? fast_pass_kernel<2> : pass == 3 ? fast_pass_kernel<3>
+                                                          : pass == 4 ? fast_pass_kernel<4> : fast_pass_kernel<5>;
+                CRESSO_CUDA(cudaFuncSetAttribute(fk, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+                fk<<<(unsigned)P.hdr.grid[0][pass], kThreads, smem, s>>>(hdr, dts, items, tmap, recs, recb);
+                CRESSO_LAUNCHED("fast_pass_kernel");
+                continue;
+            }
             const bool tc = c != 1 && pass >= 3 && RM == 8 && P.hdr.iters == 16;
             const size_t smem = pass_smem(pass, P.hdr, P.hdr.iters, tc);
             auto kern = c == 1 ? kern_gen : (c == 0 ? (tc ? kern_tc : kern_full) : (tc ? kern_tc16 : kern_full16));

@@ -131,9 +131,12 @@ CRESSO_API int cresso_hash_gather(const float* values, int64_t bins, int64_t n, 
                        cresso_stream_t stream);
 
 /* Per-process bin-index cache for `tables` salted tables over flat indices
- * [0, n): uint8 per index when bins <= 256, else uint16.  Shared by every
- * tensor with the same (bins, tables).  Replaces the per-kernel hash
- * recomputation of the reference (cu:189-201 called from K11-K17). */
+ * [0, n): uint8 per index when bins <= 256, else uint16, table t at [t * n].
+ * With two tables of at most 64 bins a joint section follows at byte offset
+ * align_up(2 n, 256): one uint16 b0 + 64 b1 per index (read by the kernels of
+ * the full-tile tensor class).  Shared by every tensor with the same (bins,
+ * tables).  Replaces the per-kernel hash recomputation of the reference
+ * (cu:189-201 called from K11-K17). */
 CRESSO_API int cresso_hash_cache_bytes(int64_t n, int64_t bins, int64_t tables, int64_t* bytes);
 CRESSO_API int cresso_hash_cache_init(int64_t n, int64_t bins, int64_t tables, void* cache, cresso_stream_t stream);
 
