@@ -31,7 +31,11 @@ absent) on all host cores, on a bounded sample of the workload (c5: one
 unit and with the same `config`.
 
 The default run (c5, one GPU) adds `per_config`: c1, c2, c3, c4 and c4s (the
-840 thin tensors on thin_matrix_route="spectral") timed the same way.  With
+840 thin tensors on thin_matrix_route="spectral") timed the same way, and
+`ref_cuda`: the same configs stepped by the reference's own CUDA extension
+(`--impl reference-cuda` in a child process before this one allocates: the
+unmodified package in baseline/_ref, JIT-built by its stock loader for
+sm_100) with this build's speed-up over it per config.  With
 N > 1 row-sharded GPUs the run first checks the sharded step against the
 single-GPU step on this box (`parity` in the line; it exits non-zero above
 1e-6 relative RMS or if the ranks' states differ) and reports the time of the
@@ -525,10 +529,36 @@ def quick_config(name, args, device, stream):
     return out
 
 
+def reference_cuda_subprocess(timeout_s=600):
+    """The reference CUDA extension timed in a child process (its own CUDA context,
+    run before this process allocates the workload), per BASELINE config; None
+    fields name why it is missing."""
+    cmd = [sys.executable, str(ROOT / "bench.py"), "--impl", "reference-cuda", "--steps", "10", "--warmup", "3"]
+    env = dict(os.environ)
+    env.setdefault("CRESSO_CUDA_BUILD_ROOT", str(ROOT / "baseline" / "_ref_build"))
+    try:
+        r = subprocess.run(cmd, capture_output=True, text=True, timeout=timeout_s, env=env, cwd=str(ROOT))
+    except subprocess.TimeoutExpired:
+        return {"unavailable": f"reference CUDA build and timing exceeded {timeout_s} s"}
+    for ln in reversed(r.stdout.splitlines()):
+        try:
+            d = json.loads(ln)
+        except ValueError:
+            continue
+        if d.get("impl") == "reference-cuda":
+            return d
+    return {"unavailable": f"reference CUDA run failed (rc {r.returncode}): {r.stderr.strip()[-300:]}"}
+
+
 def b200_arm(args, world, rank, local):
     from cresso_b200 import _lib
     import cresso_b200
     from cresso_b200.distributed import RowShardedCRESSO5, ZeroCRESSO5
+
+    # ---- the reference's own CUDA extension on this GPU, before this process allocates (default run)
+    ref_cuda = None
+    if world == 1 and args.workload == "c5" and not args.skip_configs and not args.skip_ref_cuda:
+        ref_cuda = reference_cuda_subprocess()
 
     device = torch.device("cuda", local)
     zero = world > 1 and args.sharding == "zero"  # ZeRO-1: whole tensors, replicated inputs
@@ -643,6 +673,15 @@ def b200_arm(args, world, rank, local):
         }
         if per_config is not None:
             line["per_config"] = per_config
+        if ref_cuda is not None:
+            ours = dict(per_config or {})
+            ours["c5"] = {"ms_per_step": ms}
+            rc = {"path": ref_cuda.get("path"), "unavailable": ref_cuda.get("unavailable")}
+            for name, v in (ref_cuda.get("per_config") or {}).items():
+                mine = ours.get(name, {}).get("ms_per_step")
+                rc[name] = {"ms_per_step": v["ms_per_step"], "steps": v["steps"],
+                            "speedup": round(v["ms_per_step"] / mine, 2) if mine else None}
+            line["ref_cuda"] = rc
         if parity is not None:
             line["parity"] = parity
         print(json.dumps(line), flush=True)
@@ -793,6 +832,8 @@ def main():
                     help="parameter / gradient type (work and state: float64 for f64, else float32)")
     ap.add_argument("--skip-cpu", action="store_true")
     ap.add_argument("--skip-configs", action="store_true", help="default c5 run: leave out the c1-c4 lines")
+    ap.add_argument("--skip-ref-cuda", action="store_true",
+                    help="default c5 run: leave out the reference CUDA extension timings (ref_cuda)")
     ap.add_argument("--sharding", choices=["row", "zero"], default="row",
                     help="N > 1: row sharding (default) or ZeRO-1 whole-tensor partition")
     ap.add_argument("--bucket-elements", type=int, default=0,
