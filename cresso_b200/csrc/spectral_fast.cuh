@@ -72,6 +72,16 @@ __device__ __forceinline__ bool mbar_test(uint32_t bar, uint32_t parity) {
     return ok != 0;
 }
 
+// Bounded wait in two parts: one test inline (the common case: the phase is
+// complete), the polling loop out of line so that it costs the streaming
+// loop no registers.
+__device__ __noinline__ bool mbar_wait_slow(uint32_t bar, uint32_t parity, uint64_t limit_ns) {
+    return mbar_wait_bounded(bar, parity, limit_ns);
+}
+__device__ __forceinline__ bool mbar_wait_quick(uint32_t bar, uint32_t parity, uint64_t limit_ns) {
+    return mbar_test(bar, parity) || mbar_wait_slow(bar, parity, limit_ns);
+}
+
 __device__ __forceinline__ float ex2_approx(float x) {
     float r;
     asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
@@ -136,6 +146,11 @@ struct FastCfg {
     static constexpr bool kJoint = PASS >= 3;                            // joint lookup table in shared memory
     static constexpr bool kStore = PASS == 3 || PASS == 5;               // the tile goes back to HBM
     static constexpr int kCopies = PASS == 3 ? 8 : 16;                   // fixed-point bin copies
+    // P3 keeps a barrier at the top of every item (its shared memory has no room for a
+    // second set of bin copies); the other passes wait on the stage and product
+    // barriers thread by thread and synchronise the block once per item, at its end
+    static constexpr bool kTopBar = PASS == 3;
+    static constexpr int kBinSets = kBins && !kTopBar ? 2 : 1;           // bin copies alternate by item
     static constexpr int kAcc = PASS == 4 ? kWarps * 32 : (kBins ? 2 * kRM * kThreads : 0);
 };
 
@@ -147,20 +162,21 @@ __host__ __device__ inline size_t fast_smem_layout(int pass, int tb, size_t* off
     const size_t stage = (size_t)(xb + jb + rtb + pb);
     const bool bins = pass == 2 || pass == 3;
     const int copies = pass == 3 ? 8 : 16;
+    const int sets = pass == 2 ? 2 : 1;
     const size_t acc = pass == 4 ? kWarps * 32 : (bins ? 2 * 8 * kThreads : 0);
     size_t o = 0;
     off[0] = o; o += 2 * stage;
-    off[1] = o; o += 64;                                   // full[2], tc barrier, TMEM slot, flags
+    off[1] = o; o += 64;                                   // full[2], tc and drain barriers, TMEM slot, flags
     off[2] = o; o += (size_t)kNSRec * kWarps * 8;
     off[3] = o; o += (size_t)kNSRec * 8;
     off[4] = o; o += acc * 8;
     off[5] = o; o += (4 * 8 + 4) * 4;
-    off[6] = o; o += bins ? (size_t)copies * (tb + 1) * 4 : 0;
+    off[6] = o; o += bins ? (size_t)sets * copies * (tb + 1) * 4 : 0;
     o = (o + 7) & ~(size_t)7;
     off[7] = o; o += bins ? (size_t)tb * 8 : 0;
     off[8] = o; o += bins ? (size_t)tb * 4 : 0;
     off[9] = o; o += pass >= 3 ? 4096 * 4 : 0;
-    off[10] = o; o += pass == 2 ? 16 * kWarps * 4 : (pass == 3 ? 16 * 4 : 0);
+    off[10] = o; o += pass == 2 ? 2 * 16 * kWarps * 4 : (pass == 3 ? 16 * 4 : 0);
     o = (o + 127) & ~(size_t)127;
     off[11] = o; o += pass >= 3 ? 4 * kTcTileBytes + 128 : 0;  // + slack to align the tiles to 128 bytes
     off[12] = o;
@@ -174,7 +190,7 @@ fast_pass_kernel(const GroupHdr* __restrict__ hdr, const DevTensor* __restrict__
                  double* __restrict__ rec_scal, float* __restrict__ rec_bins) {
     using Cfg = FastCfg<PASS>;
     constexpr int RM = Cfg::kRM;
-    constexpr int ITERS = 16, UNR = 4;
+    constexpr int ITERS = 16, UNR = PASS == 4 ? 2 : 4;  // rows per TMEM read (P4: its Gram holds 58 registers)
     constexpr bool TCR = Cfg::kTCR;
     extern __shared__ __align__(128) unsigned char fast_smem[];
     unsigned char* smem_raw = fast_smem;
@@ -195,8 +211,10 @@ fast_pass_kernel(const GroupHdr* __restrict__ hdr, const DevTensor* __restrict__
     unsigned char* s_stage = smem_raw + off[0];
     uint64_t* s_full = reinterpret_cast<uint64_t*>(smem_raw + off[1]);  // [0], [1]: stage barriers
     uint64_t* s_tcbar = s_full + 2;
-    uint32_t* s_tcslot = reinterpret_cast<uint32_t*>(s_full + 3);
+    uint64_t* s_drainbar = s_full + 3;
+    uint32_t* s_tcslot = reinterpret_cast<uint32_t*>(s_full + 4);
     int* s_flag = reinterpret_cast<int*>(s_tcslot + 1);
+    int* s_abort = s_flag + 1;
     double* s_red = reinterpret_cast<double*>(smem_raw + off[2]);
     double* s_tot = reinterpret_cast<double*>(smem_raw + off[3]);
     double* s_acc = reinterpret_cast<double*>(smem_raw + off[4]);
@@ -215,7 +233,11 @@ fast_pass_kernel(const GroupHdr* __restrict__ hdr, const DevTensor* __restrict__
     if (tid == 0) {
         mbar_init(&s_full[0], 1);
         mbar_init(&s_full[1], 1);
-        if constexpr (TCR) mbar_init(s_tcbar, 4);  // one arrival per issuing thread
+        if constexpr (TCR) {
+            mbar_init(s_tcbar, 4);      // one arrival per issuing thread
+            mbar_init(s_drainbar, 4);   // the same four threads, once, after a give-up
+        }
+        *s_abort = 0;
     }
     if constexpr (TCR) {
         if (warp == 0) tc_alloc(s_tcslot, kTcCols);
@@ -230,7 +252,7 @@ fast_pass_kernel(const GroupHdr* __restrict__ hdr, const DevTensor* __restrict__
     constexpr int ncopies = Cfg::kCopies;
     const int cstride = TB + 1;
     const BinFix fix = bin_fix(ncopies, ITERS);
-    int* my_bins = s_ibin + (tid & (ncopies - 1)) * cstride;
+    int ip = 0;  // item parity: the bin copies and row sums of passes without a top barrier alternate
 
     uint32_t ph = 0u;        // bit b: parity of the next completion of stage barrier b
     uint32_t inflight = 0u;  // tid 0, bit b: loads issued into stage b and not yet consumed
@@ -313,7 +335,7 @@ fast_pass_kernel(const GroupHdr* __restrict__ hdr, const DevTensor* __restrict__
             }
         }
         if constexpr (Cfg::kBins) {
-            for (int b = tid; b < ncopies * cstride; b += kThreads) s_ibin[b] = 0;
+            for (int b = tid; b < Cfg::kBinSets * ncopies * cstride; b += kThreads) s_ibin[b] = 0;
             for (int b = tid; b < TB; b += kThreads) {
                 s_lbin[b] = 0;
                 s_fbin[b] = 0.0f;
@@ -329,8 +351,9 @@ fast_pass_kernel(const GroupHdr* __restrict__ hdr, const DevTensor* __restrict__
         // Stage item (ct, band) into buffer b: warp 0, lane 0 first waits until every
         // store it issued has finished reading shared memory, then arms the barrier.
         auto stage = [&](int ct_, int band_, int b) {
+            if (lane < 16) bulk_wait_read_all();  // this lane's stores have read their rows
+            __syncwarp();
             if (lane == 0) {
-                bulk_wait_read_all();
                 mbar_arrive_expect(full_bar(b), (uint32_t)Cfg::kStage);
                 inflight |= 1u << b;
             }
@@ -420,23 +443,47 @@ fast_pass_kernel(const GroupHdr* __restrict__ hdr, const DevTensor* __restrict__
             const int nct = band + 1 == n_bands ? ct + 1 : ct;
             const bool has_next = it + 1 < seg_end;
             if (!Cfg::kStore && has_next && warp == 0) stage(nct, nband, buf ^ 1);
-            if (tid == 0) {
-                int fl = mbar_wait_bounded(full_bar(buf), (ph >> buf) & 1u, kStageWaitNs) ? 0 : 1;
-                if (!fl) inflight &= ~(1u << buf);
-                if constexpr (TCR) {
-                    if (!fl && !mbar_wait_bounded(smem_u32(s_tcbar), tc_parity, kTcWaitNs)) fl = 2;
+            if constexpr (Cfg::kTopBar) {
+                if (tid == 0) {
+                    int fl = mbar_wait_bounded(full_bar(buf), (ph >> buf) & 1u, kStageWaitNs) ? 0 : 1;
+                    if (!fl) inflight &= ~(1u << buf);
+                    if constexpr (TCR) {
+                        if (!fl && !mbar_wait_bounded(smem_u32(s_tcbar), tc_parity, kTcWaitNs)) fl = 2;
+                    }
+                    *s_flag = fl;
                 }
-                *s_flag = fl;
+                __syncthreads();
+                if (*s_flag) {  // a stage or a product never completed: stop this block (uniform)
+                    if (tid == 0) {
+                        atomicOr(hdr->status, 1);
+                        *s_abort = 1;
+                    }
+                    abort = true;
+                    break;
+                }
+                (void)mbar_test(full_bar(buf), (ph >> buf) & 1u);  // this thread's acquire of the completed stage
+                ph ^= 1u << buf;
+                if constexpr (TCR) tc_parity ^= 1;
+            } else {
+                // every thread waits for the stage and its products itself; a wait that gives
+                // up marks the block, which stops at the end of this item (the item computes
+                // on whatever the buffers hold; nothing is read or written out of bounds)
+                bool ok = mbar_wait_quick(full_bar(buf), (ph >> buf) & 1u, kStageWaitNs);
+                if (ok) {
+                    ph ^= 1u << buf;
+                    if (tid == 0) inflight &= ~(1u << buf);
+                }
+                if constexpr (TCR) {
+                    ok = mbar_wait_quick(smem_u32(s_tcbar), tc_parity, kTcWaitNs) && ok;
+                    tc_parity ^= 1;
+                }
+                if (!ok) {
+                    atomicOr(s_abort, 1);
+                    atomicOr(hdr->status, 1);
+                }
             }
-            __syncthreads();
-            if (*s_flag) {  // a stage or a product never completed: stop this block (uniform)
-                if (tid == 0) atomicOr(hdr->status, 1);
-                abort = true;  // tc_parity still names the product wait that did not complete
-                break;
-            }
-            (void)mbar_test(full_bar(buf), (ph >> buf) & 1u);  // this thread's acquire of the completed stage
-            ph ^= 1u << buf;
-            if constexpr (TCR) tc_parity ^= 1;
+            int* my_bins = s_ibin + (ip * ncopies + (tid & (ncopies - 1))) * cstride;
+            float* rows_ip = s_rows + (PASS == 2 ? ip * ITERS * kWarps : 0);
             const unsigned char* sb = s_stage + (size_t)buf * Cfg::kStage;
             float* xb = reinterpret_cast<float*>(const_cast<unsigned char*>(sb));
             const uint16_t* jb = reinterpret_cast<const uint16_t*>(sb + Cfg::kXB);
@@ -512,7 +559,7 @@ fast_pass_kernel(const GroupHdr* __restrict__ hdr, const DevTensor* __restrict__
                     // row sums over the 256 columns: a warp's 32 lanes here, the 8 warps after the item
                     const float x = group_sum4(dv, 32);
                     const int ur = 2 * ((lane & 16) != 0) + ((lane & 8) != 0);
-                    if ((lane & 7) == 0) s_rows[(m0 + ur) * kWarps + warp] = x;
+                    if ((lane & 7) == 0) rows_ip[(m0 + ur) * kWarps + warp] = x;
                 } else if constexpr (PASS == 3) {
 #pragma unroll
                     for (int u = 0; u < UNR; ++u) {
@@ -634,36 +681,41 @@ fast_pass_kernel(const GroupHdr* __restrict__ hdr, const DevTensor* __restrict__
                 tc_fence_before();
             }
             __syncthreads();  // the item's tiles and the reduction scratch are complete
+            if (*s_abort) {  // a wait gave up in this item (uniform after the barrier)
+                abort = true;
+                break;
+            }
             if constexpr (PASS == 2) {
                 if (tid < ITERS) {
                     float s = 0.0f;
 #pragma unroll
-                    for (int w = 0; w < kWarps; ++w) s += s_rows[tid * kWarps + w];
+                    for (int w = 0; w < kWarps; ++w) s += rows_ip[tid * kWarps + w];
                     Dp->rowpart[(int64_t)ct * rows + rbase + tid] = s;
                 }
             }
-            if constexpr (Cfg::kStore) {
-                if (tid == 0) {
+            if constexpr (Cfg::kStore) {  // one row per lane of warp 0, each lane its own bulk group
+                if (warp == 0 && lane < ITERS) {
                     const uint32_t src = smem_u32(PASS == 3 ? (const void*)xb : (const void*)pb);
-#pragma unroll 1
-                    for (int r = 0; r < ITERS; ++r)
-                        bulk_store(xdst + (int64_t)(rbase + r) * cols + (int64_t)ct * 256, src + r * 1024, 1024);
+                    bulk_store(xdst + (int64_t)(rbase + lane) * cols + (int64_t)ct * 256, src + lane * 1024, 1024);
                     bulk_commit();
                 }
             }
             if constexpr (TCR) tcb ^= 1;
             if constexpr (Cfg::kBins) {
-                // empty the fixed-point copies into the exact block sums (ordered before the
-                // next item's atomics by the barrier that precedes its compute)
+                // empty this item's fixed-point copies into the exact block sums: before the next
+                // item's atomics (P3: its top barrier) or before the item after it reuses them
+                // (P2: the copies alternate, and this thread reaches the next end barrier first)
+                int* cp = s_ibin + ip * ncopies * cstride;
                 for (int b = tid; b < TB; b += kThreads) {
                     long long s = 0;
                     for (int c = 0; c < ncopies; ++c) {
-                        s += s_ibin[c * cstride + b];
-                        s_ibin[c * cstride + b] = 0;
+                        s += cp[c * cstride + b];
+                        cp[c * cstride + b] = 0;
                     }
                     s_lbin[b] += s;
                 }
             }
+            if constexpr (Cfg::kBinSets > 1) ip ^= 1;
             buf ^= 1;
             ct = nct;
             band = nband;
@@ -698,8 +750,8 @@ fast_pass_kernel(const GroupHdr* __restrict__ hdr, const DevTensor* __restrict__
     }
 
     // ---- drain: stores complete, loads in flight landed, TMEM freed
+    if (warp == 0 && lane < 16) bulk_wait_all();
     if (tid == 0) {
-        bulk_wait_all();
         if (abort) {
             for (int b = 0; b < 2; ++b)
                 if (((inflight >> b) & 1u) && !mbar_wait_bounded(full_bar(b), (ph >> b) & 1u, kStageWaitNs))
@@ -707,10 +759,13 @@ fast_pass_kernel(const GroupHdr* __restrict__ hdr, const DevTensor* __restrict__
         }
     }
     if constexpr (TCR) {
-        // after a give-up the products of the next item may still be in flight: wait for them
-        // (bounded) before the TMEM is freed, and record bit 2 if they never completed
-        if (abort && tid == 0 && !mbar_wait_bounded(smem_u32(s_tcbar), tc_parity, kTcWaitNs))
-            atomicOr(hdr->status, 2);
+        // after a give-up, products may still be in flight: each issuing thread commits its
+        // tensor-core work to the drain barrier, which completes once all of it has landed;
+        // it is waited for (bounded) before the TMEM is freed, bit 2 if it never completes
+        if (abort) {
+            if ((tid & 63) == 0) tc_commit(smem_u32(s_drainbar));
+            if (tid == 0 && !mbar_wait_bounded(smem_u32(s_drainbar), 0, kTcWaitNs)) atomicOr(hdr->status, 2);
+        }
         tc_fence_before();
         __syncthreads();
         if (warp == 0) {
