@@ -515,7 +515,7 @@ fast_pass_kernel(const GroupHdr* __restrict__ hdr, const DevTensor* __restrict__
             if constexpr (PASS == 3) __syncthreads();  // s_rows written
             float s0 = 0.0f, s1 = 0.0f, colacc = 0.0f;
 
-#pragma unroll 1
+#pragma unroll
             for (int m0 = 0; m0 < ITERS; m0 += UNR) {
                 if (Cfg::kStore && m0 == ITERS / 2 && has_next && warp == 0) stage(nct, nband, buf ^ 1);
                 float R1[UNR], R2[UNR];
