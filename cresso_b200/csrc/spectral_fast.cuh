@@ -96,24 +96,42 @@ __device__ __forceinline__ float rcp_approx(float x) {
 __device__ __forceinline__ float2 f2(float a, float b) { return make_float2(a, b); }
 __device__ __forceinline__ float2 f2(float a) { return make_float2(a, a); }
 
-// tanh of two values on the two-lane fp32 pipe.  |x| < 0.625: the odd
-// polynomial x + x^3 P(x^2), P of degree 4 fitted here for minimum relative
-// error on [0, 0.625] (8e-8 in float32); above: 1 - 2 / (e^{2|x|} + 1) with
-// the special-function exp2 and reciprocal, sign restored (5e-7 relative,
-// largest just above the switch point; 1 exactly once e^{2|x|} overflows).
+// tanh of two values on the two-lane fp32 pipe: x P(x^2) / Q(x^2) with P and
+// Q of degree 4, fitted here for minimum relative error of tanh on [0, 9]
+// (4.6e-7 in float32 with the special-function reciprocal) and |x| clamped to
+// 9, where tanh is 1 in float32 to within that bound.
 __device__ __forceinline__ float2 tanh2(float2 x) {
-    const float2 y = __fmul2_rn(x, x);
-    float2 p = f2(-0.0057185678742825985f);
-    p = __ffma2_rn(p, y, f2(0.020652735605835915f));
-    p = __ffma2_rn(p, y, f2(-0.053744520992040634f));
-    p = __ffma2_rn(p, y, f2(0.1333151012659073f));
-    p = __ffma2_rn(p, y, f2(-0.3333328366279602f));
-    const float2 small = __ffma2_rn(__fmul2_rn(x, y), p, x);
-    const float ax = fabsf(x.x), ay = fabsf(x.y);
-    const float2 arg = __fmul2_rn(f2(ax, ay), f2(2.8853900817779268f));  // 2 / ln 2
-    const float2 d = __fadd2_rn(f2(ex2_approx(arg.x), ex2_approx(arg.y)), f2(1.0f));
-    const float2 big = __ffma2_rn(f2(rcp_approx(d.x), rcp_approx(d.y)), f2(-2.0f), f2(1.0f));
-    return f2(ax < 0.625f ? small.x : copysignf(big.x, x.x), ay < 0.625f ? small.y : copysignf(big.y, x.y));
+    const float2 xc = f2(fminf(fmaxf(x.x, -9.0f), 9.0f), fminf(fmaxf(x.y, -9.0f), 9.0f));
+    const float2 y = __fmul2_rn(xc, xc);
+    float2 p = f2(1.3350115679600094e-08f);
+    p = __ffma2_rn(p, y, f2(2.060582301055547e-05f));
+    p = __ffma2_rn(p, y, f2(0.003495392156764865f));
+    p = __ffma2_rn(p, y, f2(0.13380861282348633f));
+    p = __ffma2_rn(p, y, f2(1.0f));
+    float2 q = f2(7.774701771268155e-07f);
+    q = __ffma2_rn(q, y, f2(0.0003285312559455633f));
+    q = __ffma2_rn(q, y, f2(0.0258762389421463f));
+    q = __ffma2_rn(q, y, f2(0.4671417772769928f));
+    q = __ffma2_rn(q, y, f2(1.0f));
+    return __fmul2_rn(__fmul2_rn(xc, p), f2(rcp_approx(q.x), rcp_approx(q.y)));
+}
+
+// log(1 + x), x >= 0, of two values: log1p_pos lane by lane, with its series on
+// the two-lane pipe.
+__device__ __forceinline__ float2 log1p_pos2(float2 x) {
+    const float2 d = __fadd2_rn(x, f2(2.0f));  // in [2, 3] on the branch that uses it
+    const float2 z = __fmul2_rn(x, f2(rcp_approx(d.x), rcp_approx(d.y)));
+    const float2 w = __fmul2_rn(z, z);
+    float2 p = f2(1.0f / 13.0f);
+    p = __ffma2_rn(p, w, f2(1.0f / 11.0f));
+    p = __ffma2_rn(p, w, f2(1.0f / 9.0f));
+    p = __ffma2_rn(p, w, f2(1.0f / 7.0f));
+    p = __ffma2_rn(p, w, f2(1.0f / 5.0f));
+    p = __ffma2_rn(p, w, f2(1.0f / 3.0f));
+    const float2 series = __fmul2_rn(f2(2.0f), __ffma2_rn(__fmul2_rn(z, w), p, z));
+    const float2 u = __fadd2_rn(f2(1.0f), x);
+    const float2 lg = __fmul2_rn(f2(0.693147180559945309f), f2(__log2f(u.x), __log2f(u.y)));
+    return f2(x.x <= 1.0f ? series.x : lg.x, x.y <= 1.0f ? series.y : lg.y);
 }
 
 // Drive components of two elements (cresso_v5.py:1315-1326; drive_parts on a row pair).
@@ -513,7 +531,7 @@ fast_pass_kernel(const GroupHdr* __restrict__ hdr, const DevTensor* __restrict__
                 if (it + 2 < seg_end) tc_bnext = tc_load_b(nband + 1 == n_bands ? 0 : nband + 1);
             }
             if constexpr (PASS == 3) __syncthreads();  // s_rows written
-            float s0 = 0.0f, s1 = 0.0f, colacc = 0.0f;
+            float2 s02 = f2(0.0f), s12 = f2(0.0f), col2 = f2(0.0f);  // even / odd rows
 
 #pragma unroll
             for (int m0 = 0; m0 < ITERS; m0 += UNR) {
@@ -528,32 +546,39 @@ fast_pass_kernel(const GroupHdr* __restrict__ hdr, const DevTensor* __restrict__
                 if constexpr (PASS == 2) {
                     float dv[UNR];
 #pragma unroll
-                    for (int u = 0; u < UNR; ++u) {
+                    for (int u = 0; u < UNR; u += 2) {  // two rows on the two-lane pipe
                         const int m = m0 + u;
                         const int o = m * 256 + lc;
-                        const float x = xb[o];
-                        float a1[RM], a2[RM];
-                        load_row<RM>(rtb, m, a1, a2);
-                        const float rel = fminf(fabsf(x) * inv_scale + eps, 1.0e4f);  // |sgn x| = |x|
-                        const float ds = exp2f(ep * __log2f(rel));
-                        const float L = log1p_pos(ds);
-                        const float Lc = L - 0.5f;
-                        dv[u] = rel;  // instant metric power 1: the axis density is rel
-                        s0 += L;
-                        s1 += rel;
-                        colacc += rel;
-                        const float2 Lc2 = f2(Lc);
+                        float2 rel = __ffma2_rn(f2(fabsf(xb[o]), fabsf(xb[o + 256])), f2(inv_scale), f2(eps));
+                        rel = f2(fminf(rel.x, 1.0e4f), fminf(rel.y, 1.0e4f));  // |sgn x| = |x|
+                        const float2 lg = __fmul2_rn(f2(ep), f2(__log2f(rel.x), __log2f(rel.y)));
+                        const float2 ds = f2(exp2f(lg.x), exp2f(lg.y));
+                        const float2 L = log1p_pos2(ds);
+                        const float2 Lc = __fadd2_rn(L, f2(-0.5f));
+                        dv[u] = rel.x;  // instant metric power 1: the axis density is rel
+                        dv[u + 1] = rel.y;
+                        s02 = __fadd2_rn(s02, L);
+                        s12 = __fadd2_rn(s12, rel);
+                        col2 = __fadd2_rn(col2, rel);
 #pragma unroll
-                        for (int q = 1; q < RM; ++q) z12[q] = __ffma2_rn(f2(a1[q], a2[q]), Lc2, z12[q]);
-                        zc += Lc;
-                        const int j = jb[o];
-                        const bool fx = ds < fix.vmax;
-                        const int qv = fx ? __float2int_rn(ds * fix.scale) : 0;
-                        atomicAdd(&my_bins[j & 63], qv);
-                        atomicAdd(&my_bins[B + (j >> 6)], qv);
-                        if (!fx) {
-                            atomicAdd(&s_fbin[j & 63], ds);
-                            atomicAdd(&s_fbin[B + (j >> 6)], ds);
+                        for (int h = 0; h < 2; ++h) {
+                            float a1[RM], a2[RM];
+                            load_row<RM>(rtb, m + h, a1, a2);
+                            const float lc_h = h ? Lc.y : Lc.x;
+                            const float2 Lc2 = f2(lc_h);
+#pragma unroll
+                            for (int q = 1; q < RM; ++q) z12[q] = __ffma2_rn(f2(a1[q], a2[q]), Lc2, z12[q]);
+                            zc += lc_h;
+                            const float dsh = h ? ds.y : ds.x;
+                            const int j = jb[o + 256 * h];
+                            const bool fx = dsh < fix.vmax;
+                            const int qv = fx ? __float2int_rn(dsh * fix.scale) : 0;
+                            atomicAdd(&my_bins[j & 63], qv);
+                            atomicAdd(&my_bins[B + (j >> 6)], qv);
+                            if (!fx) {
+                                atomicAdd(&s_fbin[j & 63], dsh);
+                                atomicAdd(&s_fbin[B + (j >> 6)], dsh);
+                            }
                         }
                     }
                     // row sums over the 256 columns: a warp's 32 lanes here, the 8 warps after the item
@@ -562,35 +587,46 @@ fast_pass_kernel(const GroupHdr* __restrict__ hdr, const DevTensor* __restrict__
                     if ((lane & 7) == 0) rows_ip[(m0 + ur) * kWarps + warp] = x;
                 } else if constexpr (PASS == 3) {
 #pragma unroll
-                    for (int u = 0; u < UNR; ++u) {
+                    for (int u = 0; u < UNR; u += 2) {  // two rows on the two-lane pipe
                         const int m = m0 + u;
                         const int o = m * 256 + lc;
-                        const float f = sgn * xb[o];
-                        float a1[RM], a2[RM];
-                        load_row<RM>(rtb, m, a1, a2);
-                        const float lm = clampf(R1[u], -3.0f, 3.0f);
-                        const float metric = clampf(__expf(mcpl * lm), 0.06f, 16.0f);
-                        float den = scale * metric;
-                        if (flags & F_INST2D) den = den * clampf(s_rows[m] * colf, 0.08f, 12.0f);
-                        const int j = jb[o];
-                        den = den * s_joint[j];
-                        const float t = clampf(__fdividef(f, den + eps), -1.0e4f, 1.0e4f);
-                        xb[o] = t;  // in place: the tile goes back to the tangent buffer
-                        const float err = t - R2[u];
-                        s0 = fmaf(err, err, s0);
-                        s1 += t;
-                        const float2 t2 = f2(t);
+                        const float2 f = __fmul2_rn(f2(sgn), f2(xb[o], xb[o + 256]));
+                        const float2 e = __fmul2_rn(f2(mcpl), f2(clampf(R1[u], -3.0f, 3.0f), clampf(R1[u + 1], -3.0f, 3.0f)));
+                        const float2 metric = f2(clampf(__expf(e.x), 0.06f, 16.0f), clampf(__expf(e.y), 0.06f, 16.0f));
+                        float2 den = __fmul2_rn(f2(scale), metric);
+                        if (flags & F_INST2D)
+                            den = __fmul2_rn(den, f2(clampf(s_rows[m] * colf, 0.08f, 12.0f),
+                                                     clampf(s_rows[m + 1] * colf, 0.08f, 12.0f)));
+                        const int j0 = jb[o], j1 = jb[o + 256];
+                        den = __fmul2_rn(den, f2(s_joint[j0], s_joint[j1]));
+                        const float2 de = __fadd2_rn(den, f2(eps));
+                        float2 t = __fmul2_rn(f, f2(rcp_approx(de.x), rcp_approx(de.y)));
+                        t = f2(clampf(t.x, -1.0e4f, 1.0e4f), clampf(t.y, -1.0e4f, 1.0e4f));
+                        xb[o] = t.x;  // in place: the tile goes back to the tangent buffer
+                        xb[o + 256] = t.y;
+                        const float2 err = __fadd2_rn(t, f2(-R2[u], -R2[u + 1]));
+                        s02 = __ffma2_rn(err, err, s02);
+                        s12 = __fadd2_rn(s12, t);
+                        const float2 port = __ffma2_rn(f2(tmix), t, err);
 #pragma unroll
-                        for (int q = 1; q < RM; ++q) z12[q] = __ffma2_rn(f2(a1[q], a2[q]), t2, z12[q]);
-                        zc += t;
-                        const float port = err + tmix * t;
-                        const bool fx = fabsf(port) < fix.vmax;  // false for non-finite values
-                        const int qv = fx ? __float2int_rn(port * fix.scale) : 0;
-                        atomicAdd(&my_bins[j & 63], qv);
-                        atomicAdd(&my_bins[B + (j >> 6)], qv);
-                        if (!fx) {
-                            atomicAdd(&s_fbin[j & 63], port);
-                            atomicAdd(&s_fbin[B + (j >> 6)], port);
+                        for (int h = 0; h < 2; ++h) {
+                            float a1[RM], a2[RM];
+                            load_row<RM>(rtb, m + h, a1, a2);
+                            const float th = h ? t.y : t.x;
+                            const float2 t2 = f2(th);
+#pragma unroll
+                            for (int q = 1; q < RM; ++q) z12[q] = __ffma2_rn(f2(a1[q], a2[q]), t2, z12[q]);
+                            zc += th;
+                            const float ph_ = h ? port.y : port.x;
+                            const int j = h ? j1 : j0;
+                            const bool fx = fabsf(ph_) < fix.vmax;  // false for non-finite values
+                            const int qv = fx ? __float2int_rn(ph_ * fix.scale) : 0;
+                            atomicAdd(&my_bins[j & 63], qv);
+                            atomicAdd(&my_bins[B + (j >> 6)], qv);
+                            if (!fx) {
+                                atomicAdd(&s_fbin[j & 63], ph_);
+                                atomicAdd(&s_fbin[B + (j >> 6)], ph_);
+                            }
                         }
                     }
                 } else if constexpr (PASS == 4) {
@@ -634,8 +670,8 @@ fast_pass_kernel(const GroupHdr* __restrict__ hdr, const DevTensor* __restrict__
 
             // ---- item epilogue
             if constexpr (PASS == 2 || PASS == 3) {
-                acc0 += (double)s0;
-                acc1 += (double)s1;
+                acc0 += (double)(s02.x + s02.y);
+                acc1 += (double)(s12.x + s12.y);
                 if (nct != ct || it + 1 == seg_end || ++items_since_flush == 4) {
                     float b1[RM], b2[RM];
                     load_col<RM>(coltab, gcols, gc, b1, b2);
@@ -671,7 +707,7 @@ fast_pass_kernel(const GroupHdr* __restrict__ hdr, const DevTensor* __restrict__
                     items_since_flush = 0;
                 }
             }
-            if constexpr (PASS == 2) Dp->colpart[(int64_t)band * cols + col] = colacc;
+            if constexpr (PASS == 2) Dp->colpart[(int64_t)band * cols + col] = col2.x + col2.y;
             if constexpr (Cfg::kStore) tc_fence_smem();  // this thread's tile writes, before the bulk store
             if constexpr (TCR) {  // item i + 2's carrier rows into this item's B buffer (its products are done)
                 if (it + 2 < seg_end) {

@@ -173,20 +173,26 @@ class ZeroCRESSO5(CRESSO5):
         if closure is not None:
             with torch.enable_grad():
                 loss = closure()
+        self.check_device_status(block=False)
+        # route once per step, with the gradients of the tensors other ranks own hidden (so
+        # the routing cache of an unchanged step matches), then run each bucket's slice
+        mine_all = {id(p) for bucket in self.buckets for p in bucket[self.rank]}
+        hidden = [(p, p.grad) for g in self.param_groups for p in g["params"]
+                  if id(p) not in mine_all and p.grad is not None]
+        for p, _ in hidden:
+            p.grad = None
+        try:
+            routed = [self._route_group(gi, group) for gi, group in enumerate(self.param_groups)]
+        finally:
+            for p, gr in hidden:
+                p.grad = gr
+        spectral_devices: set = set()
         pending: list = []  # all-gathers of the previous bucket, still in flight
-        for bucket in self.buckets:
+        for k, bucket in enumerate(self.buckets):
             mine = {id(p) for p in bucket[self.rank]}
-            hidden = []
-            for g in self.param_groups:
-                for p in g["params"]:
-                    if id(p) not in mine and p.grad is not None:
-                        hidden.append((p, p.grad))
-                        p.grad = None
-            try:
-                super().step()
-            finally:
-                for p, gr in hidden:
-                    p.grad = gr
+            if mine:
+                for group, r in zip(self.param_groups, routed):
+                    self._run_routed(group, r, spectral_devices, select=mine, tag=("bucket", k))
             if self.world > 1:
                 started = self._gather_bucket_async(bucket)
                 # the previous bucket's exchange ran while this bucket computed; its
@@ -196,6 +202,7 @@ class ZeroCRESSO5(CRESSO5):
                 pending = started
         for item in pending:
             self._finish_gather(item)
+        self._publish_status(spectral_devices)
         exchange_status(self, self.process_group)
         return loss
 

@@ -56,6 +56,13 @@ class CRESSO5(Optimizer):
     ``micro_field_max_size > 0`` tensors up to that size keep per-element
     micro fields.  Parameters may be float32, float16, bfloat16 (float32 work
     and state) or float64 (float64 work and state), on CUDA devices only.
+
+    The state tensors are updated in place, and the descriptor tables that point
+    the kernels at them are cached across steps (keyed on the parameters, their
+    storage and their state dicts).  Change state through ``load_state_dict``
+    (which drops the caches) or in place; a caller that rebinds a state tensor
+    inside a state dict (``opt.state[p]["q_cos"] = t``) calls
+    ``invalidate_caches()`` afterwards.
     """
 
     def __init__(
@@ -383,31 +390,57 @@ class CRESSO5(Optimizer):
             with torch.enable_grad():
                 loss = closure()
         self.check_device_status(block=False)
-        spectral_devices = set()
+        spectral_devices: set = set()
         for gi, group in enumerate(self.param_groups):
-            route_sig = (group["min_spectral_size"], group["rank"], group.get("thin_matrix_route", "scalar"),
-                         group.get("thin_matrix_max_width", 64), group.get("thin_matrix_min_aspect", 4.0),
-                         group.get("micro_field_max_size", 0))
-            routed = self._route_fast(gi, group, route_sig)
-            if routed is None:
-                routed = self._route_full(gi, group, route_sig)
-            spectral, scalar, micro_items, spectral64 = routed
-            hp = None
-            for device, items in spectral.items():
-                hp = _lib.pack_hparams(group) if hp is None else hp
-                self._run_spectral(group, hp, device, items)
-                spectral_devices.add(device)
-            for device, items in scalar.items():
-                hp = _lib.pack_hparams(group) if hp is None else hp
-                self._run_scalar(hp, device, items)
-            for device, items in micro_items.items():
-                hp = _lib.pack_hparams(group) if hp is None else hp
-                self._run_micro(hp, device, items)
-            for device, items in spectral64.items():
-                hp = _lib.pack_hparams(group) if hp is None else hp
-                self._run_spectral64(group, hp, device, items)
+            self._run_routed(group, self._route_group(gi, group), spectral_devices)
         self._publish_status(spectral_devices)
         return loss
+
+    def _route_group(self, gi: int, group: dict):
+        """(spectral, scalar, micro, spectral64): per route, per device, the
+        (param, grad, state) items of the group's parameters with a gradient."""
+        route_sig = (group["min_spectral_size"], group["rank"], group.get("thin_matrix_route", "scalar"),
+                     group.get("thin_matrix_max_width", 64), group.get("thin_matrix_min_aspect", 4.0),
+                     group.get("micro_field_max_size", 0))
+        routed = self._route_fast(gi, group, route_sig)
+        if routed is None:
+            routed = self._route_full(gi, group, route_sig)
+        return routed
+
+    def _run_routed(self, group: dict, routed, spectral_devices: set, select=None, tag=None) -> None:
+        """Launches the routes of one group; `select` (a set of parameter ids) limits
+        the step to those parameters, and `tag` keys their descriptor tables apart
+        from the tables of other selections."""
+        spectral, scalar, micro_items, spectral64 = routed
+        hp = None
+        for kind, per_device in enumerate((spectral, scalar, micro_items, spectral64)):
+            for device, items in per_device.items():
+                if select is not None:
+                    items = [it for it in items if id(it[0]) in select]
+                    if not items:
+                        continue
+                hp = _lib.pack_hparams(group) if hp is None else hp
+                if kind == 0:
+                    self._run_spectral(group, hp, device, items, tag)
+                    spectral_devices.add(device)
+                elif kind == 1:
+                    self._run_scalar(hp, device, items, tag)
+                elif kind == 2:
+                    self._run_micro(hp, device, items, tag)
+                else:
+                    self._run_spectral64(group, hp, device, items)
+
+    def invalidate_caches(self) -> None:
+        """Drops the cached routing and descriptor tables; the next step rebuilds
+        them from the current parameters and state tensors."""
+        self._fast.clear()
+        self._scalar_descs.clear()
+        self._micro_descs.clear()
+        self._spectral_desc_cache.clear()
+
+    def load_state_dict(self, state_dict) -> None:  # type: ignore[override]
+        super().load_state_dict(state_dict)
+        self.invalidate_caches()
 
     # ------------------------------------------------------- failure reports
     def _status_word(self, device) -> Tensor:
@@ -557,7 +590,7 @@ class CRESSO5(Optimizer):
             self._fast.pop(gi, None)
         return routed
 
-    def _spectral_descs(self, group: dict, device, items: list) -> np.ndarray:
+    def _spectral_descs(self, group: dict, device, items: list, tag=None) -> np.ndarray:
         """Descriptor table of the spectral group.  Like the small-route tables it is
         reused while the parameters, their storage, their state dicts and the settings
         it depends on stay the same, refreshing gradient pointers and step counters;
@@ -567,7 +600,7 @@ class CRESSO5(Optimizer):
         settings = (group["rank"], group["max_frequency"], bins, tables, group.get("hard_channel_min_size"),
                     group.get("thin_matrix_hard_cutoff"))
         ident = (settings, tuple((id(p), p.data_ptr(), p.shape, id(st)) for p, g, st in items))
-        key = (device, id(group))
+        key = (device, id(group), tag)
         cached = self._spectral_desc_cache.get(key)
         if cached is not None and cached[0] == ident:
             descs = cached[1]
@@ -617,13 +650,13 @@ class CRESSO5(Optimizer):
             keep.append(held)
         return descs, keep
 
-    def _run_spectral(self, group: dict, hp: np.ndarray, device, items: list) -> None:
+    def _run_spectral(self, group: dict, hp: np.ndarray, device, items: list, tag=None) -> None:
         if int(group["rank"]) > _lib.MAX_RANK:  # float16 / bfloat16 tensors on the fused path
             raise RuntimeError(f"CRESSO5 B200 path supports rank <= {_lib.MAX_RANK} for float16 / bfloat16 "
                                f"spectral tensors (got {group['rank']}); float32 and float64 take up to "
                                f"{_lib.MAX_RANK_PLAIN}")
         L = _lib.lib()
-        descs = self._spectral_descs(group, device, items)
+        descs = self._spectral_descs(group, device, items, tag)
         n = len(items)
         num_sms = self._num_sms.get(device)
         if num_sms is None:
@@ -696,7 +729,7 @@ class CRESSO5(Optimizer):
         return scratch[off:off + 8 * length].view(torch.float64)
 
     def _small_route_descs(self, cache: dict, device, items: list, state_names: Tuple[str, ...],
-                           bytes_fn: Callable, what: str) -> Tuple[np.ndarray, int]:
+                           bytes_fn: Callable, what: str, tag=None) -> Tuple[np.ndarray, int]:
         """Descriptor table of the scalar or the micro route.  It depends on the
         parameters, their storage and their state tensors and is reused while those
         stay the same; the gradient pointers and step counters change from step to
@@ -706,7 +739,7 @@ class CRESSO5(Optimizer):
         F = _lib.DESC_INDEX
         n = len(items)
         ident = tuple((id(p), p.data_ptr(), p.shape, id(st)) for p, g, st in items)
-        cached = cache.get(device)
+        cached = cache.get((device, tag))
         if cached is not None and cached[0] == ident:
             descs, nbytes = cached[1], cached[2]
         else:
@@ -727,28 +760,28 @@ class CRESSO5(Optimizer):
             nb = np.zeros(1, dtype=np.int64)
             _lib.check(bytes_fn(_lib.ptr(descs), n, nb.ctypes.data_as(_lib._pi64)), what)
             nbytes = int(nb[0])
-            cache[device] = (ident, descs, nbytes, keep)
+            cache[(device, tag)] = (ident, descs, nbytes, keep)
         descs[:, F["grad"]] = [g.data_ptr() for _, g, _ in items]
         descs[:, F["step"]] = [st["step"] for _, _, st in items]
         return descs, nbytes
 
-    def _run_scalar(self, hp: np.ndarray, device, items: list) -> None:
+    def _run_scalar(self, hp: np.ndarray, device, items: list, tag=None) -> None:
         L = _lib.lib()
         descs, nbytes = self._small_route_descs(
             self._scalar_descs, device, items,
             ("force_rms", "drive_energy", "surprise", "action", "q", "impulse", "metric_q", "metric_impulse"),
-            L.cresso_scalar_scratch_bytes, "scalar_scratch_bytes")
+            L.cresso_scalar_scratch_bytes, "scalar_scratch_bytes", tag)
         scratch = self._scratch_buffer(device, "scalar", nbytes)
         stream = torch.cuda.current_stream(device).cuda_stream
         _lib.check(L.cresso_scalar_run(_lib.ptr(descs), len(items), _lib.ptr(hp), _lib.ptr(scratch), scratch.numel(),
                                        stream), "scalar_run")
 
-    def _run_micro(self, hp: np.ndarray, device, items: list) -> None:
+    def _run_micro(self, hp: np.ndarray, device, items: list, tag=None) -> None:
         L = _lib.lib()
         descs, nbytes = self._small_route_descs(
             self._micro_descs, device, items,
             ("force_rms", "drive_energy", "surprise", "micro_energy", "micro_impulse", "micro_refractory"),
-            L.cresso_micro_scratch_bytes, "micro_scratch_bytes")
+            L.cresso_micro_scratch_bytes, "micro_scratch_bytes", tag)
         scratch = self._scratch_buffer(device, "micro", nbytes)
         stream = torch.cuda.current_stream(device).cuda_stream
         _lib.check(L.cresso_micro_run(_lib.ptr(descs), len(items), _lib.ptr(hp), _lib.ptr(scratch), scratch.numel(),
