@@ -169,11 +169,7 @@ struct FastCfg {
     // barriers thread by thread and synchronise the block once per item, at its end
     static constexpr bool kTopBar = PASS == 3;
     static constexpr int kBinSets = kBins && !kTopBar ? 2 : 1;           // bin copies alternate by item
-    // P2 projects on the tensor cores: the density field as the A operand (columns x
-    // rows), the carrier rows as B, 3xTF32 products accumulated in TMEM over four items,
-    // and the float64 per-column sums kept in TMEM too
-    static constexpr bool kTCP = PASS == 2;
-    static constexpr int kAcc = PASS == 4 ? kWarps * 32 : (PASS == 3 ? 2 * kRM * kThreads : 0);
+    static constexpr int kAcc = PASS == 4 ? kWarps * 32 : (kBins ? 2 * kRM * kThreads : 0);
 };
 
 // Shared-memory bytes of a fast pass kernel for tb = hash_bins * hash_tables.
@@ -185,7 +181,7 @@ __host__ __device__ inline size_t fast_smem_layout(int pass, int tb, size_t* off
     const bool bins = pass == 2 || pass == 3;
     const int copies = pass == 3 ? 8 : 16;
     const int sets = pass == 2 ? 2 : 1;
-    const size_t acc = pass == 4 ? kWarps * 32 : (pass == 3 ? 2 * 8 * kThreads : 0);
+    const size_t acc = pass == 4 ? kWarps * 32 : (bins ? 2 * 8 * kThreads : 0);
     size_t o = 0;
     off[0] = o; o += 2 * stage;
     off[1] = o; o += 64;                                   // full[2], tc and drain barriers, TMEM slot, flags
@@ -200,8 +196,7 @@ __host__ __device__ inline size_t fast_smem_layout(int pass, int tb, size_t* off
     off[9] = o; o += pass >= 3 ? 4096 * 4 : 0;
     off[10] = o; o += pass == 2 ? 2 * 16 * kWarps * 4 : (pass == 3 ? 16 * 4 : 0);
     o = (o + 127) & ~(size_t)127;
-    // + slack to align the tiles to 128 bytes; P2: A tiles [half][hi, lo] of 128 x 16, B tiles [2][hi, lo]
-    off[11] = o; o += pass >= 3 ? 4 * kTcTileBytes + 128 : (pass == 2 ? 4 * 8192 + 4 * kTcTileBytes + 128 : 0);
+    off[11] = o; o += pass >= 3 ? 4 * kTcTileBytes + 128 : 0;  // + slack to align the tiles to 128 bytes
     off[12] = o;
     return o;
 }
@@ -213,7 +208,7 @@ fast_pass_kernel(const GroupHdr* __restrict__ hdr, const DevTensor* __restrict__
                  double* __restrict__ rec_scal, float* __restrict__ rec_bins) {
     using Cfg = FastCfg<PASS>;
     constexpr int RM = Cfg::kRM;
-    constexpr int ITERS = 16, UNR = 4;  // rows per TMEM read (P4: its Gram holds 58 registers)
+    constexpr int ITERS = 16, UNR = 4;  // rows per TMEM read
     constexpr bool TCR = Cfg::kTCR;
     extern __shared__ __align__(128) unsigned char fast_smem[];
     unsigned char* smem_raw = fast_smem;
@@ -253,8 +248,6 @@ fast_pass_kernel(const GroupHdr* __restrict__ hdr, const DevTensor* __restrict__
     const uint32_t full0 = smem_u32(&s_full[0]);
     auto full_bar = [&](int b) -> uint32_t { return full0 + 8u * (uint32_t)b; };
     uint32_t tc_base = 0, tc_parity = 0;
-    constexpr bool TCP = Cfg::kTCP;
-    constexpr uint32_t kCols = TCR ? kTcCols : 128;  // P2: D [0, 32), float64 sums [32, 96)
     if (tid == 0) {
         mbar_init(&s_full[0], 1);
         mbar_init(&s_full[1], 1);
@@ -262,18 +255,14 @@ fast_pass_kernel(const GroupHdr* __restrict__ hdr, const DevTensor* __restrict__
             mbar_init(s_tcbar, 4);      // one arrival per issuing thread
             mbar_init(s_drainbar, 4);   // the same four threads, once, after a give-up
         }
-        if constexpr (TCP) {
-            mbar_init(s_tcbar, 1);      // the projection products of an item, issued by thread 0
-            mbar_init(s_drainbar, 1);
-        }
         *s_abort = 0;
     }
-    if constexpr (TCR || TCP) {
-        if (warp == 0) tc_alloc(s_tcslot, kCols);
+    if constexpr (TCR) {
+        if (warp == 0) tc_alloc(s_tcslot, kTcCols);
         tc_fence_before();
     }
     __syncthreads();
-    if constexpr (TCR || TCP) {
+    if constexpr (TCR) {
         tc_fence_after();
         tc_base = *s_tcslot;
     }
@@ -373,15 +362,6 @@ fast_pass_kernel(const GroupHdr* __restrict__ hdr, const DevTensor* __restrict__
         if constexpr (Cfg::kAcc > 0) {
             for (int j = tid; j < Cfg::kAcc; j += kThreads) s_acc[j] = 0.0;
         }
-        const int tc_h = tid >> 7;
-        const uint32_t tc_lane = (uint32_t)(tid & 96) << 16;
-        if constexpr (TCP) {  // this thread's float64 projection sums (16 values) start at zero
-            uint32_t z[32];
-#pragma unroll
-            for (int q = 0; q < 32; ++q) z[q] = 0u;
-            tc_st32(tc_base + tc_lane + 32 + 32 * tc_h, z);
-            tc_wait_st();
-        }
         __syncthreads();
         double acc0 = 0.0, acc1 = 0.0;
         const int lc = tid;  // this thread's column of the 256-column tile
@@ -421,6 +401,8 @@ fast_pass_kernel(const GroupHdr* __restrict__ hdr, const DevTensor* __restrict__
         int uv_ct = -1;
         int tcb = 0;
         int a_ct = -1;
+        const int tc_h = tid >> 7;
+        const uint32_t tc_lane = (uint32_t)(tid & 96) << 16;
         auto tc_build_a = [&](int c) {
             if constexpr (TCR) tc_column_factors<RM>(coltab, gcols, col0 + (int64_t)c * 256 + lc, s_coef, tc_base + tc_lane + 32 * tc_h);
         };
@@ -455,61 +437,6 @@ fast_pass_kernel(const GroupHdr* __restrict__ hdr, const DevTensor* __restrict__
                 tc_commit(smem_u32(s_tcbar));
             }
         };
-        // P2: operand tiles, the state of the four-item window, and its contraction
-        unsigned char* s_pA = s_tcb;                 // [half][hi, lo] 8 KB each
-        unsigned char* s_pB = s_tcb + 4 * 8192;      // [buffer][hi, lo] 1 KB each
-        bool mma_out = false;       // products of the previous item issued, not yet waited for
-        bool flush_pending = false; // the previous item closed a window: its D holds the window's sums
-        bool win_start = true;      // this item opens a window (its first product overwrites D)
-        int flush_gc = 0;
-        auto tcp_wait = [&]() {  // this thread waits for the previous item's products
-            if (mma_out) {
-                if (!mbar_wait_quick(smem_u32(s_tcbar), tc_parity, kTcWaitNs)) {
-                    atomicOr(s_abort, 1);
-                    atomicOr(hdr->status, 1);
-                }
-                tc_parity ^= 1;
-                mma_out = false;
-                tc_fence_after();
-            }
-        };
-        auto tcp_flush = [&](int fgc) {  // D of the closed window into the float64 sums (column fgc)
-            float z[16];
-            tc_ld16(tc_base + tc_lane + 16 * tc_h, z);
-            uint32_t a[32];
-            tc_ld32(tc_base + tc_lane + 32 + 32 * tc_h, a);
-            tc_wait_ld();
-            float b1[RM], b2[RM];
-            load_col<RM>(coltab, gcols, fgc, b1, b2);
-            double accd[2 * RM];
-#pragma unroll
-            for (int q = 0; q < 2 * RM; ++q) accd[q] = __hiloint2double((int)a[2 * q + 1], (int)a[2 * q]);
-            accd[0] += (double)z[0];  // zero mode: the carrier (1, 0), the plain sum
-#pragma unroll
-            for (int q = 1; q < RM; ++q) {
-                const double B1 = b1[q], B2 = b2[q], Z1 = z[2 * q], Z2 = z[2 * q + 1];
-                double c, s;
-                if (mode_is_product(q)) {
-                    c = B1 * Z1;
-                    s = B2 * Z2;
-                } else {
-                    c = B1 * Z1 - B2 * Z2;
-                    s = B2 * Z1 + B1 * Z2;
-                }
-                accd[q] += c;
-                accd[RM + q] += s;
-            }
-#pragma unroll
-            for (int q = 0; q < 2 * RM; ++q) {
-                a[2 * q] = (uint32_t)__double2loint(accd[q]);
-                a[2 * q + 1] = (uint32_t)__double2hiint(accd[q]);
-            }
-            tc_st32(tc_base + tc_lane + 32 + 32 * tc_h, a);
-            tc_wait_st();
-        };
-        (void)s_pA;
-        (void)s_pB;
-        (void)flush_gc;
         float tc_bnext = 0.0f;
         if constexpr (TCR) {  // segment prologue: B of the first two items, the first item's products
             tc_build_a(ct);
@@ -583,23 +510,6 @@ fast_pass_kernel(const GroupHdr* __restrict__ hdr, const DevTensor* __restrict__
             (void)rtb;
             (void)pb;
 
-            if constexpr (TCP) {
-                // this item's carrier rows as the B operand (buffer ip; the products that read
-                // it two items ago have completed: this thread waited for them)
-                {
-                    const float v = rtb[tid];  // row tid / 16, slot tid % 16
-                    const float hi = tf32_rna(v);
-                    unsigned char* tb = s_pB + ip * 2 * kTcTileBytes;
-                    const int o = tc_kmajor_off(tid & 15, tid >> 4);
-                    *reinterpret_cast<float*>(tb + o) = hi;
-                    *reinterpret_cast<float*>(tb + kTcTileBytes + o) = tf32_rna(v - hi);
-                }
-                if (flush_pending) {
-                    tcp_wait();
-                    tcp_flush(flush_gc);
-                    flush_pending = false;
-                }
-            }
             if constexpr (PASS == 3) {
                 if (ct != uv_ct) {
                     uv_ct = ct;
@@ -634,7 +544,7 @@ fast_pass_kernel(const GroupHdr* __restrict__ hdr, const DevTensor* __restrict__
                     tc_wait_ld();
                 }
                 if constexpr (PASS == 2) {
-                    float dv[UNR], lcv[UNR];
+                    float dv[UNR];
 #pragma unroll
                     for (int u = 0; u < UNR; u += 2) {  // two rows on the two-lane pipe
                         const int m = m0 + u;
@@ -650,10 +560,15 @@ fast_pass_kernel(const GroupHdr* __restrict__ hdr, const DevTensor* __restrict__
                         s02 = __fadd2_rn(s02, L);
                         s12 = __fadd2_rn(s12, rel);
                         col2 = __fadd2_rn(col2, rel);
-                        lcv[u] = Lc.x;
-                        lcv[u + 1] = Lc.y;
 #pragma unroll
                         for (int h = 0; h < 2; ++h) {
+                            float a1[RM], a2[RM];
+                            load_row<RM>(rtb, m + h, a1, a2);
+                            const float lc_h = h ? Lc.y : Lc.x;
+                            const float2 Lc2 = f2(lc_h);
+#pragma unroll
+                            for (int q = 1; q < RM; ++q) z12[q] = __ffma2_rn(f2(a1[q], a2[q]), Lc2, z12[q]);
+                            zc += lc_h;
                             const float dsh = h ? ds.y : ds.x;
                             const int j = jb[o + 256 * h];
                             const bool fx = dsh < fix.vmax;
@@ -665,24 +580,6 @@ fast_pass_kernel(const GroupHdr* __restrict__ hdr, const DevTensor* __restrict__
                                 atomicAdd(&s_fbin[B + (j >> 6)], dsh);
                             }
                         }
-                    }
-                    // the four rows of the density field into the A operand (tf32 hi / lo), after the
-                    // previous item's products have read it
-                    if (m0 == 0) tcp_wait();
-                    {
-                        float4 hi, lo;
-                        hi.x = tf32_rna(lcv[0]);
-                        hi.y = tf32_rna(lcv[1]);
-                        hi.z = tf32_rna(lcv[2]);
-                        hi.w = tf32_rna(lcv[3]);
-                        lo.x = tf32_rna(lcv[0] - hi.x);
-                        lo.y = tf32_rna(lcv[1] - hi.y);
-                        lo.z = tf32_rna(lcv[2] - hi.z);
-                        lo.w = tf32_rna(lcv[3] - hi.w);
-                        const int mm = tid & 127;
-                        unsigned char* ta = s_pA + tc_h * 2 * 8192 + (mm >> 3) * 512 + (m0 >> 2) * 128 + (mm & 7) * 16;
-                        *reinterpret_cast<float4*>(ta) = hi;
-                        *reinterpret_cast<float4*>(ta + 8192) = lo;
                     }
                     // row sums over the 256 columns: a warp's 32 lanes here, the 8 warps after the item
                     const float x = group_sum4(dv, 32);
@@ -772,12 +669,7 @@ fast_pass_kernel(const GroupHdr* __restrict__ hdr, const DevTensor* __restrict__
             }  // rows of the item
 
             // ---- item epilogue
-            bool closes = false;  // P2: this item closes its four-item window
-            if constexpr (TCP) {
-                acc0 += (double)(s02.x + s02.y);
-                acc1 += (double)(s12.x + s12.y);
-                closes = nct != ct || it + 1 == seg_end || ++items_since_flush == 4;
-            } else if constexpr (PASS == 3) {
+            if constexpr (PASS == 2 || PASS == 3) {
                 acc0 += (double)(s02.x + s02.y);
                 acc1 += (double)(s12.x + s12.y);
                 if (nct != ct || it + 1 == seg_end || ++items_since_flush == 4) {
@@ -816,7 +708,7 @@ fast_pass_kernel(const GroupHdr* __restrict__ hdr, const DevTensor* __restrict__
                 }
             }
             if constexpr (PASS == 2) Dp->colpart[(int64_t)band * cols + col] = col2.x + col2.y;
-            if constexpr (Cfg::kStore || TCP) tc_fence_smem();  // this thread's tile writes, before the async proxy reads
+            if constexpr (Cfg::kStore) tc_fence_smem();  // this thread's tile writes, before the bulk store
             if constexpr (TCR) {  // item i + 2's carrier rows into this item's B buffer (its products are done)
                 if (it + 2 < seg_end) {
                     tc_store_b(tc_bnext, tcb);
@@ -842,33 +734,6 @@ fast_pass_kernel(const GroupHdr* __restrict__ hdr, const DevTensor* __restrict__
                     const uint32_t src = smem_u32(PASS == 3 ? (const void*)xb : (const void*)pb);
                     bulk_store(xdst + (int64_t)(rbase + lane) * cols + (int64_t)ct * 256, src + lane * 1024, 1024);
                     bulk_commit();
-                }
-            }
-            if constexpr (TCP) {  // the item's projection products, one thread
-                if (tid == 0) {
-                    tc_fence_after();
-                    constexpr uint32_t idesc = tc_idesc_tf32(128, 16);
-                    const uint32_t bhi = smem_u32(s_pB + ip * 2 * kTcTileBytes), blo = bhi + kTcTileBytes;
-#pragma unroll
-                    for (int h = 0; h < 2; ++h) {
-                        const uint32_t ahi = smem_u32(s_pA + h * 2 * 8192), alo = ahi + 8192;
-#pragma unroll
-                        for (int ks = 0; ks < 2; ++ks) {
-                            const uint32_t o = 2 * kTcLBO * ks;
-                            tc_mma_tf32_ss(tc_base + 16 * h, tc_smem_desc(ahi + o), tc_smem_desc(bhi + o), idesc,
-                                           (ks > 0 || !win_start) ? 1u : 0u);
-                            tc_mma_tf32_ss(tc_base + 16 * h, tc_smem_desc(ahi + o), tc_smem_desc(blo + o), idesc, 1u);
-                            tc_mma_tf32_ss(tc_base + 16 * h, tc_smem_desc(alo + o), tc_smem_desc(bhi + o), idesc, 1u);
-                        }
-                    }
-                    tc_commit(smem_u32(s_tcbar));
-                }
-                mma_out = true;
-                win_start = closes;
-                if (closes) {
-                    flush_pending = true;
-                    flush_gc = gc;
-                    items_since_flush = 0;
                 }
             }
             if constexpr (TCR) tcb ^= 1;
@@ -908,21 +773,8 @@ fast_pass_kernel(const GroupHdr* __restrict__ hdr, const DevTensor* __restrict__
                 double v[NS];
                 v[0] = acc0;
                 v[1] = acc1;
-                if constexpr (TCP) {
-                    if (flush_pending) {
-                        tcp_wait();
-                        tcp_flush(flush_gc);
-                        flush_pending = false;
-                    }
-                    uint32_t a[32];
-                    tc_ld32(tc_base + tc_lane + 32 + 32 * tc_h, a);
-                    tc_wait_ld();
 #pragma unroll
-                    for (int q = 0; q < 2 * RM; ++q) v[2 + q] = __hiloint2double((int)a[2 * q + 1], (int)a[2 * q]);
-                } else {
-#pragma unroll
-                    for (int q = 0; q < 2 * RM; ++q) v[2 + q] = s_acc[q * kThreads + tid];
-                }
+                for (int q = 0; q < 2 * RM; ++q) v[2 + q] = s_acc[q * kThreads + tid];
                 block_sum_to<NS>(v, s_red, s_tot);
                 for (int j = tid; j < NS; j += kThreads) out[j] = s_tot[j];
                 const double inv_fix = ldexp(1.0, -fix.s);
@@ -940,18 +792,6 @@ fast_pass_kernel(const GroupHdr* __restrict__ hdr, const DevTensor* __restrict__
             for (int b = 0; b < 2; ++b)
                 if (((inflight >> b) & 1u) && !mbar_wait_bounded(full_bar(b), (ph >> b) & 1u, kStageWaitNs))
                     atomicOr(hdr->status, 2);
-        }
-    }
-    if constexpr (TCP) {  // after a give-up: the projection products in flight land before the TMEM is freed
-        if (abort && tid == 0) {
-            tc_commit(smem_u32(s_drainbar));
-            if (!mbar_wait_bounded(smem_u32(s_drainbar), 0, kTcWaitNs)) atomicOr(hdr->status, 2);
-        }
-        tc_fence_before();
-        __syncthreads();
-        if (warp == 0) {
-            tc_fence_after();
-            tc_dealloc(tc_base, kCols);
         }
     }
     if constexpr (TCR) {

@@ -131,11 +131,24 @@ class ZeroCRESSO5(CRESSO5):
     asynchronously (NCCL runs it on its own stream) and goes on with bucket
     k + 1, so the exchange of one bucket overlaps the compute of the next;
     the gathered values are copied into the parameters at the end of the step.
-    Every rank derives the same plan from the shapes alone."""
+    Every rank derives the same plan from the shapes alone.
 
-    def __init__(self, params: Iterable[Tensor], process_group=None, bucket_elements: int = 0, **kwargs):
+    With ``defer_gather=True`` the step only starts the all-gathers: each one is
+    finished when a parameter it carries is first needed.  ``prefetch_forward
+    (model)`` registers forward pre-hooks that finish, before a module runs, the
+    all-gathers of the buckets holding its parameters, so the exchange of the
+    later buckets runs under the first layers of the next forward.  Anything
+    else that reads the parameters first calls ``wait_params()``; the next
+    step() and gather_params() do so themselves."""
+
+    def __init__(self, params: Iterable[Tensor], process_group=None, bucket_elements: int = 0,
+                 defer_gather: bool = False, **kwargs):
         super().__init__(params, **kwargs)
         self.process_group = process_group
+        self.defer_gather = bool(defer_gather)
+        self._deferred: List[tuple] = []             # all-gathers started, not yet finished
+        self._deferred_of: Dict[int, List[int]] = {}  # id(param) -> indices into _deferred
+        self._hooks: list = []
         world = dist.get_world_size(process_group) if dist.is_initialized() else 1
         self.rank = dist.get_rank(process_group) if dist.is_initialized() else 0
         self.world = world
@@ -187,6 +200,7 @@ class ZeroCRESSO5(CRESSO5):
             for p, gr in hidden:
                 p.grad = gr
         spectral_devices: set = set()
+        self.wait_params()  # a deferred exchange of the previous step, if no forward finished it
         pending: list = []  # all-gathers of the previous bucket, still in flight
         for k, bucket in enumerate(self.buckets):
             mine = {id(p) for p in bucket[self.rank]}
@@ -195,6 +209,9 @@ class ZeroCRESSO5(CRESSO5):
                     self._run_routed(group, r, spectral_devices, select=mine, tag=("bucket", k))
             if self.world > 1:
                 started = self._gather_bucket_async(bucket)
+                if self.defer_gather:  # finished by the next forward (or wait_params)
+                    self._defer(started)
+                    continue
                 # the previous bucket's exchange ran while this bucket computed; its
                 # values go into the parameters now (at most two buckets in flight)
                 for item in pending:
@@ -241,6 +258,48 @@ class ZeroCRESSO5(CRESSO5):
                 p.detach().copy_(out[off:off + p.numel()].view_as(p))
                 off += p.numel()
 
+    def _defer(self, items: list) -> None:
+        for item in items:
+            idx = len(self._deferred)
+            self._deferred.append(item)
+            for r, ps in enumerate(item[0]):
+                if r == self.rank:
+                    continue
+                for p in ps:
+                    self._deferred_of.setdefault(id(p), []).append(idx)
+
+    def wait_params(self, params: Optional[Iterable[Tensor]] = None) -> None:
+        """Finishes the deferred all-gathers carrying `params` (all of them by
+        default), in the order they were started, and copies the gathered values
+        into the parameters (stream-ordered: the current stream waits for NCCL,
+        the host does not)."""
+        if not self._deferred_of:
+            return
+        if params is None:
+            wanted = range(len(self._deferred))
+        else:
+            wanted = sorted({i for p in params for i in self._deferred_of.get(id(p), ())})
+        for i in wanted:
+            item = self._deferred[i]
+            if item is None:
+                continue
+            self._finish_gather(item)
+            self._deferred[i] = None
+        if all(item is None for item in self._deferred):
+            self._deferred.clear()
+            self._deferred_of.clear()
+
+    def prefetch_forward(self, model: torch.nn.Module) -> None:
+        """Registers on every submodule that directly owns parameters of this
+        optimizer a forward pre-hook finishing the deferred all-gathers of those
+        parameters (a no-op once they are finished)."""
+        mine = {id(p) for g in self.param_groups for p in g["params"]}
+        for module in model.modules():
+            own = [p for p in module.parameters(recurse=False) if id(p) in mine]
+            if own:
+                self._hooks.append(module.register_forward_pre_hook(
+                    lambda mod, args, own=own: self.wait_params(own)))
+
     def consolidate_state_dict(self, to: int = 0) -> Optional[dict]:
         """The optimizer state of all ranks (each holds the state of the tensors it
         owns) as one ``state_dict`` in the reference layout, on rank ``to``; the
@@ -263,6 +322,7 @@ class ZeroCRESSO5(CRESSO5):
     @torch.no_grad()
     def gather_params(self) -> None:
         """All-gathers every rank's owned parameters into all ranks, bucket by bucket."""
+        self.wait_params()
         pending = []
         for bucket in self.buckets:
             pending.extend(self._gather_bucket_async(bucket))

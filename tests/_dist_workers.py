@@ -225,3 +225,65 @@ def status_exchange_worker(rank, world, port, outdir):
     with open(os.path.join(outdir, f"status_{rank}.txt"), "w") as f:
         f.write(f"{before}\n{after}\n{raised}\n")
     dist.destroy_process_group()
+
+
+def zero_deferred_gather_worker(rank, world, port, outdir):
+    """Deferred ZeRO-1 all-gathers finished by forward pre-hooks (gloo, CPU): the
+    parameters another rank owns stay stale until a module using them runs."""
+    from cresso_b200.distributed import ZeroCRESSO5
+
+    _init(rank, world, port, "gloo")
+    torch.manual_seed(0)
+    model = torch.nn.Sequential(torch.nn.Linear(4, 5), torch.nn.Linear(5, 3))
+    for p in model.parameters():
+        p.data.fill_(-1.0)
+    # one tensor per bucket: bucket 0 holds both tensors of the first layer (the LPT
+    # partition gives rank 0 the weight and rank 1 the bias), bucket 1 the second layer's
+    opt = ZeroCRESSO5(list(model.parameters()), defer_gather=True, bucket_elements=1)
+    opt.prefetch_forward(model)
+    ps = list(model.parameters())
+    for i, p in enumerate(ps):
+        if opt.owner[p] == rank:
+            p.data.fill_(float(10 * i + 1))
+    for bucket in opt.buckets:  # what a deferred step does after its compute
+        opt._defer(opt._gather_bucket_async(bucket))
+    stale_before = [bool(torch.all(p == -1.0)) for p in ps]
+    model[0](torch.zeros(2, 4))  # the first layer only: its parameters are finished
+    after_first = [bool(torch.all(p == float(10 * i + 1))) for i, p in enumerate(ps)]
+    opt.wait_params()
+    after_all = [bool(torch.all(p == float(10 * i + 1))) for i, p in enumerate(ps)]
+    torch.save({"owner": [opt.owner[p] for p in ps], "stale_before": stale_before, "after_first": after_first,
+                "after_all": after_all}, os.path.join(outdir, f"zdefer_{rank}.pt"))
+    dist.destroy_process_group()
+
+
+def gpu_zero_deferred_worker(rank, world, port, outdir):
+    """A small model trained three steps with deferred, forward-finished ZeRO-1
+    all-gathers against the same training with gathers finished in the step."""
+    from cresso_b200.distributed import ZeroCRESSO5
+
+    torch.cuda.set_device(rank)
+    _init(rank, world, port, "nccl", timeout_s=120)
+    dev = torch.device("cuda", rank)
+    outs = []
+    for defer in (False, True):
+        torch.manual_seed(3)
+        model = torch.nn.Sequential(torch.nn.Linear(256, 512), torch.nn.GELU(), torch.nn.Linear(512, 256),
+                                    torch.nn.GELU(), torch.nn.Linear(256, 64)).to(dev)
+        opt = ZeroCRESSO5(list(model.parameters()), defer_gather=defer, bucket_elements=50000, rank=8,
+                          hash_bins=64, hash_tables=2)
+        if defer:
+            opt.prefetch_forward(model)
+        g = torch.Generator(device=dev).manual_seed(7)
+        for _ in range(3):
+            x = torch.randn(32, 256, device=dev, generator=g)
+            loss = model(x).square().mean()
+            model.zero_grad()
+            loss.backward()
+            opt.step()
+        opt.wait_params()
+        torch.cuda.synchronize()
+        outs.append([p.detach().cpu().clone() for p in model.parameters()])
+    torch.save({"plain": outs[0], "deferred": outs[1]}, os.path.join(outdir, f"gpu_zdefer_{rank}.pt"))
+    dist.barrier()
+    dist.destroy_process_group()

@@ -52,6 +52,18 @@ def test_device_failure_report_reaches_every_rank_gloo(tmp_path):
         assert "bounded wait" in r[2]  # and every rank's check raises
 
 
+def test_zero_deferred_gather_finished_by_forward_hooks_gloo(tmp_path):
+    spawn(W.zero_deferred_gather_worker, 2, tmp_path)
+    for r in range(2):
+        d = torch.load(tmp_path / f"zdefer_{r}.pt")
+        for i, own in enumerate(d["owner"]):
+            mine = own == r
+            assert d["stale_before"][i] == (not mine)  # another rank's tensor waits for its gather
+            first_layer = i < 2  # the weight and bias of model[0]
+            assert d["after_first"][i] == (mine or first_layer)
+            assert d["after_all"][i]
+
+
 def test_row_sharded_stage_orchestration_gloo(tmp_path):
     spawn(W.stages_worker, 2, tmp_path)
     r0 = torch.load(tmp_path / "stages_0.pt")
@@ -145,3 +157,17 @@ def test_zero_bucketed_step_matches_single_gpu(tmp_path):
         assert torch.equal(a, b), i  # every rank ends with the owner's values
         rel = float((a.double() - full.double()).pow(2).mean().sqrt() / full.double().pow(2).mean().sqrt())
         assert rel <= 1e-6, (i, rel)
+
+
+@pytest.mark.gpu
+def test_zero_deferred_gather_matches_in_step_gather(tmp_path):
+    """ZeRO-1 all-gathers left in flight by the step and finished by forward
+    pre-hooks of the next forward: three training steps of a small model give the
+    same parameters, bit for bit, as gathers finished inside the step."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    spawn(W.gpu_zero_deferred_worker, 2, tmp_path)
+    for k in range(2):
+        r = torch.load(tmp_path / f"gpu_zdefer_{k}.pt")
+        for a, b in zip(r["plain"], r["deferred"]):
+            assert torch.equal(a, b)
