@@ -90,11 +90,44 @@ def exchange_status(opt: CRESSO5, group=None) -> None:
 
 
 class RowShardedCRESSO5(CRESSO5):
-    """CRESSO5 over row-sharded tensors with one float64 all-reduce per pass."""
+    """CRESSO5 over row-sharded tensors with one float64 all-reduce per pass.
 
-    def __init__(self, params: Iterable[Tensor], process_group=None, **kwargs):
+    With ``pipeline_exchange`` (the default) a spectral group of two or more
+    tensors is stepped as two halves of about equal size: each half's
+    all-reduce runs (on NCCL's stream) while the other half computes its next
+    pass, so the exchange between passes leaves the compute stream's critical
+    path.  Every rank takes the same halves and collectives in the same order."""
+
+    def __init__(self, params: Iterable[Tensor], process_group=None, pipeline_exchange: bool = True, **kwargs):
         super().__init__(params, **kwargs)
         self.process_group = process_group
+        self.pipeline_exchange = bool(pipeline_exchange)
+
+    def _run_spectral(self, group: dict, hp, device, items: list, tag=None) -> None:
+        if not self.pipeline_exchange or self._world() == 1 or len(items) < 2:
+            super()._run_spectral(group, hp, device, items, tag)
+            return
+        sizes = [p.numel() for p, _, _ in items]
+        total, acc, cut = sum(sizes), 0, 1
+        for i, n in enumerate(sizes[:-1]):
+            acc += n
+            cut = i + 1
+            if 2 * acc >= total:
+                break
+        halves = [items[:cut], items[cut:]]
+        setups = [self._spectral_setup(group, hp, device, h, (tag, i), "spectral" if i == 0 else "spectral_b")
+                  for i, h in enumerate(halves)]
+        bounds = (0,) + tuple(_lib.REDUCTION_BOUNDARIES) + (_lib.SPECTRAL_STAGES,)
+        works = [None, None]
+        for k in range(len(bounds) - 1):
+            for i, (run, scratch, layout) in enumerate(setups):
+                if works[i] is not None:
+                    works[i].wait()  # the compute stream waits for this half's exchange
+                run(bounds[k], bounds[k + 1])
+                works[i] = None
+                if k + 1 < len(bounds) - 1:
+                    works[i] = dist.all_reduce(self._reduction_view(scratch, layout, k + 1), op=dist.ReduceOp.SUM,
+                                               group=self.process_group, async_op=True)
 
     @torch.no_grad()
     def step(self, closure=None):  # type: ignore[override]

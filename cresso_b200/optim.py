@@ -651,6 +651,13 @@ class CRESSO5(Optimizer):
         return descs, keep
 
     def _run_spectral(self, group: dict, hp: np.ndarray, device, items: list, tag=None) -> None:
+        run, scratch, layout = self._spectral_setup(group, hp, device, items, tag)
+        self._spectral_stages(run, scratch, layout)
+
+    def _spectral_setup(self, group: dict, hp: np.ndarray, device, items: list, tag=None,
+                        scratch_kind: str = "spectral"):
+        """Descriptor table, scratch and layout of a spectral group; returns
+        (run(begin, end) launching a stage range, scratch, layout)."""
         if int(group["rank"]) > _lib.MAX_RANK:  # float16 / bfloat16 tensors on the fused path
             raise RuntimeError(f"CRESSO5 B200 path supports rank <= {_lib.MAX_RANK} for float16 / bfloat16 "
                                f"spectral tensors (got {group['rank']}); float32 and float64 take up to "
@@ -664,7 +671,7 @@ class CRESSO5(Optimizer):
         layout = np.zeros(10, dtype=np.int64)
         _lib.check(L.cresso_spectral_layout(_lib.ptr(descs), n, _lib.ptr(hp), num_sms,
                                             layout.ctypes.data_as(_lib._pi64), 10), "spectral_layout")
-        scratch = self._scratch_buffer(device, "spectral", int(layout[0]))
+        scratch = self._scratch_buffer(device, scratch_kind, int(layout[0]))
         status = self._status_word(device)
         stream = torch.cuda.current_stream(device).cuda_stream
 
@@ -673,7 +680,7 @@ class CRESSO5(Optimizer):
                                                     scratch.numel(), begin, end, num_sms, _lib.ptr(status), stream),
                        "spectral_run")
 
-        self._spectral_stages(run, scratch, layout)
+        return run, scratch, layout
 
     def _run_spectral64(self, group: dict, hp: np.ndarray, device, items: list) -> None:
         """Float64 spectral tensors and float32 ones of rank > 16: the float64-arithmetic
