@@ -46,6 +46,7 @@ stages (`reduce_finalize_ms`) per step.
 from __future__ import annotations
 
 import argparse
+import gc
 import json
 import math
 import os
@@ -425,6 +426,7 @@ def make_inputs(name, args, world, rank, device, zero):
 def time_steps(opt, steps, device, stream, world):
     """Device time of exactly `steps` steps (CUDA events, barrier and synchronize on
     both sides, max over ranks), in ms per step."""
+    gc.collect()  # no collection of an earlier workload's objects inside the timed steps
     barrier(world)
     torch.cuda.synchronize(device)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -811,6 +813,7 @@ def time_e2e(opt, params, grads_dev, args, world, device, stream, n_total, bpe=B
     copy_in(0)
     run(max(1, args.warmup))
     torch.cuda.synchronize(device)
+    gc.collect()
     barrier(world)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)

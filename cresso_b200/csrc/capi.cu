@@ -92,9 +92,24 @@ int check_launch(const char* what) {
     return set_error(CRESSO_ECUDA, "launch of %s failed: %s (%s)", what, cudaGetErrorName(e), cudaGetErrorString(e));
 }
 
+// Copies the device status word into a host word the device can write (pinned
+// host memory under unified addressing) from a kernel: a posted write over the
+// bus, so the copy never queues on a copy engine behind the caller's transfers.
+__global__ void status_copy_kernel(const int32_t* __restrict__ word, volatile int32_t* host_word) {
+    *host_word = *word;
+}
+
 }  // namespace cresso
 
 extern "C" {
+
+int cresso_status_copy(const void* status_word, void* host_word, cresso_stream_t stream) {
+    CRESSO_REQUIRE(status_word != nullptr && host_word != nullptr, CRESSO_EINVAL, "status_copy: NULL word");
+    cresso::status_copy_kernel<<<1, 1, 0, (cudaStream_t)stream>>>(reinterpret_cast<const int32_t*>(status_word),
+                                                                  reinterpret_cast<volatile int32_t*>(host_word));
+    CRESSO_LAUNCHED("status_copy_kernel");
+    return CRESSO_OK;
+}
 
 const char* cresso_version(void) { return "cresso_b200 0.1.0 (CRESSO5 step, abi 1)"; }
 

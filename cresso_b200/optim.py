@@ -463,8 +463,12 @@ class CRESSO5(Optimizer):
                 entry = self._status_host[device] = (torch.zeros(1, dtype=torch.int32, pin_memory=True),
                                                      torch.cuda.Event())
             host, ev = entry
-            host.copy_(word, non_blocking=True)
-            ev.record(torch.cuda.current_stream(device))
+            stream = torch.cuda.current_stream(device)
+            # a kernel writes the pinned word (no copy engine: a copy could queue behind
+            # the caller's prefetch of the next step's gradients)
+            _lib.check(_lib.lib().cresso_status_copy(_lib.ptr(word), _lib.ptr(host), stream.cuda_stream),
+                       "status_copy")
+            ev.record(stream)
 
     def check_device_status(self, block: bool = True) -> None:
         """Raises RuntimeError if a spectral kernel of an earlier step reported a

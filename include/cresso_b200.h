@@ -231,6 +231,11 @@ CRESSO_API int cresso_spectral_run_status(const cresso_tensor_desc* descs, int64
                                           void* scratch, int64_t scratch_bytes, int64_t stage_begin,
                                           int64_t stage_end, int64_t num_sms, void* status_word,
                                           cresso_stream_t stream);
+/* Stream-ordered copy of a device status word into host memory the device can
+ * write (pinned host memory under unified addressing), by a one-thread kernel
+ * rather than a copy engine, so that it never waits behind the caller's own
+ * host-device transfers (no counterpart in the reference). */
+CRESSO_API int cresso_status_copy(const void* status_word, void* host_word, cresso_stream_t stream);
 
 /* Float64 parameters on the spectral route (cresso_v5.py:945-1353 with the
  * float64 work and state of cresso_v5.py:119-124).  The shape workspace holds
