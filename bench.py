@@ -706,7 +706,8 @@ def time_passes(opt, args, world, device, stream):
     exchange = isinstance(opt, RowShardedCRESSO5) and world > 1  # row sharding all-reduces between passes
     acc = {k: 0.0 for k in PASS_STAGE}
     acc["SCALAR"] = 0.0
-    other = {"reduce_finalize_ms": 0.0, "exchange_ms": 0.0}
+    other = {"reduce_finalize_ms": 0.0}
+    last = {}
     reps = max(1, min(args.steps, 3))
     orig = opt._spectral_stages
     orig_scalar = opt._run_scalar
@@ -733,8 +734,8 @@ def time_passes(opt, args, world, device, stream):
             timed(name if name is not None else "reduce_finalize_ms", lambda st=st: run(st, st + 1))
             if st + 1 in bounds and exchange:
                 k += 1
-                view = opt._reduction_view(scratch, layout, k)
-                timed("exchange_ms", lambda view=view: dist.all_reduce(view, group=opt.process_group))
+                dist.all_reduce(opt._reduction_view(scratch, layout, k), group=opt.process_group)
+        last["scratch"], last["layout"] = scratch, layout
 
     opt._spectral_stages = instrumented
     opt._run_scalar = scalar_timed
@@ -757,6 +758,23 @@ def time_passes(opt, args, world, device, stream):
         if pipelined:
             opt.pipeline_exchange = True
     extra = {k: max_over_ranks(v / reps, world, device) for k, v in other.items() if v > 0.0}
+    if exchange and last:
+        # the four float64 all-reduces of a step on their own, after a barrier (the
+        # in-step time would include one rank waiting for the other's pass)
+        views = [opt._reduction_view(last["scratch"], last["layout"], k) for k in range(1, 5)]
+        ex = 0.0
+        for _ in range(reps):
+            torch.cuda.synchronize(device)
+            barrier(world)
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            for v in views:
+                dist.all_reduce(v, group=opt.process_group)
+            b.record(stream)
+            torch.cuda.synchronize(device)
+            ex += a.elapsed_time(b)
+        extra["exchange_ms"] = max_over_ranks(ex / reps, world, device)
+        extra["exchange_bytes"] = int(sum(v.numel() * 8 for v in views))
     return {k: v / reps for k, v in acc.items() if v > 0.0}, extra
 
 

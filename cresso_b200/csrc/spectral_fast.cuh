@@ -163,11 +163,11 @@ struct FastCfg {
     static constexpr bool kBins = PASS == 2 || PASS == 3;
     static constexpr bool kJoint = PASS >= 3;                            // joint lookup table in shared memory
     static constexpr bool kStore = PASS == 3 || PASS == 5;               // the tile goes back to HBM
-    static constexpr int kCopies = PASS == 3 ? 8 : 16;                   // fixed-point bin copies
-    // P3 keeps a barrier at the top of every item (its shared memory has no room for a
-    // second set of bin copies); the other passes wait on the stage and product
-    // barriers thread by thread and synchronise the block once per item, at its end
-    static constexpr bool kTopBar = PASS == 3;
+    // fixed-point bin copies per set (P3: two sets of 4 fit its shared memory, 113 KB)
+    static constexpr int kCopies = PASS == 3 ? 4 : 16;
+    // every pass waits on the stage and product barriers thread by thread and
+    // synchronises the block once per item, at its end
+    static constexpr bool kTopBar = false;
     static constexpr int kBinSets = kBins && !kTopBar ? 2 : 1;           // bin copies alternate by item
     static constexpr int kAcc = PASS == 4 ? kWarps * 32 : (kBins ? 2 * kRM * kThreads : 0);
 };
@@ -179,14 +179,15 @@ __host__ __device__ inline size_t fast_smem_layout(int pass, int tb, size_t* off
     const int xb = 16 * 256 * 4, jb = 16 * 256 * 2, rtb = pass <= 3 ? 16 * 16 * 4 : 0, pb = pass == 5 ? xb : 0;
     const size_t stage = (size_t)(xb + jb + rtb + pb);
     const bool bins = pass == 2 || pass == 3;
-    const int copies = pass == 3 ? 8 : 16;
-    const int sets = pass == 2 ? 2 : 1;
+    const int copies = pass == 3 ? 4 : 16;
+    const int sets = bins ? 2 : 1;
     const size_t acc = pass == 4 ? kWarps * 32 : (bins ? 2 * 8 * kThreads : 0);
     size_t o = 0;
     off[0] = o; o += 2 * stage;
     off[1] = o; o += 64;                                   // full[2], tc and drain barriers, TMEM slot, flags
-    off[2] = o; o += (size_t)kNSRec * kWarps * 8;
-    off[3] = o; o += (size_t)kNSRec * 8;
+    // s_red / s_tot: only the segment flush uses them; P3-P5 lay them over the joint table
+    off[2] = o; o += pass >= 3 ? 0 : (size_t)kNSRec * kWarps * 8;
+    off[3] = o; o += pass >= 3 ? 0 : (size_t)kNSRec * 8;
     off[4] = o; o += acc * 8;
     off[5] = o; o += (4 * 8 + 4) * 4;
     off[6] = o; o += bins ? (size_t)sets * copies * (tb + 1) * 4 : 0;
@@ -194,7 +195,7 @@ __host__ __device__ inline size_t fast_smem_layout(int pass, int tb, size_t* off
     off[7] = o; o += bins ? (size_t)tb * 8 : 0;
     off[8] = o; o += bins ? (size_t)tb * 4 : 0;
     off[9] = o; o += pass >= 3 ? 4096 * 4 : 0;
-    off[10] = o; o += pass == 2 ? 2 * 16 * kWarps * 4 : (pass == 3 ? 16 * 4 : 0);
+    off[10] = o; o += pass == 2 ? 2 * 16 * kWarps * 4 : (pass == 3 ? 2 * 16 * 4 : 0);
     o = (o + 127) & ~(size_t)127;
     off[11] = o; o += pass >= 3 ? 4 * kTcTileBytes + 128 : 0;  // + slack to align the tiles to 128 bytes
     off[12] = o;
@@ -233,8 +234,8 @@ fast_pass_kernel(const GroupHdr* __restrict__ hdr, const DevTensor* __restrict__
     uint32_t* s_tcslot = reinterpret_cast<uint32_t*>(s_full + 4);
     int* s_flag = reinterpret_cast<int*>(s_tcslot + 1);
     int* s_abort = s_flag + 1;
-    double* s_red = reinterpret_cast<double*>(smem_raw + off[2]);
-    double* s_tot = reinterpret_cast<double*>(smem_raw + off[3]);
+    double* s_red = reinterpret_cast<double*>(smem_raw + (PASS >= 3 ? off[9] : off[2]));
+    double* s_tot = s_red + kNSRec * kWarps;
     double* s_acc = reinterpret_cast<double*>(smem_raw + off[4]);
     float* s_coef = reinterpret_cast<float*>(smem_raw + off[5]);
     int* s_ibin = reinterpret_cast<int*>(smem_raw + off[6]);
@@ -396,6 +397,9 @@ fast_pass_kernel(const GroupHdr* __restrict__ hdr, const DevTensor* __restrict__
         int ct = (int)((it - ibase) / n_bands);
         int band = (int)((it - ibase) - (int64_t)ct * n_bands);
         if (warp == 0) stage(ct, band, buf);
+        if constexpr (PASS == 3) {  // the first item's instant-metric row factors (the prologue barrier follows)
+            if (tid < ITERS) s_rows[ip * ITERS + tid] = Dp->rowf[band * ITERS + tid];
+        }
         int items_since_flush = 0;
         float colf = 1.0f;
         int uv_ct = -1;
@@ -515,7 +519,9 @@ fast_pass_kernel(const GroupHdr* __restrict__ hdr, const DevTensor* __restrict__
                     uv_ct = ct;
                     if (flags & F_INST2D) colf = Dp->colf[col];
                 }
-                if (tid < ITERS) s_rows[tid] = Dp->rowf[rbase + tid];
+                // the next item's instant-metric row factors into the other buffer (read after
+                // this item's end barrier); the first item's were loaded before the item loop
+                if (has_next && tid < ITERS) s_rows[(ip ^ 1) * ITERS + tid] = Dp->rowf[nband * ITERS + tid];
             }
             if constexpr (TCR) {
                 tc_fence_after();
@@ -530,7 +536,7 @@ fast_pass_kernel(const GroupHdr* __restrict__ hdr, const DevTensor* __restrict__
                 }
                 if (it + 2 < seg_end) tc_bnext = tc_load_b(nband + 1 == n_bands ? 0 : nband + 1);
             }
-            if constexpr (PASS == 3) __syncthreads();  // s_rows written
+            const float* rowf_ip = s_rows + (PASS == 3 ? ip * ITERS : 0);
             float2 s02 = f2(0.0f), s12 = f2(0.0f), col2 = f2(0.0f);  // even / odd rows
 
 #pragma unroll
@@ -595,8 +601,8 @@ fast_pass_kernel(const GroupHdr* __restrict__ hdr, const DevTensor* __restrict__
                         const float2 metric = f2(clampf(__expf(e.x), 0.06f, 16.0f), clampf(__expf(e.y), 0.06f, 16.0f));
                         float2 den = __fmul2_rn(f2(scale), metric);
                         if (flags & F_INST2D)
-                            den = __fmul2_rn(den, f2(clampf(s_rows[m] * colf, 0.08f, 12.0f),
-                                                     clampf(s_rows[m + 1] * colf, 0.08f, 12.0f)));
+                            den = __fmul2_rn(den, f2(clampf(rowf_ip[m] * colf, 0.08f, 12.0f),
+                                                     clampf(rowf_ip[m + 1] * colf, 0.08f, 12.0f)));
                         const int j0 = jb[o], j1 = jb[o + 256];
                         den = __fmul2_rn(den, f2(s_joint[j0], s_joint[j1]));
                         const float2 de = __fadd2_rn(den, f2(eps));
