@@ -367,27 +367,41 @@ fast_pass_kernel(const GroupHdr* __restrict__ hdr, const DevTensor* __restrict__
         double acc0 = 0.0, acc1 = 0.0;
         const int lc = tid;  // this thread's column of the 256-column tile
 
-        // Stage item (ct, band) into buffer b: warp 0, lane 0 first waits until every
-        // store it issued has finished reading shared memory, then arms the barrier.
+        // Stage item (ct, band) into buffer b.  Every warp issues the copies of its two rows
+        // (lanes 0-1: the tile that goes back to HBM in P3 / P5, or the gradient / tangent;
+        // lanes 2-5: the other tiles), so no warp carries the whole item's copies; thread 0
+        // arms the stage barrier with the item's bytes.  Lanes 0-1 first wait until their
+        // own stores of that buffer's previous rows have been read.
         auto stage = [&](int ct_, int band_, int b) {
-            if (lane < 16) bulk_wait_read_all();  // this lane's stores have read their rows
-            __syncwarp();
-            if (lane == 0) {
+            if constexpr (Cfg::kStore) {
+                if (lane < 2) bulk_wait_read_all();
+                __syncwarp();
+            }
+            if (tid == 0) {
                 mbar_arrive_expect(full_bar(b), (uint32_t)Cfg::kStage);
                 inflight |= 1u << b;
             }
-            __syncwarp();
             const uint32_t sb = smem_u32(s_stage + (size_t)b * Cfg::kStage);
             const int64_t rb = (int64_t)band_ * ITERS, cb = (int64_t)ct_ * 256;
-            if (lane < 16) {
-                const int64_t r = rb + lane;
-                bulk_load(sb + lane * 1024, xsrc + r * cols + cb, 1024, full_bar(b));
-                bulk_load(sb + Cfg::kXB + lane * 512, joint + (row0 + r) * gcols + col0 + cb, 512, full_bar(b));
+            const int rr = 2 * warp + (lane & 1);  // this lane's row of the item
+            const int64_t r = rb + rr;
+            const int kind = lane >> 1;
+            constexpr int kPOff = Cfg::kXB + Cfg::kJB + Cfg::kRTB;
+            if (kind == 0) {
                 if constexpr (Cfg::kPB > 0)
-                    bulk_load(sb + Cfg::kXB + Cfg::kJB + Cfg::kRTB + lane * 1024, Dp->param + r * cols + cb, 1024,
-                              full_bar(b));
-            } else if (lane == 16 && Cfg::kRTB > 0) {
-                bulk_load(sb + Cfg::kXB + Cfg::kJB, rowtab + (row0 + rb) * 2 * RM, Cfg::kRTB, full_bar(b));
+                    bulk_load(sb + kPOff + rr * 1024, Dp->param + r * cols + cb, 1024, full_bar(b));
+                else
+                    bulk_load(sb + rr * 1024, xsrc + r * cols + cb, 1024, full_bar(b));
+            } else if (kind == 1) {
+                if constexpr (Cfg::kPB > 0)
+                    bulk_load(sb + rr * 1024, xsrc + r * cols + cb, 1024, full_bar(b));
+                else
+                    bulk_load(sb + Cfg::kXB + rr * 512, joint + (row0 + r) * gcols + col0 + cb, 512, full_bar(b));
+            } else if (kind == 2) {
+                if constexpr (Cfg::kPB > 0)
+                    bulk_load(sb + Cfg::kXB + rr * 512, joint + (row0 + r) * gcols + col0 + cb, 512, full_bar(b));
+                else if (Cfg::kRTB > 0 && warp == kWarps - 1 && lane == 4)
+                    bulk_load(sb + Cfg::kXB + Cfg::kJB, rowtab + (row0 + rb) * 2 * RM, Cfg::kRTB, full_bar(b));
             }
         };
 
@@ -396,7 +410,7 @@ fast_pass_kernel(const GroupHdr* __restrict__ hdr, const DevTensor* __restrict__
         for (int q = 0; q < (PASS == 4 ? kGram : 1); ++q) g2[q] = f2(0.0f);
         int ct = (int)((it - ibase) / n_bands);
         int band = (int)((it - ibase) - (int64_t)ct * n_bands);
-        if (warp == 0) stage(ct, band, buf);
+        stage(ct, band, buf);
         if constexpr (PASS == 3) {  // the first item's instant-metric row factors (the prologue barrier follows)
             if (tid < ITERS) s_rows[ip * ITERS + tid] = Dp->rowf[band * ITERS + tid];
         }
@@ -464,7 +478,7 @@ fast_pass_kernel(const GroupHdr* __restrict__ hdr, const DevTensor* __restrict__
             const int nband = band + 1 == n_bands ? 0 : band + 1;
             const int nct = band + 1 == n_bands ? ct + 1 : ct;
             const bool has_next = it + 1 < seg_end;
-            if (!Cfg::kStore && has_next && warp == 0) stage(nct, nband, buf ^ 1);
+            if (!Cfg::kStore && has_next) stage(nct, nband, buf ^ 1);
             if constexpr (Cfg::kTopBar) {
                 if (tid == 0) {
                     int fl = mbar_wait_bounded(full_bar(buf), (ph >> buf) & 1u, kStageWaitNs) ? 0 : 1;
@@ -541,7 +555,7 @@ fast_pass_kernel(const GroupHdr* __restrict__ hdr, const DevTensor* __restrict__
 
 #pragma unroll
             for (int m0 = 0; m0 < ITERS; m0 += UNR) {
-                if (Cfg::kStore && m0 == ITERS / 2 && has_next && warp == 0) stage(nct, nband, buf ^ 1);
+                if (Cfg::kStore && m0 == ITERS / 2 && has_next) stage(nct, nband, buf ^ 1);
                 float R1[UNR], R2[UNR];
                 if constexpr (TCR) {
                     const uint32_t ta = tc_base + tc_lane + 128 + 64 * tcb + 16 * tc_h + m0;
@@ -735,10 +749,11 @@ fast_pass_kernel(const GroupHdr* __restrict__ hdr, const DevTensor* __restrict__
                     Dp->rowpart[(int64_t)ct * rows + rbase + tid] = s;
                 }
             }
-            if constexpr (Cfg::kStore) {  // one row per lane of warp 0, each lane its own bulk group
-                if (warp == 0 && lane < ITERS) {
+            if constexpr (Cfg::kStore) {  // two rows per warp, each storing lane its own bulk group
+                if (lane < 2) {  // this warp's two rows, by the lanes that load them
+                    const int rr = 2 * warp + lane;
                     const uint32_t src = smem_u32(PASS == 3 ? (const void*)xb : (const void*)pb);
-                    bulk_store(xdst + (int64_t)(rbase + lane) * cols + (int64_t)ct * 256, src + lane * 1024, 1024);
+                    bulk_store(xdst + (int64_t)(rbase + rr) * cols + (int64_t)ct * 256, src + rr * 1024, 1024);
                     bulk_commit();
                 }
             }
@@ -792,7 +807,7 @@ fast_pass_kernel(const GroupHdr* __restrict__ hdr, const DevTensor* __restrict__
     }
 
     // ---- drain: stores complete, loads in flight landed, TMEM freed
-    if (warp == 0 && lane < 16) bulk_wait_all();
+    if (lane < 2) bulk_wait_all();
     if (tid == 0) {
         if (abort) {
             for (int b = 0; b < 2; ++b)
