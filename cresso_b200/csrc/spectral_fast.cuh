@@ -363,24 +363,29 @@ fast_pass_kernel(const GroupHdr* __restrict__ hdr, const DevTensor* __restrict__
         if constexpr (Cfg::kAcc > 0) {
             for (int j = tid; j < Cfg::kAcc; j += kThreads) s_acc[j] = 0.0;
         }
+        // arm the stage barriers of the segment's first two items (the barrier below orders the
+        // arming before their copies; every thread has consumed both barriers' earlier phases)
+        auto arm_stage = [&](int b) {
+            if (tid == 0) mbar_arrive_expect(full_bar(b), (uint32_t)Cfg::kStage);
+        };
+        arm_stage(buf);
+        if (it + 1 < seg_end) arm_stage(buf ^ 1);
         __syncthreads();
         double acc0 = 0.0, acc1 = 0.0;
         const int lc = tid;  // this thread's column of the 256-column tile
 
         // Stage item (ct, band) into buffer b.  Every warp issues the copies of its two rows
         // (lanes 0-1: the tile that goes back to HBM in P3 / P5, or the gradient / tangent;
-        // lanes 2-5: the other tiles), so no warp carries the whole item's copies; thread 0
-        // arms the stage barrier with the item's bytes.  Lanes 0-1 first wait until their
+        // lanes 2-5: the other tiles), so no warp carries the whole item's copies.  The stage
+        // barrier was armed with the item's bytes by thread 0 before a block barrier that
+        // precedes every one of these copies (arm_stage).  Lanes 0-1 first wait until their
         // own stores of that buffer's previous rows have been read.
         auto stage = [&](int ct_, int band_, int b) {
             if constexpr (Cfg::kStore) {
                 if (lane < 2) bulk_wait_read_all();
                 __syncwarp();
             }
-            if (tid == 0) {
-                mbar_arrive_expect(full_bar(b), (uint32_t)Cfg::kStage);
-                inflight |= 1u << b;
-            }
+            if (tid == 0) inflight |= 1u << b;
             const uint32_t sb = smem_u32(s_stage + (size_t)b * Cfg::kStage);
             const int64_t rb = (int64_t)band_ * ITERS, cb = (int64_t)ct_ * 256;
             const int rr = 2 * warp + (lane & 1);  // this lane's row of the item
@@ -728,6 +733,9 @@ fast_pass_kernel(const GroupHdr* __restrict__ hdr, const DevTensor* __restrict__
                 }
             }
             if constexpr (PASS == 2) Dp->colpart[(int64_t)band * cols + col] = col2.x + col2.y;
+            // the buffer of this item is next staged with item i + 2: arm its barrier now, before
+            // the end barrier that precedes those copies (every thread consumed this item's phase)
+            if (it + 2 < seg_end) arm_stage(buf);
             if constexpr (Cfg::kStore) tc_fence_smem();  // this thread's tile writes, before the bulk store
             if constexpr (TCR) {  // item i + 2's carrier rows into this item's B buffer (its products are done)
                 if (it + 2 < seg_end) {
