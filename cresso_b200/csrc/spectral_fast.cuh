@@ -166,9 +166,8 @@ struct FastCfg {
     // fixed-point bin copies per set (P3: two sets of 4 fit its shared memory, 113 KB)
     static constexpr int kCopies = PASS == 3 ? 4 : 16;
     // every pass waits on the stage and product barriers thread by thread and
-    // synchronises the block once per item, at its end
-    static constexpr bool kTopBar = false;
-    static constexpr int kBinSets = kBins && !kTopBar ? 2 : 1;           // bin copies alternate by item
+    // synchronises the block once per item, at its end; the bin copies alternate by item
+    static constexpr int kBinSets = kBins ? 2 : 1;
     static constexpr int kAcc = PASS == 4 ? kWarps * 32 : (kBins ? 2 * kRM * kThreads : 0);
 };
 
@@ -229,9 +228,12 @@ fast_pass_kernel(const GroupHdr* __restrict__ hdr, const DevTensor* __restrict__
     fast_smem_layout(PASS, TB, off);
     unsigned char* s_stage = smem_raw + off[0];
     uint64_t* s_full = reinterpret_cast<uint64_t*>(smem_raw + off[1]);  // [0], [1]: stage barriers
-    uint64_t* s_tcbar = s_full + 2;
-    uint64_t* s_drainbar = s_full + 3;
-    uint32_t* s_tcslot = reinterpret_cast<uint32_t*>(s_full + 4);
+    // one product barrier per D buffer: the products of item i + 1 (issued while slower
+    // threads may still test item i's) complete the other buffer's barrier, so no barrier
+    // runs two phases ahead of a thread that waits on it
+    uint64_t* s_tcbar = s_full + 2;  // [2]
+    uint64_t* s_drainbar = s_full + 4;
+    uint32_t* s_tcslot = reinterpret_cast<uint32_t*>(s_full + 5);
     int* s_flag = reinterpret_cast<int*>(s_tcslot + 1);
     int* s_abort = s_flag + 1;
     double* s_red = reinterpret_cast<double*>(smem_raw + (PASS >= 3 ? off[9] : off[2]));
@@ -248,12 +250,13 @@ fast_pass_kernel(const GroupHdr* __restrict__ hdr, const DevTensor* __restrict__
 
     const uint32_t full0 = smem_u32(&s_full[0]);
     auto full_bar = [&](int b) -> uint32_t { return full0 + 8u * (uint32_t)b; };
-    uint32_t tc_base = 0, tc_parity = 0;
+    uint32_t tc_base = 0, tc_parity = 0;  // tc_parity bit b: parity of the next completion of s_tcbar[b]
     if (tid == 0) {
         mbar_init(&s_full[0], 1);
         mbar_init(&s_full[1], 1);
         if constexpr (TCR) {
-            mbar_init(s_tcbar, 4);      // one arrival per issuing thread
+            mbar_init(&s_tcbar[0], 4);  // one arrival per issuing thread
+            mbar_init(&s_tcbar[1], 4);
             mbar_init(s_drainbar, 4);   // the same four threads, once, after a give-up
         }
         *s_abort = 0;
@@ -457,7 +460,7 @@ fast_pass_kernel(const GroupHdr* __restrict__ hdr, const DevTensor* __restrict__
                     tc_mma_tf32_ts(d, ahi + 8 * ks, tc_smem_desc(blo + bo), idesc, 1);
                     tc_mma_tf32_ts(d, alo + 8 * ks, tc_smem_desc(bhi + bo), idesc, 1);
                 }
-                tc_commit(smem_u32(s_tcbar));
+                tc_commit(smem_u32(&s_tcbar[bb]));
             }
         };
         float tc_bnext = 0.0f;
@@ -484,45 +487,23 @@ fast_pass_kernel(const GroupHdr* __restrict__ hdr, const DevTensor* __restrict__
             const int nct = band + 1 == n_bands ? ct + 1 : ct;
             const bool has_next = it + 1 < seg_end;
             if (!Cfg::kStore && has_next) stage(nct, nband, buf ^ 1);
-            if constexpr (Cfg::kTopBar) {
-                if (tid == 0) {
-                    int fl = mbar_wait_bounded(full_bar(buf), (ph >> buf) & 1u, kStageWaitNs) ? 0 : 1;
-                    if (!fl) inflight &= ~(1u << buf);
-                    if constexpr (TCR) {
-                        if (!fl && !mbar_wait_bounded(smem_u32(s_tcbar), tc_parity, kTcWaitNs)) fl = 2;
-                    }
-                    *s_flag = fl;
-                }
-                __syncthreads();
-                if (*s_flag) {  // a stage or a product never completed: stop this block (uniform)
-                    if (tid == 0) {
-                        atomicOr(hdr->status, 1);
-                        *s_abort = 1;
-                    }
-                    abort = true;
-                    break;
-                }
-                (void)mbar_test(full_bar(buf), (ph >> buf) & 1u);  // this thread's acquire of the completed stage
+            // every thread waits for the stage and its products itself; a wait that gives
+            // up marks the block, which stops at the end of this item (the item computes
+            // on whatever the buffers hold; nothing is read or written out of bounds)
+            bool ok = mbar_wait_quick(full_bar(buf), (ph >> buf) & 1u, kStageWaitNs);
+            if (ok) {
                 ph ^= 1u << buf;
-                if constexpr (TCR) tc_parity ^= 1;
-            } else {
-                // every thread waits for the stage and its products itself; a wait that gives
-                // up marks the block, which stops at the end of this item (the item computes
-                // on whatever the buffers hold; nothing is read or written out of bounds)
-                bool ok = mbar_wait_quick(full_bar(buf), (ph >> buf) & 1u, kStageWaitNs);
-                if (ok) {
-                    ph ^= 1u << buf;
-                    if (tid == 0) inflight &= ~(1u << buf);
-                }
-                if constexpr (TCR) {
-                    ok = mbar_wait_quick(smem_u32(s_tcbar), tc_parity, kTcWaitNs) && ok;
-                    tc_parity ^= 1;
-                }
-                if (!ok) {
-                    atomicOr(s_abort, 1);
-                    atomicOr(hdr->status, 1);
-                }
+                if (tid == 0) inflight &= ~(1u << buf);
             }
+            if constexpr (TCR) {
+                ok = mbar_wait_quick(smem_u32(&s_tcbar[tcb]), (tc_parity >> tcb) & 1u, kTcWaitNs) && ok;
+                tc_parity ^= 1u << tcb;
+            }
+            if (!ok) {
+                atomicOr(s_abort, 1);
+                atomicOr(hdr->status, 1);
+            }
+
             int* my_bins = s_ibin + (ip * ncopies + (tid & (ncopies - 1))) * cstride;
             float* rows_ip = s_rows + (PASS == 2 ? ip * ITERS * kWarps : 0);
             const unsigned char* sb = s_stage + (size_t)buf * Cfg::kStage;
