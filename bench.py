@@ -842,11 +842,26 @@ def time_e2e(opt, params, grads_dev, args, world, device, stream, n_total, bpe=B
     e1.record(stream)
     torch.cuda.synchronize(device)
     ms = max_over_ranks(e0.elapsed_time(e1) / args.steps, world, device)
+    # the copy bound: the same pinned host -> device gradient copy alone, on every rank at once
+    barrier(world)
+    c0, c1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    c0.record(copy_stream)
+    reps = 2
+    with torch.cuda.stream(copy_stream):
+        for _ in range(reps):
+            dev_flat[0].copy_(host_flat, non_blocking=True)
+    c1.record(copy_stream)
+    torch.cuda.synchronize(device)
+    copy_ms = max_over_ranks(c0.elapsed_time(c1) / reps, world, device)
     for p, g in zip(params, grads_dev):
         p.grad = g
     return {"value": bpe * n_total / (ms * 1e-3) / 1e9, "unit": "GB/s", "ms_per_step": ms,
             "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": out_host.numel() * 4,
-            "overlap": "step k+1's host->device gradient copy runs on a copy stream under step k"}
+            "overlap": "step k+1's host->device gradient copy runs on a copy stream under step k",
+            "copy_bound": {"ms": copy_ms, "gbs_per_rank": h2d / (copy_ms * 1e-3) / 1e9,
+                           "note": "the step's pinned host->device gradient copy timed alone, all ranks at "
+                                   "once (max over ranks): e2e ms_per_step cannot go below max(this, the "
+                                   "device step)"}}
 
 
 def main():

@@ -31,7 +31,7 @@ HPARAM_FIELDS = (
 
 MAX_NDIM = 8
 MAX_RANK = 16        # the fused float32 spectral path
-MAX_RANK_PLAIN = 32  # the float64-arithmetic spectral path (float64 tensors, float32 tensors of rank > 16)
+MAX_RANK_PLAIN = 64  # the float64-arithmetic spectral path (float64 tensors, any tensor of rank > 16)
 SPECTRAL_STAGES = 14
 # stage boundaries after which reduction vector k (1..4) is complete
 REDUCTION_BOUNDARIES = (3, 6, 9, 12)

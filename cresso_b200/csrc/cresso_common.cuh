@@ -15,7 +15,7 @@ namespace cresso {
 constexpr int kThreads = 256;  // every kernel of the library runs 256-thread blocks
 constexpr int kWarps = kThreads / 32;
 constexpr int kMaxRank = 16;       // the fused float32 spectral path
-constexpr int kMaxRankPlain = 32;  // the float64-arithmetic spectral path and its shape workspace
+constexpr int kMaxRankPlain = 64;  // the float64-arithmetic spectral path and its shape workspace
 constexpr int kMaxTB = 8192;   // hash_tables * hash_bins held in shared memory
 constexpr int kMaxBins = 4096; // same bound as the reference CUDA hash path (cresso_v5.py:1002)
 
@@ -130,7 +130,7 @@ __host__ inline ShapeWsHeader shape_ws64_layout(int64_t ndim, int64_t grows, int
 }
 
 __host__ __device__ inline int rank_pad(int64_t rank) {
-    return rank <= 4 ? 4 : (rank <= 8 ? 8 : (rank <= 16 ? 16 : 32));
+    return rank <= 4 ? 4 : (rank <= 8 ? 8 : (rank <= 16 ? 16 : (rank <= 32 ? 32 : 64)));
 }
 
 // ---------------------------------------------------------------------------

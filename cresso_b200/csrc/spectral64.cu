@@ -1,10 +1,13 @@
 // Spectral-route CRESSO5 step for float64 parameters (cresso_v5.py:945-1353
-// with float64 work and state, cresso_v5.py:119-124).
+// with float64 work and state, cresso_v5.py:119-124), and for float32 /
+// float16 / bfloat16 parameters of rank 17 to 64 (float32 state).
 //
 // The float32 path (spectral.cu) is built around float32 tiles, tf32 tensor-core
-// reconstructions and fixed-point bin sums; a float64 tensor instead runs this
-// plain float64 pipeline, one tensor after another, with the same five passes
-// and the same reductions between them:
+// reconstructions, fixed-point bin sums and at most 16 modes held in registers;
+// these tensors instead run this plain float64 pipeline (modes padded to 4, 8,
+// 16, 32 or 64), with the same five passes and the same reductions between
+// them, each pass one launch over the blocks of a whole group of tensors and
+// each finalize one launch of a block per tensor:
 //   P1 force energy | fin1 scale
 //   P2 density, hash-bin sums and counts, density projections
 //      (+ row sums / column sums of the instant-metric density, rank >= 2)
@@ -50,20 +53,21 @@ enum {
 };
 static_assert(sizeof(cresso_hparams) == Q_COUNT * sizeof(double), "cresso_hparams field order");
 
-// P: storage type of the parameter, gradient and state (double for float64
-// tensors, float for float32 tensors of rank > 16); the arithmetic is float64.
+// P: storage type of the state (double for float64 tensors, float for float32,
+// float16 and bfloat16 tensors of rank > 16); the arithmetic is float64.  The
+// parameter and gradient keep their own type, pdt (CRESSO_DTYPE_*).
 template <typename P>
-struct T64 {
+struct alignas(16) T64 {
     int64_t ndim, N, rows, cols, step;
     int64_t dims[CRESSO_MAX_NDIM];
-    P* param;
-    const P* grad;
+    void* param;
+    const void* grad;
     const double* rowtab;  // [rows][rm][2]
     const double* coltab;  // [2 rm][cols]
     const ModeStats* stats;
     P *omega, *q_cos, *q_sin, *p_cos, *p_sin, *m_cos, *m_sin, *mp_cos, *mp_sin, *ca_cos, *ca_sin, *conf;
     P *h_energy, *h_impulse, *h_refractory, *force_rms, *drive_energy, *surprise, *action;
-    int32_t R, T, B, hard, hash_on, echo_on, inst, local_on, f32, pad;
+    int32_t R, T, B, hard, hash_on, echo_on, inst, local_on, f32, pdt;
     double hp[64];
 };
 
@@ -76,7 +80,7 @@ struct C64 {
     double c[8], gain;                      // drive = sum c_i v_i
 };
 
-struct Buf64 {
+struct alignas(16) Buf64 {
     C64* cst;
     double* rec;     // [blocks][L]
     double* lterm;   // [T * B] per-bin log hash metric (P3)
@@ -85,32 +89,118 @@ struct Buf64 {
     double* rowsum;  // [rows] instant-metric density per row, then its log factor
     double* colsum;  // [cols] same per column
     double* tbuf;    // [N] tangent
-    int blocks;
+    int blocks;      // blocks of this tensor in the element passes (records in rec)
 };
+
+// The tensors of one launch group: per-tensor descriptors and buffers in device
+// memory, and for each launch kind the first block of every tensor (blk[n] is
+// the grid).  Every kernel first finds its tensor and copies the two records
+// into shared memory.
+template <typename P>
+struct G64 {
+    const T64<P>* ts;
+    const Buf64* bufs;
+    const int* blk;      // [n + 1] element passes
+    const int* blk_row;  // [n + 1] row sums of the instant-metric density
+    const int* blk_col;  // [n + 1] column sums
+    int n;
+};
+
+// Tensor t with blk[t] <= b < blk[t + 1] (blk ascending; empty ranges skipped).
+__device__ __forceinline__ int find_tensor(const int* blk, int n, int b) {
+    int lo = 0, hi = n - 1;
+    while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (__ldg(blk + mid) <= b)
+            lo = mid;
+        else
+            hi = mid - 1;
+    }
+    return lo;
+}
+
+// Every thread: tensor t's descriptor and buffers into shared memory.
+template <typename P>
+__device__ __forceinline__ void bind_tensor(const G64<P>& G, int t, T64<P>& sD, Buf64& sB) {
+    static_assert(sizeof(T64<P>) % 16 == 0 && sizeof(Buf64) % 16 == 0, "16-byte records");
+    const int4* d = reinterpret_cast<const int4*>(G.ts + t);
+    for (int i = threadIdx.x; i < (int)(sizeof(T64<P>) / 16); i += blockDim.x) reinterpret_cast<int4*>(&sD)[i] = d[i];
+    const int4* b = reinterpret_cast<const int4*>(G.bufs + t);
+    for (int i = threadIdx.x; i < (int)(sizeof(Buf64) / 16); i += blockDim.x) reinterpret_cast<int4*>(&sB)[i] = b[i];
+    __syncthreads();
+}
+
+// Prologue of a kernel over the blocks of a group: D / Bf are this block's
+// tensor, lb its block within the tensor, gb the tensor's blocks.
+#define S64_BIND_BLOCKS(BLK)                                     \
+    __shared__ T64<P> sD;                                        \
+    __shared__ Buf64 sB;                                         \
+    const int t_ = find_tensor(G.BLK, G.n, (int)blockIdx.x);     \
+    bind_tensor(G, t_, sD, sB);                                  \
+    const T64<P>& D = sD;                                        \
+    const Buf64& Bf = sB;                                        \
+    const int64_t lb = (int64_t)blockIdx.x - G.BLK[t_];          \
+    const int64_t gb = (int64_t)(G.BLK[t_ + 1] - G.BLK[t_]);     \
+    (void)lb;                                                    \
+    (void)gb
+
+// Prologue of a finalize kernel: one block per tensor.
+#define S64_BIND_TENSOR()                                        \
+    __shared__ T64<P> sD;                                        \
+    __shared__ Buf64 sB;                                         \
+    bind_tensor(G, (int)blockIdx.x, sD, sB);                     \
+    const T64<P>& D = sD;                                        \
+    const Buf64& Bf = sB
 
 __device__ __forceinline__ double clampd(double v, double lo, double hi) { return fmin(fmax(v, lo), hi); }
 __device__ __forceinline__ double sigmoidd(double x) { return 1.0 / (1.0 + exp(-x)); }
 __device__ __forceinline__ double sgnd(double x) { return x > 0.0 ? 1.0 : (x < 0.0 ? -1.0 : 0.0); }
 
+// Normalised carrier (cos, sin) of mode k at row r, column c.
+template <int RM, typename P>
+__device__ __forceinline__ void carrier(const T64<P>& D, int64_t r, int64_t c, int k, double& ch, double& sh) {
+    const double a1 = D.rowtab[(r * RM + k) * 2], a2 = D.rowtab[(r * RM + k) * 2 + 1];
+    const double b1 = D.coltab[(int64_t)(2 * k) * D.cols + c], b2 = D.coltab[(int64_t)(2 * k + 1) * D.cols + c];
+    double rc, rs;
+    if (mode_is_product(k)) {
+        rc = a1 * b1;
+        rs = a2 * b2;
+    } else {
+        rc = a1 * b1 - a2 * b2;
+        rs = a1 * b2 + a2 * b1;
+    }
+    const ModeStats& m = D.stats[k];
+    ch = (rc - m.mu_c) * m.inv_c;
+    sh = (rs - m.mu_s) * m.inv_s;
+}
+
 // Normalised carriers (cos, sin) of modes 0..RM-1 at row r, column c.
 template <int RM, typename P>
 __device__ __forceinline__ void carriers(const T64<P>& D, int64_t r, int64_t c, double (&ch)[RM], double (&sh)[RM]) {
 #pragma unroll
+    for (int k = 0; k < RM; ++k) carrier<RM>(D, r, c, k, ch[k], sh[k]);
+}
+
+// The prediction and (when echo) the echo reconstruction at row r, column c in
+// one sweep over the modes, each carrier formed once: the same sums, in the
+// same order, as recon() over stored carriers.
+template <int RM, typename P>
+__device__ __forceinline__ void recon_pred_echo(const T64<P>& D, const C64& C, int64_t r, int64_t c, bool echo,
+                                                double& pred, double& ech) {
+    double a = 0.0, b = 0.0;
+#pragma unroll(RM > 16 ? 8 : RM)
     for (int k = 0; k < RM; ++k) {
-        const double a1 = D.rowtab[(r * RM + k) * 2], a2 = D.rowtab[(r * RM + k) * 2 + 1];
-        const double b1 = D.coltab[(int64_t)(2 * k) * D.cols + c], b2 = D.coltab[(int64_t)(2 * k + 1) * D.cols + c];
-        double rc, rs;
-        if (mode_is_product(k)) {
-            rc = a1 * b1;
-            rs = a2 * b2;
-        } else {
-            rc = a1 * b1 - a2 * b2;
-            rs = a1 * b2 + a2 * b1;
+        double chk, shk;
+        carrier<RM>(D, r, c, k, chk, shk);
+        a += chk * C.p_al[k];
+        a += shk * C.p_be[k];
+        if (echo) {
+            b += chk * C.e_al[k];
+            b += shk * C.e_be[k];
         }
-        const ModeStats& m = D.stats[k];
-        ch[k] = (rc - m.mu_c) * m.inv_c;
-        sh[k] = (rs - m.mu_s) * m.inv_s;
     }
+    pred = a;
+    ech = echo ? b : 0.0;
 }
 
 template <int RM>
@@ -125,10 +215,16 @@ __device__ __forceinline__ double recon(const double* al, const double* be, cons
     return out;
 }
 
+// Parameter / gradient element e as float64 (every storage type converts exactly).
+__device__ __forceinline__ double load_pg(const void* p, int64_t e, int dt) {
+    if (dt == CRESSO_DTYPE_F64) return static_cast<const double*>(p)[e];
+    return (double)load_elem(p, e, dt);
+}
+
 template <typename P>
 __device__ __forceinline__ double force_of(const T64<P>& D, int64_t e) {
-    double f = (D.hp[Q_MAX] != 0.0 ? -1.0 : 1.0) * D.grad[e];
-    if (D.hp[Q_WD] != 0.0) f = f + D.hp[Q_WD] * D.param[e];
+    double f = (D.hp[Q_MAX] != 0.0 ? -1.0 : 1.0) * load_pg(D.grad, e, D.pdt);
+    if (D.hp[Q_WD] != 0.0) f = f + D.hp[Q_WD] * load_pg(D.param, e, D.pdt);
     return f;
 }
 
@@ -143,7 +239,7 @@ __device__ __forceinline__ double idens_of(const T64<P>& D, double rel) {
     return fmin(pow(fmax(rel, D.hp[Q_EPS]), pw), 1.0e6);
 }
 
-// Block sum of v[0..L) into rec[blockIdx.x * L ...]; every thread calls.
+// Block sum of v[0..L) into rec[0..L); every thread calls.
 template <int L>
 __device__ __forceinline__ void block_record(double (&v)[L], double* red, double* rec) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -162,18 +258,20 @@ __device__ __forceinline__ void block_record(double (&v)[L], double* red, double
 
 // ---- P1: force energy
 template <typename P>
-__global__ void __launch_bounds__(kThreads) s64_p1(T64<P> D, Buf64 Bf) {
+__global__ void __launch_bounds__(kThreads) s64_p1(G64<P> G) {
+    S64_BIND_BLOCKS(blk);
     __shared__ double red[kWarps];
     double v[1] = {0.0};
-    for (int64_t e = blockIdx.x * (int64_t)kThreads + threadIdx.x; e < D.N; e += (int64_t)gridDim.x * kThreads) {
+    for (int64_t e = lb * kThreads + threadIdx.x; e < D.N; e += gb * kThreads) {
         const double f = force_of(D, e);
         v[0] += f * f;
     }
-    block_record<1>(v, red, Bf.rec + (int64_t)blockIdx.x * 1);
+    block_record<1>(v, red, Bf.rec + lb * 1);
 }
 
 template <typename P>
-__global__ void s64_fin1(T64<P> D, Buf64 Bf) {
+__global__ void s64_fin1(G64<P> G) {
+    S64_BIND_TENSOR();
     if (threadIdx.x != 0) return;
     double s = 0.0;
     for (int b = 0; b < Bf.blocks; ++b) s += Bf.rec[b];
@@ -187,7 +285,8 @@ __global__ void s64_fin1(T64<P> D, Buf64 Bf) {
 // ---- P2: density, bins, projections.  Record: [sum L, sum dens, sum L c_k (RM), sum L s_k (RM),
 // bin sums (TB), bin counts (TB)]
 template <int RM, typename P>
-__global__ void __launch_bounds__(kThreads) s64_p2(T64<P> D, Buf64 Bf) {
+__global__ void __launch_bounds__(kThreads) s64_p2(G64<P> G) {
+    S64_BIND_BLOCKS(blk);
     __shared__ double red[kWarps];
     extern __shared__ double sbin[];  // [TB] sums, then [TB] counts
     const int TB = D.T * D.B;
@@ -199,7 +298,7 @@ __global__ void __launch_bounds__(kThreads) s64_p2(T64<P> D, Buf64 Bf) {
     double v[2 + 2 * RM];
 #pragma unroll
     for (int j = 0; j < 2 + 2 * RM; ++j) v[j] = 0.0;
-    for (int64_t e = blockIdx.x * (int64_t)kThreads + threadIdx.x; e < D.N; e += (int64_t)gridDim.x * kThreads) {
+    for (int64_t e = lb * kThreads + threadIdx.x; e < D.N; e += gb * kThreads) {
         const double rel = rel_of(D, scale, force_of(D, e));
         const double ds = pow(rel, ep);
         const double L = log1p(ds);
@@ -220,7 +319,7 @@ __global__ void __launch_bounds__(kThreads) s64_p2(T64<P> D, Buf64 Bf) {
             }
     }
     const int RL = 2 + 2 * RM + 2 * TB;
-    double* rec = Bf.rec + (int64_t)blockIdx.x * RL;
+    double* rec = Bf.rec + lb * RL;
     block_record<2 + 2 * RM>(v, red, rec);
     if (hash_on)
         for (int i = threadIdx.x; i < 2 * TB; i += kThreads) rec[2 + 2 * RM + i] = sbin[i];
@@ -228,10 +327,11 @@ __global__ void __launch_bounds__(kThreads) s64_p2(T64<P> D, Buf64 Bf) {
 
 // Row sums of the instant-metric density: one warp per row (rank >= 2).
 template <typename P>
-__global__ void __launch_bounds__(kThreads) s64_rowsum(T64<P> D, Buf64 Bf) {
+__global__ void __launch_bounds__(kThreads) s64_rowsum(G64<P> G) {
+    S64_BIND_BLOCKS(blk_row);
     const int lane = threadIdx.x & 31;
     const double scale = Bf.cst->scale;
-    for (int64_t r = blockIdx.x * (int64_t)kWarps + (threadIdx.x >> 5); r < D.rows; r += (int64_t)gridDim.x * kWarps) {
+    for (int64_t r = lb * kWarps + (threadIdx.x >> 5); r < D.rows; r += gb * kWarps) {
         double s = 0.0;
         for (int64_t c = lane; c < D.cols; c += 32) s += idens_of(D, rel_of(D, scale, force_of(D, r * D.cols + c)));
         s = warp_sum(s);
@@ -239,19 +339,29 @@ __global__ void __launch_bounds__(kThreads) s64_rowsum(T64<P> D, Buf64 Bf) {
     }
 }
 
-// Column sums of the instant-metric density: one thread per column (rank >= 2).
+// Column sums of the instant-metric density (rank >= 2), in col_chunks(rows)
+// row chunks: block (chunk, tile) sums its chunk of rows for the 256 columns of
+// its tile, one thread per column, into tbuf[chunk][cols] (the tangent field
+// is written only later, by P3); the finalize adds the chunks in order.
+__host__ __device__ inline int64_t col_chunks(int64_t rows) { return (rows + 31) / 32 < 64 ? (rows + 31) / 32 : 64; }
+
 template <typename P>
-__global__ void __launch_bounds__(kThreads) s64_colsum(T64<P> D, Buf64 Bf) {
+__global__ void __launch_bounds__(kThreads) s64_colsum(G64<P> G) {
+    S64_BIND_BLOCKS(blk_col);
     const double scale = Bf.cst->scale;
-    for (int64_t c = blockIdx.x * (int64_t)kThreads + threadIdx.x; c < D.cols; c += (int64_t)gridDim.x * kThreads) {
-        double s = 0.0;
-        for (int64_t r = 0; r < D.rows; ++r) s += idens_of(D, rel_of(D, scale, force_of(D, r * D.cols + c)));
-        Bf.colsum[c] = s;
-    }
+    const int64_t tiles = (D.cols + kThreads - 1) / kThreads, chunks = col_chunks(D.rows);
+    const int64_t per = (D.rows + chunks - 1) / chunks;
+    const int64_t chunk = lb / tiles, c = (lb % tiles) * kThreads + threadIdx.x;
+    if (c >= D.cols) return;
+    const int64_t r0 = chunk * per, r1 = r0 + per < D.rows ? r0 + per : D.rows;
+    double s = 0.0;
+    for (int64_t r = r0; r < r1; ++r) s += idens_of(D, rel_of(D, scale, force_of(D, r * D.cols + c)));
+    Bf.tbuf[chunk * D.cols + c] = s;
 }
 
 template <int RM, typename P>
-__global__ void __launch_bounds__(kThreads) s64_fin2(T64<P> D, Buf64 Bf) {
+__global__ void __launch_bounds__(kThreads) s64_fin2(G64<P> G) {
+    S64_BIND_TENSOR();
     __shared__ double tot[2 + 2 * RM];
     __shared__ double emean[8];
     __shared__ double s_lax[kMaxLeadSum64];
@@ -332,8 +442,12 @@ __global__ void __launch_bounds__(kThreads) s64_fin2(T64<P> D, Buf64 Bf) {
     if (D.inst && D.ndim >= 2) {
         __syncthreads();
         const double gm = C.gm;
-        for (int64_t c = tid; c < D.cols; c += kThreads)
-            Bf.colsum[c] = log(fmax((Bf.colsum[c] / (double)D.rows) / gm, eps));
+        const int64_t chunks = col_chunks(D.rows);
+        for (int64_t c = tid; c < D.cols; c += kThreads) {
+            double s = 0.0;
+            for (int64_t ch = 0; ch < chunks; ++ch) s += Bf.tbuf[ch * D.cols + c];
+            Bf.colsum[c] = log(fmax((s / (double)D.rows) / gm, eps));
+        }
         if (D.ndim == 2) {
             for (int64_t r = tid; r < D.rows; r += kThreads)
                 Bf.rowsum[r] = log(fmax((Bf.rowsum[r] / (double)D.cols) / gm, eps));
@@ -376,7 +490,8 @@ __global__ void __launch_bounds__(kThreads) s64_fin2(T64<P> D, Buf64 Bf) {
 // ---- P3: tangent, error, projections of the port and of the tangent, port bins.
 // Record: [sum err^2, sum port c_k (RM), sum port s_k (RM), sum t c_k (RM), sum t s_k (RM), port bins (TB)]
 template <int RM, typename P>
-__global__ void __launch_bounds__(kThreads) s64_p3(T64<P> D, Buf64 Bf) {
+__global__ void __launch_bounds__(kThreads) s64_p3(G64<P> G) {
+    S64_BIND_BLOCKS(blk);
     __shared__ double red[kWarps];
     extern __shared__ double sbin[];
     const int TB = D.T * D.B;
@@ -389,7 +504,7 @@ __global__ void __launch_bounds__(kThreads) s64_p3(T64<P> D, Buf64 Bf) {
     double v[1 + 4 * RM];
 #pragma unroll
     for (int j = 0; j < 1 + 4 * RM; ++j) v[j] = 0.0;
-    for (int64_t e = blockIdx.x * (int64_t)kThreads + threadIdx.x; e < D.N; e += (int64_t)gridDim.x * kThreads) {
+    for (int64_t e = lb * kThreads + threadIdx.x; e < D.N; e += gb * kThreads) {
         const int64_t r = e / D.cols, c = e % D.cols;
         const double f = force_of(D, e);
         const double rel = rel_of(D, scale, f);
@@ -425,14 +540,15 @@ __global__ void __launch_bounds__(kThreads) s64_p3(T64<P> D, Buf64 Bf) {
             for (int tb = 0; tb < D.T; ++tb) atomicAdd(&sbin[tb * D.B + (int)hash_bin(e, D.B, tb)], port);
     }
     const int RL = 1 + 4 * RM + TB;
-    double* rec = Bf.rec + (int64_t)blockIdx.x * RL;
+    double* rec = Bf.rec + lb * RL;
     block_record<1 + 4 * RM>(v, red, rec);
     if (hash_on)
         for (int i = threadIdx.x; i < TB; i += kThreads) rec[1 + 4 * RM + i] = sbin[i];
 }
 
 template <int RM, typename P>
-__global__ void __launch_bounds__(kThreads) s64_fin3(T64<P> D, Buf64 Bf) {
+__global__ void __launch_bounds__(kThreads) s64_fin3(G64<P> G) {
+    S64_BIND_TENSOR();
     __shared__ double tot[1 + 4 * RM];
     const int tid = threadIdx.x;
     const int TB = D.T * D.B;
@@ -534,17 +650,16 @@ template <int RM, typename P>
 __device__ __forceinline__ void drive_vectors(const T64<P>& D, const Buf64& Bf, int64_t e, double (&v)[8]) {
     const C64& C = *Bf.cst;
     const double eps = D.hp[Q_EPS], clip = C.clip;
-    double ch[RM], sh[RM];
-    carriers<RM>(D, e / D.cols, e % D.cols, ch, sh);
     const double t = Bf.tbuf[e];
-    const double pred = recon<RM>(C.p_al, C.p_be, ch, sh);
+    double pred, echo;
+    recon_pred_echo<RM>(D, C, e / D.cols, e % D.cols, D.echo_on != 0, pred, echo);
     v[0] = t / (1.0 + fabs(t) / clip);
     v[1] = tanh(t / clip) * clip;
     v[2] = sgnd(t) * sqrt(fmin(fabs(t), clip * clip) + eps);
     v[3] = t;
     v[4] = pred;
     v[5] = tanh((t - pred) / (clip * (1.0 + C.S))) * clip;
-    v[6] = D.echo_on ? recon<RM>(C.e_al, C.e_be, ch, sh) : 0.0;
+    v[6] = echo;
     double hp = 0.0;
     if (D.hash_on) {
         for (int t2 = 0; t2 < D.T; ++t2) hp += Bf.impv[t2 * D.B + (int)hash_bin(e, D.B, t2)];
@@ -556,12 +671,13 @@ __device__ __forceinline__ void drive_vectors(const T64<P>& D, const Buf64& Bf, 
 __host__ __device__ constexpr int g8(int a, int b) { return a * 8 - (a * (a - 1)) / 2 + (b - a); }
 
 template <int RM, typename P>
-__global__ void __launch_bounds__(kThreads) s64_p4(T64<P> D, Buf64 Bf) {
+__global__ void __launch_bounds__(kThreads) s64_p4(G64<P> G) {
+    S64_BIND_BLOCKS(blk);
     __shared__ double red[kWarps];
     double g[kGram64];
 #pragma unroll
     for (int j = 0; j < kGram64; ++j) g[j] = 0.0;
-    for (int64_t e = blockIdx.x * (int64_t)kThreads + threadIdx.x; e < D.N; e += (int64_t)gridDim.x * kThreads) {
+    for (int64_t e = lb * kThreads + threadIdx.x; e < D.N; e += gb * kThreads) {
         double v[8];
         drive_vectors<RM>(D, Bf, e, v);
 #pragma unroll
@@ -569,24 +685,25 @@ __global__ void __launch_bounds__(kThreads) s64_p4(T64<P> D, Buf64 Bf) {
 #pragma unroll
             for (int b = a; b < 8; ++b) g[g8(a, b)] += v[a] * v[b];
     }
-    block_record<kGram64>(g, red, Bf.rec + (int64_t)blockIdx.x * kGram64);
+    block_record<kGram64>(g, red, Bf.rec + lb * kGram64);
 }
 
 // Drive coefficients from the Gram (cresso_v5.py:1303-1353).
 template <typename P>
-__global__ void s64_fin4(T64<P> D, Buf64 Bf) {
-    __shared__ double G[kGram64];
+__global__ void s64_fin4(G64<P> G) {
+    S64_BIND_TENSOR();
+    __shared__ double Gs[kGram64];
     const int tid = threadIdx.x;
     for (int j = tid; j < kGram64; j += kThreads) {
         double s = 0.0;
         for (int b = 0; b < Bf.blocks; ++b) s += Bf.rec[(int64_t)b * kGram64 + j];
-        G[j] = s;
+        Gs[j] = s;
     }
     __syncthreads();
     if (tid != 0) return;
     C64& C = *Bf.cst;
     const double N = (double)D.N, eps = D.hp[Q_EPS], S = C.S;
-    auto Gm = [&](int a, int b) { return a <= b ? G[g8(a, b)] : G[g8(b, a)]; };
+    auto Gm = [&](int a, int b) { return a <= b ? Gs[g8(a, b)] : Gs[g8(b, a)]; };
     enum { RAT, BND, ROOT, TT, PR, NOV, ECHO, HASH };
     auto rms_of = [&](const double* c8) {  // sqrt(mean((sum c_i v_i)^2) + eps)
         double s = 0.0;
@@ -642,33 +759,73 @@ __global__ void s64_fin4(T64<P> D, Buf64 Bf) {
 }
 
 template <int RM, typename P>
-__global__ void __launch_bounds__(kThreads) s64_p5(T64<P> D, Buf64 Bf) {
+__global__ void __launch_bounds__(kThreads) s64_p5(G64<P> G) {
+    S64_BIND_BLOCKS(blk);
     const C64& C = *Bf.cst;
     const double neg_lr = -D.hp[Q_LR], gain = C.gain;
-    for (int64_t e = blockIdx.x * (int64_t)kThreads + threadIdx.x; e < D.N; e += (int64_t)gridDim.x * kThreads) {
+    const float neg_lr16 = neg_lr_in(D.hp[Q_LR], D.pdt);
+    for (int64_t e = lb * kThreads + threadIdx.x; e < D.N; e += gb * kThreads) {
         double v[8];
         drive_vectors<RM>(D, Bf, e, v);
         double drive = 0.0;
 #pragma unroll
         for (int i = 0; i < 8; ++i) drive += C.c[i] * v[i];
-        D.param[e] = D.param[e] + neg_lr * (drive * gain);
+        if (D.pdt == CRESSO_DTYPE_F64) {
+            double* p = static_cast<double*>(D.param);
+            p[e] = p[e] + neg_lr * (drive * gain);
+        } else if (D.pdt == CRESSO_DTYPE_F32) {
+            float* p = static_cast<float*>(D.param);
+            p[e] = (float)((double)p[e] + neg_lr * (drive * gain));
+        } else {
+            // 16-bit: the update rounded to the parameter type, then param.add_(u, alpha=-lr)
+            apply_update(D.param, e, D.pdt, 0.0f, neg_lr16, (float)(drive * gain));
+        }
     }
 }
 
 // Both storage types have the same layout (every pointer the same size), so the
-// plan keeps T64<double> and a float32 tensor is launched as its T64<float> copy.
+// plan keeps T64<double> and the tensors of a float32-state group are uploaded
+// as T64<float> records (the same bytes).
 static_assert(sizeof(T64<float>) == sizeof(T64<double>), "T64 layout");
-T64<float> as_f32(const T64<double>& d) {
-    T64<float> f;
-    memcpy(&f, &d, sizeof(f));
-    return f;
-}
 
+// Tensors are launched in groups: consecutive tensors of one state type whose
+// scratch (tables, block records, bin and axis buffers, the tangent field)
+// stays within kGroupBytes64; a larger tensor forms a group of its own.  The
+// groups run one after another and reuse the same scratch.
+constexpr int64_t kGroupBytes64 = 1LL << 30;
+constexpr int kGroupTensors64 = 4096;
+
+struct Item64 {
+    int blocks, rblocks, cblocks;  // element passes, row sums, column sums
+    int64_t L;                     // doubles per block record
+    int64_t bytes;                 // scratch of this tensor
+};
+struct Group64 {
+    int first, count;
+    bool f32;
+    int64_t bytes;
+};
 struct Plan64 {
     std::vector<T64<double>> ts;
-    int64_t bytes, off_cst, off_rec, off_lterm, off_impv, off_counts, off_row, off_col, off_tbuf;
-    int blocks;
+    std::vector<Item64> items;
+    std::vector<Group64> groups;
+    int64_t bytes;
 };
+
+int64_t tensor_scratch64(const T64<double>& T, const Item64& it) {
+    const int64_t TB = std::max<int64_t>((int64_t)T.T * T.B, 1);
+    int64_t b = align_up((int64_t)sizeof(C64), 256);
+    b += align_up(8 * it.L * it.blocks, 256);
+    b += 3 * align_up(8 * TB, 256);
+    b += align_up(8 * T.rows, 256) + align_up(8 * T.cols, 256);
+    b += align_up(8 * T.N, 256);
+    return b;
+}
+
+int64_t group_tables64(int n) {
+    return align_up((int64_t)sizeof(T64<double>) * n, 256) + align_up((int64_t)sizeof(Buf64) * n, 256) +
+           align_up(3 * 4 * (int64_t)(n + 1), 256);
+}
 
 int plan64(const cresso_tensor_desc* descs, int64_t n, const cresso_hparams* hp, Plan64& P) {
     CRESSO_REQUIRE(descs != nullptr && hp != nullptr && n >= 1, CRESSO_EINVAL, "spectral64: need tensors and hparams");
@@ -679,12 +836,15 @@ int plan64(const cresso_tensor_desc* descs, int64_t n, const cresso_hparams* hp,
     CRESSO_REQUIRE(bins * tables <= kMaxTB64, CRESSO_EUNSUPPORTED,
                    "hash_bins * hash_tables must be <= %d for float64 parameters", kMaxTB64);
     const int rm = rank_pad(rank);
-    int64_t max_rows = 1, max_cols = 1, max_n = 1;
     P.ts.assign(n, T64<double>{});
     for (int64_t i = 0; i < n; ++i) {
         const cresso_tensor_desc& d = descs[i];
-        CRESSO_REQUIRE(d.dtype == CRESSO_DTYPE_F64 || (d.dtype == CRESSO_DTYPE_F32 && rank > kMaxRank), CRESSO_EINVAL,
-                       "tensor %lld: spectral64 takes float64 tensors, and float32 tensors when rank > %d",
+        CRESSO_REQUIRE(d.dtype == CRESSO_DTYPE_F64 || ((d.dtype == CRESSO_DTYPE_F32 || d.dtype == CRESSO_DTYPE_F16 ||
+                                                         d.dtype == CRESSO_DTYPE_BF16) &&
+                                                        rank > kMaxRank),
+                       CRESSO_EINVAL,
+                       "tensor %lld: spectral64 takes float64 tensors, and float32 / float16 / bfloat16 tensors "
+                       "when rank > %d",
                        (long long)i, kMaxRank);
         CRESSO_REQUIRE(d.ndim >= 1 && d.ndim <= CRESSO_MAX_NDIM, CRESSO_EUNSUPPORTED,
                        "tensor %lld: spectral route supports tensors of rank 1 to %d", (long long)i, CRESSO_MAX_NDIM);
@@ -714,9 +874,10 @@ int plan64(const cresso_tensor_desc* descs, int64_t n, const cresso_hparams* hp,
         T.N = rows * cols;
         T.step = d.step;
         for (int64_t a = 0; a < CRESSO_MAX_NDIM; ++a) T.dims[a] = a < d.ndim ? d.shape[a] : 0;
-        T.param = (double*)d.param;  // storage type: double, or float when f32 (see as_f32)
-        T.grad = (const double*)d.grad;
-        T.f32 = d.dtype == CRESSO_DTYPE_F32;
+        T.param = (void*)d.param;
+        T.grad = (const void*)d.grad;
+        T.pdt = (int32_t)d.dtype;
+        T.f32 = d.dtype != CRESSO_DTYPE_F64;  // state storage: float (see as_f32) unless float64
         const ShapeWsHeader wh = shape_ws64_layout(d.ndim, rows, cols, rank, rm);
         const char* ws = (const char*)d.shape_ws;
         T.rowtab = (const double*)(ws + wh.off_rowtab);
@@ -755,77 +916,134 @@ int plan64(const cresso_tensor_desc* descs, int64_t n, const cresso_hparams* hp,
         T.inst = hard && hp->instant_metric_coupling != 0.0 && T.N > 1;
         T.local_on = hp->local_sharpness != 0.0;
         memcpy(T.hp, hp, sizeof(cresso_hparams));
-        max_rows = std::max(max_rows, rows);
-        max_cols = std::max(max_cols, cols);
-        max_n = std::max(max_n, T.N);
     }
     int dev = 0, sms = 148;
     CRESSO_CUDA(cudaGetDevice(&dev));
     CRESSO_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
-    P.blocks = (int)std::min<int64_t>(std::min<int64_t>(ceil_div(max_n, kThreads * 4), kMaxBlocks64), 2 * sms);
-    P.blocks = std::max(P.blocks, 1);
-    const int64_t TB = bins * tables;
-    const int64_t L = std::max<int64_t>(std::max<int64_t>(2 + 2 * rm + 2 * TB, 1 + 4 * rm + TB), kGram64);
-    int64_t off = 0;
-    P.off_cst = off;
-    off = align_up(off + (int64_t)sizeof(C64), 256);
-    P.off_rec = off;
-    off = align_up(off + 8 * L * P.blocks, 256);
-    P.off_lterm = off;
-    off = align_up(off + 8 * std::max<int64_t>(TB, 1), 256);
-    P.off_impv = off;
-    off = align_up(off + 8 * std::max<int64_t>(TB, 1), 256);
-    P.off_counts = off;
-    off = align_up(off + 8 * std::max<int64_t>(TB, 1), 256);
-    P.off_row = off;
-    off = align_up(off + 8 * max_rows, 256);
-    P.off_col = off;
-    off = align_up(off + 8 * max_cols, 256);
-    P.off_tbuf = off;
-    off = align_up(off + 8 * max_n, 256);
-    P.bytes = off;
+    P.items.assign(n, Item64{});
+    P.groups.clear();
+    P.bytes = 0;
+    for (int64_t i = 0; i < n; ++i) {
+        const T64<double>& T = P.ts[i];
+        Item64& it = P.items[i];
+        it.blocks = (int)std::max<int64_t>(
+            1, std::min<int64_t>(std::min<int64_t>(ceil_div(T.N, kThreads * 4), kMaxBlocks64), 2 * sms));
+        const bool axes = T.inst && T.ndim >= 2;
+        it.rblocks = axes ? (int)std::min<int64_t>(ceil_div(T.rows, kWarps), 4096) : 0;
+        it.cblocks = axes ? (int)(ceil_div(T.cols, kThreads) * col_chunks(T.rows)) : 0;
+        const int64_t TBi = (int64_t)T.T * T.B;
+        it.L = std::max<int64_t>(std::max<int64_t>(2 + 2 * rm + 2 * TBi, 1 + 4 * rm + TBi), kGram64);
+        it.bytes = tensor_scratch64(T, it);
+        const bool f32 = T.f32 != 0;
+        if (P.groups.empty() || P.groups.back().f32 != f32 || P.groups.back().count == kGroupTensors64 ||
+            group_tables64(P.groups.back().count + 1) + P.groups.back().bytes + it.bytes > kGroupBytes64)
+            P.groups.push_back(Group64{(int)i, 0, f32, 0});
+        Group64& g = P.groups.back();
+        ++g.count;
+        g.bytes += it.bytes;  // the tensors' scratch; the tables are added below
+    }
+    for (const Group64& g : P.groups) P.bytes = std::max(P.bytes, group_tables64(g.count) + g.bytes);
     return CRESSO_OK;
 }
 
+// One group: its tables uploaded to the front of the scratch, then every pass
+// as one launch over the blocks of all its tensors and every finalize as one
+// launch of a block per tensor.
 template <int RM, typename P>
-int run_tensor(const T64<P>& T, Buf64 Bf, cudaStream_t s) {
-    const int g = Bf.blocks;
-    const size_t smem2 = T.hash_on ? (size_t)2 * T.T * T.B * 8 : 0;
-    const size_t smem3 = T.hash_on ? (size_t)T.T * T.B * 8 : 0;
+int run_group(const Plan64& PL, const Group64& Gr, char* base, cudaStream_t s) {
+    const int n = Gr.count;
+    std::vector<T64<P>> ts(n);
+    std::vector<Buf64> bufs(n);
+    std::vector<int> blk(3 * (n + 1));
+    T64<P>* d_ts = reinterpret_cast<T64<P>*>(base);
+    int64_t off = align_up((int64_t)sizeof(T64<P>) * n, 256);
+    Buf64* d_bufs = reinterpret_cast<Buf64*>(base + off);
+    off += align_up((int64_t)sizeof(Buf64) * n, 256);
+    int* d_blk = reinterpret_cast<int*>(base + off);
+    off += align_up(3 * 4 * (int64_t)(n + 1), 256);
+    int g = 0, gr = 0, gc = 0;
+    bool any_axes = false;
+    size_t smem2 = 0, smem3 = 0;
+    for (int j = 0; j < n; ++j) {
+        const int i = Gr.first + j;
+        const T64<double>& T = PL.ts[i];
+        const Item64& it = PL.items[i];
+        memcpy(&ts[j], &T, sizeof(T64<P>));
+        const int64_t TB = std::max<int64_t>((int64_t)T.T * T.B, 1);
+        char* q = base + off;
+        Buf64& bf = bufs[j];
+        bf.cst = reinterpret_cast<C64*>(q);
+        q += align_up((int64_t)sizeof(C64), 256);
+        bf.rec = reinterpret_cast<double*>(q);
+        q += align_up(8 * it.L * it.blocks, 256);
+        bf.lterm = reinterpret_cast<double*>(q);
+        q += align_up(8 * TB, 256);
+        bf.impv = reinterpret_cast<double*>(q);
+        q += align_up(8 * TB, 256);
+        bf.counts = reinterpret_cast<double*>(q);
+        q += align_up(8 * TB, 256);
+        bf.rowsum = reinterpret_cast<double*>(q);
+        q += align_up(8 * T.rows, 256);
+        bf.colsum = reinterpret_cast<double*>(q);
+        q += align_up(8 * T.cols, 256);
+        bf.tbuf = reinterpret_cast<double*>(q);
+        q += align_up(8 * T.N, 256);
+        bf.blocks = it.blocks;
+        off += it.bytes;
+        blk[j] = g;
+        blk[n + 1 + j] = gr;
+        blk[2 * (n + 1) + j] = gc;
+        g += it.blocks;
+        gr += it.rblocks;
+        gc += it.cblocks;
+        if (T.hash_on) {
+            smem2 = std::max(smem2, (size_t)2 * T.T * T.B * 8);
+            smem3 = std::max(smem3, (size_t)T.T * T.B * 8);
+        }
+        any_axes = any_axes || it.rblocks > 0;
+    }
+    blk[n] = g;
+    blk[2 * n + 1] = gr;
+    blk[3 * n + 2] = gc;
+    // pageable sources: each copy returns once its bytes are staged, so the vectors may go
+    CRESSO_CUDA(cudaMemcpyAsync(d_ts, ts.data(), sizeof(T64<P>) * n, cudaMemcpyHostToDevice, s));
+    CRESSO_CUDA(cudaMemcpyAsync(d_bufs, bufs.data(), sizeof(Buf64) * n, cudaMemcpyHostToDevice, s));
+    CRESSO_CUDA(cudaMemcpyAsync(d_blk, blk.data(), sizeof(int) * blk.size(), cudaMemcpyHostToDevice, s));
+    const G64<P> G{d_ts, d_bufs, d_blk, d_blk + (n + 1), d_blk + 2 * (n + 1), n};
     {
         NvtxRange r("cresso64 P1 force energy");
-        s64_p1<P><<<g, kThreads, 0, s>>>(T, Bf);
+        s64_p1<P><<<g, kThreads, 0, s>>>(G);
         CRESSO_LAUNCHED("s64_p1");
-        s64_fin1<P><<<1, 32, 0, s>>>(T, Bf);
+        s64_fin1<P><<<n, 32, 0, s>>>(G);
         CRESSO_LAUNCHED("s64_fin1");
     }
     {
         NvtxRange r("cresso64 P2 density / bins / projection");
-        s64_p2<RM, P><<<g, kThreads, smem2, s>>>(T, Bf);
+        s64_p2<RM, P><<<g, kThreads, smem2, s>>>(G);
         CRESSO_LAUNCHED("s64_p2");
-        if (T.inst && T.ndim >= 2) {
-            s64_rowsum<P><<<(int)std::min<int64_t>(ceil_div(T.rows, kWarps), 4096), kThreads, 0, s>>>(T, Bf);
+        if (any_axes) {
+            s64_rowsum<P><<<gr, kThreads, 0, s>>>(G);
             CRESSO_LAUNCHED("s64_rowsum");
-            s64_colsum<P><<<(int)std::min<int64_t>(ceil_div(T.cols, kThreads), 4096), kThreads, 0, s>>>(T, Bf);
+            s64_colsum<P><<<gc, kThreads, 0, s>>>(G);
             CRESSO_LAUNCHED("s64_colsum");
         }
-        s64_fin2<RM, P><<<1, kThreads, 0, s>>>(T, Bf);
+        s64_fin2<RM, P><<<n, kThreads, 0, s>>>(G);
         CRESSO_LAUNCHED("s64_fin2");
     }
     {
         NvtxRange r("cresso64 P3 tangent / port");
-        s64_p3<RM, P><<<g, kThreads, smem3, s>>>(T, Bf);
+        s64_p3<RM, P><<<g, kThreads, smem3, s>>>(G);
         CRESSO_LAUNCHED("s64_p3");
-        s64_fin3<RM, P><<<1, kThreads, 0, s>>>(T, Bf);
+        s64_fin3<RM, P><<<n, kThreads, 0, s>>>(G);
         CRESSO_LAUNCHED("s64_fin3");
     }
     {
         NvtxRange r("cresso64 P4 drive Gram / P5 update");
-        s64_p4<RM, P><<<g, kThreads, 0, s>>>(T, Bf);
+        s64_p4<RM, P><<<g, kThreads, 0, s>>>(G);
         CRESSO_LAUNCHED("s64_p4");
-        s64_fin4<P><<<1, kThreads, 0, s>>>(T, Bf);
+        s64_fin4<P><<<n, kThreads, 0, s>>>(G);
         CRESSO_LAUNCHED("s64_fin4");
-        s64_p5<RM, P><<<g, kThreads, 0, s>>>(T, Bf);
+        s64_p5<RM, P><<<g, kThreads, 0, s>>>(G);
         CRESSO_LAUNCHED("s64_p5");
     }
     return CRESSO_OK;
@@ -859,34 +1077,25 @@ int cresso_spectral64_run(const cresso_tensor_desc* descs, int64_t n, const cres
                    (long long)scratch_bytes, (long long)P.bytes);
     NvtxRange range("cresso_spectral64_run %lld tensors", (long long)n);
     char* base = (char*)scratch;
-    Buf64 Bf;
-    Bf.cst = reinterpret_cast<C64*>(base + P.off_cst);
-    Bf.rec = reinterpret_cast<double*>(base + P.off_rec);
-    Bf.lterm = reinterpret_cast<double*>(base + P.off_lterm);
-    Bf.impv = reinterpret_cast<double*>(base + P.off_impv);
-    Bf.counts = reinterpret_cast<double*>(base + P.off_counts);
-    Bf.rowsum = reinterpret_cast<double*>(base + P.off_row);
-    Bf.colsum = reinterpret_cast<double*>(base + P.off_col);
-    Bf.tbuf = reinterpret_cast<double*>(base + P.off_tbuf);
-    Bf.blocks = P.blocks;
     cudaStream_t s = (cudaStream_t)stream;
     const int rm = rank_pad((int64_t)hp->rank);
-    // tensors one after another on the stream: each reuses the same scratch
-    for (const T64<double>& T : P.ts) {
-        if (T.f32) {
-            const T64<float> F = as_f32(T);
+    // groups one after another on the stream: each reuses the same scratch
+    for (const Group64& G : P.groups) {
+        if (G.f32) {
             switch (rm) {
-                case 4: st = run_tensor<4>(F, Bf, s); break;
-                case 8: st = run_tensor<8>(F, Bf, s); break;
-                case 16: st = run_tensor<16>(F, Bf, s); break;
-                default: st = run_tensor<32>(F, Bf, s); break;
+                case 4: st = run_group<4, float>(P, G, base, s); break;
+                case 8: st = run_group<8, float>(P, G, base, s); break;
+                case 16: st = run_group<16, float>(P, G, base, s); break;
+                case 32: st = run_group<32, float>(P, G, base, s); break;
+                default: st = run_group<64, float>(P, G, base, s); break;
             }
         } else {
             switch (rm) {
-                case 4: st = run_tensor<4>(T, Bf, s); break;
-                case 8: st = run_tensor<8>(T, Bf, s); break;
-                case 16: st = run_tensor<16>(T, Bf, s); break;
-                default: st = run_tensor<32>(T, Bf, s); break;
+                case 4: st = run_group<4, double>(P, G, base, s); break;
+                case 8: st = run_group<8, double>(P, G, base, s); break;
+                case 16: st = run_group<16, double>(P, G, base, s); break;
+                case 32: st = run_group<32, double>(P, G, base, s); break;
+                default: st = run_group<64, double>(P, G, base, s); break;
             }
         }
         if (st) return st;

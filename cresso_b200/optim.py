@@ -559,9 +559,10 @@ class CRESSO5(Optimizer):
                 if spectral_route is None:
                     spectral_route = self._route_cache[rkey] = self._use_spectral_route(param, group)
                 if spectral_route:
-                    # float64 tensors, and float32 tensors of rank > 16: the float64-arithmetic pipeline
+                    # float64 tensors, and tensors of every type at rank > 16: the float64-arithmetic
+                    # pipeline (float32 state for float32 / float16 / bfloat16 parameters)
                     wide = int(group["rank"]) > _lib.MAX_RANK
-                    if param.dtype is torch.float64 or (wide and param.dtype is torch.float32):
+                    if param.dtype is torch.float64 or wide:
                         if wide and int(group["rank"]) > _lib.MAX_RANK_PLAIN:
                             raise RuntimeError(f"CRESSO5 B200 path supports rank <= {_lib.MAX_RANK_PLAIN} "
                                                f"(got {group['rank']})")
@@ -662,10 +663,8 @@ class CRESSO5(Optimizer):
                         scratch_kind: str = "spectral"):
         """Descriptor table, scratch and layout of a spectral group; returns
         (run(begin, end) launching a stage range, scratch, layout)."""
-        if int(group["rank"]) > _lib.MAX_RANK:  # float16 / bfloat16 tensors on the fused path
-            raise RuntimeError(f"CRESSO5 B200 path supports rank <= {_lib.MAX_RANK} for float16 / bfloat16 "
-                               f"spectral tensors (got {group['rank']}); float32 and float64 take up to "
-                               f"{_lib.MAX_RANK_PLAIN}")
+        if int(group["rank"]) > _lib.MAX_RANK:  # routing sends such tensors to the float64 pipeline
+            raise RuntimeError(f"CRESSO5: rank {group['rank']} > {_lib.MAX_RANK} reached the fused spectral path")
         L = _lib.lib()
         descs = self._spectral_descs(group, device, items, tag)
         n = len(items)
@@ -687,8 +686,8 @@ class CRESSO5(Optimizer):
         return run, scratch, layout
 
     def _run_spectral64(self, group: dict, hp: np.ndarray, device, items: list) -> None:
-        """Float64 spectral tensors and float32 ones of rank > 16: the float64-arithmetic
-        pipeline, whole tensors."""
+        """Float64 spectral tensors and spectral tensors of any type at rank > 16: the
+        float64-arithmetic pipeline, whole tensors."""
         L = _lib.lib()
         F = _lib.DESC_INDEX
         descs = _lib.new_descs(len(items))

@@ -238,11 +238,15 @@ CRESSO_API int cresso_spectral_run_status(const cresso_tensor_desc* descs, int64
 CRESSO_API int cresso_status_copy(const void* status_word, void* host_word, cresso_stream_t stream);
 
 /* Float64 parameters on the spectral route (cresso_v5.py:945-1353 with the
- * float64 work and state of cresso_v5.py:119-124).  The shape workspace holds
- * float64 axis tables and the carrier stats built from them; state pointers of
- * the descriptors point at float64 values, `shape_ws` at this workspace.  The
- * step runs the same five passes as cresso_spectral_run in float64, tensor by
- * tensor; tensors are whole (not sharded), hash_bins * hash_tables <= 2048. */
+ * float64 work and state of cresso_v5.py:119-124), and float32 / float16 /
+ * bfloat16 parameters when rank > CRESSO_MAX_RANK (rank up to 64).  The shape
+ * workspace holds float64 axis tables and the carrier stats built from them;
+ * state pointers of the descriptors point at float64 values for float64
+ * parameters and at float32 values otherwise, `shape_ws` at this workspace.
+ * The step runs the same five passes as cresso_spectral_run in float64
+ * arithmetic, tensor by tensor; a 16-bit parameter receives the update rounded
+ * to its type, as in cresso_spectral_run.  Tensors are whole (not sharded),
+ * hash_bins * hash_tables <= 2048. */
 CRESSO_API int cresso_shape_workspace64_bytes(int64_t ndim, const int64_t* shape, int64_t rank, int64_t* bytes);
 CRESSO_API int cresso_shape_workspace64_init(int64_t ndim, const int64_t* shape, int64_t rank, const int64_t* freqs,
                                              void* ws, cresso_stream_t stream);

@@ -132,6 +132,14 @@ EXTRA_CASES = {
     "r20_6x8x30": ((6, 8, 30), dict(rank=20, hash_bins=37, hash_tables=1, local_sharpness=0.2), 3, 83, 0.02, 1e-3,
                    "float32"),
     "r32_f64_64x48": ((64, 48), dict(rank=32), 3, 84, 0.02, 1e-3, "float64"),
+    # 16-bit parameters above rank 16, and ranks 33 to 64 (the same float64-arithmetic path)
+    "r24_bf16_80x96": ((80, 96), dict(rank=24, hash_bins=64, hash_tables=2), 3, 85, 0.02, 1e-3, "bfloat16"),
+    "r20_f16_2000_wd": ((2000,), dict(rank=20, weight_decay=0.01, max_frequency=7), 3, 86, 0.02, 1e-3, "float16"),
+    "r48_64x80": ((64, 80), dict(rank=48, hash_bins=64, hash_tables=2), 3, 87, 0.02, 1e-3, "float32"),
+    "r40_5x6x20_local": ((5, 6, 20), dict(rank=40, hash_bins=37, hash_tables=1, local_sharpness=0.2), 3, 88, 0.02,
+                         1e-3, "float32"),
+    "r64_f64_40x50": ((40, 50), dict(rank=64, hash_bins=64, hash_tables=2), 3, 89, 0.02, 1e-3, "float64"),
+    "r64_bf16_48x64": ((48, 64), dict(rank=64, max_frequency=7), 3, 90, 0.02, 1e-3, "bfloat16"),
 }
 
 

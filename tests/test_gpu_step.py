@@ -524,6 +524,62 @@ def test_float64_spectral_route_in_a_mixed_group():
                           ref64.state[r64], upd_tol=5e-4)
 
 
+def test_float64_pipeline_groups_of_many_tensors():
+    """Rank 24 in one group: 30 float64 tensors and float32 / float16 / bfloat16
+    ones interleaved (the float64-arithmetic pipeline launches consecutive
+    tensors of one state type as one group, so this runs many groups of one to
+    several tensors), with shapes from 1-D to 3-D and hashed and hash-less
+    (non-hard) tensors, against the oracle."""
+    g = torch.Generator().manual_seed(24)
+    specs = []
+    for i in range(30):
+        shape = [(40, 33), (700,), (5, 6, 21), (3, 200), (64, 64)][i % 5]
+        specs.append((shape, torch.float64))
+        if i % 6 == 2:
+            specs.append(((48, 40), torch.float32))
+        if i % 6 == 4:
+            specs.append(((30, 50), [torch.bfloat16, torch.float16][i % 4 // 2]))
+    inits = [torch.randn(s, generator=g) * 0.02 for s, _ in specs]
+    grads = [[torch.randn(s, generator=g) * 1e-3 for s, _ in specs] for _ in range(3)]
+    kw = dict(rank=24, hash_bins=64, hash_tables=2, hard_channel_min_size=1500, min_spectral_size=1,
+              thin_matrix_route="spectral")
+    ps = [torch.nn.Parameter(x.clone().to("cuda", dt)) for x, (_, dt) in zip(inits, specs)]
+    rs = [torch.nn.Parameter(x.clone().to(dt)) for x, (_, dt) in zip(inits, specs)]
+    r64s = [torch.nn.Parameter(x.clone().to(dt).double()) for x, (_, dt) in zip(inits, specs)]
+    opt = cresso_b200.CRESSO5(ps, **kw)
+    ref = O.OracleCRESSO5(rs, **kw)
+    ref64 = O.OracleCRESSO5(r64s, **kw)
+    for gs in grads:
+        for p, r, r64, gg, (_, dt) in zip(ps, rs, r64s, gs, specs):
+            p.grad = gg.to("cuda", dt)
+            r.grad = gg.to(dt)
+            r64.grad = gg.to(dt).double()
+        opt.step()
+        ref.step()
+        ref64.step()
+    torch.cuda.synchronize()
+    assert opt._device_status() == 0
+    for (shape, dt), p, r, r64, x0 in zip(specs, ps, rs, r64s, inits):
+        assert p.dtype == dt
+        if dt == torch.float64:
+            assert rel_rms(p.detach().cpu().double(), r.detach().double()) <= 1e-12, shape
+            for k, v in ref.state[r].items():
+                if torch.is_tensor(v) and v.dtype.is_floating_point:
+                    assert opt.state[p][k].dtype == torch.float64, (shape, k)
+                    assert rel_rms(opt.state[p][k].cpu().double(), v.double()) <= 1e-9, (shape, k)
+        elif dt == torch.float32:
+            st = {k: (v.cpu() if torch.is_tensor(v) else v) for k, v in opt.state[p].items()}
+            check_against(f"r24group{shape}", x0, p.detach().cpu(), st, r.detach(), ref.state[r], r64.detach(),
+                          ref64.state[r64], upd_tol=5e-4)
+        else:  # 16-bit: within one unit of the parameter type per step, mostly exact
+            ulps = ulp_distance(p.detach().float().cpu().numpy(), r.detach().float().numpy(),
+                                str(dt).split(".")[-1])
+            assert ulps.max() <= 3 and float(np.mean(ulps)) <= 0.15, (shape, dt, float(ulps.max()))
+            for k, v in ref64.state[r64].items():
+                if torch.is_tensor(v) and v.dtype.is_floating_point:
+                    assert opt.state[p][k].dtype == torch.float32, (shape, k)
+
+
 def test_bounded_wait_runs_out_and_reports_status():
     """The bounded in-kernel wait that guards the tensor-core passes, on a GPU:
     an mbarrier nothing arrives on makes the wait give up after its limit and
