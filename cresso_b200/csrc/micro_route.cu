@@ -366,8 +366,12 @@ int cresso_micro_run(const cresso_tensor_desc* descs, int64_t n, const cresso_hp
     memcpy(h.hp, hp, sizeof(cresso_hparams));
     const int64_t off_dts = align_up((int64_t)sizeof(MicroHdr), 256);
     cudaStream_t s = (cudaStream_t)stream;
-    int ust = upload_async(base, &h, sizeof(h), s);
-    if (!ust) ust = upload_async(base + off_dts, dts.data(), sizeof(MicroTensor) * n, s);
+    // header and descriptors in one upload
+    static thread_local std::vector<unsigned char> blob;
+    blob.assign((size_t)(off_dts + (int64_t)sizeof(MicroTensor) * n), 0);
+    memcpy(blob.data(), &h, sizeof(h));
+    memcpy(blob.data() + off_dts, dts.data(), sizeof(MicroTensor) * n);
+    int ust = upload_async(base, blob.data(), blob.size(), s);
     if (ust) return ust;
     const MicroHdr* dh = reinterpret_cast<const MicroHdr*>(base);
     const MicroTensor* dd = reinterpret_cast<const MicroTensor*>(base + off_dts);

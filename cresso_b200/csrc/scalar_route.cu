@@ -959,8 +959,12 @@ static int scal_launch(std::vector<ScalTensor>& dts, const cresso_hparams* hp, c
     h.n = n;
     memcpy(h.hp, hp, sizeof(cresso_hparams));
     const int64_t off_dts = align_up((int64_t)sizeof(ScalHdr), 256);
-    int ust = upload_async(base, &h, sizeof(h), s);
-    if (!ust) ust = upload_async(base + off_dts, ord.data(), sizeof(ScalTensor) * n, s);
+    // header and descriptors in one upload
+    static thread_local std::vector<unsigned char> blob;
+    blob.assign((size_t)(off_dts + (int64_t)sizeof(ScalTensor) * n), 0);
+    memcpy(blob.data(), &h, sizeof(h));
+    memcpy(blob.data() + off_dts, ord.data(), sizeof(ScalTensor) * n);
+    int ust = upload_async(base, blob.data(), blob.size(), s);
     if (ust) return ust;
     const ScalHdr* dh = reinterpret_cast<const ScalHdr*>(base);
     const ScalTensor* dd = reinterpret_cast<const ScalTensor*>(base + off_dts);

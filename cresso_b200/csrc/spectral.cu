@@ -1118,26 +1118,58 @@ __host__ __device__ inline int64_t red_len(int pass, int64_t rm, int64_t tb, int
     }
 }
 
-__global__ void reduce_kernel(int pass, const GroupHdr* __restrict__ hdr, const DevTensor* __restrict__ dts,
-                              const double* __restrict__ rec_scal, const float* __restrict__ rec_bins) {
+// The per-block records of a pass summed into D.red[pass] in float64.  Every
+// output is added in one fixed order - G interleaved partial sums (records g,
+// g + G, g + 2G, ... in increasing order), then the G partials in order - so
+// the result does not depend on the launch or the GPU.  Block kinds: the
+// scalar and hash-bin outputs (records of the blocks that covered the tensor)
+// take 8 outputs x 32 groups per block; the column sums of pass 2 (one
+// partial per row band) take 64 outputs x 4 groups.  grid.x = the largest
+// number of scalar blocks over the tensors + the largest number of column
+// blocks; grid.y = tensors.
+constexpr int kRedOutA = 8, kRedGrpA = kThreads / kRedOutA;   // 8 x 32
+constexpr int kRedOutB = 64, kRedGrpB = kThreads / kRedOutB;  // 64 x 4
+
+__host__ __device__ inline int64_t red_scal_len(int pass, int64_t rm, int64_t tb) {
+    return pass == 1 ? 1 : (pass == 4 ? kGram : 2 + 2 * rm + tb);
+}
+
+__global__ void reduce_kernel(int pass, int blocks_a, const GroupHdr* __restrict__ hdr,
+                              const DevTensor* __restrict__ dts, const double* __restrict__ rec_scal,
+                              const float* __restrict__ rec_bins) {
+    __shared__ double part[kThreads];
     const DevTensor& D = dts[blockIdx.y];
     const int64_t rm = hdr->rm, tb = hdr->tb;
-    const int64_t len = red_len(pass, rm, tb, D.cols, D.ndim);
     const int64_t ns = pass == 1 ? 1 : (pass == 4 ? kGram : 2 + 2 * rm);
-    const int64_t o = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-    if (o >= len) return;
-    const int r0 = D.recbase[pass], nr = D.nrec[pass];
+    const int64_t na = red_scal_len(pass, rm, tb);                      // scalar + bin outputs
+    const int64_t nc = red_len(pass, rm, tb, D.cols, D.ndim) - na;      // column outputs
+    const bool kind_a = (int)blockIdx.x < blocks_a;
+    const int outs = kind_a ? kRedOutA : kRedOutB, grps = kind_a ? kRedGrpA : kRedGrpB;
+    const int64_t first = kind_a ? (int64_t)blockIdx.x * kRedOutA : na + (int64_t)(blockIdx.x - blocks_a) * kRedOutB;
+    const int64_t last = kind_a ? na : na + nc;
+    if (first >= last) return;  // block-uniform
+    const int j = threadIdx.x % outs, g = threadIdx.x / outs;
+    const int64_t o = first + j;
     double s = 0.0;
-    if (o < ns) {
-        for (int r = 0; r < nr; ++r) s += rec_scal[(int64_t)(r0 + r) * kNSRec + o];
-    } else if (o < ns + tb) {
-        if (D.flags & F_HASH)
-            for (int r = 0; r < nr; ++r) s += (double)rec_bins[(int64_t)(r0 + r) * tb + (o - ns)];
-    } else {
-        const int64_t c = o - ns - tb;
-        for (int b = 0; b < D.n_bands; ++b) s += (double)D.colpart[(int64_t)b * D.cols + c];
+    if (o < last) {
+        const int r0 = D.recbase[pass], nr = D.nrec[pass];
+        if (o < ns) {
+            for (int r = g; r < nr; r += grps) s += rec_scal[(int64_t)(r0 + r) * kNSRec + o];
+        } else if (o < na) {
+            if (D.flags & F_HASH)
+                for (int r = g; r < nr; r += grps) s += (double)rec_bins[(int64_t)(r0 + r) * tb + (o - ns)];
+        } else {
+            const int64_t c = o - na;
+            for (int b = g; b < D.n_bands; b += grps) s += (double)D.colpart[(int64_t)b * D.cols + c];
+        }
     }
-    D.red[pass][o] = s;
+    part[g * outs + j] = s;
+    __syncthreads();
+    if (g == 0 && o < last) {
+        double t = part[j];
+        for (int q = 1; q < grps; ++q) t += part[q * outs + j];
+        D.red[pass][o] = t;
+    }
 }
 
 // ---------------------------------------------------------------------------
@@ -1197,6 +1229,29 @@ __global__ void finalize2_kernel(const GroupHdr* __restrict__ hdr, const DevTens
     const double* red = D.red[2];
     const double sumL = red[0], sumd = red[1];
     const int64_t rm = hdr->rm;
+    if (blockIdx.y > 0) {
+        // blocks 1..gridDim.y-1 of a 2-D tensor: the instant axial metric factors of its
+        // rows and columns (cresso_v5.py:243-262), exp(c / (2 p) (log(max(axis mean / mean,
+        // eps)))); a row's sum adds its column-tile partials in order
+        if (!(D.flags & F_INST2D) || D.ndim != 2) return;
+        const float pw = fmaxf((float)hp[H_IP], 0.25f);
+        const float gmc = fmaxf((float)(sumd / N), eps);
+        const float kk = (float)(hp[H_IC] / ((double)D.ndim * (double)pw));
+        const int64_t grows = D.N / D.gcols;
+        const int64_t step = (int64_t)(gridDim.y - 1) * kThreads;
+        for (int64_t r = (int64_t)(blockIdx.y - 1) * kThreads + tid; r < D.rows; r += step) {
+            double s = 0.0;
+            for (int c = 0; c < D.n_ct; ++c) s += (double)D.rowpart[(int64_t)c * D.rows + r];
+            const float rmean = (float)(s / (double)D.gcols);
+            D.rowf[r] = expf(kk * logf(fmaxf(rmean / gmc, eps)));
+        }
+        const double* cols = red + 2 + 2 * rm + TB;
+        for (int64_t c = (int64_t)(blockIdx.y - 1) * kThreads + tid; c < D.cols; c += step) {
+            const float cmean = (float)(cols[c] / (double)grows);
+            D.colf[c] = expf(kk * logf(fmaxf(cmean / gmc, eps)));
+        }
+        return;
+    }
 
     // ---- hash metric (cresso_v5.py:1013-1056)
     if (D.flags & F_HASH) {
@@ -1276,12 +1331,7 @@ __global__ void finalize2_kernel(const GroupHdr* __restrict__ hdr, const DevTens
         const float kk = (float)(hp[H_IC] / ((double)D.ndim * (double)pw));
         const int64_t grows = D.N / D.gcols;
         if (D.ndim == 2) {
-            for (int64_t r = tid; r < D.rows; r += kThreads) {
-                double s = 0.0;
-                for (int c = 0; c < D.n_ct; ++c) s += (double)D.rowpart[(int64_t)c * D.rows + r];
-                const float rmean = (float)(s / (double)D.gcols);
-                D.rowf[r] = expf(kk * logf(fmaxf(rmean / gmc, eps)));
-            }
+            // rows and columns: the blocks with blockIdx.y > 0 (above)
         } else {
             // rank >= 3 (never sharded): the row index is the flattened leading axes.  Row
             // sums into rowf, then per leading axis a and coordinate c the marginal mean
@@ -1325,10 +1375,12 @@ __global__ void finalize2_kernel(const GroupHdr* __restrict__ hdr, const DevTens
                 D.rowf[r] = expf(kk * lsum);
             }
         }
-        const double* cols = red + 2 + 2 * rm + TB;
-        for (int64_t c = tid; c < D.cols; c += kThreads) {
-            const float cmean = (float)(cols[c] / (double)grows);
-            D.colf[c] = expf(kk * logf(fmaxf(cmean / gmc, eps)));
+        if (D.ndim != 2) {
+            const double* cols = red + 2 + 2 * rm + TB;
+            for (int64_t c = tid; c < D.cols; c += kThreads) {
+                const float cmean = (float)(cols[c] / (double)grows);
+                D.colf[c] = expf(kk * logf(fmaxf(cmean / gmc, eps)));
+            }
         }
     }
     if (tid == 0) {
@@ -2030,10 +2082,12 @@ static int launch_stage(int stage, const Plan& P, char* base, cudaStream_t s) {
         return CRESSO_OK;
     };
     auto run_reduce = [&](int pass) -> int {
-        int64_t maxlen = 0;
-        for (auto& D : P.dts) maxlen = std::max(maxlen, red_len(pass, P.rm, P.hdr.tb, D.cols, D.ndim));
-        dim3 grid((unsigned)ceil_div(maxlen, kThreads), (unsigned)n);
-        reduce_kernel<<<grid, kThreads, 0, s>>>(pass, hdr, dts, recs, recb);
+        const int64_t na = red_scal_len(pass, P.rm, P.hdr.tb);
+        int64_t maxc = 0;
+        for (auto& D : P.dts) maxc = std::max(maxc, red_len(pass, P.rm, P.hdr.tb, D.cols, D.ndim) - na);
+        const int blocks_a = (int)ceil_div(na, kRedOutA);
+        dim3 grid((unsigned)(blocks_a + ceil_div(maxc, kRedOutB)), (unsigned)n);
+        reduce_kernel<<<grid, kThreads, 0, s>>>(pass, blocks_a, hdr, dts, recs, recb);
         CRESSO_LAUNCHED("reduce_kernel");
         return CRESSO_OK;
     };
@@ -2050,10 +2104,16 @@ static int launch_stage(int stage, const Plan& P, char* base, cudaStream_t s) {
                             spectral_pass_kernel<2, RM, NT, false, false>, spectral_pass_kernel<2, RM, NT, true, false>,
                             spectral_pass_kernel<2, RM, NT, true, false>, 2);
         case 5: return run_reduce(2);
-        case 6:
-            finalize2_kernel<RM><<<n, kThreads, 0, s>>>(hdr, dts);
+        case 6: {
+            // blocks 1.. of grid.y: the row / column factors of the 2-D tensors
+            int64_t axis = 0;
+            for (auto& D : P.dts)
+                if ((D.flags & F_INST2D) && D.ndim == 2) axis = std::max<int64_t>(axis, std::max<int64_t>(D.rows, D.cols));
+            const unsigned gy = 1 + (unsigned)std::min<int64_t>(ceil_div(axis, kThreads), 32);
+            finalize2_kernel<RM><<<dim3((unsigned)n, gy), kThreads, 0, s>>>(hdr, dts);
             CRESSO_LAUNCHED("finalize2_kernel");
             return CRESSO_OK;
+        }
         case 7: return run_pass(spectral_pass_kernel<3, RM, NT, true, RM == 8>, spectral_pass_kernel<3, RM, NT, true, false>,
                             spectral_pass_kernel<3, RM, NT, false, false>, spectral_pass_kernel<3, RM, NT, true, RM == 8>,
                             spectral_pass_kernel<3, RM, NT, true, false>, 3);
@@ -2141,12 +2201,16 @@ int cresso_spectral_run_status(const cresso_tensor_desc* descs, int64_t n, const
     // which stage 0 clears
     P.hdr.status = status_word ? reinterpret_cast<int32_t*>(status_word) : reinterpret_cast<int32_t*>(base + P.off_status);
     if (stage_begin == 0) {
-        const int32_t zero = 0;
-        int ust = upload_async(base + P.off_status, &zero, sizeof(zero), s);
-        if (!ust) ust = upload_async(base + P.off_hdr, &P.hdr, sizeof(GroupHdr), s);
-        if (!ust) ust = upload_async(base + P.off_dts, P.dts.data(), sizeof(DevTensor) * n, s);
-        if (!ust) ust = upload_async(base + P.off_items, P.item_lists.data(), sizeof(int64_t) * (n + 3), s);
-        if (!ust) ust = upload_async(base + P.off_tmap, P.tensor_lists.data(), sizeof(int32_t) * n, s);
+        // header, descriptors, item and tensor lists and the cleared scratch status word
+        // lie back to back in the scratch: one upload of the whole range
+        static thread_local std::vector<unsigned char> blob;
+        const int64_t lo = P.off_hdr, hi = P.off_status + (int64_t)sizeof(int32_t);
+        blob.assign((size_t)(hi - lo), 0);
+        memcpy(blob.data() + (P.off_hdr - lo), &P.hdr, sizeof(GroupHdr));
+        memcpy(blob.data() + (P.off_dts - lo), P.dts.data(), sizeof(DevTensor) * n);
+        memcpy(blob.data() + (P.off_items - lo), P.item_lists.data(), sizeof(int64_t) * (n + 3));
+        memcpy(blob.data() + (P.off_tmap - lo), P.tensor_lists.data(), sizeof(int32_t) * n);
+        const int ust = upload_async(base + lo, blob.data(), blob.size(), s);
         if (ust) return ust;
         const int hs = launch_half_widen(P, base, s);
         if (hs) return hs;
