@@ -377,7 +377,9 @@ def workload_config(workload, shapes, kw, dtype):
     desc = {"c5": f"7B-shaped {dtype} set, 290 tensors, 6,738,411,520 elements",
             "c3": "64 LoRA-thin (4096, 16) / (16, 4096), scalar route",
             "c4": "840 LoRA-thin (4096, 16) / (16, 4096), scalar route",
-            "c4s": "840 LoRA-thin (4096, 16) / (16, 4096), thin_matrix_route='spectral'"}.get(workload, str(shapes[0]))
+            "c4s": "840 LoRA-thin (4096, 16) / (16, 4096), thin_matrix_route='spectral'",
+            "c5layer": "one layer of c5: 4 x (4096, 4096), 2 x (11008, 4096), (4096, 11008), 2 x (4096,)",
+            "c5embed": "the (32000, 4096) embedding / lm_head shape of c5"}.get(workload, str(shapes[0]))
     return {"workload": f"{workload}: {desc}", "rank": kw["rank"], "hash_bins": kw["hash_bins"],
             "hash_tables": kw["hash_tables"], "elements": n_total,
             "l2": "no flush: inputs of every step (grads + params) exceed the 126 MB L2"
