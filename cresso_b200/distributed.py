@@ -268,10 +268,13 @@ class ZeroCRESSO5(CRESSO5):
             per_rank = [[p for p in ps if p.dtype == dtype] for ps in bucket]
             width = max(max(sum(p.numel() for p in ps) for ps in per_rank), 1)
             dev = next(p for ps in per_rank for p in ps).device
-            local = torch.zeros(width, dtype=dtype, device=dev)
-            if per_rank[self.rank]:
-                flat = torch.cat([p.detach().reshape(-1) for p in per_rank[self.rank]])
-                local[: flat.numel()].copy_(flat)
+            local = torch.empty(width, dtype=dtype, device=dev)
+            mine = per_rank[self.rank]
+            n_mine = sum(p.numel() for p in mine)
+            if mine:
+                torch.cat([p.detach().reshape(-1) for p in mine], out=local[:n_mine])
+            if n_mine < width:
+                local[n_mine:].zero_()
             out = torch.empty(width * self.world, dtype=dtype, device=dev)
             if dist.get_backend(self.process_group) == "nccl":
                 work = dist.all_gather_into_tensor(out, local, group=self.process_group, async_op=True)
@@ -283,13 +286,17 @@ class ZeroCRESSO5(CRESSO5):
     def _finish_gather(self, item) -> None:
         per_rank, width, out, _local, work = item
         work.wait()
+        dsts, srcs = [], []
         for r, ps in enumerate(per_rank):
             if r == self.rank:
                 continue
             off = r * width
             for p in ps:
-                p.detach().copy_(out[off:off + p.numel()].view_as(p))
+                dsts.append(p.detach())
+                srcs.append(out[off:off + p.numel()].view_as(p))
                 off += p.numel()
+        if dsts:
+            torch._foreach_copy_(dsts, srcs)  # a few multi-tensor launches instead of one per tensor
 
     def _defer(self, items: list) -> None:
         for item in items:
