@@ -88,7 +88,11 @@ struct DevTensor {
     int64_t dims[CRESSO_MAX_NDIM];  // global shape (rank >= 3: leading-axis factors of the instant metric)
     int64_t item_base, n_items, step, hidx_n;  // item_base: first item in the class's item list
     int32_t ndim, R, TC, RPI, RB, n_ct, n_bands, flags;
-    int32_t cfirst[6], recbase[6], nrec[6], pad0;
+    int32_t cfirst[6], recbase[6], nrec[6];
+    // 1: the pass-2 column sums of the lean kernel, one float64 per (block record,
+    // column) summed over the bands of the block's run of that column tile; 0: one
+    // float per (row band, column)
+    int32_t col_runs;
     float* param;   // float32 parameter (the caller's, or the scratch copy of a 16-bit one)
     const float* grad;  // float32 gradient (the caller's, or the scratch copy in tbuf)
     float* tbuf;
@@ -1160,7 +1164,20 @@ __global__ void reduce_kernel(int pass, int blocks_a, const GroupHdr* __restrict
                 for (int r = g; r < nr; r += grps) s += (double)rec_bins[(int64_t)(r0 + r) * tb + (o - ns)];
         } else {
             const int64_t c = o - na;
-            for (int b = g; b < D.n_bands; b += grps) s += (double)D.colpart[(int64_t)b * D.cols + c];
+            if (D.col_runs) {
+                // the records of the blocks whose items cover column tile c / TC: block b of
+                // the launch owns items [b ci / g, (b + 1) ci / g), so item x lies in block
+                // ((x + 1) g - 1) / ci
+                if (g == 0) {
+                    const int64_t ci = hdr->cls_items[0], gg = hdr->grid[0][2];
+                    const int64_t first = D.item_base + (c / D.TC) * D.n_bands, last = first + D.n_bands - 1;
+                    const int64_t b0 = ((first + 1) * gg - 1) / ci, b1 = ((last + 1) * gg - 1) / ci;
+                    const double* cp = reinterpret_cast<const double*>(D.colpart);
+                    for (int64_t b = b0; b <= b1; ++b) s += cp[(b - D.cfirst[2]) * D.cols + c];
+                }
+            } else {
+                for (int b = g; b < D.n_bands; b += grps) s += (double)D.colpart[(int64_t)b * D.cols + c];
+            }
         }
     }
     part[g * outs + j] = s;
@@ -1602,6 +1619,13 @@ __global__ void finalize4_kernel(const GroupHdr* __restrict__ hdr, const DevTens
 // ---------------------------------------------------------------------------
 // Host plan
 // ---------------------------------------------------------------------------
+// Floats of a tensor's pass-2 column partials (a multiple of 64, so every tensor's
+// region starts on a 256-byte boundary).
+static int64_t colpart_floats(const DevTensor& D) {
+    const int64_t n = D.col_runs ? 2 * (int64_t)D.nrec[2] * D.cols : (int64_t)D.n_bands * D.cols;
+    return align_up(n, 64);
+}
+
 struct Plan {
     GroupHdr hdr;
     std::vector<DevTensor> dts;
@@ -1869,6 +1893,10 @@ static int build_plan(const cresso_tensor_desc* descs, int64_t n, const cresso_h
         }
         P.n_rec_max = std::max(P.n_rec_max, rb);
     }
+    for (int64_t i = 0; i < n; ++i) {
+        const bool cls0 = full[i] && !(P.dts[i].flags & (F_F16 | F_BF16));
+        P.dts[i].col_runs = (P.fast && cls0 && (P.dts[i].flags & F_INST2D)) ? 1 : 0;
+    }
 
     // scratch layout
     int64_t off = 0;
@@ -1883,7 +1911,7 @@ static int build_plan(const cresso_tensor_desc* descs, int64_t n, const cresso_h
         rows_tot += D.rows;
         cols_tot += D.cols;
         rowpart_tot += (int64_t)D.n_ct * D.rows;
-        colpart_tot += (int64_t)D.n_bands * D.cols;
+        colpart_tot += colpart_floats(D);
         elems += align_up(D.rows * D.cols, 64);
     }
     P.off_htab = take(off, 4 * std::max<int64_t>(H.tb, 1) * n);
@@ -1935,7 +1963,7 @@ static void bind_scratch(Plan& P, char* base) {
         rows_o += D.rows;
         cols_o += D.cols;
         rowpart_o += (int64_t)D.n_ct * D.rows;
-        colpart_o += (int64_t)D.n_bands * D.cols;
+        colpart_o += colpart_floats(D);
         elem_o += align_up(D.rows * D.cols, 64);
     }
 }

@@ -476,6 +476,7 @@ fast_pass_kernel(const GroupHdr* __restrict__ hdr, const DevTensor* __restrict__
         }
         float2 z12[RM];
         float zc = 0.0f;
+        double colrun = 0.0;  // P2: this column's density over the current run of bands
 #pragma unroll
         for (int q = 0; q < RM; ++q) z12[q] = f2(0.0f);
 
@@ -538,6 +539,7 @@ fast_pass_kernel(const GroupHdr* __restrict__ hdr, const DevTensor* __restrict__
             }
             const float* rowf_ip = s_rows + (PASS == 3 ? ip * ITERS : 0);
             float2 s02 = f2(0.0f), s12 = f2(0.0f), col2 = f2(0.0f);  // even / odd rows
+            bool big = false;  // a bin value too large for the fixed-point sums (added after the rows)
 
 #pragma unroll
             for (int m0 = 0; m0 < ITERS; m0 += UNR) {
@@ -581,10 +583,7 @@ fast_pass_kernel(const GroupHdr* __restrict__ hdr, const DevTensor* __restrict__
                             const int qv = fx ? __float2int_rn(dsh * fix.scale) : 0;
                             atomicAdd(&my_bins[j & 63], qv);
                             atomicAdd(&my_bins[B + (j >> 6)], qv);
-                            if (!fx) {
-                                atomicAdd(&s_fbin[j & 63], dsh);
-                                atomicAdd(&s_fbin[B + (j >> 6)], dsh);
-                            }
+                            big |= !fx;
                         }
                     }
                     // row sums over the 256 columns: a warp's 32 lanes here, the 8 warps after the item
@@ -629,10 +628,7 @@ fast_pass_kernel(const GroupHdr* __restrict__ hdr, const DevTensor* __restrict__
                             const int qv = fx ? __float2int_rn(ph_ * fix.scale) : 0;
                             atomicAdd(&my_bins[j & 63], qv);
                             atomicAdd(&my_bins[B + (j >> 6)], qv);
-                            if (!fx) {
-                                atomicAdd(&s_fbin[j & 63], ph_);
-                                atomicAdd(&s_fbin[B + (j >> 6)], ph_);
-                            }
+                            big |= !fx;
                         }
                     }
                 } else if constexpr (PASS == 4) {
@@ -674,6 +670,45 @@ fast_pass_kernel(const GroupHdr* __restrict__ hdr, const DevTensor* __restrict__
                 }
             }  // rows of the item
 
+            if constexpr (PASS == 2 || PASS == 3) {
+                // the rare values the fixed-point sums cannot hold go to the float bins here, off
+                // the row loop: each is recomputed with the row loop's operations (so the same
+                // elements fail its test); P3 reads its prediction from TMEM again (this item's
+                // products stay there until the item after next is issued).  The condition is
+                // warp-uniform, as the tensor-memory loads need.
+                if (__any_sync(0xffffffffu, big)) {
+#pragma unroll 1
+                    for (int m0 = 0; m0 < ITERS; m0 += UNR) {
+                        float R2[UNR];
+                        if constexpr (TCR) {
+                            const uint32_t ta = tc_base + tc_lane + 128 + 64 * tcb + 16 * tc_h + m0;
+                            tc_ld<UNR>(ta + 32, R2);
+                            tc_wait_ld();
+                        }
+#pragma unroll
+                        for (int u = 0; u < UNR; ++u) {
+                            const int o = (m0 + u) * 256 + lc;
+                            float v;
+                            bool fx;
+                            if constexpr (PASS == 2) {
+                                const float rel = fminf(__fmaf_rn(fabsf(xb[o]), inv_scale, eps), 1.0e4f);
+                                v = exp2f(__fmul_rn(ep, __log2f(rel)));
+                                fx = v < fix.vmax;
+                            } else {
+                                const float t = xb[o];
+                                v = __fmaf_rn(tmix, t, __fadd_rn(t, -R2[u]));
+                                fx = fabsf(v) < fix.vmax;
+                            }
+                            if (!fx) {
+                                const int j = jb[o];
+                                atomicAdd(&s_fbin[j & 63], v);
+                                atomicAdd(&s_fbin[B + (j >> 6)], v);
+                            }
+                        }
+                    }
+                }
+            }
+
             // ---- item epilogue
             if constexpr (PASS == 2 || PASS == 3) {
                 acc0 += (double)(s02.x + s02.y);
@@ -713,7 +748,16 @@ fast_pass_kernel(const GroupHdr* __restrict__ hdr, const DevTensor* __restrict__
                     items_since_flush = 0;
                 }
             }
-            if constexpr (PASS == 2) Dp->colpart[(int64_t)band * cols + col] = col2.x + col2.y;
+            if constexpr (PASS == 2) {
+                // column sums: one float64 per column over the block's run of bands of this
+                // column tile, written when the run ends (reduce_kernel, col_runs)
+                colrun += (double)(col2.x + col2.y);
+                if (nct != ct || it + 1 == seg_end) {
+                    reinterpret_cast<double*>(Dp->colpart)[(int64_t)((int)blockIdx.x - Dp->cfirst[2]) * cols + col] =
+                        colrun;
+                    colrun = 0.0;
+                }
+            }
             // the buffer of this item is next staged with item i + 2: arm its barrier now, before
             // the end barrier that precedes those copies (every thread consumed this item's phase)
             if (it + 2 < seg_end) arm_stage(buf);

@@ -524,6 +524,29 @@ def test_float64_spectral_route_in_a_mixed_group():
                           ref64.state[r64], upd_tol=5e-4)
 
 
+def test_bin_values_beyond_the_fixed_point_range():
+    """Hash-bin sums take fixed-point shared-memory atomics for values below a
+    bound and float atomics for the rest (outlier gradients): a class-0 tensor
+    (full 256-column tiles, the lean kernels) with planted outliers 1000x the
+    gradient scale, whose P2 densities and P3 ports exceed the fixed-point range,
+    against the oracle."""
+    g = torch.Generator().manual_seed(77)
+    shape = (512, 1024)
+    init = torch.randn(shape, generator=g) * 0.02
+    grads = []
+    for _ in range(3):
+        x = torch.randn(shape, generator=g) * 1e-3
+        idx = torch.randint(0, x.numel(), (64,), generator=g)
+        x.view(-1)[idx] = torch.sign(torch.randn(64, generator=g)) * 1.0
+        grads.append(x)
+    kw = dict(rank=8, hash_bins=64, hash_tables=2)
+    p, st, opt = run_cuda(shape, kw, init, grads)
+    assert opt._device_status() == 0
+    p_ref, st_ref = run_oracle(kw, init, grads)
+    p64, st64 = run_oracle(kw, init, grads, torch.float64)
+    check_against("outliers", init, p, st, p_ref, st_ref, p64, st64)
+
+
 def test_float64_pipeline_groups_of_many_tensors():
     """Rank 24 in one group: 30 float64 tensors and float32 / float16 / bfloat16
     ones interleaved (the float64-arithmetic pipeline launches consecutive
