@@ -31,7 +31,8 @@ HPARAM_FIELDS = (
 
 MAX_NDIM = 8
 MAX_RANK = 16        # the fused float32 spectral path
-MAX_RANK_PLAIN = 64  # the float64-arithmetic spectral path (float64 tensors, any tensor of rank > 16)
+MAX_RANK_PLAIN = 64  # the float64-arithmetic spectral path with its modes in registers
+MAX_RANK_WIDE = 4096  # the same path with its modes in memory (the reference CUDA contact kernel's bound)
 SPECTRAL_STAGES = 14
 # stage boundaries after which reduction vector k (1..4) is complete
 REDUCTION_BOUNDARIES = (3, 6, 9, 12)

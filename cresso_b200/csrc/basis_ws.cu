@@ -59,22 +59,31 @@ static AxisParam axis_param(int64_t mode, int64_t axis, int64_t f) {
     return a;
 }
 
+static_assert(sizeof(ModeParam) <= kModeParamBytes, "mode parameters fit their workspace slot");
+
+// Carrier parameters of mode k (frequencies freqs[k][ndim]).
+static void fill_mode(ModeParam& m, int64_t ndim, int64_t k, const int64_t* freqs) {
+    int64_t fsum = 0;
+    for (int64_t a = 0; a < ndim; ++a) fsum += freqs[k * ndim + a] < 0 ? -freqs[k * ndim + a] : freqs[k * ndim + a];
+    m.zero = fsum == 0;
+    m.kind = (int32_t)(k % 4);
+    m.nlead = (int32_t)(ndim - 1);
+    for (int64_t a = 0; a + 1 < ndim; ++a) m.lead[a] = axis_param(k, a, freqs[k * ndim + a]);
+    m.col = axis_param(k, ndim - 1, freqs[k * ndim + ndim - 1]);
+}
+
 static ModePack make_modes(int64_t ndim, const int64_t* shape, int64_t rank, const int64_t* freqs) {
     ModePack p;
     memset(&p, 0, sizeof(p));
     for (int64_t a = 0; a + 1 < ndim; ++a) p.ldim[a] = shape[a];
-    for (int64_t k = 0; k < rank; ++k) {
-        ModeParam& m = p.m[k];
-        int64_t fsum = 0;
-        for (int64_t a = 0; a < ndim; ++a) fsum += freqs[k * ndim + a] < 0 ? -freqs[k * ndim + a] : freqs[k * ndim + a];
-        m.zero = fsum == 0;
-        m.kind = (int32_t)(k % 4);
-        m.nlead = (int32_t)(ndim - 1);
-        for (int64_t a = 0; a + 1 < ndim; ++a) m.lead[a] = axis_param(k, a, freqs[k * ndim + a]);
-        m.col = axis_param(k, ndim - 1, freqs[k * ndim + ndim - 1]);
-    }
+    for (int64_t k = 0; k < rank; ++k) fill_mode(p.m[k], ndim, k, freqs);
     return p;
 }
+
+// Leading axis lengths, passed by value to the wide-rank set-up kernels.
+struct Ldim {
+    int64_t d[CRESSO_MAX_NDIM];
+};
 
 // ---------------------------------------------------------------------------
 // Set-up kernels
@@ -112,6 +121,38 @@ __device__ void axis_value(const ModeParam& m, const AxisParam& ax, int64_t idx,
     }
 }
 
+// Table value (x1, x2) of mode m at table index idx: a global row (idx < grows,
+// the composition of the leading axes) or column idx - grows.
+__device__ __forceinline__ void table_value(const ModeParam& m, const int64_t* ldim, int64_t idx, int64_t grows,
+                                            int64_t gcols, double& x1, double& x2) {
+    if (idx >= grows) {
+        axis_value(m, m.col, idx - grows, gcols, x1, x2);
+    } else if (m.zero) {
+        x1 = 1.0;
+        x2 = 0.0;
+    } else {
+        // leading axes, last one fastest; start from the identity of the composition
+        x1 = 1.0;
+        x2 = m.kind == 1 ? 1.0 : 0.0;
+        int64_t rem = idx;
+        for (int a = m.nlead - 1; a >= 0; --a) {
+            const int64_t dim = ldim[a];
+            const int64_t coord = rem % dim;
+            rem /= dim;
+            double y1, y2;
+            axis_value(m, m.lead[a], coord, dim, y1, y2);
+            if (m.kind == 1) {
+                x1 *= y1;
+                x2 *= y2;
+            } else {
+                const double t1 = x1 * y1 - x2 * y2;
+                x2 = x1 * y2 + x2 * y1;
+                x1 = t1;
+            }
+        }
+    }
+}
+
 // Axis tables in T (float for the float32 path, double for float64 tensors).
 template <typename T>
 __global__ void build_tables_kernel(ModePack modes, int rank, int rm, int64_t grows, int64_t gcols, T* rowtab,
@@ -121,35 +162,7 @@ __global__ void build_tables_kernel(ModePack modes, int rank, int rm, int64_t gr
         const int k = (int)(t % rm);
         const int64_t idx = t / rm;
         double x1 = 0.0, x2 = 0.0;
-        if (k < rank) {
-            const ModeParam& m = modes.m[k];
-            if (idx >= grows) {
-                axis_value(m, m.col, idx - grows, gcols, x1, x2);
-            } else if (m.zero) {
-                x1 = 1.0;
-                x2 = 0.0;
-            } else {
-                // leading axes, last one fastest; start from the identity of the composition
-                x1 = 1.0;
-                x2 = m.kind == 1 ? 1.0 : 0.0;
-                int64_t rem = idx;
-                for (int a = m.nlead - 1; a >= 0; --a) {
-                    const int64_t dim = modes.ldim[a];
-                    const int64_t coord = rem % dim;
-                    rem /= dim;
-                    double y1, y2;
-                    axis_value(m, m.lead[a], coord, dim, y1, y2);
-                    if (m.kind == 1) {
-                        x1 *= y1;
-                        x2 *= y2;
-                    } else {
-                        const double t1 = x1 * y1 - x2 * y2;
-                        x2 = x1 * y2 + x2 * y1;
-                        x1 = t1;
-                    }
-                }
-            }
-        }
+        if (k < rank) table_value(modes.m[k], modes.ldim, idx, grows, gcols, x1, x2);
         if (idx < grows) {
             rowtab[(idx * rm + k) * 2 + 0] = (T)x1;
             rowtab[(idx * rm + k) * 2 + 1] = (T)x2;
@@ -237,6 +250,44 @@ __device__ int basis_terms(int X, Term* t) {
     return 2;
 }
 
+// Stats of raw basis function X = 2k + comp with mean m and mean square m2
+// over the tensor: its mean and inverse RMS (zero-mode carriers stay (1, 0)).
+__device__ void store_stat(ModeStats* stats, int X, int rank, bool zero, double m, double m2, double& mu_x,
+                           double& inv_x) {
+    const int k = X >> 1;
+    double mhat = 0.0;
+    mu_x = 0.0;
+    inv_x = 0.0;
+    if (k < rank) {
+        if (zero) {
+            inv_x = 1.0;
+            mhat = m;  // unnormalised (1, 0) carrier: mean 1 for cos, 0 for sin
+        } else {
+            const double var = fmax(m2 - m * m, 0.0);
+            // A carrier that is constant over the tensor (an axis of length 1)
+            // normalises to zero (the reference divides fp32 rounding noise
+            // by 1e-6 there); everything else follows the reference formula.
+            if (var <= 1e-10 * m2) {
+                inv_x = 0.0;
+            } else {
+                inv_x = 1.0 / fmax(sqrt(var + 1e-12), 1e-6);
+            }
+            mu_x = m;
+        }
+    }
+    if ((X & 1) == 0) {
+        stats[k].mu_c = mu_x;
+        stats[k].inv_c = inv_x;
+        stats[k].mhat_c = mhat;
+        stats[k].rawmean_c = k < rank ? m : 0.0;
+    } else {
+        stats[k].mu_s = mu_x;
+        stats[k].inv_s = inv_x;
+        stats[k].mhat_s = mhat;
+        stats[k].rawmean_s = k < rank ? m : 0.0;
+    }
+}
+
 // Normalisation stats and the Gram matrix of the normalised carriers, from
 // the table sums.  _normalize_basis (cresso_v5.py:138-142): zero mean, divide
 // by max(sqrt(mean(x^2) + 1e-12), 1e-6).  The zero mode stays (1, 0).
@@ -259,39 +310,11 @@ __global__ void stats_gram_kernel(ModePack modes, int rank, int rm, double n, co
         }
         m /= n;
         m2 /= n;
-        double mu_x = 0.0, inv_x = 0.0, mhat = 0.0;
-        if (k < rank) {
-            if (modes.m[k].zero) {
-                mu_x = 0.0;
-                inv_x = 1.0;
-                mhat = m;  // unnormalised (1, 0) carrier: mean 1 for cos, 0 for sin
-            } else {
-                const double var = fmax(m2 - m * m, 0.0);
-                // A carrier that is constant over the tensor (an axis of length 1)
-                // normalises to zero (the reference divides fp32 rounding noise
-                // by 1e-6 there); everything else follows the reference formula.
-                if (var <= 1e-10 * m2) {
-                    inv_x = 0.0;
-                } else {
-                    inv_x = 1.0 / fmax(sqrt(var + 1e-12), 1e-6);
-                }
-                mu_x = m;
-            }
-        }
+        double mu_x, inv_x;
+        store_stat(stats, X, rank, k < rank && modes.m[k].zero, m, m2, mu_x, inv_x);
         mu[X] = mu_x;
         inv[X] = inv_x;
         ex2[X] = m;
-        if ((X & 1) == 0) {
-            stats[k].mu_c = mu_x;
-            stats[k].inv_c = inv_x;
-            stats[k].mhat_c = mhat;
-            stats[k].rawmean_c = k < rank ? m : 0.0;
-        } else {
-            stats[k].mu_s = mu_x;
-            stats[k].inv_s = inv_x;
-            stats[k].mhat_s = mhat;
-            stats[k].rawmean_s = k < rank ? m : 0.0;
-        }
     }
     __syncthreads();
     for (int w = threadIdx.x; w < P * P; w += blockDim.x) {
@@ -305,6 +328,90 @@ __global__ void stats_gram_kernel(ModePack modes, int rank, int rm, double n, co
         // mean((raw_X - mu_X)(raw_Y - mu_Y)) = E[XY] - mu_X E[Y] - mu_Y E[X] + mu_X mu_Y
         const double cov = e - mu[X] * ex2[Y] - mu[Y] * ex2[X] + mu[X] * mu[Y];
         gram[w] = inv[X] * inv[Y] * cov;
+    }
+}
+
+// ---- Wide rank (65 to 4096 modes, float64 workspace): the mode parameters are
+// read from device memory, and only each mode's own table sums are formed (the
+// float64 spectral path needs no carrier Gram).
+
+__global__ void build_tables_wide_kernel(const ModeParam* __restrict__ modes, Ldim ldim, int rank, int rm,
+                                         int64_t grows, int64_t gcols, double* rowtab, double* coltab) {
+    const int64_t total = (grows + gcols) * rm;
+    for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < total; t += (int64_t)gridDim.x * blockDim.x) {
+        const int k = (int)(t % rm);
+        const int64_t idx = t / rm;
+        double x1 = 0.0, x2 = 0.0;
+        if (k < rank) table_value(modes[k], ldim.d, idx, grows, gcols, x1, x2);
+        if (idx < grows) {
+            rowtab[(idx * rm + k) * 2 + 0] = x1;
+            rowtab[(idx * rm + k) * 2 + 1] = x2;
+        } else {
+            const int64_t j = idx - grows;
+            coltab[(2 * k) * gcols + j] = x1;
+            coltab[(2 * k + 1) * gcols + j] = x2;
+        }
+    }
+}
+
+// Per axis (blockIdx.y: 0 rows, 1 columns) and mode k: S1[2k + c] = sum x_c and
+// the mode's block D[k][2c + c'] = sum x_c x_c' (c, c' = 0 cos, 1 sin), summed
+// in index order.  Axis a's sums start at tmp + 6 rm a: S1[2 rm], then D[rm][4].
+__global__ void table_sums_blocks_kernel(const double* __restrict__ rowtab, const double* __restrict__ coltab, int rm,
+                                         int64_t grows, int64_t gcols, double* tmp) {
+    const int k = blockIdx.x * blockDim.x + threadIdx.x;
+    if (k >= rm) return;
+    const bool rows = blockIdx.y == 0;
+    const int64_t len = rows ? grows : gcols;
+    double s1 = 0.0, s2 = 0.0, s11 = 0.0, s12 = 0.0, s22 = 0.0;
+    for (int64_t i = 0; i < len; ++i) {
+        double x1, x2;
+        if (rows) {
+            x1 = rowtab[(i * rm + k) * 2];
+            x2 = rowtab[(i * rm + k) * 2 + 1];
+        } else {
+            x1 = coltab[(int64_t)(2 * k) * gcols + i];
+            x2 = coltab[(int64_t)(2 * k + 1) * gcols + i];
+        }
+        s1 += x1;
+        s2 += x2;
+        s11 += x1 * x1;
+        s12 += x1 * x2;
+        s22 += x2 * x2;
+    }
+    double* S1 = tmp + (rows ? 0 : 6 * rm);
+    double* Dk = S1 + 2 * rm + 4 * k;
+    S1[2 * k] = s1;
+    S1[2 * k + 1] = s2;
+    Dk[0] = s11;
+    Dk[1] = s12;
+    Dk[2] = s12;
+    Dk[3] = s22;
+}
+
+// Normalisation stats from the per-mode table sums: the terms of a raw basis
+// function only pair the tables of its own mode.
+__global__ void stats_wide_kernel(const ModeParam* __restrict__ modes, int rank, int rm, double n,
+                                  const double* __restrict__ tmp, ModeStats* stats) {
+    const int P = 2 * rm;
+    const double* A1 = tmp;
+    const double* AD = tmp + P;
+    const double* B1 = tmp + 6 * rm;
+    const double* BD = B1 + P;
+    for (int X = blockIdx.x * blockDim.x + threadIdx.x; X < P; X += gridDim.x * blockDim.x) {
+        const int k = X >> 1;
+        Term t[2];
+        const int nt = basis_terms(X, t);
+        auto blk = [&](const double* Dm, int p, int q) { return Dm[4 * k + 2 * (p - 2 * k) + (q - 2 * k)]; };
+        double m = 0.0, m2 = 0.0;
+        for (int a = 0; a < nt; ++a) {
+            m += t[a].c * A1[t[a].p] * B1[t[a].q];
+            for (int b = 0; b < nt; ++b) m2 += t[a].c * t[b].c * blk(AD, t[a].p, t[b].p) * blk(BD, t[a].q, t[b].q);
+        }
+        m /= n;
+        m2 /= n;
+        double mu_x, inv_x;
+        store_stat(stats, X, rank, k < rank && modes[k].zero, m, m2, mu_x, inv_x);
     }
 }
 
@@ -714,8 +821,8 @@ int cresso_shape_workspace64_bytes(int64_t ndim, const int64_t* shape, int64_t r
     int st = checked_shape(ndim, shape, &grows, &gcols);
     if (st) return st;
     CRESSO_REQUIRE(bytes != nullptr, CRESSO_EINVAL, "shape_workspace64_bytes: NULL output");
-    CRESSO_REQUIRE(rank >= 1 && rank <= kMaxRankPlain, CRESSO_EUNSUPPORTED,
-                   "rank must be in [1, %d] on the CUDA path (got %lld)", kMaxRankPlain, (long long)rank);
+    CRESSO_REQUIRE(rank >= 1 && rank <= kMaxRankWide, CRESSO_EUNSUPPORTED,
+                   "rank must be in [1, %d] on the CUDA path (got %lld)", kMaxRankWide, (long long)rank);
     *bytes = shape_ws64_layout(ndim, grows, gcols, rank, rank_pad(rank)).bytes;
     return CRESSO_OK;
 }
@@ -725,18 +832,41 @@ int cresso_shape_workspace64_init(int64_t ndim, const int64_t* shape, int64_t ra
     int64_t grows, gcols;
     int st = checked_shape(ndim, shape, &grows, &gcols);
     if (st) return st;
-    CRESSO_REQUIRE(rank >= 1 && rank <= kMaxRankPlain, CRESSO_EUNSUPPORTED,
-                   "rank must be in [1, %d] on the CUDA path (got %lld)", kMaxRankPlain, (long long)rank);
+    CRESSO_REQUIRE(rank >= 1 && rank <= kMaxRankWide, CRESSO_EUNSUPPORTED,
+                   "rank must be in [1, %d] on the CUDA path (got %lld)", kMaxRankWide, (long long)rank);
     CRESSO_REQUIRE(freqs != nullptr && ws != nullptr, CRESSO_EINVAL, "shape_workspace64_init: NULL pointer");
     const int rm = rank_pad(rank);
     ShapeWsHeader h = shape_ws64_layout(ndim, grows, gcols, rank, rm);
     cudaStream_t s = (cudaStream_t)stream;
     char* base = (char*)ws;
-    ModePack modes = make_modes(ndim, shape, rank, freqs);
     double* rowtab = reinterpret_cast<double*>(base + h.off_rowtab);
     double* coltab = reinterpret_cast<double*>(base + h.off_coltab);
     double* tmp = reinterpret_cast<double*>(base + h.off_tmp);
     const int64_t cells = (grows + gcols) * rm;
+    if (rm > kMaxRankPlain) {
+        // wide rank: the mode parameters go to the workspace (after the table sums)
+        std::vector<ModeParam> mv((size_t)rm);
+        memset(mv.data(), 0, sizeof(ModeParam) * mv.size());
+        for (int64_t k = 0; k < rank; ++k) fill_mode(mv[(size_t)k], ndim, k, freqs);
+        Ldim ld{};
+        for (int64_t a = 0; a + 1 < ndim; ++a) ld.d[a] = shape[a];
+        ModeParam* d_modes = reinterpret_cast<ModeParam*>(base + h.off_tmp + align_up(2 * (2 * rm + 4 * rm) * 8, 256));
+        // pageable source: the copy has staged its bytes when it returns
+        CRESSO_CUDA(cudaMemcpyAsync(d_modes, mv.data(), sizeof(ModeParam) * mv.size(), cudaMemcpyHostToDevice, s));
+        build_tables_wide_kernel<<<(int)std::min<int64_t>(ceil_div(cells, kThreads), 4096), kThreads, 0, s>>>(
+            d_modes, ld, (int)rank, rm, grows, gcols, rowtab, coltab);
+        CRESSO_LAUNCHED("build_tables_wide_kernel");
+        table_sums_blocks_kernel<<<dim3((unsigned)ceil_div(rm, kThreads), 2), kThreads, 0, s>>>(rowtab, coltab, rm, grows,
+                                                                                                 gcols, tmp);
+        CRESSO_LAUNCHED("table_sums_blocks_kernel");
+        stats_wide_kernel<<<(int)ceil_div(2 * rm, kThreads), kThreads, 0, s>>>(
+            d_modes, (int)rank, rm, (double)grows * (double)gcols, tmp, reinterpret_cast<ModeStats*>(base + h.off_stats));
+        CRESSO_LAUNCHED("stats_wide_kernel");
+        CRESSO_CUDA(cudaMemcpyAsync(ws, &h, sizeof(h), cudaMemcpyHostToDevice, s));
+        CRESSO_CUDA(cudaStreamSynchronize(s));
+        return CRESSO_OK;
+    }
+    ModePack modes = make_modes(ndim, shape, rank, freqs);
     build_tables_kernel<double><<<(int)std::min<int64_t>(ceil_div(cells, kThreads), 4096), kThreads, 0, s>>>(
         modes, (int)rank, rm, grows, gcols, rowtab, coltab);
     CRESSO_LAUNCHED("build_tables_kernel<double>");

@@ -15,7 +15,9 @@ namespace cresso {
 constexpr int kThreads = 256;  // every kernel of the library runs 256-thread blocks
 constexpr int kWarps = kThreads / 32;
 constexpr int kMaxRank = 16;       // the fused float32 spectral path
-constexpr int kMaxRankPlain = 64;  // the float64-arithmetic spectral path and its shape workspace
+constexpr int kMaxRankPlain = 64;  // the float64-arithmetic spectral path with its modes in registers
+constexpr int kMaxRankWide = 4096; // the same path with its modes in memory (rank 65 to 4096)
+constexpr int kChunkW = 32;        // modes per projection chunk of the wide-rank kernels
 constexpr int kMaxTB = 8192;   // hash_tables * hash_bins held in shared memory
 constexpr int kMaxBins = 4096; // same bound as the reference CUDA hash path (cresso_v5.py:1002)
 
@@ -103,6 +105,7 @@ __host__ inline ShapeWsHeader shape_ws_layout(int64_t ndim, int64_t grows, int64
 // Float64 shape workspace (float64 parameters on the spectral route): float64
 // axis tables rowtab [grows][rm][2] and coltab [2 rm][gcols], the carrier stats
 // and Gram from them; no hash counts.
+constexpr int64_t kModeParamBytes = 512;  // room for one mode's carrier parameters (basis_ws.cu ModeParam)
 constexpr int64_t kShapeWs64Magic = 0x43524553534f3544LL;  // "CRESSO5D"
 __host__ inline ShapeWsHeader shape_ws64_layout(int64_t ndim, int64_t grows, int64_t gcols, int64_t rank, int64_t rm) {
     ShapeWsHeader h{};
@@ -119,17 +122,27 @@ __host__ inline ShapeWsHeader shape_ws64_layout(int64_t ndim, int64_t grows, int
     h.off_coltab = off;
     off = align_up(off + 2 * rm * gcols * 8, 256);
     h.off_stats = off;
-    off = align_up(off + 64 * kMaxRankPlain, 256);  // ModeStats: 8 doubles per mode
+    off = align_up(off + 64 * (rm > kMaxRankPlain ? rm : kMaxRankPlain), 256);  // ModeStats: 8 doubles per mode
     h.off_gram = off;
-    off = align_up(off + (2 * rm) * (2 * rm) * 8, 256);
-    h.off_tmp = off;
-    off = align_up(off + 2 * (2 * rm + 4 * rm * rm) * 8, 256);
+    if (rm <= kMaxRankPlain) {
+        off = align_up(off + (2 * rm) * (2 * rm) * 8, 256);
+        h.off_tmp = off;
+        off = align_up(off + 2 * (2 * rm + 4 * rm * rm) * 8, 256);
+    } else {
+        // wide rank: no carrier Gram (the float64 path does not use it); per axis the
+        // table sums S1[2 rm] and each mode's own 2 x 2 block of cross sums, then the
+        // mode parameters (kModeParamBytes per mode) uploaded for the set-up kernels
+        h.off_tmp = off;
+        off = align_up(off + 2 * (2 * rm + 4 * rm) * 8, 256);
+        off = align_up(off + kModeParamBytes * rm, 256);
+    }
     h.off_counts = off;
     h.bytes = off;
     return h;
 }
 
 __host__ __device__ inline int rank_pad(int64_t rank) {
+    if (rank > kMaxRankPlain) return (int)align_up(rank, kChunkW);  // wide rank: whole projection chunks
     return rank <= 4 ? 4 : (rank <= 8 ? 8 : (rank <= 16 ? 16 : (rank <= 32 ? 32 : 64)));
 }
 

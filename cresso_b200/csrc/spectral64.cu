@@ -1,6 +1,6 @@
 // Spectral-route CRESSO5 step for float64 parameters (cresso_v5.py:945-1353
 // with float64 work and state, cresso_v5.py:119-124), and for float32 /
-// float16 / bfloat16 parameters of rank 17 to 64 (float32 state).
+// float16 / bfloat16 parameters of rank 17 to 4096 (float32 state).
 //
 // The float32 path (spectral.cu) is built around float32 tiles, tf32 tensor-core
 // reconstructions, fixed-point bin sums and at most 16 modes held in registers;
@@ -22,7 +22,8 @@
 // (cresso_shape_workspace64_init).  Block partial sums are written per block and
 // added in block order by the one-block finalize kernels; the bin sums inside a
 // block use shared-memory float64 atomics (their order, and so the last bit of
-// a bin sum, can vary from run to run).
+// a bin sum, can vary from run to run).  Above rank 64 the modes leave the
+// registers (the wide-rank kernels s64w_*, RM == 0 in the launch templates).
 #include <cuda_runtime.h>
 #include <math.h>
 #include <stdint.h>
@@ -68,6 +69,7 @@ struct alignas(16) T64 {
     P *omega, *q_cos, *q_sin, *p_cos, *p_sin, *m_cos, *m_sin, *mp_cos, *mp_sin, *ca_cos, *ca_sin, *conf;
     P *h_energy, *h_impulse, *h_refractory, *force_rms, *drive_energy, *surprise, *action;
     int32_t R, T, B, hard, hash_on, echo_on, inst, local_on, f32, pdt;
+    int32_t RW, pad_;  // padded rank: the mode stride of the tables and coefficient vectors
     double hp[64];
 };
 
@@ -89,6 +91,10 @@ struct alignas(16) Buf64 {
     double* rowsum;  // [rows] instant-metric density per row, then its log factor
     double* colsum;  // [cols] same per column
     double* tbuf;    // [N] tangent
+    // wide rank only (rank > kMaxRankPlain):
+    double* wcoef;   // [W_COUNT][RW] reconstruction coefficients and contact temporaries
+    double* pbuf;    // [N] port field (P3)
+    double* rec2;    // [chunks][blocks][kRec2] per-chunk projection records
     int blocks;      // blocks of this tensor in the element passes (records in rec)
 };
 
@@ -156,10 +162,12 @@ __device__ __forceinline__ double clampd(double v, double lo, double hi) { retur
 __device__ __forceinline__ double sigmoidd(double x) { return 1.0 / (1.0 + exp(-x)); }
 __device__ __forceinline__ double sgnd(double x) { return x > 0.0 ? 1.0 : (x < 0.0 ? -1.0 : 0.0); }
 
-// Normalised carrier (cos, sin) of mode k at row r, column c.
-template <int RM, typename P>
-__device__ __forceinline__ void carrier(const T64<P>& D, int64_t r, int64_t c, int k, double& ch, double& sh) {
-    const double a1 = D.rowtab[(r * RM + k) * 2], a2 = D.rowtab[(r * RM + k) * 2 + 1];
+// Normalised carrier (cos, sin) of mode k at row r, column c; the row table
+// holds rm modes per row.
+template <typename P>
+__device__ __forceinline__ void carrier_at(const T64<P>& D, int64_t rm, int64_t r, int64_t c, int k, double& ch,
+                                           double& sh) {
+    const double a1 = D.rowtab[(r * rm + k) * 2], a2 = D.rowtab[(r * rm + k) * 2 + 1];
     const double b1 = D.coltab[(int64_t)(2 * k) * D.cols + c], b2 = D.coltab[(int64_t)(2 * k + 1) * D.cols + c];
     double rc, rs;
     if (mode_is_product(k)) {
@@ -172,6 +180,11 @@ __device__ __forceinline__ void carrier(const T64<P>& D, int64_t r, int64_t c, i
     const ModeStats& m = D.stats[k];
     ch = (rc - m.mu_c) * m.inv_c;
     sh = (rs - m.mu_s) * m.inv_s;
+}
+
+template <int RM, typename P>
+__device__ __forceinline__ void carrier(const T64<P>& D, int64_t r, int64_t c, int k, double& ch, double& sh) {
+    carrier_at(D, RM, r, c, k, ch, sh);
 }
 
 // Normalised carriers (cos, sin) of modes 0..RM-1 at row r, column c.
@@ -359,57 +372,143 @@ __global__ void __launch_bounds__(kThreads) s64_colsum(G64<P> G) {
     Bf.tbuf[chunk * D.cols + c] = s;
 }
 
+// Hash energy reservoirs and the per-bin log metric (cresso_v5.py:995-1056)
+// from the blocks' bin sums and counts: block b's sums at rec[b * L + off + i],
+// its counts TB further on.  Every thread calls.
+template <typename P>
+__device__ void fin2_hash(const T64<P>& D, const Buf64& Bf, int64_t L, int64_t off) {
+    __shared__ double emean[8];
+    const int tid = threadIdx.x;
+    const int TB = D.T * D.B;
+    const double eps = D.hp[Q_EPS];
+    for (int i = tid; i < TB; i += kThreads) {
+        double s = 0.0, n = 0.0;
+        for (int b = 0; b < Bf.blocks; ++b) {
+            s += Bf.rec[(int64_t)b * L + off + i];
+            n += Bf.rec[(int64_t)b * L + off + TB + i];
+        }
+        Bf.counts[i] = n;
+        const double cell = s / fmax(n, 1.0);
+        D.h_energy[i] = reservoir((double)D.h_energy[i], cell, D.hp[Q_HD], D.step);
+    }
+    __syncthreads();
+    if (tid < D.T) {
+        double s = 0.0;
+        for (int b = 0; b < D.B; ++b) s += D.h_energy[tid * D.B + b];
+        emean[tid] = fmax(s / (double)D.B, eps);
+    }
+    __syncthreads();
+    const double xp = D.hp[Q_HMC] / fmax(0.25, D.hp[Q_EP]);
+    for (int i = tid; i < TB; i += kThreads) {
+        const double hm = fmax(D.h_energy[i] / emean[i / D.B], eps);
+        Bf.lterm[i] = log(fmax(clampd(pow(hm, xp), 0.08, 12.0), eps));
+    }
+}
+
+// Thread 0: the density mean, the instant-metric mean and exponent.
+template <typename P>
+__device__ void fin2_scalars(const T64<P>& D, C64& C, double sum_l, double sum_dens) {
+    const double N = (double)D.N, eps = D.hp[Q_EPS];
+    C.meanL = fmax(sum_l / N, eps);
+    C.gm = fmax(sum_dens / N, eps);
+    const double pw = fmax(D.hp[Q_IP], 0.25);
+    const double ic = D.hard ? D.hp[Q_IC] : 0.0;
+    C.kk = ic / ((double)D.ndim * pw);
+}
+
+// Metric oscillator of mode k < R driven by the density projection (pc, ps)
+// (cresso_v5.py:1057-1093), and the mode's log-metric and prediction
+// coefficients (the prediction from the old oscillators, cresso_v5.py:1125-1129).
+template <typename P>
+__device__ void fin2_mode(const T64<P>& D, int k, double pc, double ps, double shrink, double& m_al, double& m_be,
+                          double& p_al, double& p_be) {
+    const double mdt = D.hp[Q_MDT];
+    const double damp = fmax(0.0, 1.0 - mdt * D.hp[Q_MF]);
+    const double om2 = D.omega[k] * D.omega[k];
+    double mp = D.mp_cos[k] * damp + mdt * (pc - om2 * D.m_cos[k]);
+    double mq = clampd(D.m_cos[k] + mdt * mp, -3.0, 3.0);
+    D.mp_cos[k] = mp;
+    D.m_cos[k] = mq;
+    m_al = mq * shrink;
+    mp = D.mp_sin[k] * damp + mdt * (ps - om2 * D.m_sin[k]);
+    mq = clampd(D.m_sin[k] + mdt * mp, -3.0, 3.0);
+    D.mp_sin[k] = mp;
+    D.m_sin[k] = mq;
+    m_be = mq * shrink;
+    const double g = sigmoidd(D.hp[Q_CONFG] * D.conf[k]);
+    p_al = D.q_cos[k] * shrink * g;
+    p_be = D.q_sin[k] * shrink * g;
+}
+
+// Instant-metric factors (cresso_v5.py:243-262): logs of the axis means over the
+// mean.  Every thread calls, after C.gm is set.
+template <typename P>
+__device__ void fin2_axes(const T64<P>& D, const Buf64& Bf, double gm) {
+    __shared__ double s_lax[kMaxLeadSum64];
+    const int tid = threadIdx.x;
+    const double N = (double)D.N, eps = D.hp[Q_EPS];
+    const int64_t chunks = col_chunks(D.rows);
+    for (int64_t c = tid; c < D.cols; c += kThreads) {
+        double s = 0.0;
+        for (int64_t ch = 0; ch < chunks; ++ch) s += Bf.tbuf[ch * D.cols + c];
+        Bf.colsum[c] = log(fmax((s / (double)D.rows) / gm, eps));
+    }
+    if (D.ndim == 2) {
+        for (int64_t r = tid; r < D.rows; r += kThreads)
+            Bf.rowsum[r] = log(fmax((Bf.rowsum[r] / (double)D.cols) / gm, eps));
+        return;
+    }
+    // rank >= 3: per leading axis and coordinate the marginal mean (a fixed-order sum of
+    // the row sums with that coordinate); a row's log factor sums its axes' logs
+    const int nl = (int)D.ndim - 1;
+    int lead_sum = 0;
+    for (int a = 0; a < nl; ++a) lead_sum += (int)D.dims[a];
+    for (int j = tid; j < lead_sum; j += kThreads) {
+        int a = 0, c = j;
+        while (c >= D.dims[a]) {
+            c -= (int)D.dims[a];
+            ++a;
+        }
+        int64_t inner = 1;
+        for (int b = a + 1; b < nl; ++b) inner *= D.dims[b];
+        const int64_t outer = D.rows / (D.dims[a] * inner);
+        double m = 0.0;
+        for (int64_t o = 0; o < outer; ++o)
+            for (int64_t i = 0; i < inner; ++i) m += Bf.rowsum[(o * D.dims[a] + c) * inner + i];
+        s_lax[j] = log(fmax((m / (N / (double)D.dims[a])) / gm, eps));
+    }
+    __syncthreads();
+    for (int64_t r = tid; r < D.rows; r += kThreads) {
+        double lsum = 0.0;
+        int64_t rem = r;
+        int off = lead_sum;
+        for (int a = nl - 1; a >= 0; --a) {
+            off -= (int)D.dims[a];
+            lsum += s_lax[off + (int)(rem % D.dims[a])];
+            rem /= D.dims[a];
+        }
+        Bf.rowsum[r] = lsum;
+    }
+}
+
 template <int RM, typename P>
 __global__ void __launch_bounds__(kThreads) s64_fin2(G64<P> G) {
     S64_BIND_TENSOR();
     __shared__ double tot[2 + 2 * RM];
-    __shared__ double emean[8];
-    __shared__ double s_lax[kMaxLeadSum64];
     const int tid = threadIdx.x;
     const int TB = D.T * D.B;
     const int L = 2 + 2 * RM + 2 * TB;
-    const double N = (double)D.N, eps = D.hp[Q_EPS];
+    const double N = (double)D.N;
     C64& C = *Bf.cst;
     for (int j = tid; j < 2 + 2 * RM; j += kThreads) {
         double s = 0.0;
         for (int b = 0; b < Bf.blocks; ++b) s += Bf.rec[(int64_t)b * L + j];
         tot[j] = s;
     }
-    // ---- hash energy and the per-bin log metric (cresso_v5.py:995-1056)
-    if (D.hash_on) {
-        for (int i = tid; i < TB; i += kThreads) {
-            double s = 0.0, n = 0.0;
-            for (int b = 0; b < Bf.blocks; ++b) {
-                s += Bf.rec[(int64_t)b * L + 2 + 2 * RM + i];
-                n += Bf.rec[(int64_t)b * L + 2 + 2 * RM + TB + i];
-            }
-            Bf.counts[i] = n;
-            const double cell = s / fmax(n, 1.0);
-            D.h_energy[i] = reservoir((double)D.h_energy[i], cell, D.hp[Q_HD], D.step);
-        }
-        __syncthreads();
-        if (tid < D.T) {
-            double s = 0.0;
-            for (int b = 0; b < D.B; ++b) s += D.h_energy[tid * D.B + b];
-            emean[tid] = fmax(s / (double)D.B, eps);
-        }
-        __syncthreads();
-        const double xp = D.hp[Q_HMC] / fmax(0.25, D.hp[Q_EP]);
-        for (int i = tid; i < TB; i += kThreads) {
-            const double hm = fmax(D.h_energy[i] / emean[i / D.B], eps);
-            Bf.lterm[i] = log(fmax(clampd(pow(hm, xp), 0.08, 12.0), eps));
-        }
-    }
+    if (D.hash_on) fin2_hash(D, Bf, L, 2 + 2 * RM);
     __syncthreads();
-    // ---- metric oscillator and the log-metric coefficients (cresso_v5.py:1057-1093)
     const double shrink = 1.0 / sqrt(fmax(1.0, 0.7 * log2((double)D.R + 1.0)));
-    if (tid == 0) {
-        C.meanL = fmax(tot[0] / N, eps);
-        C.gm = fmax(tot[1] / N, eps);
-        const double pw = fmax(D.hp[Q_IP], 0.25);
-        const double ic = D.hard ? D.hp[Q_IC] : 0.0;
-        C.kk = ic / ((double)D.ndim * pw);
-    }
+    if (tid == 0) fin2_scalars(D, C, tot[0], tot[1]);
     __syncthreads();
     if (tid < RM) {
         const int k = tid;
@@ -417,74 +516,37 @@ __global__ void __launch_bounds__(kThreads) s64_fin2(G64<P> G) {
             const ModeStats& m = D.stats[k];
             const double pc = tot[2 + k] / N / C.meanL - m.mhat_c;
             const double ps = tot[2 + RM + k] / N / C.meanL - m.mhat_s;
-            const double mdt = D.hp[Q_MDT];
-            const double damp = fmax(0.0, 1.0 - mdt * D.hp[Q_MF]);
-            const double om2 = D.omega[k] * D.omega[k];
-            double mp = D.mp_cos[k] * damp + mdt * (pc - om2 * D.m_cos[k]);
-            double mq = clampd(D.m_cos[k] + mdt * mp, -3.0, 3.0);
-            D.mp_cos[k] = mp;
-            D.m_cos[k] = mq;
-            C.m_al[k] = mq * shrink;
-            mp = D.mp_sin[k] * damp + mdt * (ps - om2 * D.m_sin[k]);
-            mq = clampd(D.m_sin[k] + mdt * mp, -3.0, 3.0);
-            D.mp_sin[k] = mp;
-            D.m_sin[k] = mq;
-            C.m_be[k] = mq * shrink;
-            // prediction from the old oscillators (cresso_v5.py:1125-1129)
-            const double g = sigmoidd(D.hp[Q_CONFG] * D.conf[k]);
-            C.p_al[k] = D.q_cos[k] * shrink * g;
-            C.p_be[k] = D.q_sin[k] * shrink * g;
+            fin2_mode(D, k, pc, ps, shrink, C.m_al[k], C.m_be[k], C.p_al[k], C.p_be[k]);
         } else {
             C.m_al[k] = C.m_be[k] = C.p_al[k] = C.p_be[k] = 0.0;
         }
     }
-    // ---- instant metric factors (cresso_v5.py:243-262): logs of the axis means over the mean
     if (D.inst && D.ndim >= 2) {
         __syncthreads();
-        const double gm = C.gm;
-        const int64_t chunks = col_chunks(D.rows);
-        for (int64_t c = tid; c < D.cols; c += kThreads) {
-            double s = 0.0;
-            for (int64_t ch = 0; ch < chunks; ++ch) s += Bf.tbuf[ch * D.cols + c];
-            Bf.colsum[c] = log(fmax((s / (double)D.rows) / gm, eps));
-        }
-        if (D.ndim == 2) {
-            for (int64_t r = tid; r < D.rows; r += kThreads)
-                Bf.rowsum[r] = log(fmax((Bf.rowsum[r] / (double)D.cols) / gm, eps));
-            return;
-        }
-        // rank >= 3: per leading axis and coordinate the marginal mean (a fixed-order sum of
-        // the row sums with that coordinate); a row's log factor sums its axes' logs
-        const int nl = (int)D.ndim - 1;
-        int lead_sum = 0;
-        for (int a = 0; a < nl; ++a) lead_sum += (int)D.dims[a];
-        for (int j = tid; j < lead_sum; j += kThreads) {
-            int a = 0, c = j;
-            while (c >= D.dims[a]) {
-                c -= (int)D.dims[a];
-                ++a;
-            }
-            int64_t inner = 1;
-            for (int b = a + 1; b < nl; ++b) inner *= D.dims[b];
-            const int64_t outer = D.rows / (D.dims[a] * inner);
-            double m = 0.0;
-            for (int64_t o = 0; o < outer; ++o)
-                for (int64_t i = 0; i < inner; ++i) m += Bf.rowsum[(o * D.dims[a] + c) * inner + i];
-            s_lax[j] = log(fmax((m / (N / (double)D.dims[a])) / gm, eps));
-        }
-        __syncthreads();
-        for (int64_t r = tid; r < D.rows; r += kThreads) {
-            double lsum = 0.0;
-            int64_t rem = r;
-            int off = lead_sum;
-            for (int a = nl - 1; a >= 0; --a) {
-                off -= (int)D.dims[a];
-                lsum += s_lax[off + (int)(rem % D.dims[a])];
-                rem /= D.dims[a];
-            }
-            Bf.rowsum[r] = lsum;
-        }
+        fin2_axes(D, Bf, C.gm);
     }
+}
+
+// Tangent of element e (row r, column c) with force f, relative magnitude rel
+// and clamped log metric lm (cresso_v5.py:1095-1123).
+template <typename P>
+__device__ __forceinline__ double tangent_of(const T64<P>& D, const Buf64& Bf, const C64& C, int64_t e, int64_t r,
+                                             int64_t c, double f, double rel, double lm) {
+    const double eps = D.hp[Q_EPS];
+    const double metric = clampd(exp(D.hp[Q_MC] * lm), 0.06, 16.0);
+    const double local = D.local_on ? clampd(1.0 + D.hp[Q_LS] * sqrt(fmin(rel, 100.0)), 1.0, 8.0) : 1.0;
+    double inst = 1.0;
+    if (D.inst) {
+        const double lg = D.ndim >= 2 ? Bf.rowsum[r] + Bf.colsum[c] : log(fmax(idens_of(D, rel) / C.gm, eps));
+        inst = clampd(exp(C.kk * lg), 0.08, 12.0);
+    }
+    double hm = 1.0;
+    if (D.hash_on) {
+        double lsum = 0.0;
+        for (int t = 0; t < D.T; ++t) lsum += Bf.lterm[t * D.B + (int)hash_bin(e, D.B, t)];
+        hm = clampd(exp(lsum / (double)D.T), 0.08, 12.0);
+    }
+    return clampd(f / (C.scale * metric * local * inst * hm + eps), -1.0e4, 1.0e4);
 }
 
 // ---- P3: tangent, error, projections of the port and of the tangent, port bins.
@@ -500,7 +562,7 @@ __global__ void __launch_bounds__(kThreads) s64_p3(G64<P> G) {
         for (int i = threadIdx.x; i < TB; i += kThreads) sbin[i] = 0.0;
     __syncthreads();
     const C64& C = *Bf.cst;
-    const double scale = C.scale, eps = D.hp[Q_EPS], mc = D.hp[Q_MC], ls = D.hp[Q_LS], tm = D.hp[Q_TM];
+    const double scale = C.scale, tm = D.hp[Q_TM];
     double v[1 + 4 * RM];
 #pragma unroll
     for (int j = 0; j < 1 + 4 * RM; ++j) v[j] = 0.0;
@@ -511,20 +573,7 @@ __global__ void __launch_bounds__(kThreads) s64_p3(G64<P> G) {
         double ch[RM], sh[RM];
         carriers<RM>(D, r, c, ch, sh);
         const double lm = clampd(recon<RM>(C.m_al, C.m_be, ch, sh), -3.0, 3.0);
-        const double metric = clampd(exp(mc * lm), 0.06, 16.0);
-        const double local = D.local_on ? clampd(1.0 + ls * sqrt(fmin(rel, 100.0)), 1.0, 8.0) : 1.0;
-        double inst = 1.0;
-        if (D.inst) {
-            const double lg = D.ndim >= 2 ? Bf.rowsum[r] + Bf.colsum[c] : log(fmax(idens_of(D, rel) / C.gm, eps));
-            inst = clampd(exp(C.kk * lg), 0.08, 12.0);
-        }
-        double hm = 1.0;
-        if (hash_on) {
-            double lsum = 0.0;
-            for (int t = 0; t < D.T; ++t) lsum += Bf.lterm[t * D.B + (int)hash_bin(e, D.B, t)];
-            hm = clampd(exp(lsum / (double)D.T), 0.08, 12.0);
-        }
-        const double t = clampd(f / (scale * metric * local * inst * hm + eps), -1.0e4, 1.0e4);
+        const double t = tangent_of(D, Bf, C, e, r, c, f, rel, lm);
         Bf.tbuf[e] = t;
         const double err = t - recon<RM>(C.p_al, C.p_be, ch, sh);
         v[0] += err * err;
@@ -546,49 +595,32 @@ __global__ void __launch_bounds__(kThreads) s64_p3(G64<P> G) {
         for (int i = threadIdx.x; i < TB; i += kThreads) rec[1 + 4 * RM + i] = sbin[i];
 }
 
-template <int RM, typename P>
-__global__ void __launch_bounds__(kThreads) s64_fin3(G64<P> G) {
-    S64_BIND_TENSOR();
-    __shared__ double tot[1 + 4 * RM];
-    const int tid = threadIdx.x;
+// Hash impulse reservoirs (cresso_v5.py:1140-1184) from the blocks' port bin
+// sums at rec[b * L + off + i].  Every thread calls.
+template <typename P>
+__device__ void fin3_hash(const T64<P>& D, const Buf64& Bf, int64_t L, int64_t off) {
     const int TB = D.T * D.B;
-    const int L = 1 + 4 * RM + TB;
-    const double N = (double)D.N, eps = D.hp[Q_EPS];
-    C64& C = *Bf.cst;
-    for (int j = tid; j < 1 + 4 * RM; j += kThreads) {
+    const double hd = D.hp[Q_HD], hid = D.hp[Q_HID], rg = D.hp[Q_RG];
+    for (int i = threadIdx.x; i < TB; i += kThreads) {
         double s = 0.0;
-        for (int b = 0; b < Bf.blocks; ++b) s += Bf.rec[(int64_t)b * L + j];
-        tot[j] = s;
+        for (int b = 0; b < Bf.blocks; ++b) s += Bf.rec[(int64_t)b * L + off + i];
+        const double cell = s / fmax(Bf.counts[i], 1.0);
+        const double href = D.h_refractory[i] * hd + (1.0 - hd) * fabs(cell);
+        D.h_refractory[i] = href;
+        const double hg = 1.0 / (1.0 + rg * href);
+        const double himp = D.h_impulse[i] * hid + (1.0 - hid) * (cell * hg);
+        D.h_impulse[i] = himp;
+        Bf.impv[i] = himp;
     }
-    // ---- hash impulse reservoirs (cresso_v5.py:1140-1184)
-    if (D.hash_on) {
-        const double hd = D.hp[Q_HD], hid = D.hp[Q_HID], rg = D.hp[Q_RG];
-        for (int i = tid; i < TB; i += kThreads) {
-            double s = 0.0;
-            for (int b = 0; b < Bf.blocks; ++b) s += Bf.rec[(int64_t)b * L + 1 + 4 * RM + i];
-            const double cell = s / fmax(Bf.counts[i], 1.0);
-            const double href = D.h_refractory[i] * hd + (1.0 - hd) * fabs(cell);
-            D.h_refractory[i] = href;
-            const double hg = 1.0 / (1.0 + rg * href);
-            const double himp = D.h_impulse[i] * hid + (1.0 - hid) * (cell * hg);
-            D.h_impulse[i] = himp;
-            Bf.impv[i] = himp;
-        }
-    }
-    __syncthreads();
-    if (tid != 0) return;
-    // ---- surprise (cresso_v5.py:1132-1134)
-    const double S = reservoir((double)*D.surprise, sqrt(tot[0] / N + eps), D.hp[Q_SD], D.step);
-    *D.surprise = S;
-    C.S = S;
+}
+
+// Thread 0: confidence from the old oscillators (cresso_v5.py:1186-1202), then
+// the contact oscillators, cos half then sin half (cresso_v5.py:914-943,
+// 1204-1250), driven by the port projection (pc, ps); gp is R doubles of room.
+template <typename P>
+__device__ void fin3_contact(const T64<P>& D, double S, const double* pc, const double* ps, double* gp) {
     const int R = D.R;
-    const double shrink = 1.0 / sqrt(fmax(1.0, 0.7 * log2((double)R + 1.0)));
-    double pc[kMaxRankPlain], ps[kMaxRankPlain];
-    for (int k = 0; k < R; ++k) {
-        pc[k] = tot[1 + k] / N;
-        ps[k] = tot[1 + RM + k] / N;
-    }
-    // ---- confidence from the old oscillators (cresso_v5.py:1186-1202)
+    const double eps = D.hp[Q_EPS];
     const double cd = D.hp[Q_CD];
     for (int k = 0; k < R; ++k) {
         const double qc = D.q_cos[k], qs = D.q_sin[k];
@@ -596,7 +628,6 @@ __global__ void __launch_bounds__(kThreads) s64_fin3(G64<P> G) {
         const double support = (pc[k] * qc + ps[k] * qs) / (pe * sqrt(qc * qc + qs * qs + eps) + eps);
         D.conf[k] = clampd(D.conf[k] * cd + (1.0 - cd) * clampd(support, -1.0, 1.0), -4.0, 4.0);
     }
-    // ---- contact oscillators, cos half then sin half (cresso_v5.py:914-943, 1204-1250)
     const double dt = D.hp[Q_DT], rd = D.hp[Q_REFD], rg = D.hp[Q_RG];
     const double plast = 1.0 + D.hp[Q_SG] * S / (1.0 + S);
     const double brake = 1.0 / (1.0 + D.hp[Q_SB] * S);
@@ -606,7 +637,6 @@ __global__ void __launch_bounds__(kThreads) s64_fin3(G64<P> G) {
         P* p = half ? D.p_sin : D.p_cos;
         P* ca = half ? D.ca_sin : D.ca_cos;
         const double* port = half ? ps : pc;
-        double gp[kMaxRankPlain];
         double p2 = 0.0, oq2 = 0.0, pp = 0.0;
         for (int k = 0; k < R; ++k) {
             ca[k] = ca[k] * rd + (1.0 - rd) * fabs(port[k]);
@@ -628,6 +658,37 @@ __global__ void __launch_bounds__(kThreads) s64_fin3(G64<P> G) {
         }
     }
     *D.action = action;
+}
+
+template <int RM, typename P>
+__global__ void __launch_bounds__(kThreads) s64_fin3(G64<P> G) {
+    S64_BIND_TENSOR();
+    __shared__ double tot[1 + 4 * RM];
+    const int tid = threadIdx.x;
+    const int TB = D.T * D.B;
+    const int L = 1 + 4 * RM + TB;
+    const double N = (double)D.N, eps = D.hp[Q_EPS];
+    C64& C = *Bf.cst;
+    for (int j = tid; j < 1 + 4 * RM; j += kThreads) {
+        double s = 0.0;
+        for (int b = 0; b < Bf.blocks; ++b) s += Bf.rec[(int64_t)b * L + j];
+        tot[j] = s;
+    }
+    if (D.hash_on) fin3_hash(D, Bf, L, 1 + 4 * RM);
+    __syncthreads();
+    if (tid != 0) return;
+    // ---- surprise (cresso_v5.py:1132-1134)
+    const double S = reservoir((double)*D.surprise, sqrt(tot[0] / N + eps), D.hp[Q_SD], D.step);
+    *D.surprise = S;
+    C.S = S;
+    const int R = D.R;
+    const double shrink = 1.0 / sqrt(fmax(1.0, 0.7 * log2((double)R + 1.0)));
+    double pc[kMaxRankPlain], ps[kMaxRankPlain], gp[kMaxRankPlain];
+    for (int k = 0; k < R; ++k) {
+        pc[k] = tot[1 + k] / N;
+        ps[k] = tot[1 + RM + k] / N;
+    }
+    fin3_contact(D, S, pc, ps, gp);
     // ---- second prediction and echo coefficients (cresso_v5.py:1252-1258)
     for (int k = 0; k < RM; ++k) {
         if (k < R) {
@@ -643,16 +704,280 @@ __global__ void __launch_bounds__(kThreads) s64_fin3(G64<P> G) {
     C.clip = D.hp[Q_CLIP];
 }
 
+// ---- Wide rank (kMaxRankPlain < rank <= kMaxRankWide)
+// The modes no longer fit registers.  Reconstructions loop over the modes with
+// their coefficients in the scratch (Bf.wcoef); projections run in chunks of
+// kChunkW modes, chunk y of a pass being the blocks with blockIdx.y == y, each
+// block writing one record per chunk (Bf.rec2).  P3 is split: an element pass
+// stores the tangent and the port, and a chunked pass projects both from the
+// stored fields, so every pass costs O(rank) per element.
+enum { W_MAL, W_MBE, W_PAL, W_PBE, W_EAL, W_EBE, W_PC, W_PS, W_GP, W_COUNT };
+constexpr int kRec2 = 4 * kChunkW;  // doubles per (chunk, block) record
+
+// Prediction and (when echo) echo at row r, column c from the wide coefficients.
+template <typename P>
+__device__ __forceinline__ void recon_pred_echo_w(const T64<P>& D, const Buf64& Bf, int64_t r, int64_t c, bool echo,
+                                                  double& pred, double& ech) {
+    const int RW = D.RW;
+    const double* pal = Bf.wcoef + W_PAL * RW;
+    const double* pbe = Bf.wcoef + W_PBE * RW;
+    const double* eal = Bf.wcoef + W_EAL * RW;
+    const double* ebe = Bf.wcoef + W_EBE * RW;
+    double a = 0.0, b = 0.0;
+    for (int k = 0; k < D.R; ++k) {
+        double chk, shk;
+        carrier_at(D, RW, r, c, k, chk, shk);
+        a += chk * pal[k];
+        a += shk * pbe[k];
+        if (echo) {
+            b += chk * eal[k];
+            b += shk * ebe[k];
+        }
+    }
+    pred = a;
+    ech = echo ? b : 0.0;
+}
+
+// P2, chunk y = blockIdx.y: the density sums and the hash bins (chunk 0) and the
+// density projection on modes [y kChunkW, (y + 1) kChunkW).  rec2 record: [sum L,
+// sum dens, cos (kChunkW), sin (kChunkW)]; bin sums and counts in rec ([blocks][2 TB]).
+template <typename P>
+__global__ void __launch_bounds__(kThreads) s64w_p2(G64<P> G) {
+    S64_BIND_BLOCKS(blk);
+    __shared__ double red[kWarps];
+    extern __shared__ double sbin[];  // [TB] sums, then [TB] counts
+    const int TB = D.T * D.B;
+    const int y = blockIdx.y;
+    const bool bins = D.hash_on != 0 && y == 0;
+    if (bins)
+        for (int i = threadIdx.x; i < 2 * TB; i += kThreads) sbin[i] = 0.0;
+    __syncthreads();
+    const double scale = Bf.cst->scale, ep = D.hp[Q_EP];
+    const int k0 = y * kChunkW;
+    const int kn = min(kChunkW, D.R - k0);  // modes of this chunk below the rank
+    double v[2 + 2 * kChunkW];
+#pragma unroll
+    for (int j = 0; j < 2 + 2 * kChunkW; ++j) v[j] = 0.0;
+    for (int64_t e = lb * kThreads + threadIdx.x; e < D.N; e += gb * kThreads) {
+        const double rel = rel_of(D, scale, force_of(D, e));
+        const double ds = pow(rel, ep);
+        const double L = log1p(ds);
+        v[0] += L;
+        if (D.inst) v[1] += idens_of(D, rel);
+        const int64_t r = e / D.cols, c = e % D.cols;
+#pragma unroll
+        for (int j = 0; j < kChunkW; ++j) {
+            if (j < kn) {
+                double ch, sh;
+                carrier_at(D, D.RW, r, c, k0 + j, ch, sh);
+                v[2 + j] += L * ch;
+                v[2 + kChunkW + j] += L * sh;
+            }
+        }
+        if (bins)
+            for (int t = 0; t < D.T; ++t) {
+                const int b = (int)hash_bin(e, D.B, t);
+                atomicAdd(&sbin[t * D.B + b], ds);
+                atomicAdd(&sbin[TB + t * D.B + b], 1.0);
+            }
+    }
+    block_record<2 + 2 * kChunkW>(v, red, Bf.rec2 + ((int64_t)y * Bf.blocks + lb) * kRec2);
+    if (bins)
+        for (int i = threadIdx.x; i < 2 * TB; i += kThreads) Bf.rec[lb * 2 * TB + i] = sbin[i];
+}
+
+template <typename P>
+__global__ void __launch_bounds__(kThreads) s64w_fin2(G64<P> G) {
+    S64_BIND_TENSOR();
+    __shared__ double tot[2];
+    const int tid = threadIdx.x;
+    const int TB = D.T * D.B;
+    const int RW = D.RW;
+    const double N = (double)D.N;
+    C64& C = *Bf.cst;
+    if (tid < 2) {  // chunk 0's records
+        double s = 0.0;
+        for (int b = 0; b < Bf.blocks; ++b) s += Bf.rec2[(int64_t)b * kRec2 + tid];
+        tot[tid] = s;
+    }
+    if (D.hash_on) fin2_hash(D, Bf, 2 * TB, 0);
+    __syncthreads();
+    const double shrink = 1.0 / sqrt(fmax(1.0, 0.7 * log2((double)D.R + 1.0)));
+    if (tid == 0) fin2_scalars(D, C, tot[0], tot[1]);
+    __syncthreads();
+    double* w = Bf.wcoef;
+    for (int k = tid; k < RW; k += kThreads) {
+        if (k < D.R) {
+            const int64_t y = k / kChunkW, j = k % kChunkW;
+            double sc = 0.0, ss = 0.0;
+            for (int b = 0; b < Bf.blocks; ++b) {
+                const double* r2 = Bf.rec2 + (y * Bf.blocks + b) * kRec2;
+                sc += r2[2 + j];
+                ss += r2[2 + kChunkW + j];
+            }
+            const ModeStats& m = D.stats[k];
+            fin2_mode(D, k, sc / N / C.meanL - m.mhat_c, ss / N / C.meanL - m.mhat_s, shrink, w[W_MAL * RW + k],
+                      w[W_MBE * RW + k], w[W_PAL * RW + k], w[W_PBE * RW + k]);
+        } else {
+            w[W_MAL * RW + k] = w[W_MBE * RW + k] = w[W_PAL * RW + k] = w[W_PBE * RW + k] = 0.0;
+        }
+    }
+    if (D.inst && D.ndim >= 2) {
+        __syncthreads();
+        fin2_axes(D, Bf, C.gm);
+    }
+}
+
+// P3 element pass: the tangent and the port stored (tbuf, pbuf), sum err^2 and
+// the port bins.  rec record: [sum err^2, port bins (TB)].
+template <typename P>
+__global__ void __launch_bounds__(kThreads) s64w_p3a(G64<P> G) {
+    S64_BIND_BLOCKS(blk);
+    __shared__ double red[kWarps];
+    extern __shared__ double sbin[];
+    const int TB = D.T * D.B;
+    const bool hash_on = D.hash_on != 0;
+    if (hash_on)
+        for (int i = threadIdx.x; i < TB; i += kThreads) sbin[i] = 0.0;
+    __syncthreads();
+    const C64& C = *Bf.cst;
+    const double scale = C.scale, tm = D.hp[Q_TM];
+    const int RW = D.RW;
+    const double* mal = Bf.wcoef + W_MAL * RW;
+    const double* mbe = Bf.wcoef + W_MBE * RW;
+    const double* pal = Bf.wcoef + W_PAL * RW;
+    const double* pbe = Bf.wcoef + W_PBE * RW;
+    double v[1] = {0.0};
+    for (int64_t e = lb * kThreads + threadIdx.x; e < D.N; e += gb * kThreads) {
+        const int64_t r = e / D.cols, c = e % D.cols;
+        const double f = force_of(D, e);
+        const double rel = rel_of(D, scale, f);
+        double lm = 0.0, pr = 0.0;
+        for (int k = 0; k < D.R; ++k) {
+            double ch, sh;
+            carrier_at(D, RW, r, c, k, ch, sh);
+            lm += ch * mal[k];
+            lm += sh * mbe[k];
+            pr += ch * pal[k];
+            pr += sh * pbe[k];
+        }
+        const double t = tangent_of(D, Bf, C, e, r, c, f, rel, clampd(lm, -3.0, 3.0));
+        Bf.tbuf[e] = t;
+        const double err = t - pr;
+        v[0] += err * err;
+        const double port = err + tm * t;
+        Bf.pbuf[e] = port;
+        if (hash_on)
+            for (int tb = 0; tb < D.T; ++tb) atomicAdd(&sbin[tb * D.B + (int)hash_bin(e, D.B, tb)], port);
+    }
+    double* rec = Bf.rec + lb * (1 + TB);
+    block_record<1>(v, red, rec);
+    if (hash_on)
+        for (int i = threadIdx.x; i < TB; i += kThreads) rec[1 + i] = sbin[i];
+}
+
+// P3 projections, chunk y = blockIdx.y: the stored port and tangent on modes
+// [y kChunkW, (y + 1) kChunkW).  rec2 record: [port cos, port sin, t cos, t sin]
+// (kChunkW each).
+template <typename P>
+__global__ void __launch_bounds__(kThreads) s64w_p3b(G64<P> G) {
+    S64_BIND_BLOCKS(blk);
+    __shared__ double red[kWarps];
+    const int y = blockIdx.y;
+    const int k0 = y * kChunkW;
+    const int kn = min(kChunkW, D.R - k0);
+    double v[4 * kChunkW];
+#pragma unroll
+    for (int j = 0; j < 4 * kChunkW; ++j) v[j] = 0.0;
+    for (int64_t e = lb * kThreads + threadIdx.x; e < D.N; e += gb * kThreads) {
+        const int64_t r = e / D.cols, c = e % D.cols;
+        const double port = Bf.pbuf[e], t = Bf.tbuf[e];
+#pragma unroll
+        for (int j = 0; j < kChunkW; ++j) {
+            if (j < kn) {
+                double ch, sh;
+                carrier_at(D, D.RW, r, c, k0 + j, ch, sh);
+                v[j] += port * ch;
+                v[kChunkW + j] += port * sh;
+                v[2 * kChunkW + j] += t * ch;
+                v[3 * kChunkW + j] += t * sh;
+            }
+        }
+    }
+    block_record<4 * kChunkW>(v, red, Bf.rec2 + ((int64_t)y * Bf.blocks + lb) * kRec2);
+}
+
+template <typename P>
+__global__ void __launch_bounds__(kThreads) s64w_fin3(G64<P> G) {
+    S64_BIND_TENSOR();
+    __shared__ double tot0;
+    const int tid = threadIdx.x;
+    const int TB = D.T * D.B;
+    const int RW = D.RW;
+    const double N = (double)D.N, eps = D.hp[Q_EPS];
+    C64& C = *Bf.cst;
+    double* w = Bf.wcoef;
+    if (tid == 0) {
+        double s = 0.0;
+        for (int b = 0; b < Bf.blocks; ++b) s += Bf.rec[(int64_t)b * (1 + TB)];
+        tot0 = s;
+    }
+    if (D.hash_on) fin3_hash(D, Bf, 1 + TB, 1);
+    // per mode: the port projection (contact drive) and the tangent projection (echo)
+    for (int k = tid; k < RW; k += kThreads) {
+        const int64_t y = k / kChunkW, j = k % kChunkW;
+        double pc = 0.0, ps = 0.0, tc = 0.0, ts = 0.0;
+        for (int b = 0; b < Bf.blocks; ++b) {
+            const double* r2 = Bf.rec2 + (y * Bf.blocks + b) * kRec2;
+            pc += r2[j];
+            ps += r2[kChunkW + j];
+            tc += r2[2 * kChunkW + j];
+            ts += r2[3 * kChunkW + j];
+        }
+        w[W_PC * RW + k] = pc / N;
+        w[W_PS * RW + k] = ps / N;
+        w[W_EAL * RW + k] = tc / N;
+        w[W_EBE * RW + k] = ts / N;
+    }
+    __syncthreads();
+    if (tid == 0) {
+        // ---- surprise (cresso_v5.py:1132-1134), confidence and contact oscillators
+        const double S = reservoir((double)*D.surprise, sqrt(tot0 / N + eps), D.hp[Q_SD], D.step);
+        *D.surprise = S;
+        C.S = S;
+        fin3_contact(D, S, w + W_PC * RW, w + W_PS * RW, w + W_GP * RW);
+        C.clip = D.hp[Q_CLIP];
+    }
+    __syncthreads();
+    // ---- second prediction and echo coefficients (cresso_v5.py:1252-1258)
+    const double shrink = 1.0 / sqrt(fmax(1.0, 0.7 * log2((double)D.R + 1.0)));
+    for (int k = tid; k < RW; k += kThreads) {
+        if (k < D.R) {
+            const double g = sigmoidd(D.hp[Q_CONFG] * D.conf[k]);
+            w[W_PAL * RW + k] = D.q_cos[k] * shrink * g;
+            w[W_PBE * RW + k] = D.q_sin[k] * shrink * g;
+            w[W_EAL * RW + k] = D.echo_on ? w[W_EAL * RW + k] * shrink : 0.0;
+            w[W_EBE * RW + k] = D.echo_on ? w[W_EBE * RW + k] * shrink : 0.0;
+        } else {
+            w[W_PAL * RW + k] = w[W_PBE * RW + k] = w[W_EAL * RW + k] = w[W_EBE * RW + k] = 0.0;
+        }
+    }
+}
+
 // The eight drive vectors of one element (cresso_v5.py:1303-1326):
 // rational, bounded, root (before its normalisation), tangent, prediction,
 // novelty, echo (raw), hash prediction (raw).
+// RM == 0: wide rank (the coefficients in Bf.wcoef).
 template <int RM, typename P>
 __device__ __forceinline__ void drive_vectors(const T64<P>& D, const Buf64& Bf, int64_t e, double (&v)[8]) {
     const C64& C = *Bf.cst;
     const double eps = D.hp[Q_EPS], clip = C.clip;
     const double t = Bf.tbuf[e];
     double pred, echo;
-    recon_pred_echo<RM>(D, C, e / D.cols, e % D.cols, D.echo_on != 0, pred, echo);
+    if constexpr (RM == 0)
+        recon_pred_echo_w(D, Bf, e / D.cols, e % D.cols, D.echo_on != 0, pred, echo);
+    else
+        recon_pred_echo<RM>(D, C, e / D.cols, e % D.cols, D.echo_on != 0, pred, echo);
     v[0] = t / (1.0 + fabs(t) / clip);
     v[1] = tanh(t / clip) * clip;
     v[2] = sgnd(t) * sqrt(fmin(fabs(t), clip * clip) + eps);
@@ -819,6 +1144,11 @@ int64_t tensor_scratch64(const T64<double>& T, const Item64& it) {
     b += 3 * align_up(8 * TB, 256);
     b += align_up(8 * T.rows, 256) + align_up(8 * T.cols, 256);
     b += align_up(8 * T.N, 256);
+    if (T.RW > kMaxRankPlain) {  // wcoef, pbuf, rec2
+        b += align_up(8 * (int64_t)W_COUNT * T.RW, 256);
+        b += align_up(8 * T.N, 256);
+        b += align_up(8 * (int64_t)(T.RW / kChunkW) * it.blocks * kRec2, 256);
+    }
     return b;
 }
 
@@ -830,8 +1160,8 @@ int64_t group_tables64(int n) {
 int plan64(const cresso_tensor_desc* descs, int64_t n, const cresso_hparams* hp, Plan64& P) {
     CRESSO_REQUIRE(descs != nullptr && hp != nullptr && n >= 1, CRESSO_EINVAL, "spectral64: need tensors and hparams");
     const int64_t rank = (int64_t)hp->rank, bins = (int64_t)hp->hash_bins, tables = (int64_t)hp->hash_tables;
-    CRESSO_REQUIRE(rank >= 1 && rank <= kMaxRankPlain, CRESSO_EUNSUPPORTED,
-                   "rank must be in [1, %d] on the CUDA spectral path (got %lld)", kMaxRankPlain, (long long)rank);
+    CRESSO_REQUIRE(rank >= 1 && rank <= kMaxRankWide, CRESSO_EUNSUPPORTED,
+                   "rank must be in [1, %d] on the CUDA spectral path (got %lld)", kMaxRankWide, (long long)rank);
     CRESSO_REQUIRE(bins >= 0 && tables >= 1, CRESSO_EINVAL, "hash_bins must be >= 0, hash_tables >= 1");
     CRESSO_REQUIRE(bins * tables <= kMaxTB64, CRESSO_EUNSUPPORTED,
                    "hash_bins * hash_tables must be <= %d for float64 parameters", kMaxTB64);
@@ -903,6 +1233,7 @@ int plan64(const cresso_tensor_desc* descs, int64_t n, const cresso_hparams* hp,
         T.surprise = (double*)d.surprise;
         T.action = (double*)d.action;
         T.R = (int32_t)rank;
+        T.RW = (int32_t)rm;
         T.T = (int32_t)tables;
         T.B = (int32_t)bins;
         // hard channel: numel >= hard_channel_min_size and not a thin 2-D matrix (cresso_v5.py:983-989)
@@ -932,7 +1263,10 @@ int plan64(const cresso_tensor_desc* descs, int64_t n, const cresso_hparams* hp,
         it.rblocks = axes ? (int)std::min<int64_t>(ceil_div(T.rows, kWarps), 4096) : 0;
         it.cblocks = axes ? (int)(ceil_div(T.cols, kThreads) * col_chunks(T.rows)) : 0;
         const int64_t TBi = (int64_t)T.T * T.B;
-        it.L = std::max<int64_t>(std::max<int64_t>(2 + 2 * rm + 2 * TBi, 1 + 4 * rm + TBi), kGram64);
+        if (rm > kMaxRankPlain)  // wide rank: the projections go to rec2
+            it.L = std::max<int64_t>(std::max<int64_t>(2 * TBi, 1 + TBi), kGram64);
+        else
+            it.L = std::max<int64_t>(std::max<int64_t>(2 + 2 * rm + 2 * TBi, 1 + 4 * rm + TBi), kGram64);
         it.bytes = tensor_scratch64(T, it);
         const bool f32 = T.f32 != 0;
         if (P.groups.empty() || P.groups.back().f32 != f32 || P.groups.back().count == kGroupTensors64 ||
@@ -988,6 +1322,15 @@ int run_group(const Plan64& PL, const Group64& Gr, char* base, cudaStream_t s) {
         q += align_up(8 * T.cols, 256);
         bf.tbuf = reinterpret_cast<double*>(q);
         q += align_up(8 * T.N, 256);
+        bf.wcoef = bf.pbuf = bf.rec2 = nullptr;
+        if (T.RW > kMaxRankPlain) {
+            bf.wcoef = reinterpret_cast<double*>(q);
+            q += align_up(8 * (int64_t)W_COUNT * T.RW, 256);
+            bf.pbuf = reinterpret_cast<double*>(q);
+            q += align_up(8 * T.N, 256);
+            bf.rec2 = reinterpret_cast<double*>(q);
+            q += align_up(8 * (int64_t)(T.RW / kChunkW) * it.blocks * kRec2, 256);
+        }
         bf.blocks = it.blocks;
         off += it.bytes;
         blk[j] = g;
@@ -1017,25 +1360,45 @@ int run_group(const Plan64& PL, const Group64& Gr, char* base, cudaStream_t s) {
         s64_fin1<P><<<n, 32, 0, s>>>(G);
         CRESSO_LAUNCHED("s64_fin1");
     }
+    const unsigned chunks = RM == 0 ? (unsigned)(PL.ts[Gr.first].RW / kChunkW) : 1u;  // one rank per group
     {
         NvtxRange r("cresso64 P2 density / bins / projection");
-        s64_p2<RM, P><<<g, kThreads, smem2, s>>>(G);
-        CRESSO_LAUNCHED("s64_p2");
+        if constexpr (RM == 0) {
+            s64w_p2<P><<<dim3(g, chunks), kThreads, smem2, s>>>(G);
+            CRESSO_LAUNCHED("s64w_p2");
+        } else {
+            s64_p2<RM, P><<<g, kThreads, smem2, s>>>(G);
+            CRESSO_LAUNCHED("s64_p2");
+        }
         if (any_axes) {
             s64_rowsum<P><<<gr, kThreads, 0, s>>>(G);
             CRESSO_LAUNCHED("s64_rowsum");
             s64_colsum<P><<<gc, kThreads, 0, s>>>(G);
             CRESSO_LAUNCHED("s64_colsum");
         }
-        s64_fin2<RM, P><<<n, kThreads, 0, s>>>(G);
-        CRESSO_LAUNCHED("s64_fin2");
+        if constexpr (RM == 0) {
+            s64w_fin2<P><<<n, kThreads, 0, s>>>(G);
+            CRESSO_LAUNCHED("s64w_fin2");
+        } else {
+            s64_fin2<RM, P><<<n, kThreads, 0, s>>>(G);
+            CRESSO_LAUNCHED("s64_fin2");
+        }
     }
     {
         NvtxRange r("cresso64 P3 tangent / port");
-        s64_p3<RM, P><<<g, kThreads, smem3, s>>>(G);
-        CRESSO_LAUNCHED("s64_p3");
-        s64_fin3<RM, P><<<n, kThreads, 0, s>>>(G);
-        CRESSO_LAUNCHED("s64_fin3");
+        if constexpr (RM == 0) {
+            s64w_p3a<P><<<g, kThreads, smem3, s>>>(G);
+            CRESSO_LAUNCHED("s64w_p3a");
+            s64w_p3b<P><<<dim3(g, chunks), kThreads, 0, s>>>(G);
+            CRESSO_LAUNCHED("s64w_p3b");
+            s64w_fin3<P><<<n, kThreads, 0, s>>>(G);
+            CRESSO_LAUNCHED("s64w_fin3");
+        } else {
+            s64_p3<RM, P><<<g, kThreads, smem3, s>>>(G);
+            CRESSO_LAUNCHED("s64_p3");
+            s64_fin3<RM, P><<<n, kThreads, 0, s>>>(G);
+            CRESSO_LAUNCHED("s64_fin3");
+        }
     }
     {
         NvtxRange r("cresso64 P4 drive Gram / P5 update");
@@ -1087,7 +1450,8 @@ int cresso_spectral64_run(const cresso_tensor_desc* descs, int64_t n, const cres
                 case 8: st = run_group<8, float>(P, G, base, s); break;
                 case 16: st = run_group<16, float>(P, G, base, s); break;
                 case 32: st = run_group<32, float>(P, G, base, s); break;
-                default: st = run_group<64, float>(P, G, base, s); break;
+                case 64: st = run_group<64, float>(P, G, base, s); break;
+                default: st = run_group<0, float>(P, G, base, s); break;  // wide rank
             }
         } else {
             switch (rm) {
@@ -1095,7 +1459,8 @@ int cresso_spectral64_run(const cresso_tensor_desc* descs, int64_t n, const cres
                 case 8: st = run_group<8, double>(P, G, base, s); break;
                 case 16: st = run_group<16, double>(P, G, base, s); break;
                 case 32: st = run_group<32, double>(P, G, base, s); break;
-                default: st = run_group<64, double>(P, G, base, s); break;
+                case 64: st = run_group<64, double>(P, G, base, s); break;
+                default: st = run_group<0, double>(P, G, base, s); break;  // wide rank
             }
         }
         if (st) return st;

@@ -563,8 +563,8 @@ class CRESSO5(Optimizer):
                     # pipeline (float32 state for float32 / float16 / bfloat16 parameters)
                     wide = int(group["rank"]) > _lib.MAX_RANK
                     if param.dtype is torch.float64 or wide:
-                        if wide and int(group["rank"]) > _lib.MAX_RANK_PLAIN:
-                            raise RuntimeError(f"CRESSO5 B200 path supports rank <= {_lib.MAX_RANK_PLAIN} "
+                        if wide and int(group["rank"]) > _lib.MAX_RANK_WIDE:
+                            raise RuntimeError(f"CRESSO5 B200 path supports rank <= {_lib.MAX_RANK_WIDE} "
                                                f"(got {group['rank']})")
                         if getattr(param, "_cresso_shard", None) is not None:
                             raise RuntimeError("float64 and rank > 16 spectral tensors are not sharded: pass them "

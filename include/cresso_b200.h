@@ -239,12 +239,16 @@ CRESSO_API int cresso_status_copy(const void* status_word, void* host_word, cres
 
 /* Float64 parameters on the spectral route (cresso_v5.py:945-1353 with the
  * float64 work and state of cresso_v5.py:119-124), and float32 / float16 /
- * bfloat16 parameters when rank > CRESSO_MAX_RANK (rank up to 64).  The shape
+ * bfloat16 parameters when rank > CRESSO_MAX_RANK (rank up to 4096, the bound of
+ * the reference's CUDA contact kernel, cresso_cuda_kernel.cu:1937; the
+ * reference's PyTorch path takes any rank).  The shape
  * workspace holds float64 axis tables and the carrier stats built from them;
  * state pointers of the descriptors point at float64 values for float64
  * parameters and at float32 values otherwise, `shape_ws` at this workspace.
  * The step runs the same five passes as cresso_spectral_run in float64
- * arithmetic, tensor by tensor; a 16-bit parameter receives the update rounded
+ * arithmetic, a group of tensors at a time (above rank 64 the reconstructions
+ * loop over the modes and the projections run in chunks of 16 modes, with the
+ * port field stored between them); a 16-bit parameter receives the update rounded
  * to its type, as in cresso_spectral_run.  Tensors are whole (not sharded),
  * hash_bins * hash_tables <= 2048. */
 CRESSO_API int cresso_shape_workspace64_bytes(int64_t ndim, const int64_t* shape, int64_t rank, int64_t* bytes);

@@ -140,6 +140,14 @@ EXTRA_CASES = {
                          1e-3, "float32"),
     "r64_f64_40x50": ((40, 50), dict(rank=64, hash_bins=64, hash_tables=2), 3, 89, 0.02, 1e-3, "float64"),
     "r64_bf16_48x64": ((48, 64), dict(rank=64, max_frequency=7), 3, 90, 0.02, 1e-3, "bfloat16"),
+    # ranks above 64 (modes in memory, projections in chunks of modes)
+    "r96_64x80": ((64, 80), dict(rank=96, hash_bins=64, hash_tables=2), 3, 91, 0.02, 1e-3, "float32"),
+    "r65_40x50": ((40, 50), dict(rank=65, hash_bins=37, hash_tables=3, instant_metric_power=0.7), 3, 92, 0.02,
+                  1e-3, "float32"),
+    "r128_3000_wd": ((3000,), dict(rank=128, weight_decay=0.01, max_frequency=7), 3, 93, 0.02, 1e-3, "float32"),
+    "r80_f64_6x8x30": ((6, 8, 30), dict(rank=80, hash_bins=37, hash_tables=1, local_sharpness=0.2), 3, 94, 0.02,
+                       1e-3, "float64"),
+    "r200_bf16_48x64": ((48, 64), dict(rank=200, max_frequency=7), 3, 95, 0.02, 1e-3, "bfloat16"),
 }
 
 

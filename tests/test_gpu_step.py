@@ -97,8 +97,9 @@ def test_extra_golden_parity(golden_extra, name):
     """The second golden table against the reference's own output: float16 /
     bfloat16 parameters (spectral and scalar routes), spectral tensors of
     rank 3 to 5 (leading axes flattened into rows, carriers and the instant
-    metric composed over every axis), the micro-field route and float64
-    parameters (every route, float64 work and state).
+    metric composed over every axis), the micro-field route, float64
+    parameters (every route, float64 work and state) and mode ranks 17 to 200
+    (the float64-arithmetic pipeline; above 64 with its modes in memory).
 
     float32 parameters: the criterion of the float32 golden cases.  16-bit
     parameters: every element within one unit in the last place of the
