@@ -219,7 +219,12 @@ fast_pass_kernel(const GroupHdr* __restrict__ hdr, const DevTensor* __restrict__
     const int TB = (int)hdr->tb, B = (int)hdr->bins;
     const float eps = (float)hdr->hp[H_EPS];
     const float ep = (float)hdr->hp[H_EP];
-    const float mcpl = (float)hdr->hp[H_MC];
+    // P3's metric: exp(coupling * clamp(lm, -3, 3)) = 2^clamp(mc2 lm, -mhi, mhi), with the
+    // factor mc2 folded into the reconstruction coefficients; clamping to [0.06, 16]
+    // afterwards changes nothing when |3 mc2| <= 3.99 (2^3.99 < 16, 2^-3.99 > 0.06)
+    const float mc2 = (float)hdr->hp[H_MC] * 1.4426950408889634f;
+    const float mhi = fabsf(3.0f * mc2);
+    const bool mclamp = !(mhi <= 3.99f);
     const float tmix = (float)hdr->hp[H_TM];
     const int64_t it0 = (int64_t)blockIdx.x * n_items / gridDim.x;
     const int64_t it1 = ((int64_t)blockIdx.x + 1) * n_items / gridDim.x;
@@ -300,12 +305,14 @@ fast_pass_kernel(const GroupHdr* __restrict__ hdr, const DevTensor* __restrict__
         float* __restrict__ xdst = PASS == 3 ? Dp->tbuf : Dp->param;  // where the stored tile goes
         const TensorConsts* __restrict__ Cp = Dp->cst;
         const float sgn = (flags & F_MAXIMIZE) ? -1.0f : 1.0f;
-        float scale = 0.f, inv_scale = 0.f;
+        float scale = 0.f, inv_scale = 0.f, sscale = 0.f, seps = 0.f;
         DriveK dk{};
         float c_u = 0.f, c_root = 0.f, c_t = 0.f, c_nov = 0.f, c_hp = 0.f, gain = 0.f, neg_lr = 0.f;
         if constexpr (PASS == 2 || PASS == 3) {
             scale = Cp->scale;
             inv_scale = Cp->inv_scale;
+            sscale = sgn * scale;
+            seps = sgn * eps;
         }
         if constexpr (PASS >= 4) dk = DriveK{Cp->clip, Cp->inv_clip, Cp->clip2, Cp->sp, Cp->invD, eps};
         if constexpr (PASS == 5) {
@@ -324,14 +331,17 @@ fast_pass_kernel(const GroupHdr* __restrict__ hdr, const DevTensor* __restrict__
             const float* be1 = PASS == 3 ? Cp->m_be : Cp->pr_be;
             const float* al2 = PASS == 3 ? Cp->p0_al : (PASS == 4 ? Cp->ec_al : Cp->cb_al);
             const float* be2 = PASS == 3 ? Cp->p0_be : (PASS == 4 ? Cp->ec_be : Cp->cb_be);
+            // P3: the log-metric coefficients scaled by mc2 = coupling * log2(e), so that the
+            // product holds the exponent of the metric in base 2 directly
+            const float c1 = PASS == 3 ? mc2 : 1.0f;
             if (tid < RM) {
-                s_coef[tid] = al1[tid];
-                s_coef[RM + tid] = be1[tid];
+                s_coef[tid] = al1[tid] * c1;
+                s_coef[RM + tid] = be1[tid] * c1;
                 s_coef[2 * RM + tid] = al2[tid];
                 s_coef[3 * RM + tid] = be2[tid];
             }
             if (tid == 0) {
-                s_coef[4 * RM] = PASS == 3 ? Cp->m_K : Cp->pr_K;
+                s_coef[4 * RM] = PASS == 3 ? Cp->m_K * c1 : Cp->pr_K;
                 s_coef[4 * RM + 1] = PASS == 3 ? Cp->p0_K : (PASS == 4 ? Cp->ec_K : Cp->cb_K);
             }
             // joint table over the bin pairs (b0, b1), j = b0 + 64 b1:
@@ -560,7 +570,7 @@ fast_pass_kernel(const GroupHdr* __restrict__ hdr, const DevTensor* __restrict__
                         float2 rel = __ffma2_rn(f2(fabsf(xb[o]), fabsf(xb[o + 256])), f2(inv_scale), f2(eps));
                         rel = f2(fminf(rel.x, 1.0e4f), fminf(rel.y, 1.0e4f));  // |sgn x| = |x|
                         const float2 lg = __fmul2_rn(f2(ep), f2(__log2f(rel.x), __log2f(rel.y)));
-                        const float2 ds = f2(exp2f(lg.x), exp2f(lg.y));
+                        const float2 ds = f2(ex2_approx(lg.x), ex2_approx(lg.y));
                         const float2 L = log1p_pos2(ds);
                         const float2 Lc = __fadd2_rn(L, f2(-0.5f));
                         dv[u] = rel.x;  // instant metric power 1: the axis density is rel
@@ -595,16 +605,18 @@ fast_pass_kernel(const GroupHdr* __restrict__ hdr, const DevTensor* __restrict__
                     for (int u = 0; u < UNR; u += 2) {  // two rows on the two-lane pipe
                         const int m = m0 + u;
                         const int o = m * 256 + lc;
-                        const float2 f = __fmul2_rn(f2(sgn), f2(xb[o], xb[o + 256]));
-                        const float2 e = __fmul2_rn(f2(mcpl), f2(clampf(R1[u], -3.0f, 3.0f), clampf(R1[u + 1], -3.0f, 3.0f)));
-                        const float2 metric = f2(clampf(__expf(e.x), 0.06f, 16.0f), clampf(__expf(e.y), 0.06f, 16.0f));
-                        float2 den = __fmul2_rn(f2(scale), metric);
+                        // t = sgn x / (den + eps) = x / (sgn den + sgn eps): the sign rides on the
+                        // scale and on eps (exact)
+                        const float2 f = f2(xb[o], xb[o + 256]);
+                        float2 metric = f2(ex2_approx(clampf(R1[u], -mhi, mhi)), ex2_approx(clampf(R1[u + 1], -mhi, mhi)));
+                        if (mclamp) metric = f2(clampf(metric.x, 0.06f, 16.0f), clampf(metric.y, 0.06f, 16.0f));
+                        float2 den = __fmul2_rn(f2(sscale), metric);
                         if (flags & F_INST2D)
                             den = __fmul2_rn(den, f2(clampf(rowf_ip[m] * colf, 0.08f, 12.0f),
                                                      clampf(rowf_ip[m + 1] * colf, 0.08f, 12.0f)));
                         const int j0 = jb[o], j1 = jb[o + 256];
                         den = __fmul2_rn(den, f2(s_joint[j0], s_joint[j1]));
-                        const float2 de = __fadd2_rn(den, f2(eps));
+                        const float2 de = __fadd2_rn(den, f2(seps));
                         float2 t = __fmul2_rn(f, f2(rcp_approx(de.x), rcp_approx(de.y)));
                         t = f2(clampf(t.x, -1.0e4f, 1.0e4f), clampf(t.y, -1.0e4f, 1.0e4f));
                         xb[o] = t.x;  // in place: the tile goes back to the tangent buffer
@@ -692,7 +704,7 @@ fast_pass_kernel(const GroupHdr* __restrict__ hdr, const DevTensor* __restrict__
                             bool fx;
                             if constexpr (PASS == 2) {
                                 const float rel = fminf(__fmaf_rn(fabsf(xb[o]), inv_scale, eps), 1.0e4f);
-                                v = exp2f(__fmul_rn(ep, __log2f(rel)));
+                                v = ex2_approx(__fmul_rn(ep, __log2f(rel)));
                                 fx = v < fix.vmax;
                             } else {
                                 const float t = xb[o];
