@@ -390,19 +390,25 @@ def workload_config(workload, shapes, kw, dtype):
 # B200 arm
 # ---------------------------------------------------------------------------
 def make_inputs(name, args, world, rank, device, zero):
-    """Parameters (with gradients attached) of a workload on this rank: row blocks of
-    every tensor under row sharding, the whole set otherwise.  Returns (shapes, kw,
-    params, device gradients, local elements, total elements, bytes per element)."""
+    """Parameters (with gradients attached) of a workload on this rank: under row
+    sharding row blocks of every 1-D / 2-D tensor on the spectral route and the
+    other tensors whole (their owners step them), the whole set otherwise.
+    Returns (shapes, kw, params, device gradients, local elements, total
+    elements, bytes per element)."""
+    import cresso_b200
+    from cresso_b200._host import uses_spectral_route
     from cresso_b200.distributed import mark_row_shard, row_block
 
     shapes, kw, istd = workload_shapes(name)
+    settings = cresso_b200.CRESSO5([torch.nn.Parameter(torch.zeros(1, device=device))], **kw).defaults
     pdt = {"f32": torch.float32, "bf16": torch.bfloat16, "f16": torch.float16, "f64": torch.float64}[args.dtype]
     bpe = 3 * torch.empty((), dtype=pdt).element_size()  # grad read + param read + param write
     gen = torch.Generator(device=device)
     gen.manual_seed(1234 + (0 if zero else rank))
     params, grads_dev, n_local = [], [], 0
     for s in shapes:
-        if world > 1 and not zero:
+        shard = world > 1 and not zero and len(s) <= 2 and uses_spectral_route(s, settings)
+        if shard:
             start, stop = row_block(s[0], rank, world)
             local_shape = (stop - start,) + tuple(s[1:])
         else:
@@ -410,7 +416,7 @@ def make_inputs(name, args, world, rank, device, zero):
         p = torch.empty(local_shape, device=device)
         p.normal_(0.0, istd, generator=gen)
         p = torch.nn.Parameter(p.to(pdt))
-        if world > 1 and not zero:
+        if shard:
             mark_row_shard(p, s, start)
         g = torch.empty(local_shape, device=device)
         g.normal_(0.0, 1e-3, generator=gen)

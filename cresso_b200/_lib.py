@@ -64,7 +64,7 @@ EXPORTS = (
     "cresso_spectral_layout", "cresso_spectral_run", "cresso_scalar_scratch_bytes", "cresso_scalar_run",
     "cresso_scalar_run_noalloc", "cresso_micro_scratch_bytes", "cresso_micro_run", "cresso_selftest_bounded_wait",
     "cresso_shape_workspace64_bytes", "cresso_shape_workspace64_init", "cresso_spectral64_scratch_bytes",
-    "cresso_spectral64_run", "cresso_spectral_run_status", "cresso_status_copy",
+    "cresso_spectral64_run", "cresso_spectral_run_status", "cresso_status_copy", "cresso_copy_segments",
 )
 
 _lock = threading.Lock()
@@ -98,6 +98,7 @@ def _declare(lib) -> None:
         "cresso_spectral_run": (ctypes.c_int, [_p, _i64, _p, _p, _i64, _i64, _i64, _i64, _p]),
         "cresso_spectral_run_status": (ctypes.c_int, [_p, _i64, _p, _p, _i64, _i64, _i64, _i64, _p, _p]),
         "cresso_status_copy": (ctypes.c_int, [_p, _p, _p]),
+        "cresso_copy_segments": (ctypes.c_int, [_p, _i64, _p]),
         "cresso_scalar_scratch_bytes": (ctypes.c_int, [_p, _i64, _pi64]),
         "cresso_scalar_run": (ctypes.c_int, [_p, _i64, _p, _p, _i64, _p]),
         "cresso_scalar_run_noalloc": (ctypes.c_int, [_p, _i64, _p, _p]),

@@ -14,8 +14,12 @@ spreading one optimizer step over the GPUs of a box are provided:
     Every rank then holds identical rank / hash / scalar state, and updates its
     own rows.  Hash indices and carrier coordinates use global indices, so the
     result equals the single-GPU step up to the float64 summation order.
-    Small and LoRA-thin (scalar-route) tensors and tensors of rank >= 3 are
-    passed whole and stepped redundantly on every rank.
+    Tensors passed whole (small and LoRA-thin scalar-route tensors, micro-field
+    tensors, spectral tensors of rank >= 3, float64 or rank > 16 spectral
+    tensors, and any tensor not marked as a shard) take no part in the
+    exchange: each is stepped by one owner rank (a greedy partition on element
+    counts) and its updated values and state reach the other ranks in one
+    all-gather, so a LoRA-heavy set is split over the GPUs too.
 
 ``ZeroCRESSO5`` (ZeRO-1 partition)
     Whole tensors are assigned to ranks by a longest-processing-time greedy
@@ -89,6 +93,94 @@ def exchange_status(opt: CRESSO5, group=None) -> None:
     opt._publish_status([device])
 
 
+def _whole_segments(items: Sequence[tuple]) -> List[List[Tensor]]:
+    """Per item the tensors an owner sends: the parameter, then its floating-point
+    state tensors by key (integer state, the frequency pack, never changes)."""
+    out = []
+    for p, _, st in items:
+        ts = [p.data]
+        for k in sorted(st):
+            v = st[k]
+            if torch.is_tensor(v) and v.is_floating_point():
+                ts.append(v)
+        out.append(ts)
+    return out
+
+
+class WholeExchange:
+    """The exchange of the tensors stepped whole under row sharding: after each
+    owner stepped its tensors, every rank receives the owners' parameters and
+    floating-point state.
+
+    One byte layout per plan: rank r's tensors (parameter, then state by key)
+    at 16-byte aligned offsets of an S-byte block, S the largest rank's total.
+    Each step packs this rank's block, all-gathers the blocks (one collective)
+    and unpacks the other ranks' blocks into the tensors.  On CUDA devices the
+    packing and the unpacking are one launch each (``cresso_copy_segments``
+    over device tables of (source, destination, bytes) rows built once); the
+    tables hold device addresses, so the plan is rebuilt when the parameters or
+    state tensors are replaced (``invalidate_caches``).  CPU tensors (gloo test
+    ranks) take the same layout through tensor copies."""
+
+    def __init__(self, items: Sequence[tuple], owners: Sequence[int], world: int, rank: int):
+        self.world, self.rank = int(world), int(rank)
+        segs = _whole_segments(items)
+        per_rank: List[List[Tuple[Tensor, int, int]]] = [[] for _ in range(self.world)]  # (tensor, offset, bytes)
+        used = [0] * self.world
+        for ts, o in zip(segs, owners):
+            for t in ts:
+                nb = t.numel() * t.element_size()
+                per_rank[o].append((t, used[o], nb))
+                used[o] += (nb + 15) // 16 * 16
+        self.block = max(max(used), 16)
+        device = items[0][0].device
+        self.device = device
+        self.send = torch.zeros(self.block, dtype=torch.uint8, device=device)
+        self.recv = torch.zeros(self.world * self.block, dtype=torch.uint8, device=device)
+        self.per_rank = per_rank
+        if device.type == "cuda":
+            sb, rb = self.send.data_ptr(), self.recv.data_ptr()
+            pack = [(t.data_ptr(), sb + off, nb) for t, off, nb in per_rank[self.rank]]
+            unpack = [(rb + r * self.block + off, t.data_ptr(), nb)
+                      for r in range(self.world) if r != self.rank for t, off, nb in per_rank[r]]
+            self.pack_table = self._table(pack, device)
+            self.unpack_table = self._table(unpack, device)
+            self.n_pack, self.n_unpack = len(pack), len(unpack)
+
+    @staticmethod
+    def _table(rows, device) -> Tensor:
+        if not rows:
+            return torch.zeros(3, dtype=torch.int64, device=device)
+        return torch.tensor(rows, dtype=torch.int64).reshape(-1).to(device)
+
+    def run(self, group=None) -> None:
+        if self.device.type == "cuda":
+            L = _lib.lib()
+            stream = torch.cuda.current_stream(self.device).cuda_stream
+            _lib.check(L.cresso_copy_segments(_lib.ptr(self.pack_table), self.n_pack, stream), "copy_segments")
+            dist.all_gather_into_tensor(self.recv, self.send, group=group)
+            _lib.check(L.cresso_copy_segments(_lib.ptr(self.unpack_table), self.n_unpack, stream), "copy_segments")
+            return
+        for t, off, nb in self.per_rank[self.rank]:
+            self.send[off:off + nb].copy_(t.reshape(-1).view(torch.uint8))
+        dist.all_gather(list(self.recv.split(self.block)), self.send, group=group)
+        for r in range(self.world):
+            if r == self.rank:
+                continue
+            for t, off, nb in self.per_rank[r]:
+                base = r * self.block + off
+                t.reshape(-1).view(torch.uint8).copy_(self.recv[base:base + nb])
+
+
+def broadcast_whole(items: Sequence[tuple], owners: Sequence[int], world: int, group=None) -> None:
+    """One exchange of whole tensors (a WholeExchange built for this call)."""
+    WholeExchange(items, owners, world, dist.get_rank(group)).run(group)
+
+
+def _is_shard(param: Tensor) -> bool:
+    return getattr(param, "_cresso_shard", None) is not None
+
+
 class RowShardedCRESSO5(CRESSO5):
     """CRESSO5 over row-sharded tensors with one float64 all-reduce per pass.
 
@@ -96,15 +188,71 @@ class RowShardedCRESSO5(CRESSO5):
     tensors is stepped as two halves of about equal size: each half's
     all-reduce runs (on NCCL's stream) while the other half computes its next
     pass, so the exchange between passes leaves the compute stream's critical
-    path.  Every rank takes the same halves and collectives in the same order."""
+    path.  Every rank takes the same halves and collectives in the same order.
 
-    def __init__(self, params: Iterable[Tensor], process_group=None, pipeline_exchange: bool = True, **kwargs):
+    Tensors passed whole are stepped without any exchange between passes.  With
+    ``partition_whole`` (the default) each is stepped by one owner rank (LPT on
+    element counts over the group's whole tensors, the same plan on every rank)
+    and its values reach the other ranks in one all-gather (``WholeExchange``);
+    without it every rank steps every whole tensor itself."""
+
+    def __init__(self, params: Iterable[Tensor], process_group=None, pipeline_exchange: bool = True,
+                 partition_whole: bool = True, **kwargs):
         super().__init__(params, **kwargs)
         self.process_group = process_group
         self.pipeline_exchange = bool(pipeline_exchange)
+        self.partition_whole = bool(partition_whole)
+        self._local = False  # set while whole tensors are stepped: their sums are complete per rank
+        self._whole_plans: Dict[tuple, tuple] = {}  # (owners, WholeExchange) per group layout
+
+    def _run_routed(self, group: dict, routed, spectral_devices: set, select=None, tag=None) -> None:
+        world = self._world()
+        if world == 1 or select is not None:
+            super()._run_routed(group, routed, spectral_devices, select, tag)
+            return
+        spectral, scalar, micro_items, spectral64 = routed
+        sharded = {d: [it for it in its if _is_shard(it[0])] for d, its in spectral.items()}
+        sharded = {d: its for d, its in sharded.items() if its}
+        whole_spec = {d: [it for it in its if not _is_shard(it[0])] for d, its in spectral.items()}
+        whole = tuple({d: its for d, its in per.items() if its}
+                      for per in (whole_spec, scalar, micro_items, spectral64))
+        if sharded:  # the exchanged step of the row shards
+            super()._run_routed(group, (sharded, {}, {}, {}), spectral_devices, None, tag)
+        if not any(whole):
+            return
+        wtag = ("whole", tag)
+        if not self.partition_whole:
+            self._local = True
+            try:
+                super()._run_routed(group, whole, spectral_devices, None, wtag)
+            finally:
+                self._local = False
+            return
+        flat = [(kind, d, it) for kind, per in enumerate(whole) for d, its in per.items() for it in its]
+        key = (id(group), tuple((kind, tuple(it[0].shape), it[0].data_ptr()) for kind, _, it in flat))
+        me = dist.get_rank(self.process_group)
+        plan = self._whole_plans.get(key)
+        if plan is None:
+            owners = lpt_partition([it[0].numel() for _, _, it in flat], world)
+            plan = self._whole_plans[key] = (owners, WholeExchange([it for _, _, it in flat], owners, world, me))
+        owners, exchange = plan
+        mine: Tuple[Dict, ...] = ({}, {}, {}, {})
+        for (kind, d, it), o in zip(flat, owners):
+            if o == me:
+                mine[kind].setdefault(d, []).append(it)
+        self._local = True
+        try:
+            super()._run_routed(group, mine, spectral_devices, None, wtag)
+        finally:
+            self._local = False
+        exchange.run(self.process_group)
+
+    def invalidate_caches(self) -> None:
+        super().invalidate_caches()
+        self._whole_plans.clear()
 
     def _run_spectral(self, group: dict, hp, device, items: list, tag=None) -> None:
-        if not self.pipeline_exchange or self._world() == 1 or len(items) < 2:
+        if self._local or not self.pipeline_exchange or self._world() == 1 or len(items) < 2:
             super()._run_spectral(group, hp, device, items, tag)
             return
         sizes = [p.numel() for p, _, _ in items]
@@ -143,7 +291,7 @@ class RowShardedCRESSO5(CRESSO5):
         return dist.get_world_size(self.process_group)
 
     def _spectral_stages(self, run, scratch: Tensor, layout) -> None:
-        if self._world() == 1:
+        if self._local or self._world() == 1:
             run(0, _lib.SPECTRAL_STAGES)
             return
         begin = 0

@@ -237,6 +237,16 @@ CRESSO_API int cresso_spectral_run_status(const cresso_tensor_desc* descs, int64
  * host-device transfers (no counterpart in the reference). */
 CRESSO_API int cresso_status_copy(const void* status_word, void* host_word, cresso_stream_t stream);
 
+/* Copies n_segments byte ranges in one launch.  `table` is device memory of
+ * n_segments rows of three uint64 values: source address, destination
+ * address, byte count (ranges must not overlap).  No counterpart in the
+ * reference, which has no multi-GPU path: the row-sharded optimizer packs the
+ * parameters and floating-point state of the tensors it steps whole (one
+ * owner rank each) into one byte buffer before an all-gather, and unpacks
+ * the gathered buffer into every rank's tensors, with one launch each instead
+ * of one copy per tensor. */
+CRESSO_API int cresso_copy_segments(const uint64_t* table, int64_t n_segments, cresso_stream_t stream);
+
 /* Float64 parameters on the spectral route (cresso_v5.py:945-1353 with the
  * float64 work and state of cresso_v5.py:119-124), and float32 / float16 /
  * bfloat16 parameters when rank > CRESSO_MAX_RANK (rank up to 4096, the bound of

@@ -151,8 +151,11 @@ def gpu_row_shard_worker(rank, world, port, outdir):
     dev = torch.device("cuda", rank)
     g = torch.Generator().manual_seed(3)
     shapes = [(256, 192), (1536,), (96, 64)]
-    inits = [torch.randn(s, generator=g) * 0.02 for s in shapes]
-    grads = [[torch.randn(s, generator=g) * 1e-3 for s in shapes] for _ in range(3)]
+    # passed whole in the same group: LoRA-thin and small (scalar route), a 4-D and an
+    # unmarked 2-D spectral tensor; each is stepped by its owner and all-gathered
+    whole_shapes = [(512, 16), (7, 9), (8, 16, 3, 3), (80, 48), (16, 300)]
+    inits = [torch.randn(s, generator=g) * 0.02 for s in shapes + whole_shapes]
+    grads = [[torch.randn(s, generator=g) * 1e-3 for s in shapes + whole_shapes] for _ in range(3)]
     kw = dict(rank=8, hash_bins=64, hash_tables=2, min_spectral_size=1024)
     ps = []
     for s, x in zip(shapes, inits):
@@ -160,15 +163,21 @@ def gpu_row_shard_worker(rank, world, port, outdir):
         p = torch.nn.Parameter(x[a:b].clone().to(dev))
         mark_row_shard(p, s, a)
         ps.append(p)
-    opt = RowShardedCRESSO5(ps, **kw)
+    ws = [torch.nn.Parameter(x.clone().to(dev)) for x in inits[len(shapes):]]
+    opt = RowShardedCRESSO5(ps + ws, **kw)
     for gs in grads:
         for p, s, gg in zip(ps, shapes, gs):
             a, b = row_block(s[0], rank, world)
             p.grad = gg[a:b].clone().to(dev)
+        for p, gg in zip(ws, gs[len(shapes):]):
+            p.grad = gg.clone().to(dev)
         opt.step()
     torch.cuda.synchronize()
     shard = [p.detach().cpu() for p in ps]
     states = [{k: (v.detach().cpu() if torch.is_tensor(v) else v) for k, v in opt.state[p].items()} for p in ps]
+    whole = [p.detach().cpu() for p in ws]
+    whole_states = [{k: (v.detach().cpu() if torch.is_tensor(v) else v) for k, v in opt.state[p].items()} for p in ws]
+    owners = next(iter(opt._whole_plans.values()))[0]
     if rank == 0:
         full = [torch.nn.Parameter(x.clone().to(dev)) for x in inits]
         ref = cresso_b200.CRESSO5(full, **kw)
@@ -181,7 +190,8 @@ def gpu_row_shard_worker(rank, world, port, outdir):
                    [{k: (v.detach().cpu() if torch.is_tensor(v) else v) for k, v in ref.state[p].items()} for p in full])
     else:
         ref_out = None
-    torch.save({"shard": shard, "states": states, "ref": ref_out}, os.path.join(outdir, f"gpu_rs_{rank}.pt"))
+    torch.save({"shard": shard, "states": states, "whole": whole, "whole_states": whole_states, "owners": owners,
+                "n_sharded": len(shapes), "ref": ref_out}, os.path.join(outdir, f"gpu_rs_{rank}.pt"))
     dist.barrier()
     dist.destroy_process_group()
 
@@ -286,4 +296,32 @@ def gpu_zero_deferred_worker(rank, world, port, outdir):
         outs.append([p.detach().cpu().clone() for p in model.parameters()])
     torch.save({"plain": outs[0], "deferred": outs[1]}, os.path.join(outdir, f"gpu_zdefer_{rank}.pt"))
     dist.barrier()
+    dist.destroy_process_group()
+
+
+def whole_broadcast_worker(rank, world, port, outdir):
+    """The whole-tensor exchange on CPU ranks: each rank writes distinctive values
+    into the tensors it owns and garbage elsewhere; afterwards every rank holds the
+    owners' parameters and floating state (float32 and float64), and integer
+    state is left alone."""
+    from cresso_b200.distributed import broadcast_whole, lpt_partition
+
+    _init(rank, world, port, "gloo")
+    shapes = [(7, 5), (13,), (4, 4, 2), (30,), ()]
+    items = []
+    for s in shapes:
+        st = {"step": 3, "q": torch.full((), -1.0), "metric": torch.full(s, -1.0, dtype=torch.float64),
+              "freqs": torch.full((2,), -1, dtype=torch.int64)}
+        items.append((torch.full(s, -1.0), None, st))
+    owners = lpt_partition([max(1, p.numel()) for p, _, _ in items], world)
+    for i, ((p, _, st), o) in enumerate(zip(items, owners)):
+        if o == rank:
+            p.fill_(100 * i + 7)
+            st["q"].fill_(i)
+            st["metric"].fill_(0.5 * i)
+            st["freqs"].fill_(rank)
+    broadcast_whole(items, owners, world)
+    torch.save({"owners": owners, "params": [p for p, _, _ in items], "q": [st["q"] for _, _, st in items],
+                "metric": [st["metric"] for _, _, st in items], "freqs": [st["freqs"] for _, _, st in items]},
+               os.path.join(outdir, f"wbcast_{rank}.pt"))
     dist.destroy_process_group()

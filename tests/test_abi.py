@@ -21,7 +21,7 @@ def declared_symbols():
 def test_library_exports_every_declared_symbol():
     lib = _lib.lib()
     names = declared_symbols()
-    assert len(names) == 29
+    assert len(names) == 30
     for name in names:
         assert hasattr(lib, name), name
     assert sorted(_lib.EXPORTS) == names

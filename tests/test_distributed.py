@@ -123,6 +123,18 @@ def test_failed_rank_surfaces_as_an_error_not_a_hang_gloo(tmp_path):
     assert s0[0] != "ok" and float(s0[1]) < 30.0
 
 
+def test_whole_tensors_reach_every_rank_from_their_owners_gloo(tmp_path):
+    spawn(W.whole_broadcast_worker, 2, tmp_path)
+    r = [torch.load(tmp_path / f"wbcast_{k}.pt") for k in range(2)]
+    assert r[0]["owners"] == r[1]["owners"] and set(r[0]["owners"]) == {0, 1}
+    for k in range(2):
+        for i, o in enumerate(r[k]["owners"]):
+            assert torch.all(r[k]["params"][i] == 100 * i + 7)
+            assert float(r[k]["q"][i]) == i
+            assert r[k]["metric"][i].dtype == torch.float64 and torch.all(r[k]["metric"][i] == 0.5 * i)
+            assert torch.all(r[k]["freqs"][i] == (k if o == k else -1))  # integer state is not sent
+
+
 @pytest.mark.gpu
 def test_row_sharded_step_matches_single_gpu(tmp_path):
     if torch.cuda.device_count() < 2:
@@ -130,7 +142,7 @@ def test_row_sharded_step_matches_single_gpu(tmp_path):
     spawn(W.gpu_row_shard_worker, 2, tmp_path)
     r = [torch.load(tmp_path / f"gpu_rs_{k}.pt") for k in range(2)]
     ref_params, ref_states = r[0]["ref"]
-    for i, full in enumerate(ref_params):
+    for i, full in enumerate(ref_params[:r[0]["n_sharded"]]):
         got = torch.cat([r[0]["shard"][i], r[1]["shard"][i]])
         rel = float((got.double() - full.double()).pow(2).mean().sqrt() / full.double().pow(2).mean().sqrt())
         assert rel <= 1e-6, (i, rel)
@@ -143,6 +155,23 @@ def test_row_sharded_step_matches_single_gpu(tmp_path):
                     assert d <= 1e-4 * max(float(v.double().abs().max()), 1e-6), (i, k, d)
             else:
                 assert a == v == b
+    # tensors passed whole: stepped by their owners (both ranks own some) and all-gathered
+    assert set(r[0]["owners"]) == {0, 1}
+    n = r[0]["n_sharded"]
+    for i, (a, b) in enumerate(zip(r[0]["whole"], r[1]["whole"])):
+        full = ref_params[n + i]
+        assert torch.equal(a, b), i
+        rel = float((a.double() - full.double()).pow(2).mean().sqrt() / full.double().pow(2).mean().sqrt())
+        assert rel <= 1e-6, (i, rel)
+        for k, v in ref_states[n + i].items():
+            x, y = r[0]["whole_states"][i][k], r[1]["whole_states"][i][k]
+            if torch.is_tensor(v):
+                assert torch.equal(x, y), (i, k)
+                if v.dtype.is_floating_point:
+                    d = float((x.double() - v.double()).abs().max())
+                    assert d <= 1e-4 * max(float(v.double().abs().max()), 1e-6), (i, k, d)
+            else:
+                assert x == v == y
 
 
 @pytest.mark.gpu
