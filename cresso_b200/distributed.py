@@ -194,7 +194,11 @@ class RowShardedCRESSO5(CRESSO5):
     ``partition_whole`` (the default) each is stepped by one owner rank (LPT on
     element counts over the group's whole tensors, the same plan on every rank)
     and its values reach the other ranks in one all-gather (``WholeExchange``);
-    without it every rank steps every whole tensor itself."""
+    without it every rank steps every whole tensor itself.  The plan is cached
+    per group and keyed on the parameter objects; it holds the device addresses
+    of the parameters and state tensors, so a caller that replaces a
+    parameter's storage (``p.data = t``) or a state tensor calls
+    ``invalidate_caches()`` afterwards (``load_state_dict`` does so itself)."""
 
     def __init__(self, params: Iterable[Tensor], process_group=None, pipeline_exchange: bool = True,
                  partition_whole: bool = True, **kwargs):
@@ -203,49 +207,55 @@ class RowShardedCRESSO5(CRESSO5):
         self.pipeline_exchange = bool(pipeline_exchange)
         self.partition_whole = bool(partition_whole)
         self._local = False  # set while whole tensors are stepped: their sums are complete per rank
-        self._whole_plans: Dict[tuple, tuple] = {}  # (owners, WholeExchange) per group layout
+        self._whole_plans: Dict[tuple, tuple] = {}  # per group: positions, owners, WholeExchange
 
     def _run_routed(self, group: dict, routed, spectral_devices: set, select=None, tag=None) -> None:
         world = self._world()
         if world == 1 or select is not None:
             super()._run_routed(group, routed, spectral_devices, select, tag)
             return
-        spectral, scalar, micro_items, spectral64 = routed
-        sharded = {d: [it for it in its if _is_shard(it[0])] for d, its in spectral.items()}
-        sharded = {d: its for d, its in sharded.items() if its}
-        whole_spec = {d: [it for it in its if not _is_shard(it[0])] for d, its in spectral.items()}
-        whole = tuple({d: its for d, its in per.items() if its}
-                      for per in (whole_spec, scalar, micro_items, spectral64))
-        if sharded:  # the exchanged step of the row shards
-            super()._run_routed(group, (sharded, {}, {}, {}), spectral_devices, None, tag)
-        if not any(whole):
-            return
-        wtag = ("whole", tag)
-        if not self.partition_whole:
-            self._local = True
-            try:
-                super()._run_routed(group, whole, spectral_devices, None, wtag)
-            finally:
-                self._local = False
-            return
-        flat = [(kind, d, it) for kind, per in enumerate(whole) for d, its in per.items() for it in its]
-        key = (id(group), tuple((kind, tuple(it[0].shape), it[0].data_ptr()) for kind, _, it in flat))
-        me = dist.get_rank(self.process_group)
+        # the group's routed items in a fixed order; the plan (which items are row shards,
+        # which whole ones this rank steps, the exchange) is keyed on the parameters
+        flat = [(kind, d, it) for kind, per in enumerate(routed) for d, its in per.items() for it in its]
+        key = (id(group), tuple(id(it[0]) for _, _, it in flat))
         plan = self._whole_plans.get(key)
         if plan is None:
-            owners = lpt_partition([it[0].numel() for _, _, it in flat], world)
-            plan = self._whole_plans[key] = (owners, WholeExchange([it for _, _, it in flat], owners, world, me))
-        owners, exchange = plan
-        mine: Tuple[Dict, ...] = ({}, {}, {}, {})
-        for (kind, d, it), o in zip(flat, owners):
-            if o == me:
-                mine[kind].setdefault(d, []).append(it)
+            plan = self._whole_plans[key] = self._plan_whole(flat, world)
+        sharded_idx, whole_idx, mine_idx, owners, exchange = plan
+
+        def subset(idx):
+            out: Tuple[Dict, ...] = ({}, {}, {}, {})
+            for i in idx:
+                kind, d, it = flat[i]
+                out[kind].setdefault(d, []).append(it)
+            return out
+
+        if sharded_idx:  # the exchanged step of the row shards
+            super()._run_routed(group, subset(sharded_idx), spectral_devices, None, tag)
+        if not whole_idx:
+            return
         self._local = True
         try:
-            super()._run_routed(group, mine, spectral_devices, None, wtag)
+            super()._run_routed(group, subset(mine_idx), spectral_devices, None, ("whole", tag))
         finally:
             self._local = False
-        exchange.run(self.process_group)
+        if exchange is not None:
+            exchange.run(self.process_group)
+
+    def _plan_whole(self, flat: list, world: int) -> tuple:
+        """(row-shard positions, whole positions, positions this rank steps, owners,
+        exchange) of a group's routed items."""
+        sharded_idx = [i for i, (kind, _, it) in enumerate(flat) if kind == 0 and _is_shard(it[0])]
+        whole_idx = [i for i, (kind, _, it) in enumerate(flat) if not (kind == 0 and _is_shard(it[0]))]
+        if not whole_idx:
+            return sharded_idx, whole_idx, [], [], None
+        if not self.partition_whole:
+            return sharded_idx, whole_idx, whole_idx, [], None
+        me = dist.get_rank(self.process_group)
+        items = [flat[i][2] for i in whole_idx]
+        owners = lpt_partition([it[0].numel() for it in items], world)
+        mine_idx = [i for i, o in zip(whole_idx, owners) if o == me]
+        return sharded_idx, whole_idx, mine_idx, owners, WholeExchange(items, owners, world, me)
 
     def invalidate_caches(self) -> None:
         super().invalidate_caches()

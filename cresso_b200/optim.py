@@ -47,6 +47,14 @@ _SPECTRAL_RANK_STATE = ("q_cos", "q_sin", "p_cos", "p_sin", "metric_cos", "metri
                         "metric_p_sin", "calcium_cos", "calcium_sin", "mode_confidence")
 
 
+def _items_ident(items: list) -> tuple:
+    """What a cached descriptor table depends on: the parameter objects, their
+    storage addresses and their state dicts (the cache entry holds references to
+    all of them, so no id can be reused while it lives)."""
+    ps = [it[0] for it in items]
+    return tuple(map(id, ps)), tuple([p.data_ptr() for p in ps]), tuple([id(it[2]) for it in items])
+
+
 class CRESSO5(Optimizer):
     """Contact-Refractory Axial-Spectral Optimizer (B200-native step).
 
@@ -59,9 +67,10 @@ class CRESSO5(Optimizer):
 
     The state tensors are updated in place, and the descriptor tables that point
     the kernels at them are cached across steps (keyed on the parameters, their
-    storage and their state dicts).  Change state through ``load_state_dict``
-    (which drops the caches) or in place; a caller that rebinds a state tensor
-    inside a state dict (``opt.state[p]["q_cos"] = t``) calls
+    storage addresses and their state dicts).  Change state through
+    ``load_state_dict`` (which drops the caches) or in place; a caller that
+    rebinds a state tensor inside a state dict (``opt.state[p]["q_cos"] = t``),
+    or gives a parameter a new shape over the same storage, calls
     ``invalidate_caches()`` afterwards.
     """
 
@@ -604,7 +613,7 @@ class CRESSO5(Optimizer):
         bins, tables = int(group["hash_bins"]), int(group["hash_tables"])
         settings = (group["rank"], group["max_frequency"], bins, tables, group.get("hard_channel_min_size"),
                     group.get("thin_matrix_hard_cutoff"))
-        ident = (settings, tuple((id(p), p.data_ptr(), p.shape, id(st)) for p, g, st in items))
+        ident = (settings, _items_ident(items))
         key = (device, id(group), tag)
         cached = self._spectral_desc_cache.get(key)
         if cached is not None and cached[0] == ident:
@@ -748,7 +757,7 @@ class CRESSO5(Optimizer):
         be freed (and its id or device address reused) while the entry lives."""
         F = _lib.DESC_INDEX
         n = len(items)
-        ident = tuple((id(p), p.data_ptr(), p.shape, id(st)) for p, g, st in items)
+        ident = _items_ident(items)
         cached = cache.get((device, tag))
         if cached is not None and cached[0] == ident:
             descs, nbytes = cached[1], cached[2]

@@ -177,7 +177,7 @@ def gpu_row_shard_worker(rank, world, port, outdir):
     states = [{k: (v.detach().cpu() if torch.is_tensor(v) else v) for k, v in opt.state[p].items()} for p in ps]
     whole = [p.detach().cpu() for p in ws]
     whole_states = [{k: (v.detach().cpu() if torch.is_tensor(v) else v) for k, v in opt.state[p].items()} for p in ws]
-    owners = next(iter(opt._whole_plans.values()))[0]
+    owners = next(iter(opt._whole_plans.values()))[3]
     if rank == 0:
         full = [torch.nn.Parameter(x.clone().to(dev)) for x in inits]
         ref = cresso_b200.CRESSO5(full, **kw)
