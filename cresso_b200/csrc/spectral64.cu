@@ -21,8 +21,8 @@
 // Carriers come from the float64 axis tables of a float64 shape workspace
 // (cresso_shape_workspace64_init).  Block partial sums are written per block and
 // added in block order by the one-block finalize kernels; the bin sums inside a
-// block use shared-memory float64 atomics (their order, and so the last bit of
-// a bin sum, can vary from run to run).  Above rank 64 the modes leave the
+// block are exact integer sums (exact_bins_add), so every sum of the pipeline
+// is the same from run to run.  Above rank 64 the modes leave the
 // registers (the wide-rank kernels s64w_*, RM == 0 in the launch templates).
 #include <cuda_runtime.h>
 #include <math.h>
@@ -269,6 +269,55 @@ __device__ __forceinline__ void block_record(double (&v)[L], double* red, double
     }
 }
 
+// ---- Exact hash-bin sums.  A value v with |v| < 2^66 is the integer
+// s = round(|v| 2^60) split into three limbs of 42 bits (high, middle, low; each
+// negated for negative v), each added into the bin with a native 64-bit
+// shared-memory integer atomic.  Integer sums do not depend on the order of the
+// additions, and a block's limb sums (exact for up to 2^21 values per bin) turn
+// into one double by a fixed formula, so the bin sums are the same in every run;
+// the only rounding is that of s (at most 2^-61 per value).  Values out of that
+// range, and non-finite ones, go to a float64 side sum of the bin (so that they
+// still propagate as they do in the reference).
+// Shared layout for tb bins: long long limbs [3][tb], then double side [tb].
+__host__ __device__ constexpr size_t exact_bins_bytes(int tb) { return (size_t)tb * 4 * 8; }
+
+__device__ __forceinline__ void exact_bins_zero(unsigned char* base, int tb) {
+    long long* lim = reinterpret_cast<long long*>(base);
+    double* side = reinterpret_cast<double*>(lim + 3 * tb);
+    for (int i = threadIdx.x; i < 3 * tb; i += blockDim.x) lim[i] = 0;
+    for (int i = threadIdx.x; i < tb; i += blockDim.x) side[i] = 0.0;
+}
+
+__device__ __forceinline__ void exact_bins_add(unsigned char* base, int tb, int b, double v) {
+    unsigned long long* lim = reinterpret_cast<unsigned long long*>(base);
+    const double a = fabs(v);
+    if (a < 0x1p66) {
+        const double sc = a * 0x1p60;                 // exact (power-of-two scaling)
+        const double h = floor(sc * 0x1p-84);
+        const double r1 = sc - h * 0x1p84;            // exact, in [0, 2^84)
+        const double m = floor(r1 * 0x1p-42);
+        const double r0 = r1 - m * 0x1p42;            // exact, in [0, 2^42)
+        long long hi = (long long)h, mid = (long long)m, lo = llrint(r0);
+        if (v < 0.0) {
+            hi = -hi;
+            mid = -mid;
+            lo = -lo;
+        }
+        atomicAdd(&lim[b], (unsigned long long)hi);
+        atomicAdd(&lim[tb + b], (unsigned long long)mid);
+        atomicAdd(&lim[2 * tb + b], (unsigned long long)lo);
+    } else {
+        double* side = reinterpret_cast<double*>(lim + 3 * tb);
+        atomicAdd(&side[b], v);
+    }
+}
+
+__device__ __forceinline__ double exact_bins_value(const unsigned char* base, int tb, int b) {
+    const long long* lim = reinterpret_cast<const long long*>(base);
+    const double* side = reinterpret_cast<const double*>(lim + 3 * tb);
+    return ((double)lim[b] * 0x1p24 + (double)lim[tb + b] * 0x1p-18 + (double)lim[2 * tb + b] * 0x1p-60) + side[b];
+}
+
 // ---- P1: force energy
 template <typename P>
 __global__ void __launch_bounds__(kThreads) s64_p1(G64<P> G) {
@@ -301,11 +350,14 @@ template <int RM, typename P>
 __global__ void __launch_bounds__(kThreads) s64_p2(G64<P> G) {
     S64_BIND_BLOCKS(blk);
     __shared__ double red[kWarps];
-    extern __shared__ double sbin[];  // [TB] sums, then [TB] counts
+    extern __shared__ __align__(16) unsigned char s64_smem[];  // exact bin sums, then [TB] counts
     const int TB = D.T * D.B;
     const bool hash_on = D.hash_on != 0;
-    if (hash_on)
-        for (int i = threadIdx.x; i < 2 * TB; i += kThreads) sbin[i] = 0.0;
+    double* cnt = reinterpret_cast<double*>(s64_smem + exact_bins_bytes(TB));
+    if (hash_on) {
+        exact_bins_zero(s64_smem, TB);
+        for (int i = threadIdx.x; i < TB; i += kThreads) cnt[i] = 0.0;
+    }
     __syncthreads();
     const double scale = Bf.cst->scale, ep = D.hp[Q_EP];
     double v[2 + 2 * RM];
@@ -327,15 +379,18 @@ __global__ void __launch_bounds__(kThreads) s64_p2(G64<P> G) {
         if (hash_on)
             for (int t = 0; t < D.T; ++t) {
                 const int b = (int)hash_bin(e, D.B, t);
-                atomicAdd(&sbin[t * D.B + b], ds);
-                atomicAdd(&sbin[TB + t * D.B + b], 1.0);
+                exact_bins_add(s64_smem, TB, t * D.B + b, ds);
+                atomicAdd(&cnt[t * D.B + b], 1.0);  // whole numbers: exact in any order
             }
     }
     const int RL = 2 + 2 * RM + 2 * TB;
     double* rec = Bf.rec + lb * RL;
-    block_record<2 + 2 * RM>(v, red, rec);
+    block_record<2 + 2 * RM>(v, red, rec);  // its barriers order the bin atomics before the reads
     if (hash_on)
-        for (int i = threadIdx.x; i < 2 * TB; i += kThreads) rec[2 + 2 * RM + i] = sbin[i];
+        for (int i = threadIdx.x; i < TB; i += kThreads) {
+            rec[2 + 2 * RM + i] = exact_bins_value(s64_smem, TB, i);
+            rec[2 + 2 * RM + TB + i] = cnt[i];
+        }
 }
 
 // Row sums of the instant-metric density: one warp per row (rank >= 2).
@@ -555,11 +610,10 @@ template <int RM, typename P>
 __global__ void __launch_bounds__(kThreads) s64_p3(G64<P> G) {
     S64_BIND_BLOCKS(blk);
     __shared__ double red[kWarps];
-    extern __shared__ double sbin[];
+    extern __shared__ __align__(16) unsigned char s64_smem[];  // exact bin sums
     const int TB = D.T * D.B;
     const bool hash_on = D.hash_on != 0;
-    if (hash_on)
-        for (int i = threadIdx.x; i < TB; i += kThreads) sbin[i] = 0.0;
+    if (hash_on) exact_bins_zero(s64_smem, TB);
     __syncthreads();
     const C64& C = *Bf.cst;
     const double scale = C.scale, tm = D.hp[Q_TM];
@@ -586,13 +640,13 @@ __global__ void __launch_bounds__(kThreads) s64_p3(G64<P> G) {
             v[1 + 3 * RM + k] += t * sh[k];
         }
         if (hash_on)
-            for (int tb = 0; tb < D.T; ++tb) atomicAdd(&sbin[tb * D.B + (int)hash_bin(e, D.B, tb)], port);
+            for (int tb = 0; tb < D.T; ++tb) exact_bins_add(s64_smem, TB, tb * D.B + (int)hash_bin(e, D.B, tb), port);
     }
     const int RL = 1 + 4 * RM + TB;
     double* rec = Bf.rec + lb * RL;
     block_record<1 + 4 * RM>(v, red, rec);
     if (hash_on)
-        for (int i = threadIdx.x; i < TB; i += kThreads) rec[1 + 4 * RM + i] = sbin[i];
+        for (int i = threadIdx.x; i < TB; i += kThreads) rec[1 + 4 * RM + i] = exact_bins_value(s64_smem, TB, i);
 }
 
 // Hash impulse reservoirs (cresso_v5.py:1140-1184) from the blocks' port bin
@@ -745,12 +799,15 @@ template <typename P>
 __global__ void __launch_bounds__(kThreads) s64w_p2(G64<P> G) {
     S64_BIND_BLOCKS(blk);
     __shared__ double red[kWarps];
-    extern __shared__ double sbin[];  // [TB] sums, then [TB] counts
+    extern __shared__ __align__(16) unsigned char s64_smem[];  // exact bin sums, then [TB] counts
     const int TB = D.T * D.B;
     const int y = blockIdx.y;
     const bool bins = D.hash_on != 0 && y == 0;
-    if (bins)
-        for (int i = threadIdx.x; i < 2 * TB; i += kThreads) sbin[i] = 0.0;
+    double* cnt = reinterpret_cast<double*>(s64_smem + exact_bins_bytes(TB));
+    if (bins) {
+        exact_bins_zero(s64_smem, TB);
+        for (int i = threadIdx.x; i < TB; i += kThreads) cnt[i] = 0.0;
+    }
     __syncthreads();
     const double scale = Bf.cst->scale, ep = D.hp[Q_EP];
     const int k0 = y * kChunkW;
@@ -777,13 +834,16 @@ __global__ void __launch_bounds__(kThreads) s64w_p2(G64<P> G) {
         if (bins)
             for (int t = 0; t < D.T; ++t) {
                 const int b = (int)hash_bin(e, D.B, t);
-                atomicAdd(&sbin[t * D.B + b], ds);
-                atomicAdd(&sbin[TB + t * D.B + b], 1.0);
+                exact_bins_add(s64_smem, TB, t * D.B + b, ds);
+                atomicAdd(&cnt[t * D.B + b], 1.0);
             }
     }
     block_record<2 + 2 * kChunkW>(v, red, Bf.rec2 + ((int64_t)y * Bf.blocks + lb) * kRec2);
     if (bins)
-        for (int i = threadIdx.x; i < 2 * TB; i += kThreads) Bf.rec[lb * 2 * TB + i] = sbin[i];
+        for (int i = threadIdx.x; i < TB; i += kThreads) {
+            Bf.rec[lb * 2 * TB + i] = exact_bins_value(s64_smem, TB, i);
+            Bf.rec[lb * 2 * TB + TB + i] = cnt[i];
+        }
 }
 
 template <typename P>
@@ -834,11 +894,10 @@ template <typename P>
 __global__ void __launch_bounds__(kThreads) s64w_p3a(G64<P> G) {
     S64_BIND_BLOCKS(blk);
     __shared__ double red[kWarps];
-    extern __shared__ double sbin[];
+    extern __shared__ __align__(16) unsigned char s64_smem[];  // exact bin sums
     const int TB = D.T * D.B;
     const bool hash_on = D.hash_on != 0;
-    if (hash_on)
-        for (int i = threadIdx.x; i < TB; i += kThreads) sbin[i] = 0.0;
+    if (hash_on) exact_bins_zero(s64_smem, TB);
     __syncthreads();
     const C64& C = *Bf.cst;
     const double scale = C.scale, tm = D.hp[Q_TM];
@@ -868,12 +927,12 @@ __global__ void __launch_bounds__(kThreads) s64w_p3a(G64<P> G) {
         const double port = err + tm * t;
         Bf.pbuf[e] = port;
         if (hash_on)
-            for (int tb = 0; tb < D.T; ++tb) atomicAdd(&sbin[tb * D.B + (int)hash_bin(e, D.B, tb)], port);
+            for (int tb = 0; tb < D.T; ++tb) exact_bins_add(s64_smem, TB, tb * D.B + (int)hash_bin(e, D.B, tb), port);
     }
     double* rec = Bf.rec + lb * (1 + TB);
     block_record<1>(v, red, rec);
     if (hash_on)
-        for (int i = threadIdx.x; i < TB; i += kThreads) rec[1 + i] = sbin[i];
+        for (int i = threadIdx.x; i < TB; i += kThreads) rec[1 + i] = exact_bins_value(s64_smem, TB, i);
 }
 
 // P3 projections, chunk y = blockIdx.y: the stored port and tangent on modes
@@ -1280,6 +1339,13 @@ int plan64(const cresso_tensor_desc* descs, int64_t n, const cresso_hparams* hp,
     return CRESSO_OK;
 }
 
+// Dynamic shared memory beyond the default 48 KB needs the kernel's opt-in.
+template <typename K>
+cudaError_t set_smem(K* kernel, size_t bytes) {
+    if (bytes <= 48 * 1024) return cudaSuccess;
+    return cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+}
+
 // One group: its tables uploaded to the front of the scratch, then every pass
 // as one launch over the blocks of all its tensors and every finalize as one
 // launch of a block per tensor.
@@ -1340,8 +1406,8 @@ int run_group(const Plan64& PL, const Group64& Gr, char* base, cudaStream_t s) {
         gr += it.rblocks;
         gc += it.cblocks;
         if (T.hash_on) {
-            smem2 = std::max(smem2, (size_t)2 * T.T * T.B * 8);
-            smem3 = std::max(smem3, (size_t)T.T * T.B * 8);
+            smem2 = std::max(smem2, exact_bins_bytes(T.T * T.B) + (size_t)T.T * T.B * 8);
+            smem3 = std::max(smem3, exact_bins_bytes(T.T * T.B));
         }
         any_axes = any_axes || it.rblocks > 0;
     }
@@ -1364,9 +1430,11 @@ int run_group(const Plan64& PL, const Group64& Gr, char* base, cudaStream_t s) {
     {
         NvtxRange r("cresso64 P2 density / bins / projection");
         if constexpr (RM == 0) {
+            CRESSO_CUDA(set_smem(s64w_p2<P>, smem2));
             s64w_p2<P><<<dim3(g, chunks), kThreads, smem2, s>>>(G);
             CRESSO_LAUNCHED("s64w_p2");
         } else {
+            CRESSO_CUDA(set_smem(s64_p2<RM, P>, smem2));
             s64_p2<RM, P><<<g, kThreads, smem2, s>>>(G);
             CRESSO_LAUNCHED("s64_p2");
         }
@@ -1387,6 +1455,7 @@ int run_group(const Plan64& PL, const Group64& Gr, char* base, cudaStream_t s) {
     {
         NvtxRange r("cresso64 P3 tangent / port");
         if constexpr (RM == 0) {
+            CRESSO_CUDA(set_smem(s64w_p3a<P>, smem3));
             s64w_p3a<P><<<g, kThreads, smem3, s>>>(G);
             CRESSO_LAUNCHED("s64w_p3a");
             s64w_p3b<P><<<dim3(g, chunks), kThreads, 0, s>>>(G);
@@ -1394,6 +1463,7 @@ int run_group(const Plan64& PL, const Group64& Gr, char* base, cudaStream_t s) {
             s64w_fin3<P><<<n, kThreads, 0, s>>>(G);
             CRESSO_LAUNCHED("s64w_fin3");
         } else {
+            CRESSO_CUDA(set_smem(s64_p3<RM, P>, smem3));
             s64_p3<RM, P><<<g, kThreads, smem3, s>>>(G);
             CRESSO_LAUNCHED("s64_p3");
             s64_fin3<RM, P><<<n, kThreads, 0, s>>>(G);

@@ -399,16 +399,31 @@ def test_scalar_route_cluster_shapes(variant):
                       upd_tol=5e-4)
 
 
-def test_run_to_run_deterministic():
-    shapes, kw, inits, grads = _bench_inputs("c1", 3)
+@pytest.mark.parametrize("case", ["c1", "f64", "r96"])
+def test_run_to_run_deterministic(case):
+    """The same inputs give bit-identical parameters and state in two runs: the
+    fused float32 path (c1), the float64 pipeline and its wide-rank form, whose
+    hash-bin sums are exact integer sums inside a block and fixed-order float64
+    sums across blocks."""
+    if case == "c1":
+        shapes, kw, inits, grads = _bench_inputs("c1", 3)
+        init, gl, dt = inits[0], [gs[0] for gs in grads], torch.float32
+    else:
+        g = torch.Generator().manual_seed(11)
+        shape = (192, 160) if case == "f64" else (96, 80)
+        kw = dict(rank=8 if case == "f64" else 96, hash_bins=64, hash_tables=2, min_spectral_size=1024)
+        dt = torch.float64 if case == "f64" else torch.float32
+        init = torch.randn(shape, generator=g) * 0.02
+        gl = [torch.randn(shape, generator=g) * 1e-3 for _ in range(3)]
     outs = []
     for _ in range(2):
-        p = torch.nn.Parameter(inits[0].clone().cuda())
+        p = torch.nn.Parameter(init.clone().to("cuda", dt))
         opt = cresso_b200.CRESSO5([p], **kw)
-        for gs in grads:
-            p.grad = gs[0].cuda()
+        for gg in gl:
+            p.grad = gg.to("cuda", dt)
             opt.step()
         outs.append((p.detach().cpu(), {k: v.cpu() for k, v in opt.state[p].items() if torch.is_tensor(v)}))
+    assert "hash_energy" in outs[0][1]
     assert torch.equal(outs[0][0], outs[1][0])
     for k in outs[0][1]:
         assert torch.equal(outs[0][1][k], outs[1][1][k]), k
