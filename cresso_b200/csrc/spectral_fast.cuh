@@ -135,19 +135,32 @@ __device__ __forceinline__ float2 log1p_pos2(float2 x) {
 }
 
 // Drive components of two elements (cresso_v5.py:1315-1326; drive_parts on a row pair).
+// The bounded channel tanh(t / clip) clip enters only u, so its factor clip rides
+// on the spike mix (DriveK2::sp_clip).  NOV_SCALED false returns the novelty
+// without its factor clip, for a caller that folds clip into the novelty's
+// coefficient (P5).
 struct Drive2 {
     float2 u, root, nov, rat;
 };
-__device__ __forceinline__ Drive2 drive_parts2(float2 t, float2 pred, const DriveK& c) {
+// Per-tensor constants of the drive shaping: omsp = 1 - sp and sp_clip = sp clip
+// in place of the spike mix sp, and clip2e = clip^2 + eps: min(|t|, clip^2) + eps
+// = min(|t| + eps, clip^2 + eps) exactly (rounding is monotone).
+struct DriveK2 {
+    float clip, inv_clip, clip2e, omsp, sp_clip, invD, eps;
+};
+template <bool NOV_SCALED = true>
+__device__ __forceinline__ Drive2 drive_parts2(float2 t, float2 pred, const DriveK2& c) {
     Drive2 d;
     const float2 at = f2(fabsf(t.x), fabsf(t.y));
     const float2 den = __ffma2_rn(at, f2(c.inv_clip), f2(1.0f));  // in [1, 1 + 1e4 / clip]
     d.rat = __fmul2_rn(t, f2(rcp_approx(den.x), rcp_approx(den.y)));
-    const float2 bnd = __fmul2_rn(tanh2(__fmul2_rn(t, f2(c.inv_clip))), f2(c.clip));
-    const float2 rr = __fadd2_rn(f2(fminf(at.x, c.clip2), fminf(at.y, c.clip2)), f2(c.eps));
+    const float2 bnd1 = tanh2(__fmul2_rn(t, f2(c.inv_clip)));  // bounded channel over clip
+    const float2 ae = __fadd2_rn(at, f2(c.eps));
+    const float2 rr = f2(fminf(ae.x, c.clip2e), fminf(ae.y, c.clip2e));
     d.root = f2(t.x != 0.0f ? copysignf(sqrt_sfu(rr.x), t.x) : 0.0f, t.y != 0.0f ? copysignf(sqrt_sfu(rr.y), t.y) : 0.0f);
-    d.u = __ffma2_rn(f2(c.sp), bnd, __fmul2_rn(f2(1.0f - c.sp), d.rat));
-    d.nov = __fmul2_rn(tanh2(__fmul2_rn(__fadd2_rn(t, f2(-pred.x, -pred.y)), f2(c.invD))), f2(c.clip));
+    d.u = __ffma2_rn(f2(c.sp_clip), bnd1, __fmul2_rn(f2(c.omsp), d.rat));
+    d.nov = tanh2(__fmul2_rn(__fadd2_rn(t, f2(-pred.x, -pred.y)), f2(c.invD)));
+    if constexpr (NOV_SCALED) d.nov = __fmul2_rn(d.nov, f2(c.clip));
     return d;
 }
 
@@ -306,7 +319,7 @@ fast_pass_kernel(const GroupHdr* __restrict__ hdr, const DevTensor* __restrict__
         const TensorConsts* __restrict__ Cp = Dp->cst;
         const float sgn = (flags & F_MAXIMIZE) ? -1.0f : 1.0f;
         float scale = 0.f, inv_scale = 0.f, sscale = 0.f, seps = 0.f;
-        DriveK dk{};
+        DriveK2 dk{};
         float c_u = 0.f, c_root = 0.f, c_t = 0.f, c_nov = 0.f, c_hp = 0.f, gain = 0.f, neg_lr = 0.f;
         if constexpr (PASS == 2 || PASS == 3) {
             scale = Cp->scale;
@@ -314,12 +327,13 @@ fast_pass_kernel(const GroupHdr* __restrict__ hdr, const DevTensor* __restrict__
             sscale = sgn * scale;
             seps = sgn * eps;
         }
-        if constexpr (PASS >= 4) dk = DriveK{Cp->clip, Cp->inv_clip, Cp->clip2, Cp->sp, Cp->invD, eps};
+        if constexpr (PASS >= 4)
+            dk = DriveK2{Cp->clip, Cp->inv_clip, Cp->clip2 + eps, 1.0f - Cp->sp, Cp->sp * Cp->clip, Cp->invD, eps};
         if constexpr (PASS == 5) {
             c_u = Cp->c_u;
             c_root = Cp->c_root;
             c_t = Cp->c_t;
-            c_nov = Cp->c_nov;
+            c_nov = Cp->c_nov * Cp->clip;  // the novelty comes without its factor clip (drive_parts2<false>)
             c_hp = Cp->c_hp;
             gain = Cp->gain;
             neg_lr = Cp->neg_lr;
@@ -651,7 +665,7 @@ fast_pass_kernel(const GroupHdr* __restrict__ hdr, const DevTensor* __restrict__
                         const float2 pred = f2(R1[u], R1[u + 1]);
                         const float2 echo = echo_on ? f2(R2[u], R2[u + 1]) : f2(0.0f);
                         const float2 hp = f2(s_joint[jb[o]], s_joint[jb[o + 256]]);
-                        const Drive2 dp = drive_parts2(t, pred, dk);
+                        const Drive2 dp = drive_parts2<true>(t, pred, dk);
                         const float2 v[7] = {dp.u, dp.root, t, pred, dp.nov, echo, hp};
 #pragma unroll
                         for (int a = 0; a < 7; ++a)
@@ -667,7 +681,7 @@ fast_pass_kernel(const GroupHdr* __restrict__ hdr, const DevTensor* __restrict__
                         const float2 pred = f2(R1[u], R1[u + 1]);
                         const float2 comb = f2(R2[u], R2[u + 1]);
                         const float2 hp = f2(s_joint[jb[o]], s_joint[jb[o + 256]]);
-                        const Drive2 dp = drive_parts2(t, pred, dk);
+                        const Drive2 dp = drive_parts2<false>(t, pred, dk);
                         float2 drive = __fmul2_rn(f2(c_u), dp.u);
                         drive = __ffma2_rn(f2(c_root), dp.root, drive);
                         drive = __ffma2_rn(f2(c_t), t, drive);
