@@ -382,8 +382,10 @@ def workload_config(workload, shapes, kw, dtype):
             "c5embed": "the (32000, 4096) embedding / lm_head shape of c5"}.get(workload, str(shapes[0]))
     return {"workload": f"{workload}: {desc}", "rank": kw["rank"], "hash_bins": kw["hash_bins"],
             "hash_tables": kw["hash_tables"], "elements": n_total,
-            "l2": "no flush: inputs of every step (grads + params) exceed the 126 MB L2"
-                  if n_total * 8 > 2 * 126e6 else "inputs fit in the 126 MB L2 (no flush)"}
+            "l2": "flushed: inputs fit in the 126 MB L2, so every step is timed on its own with a "
+                  "256 MB buffer written between steps, outside the timed intervals"
+                  if fits_in_l2(n_total, 12 if dtype == "f32" else (6 if dtype in ("bf16", "f16") else 24))
+                  else "no flush: inputs of every step (grads + params) exceed the 126 MB L2"}
 
 
 # ---------------------------------------------------------------------------
@@ -431,20 +433,43 @@ def make_inputs(name, args, world, rank, device, zero):
     return shapes, kw, params, grads_dev, n_local, sum(numel(s) for s in shapes), bpe
 
 
-def time_steps(opt, steps, device, stream, world):
+L2_FLUSH_BYTES = 256 << 20  # twice the B200's 126 MB L2
+
+
+def fits_in_l2(n_total, bpe):
+    """Whether a step's inputs (gradients and parameters) could stay in L2 between steps."""
+    return n_total * (2 * bpe // 3) <= 2 * 126e6
+
+
+def time_steps(opt, steps, device, stream, world, flush=False):
     """Device time of exactly `steps` steps (CUDA events, barrier and synchronize on
-    both sides, max over ranks), in ms per step."""
+    both sides, max over ranks), in ms per step.  With `flush` (inputs that fit in
+    L2) every step is timed on its own and a 256 MB buffer is written between the
+    steps, outside the timed intervals, so no step finds its inputs in L2."""
     gc.collect()  # no collection of an earlier workload's objects inside the timed steps
+    buf = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=device) if flush else None
     barrier(world)
     torch.cuda.synchronize(device)
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    for _ in range(steps):
+    if not flush:
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(steps):
+            opt.step()
+        e1.record(stream)
+        torch.cuda.synchronize(device)
+        barrier(world)
+        return max_over_ranks(e0.elapsed_time(e1) / steps, world, device)
+    pairs = []
+    for i in range(steps):
+        buf.fill_(i & 255)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
         opt.step()
-    e1.record(stream)
+        b.record(stream)
+        pairs.append((a, b))
     torch.cuda.synchronize(device)
     barrier(world)
-    return max_over_ranks(e0.elapsed_time(e1) / steps, world, device)
+    return max_over_ranks(sum(a.elapsed_time(b) for a, b in pairs) / steps, world, device)
 
 
 def sharded_parity_check(world, rank, device, steps=3):
@@ -533,11 +558,12 @@ def quick_config(name, args, device, stream):
     for _ in range(args.warmup):
         opt.step()
     torch.cuda.synchronize(device)
-    ms = time_steps(opt, args.steps, device, stream, 1)
+    ms = time_steps(opt, args.steps, device, stream, 1, flush=fits_in_l2(n_total, bpe))
     e2e = time_e2e(opt, params, grads_dev, args, 1, device, stream, n_total, bpe)
     opt.check_device_status()
     out = {"ms_per_step": round(ms, 5), "value": round(bpe * n_total / (ms * 1e-3) / 1e9, 3), "unit": "GB/s",
            "elements": n_total, "workload": workload_config(name, shapes, kw, args.dtype)["workload"],
+           "l2": workload_config(name, shapes, kw, args.dtype)["l2"],
            "e2e": {"value": round(e2e["value"], 3), "ms_per_step": round(e2e["ms_per_step"], 5)}}
     del opt, params, grads_dev
     torch.cuda.empty_cache()
@@ -611,7 +637,7 @@ def b200_arm(args, world, rank, local):
             pass
     launches0 = _lib.launch_count()
     with ClockSampler(rank == 0, uuids) as clk:
-        ms = time_steps(opt, args.steps, device, stream, world)
+        ms = time_steps(opt, args.steps, device, stream, world, flush=fits_in_l2(n_total, bpe))
     launches = _lib.launch_count() - launches0
     opt.check_device_status()
     value = bpe * n_total / (ms * 1e-3) / 1e9
