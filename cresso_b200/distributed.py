@@ -134,6 +134,8 @@ class WholeExchange:
                 used[o] += (nb + 15) // 16 * 16
         self.block = max(max(used), 16)
         device = items[0][0].device
+        if any(it[0].device != device for it in items):
+            raise RuntimeError("RowShardedCRESSO5: the tensors stepped whole must all be on this rank's device")
         self.device = device
         self.send = torch.zeros(self.block, dtype=torch.uint8, device=device)
         self.recv = torch.zeros(self.world * self.block, dtype=torch.uint8, device=device)
