@@ -1128,7 +1128,8 @@ __host__ __device__ inline int64_t red_len(int pass, int64_t rm, int64_t tb, int
 // the result does not depend on the launch or the GPU.  Block kinds: the
 // scalar and hash-bin outputs (records of the blocks that covered the tensor)
 // take 8 outputs x 32 groups per block; the column sums of pass 2 (one
-// partial per row band) take 64 outputs x 4 groups.  grid.x = the largest
+// partial per row band) take 64 outputs x 4 groups, or 256 outputs of one
+// group when the partials are per block run (col_runs).  grid.x = the largest
 // number of scalar blocks over the tensors + the largest number of column
 // blocks; grid.y = tensors.
 constexpr int kRedOutA = 8, kRedGrpA = kThreads / kRedOutA;   // 8 x 32
@@ -1148,8 +1149,12 @@ __global__ void reduce_kernel(int pass, int blocks_a, const GroupHdr* __restrict
     const int64_t na = red_scal_len(pass, rm, tb);                      // scalar + bin outputs
     const int64_t nc = red_len(pass, rm, tb, D.cols, D.ndim) - na;      // column outputs
     const bool kind_a = (int)blockIdx.x < blocks_a;
-    const int outs = kind_a ? kRedOutA : kRedOutB, grps = kind_a ? kRedGrpA : kRedGrpB;
-    const int64_t first = kind_a ? (int64_t)blockIdx.x * kRedOutA : na + (int64_t)(blockIdx.x - blocks_a) * kRedOutB;
+    // column outputs of a tensor with per-run partials (col_runs): a thread per output,
+    // each adding its column's one or two block runs, so every thread of the block works
+    const bool runs = !kind_a && D.col_runs;
+    const int outs = kind_a ? kRedOutA : (runs ? kThreads : kRedOutB);
+    const int grps = kind_a ? kRedGrpA : (runs ? 1 : kRedGrpB);
+    const int64_t first = kind_a ? (int64_t)blockIdx.x * kRedOutA : na + (int64_t)(blockIdx.x - blocks_a) * outs;
     const int64_t last = kind_a ? na : na + nc;
     if (first >= last) return;  // block-uniform
     const int j = threadIdx.x % outs, g = threadIdx.x / outs;
@@ -2111,10 +2116,12 @@ static int launch_stage(int stage, const Plan& P, char* base, cudaStream_t s) {
     };
     auto run_reduce = [&](int pass) -> int {
         const int64_t na = red_scal_len(pass, P.rm, P.hdr.tb);
-        int64_t maxc = 0;
-        for (auto& D : P.dts) maxc = std::max(maxc, red_len(pass, P.rm, P.hdr.tb, D.cols, D.ndim) - na);
+        int64_t maxb = 0;  // column blocks of the tensor that needs the most
+        for (auto& D : P.dts)
+            maxb = std::max(maxb, ceil_div(red_len(pass, P.rm, P.hdr.tb, D.cols, D.ndim) - na,
+                                           D.col_runs ? kThreads : kRedOutB));
         const int blocks_a = (int)ceil_div(na, kRedOutA);
-        dim3 grid((unsigned)(blocks_a + ceil_div(maxc, kRedOutB)), (unsigned)n);
+        dim3 grid((unsigned)(blocks_a + maxb), (unsigned)n);
         reduce_kernel<<<grid, kThreads, 0, s>>>(pass, blocks_a, hdr, dts, recs, recb);
         CRESSO_LAUNCHED("reduce_kernel");
         return CRESSO_OK;
