@@ -450,26 +450,31 @@ def time_steps(opt, steps, device, stream, world, flush=False):
     buf = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=device) if flush else None
     barrier(world)
     torch.cuda.synchronize(device)
-    if not flush:
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record(stream)
-        for _ in range(steps):
-            opt.step()
-        e1.record(stream)
-        torch.cuda.synchronize(device)
-        barrier(world)
-        return max_over_ranks(e0.elapsed_time(e1) / steps, world, device)
-    pairs = []
-    for i in range(steps):
-        buf.fill_(i & 255)
-        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        a.record(stream)
-        opt.step()
-        b.record(stream)
-        pairs.append((a, b))
-    torch.cuda.synchronize(device)
+    gc.disable()  # nor a collector pause (they reach milliseconds once a process holds many objects)
+    try:
+        if not flush:
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            for _ in range(steps):
+                opt.step()
+            e1.record(stream)
+            torch.cuda.synchronize(device)
+            ms = e0.elapsed_time(e1) / steps
+        else:
+            pairs = []
+            for i in range(steps):
+                buf.fill_(i & 255)
+                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                a.record(stream)
+                opt.step()
+                b.record(stream)
+                pairs.append((a, b))
+            torch.cuda.synchronize(device)
+            ms = sum(a.elapsed_time(b) for a, b in pairs) / steps
+    finally:
+        gc.enable()
     barrier(world)
-    return max_over_ranks(sum(a.elapsed_time(b) for a, b in pairs) / steps, world, device)
+    return max_over_ranks(ms, world, device)
 
 
 def sharded_parity_check(world, rank, device, steps=3):
