@@ -209,7 +209,7 @@ class RowShardedCRESSO5(CRESSO5):
         self.pipeline_exchange = bool(pipeline_exchange)
         self.partition_whole = bool(partition_whole)
         self._local = False  # set while whole tensors are stepped: their sums are complete per rank
-        self._whole_plans: Dict[tuple, tuple] = {}  # per group: positions, owners, WholeExchange
+        self._whole_plans: Dict[int, tuple] = {}  # id(group) -> (parameter ids, plan)
 
     def _run_routed(self, group: dict, routed, spectral_devices: set, select=None, tag=None) -> None:
         world = self._world()
@@ -219,11 +219,11 @@ class RowShardedCRESSO5(CRESSO5):
         # the group's routed items in a fixed order; the plan (which items are row shards,
         # which whole ones this rank steps, the exchange) is keyed on the parameters
         flat = [(kind, d, it) for kind, per in enumerate(routed) for d, its in per.items() for it in its]
-        key = (id(group), tuple(id(it[0]) for _, _, it in flat))
-        plan = self._whole_plans.get(key)
-        if plan is None:
-            plan = self._whole_plans[key] = self._plan_whole(flat, world)
-        sharded_idx, whole_idx, mine_idx, owners, exchange = plan
+        ident = tuple(id(it[0]) for _, _, it in flat)
+        cached = self._whole_plans.get(id(group))  # the group's last plan only
+        if cached is None or cached[0] != ident:
+            cached = self._whole_plans[id(group)] = (ident, self._plan_whole(flat, world))
+        sharded_idx, whole_idx, mine_idx, owners, exchange = cached[1]
 
         def subset(idx):
             out: Tuple[Dict, ...] = ({}, {}, {}, {})

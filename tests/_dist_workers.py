@@ -177,7 +177,7 @@ def gpu_row_shard_worker(rank, world, port, outdir):
     states = [{k: (v.detach().cpu() if torch.is_tensor(v) else v) for k, v in opt.state[p].items()} for p in ps]
     whole = [p.detach().cpu() for p in ws]
     whole_states = [{k: (v.detach().cpu() if torch.is_tensor(v) else v) for k, v in opt.state[p].items()} for p in ws]
-    owners = next(iter(opt._whole_plans.values()))[3]
+    owners = next(iter(opt._whole_plans.values()))[1][3]
     if rank == 0:
         full = [torch.nn.Parameter(x.clone().to(dev)) for x in inits]
         ref = cresso_b200.CRESSO5(full, **kw)
@@ -324,4 +324,48 @@ def whole_broadcast_worker(rank, world, port, outdir):
     torch.save({"owners": owners, "params": [p for p, _, _ in items], "q": [st["q"] for _, _, st in items],
                 "metric": [st["metric"] for _, _, st in items], "freqs": [st["freqs"] for _, _, st in items]},
                os.path.join(outdir, f"wbcast_{rank}.pt"))
+    dist.destroy_process_group()
+
+
+def whole_plan_worker(rank, world, port, outdir):
+    """RowShardedCRESSO5's split of a routed group on CPU ranks, with the kernel
+    launches replaced by a recorder that 'steps' a tensor by writing a value into
+    it: the row shards go to the exchanged step on every rank, each whole tensor
+    is stepped on its owner only and reaches every rank through the exchange; a
+    second call reuses the cached plan."""
+    import cresso_b200.optim as optim
+    from cresso_b200.distributed import RowShardedCRESSO5, mark_row_shard
+
+    _init(rank, world, port, "gloo")
+    calls = []
+
+    def fake_run_routed(self, group, routed, spectral_devices, select=None, tag=None):
+        kinds = []
+        for kind, per in enumerate(routed):
+            for d, its in per.items():
+                for p, g, st in its:
+                    kinds.append((kind, int(p.numel()), bool(getattr(p, "_cresso_shard", None))))
+                    if not getattr(p, "_cresso_shard", None):
+                        p.data.fill_(1000 + 10 * int(p.numel()) + kind)
+                        st["q"].fill_(float(p.numel()))
+        calls.append((tag, sorted(kinds)))
+
+    optim.CRESSO5._run_routed = fake_run_routed
+    cpu = torch.device("cpu")
+    shard = mark_row_shard(torch.nn.Parameter(torch.zeros(4, 8)), (8, 8), 4 * rank)
+    whole = [torch.nn.Parameter(torch.zeros(s)) for s in [(64, 16), (7, 9), (3, 4, 5), (30,), (16, 64)]]
+    opt = RowShardedCRESSO5([shard] + whole, rank=8)
+    states = {id(p): {"step": 1, "q": torch.zeros(())} for p in [shard] + whole}
+    routed = ({cpu: [(shard, None, states[id(shard)]), (whole[2], None, states[id(whole[2])])]},
+              {cpu: [(p, None, states[id(p)]) for p in (whole[0], whole[1], whole[4])]},
+              {cpu: [(whole[3], None, states[id(whole[3])])]}, {})
+    group = opt.param_groups[0]
+    opt._run_routed(group, routed, set())
+    n_plans = len(opt._whole_plans)
+    opt._run_routed(group, routed, set())  # the cached plan
+    owners = next(iter(opt._whole_plans.values()))[1][3]
+    torch.save({"calls": calls, "owners": owners, "n_plans": n_plans, "n_plans2": len(opt._whole_plans),
+                "whole": [p.detach().clone() for p in whole],
+                "q": [states[id(p)]["q"].clone() for p in whole]},
+               os.path.join(outdir, f"wplan_{rank}.pt"))
     dist.destroy_process_group()

@@ -135,6 +135,26 @@ def test_whole_tensors_reach_every_rank_from_their_owners_gloo(tmp_path):
             assert torch.all(r[k]["freqs"][i] == (k if o == k else -1))  # integer state is not sent
 
 
+def test_row_sharded_split_and_whole_exchange_gloo(tmp_path):
+    spawn(W.whole_plan_worker, 2, tmp_path)
+    r = [torch.load(tmp_path / f"wplan_{k}.pt") for k in range(2)]
+    assert r[0]["owners"] == r[1]["owners"] and set(r[0]["owners"]) == {0, 1}
+    assert r[0]["n_plans"] == r[0]["n_plans2"] == 1  # the second call reused the plan
+    for k in range(2):
+        sharded = [c for c in r[k]["calls"] if c[0] is None]
+        owned = [c for c in r[k]["calls"] if c[0] is not None]
+        assert len(sharded) == 2 and all(c[1] == [(0, 32, True)] for c in sharded)  # the shard alone
+        # this rank stepped exactly the whole tensors it owns (plan order: kinds 0, 1, 2)
+        order = [(0, 60), (1, 1024), (1, 63), (1, 1024), (2, 30)]
+        mine = sorted((kind, n, False) for (kind, n), o in zip(order, r[k]["owners"]) if o == k)
+        assert all(c[1] == mine for c in owned), (owned, mine)
+        # every rank ends with each owner's values
+        kinds = {60: 0, 1024: 1, 63: 1, 30: 2}
+        for p, q in zip(r[k]["whole"], r[k]["q"]):
+            n = p.numel()
+            assert torch.all(p == 1000 + 10 * n + kinds[n]) and float(q) == n
+
+
 @pytest.mark.gpu
 def test_row_sharded_step_matches_single_gpu(tmp_path):
     if torch.cuda.device_count() < 2:
