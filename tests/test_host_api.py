@@ -89,3 +89,26 @@ def test_count_state_elements_helper():
     class Fake:
         state = {0: {"a": torch.zeros(3, 2), "step": 4}, 1: {"b": torch.zeros(())}}
     assert cresso_b200.count_optimizer_state_elements(Fake()) == 7
+
+
+@pytest.mark.parametrize("workload,sharded", [("c2", True), ("c3", False)])
+def test_bench_row_sharding_marks_only_spectral_route_tensors(workload, sharded):
+    """bench.py at N > 1 (row sharding): 1-D / 2-D tensors on the spectral route
+    are cut into row blocks, the rest (LoRA-thin scalar-route tensors) stay whole
+    for their owner ranks."""
+    import bench
+    from cresso_b200.distributed import row_block
+
+    class Args:
+        dtype = "f32"
+
+    shapes, kw, params, grads, n_local, n_total, bpe = bench.make_inputs(workload, Args, 2, 1, torch.device("cpu"),
+                                                                        False)
+    for s, p in zip(shapes, params):
+        spec = getattr(p, "_cresso_shard", None)
+        assert (spec is not None) == sharded
+        if sharded:
+            start, stop = row_block(s[0], 1, 2)
+            assert tuple(p.shape) == (stop - start,) + tuple(s[1:]) and spec == (tuple(s), start)
+        else:
+            assert tuple(p.shape) == tuple(s)
